@@ -1,0 +1,27 @@
+#!/usr/bin/env bash
+# Builds the unmodified reference (DeRuiChen258/Turbol, turbol_vllm tree) with
+# its own CMake for sm_100 and installs its Python package + benchmark binaries
+# into baseline/_ref (git-ignored).  The reference ships no setup.py or
+# pyproject.toml at its root, so `pip install /root/reference` cannot work;
+# this runs the build the reference's own CMakeLists.txt defines, from a copy
+# (the source tree is read-only).  Tests are off (GoogleTest is not installed)
+# and NCCL is off (its NCCL build calls a function NCCL does not have).
+set -euo pipefail
+REF=${REF:-/root/reference}
+HERE=$(cd "$(dirname "$0")" && pwd)
+SRC=$(mktemp -d /tmp/ref_src.XXXX)
+BLD=$(mktemp -d /tmp/ref_build.XXXX)
+cp -r "$REF"/. "$SRC"/
+chmod -R u+w "$SRC"
+TORCH_DIR=$(python -c 'import torch,os;print(os.path.join(os.path.dirname(torch.__file__),"share/cmake/Torch"))')
+PYBIND_DIR=$(python -c 'import pybind11;print(pybind11.get_cmake_dir())')
+cmake -S "$SRC/turbol_vllm" -B "$BLD" -G Ninja -DCMAKE_BUILD_TYPE=Release -DCMAKE_CUDA_ARCHITECTURES=100 \
+  -DTURBORL_ENABLE_TESTS=OFF -DTURBORL_ENABLE_PYTHON=ON -DTURBORL_USE_NCCL=OFF \
+  -DTorch_DIR="$TORCH_DIR" -Dpybind11_DIR="$PYBIND_DIR" -DPython_EXECUTABLE="$(which python)"
+cmake --build "$BLD" -j "$(nproc)"
+mkdir -p "$HERE/_ref/bin"
+rm -rf "$HERE/_ref/turbol" "$HERE/_ref/examples"
+cp -r "$SRC/turbol_vllm/python/turbol" "$HERE/_ref/"
+cp -r "$SRC/turbol_vllm/examples" "$HERE/_ref/examples"
+cp "$BLD"/benchmark_components "$BLD"/benchmark_tensor "$BLD"/benchmark_attention "$BLD"/turbol_example "$HERE/_ref/bin/"
+echo "reference installed in $HERE/_ref"

@@ -1,0 +1,342 @@
+// torch-tensor entry points of the RL kernels (turbol_b200.turbol_core.ops).
+// Each op checks device, dtype, contiguity and shapes, then launches on the
+// current torch CUDA stream; errors raise.  No op allocates scratch behind the
+// caller's back except where the output itself is returned.
+#include <pybind11/pybind11.h>
+#include <torch/extension.h>
+
+#include "kernels.h"
+#include "turbol/common.hpp"
+
+namespace py = pybind11;
+
+namespace {
+
+#define TB_CHECK(cond, msg)                                  \
+  do {                                                       \
+    if (!(cond)) throw std::invalid_argument(std::string(msg)); \
+  } while (0)
+
+void cuda_ok(int e, const char* what) {
+  if (e != 0) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(static_cast<cudaError_t>(e)));
+}
+
+void need(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TB_CHECK(t.defined(), std::string(name) + " is undefined");
+  TB_CHECK(t.is_cuda(), std::string(name) + " must be a CUDA tensor");
+  TB_CHECK(t.scalar_type() == dt, std::string(name) + " has the wrong dtype");
+  TB_CHECK(t.is_contiguous(), std::string(name) + " must be contiguous");
+}
+
+cudaStream_t stream_of(const at::Tensor& t) { return turbol::StreamFor(t); }
+
+TbCartPoleParams cp_params(py::dict d) {
+  TbCartPoleParams p{9.8f, 1.0f, 0.1f, 0.5f, 10.0f, 0.02f, 2.4f, 12.0f * 2.0f * 3.14159265358979f / 360.0f, 0.05f, 500};
+  if (d.contains("gravity")) p.gravity = d["gravity"].cast<float>();
+  if (d.contains("masscart")) p.masscart = d["masscart"].cast<float>();
+  if (d.contains("masspole")) p.masspole = d["masspole"].cast<float>();
+  if (d.contains("length")) p.length = d["length"].cast<float>();
+  if (d.contains("force_mag")) p.force_mag = d["force_mag"].cast<float>();
+  if (d.contains("tau")) p.tau = d["tau"].cast<float>();
+  if (d.contains("x_threshold")) p.x_threshold = d["x_threshold"].cast<float>();
+  if (d.contains("theta_threshold")) p.theta_threshold = d["theta_threshold"].cast<float>();
+  if (d.contains("init_range")) p.init_range = d["init_range"].cast<float>();
+  if (d.contains("max_steps")) p.max_steps = d["max_steps"].cast<int>();
+  return p;
+}
+
+}  // namespace
+
+void register_kernel_ops(py::module_& m) {
+  // ---------------- environments ----------------
+  m.def("cartpole_reset",
+        [](at::Tensor state, at::Tensor ep_len, at::Tensor ep_ret, at::Tensor ep_count, uint64_t seed, float range) {
+          need(state, at::kFloat, "state");
+          need(ep_len, at::kInt, "ep_len");
+          need(ep_ret, at::kFloat, "ep_ret");
+          need(ep_count, at::kInt, "ep_count");
+          const int n = static_cast<int>(ep_len.numel());
+          TB_CHECK(state.numel() == 4LL * n, "state must be [N, 4]");
+          cuda_ok(tb_cartpole_reset(state.data_ptr<float>(), ep_len.data_ptr<int>(), ep_ret.data_ptr<float>(),
+                                    reinterpret_cast<unsigned*>(ep_count.data_ptr<int>()), n, seed, range,
+                                    stream_of(state)),
+                  "cartpole_reset");
+        },
+        py::arg("state"), py::arg("ep_len"), py::arg("ep_ret"), py::arg("ep_count"), py::arg("seed"),
+        py::arg("init_range") = 0.05f);
+
+  m.def("ppo_cartpole_act_step",
+        [](at::Tensor logits, at::Tensor values, at::Tensor state, at::Tensor ep_len, at::Tensor ep_ret,
+           at::Tensor ep_count, at::Tensor stats, at::Tensor obs_buf, at::Tensor act_buf, at::Tensor logp_buf,
+           at::Tensor val_buf, at::Tensor rew_buf, at::Tensor done_buf, py::object iter_ptr, int t,
+           uint64_t policy_seed, uint64_t env_seed, py::dict params) {
+          need(logits, at::kFloat, "logits");
+          need(values, at::kFloat, "values");
+          need(state, at::kFloat, "state");
+          need(obs_buf, at::kFloat, "obs_buf");
+          need(act_buf, at::kInt, "act_buf");
+          need(logp_buf, at::kFloat, "logp_buf");
+          need(val_buf, at::kFloat, "val_buf");
+          need(rew_buf, at::kFloat, "rew_buf");
+          TB_CHECK(done_buf.is_cuda() && done_buf.element_size() == 1 && done_buf.is_contiguous(), "done_buf u8");
+          const int n = static_cast<int>(state.size(0));
+          const int A = static_cast<int>(logits.size(1));
+          TB_CHECK(logits.size(0) == n && values.numel() == n, "logits/values batch mismatch");
+          TB_CHECK(obs_buf.dim() == 3 && obs_buf.size(1) == n && t >= 0 && t < obs_buf.size(0), "obs_buf [T, N, 4]");
+          const long long* ip = nullptr;
+          if (!iter_ptr.is_none()) {
+            at::Tensor it = iter_ptr.cast<at::Tensor>();
+            need(it, at::kLong, "iter");
+            ip = reinterpret_cast<const long long*>(it.data_ptr<int64_t>());
+          }
+          cuda_ok(tb_ppo_cartpole_act_step(
+                      logits.data_ptr<float>(), A, values.data_ptr<float>(), state.data_ptr<float>(),
+                      ep_len.data_ptr<int>(), ep_ret.data_ptr<float>(),
+                      reinterpret_cast<unsigned*>(ep_count.data_ptr<int>()), stats.data_ptr<float>(),
+                      obs_buf.data_ptr<float>(), act_buf.data_ptr<int>(), logp_buf.data_ptr<float>(),
+                      val_buf.data_ptr<float>(), rew_buf.data_ptr<float>(),
+                      static_cast<uint8_t*>(done_buf.data_ptr()), ip, t, n, policy_seed, env_seed, cp_params(params),
+                      stream_of(state)),
+                  "ppo_cartpole_act_step");
+        });
+
+  // ---------------- replay ----------------
+  m.def("sample_indices",
+        [](int64_t n, int64_t size, uint64_t seed, uint64_t counter, at::Device dev) {
+          at::Tensor idx = at::empty({n}, at::TensorOptions().dtype(at::kInt).device(dev));
+          cuda_ok(tb_sample_indices(idx.data_ptr<int>(), static_cast<int>(n), size, seed, counter, stream_of(idx)),
+                  "sample_indices");
+          return idx;
+        });
+
+  // Pushes rows of several tensors (each [B, ...], same B) into ring tensors
+  // ([cap, ...]) at slots (head + i) mod cap, in one launch.
+  m.def("ring_push",
+        [](std::vector<at::Tensor> src, std::vector<at::Tensor> dst, int64_t head) {
+          TB_CHECK(src.size() == dst.size() && !src.empty() && src.size() <= TB_MAX_FIELDS, "field count");
+          const int64_t B = src[0].size(0), cap = dst[0].size(0);
+          TbFieldSet fs{};
+          for (size_t k = 0; k < src.size(); ++k) {
+            TB_CHECK(src[k].is_cuda() && dst[k].is_cuda() && src[k].is_contiguous() && dst[k].is_contiguous(),
+                     "ring_push needs contiguous CUDA tensors");
+            TB_CHECK(src[k].size(0) == B && dst[k].size(0) == cap, "ring_push row count mismatch");
+            TB_CHECK(src[k].scalar_type() == dst[k].scalar_type(), "ring_push dtype mismatch");
+            const int64_t rb = src[k].numel() / std::max<int64_t>(B, 1) * src[k].element_size();
+            TB_CHECK(rb == dst[k].numel() / cap * dst[k].element_size(), "ring_push row size mismatch");
+            fs.f[k] = TbField{src[k].data_ptr(), dst[k].data_ptr(), static_cast<int>(rb)};
+          }
+          cuda_ok(tb_ring_push(fs, static_cast<int>(src.size()), static_cast<int>(B), head, cap, stream_of(src[0])),
+                  "ring_push");
+        });
+
+  m.def("ring_gather",
+        [](std::vector<at::Tensor> src, std::vector<at::Tensor> dst, at::Tensor idx) {
+          TB_CHECK(src.size() == dst.size() && !src.empty() && src.size() <= TB_MAX_FIELDS, "field count");
+          need(idx, at::kInt, "idx");
+          const int64_t B = idx.numel();
+          TbFieldSet fs{};
+          for (size_t k = 0; k < src.size(); ++k) {
+            TB_CHECK(src[k].is_contiguous() && dst[k].is_contiguous() && dst[k].size(0) == B, "ring_gather shapes");
+            const int64_t rb = dst[k].numel() / std::max<int64_t>(B, 1) * dst[k].element_size();
+            fs.f[k] = TbField{src[k].data_ptr(), dst[k].data_ptr(), static_cast<int>(rb)};
+          }
+          cuda_ok(tb_ring_gather(fs, static_cast<int>(src.size()), static_cast<int>(B), idx.data_ptr<int>(),
+                                 stream_of(idx)),
+                  "ring_gather");
+        });
+
+  m.def("per_update",
+        [](at::Tensor tree, at::Tensor idx, at::Tensor prio, float alpha, float eps, int64_t capacity) {
+          need(tree, at::kFloat, "tree");
+          need(idx, at::kLong, "idx");
+          need(prio, at::kFloat, "prio");
+          const int64_t L = tree.numel() / 2;
+          cuda_ok(tb_per_update(tree.data_ptr<float>(), L, reinterpret_cast<const long long*>(idx.data_ptr<int64_t>()), prio.data_ptr<float>(),
+                                static_cast<int>(idx.numel()), alpha, eps, capacity, nullptr, stream_of(tree)),
+                  "per_update");
+        });
+
+  m.def("per_rebuild", [](at::Tensor tree) {
+    need(tree, at::kFloat, "tree");
+    cuda_ok(tb_per_rebuild(tree.data_ptr<float>(), tree.numel() / 2, stream_of(tree)), "per_rebuild");
+  });
+
+  m.def("per_sample",
+        [](at::Tensor tree, int64_t size, int64_t n, float beta, uint64_t seed, uint64_t counter) {
+          need(tree, at::kFloat, "tree");
+          auto o = tree.options();
+          at::Tensor idx = at::empty({n}, o.dtype(at::kLong));
+          at::Tensor w = at::empty({n}, o.dtype(at::kFloat));
+          at::Tensor p = at::empty({n}, o.dtype(at::kFloat));
+          at::Tensor mx = at::empty({1}, o.dtype(at::kInt));
+          cuda_ok(tb_per_sample(tree.data_ptr<float>(), tree.numel() / 2, size, static_cast<int>(n), beta, seed,
+                                counter, reinterpret_cast<long long*>(idx.data_ptr<int64_t>()), w.data_ptr<float>(), p.data_ptr<float>(),
+                                reinterpret_cast<unsigned*>(mx.data_ptr<int>()), stream_of(tree)),
+                  "per_sample");
+          return py::make_tuple(idx, w, p);
+        });
+
+  // ---------------- advantages ----------------
+  m.def("gae_scratch_numel", [](int T, int N) { return static_cast<int64_t>(tb_gae_scratch_bytes(T, N) / 4); });
+  m.def("gae",
+        [](at::Tensor rew, at::Tensor val, at::Tensor done, at::Tensor adv, at::Tensor ret, py::object stats,
+           py::object scratch, float gamma, float lam) {
+          need(rew, at::kFloat, "rewards");
+          need(val, at::kFloat, "values");
+          need(adv, at::kFloat, "advantages");
+          need(ret, at::kFloat, "returns");
+          TB_CHECK(done.is_cuda() && done.element_size() == 1 && done.is_contiguous(), "done must be bool/u8");
+          TB_CHECK(rew.dim() == 2, "rewards must be [T, N]");
+          const int T = static_cast<int>(rew.size(0)), N = static_cast<int>(rew.size(1));
+          TB_CHECK(val.numel() == static_cast<int64_t>(T + 1) * N, "values must be [T+1, N]");
+          TB_CHECK(done.numel() == static_cast<int64_t>(T) * N && adv.numel() == rew.numel() &&
+                       ret.numel() == rew.numel(),
+                   "shape mismatch");
+          double* sp = nullptr;
+          if (!stats.is_none()) {
+            at::Tensor s = stats.cast<at::Tensor>();
+            need(s, at::kDouble, "stats");
+            sp = s.data_ptr<double>();
+          }
+          at::Tensor scr;
+          const size_t need_bytes = tb_gae_scratch_bytes(T, N);
+          if (need_bytes > 0) {
+            if (!scratch.is_none()) {
+              scr = scratch.cast<at::Tensor>();
+              need(scr, at::kFloat, "scratch");
+              TB_CHECK(static_cast<size_t>(scr.numel()) * 4 >= need_bytes, "scratch too small");
+            } else {
+              scr = at::empty({static_cast<int64_t>(need_bytes / 4)}, rew.options());
+            }
+          }
+          cuda_ok(tb_gae(rew.data_ptr<float>(), val.data_ptr<float>(), static_cast<const uint8_t*>(done.data_ptr()),
+                         adv.data_ptr<float>(), ret.data_ptr<float>(), sp,
+                         scr.defined() ? scr.data_ptr<float>() : nullptr, T, N, gamma, lam, stream_of(rew)),
+                  "gae");
+        },
+        py::arg("rewards"), py::arg("values"), py::arg("dones"), py::arg("advantages"), py::arg("returns"),
+        py::arg("stats") = py::none(), py::arg("scratch") = py::none(), py::arg("gamma") = 0.99f,
+        py::arg("lam") = 0.95f);
+
+  m.def("grpo_advantage",
+        [](at::Tensor rewards, int G, float eps, bool scale_by_std) {
+          need(rewards, at::kFloat, "rewards");
+          TB_CHECK(G > 0 && rewards.numel() % G == 0, "rewards must be a multiple of the group size");
+          at::Tensor adv = at::empty_like(rewards);
+          cuda_ok(tb_grpo_advantage(rewards.data_ptr<float>(), adv.data_ptr<float>(),
+                                    static_cast<int>(rewards.numel() / G), G, eps, scale_by_std ? 1 : 0,
+                                    stream_of(rewards)),
+                  "grpo_advantage");
+          return adv;
+        },
+        py::arg("rewards"), py::arg("group_size"), py::arg("eps") = 1e-4f, py::arg("scale_by_std") = true);
+
+  // ---------------- PPO ----------------
+  m.def("ppo_gather",
+        [](at::Tensor obs, at::Tensor act, at::Tensor logp, at::Tensor adv, at::Tensor ret, at::Tensor val,
+           py::object adv_stats, at::Tensor o_obs, at::Tensor o_act, at::Tensor o_logp, at::Tensor o_adv,
+           at::Tensor o_ret, py::object o_val, int n_mb, py::object step_ptr, py::object iter_ptr, int64_t step,
+           uint64_t seed, bool normalize) {
+          need(obs, at::kFloat, "obs");
+          need(act, at::kInt, "act");
+          const int total = static_cast<int>(act.numel());
+          const int obs_dim = static_cast<int>(obs.numel() / total);
+          const int mb = static_cast<int>(o_act.numel());
+          const double* sp = nullptr;
+          if (!adv_stats.is_none()) sp = adv_stats.cast<at::Tensor>().data_ptr<double>();
+          float* ov = o_val.is_none() ? nullptr : o_val.cast<at::Tensor>().data_ptr<float>();
+          const long long* stp = step_ptr.is_none()
+                                     ? nullptr
+                                     : reinterpret_cast<const long long*>(step_ptr.cast<at::Tensor>().data_ptr<int64_t>());
+          const long long* itp = iter_ptr.is_none()
+                                     ? nullptr
+                                     : reinterpret_cast<const long long*>(iter_ptr.cast<at::Tensor>().data_ptr<int64_t>());
+          cuda_ok(tb_ppo_gather(obs.data_ptr<float>(), obs_dim, act.data_ptr<int>(), logp.data_ptr<float>(),
+                                adv.data_ptr<float>(), ret.data_ptr<float>(), val.data_ptr<float>(), sp,
+                                o_obs.data_ptr<float>(), o_act.data_ptr<int>(), o_logp.data_ptr<float>(),
+                                o_adv.data_ptr<float>(), o_ret.data_ptr<float>(), ov, total, mb, n_mb, stp, itp, step,
+                                seed, normalize ? 1 : 0, stream_of(obs)),
+                  "ppo_gather");
+        });
+
+  m.def("ppo_loss",
+        [](at::Tensor logits, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv, at::Tensor ret,
+           py::object old_val, at::Tensor dlogits, at::Tensor dvalue, py::object stats, float clip, float vclip,
+           float vf_coef, float ent_coef) {
+          need(logits, at::kFloat, "logits");
+          need(value, at::kFloat, "value");
+          need(act, at::kInt, "act");
+          need(dlogits, at::kFloat, "dlogits");
+          need(dvalue, at::kFloat, "dvalue");
+          const int B = static_cast<int>(act.numel());
+          const int A = static_cast<int>(logits.numel() / B);
+          const float* ov = old_val.is_none() ? nullptr : old_val.cast<at::Tensor>().data_ptr<float>();
+          float* sp = stats.is_none() ? nullptr : stats.cast<at::Tensor>().data_ptr<float>();
+          cuda_ok(tb_ppo_loss(logits.data_ptr<float>(), A, value.data_ptr<float>(), act.data_ptr<int>(),
+                              old_logp.data_ptr<float>(), adv.data_ptr<float>(), ret.data_ptr<float>(), ov,
+                              dlogits.data_ptr<float>(), dvalue.data_ptr<float>(), sp, B, clip, vclip, vf_coef,
+                              ent_coef, stream_of(logits)),
+                  "ppo_loss");
+        });
+
+  m.def("counter_add", [](at::Tensor c, int64_t v) {
+    need(c, at::kLong, "counter");
+    cuda_ok(tb_counter_add(reinterpret_cast<long long*>(c.data_ptr<int64_t>()), v, stream_of(c)), "counter_add");
+  });
+
+  // ---------------- optimizer / elementwise ----------------
+  m.def("adam",
+        [](at::Tensor p, at::Tensor g, at::Tensor m1, at::Tensor m2, py::object p_bf16, float lr, float b1, float b2,
+           float eps, float wd, float grad_scale, float max_norm, py::object step_ptr, int64_t step,
+           py::object gnorm_sq) {
+          need(p, at::kFloat, "param");
+          need(g, at::kFloat, "grad");
+          need(m1, at::kFloat, "exp_avg");
+          need(m2, at::kFloat, "exp_avg_sq");
+          TB_CHECK(g.numel() == p.numel() && m1.numel() == p.numel() && m2.numel() == p.numel(), "adam sizes");
+          void* pb = nullptr;
+          if (!p_bf16.is_none()) {
+            at::Tensor b = p_bf16.cast<at::Tensor>();
+            need(b, at::kBFloat16, "p_bf16");
+            TB_CHECK(b.numel() == p.numel(), "p_bf16 size");
+            pb = b.data_ptr();
+          }
+          const long long* sp = step_ptr.is_none()
+                                    ? nullptr
+                                    : reinterpret_cast<const long long*>(step_ptr.cast<at::Tensor>().data_ptr<int64_t>());
+          const float* gn = gnorm_sq.is_none() ? nullptr : gnorm_sq.cast<at::Tensor>().data_ptr<float>();
+          TbAdamParams hp{lr, b1, b2, eps, wd, grad_scale, max_norm, step};
+          cuda_ok(tb_adam(p.data_ptr<float>(), g.data_ptr<float>(), m1.data_ptr<float>(), m2.data_ptr<float>(), pb,
+                          p.numel(), hp, sp, gn, stream_of(p)),
+                  "adam");
+        },
+        py::arg("param"), py::arg("grad"), py::arg("exp_avg"), py::arg("exp_avg_sq"), py::arg("param_bf16") = py::none(),
+        py::arg("lr") = 3e-4f, py::arg("beta1") = 0.9f, py::arg("beta2") = 0.999f, py::arg("eps") = 1e-8f,
+        py::arg("weight_decay") = 0.0f, py::arg("grad_scale") = 1.0f, py::arg("max_grad_norm") = 0.0f,
+        py::arg("step_ptr") = py::none(), py::arg("step") = 0, py::arg("gnorm_sq") = py::none());
+
+  m.def("sumsq", [](at::Tensor x, at::Tensor out) {
+    need(x, at::kFloat, "x");
+    need(out, at::kFloat, "out");
+    cuda_ok(tb_sumsq(x.data_ptr<float>(), x.numel(), out.data_ptr<float>(), stream_of(x)), "sumsq");
+  });
+
+  m.def("elementwise",
+        [](at::Tensor out, py::object x, py::object y, float a, int op) {
+          need(out, at::kFloat, "out");
+          const float* xp = x.is_none() ? nullptr : x.cast<at::Tensor>().data_ptr<float>();
+          const float* yp = y.is_none() ? nullptr : y.cast<at::Tensor>().data_ptr<float>();
+          cuda_ok(tb_elementwise(out.data_ptr<float>(), xp, yp, out.numel(), a, op, stream_of(out)), "elementwise");
+        });
+
+  // ---------------- rewards ----------------
+  m.def("hash_reward", [](at::Tensor ids, at::Tensor lens) {
+    need(ids, at::kInt, "ids");
+    need(lens, at::kInt, "lens");
+    at::Tensor out = at::empty({ids.size(0)}, ids.options().dtype(at::kFloat));
+    cuda_ok(tb_hash_reward(ids.data_ptr<int>(), lens.data_ptr<int>(), static_cast<int>(ids.size(0)),
+                           static_cast<int>(ids.size(1)), out.data_ptr<float>(), stream_of(ids)),
+            "hash_reward");
+    return out;
+  });
+}

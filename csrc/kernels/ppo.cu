@@ -1,0 +1,244 @@
+// PPO training-side kernels for vectorized-env policies:
+//   * minibatch gather through an on-device random permutation (a Feistel
+//     bijection with cycle walking), fused with global advantage normalization;
+//   * the categorical clipped-surrogate loss with value loss and entropy bonus,
+//     forward and backward in one pass (one thread per sample);
+//   * device counters that CUDA-graph-captured loops read instead of host
+//     immediates.
+//
+// The loss follows Schulman et al., "Proximal Policy Optimization Algorithms"
+// (2017), eq. 7 and 9.  The reference's PolicyEngine::Update
+// (turbol_vllm/src/policy/policy_engine.cpp:103-138) is REINFORCE with no clip;
+// its Gaussian mode is kept in the Python engine, this kernel is the PPO path.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace {
+
+constexpr int kBlock = 256;
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+  // integer finaliser (Murmur3 fmix32)
+  x ^= x >> 16;
+  x *= 0x85ebca6bu;
+  x ^= x >> 13;
+  x *= 0xc2b2ae35u;
+  x ^= x >> 16;
+  return x;
+}
+
+// Bijection on [0, 2^bits) (balanced/unbalanced Feistel, 4 rounds), walked
+// until it lands in [0, M).  M <= 2^bits < 2M, so the expected number of
+// walks is below 2.
+__device__ __forceinline__ uint32_t feistel_perm(uint32_t x, uint32_t M, int bits, uint32_t key) {
+  const int lb = bits / 2, rb = bits - lb;
+  const uint32_t lmask = (1u << lb) - 1u, rmask = (1u << rb) - 1u;
+  do {
+    uint32_t l = x >> rb, r = x & rmask;
+    // 4 rounds; the halves alternate widths, so use an even round count
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if ((k & 1) == 0) {
+        const uint32_t nl = (l ^ mix32(r ^ (key + k * 0x9E3779B9u))) & lmask;
+        l = nl;
+      } else {
+        const uint32_t nr = (r ^ mix32(l ^ (key + k * 0x9E3779B9u))) & rmask;
+        r = nr;
+      }
+    }
+    x = (l << rb) | r;
+  } while (x >= M);
+  return x;
+}
+
+// Gathers minibatch `mb` of epoch `epoch` (read from a device counter when
+// step_ptr != null: step = epoch * n_mb + mb).
+__global__ void ppo_gather_kernel(const float* __restrict__ obs, int obs_dim, const int* __restrict__ act,
+                                  const float* __restrict__ logp, const float* __restrict__ adv,
+                                  const float* __restrict__ ret, const float* __restrict__ val,
+                                  const double* __restrict__ adv_stats, float* __restrict__ o_obs,
+                                  int* __restrict__ o_act, float* __restrict__ o_logp, float* __restrict__ o_adv,
+                                  float* __restrict__ o_ret, float* __restrict__ o_val, int total, int bits,
+                                  int mb_size, int n_mb, const long long* __restrict__ step_ptr,
+                                  const long long* __restrict__ iter_ptr, long long step_imm,
+                                  unsigned long long seed, int normalize) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= mb_size) return;
+  const long long step = step_ptr ? *step_ptr : step_imm;
+  const long long it = iter_ptr ? *iter_ptr : 0;
+  const int epoch = static_cast<int>(step / n_mb), mb = static_cast<int>(step % n_mb);
+  const uint32_t key = mix32(static_cast<uint32_t>(seed) ^ mix32(static_cast<uint32_t>(it) * 0x27d4eb2fu) ^
+                             mix32(static_cast<uint32_t>(epoch) + 0x165667b1u));
+  const uint32_t pos = static_cast<uint32_t>(mb) * mb_size + i;
+  const uint32_t j = feistel_perm(pos, static_cast<uint32_t>(total), bits, key);
+  for (int k = 0; k < obs_dim; ++k)
+    o_obs[static_cast<size_t>(i) * obs_dim + k] = obs[static_cast<size_t>(j) * obs_dim + k];
+  o_act[i] = act[j];
+  o_logp[i] = logp[j];
+  float a = adv[j];
+  if (normalize && adv_stats != nullptr) {
+    const double n = static_cast<double>(total);
+    const double mean = adv_stats[0] / n;
+    double var = (adv_stats[1] - n * mean * mean) / fmax(n - 1.0, 1.0);
+    var = var > 0.0 ? var : 0.0;
+    a = static_cast<float>((static_cast<double>(a) - mean) / (sqrt(var) + 1e-8));
+  }
+  o_adv[i] = a;
+  o_ret[i] = ret[j];
+  if (o_val) o_val[i] = val[j];
+}
+
+// Categorical PPO loss.  Per sample:
+//   logp = l[a] - lse(l), ratio = exp(logp - old), pg = -min(ratio*A, clip(ratio)*A)
+//   v    = 0.5 * (V - R)^2  (or the clipped-value max form when vclip > 0)
+//   H    = -sum p log p
+//   loss = mean(pg) + vf_coef * mean(v) - ent_coef * mean(H)
+// Writes d loss / d logits and d loss / d V (already divided by B) and adds
+// [pg, v, H, approx_kl, clipfrac] sums into stats[0..4].
+template <int A>
+__global__ void ppo_loss_kernel(const float* __restrict__ logits, const float* __restrict__ value,
+                                const int* __restrict__ act, const float* __restrict__ old_logp,
+                                const float* __restrict__ adv, const float* __restrict__ ret,
+                                const float* __restrict__ old_val, float* __restrict__ dlogits,
+                                float* __restrict__ dvalue, float* __restrict__ stats, int B, float clip,
+                                float vclip, float vf_coef, float ent_coef) {
+  __shared__ float red[kBlock / 32];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  float s_pg = 0.f, s_v = 0.f, s_h = 0.f, s_kl = 0.f, s_cf = 0.f;
+  if (i < B) {
+    float l[A], p[A];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      l[k] = logits[static_cast<size_t>(i) * A + k];
+      mx = fmaxf(mx, l[k]);
+    }
+    float se = 0.f;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      p[k] = __expf(l[k] - mx);
+      se += p[k];
+    }
+    const float inv = 1.f / se, lse = mx + __logf(se);
+    float H = 0.f;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      p[k] *= inv;
+      H -= p[k] * (l[k] - lse);
+    }
+    const int a = act[i];
+    const float lp = l[a] - lse;
+    const float lr = lp - old_logp[i];
+    const float ratio = __expf(lr);
+    const float Ad = adv[i];
+    const float un = ratio * Ad;
+    const float rc = fminf(fmaxf(ratio, 1.f - clip), 1.f + clip);
+    const float cl = rc * Ad;
+    const bool use_unclipped = un <= cl || (ratio > 1.f - clip && ratio < 1.f + clip);
+    const float pg = -fminf(un, cl);
+    const float dlp = use_unclipped ? -Ad * ratio : 0.f;  // d pg / d logp
+
+    const float V = value[i], R = ret[i];
+    float vl, dv;
+    if (vclip > 0.f && old_val != nullptr) {
+      const float ov = old_val[i];
+      const float vc = ov + fminf(fmaxf(V - ov, -vclip), vclip);
+      const float e1 = (V - R) * (V - R), e2 = (vc - R) * (vc - R);
+      if (e1 >= e2) {
+        vl = 0.5f * e1;
+        dv = V - R;
+      } else {
+        vl = 0.5f * e2;
+        dv = (fabsf(V - ov) < vclip) ? (vc - R) : 0.f;
+      }
+    } else {
+      vl = 0.5f * (V - R) * (V - R);
+      dv = V - R;
+    }
+    const float scale = 1.f / static_cast<float>(B);
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      const float logpk = l[k] - lse;
+      // d(logp_a)/d l_k = [k==a] - p_k ;  dH/dl_k = -p_k (log p_k + H)
+      const float g = dlp * ((k == a ? 1.f : 0.f) - p[k]) + ent_coef * p[k] * (logpk + H);
+      dlogits[static_cast<size_t>(i) * A + k] = g * scale;
+    }
+    dvalue[i] = vf_coef * dv * scale;
+    s_pg = pg;
+    s_v = vl;
+    s_h = H;
+    s_kl = (ratio - 1.f) - lr;  // k3 estimator of KL(old || new)
+    s_cf = fabsf(ratio - 1.f) > clip ? 1.f : 0.f;
+  }
+  if (stats) {
+    s_pg = tb::block_sum(s_pg, red);
+    s_v = tb::block_sum(s_v, red);
+    s_h = tb::block_sum(s_h, red);
+    s_kl = tb::block_sum(s_kl, red);
+    s_cf = tb::block_sum(s_cf, red);
+    if (threadIdx.x == 0) {
+      atomicAdd(&stats[0], s_pg);
+      atomicAdd(&stats[1], s_v);
+      atomicAdd(&stats[2], s_h);
+      atomicAdd(&stats[3], s_kl);
+      atomicAdd(&stats[4], s_cf);
+      atomicAdd(&stats[5], static_cast<float>(min(B - static_cast<int>(blockIdx.x) * kBlock, kBlock)));
+    }
+  }
+}
+
+__global__ void counter_add_kernel(long long* c, long long v) { *c += v; }
+
+}  // namespace
+
+extern "C" {
+
+int tb_ppo_gather(const float* obs, int obs_dim, const int* act, const float* logp, const float* adv, const float* ret,
+                  const float* val, const double* adv_stats, float* o_obs, int* o_act, float* o_logp, float* o_adv,
+                  float* o_ret, float* o_val, int total, int mb_size, int n_mb, const long long* step_ptr,
+                  const long long* iter_ptr, long long step_imm, unsigned long long seed, int normalize,
+                  cudaStream_t s) {
+  if (mb_size <= 0) return 0;
+  if (static_cast<long long>(mb_size) * n_mb > total) return static_cast<int>(cudaErrorInvalidValue);
+  int bits = 1;
+  while ((1LL << bits) < total) ++bits;
+  ppo_gather_kernel<<<(mb_size + kBlock - 1) / kBlock, kBlock, 0, s>>>(
+      obs, obs_dim, act, logp, adv, ret, val, adv_stats, o_obs, o_act, o_logp, o_adv, o_ret, o_val, total, bits,
+      mb_size, n_mb, step_ptr, iter_ptr, step_imm, seed, normalize);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,
+                const float* adv, const float* ret, const float* old_val, float* dlogits, float* dvalue, float* stats,
+                int B, float clip, float vclip, float vf_coef, float ent_coef, cudaStream_t s) {
+  if (B <= 0) return 0;
+  const int g = (B + kBlock - 1) / kBlock;
+#define TB_PPO_CASE(K)                                                                                          \
+  case K:                                                                                                       \
+    ppo_loss_kernel<K><<<g, kBlock, 0, s>>>(logits, value, act, old_logp, adv, ret, old_val, dlogits, dvalue,   \
+                                            stats, B, clip, vclip, vf_coef, ent_coef);                          \
+    break;
+  switch (A) {
+    TB_PPO_CASE(2)
+    TB_PPO_CASE(3)
+    TB_PPO_CASE(4)
+    TB_PPO_CASE(6)
+    TB_PPO_CASE(8)
+    TB_PPO_CASE(16)
+    default:
+      return static_cast<int>(cudaErrorInvalidValue);
+  }
+#undef TB_PPO_CASE
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_counter_add(long long* counter, long long v, cudaStream_t s) {
+  counter_add_kernel<<<1, 1, 0, s>>>(counter, v);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+"""Build the native core of turbol_b200 in-tree.
+
+    python setup.py build_ext --inplace
+
+One extension, ``turbol_b200.turbol_core``, holds both the C++ host runtime
+(Tensor/Config/engines/profiler/writers/bootstrap store/pybind11 bindings) and
+the hand-written CUDA kernels.  Every ``.cu`` file is compiled for sm_100a only:
+the ``-gencode`` flag below makes ``torch.utils.cpp_extension`` skip its own
+arch list.  Kernel sources include no torch headers, so they compile in seconds;
+only the binding/engine ``.cpp`` files pay for the torch headers.
+"""
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def sources():
+    pats = ["csrc/core/*.cpp", "csrc/engines/*.cpp", "csrc/bindings/*.cpp", "csrc/kernels/*.cu"]
+    out = []
+    for p in pats:
+        out += sorted(glob.glob(os.path.join(ROOT, p)))
+    return [os.path.relpath(s, ROOT) for s in out]
+
+
+nvcc_flags = ARCH + [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas=-v" if os.environ.get("TURBOL_PTXAS_VERBOSE") else "-Xptxas=-O3",
+    "-DTURBOL_CUDA=1",
+]
+cxx_flags = ["-O3", "-std=c++17", "-DTURBOL_CUDA=1", "-Wno-unused-function"]
+
+ext = CUDAExtension(
+    name="turbol_b200.turbol_core",
+    sources=sources(),
+    include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")],
+    extra_compile_args={"cxx": cxx_flags, "nvcc": nvcc_flags},
+    libraries=["nccl"] if os.environ.get("TURBOL_LINK_NCCL") else [],
+    # Link the C++ runtime dynamically: a toolchain whose libstdc++.so link is
+    # missing falls back to libstdc++.a, and a private static copy of the
+    # iostream/locale machinery inside this library crashes on the first
+    # number it formats (its facet ids differ from the process's libstdc++).
+    extra_link_args=["-l:libstdc++.so.6"],
+)
+
+setup(
+    name="turbol_b200",
+    version="0.1.0",
+    packages=["turbol_b200"],
+    ext_modules=[ext],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

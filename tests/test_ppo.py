@@ -1,0 +1,135 @@
+"""PPO: fused loss kernel and Adam kernel vs autograd/fp32 oracles; the
+on-device permutation; end-to-end learning on CPU and GPU."""
+import pytest
+import torch
+
+import turbol_b200 as turbol
+from turbol_b200._native import ops
+from turbol_b200.ops import reference as ref
+from turbol_b200.ops.rl import FusedAdam, ppo_categorical_loss
+from turbol_b200.rl.ppo import PPOConfig, PPOTrainer
+
+
+def test_ppo_cpu_learns_cartpole():
+    cfg = PPOConfig(num_envs=64, rollout_steps=32, minibatch_size=256, hidden=(64, 64), seed=1)
+    tr = PPOTrainer(cfg, device="cpu")
+    first = None
+    for i in range(25):
+        tr.train_iteration()
+        if i == 2:
+            first = tr.metrics()["mean_return"]
+    tr.metrics()
+    for _ in range(3):
+        tr.train_iteration()
+    last = tr.metrics()["mean_return"]
+    assert last > 2 * first and last > 60, (first, last)
+
+
+def test_policy_engine_reference_api():
+    pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu")
+    assert pe.initialize().ok()
+    obs = turbol.Tensor([8, 4], "float32", "cpu")
+    a, lp = turbol.Tensor(), turbol.Tensor()
+    assert pe.forward(obs, a, lp).ok()
+    assert a.shape().to_list() == [8, 2] and lp.shape().to_list() == [8]
+    assert float(a.torch().abs().max()) <= 1.0
+    v = turbol.Tensor()
+    assert pe.get_value(obs, v).ok() and v.shape().to_list() == [8]
+    act, logp = pe.forward(obs)  # README form
+    batch = torch.randn(8, 4 + 2 + 2)
+    before = pe.net.fp.flat.clone()
+    assert pe.update(turbol.from_torch(batch)).ok()
+    assert not torch.equal(before, pe.net.fp.flat)
+
+
+def test_policy_engine_discrete_ppo_update():
+    pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu", hidden=(32,), discrete=True)
+    pe.initialize()
+    obs = torch.randn(16, 4)
+    act, logp = pe.forward(obs)
+    batch = torch.cat([obs, act[:, None].float(), torch.randn(16, 1), torch.randn(16, 1), logp[:, None]], 1)
+    assert pe.update(batch).ok()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("A", [2, 3, 8])
+def test_ppo_loss_kernel_grads(A, dev):
+    B = 5000
+    g = torch.Generator().manual_seed(A)
+    logits = torch.randn(B, A, generator=g)
+    value = torch.randn(B, generator=g)
+    act = torch.randint(0, A, (B,), generator=g, dtype=torch.int32)
+    old = torch.log_softmax(logits + 0.3 * torch.randn(B, A, generator=g), -1).gather(1, act.long()[:, None]).squeeze(1)
+    adv = torch.randn(B, generator=g)
+    ret = torch.randn(B, generator=g)
+    lr_, vr = logits.clone().double().requires_grad_(), value.clone().double().requires_grad_()
+    loss, st = ref.ppo_categorical_loss(lr_, vr, act, old.double(), adv.double(), ret.double(), 0.2, 0.5, 0.01)
+    loss.backward()
+    stats = torch.zeros(8, device=dev)
+    lg = logits.to(dev).requires_grad_()
+    vg = value.to(dev).requires_grad_()
+    out = ppo_categorical_loss(lg, vg, act.to(dev), old.to(dev), adv.to(dev), ret.to(dev), 0.2, 0.5, 0.01,
+                               stats=stats)
+    out.backward()
+    assert torch.allclose(lg.grad.cpu().double(), lr_.grad, atol=1e-6, rtol=1e-4)
+    assert torch.allclose(vg.grad.cpu().double(), vr.grad, atol=1e-7, rtol=1e-4)
+    s = stats.cpu().double()
+    assert torch.allclose(s[:6], st.double(), rtol=1e-3, atol=1e-2)
+
+
+@pytest.mark.gpu
+def test_adam_kernel_matches_reference(dev):
+    n = 100003
+    g = torch.Generator().manual_seed(0)
+    p = torch.randn(n, generator=g)
+    opt = FusedAdam(p.clone().to(dev), torch.zeros(n, device=dev), lr=1e-3, weight_decay=0.01, bf16_shadow=True)
+    pr, m, v = p.clone().double(), torch.zeros(n, dtype=torch.float64), torch.zeros(n, dtype=torch.float64)
+    for step in range(1, 6):
+        grad = torch.randn(n, generator=g)
+        opt.g.copy_(grad.to(dev))
+        opt.step(grad_scale=0.5)
+        ref.adam_step(pr, grad.double(), m, v, step, 1e-3, 0.9, 0.999, 1e-8, 0.01, 0.5)
+    assert torch.allclose(opt.p.cpu().double(), pr, atol=1e-6)
+    assert torch.allclose(opt.shadow.float().cpu(), opt.p.cpu(), rtol=1e-2, atol=1e-3)
+    assert int(opt.step_t.item()) == 5
+
+
+@pytest.mark.gpu
+def test_gather_permutation_covers_batch(dev):
+    T, N, MB = 8, 512, 1024
+    total = T * N
+    obs = torch.arange(total * 4, dtype=torch.float32, device=dev).view(T, N, 4)
+    act = torch.arange(total, dtype=torch.int32, device=dev).view(T, N)
+    f = torch.arange(total, dtype=torch.float32, device=dev).view(T, N)
+    outs = [torch.empty(MB, 4, device=dev), torch.empty(MB, dtype=torch.int32, device=dev)] + \
+        [torch.empty(MB, device=dev) for _ in range(3)]
+    seen = []
+    n_mb = total // MB
+    for step in range(n_mb):
+        ops().ppo_gather(obs, act, f, f, f, f, None, outs[0], outs[1], outs[2], outs[3], outs[4], None, n_mb, None,
+                         None, step, 1234, False)
+        seen.append(outs[1].cpu().clone())
+        assert torch.equal(outs[0][:, 0].long().cpu(), outs[1].long().cpu() * 4)
+        assert torch.equal(outs[2].cpu(), outs[1].float().cpu())
+    allidx = torch.cat(seen)
+    assert torch.equal(torch.sort(allidx).values, torch.arange(total, dtype=torch.int32))
+    assert not torch.equal(allidx, torch.arange(total, dtype=torch.int32))  # actually shuffled
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("graphs", [False, True])
+def test_ppo_gpu_learns(graphs, dev):
+    cfg = PPOConfig(num_envs=1024, rollout_steps=32, minibatch_size=2048, hidden=(64, 64), seed=1,
+                    cuda_graphs=graphs)
+    tr = PPOTrainer(cfg, device=dev)
+    tr.train_iteration()
+    first = tr.metrics()["mean_return"]
+    for _ in range(30):
+        tr.train_iteration()
+    tr.metrics()
+    for _ in range(3):
+        tr.train_iteration()
+    m = tr.metrics()
+    tr.release_graphs()
+    assert m["mean_return"] > 2 * first and m["mean_return"] > 80, (first, m)
+    assert 0 <= m["clipfrac"] <= 1 and m["entropy"] > 0

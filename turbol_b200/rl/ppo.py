@@ -1,0 +1,323 @@
+"""PPO for vectorized device-resident environments (CartPole).
+
+One training iteration = a rollout of ``rollout_steps`` steps over
+``num_envs`` environments, GAE, then ``epochs`` passes of shuffled minibatches
+of the clipped-surrogate objective.
+
+GPU path (everything stays on the device, no host round trip per step):
+  rollout step   policy MLP forward (bf16 tensor cores under autocast) ->
+                 one fused kernel: sample action (Gumbel-max), log-prob, store
+                 the transition at row t, step CartPole with auto-reset;
+  advantages     one GAE kernel that also accumulates the advantage moments;
+  minibatch      gather through an on-device Feistel permutation (fused with
+                 advantage normalization) -> forward -> fused PPO loss
+                 forward+backward kernel -> autograd backward into one flat
+                 gradient buffer -> [data-parallel gradient reduction] -> one
+                 fused Adam launch.
+The rollout, the advantage pass and one minibatch step are each captured as a
+CUDA graph; the minibatch graph is replayed epochs * n_minibatches times and
+reads its (epoch, minibatch) position from a device counter.
+
+CPU path: the same algorithm in eager PyTorch with the reference math (used by
+the CPU tests and as the oracle for the kernels).
+
+The reference's ppo_example.py (turbol_vllm/examples/py/ppo_example.py:146-210)
+steps a linear env with random actions and never runs GAE or a clipped update;
+this module is the algorithm its name promises.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import torch
+import torch.nn.functional as F
+
+from .._native import core as _core, ops as _ops
+from ..models.mlp import ActorCritic
+from ..ops import reference as ref
+from ..ops.rl import FusedAdam, gae, ppo_categorical_loss
+
+
+@dataclass
+class PPOConfig:
+    num_envs: int = 256
+    rollout_steps: int = 32
+    hidden: tuple = (64, 64)
+    epochs: int = 4
+    minibatch_size: int = 64
+    lr: float = 3e-4
+    gamma: float = 0.99
+    lam: float = 0.95
+    clip: float = 0.2
+    vf_coef: float = 0.5
+    ent_coef: float = 0.0
+    max_grad_norm: float = 0.0
+    norm_adv: bool = True
+    seed: int = 1
+    compute_dtype: str = "bf16"  # "bf16" (tensor cores, fp32 master weights) or "fp32"
+    cuda_graphs: bool = True
+    env: str = "cartpole"
+
+    @property
+    def batch(self) -> int:
+        return self.num_envs * self.rollout_steps
+
+    @property
+    def n_minibatches(self) -> int:
+        return max(1, self.batch // self.minibatch_size)
+
+
+class PPOTrainer:
+    """PPO trainer; ``grad_sync`` (optional) reduces the flat gradient across
+    data-parallel ranks in place and returns the scale Adam applies."""
+
+    def __init__(self, cfg: PPOConfig, device="cuda:0", grad_sync: Optional[Callable] = None, rank: int = 0):
+        self.cfg, self.rank = cfg, rank
+        self.device = torch.device(device)
+        self.cuda = self.device.type == "cuda"
+        C = _core()
+        T, N = cfg.rollout_steps, cfg.num_envs
+        if cfg.batch % cfg.minibatch_size != 0:
+            raise ValueError("num_envs * rollout_steps must be a multiple of minibatch_size")
+        dev = str(self.device) if self.cuda else "cpu"
+        self.env = C.GPUEnvironment(N, 4, 2, dev, "cartpole", seed=cfg.seed * 7919 + rank * 104729 + 17)
+        self.policy = ActorCritic(4, 2, cfg.hidden, discrete=True, device=self.device, seed=cfg.seed)
+        self.opt = FusedAdam(self.policy.fp.flat, self.policy.fp.grad, lr=cfg.lr, max_grad_norm=cfg.max_grad_norm)
+        self.grad_sync = grad_sync
+        self.state = self.env.state()  # live [N, 4] view
+        self.ep_len, self.ep_ret, self.ep_count, self.ep_stats = self.env.episode_buffers()
+        f32 = dict(device=self.device, dtype=torch.float32)
+        self.obs_buf = torch.zeros(T, N, 4, **f32)
+        self.act_buf = torch.zeros(T, N, device=self.device, dtype=torch.int32)
+        self.logp_buf = torch.zeros(T, N, **f32)
+        self.val_buf = torch.zeros(T + 1, N, **f32)
+        self.rew_buf = torch.zeros(T, N, **f32)
+        self.done_buf = torch.zeros(T, N, device=self.device, dtype=torch.uint8)
+        self.adv = torch.zeros(T, N, **f32)
+        self.ret = torch.zeros(T, N, **f32)
+        self.adv_stats = torch.zeros(2, device=self.device, dtype=torch.float64)
+        MB = cfg.minibatch_size
+        self.mb_obs = torch.zeros(MB, 4, **f32)
+        self.mb_act = torch.zeros(MB, device=self.device, dtype=torch.int32)
+        self.mb_logp = torch.zeros(MB, **f32)
+        self.mb_adv = torch.zeros(MB, **f32)
+        self.mb_ret = torch.zeros(MB, **f32)
+        self.loss_stats = torch.zeros(8, **f32)
+        self.iter_t = torch.zeros(1, device=self.device, dtype=torch.int64)
+        self.mb_step_t = torch.zeros(1, device=self.device, dtype=torch.int64)
+        self.scratch = None
+        if self.cuda:
+            n = _ops().gae_scratch_numel(T, N)
+            self.scratch = torch.empty(max(n, 1), **f32)
+        self.policy_seed = (cfg.seed * 0x9E3779B1 + rank * 0x85EBCA6B + 1) & 0xFFFFFFFFFFFF
+        self.env_seed = self.env.seed()
+        self._graphs = None
+        self.iteration = 0
+        self._cpu_gen = torch.Generator().manual_seed(cfg.seed + 1000 * rank)
+
+    # ------------------------------------------------------------------ GPU
+    def _autocast(self):
+        if self.cuda and self.cfg.compute_dtype == "bf16":
+            return torch.autocast("cuda", dtype=torch.bfloat16)
+        return torch.autocast("cuda", enabled=False) if self.cuda else torch.autocast("cpu", enabled=False)
+
+    def _rollout_gpu(self):
+        o = _ops()
+        T = self.cfg.rollout_steps
+        params = {}
+        with torch.no_grad(), self._autocast():
+            for t in range(T):
+                logits, v = self.policy(self.state)
+                o.ppo_cartpole_act_step(logits.float().contiguous(), v.float().contiguous(), self.state, self.ep_len,
+                                        self.ep_ret, self.ep_count, self.ep_stats, self.obs_buf, self.act_buf,
+                                        self.logp_buf, self.val_buf, self.rew_buf, self.done_buf, self.iter_t, t,
+                                        self.policy_seed, self.env_seed, params)
+            self.val_buf[T].copy_(self.policy.critic(self.state).float())
+        self.adv_stats.zero_()
+        gae(self.rew_buf, self.val_buf, self.done_buf, self.cfg.gamma, self.cfg.lam, stats=self.adv_stats,
+            scratch=self.scratch, out=(self.adv, self.ret))
+        self.mb_step_t.zero_()
+
+    def _minibatch_gpu(self):
+        self._minibatch_grad_gpu()
+        self._minibatch_apply_gpu(self._sync_grads())
+
+    def _sync_grads(self):
+        return self.grad_sync(self.policy.fp.grad) if self.grad_sync is not None else 1.0
+
+    def _minibatch_apply_gpu(self, scale):
+        self.opt.step(grad_scale=scale)
+        _ops().counter_add(self.mb_step_t, 1)
+
+    def _minibatch_grad_gpu(self):
+        cfg = self.cfg
+        o = _ops()
+        o.ppo_gather(self.obs_buf, self.act_buf, self.logp_buf, self.adv, self.ret, self.val_buf, self.adv_stats,
+                     self.mb_obs, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, None, cfg.n_minibatches,
+                     self.mb_step_t, self.iter_t, 0, self.policy_seed ^ 0x5851F42D, cfg.norm_adv)
+        self.policy.fp.grad.zero_()
+        with self._autocast():
+            logits, v = self.policy(self.mb_obs)
+        loss = ppo_categorical_loss(logits.float(), v.float(), self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret,
+                                    cfg.clip, cfg.vf_coef, cfg.ent_coef, stats=self.loss_stats)
+        loss.backward()
+
+    def _end_iteration_gpu(self):
+        _ops().counter_add(self.iter_t, 1)
+
+    def _sync_capturable(self) -> bool:
+        return self.grad_sync is None or getattr(self.grad_sync, "capturable", False)
+
+    def _build_graphs(self):
+        if not (self.cuda and self.cfg.cuda_graphs):
+            return
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        # Warm-up on a side stream (autograd/cuBLAS workspaces get allocated
+        # here, outside capture).  This advances the env and the optimizer
+        # state once, which is harmless: it is one real training step.
+        with torch.cuda.stream(s):
+            self._rollout_gpu()
+            for _ in range(2):
+                self._minibatch_gpu()
+            self._end_iteration_gpu()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        pool = torch.cuda.graph_pool_handle()
+        g_roll, g_end = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_roll, pool=pool):
+            self._rollout_gpu()
+        if self._sync_capturable():
+            g_mb = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_mb, pool=pool):
+                self._minibatch_gpu()
+            mb = (g_mb,)
+        else:
+            # a library collective stays outside the graphs: grads -> sync -> apply
+            scale = getattr(self.grad_sync, "scale", 1.0)
+            g_grad, g_apply = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_grad, pool=pool):
+                self._minibatch_grad_gpu()
+            with torch.cuda.graph(g_apply, pool=pool):
+                self._minibatch_apply_gpu(scale)
+            mb = (g_grad, g_apply)
+        with torch.cuda.graph(g_end, pool=pool):
+            self._end_iteration_gpu()
+        torch.cuda.synchronize(self.device)
+        self.policy.fp.rebind_grads()
+        self._graphs = (g_roll, mb, g_end)
+
+    def release_graphs(self):
+        self._graphs = None
+
+    # ------------------------------------------------------------------ CPU
+    def _rollout_cpu(self):
+        T = self.cfg.rollout_steps
+        with torch.no_grad():
+            for t in range(T):
+                logits, v = self.policy(self.state)
+                logp_all = F.log_softmax(logits.float(), -1)
+                g = -torch.log(-torch.log(torch.rand(logits.shape, generator=self._cpu_gen).clamp_(1e-9, 1 - 1e-7)))
+                a = (logits + g).argmax(-1).to(torch.int32)
+                self.obs_buf[t].copy_(self.state)
+                self.act_buf[t].copy_(a)
+                self.logp_buf[t].copy_(logp_all.gather(1, a.long()[:, None]).squeeze(1))
+                self.val_buf[t].copy_(v)
+                obs = torch.empty_like(self.state)
+                rew = torch.empty(self.state.shape[0])
+                done = torch.empty(self.state.shape[0], dtype=torch.bool)
+                self.env.step_into(a, obs, rew, done)
+                self.rew_buf[t].copy_(rew)
+                self.done_buf[t].copy_(done.to(torch.uint8))
+            self.val_buf[T].copy_(self.policy.critic(self.state))
+        adv, ret = ref.gae(self.rew_buf, self.val_buf, self.done_buf, self.cfg.gamma, self.cfg.lam)
+        self.adv.copy_(adv)
+        self.ret.copy_(ret)
+
+    def _update_cpu(self):
+        cfg = self.cfg
+        B = cfg.batch
+        obs = self.obs_buf.view(B, 4)
+        act, logp, adv, ret = (x.reshape(B) for x in (self.act_buf, self.logp_buf, self.adv, self.ret))
+        if cfg.norm_adv:
+            adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        for _ in range(cfg.epochs):
+            perm = torch.randperm(B, generator=self._cpu_gen)
+            for k in range(cfg.n_minibatches):
+                idx = perm[k * cfg.minibatch_size:(k + 1) * cfg.minibatch_size]
+                self.policy.fp.grad.zero_()
+                logits, v = self.policy(obs[idx])
+                loss = ppo_categorical_loss(logits, v, act[idx], logp[idx], adv[idx], ret[idx], cfg.clip,
+                                            cfg.vf_coef, cfg.ent_coef, stats=self.loss_stats)
+                loss.backward()
+                scale = self.grad_sync(self.policy.fp.grad) if self.grad_sync is not None else 1.0
+                self.opt.step(grad_scale=scale)
+
+    # ------------------------------------------------------------------ API
+    def train_iteration(self):
+        """Runs one rollout + update.  Returns nothing (metrics are read
+        lazily by :meth:`metrics`, which synchronizes)."""
+        cfg = self.cfg
+        if not self.cuda:
+            self._rollout_cpu()
+            self._update_cpu()
+            self.iteration += 1
+            return
+        if cfg.cuda_graphs and self._graphs is None:
+            self._build_graphs()
+        if self._graphs is not None:
+            g_roll, mb, g_end = self._graphs
+            g_roll.replay()
+            if len(mb) == 1:
+                for _ in range(cfg.epochs * cfg.n_minibatches):
+                    mb[0].replay()
+            else:
+                for _ in range(cfg.epochs * cfg.n_minibatches):
+                    mb[0].replay()
+                    self.grad_sync(self.policy.fp.grad)
+                    mb[1].replay()
+            g_end.replay()
+        else:
+            self._rollout_gpu()
+            for _ in range(cfg.epochs * cfg.n_minibatches):
+                self._minibatch_gpu()
+            self._end_iteration_gpu()
+        self.iteration += 1
+
+    def metrics(self) -> dict:
+        """Episode and loss statistics since the previous call (synchronizes)."""
+        s = self.env.take_episode_stats()
+        ls = self.loss_stats.double().cpu().tolist()
+        self.loss_stats.zero_()
+        n = max(ls[5], 1.0)
+        out = {
+            "episodes": s[1],
+            "mean_return": s[0] / s[1] if s[1] > 0 else float("nan"),
+            "mean_length": s[2] / s[1] if s[1] > 0 else float("nan"),
+            "policy_loss": ls[0] / n,
+            "value_loss": ls[1] / n,
+            "entropy": ls[2] / n,
+            "approx_kl": ls[3] / n,
+            "clipfrac": ls[4] / n,
+        }
+        return out
+
+    def env_steps_per_iteration(self) -> int:
+        return self.cfg.batch
+
+    def state_dict(self):
+        return {"policy": self.policy.state_dict(), "optim": self.opt.state_dict(), "iteration": self.iteration,
+                "iter_t": self.iter_t.clone(), "env_state": self.state.clone(),
+                "ep": (self.ep_len.clone(), self.ep_ret.clone(), self.ep_count.clone())}
+
+    def load_state_dict(self, sd):
+        with torch.no_grad():
+            self.policy.load_state_dict(sd["policy"])
+            self.opt.load_state_dict(sd["optim"])
+            self.iteration = int(sd["iteration"])
+            self.iter_t.copy_(sd["iter_t"])
+            self.state.copy_(sd["env_state"])
+            for dst, src in zip((self.ep_len, self.ep_ret, self.ep_count), sd["ep"]):
+                dst.copy_(src)
