@@ -6,6 +6,8 @@
 # this runs the build the reference's own CMakeLists.txt defines, from a copy
 # (the source tree is read-only).  Tests are off (GoogleTest is not installed)
 # and NCCL is off (its NCCL build calls a function NCCL does not have).
+# Its CMakeLists.txt pins libtorch's arch list to 12.0 (sm_120 only), so an
+# sm_100 -gencode is added through CMAKE_CUDA_FLAGS (appended to, not replaced).
 set -euo pipefail
 REF=${REF:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
@@ -17,6 +19,7 @@ TORCH_DIR=$(python -c 'import torch,os;print(os.path.join(os.path.dirname(torch.
 PYBIND_DIR=$(python -c 'import pybind11;print(pybind11.get_cmake_dir())')
 cmake -S "$SRC/turbol_vllm" -B "$BLD" -G Ninja -DCMAKE_BUILD_TYPE=Release -DCMAKE_CUDA_ARCHITECTURES=100 \
   -DTURBORL_ENABLE_TESTS=OFF -DTURBORL_ENABLE_PYTHON=ON -DTURBORL_USE_NCCL=OFF \
+  -DCMAKE_CUDA_FLAGS="-gencode arch=compute_100,code=sm_100" \
   -DTorch_DIR="$TORCH_DIR" -Dpybind11_DIR="$PYBIND_DIR" -DPython_EXECUTABLE="$(which python)"
 cmake --build "$BLD" -j "$(nproc)"
 mkdir -p "$HERE/_ref/bin"

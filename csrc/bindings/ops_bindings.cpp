@@ -65,11 +65,21 @@ void register_kernel_ops(py::module_& m) {
         py::arg("state"), py::arg("ep_len"), py::arg("ep_ret"), py::arg("ep_count"), py::arg("seed"),
         py::arg("init_range") = 0.05f);
 
+  m.def("pad_obs_bf16", [](at::Tensor state, at::Tensor out) {
+    need(state, at::kFloat, "state");
+    need(out, at::kBFloat16, "out");
+    const int n = static_cast<int>(state.size(0));
+    TB_CHECK(state.numel() == 4LL * n && out.numel() == 8LL * n, "pad_obs_bf16: [N,4] -> [N,8]");
+    cuda_ok(tb_pad_obs_bf16(state.data_ptr<float>(), out.data_ptr(), n, stream_of(state)), "pad_obs_bf16");
+  });
+
+  // logits [N, ldl] (first A columns used), values [N, ldv] (column 0);
+  // obs_bf16 (optional) receives the next observation as bf16 [N, 8].
   m.def("ppo_cartpole_act_step",
-        [](at::Tensor logits, at::Tensor values, at::Tensor state, at::Tensor ep_len, at::Tensor ep_ret,
-           at::Tensor ep_count, at::Tensor stats, at::Tensor obs_buf, at::Tensor act_buf, at::Tensor logp_buf,
-           at::Tensor val_buf, at::Tensor rew_buf, at::Tensor done_buf, py::object iter_ptr, int t,
-           uint64_t policy_seed, uint64_t env_seed, py::dict params) {
+        [](at::Tensor logits, int A, at::Tensor values, at::Tensor state, py::object obs_bf16, at::Tensor ep_len,
+           at::Tensor ep_ret, at::Tensor ep_count, at::Tensor stats, at::Tensor obs_buf, at::Tensor act_buf,
+           at::Tensor logp_buf, at::Tensor val_buf, at::Tensor rew_buf, at::Tensor done_buf, py::object iter_ptr,
+           int t, uint64_t policy_seed, uint64_t env_seed, py::dict params) {
           need(logits, at::kFloat, "logits");
           need(values, at::kFloat, "values");
           need(state, at::kFloat, "state");
@@ -80,9 +90,17 @@ void register_kernel_ops(py::module_& m) {
           need(rew_buf, at::kFloat, "rew_buf");
           TB_CHECK(done_buf.is_cuda() && done_buf.element_size() == 1 && done_buf.is_contiguous(), "done_buf u8");
           const int n = static_cast<int>(state.size(0));
-          const int A = static_cast<int>(logits.size(1));
-          TB_CHECK(logits.size(0) == n && values.numel() == n, "logits/values batch mismatch");
+          TB_CHECK(logits.dim() == 2 && logits.size(0) == n && logits.size(1) >= A, "logits [N, >=A]");
+          TB_CHECK(values.size(0) == n, "values batch mismatch");
           TB_CHECK(obs_buf.dim() == 3 && obs_buf.size(1) == n && t >= 0 && t < obs_buf.size(0), "obs_buf [T, N, 4]");
+          const int ldv = values.dim() == 2 ? static_cast<int>(values.size(1)) : 1;
+          void* ob = nullptr;
+          if (!obs_bf16.is_none()) {
+            at::Tensor x = obs_bf16.cast<at::Tensor>();
+            need(x, at::kBFloat16, "obs_bf16");
+            TB_CHECK(x.numel() == 8LL * n, "obs_bf16 [N, 8]");
+            ob = x.data_ptr();
+          }
           const long long* ip = nullptr;
           if (!iter_ptr.is_none()) {
             at::Tensor it = iter_ptr.cast<at::Tensor>();
@@ -90,8 +108,8 @@ void register_kernel_ops(py::module_& m) {
             ip = reinterpret_cast<const long long*>(it.data_ptr<int64_t>());
           }
           cuda_ok(tb_ppo_cartpole_act_step(
-                      logits.data_ptr<float>(), A, values.data_ptr<float>(), state.data_ptr<float>(),
-                      ep_len.data_ptr<int>(), ep_ret.data_ptr<float>(),
+                      logits.data_ptr<float>(), A, static_cast<int>(logits.size(1)), values.data_ptr<float>(), ldv,
+                      state.data_ptr<float>(), ob, ep_len.data_ptr<int>(), ep_ret.data_ptr<float>(),
                       reinterpret_cast<unsigned*>(ep_count.data_ptr<int>()), stats.data_ptr<float>(),
                       obs_buf.data_ptr<float>(), act_buf.data_ptr<int>(), logp_buf.data_ptr<float>(),
                       val_buf.data_ptr<float>(), rew_buf.data_ptr<float>(),
@@ -236,7 +254,7 @@ void register_kernel_ops(py::module_& m) {
         [](at::Tensor obs, at::Tensor act, at::Tensor logp, at::Tensor adv, at::Tensor ret, at::Tensor val,
            py::object adv_stats, at::Tensor o_obs, at::Tensor o_act, at::Tensor o_logp, at::Tensor o_adv,
            at::Tensor o_ret, py::object o_val, int n_mb, py::object step_ptr, py::object iter_ptr, int64_t step,
-           uint64_t seed, bool normalize) {
+           uint64_t seed, bool normalize, py::object o_obs_bf16) {
           need(obs, at::kFloat, "obs");
           need(act, at::kInt, "act");
           const int total = static_cast<int>(act.numel());
@@ -245,6 +263,8 @@ void register_kernel_ops(py::module_& m) {
           const double* sp = nullptr;
           if (!adv_stats.is_none()) sp = adv_stats.cast<at::Tensor>().data_ptr<double>();
           float* ov = o_val.is_none() ? nullptr : o_val.cast<at::Tensor>().data_ptr<float>();
+          void* ob = o_obs_bf16.is_none() ? nullptr : o_obs_bf16.cast<at::Tensor>().data_ptr();
+          float* oo = o_obs.numel() > 0 ? o_obs.data_ptr<float>() : nullptr;
           const long long* stp = step_ptr.is_none()
                                      ? nullptr
                                      : reinterpret_cast<const long long*>(step_ptr.cast<at::Tensor>().data_ptr<int64_t>());
@@ -253,11 +273,49 @@ void register_kernel_ops(py::module_& m) {
                                      : reinterpret_cast<const long long*>(iter_ptr.cast<at::Tensor>().data_ptr<int64_t>());
           cuda_ok(tb_ppo_gather(obs.data_ptr<float>(), obs_dim, act.data_ptr<int>(), logp.data_ptr<float>(),
                                 adv.data_ptr<float>(), ret.data_ptr<float>(), val.data_ptr<float>(), sp,
-                                o_obs.data_ptr<float>(), o_act.data_ptr<int>(), o_logp.data_ptr<float>(),
-                                o_adv.data_ptr<float>(), o_ret.data_ptr<float>(), ov, total, mb, n_mb, stp, itp, step,
-                                seed, normalize ? 1 : 0, stream_of(obs)),
+                                oo, o_act.data_ptr<int>(), o_logp.data_ptr<float>(), o_adv.data_ptr<float>(),
+                                o_ret.data_ptr<float>(), ov, ob, total, mb, n_mb, stp, itp, step, seed,
+                                normalize ? 1 : 0, stream_of(obs)),
                   "ppo_gather");
-        });
+        },
+        py::arg("obs"), py::arg("act"), py::arg("logp"), py::arg("adv"), py::arg("ret"), py::arg("val"),
+        py::arg("adv_stats"), py::arg("o_obs"), py::arg("o_act"), py::arg("o_logp"), py::arg("o_adv"),
+        py::arg("o_ret"), py::arg("o_val"), py::arg("n_mb"), py::arg("step_ptr"), py::arg("iter_ptr"),
+        py::arg("step"), py::arg("seed"), py::arg("normalize"), py::arg("o_obs_bf16") = py::none());
+
+  m.def("ppo_loss_padded",
+        [](at::Tensor logits, int A, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv,
+           at::Tensor ret, at::Tensor dlog, at::Tensor dval, py::object stats, float clip, float vf_coef,
+           float ent_coef, py::object db_log, py::object db_val) {
+          need(logits, at::kFloat, "logits");
+          need(value, at::kFloat, "value");
+          need(act, at::kInt, "act");
+          need(dlog, at::kBFloat16, "dlog");
+          need(dval, at::kBFloat16, "dval");
+          const int B = static_cast<int>(act.numel());
+          TB_CHECK(logits.size(0) == B && dlog.numel() == 8LL * B && dval.numel() == 8LL * B, "padded loss shapes");
+          float* sp = stats.is_none() ? nullptr : stats.cast<at::Tensor>().data_ptr<float>();
+          cuda_ok(tb_ppo_loss_padded(logits.data_ptr<float>(), static_cast<int>(logits.size(1)), A,
+                                     value.data_ptr<float>(), static_cast<int>(value.size(1)), act.data_ptr<int>(),
+                                     old_logp.data_ptr<float>(), adv.data_ptr<float>(), ret.data_ptr<float>(),
+                                     dlog.data_ptr(), dval.data_ptr(), sp, B, clip, vf_coef, ent_coef,
+                                     db_log.is_none() ? nullptr : db_log.cast<at::Tensor>().data_ptr<float>(),
+                                     db_val.is_none() ? nullptr : db_val.cast<at::Tensor>().data_ptr<float>(),
+                                     stream_of(logits)),
+                  "ppo_loss_padded");
+        },
+        py::arg("logits"), py::arg("A"), py::arg("value"), py::arg("act"), py::arg("old_logp"), py::arg("adv"),
+        py::arg("ret"), py::arg("dlog"), py::arg("dval"), py::arg("stats"), py::arg("clip"), py::arg("vf_coef"),
+        py::arg("ent_coef"), py::arg("db_log") = py::none(), py::arg("db_val") = py::none());
+
+  m.def("colsum_bf16", [](at::Tensor x, at::Tensor out) {
+    TB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "colsum: bf16 2-D");
+    need(out, at::kFloat, "out");
+    TB_CHECK(out.numel() == x.size(1), "colsum: out [cols]");
+    cuda_ok(tb_colsum_bf16(x.data_ptr(), x.stride(0), static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
+                           out.data_ptr<float>(), stream_of(x)),
+            "colsum_bf16");
+  });
 
   m.def("ppo_loss",
         [](at::Tensor logits, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv, at::Tensor ret,

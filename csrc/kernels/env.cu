@@ -18,6 +18,7 @@
 // one vector load/store per env).  A step over 65,536 envs moves ~3 MB, so
 // these launches are latency bound; the rollout driver captures them in a
 // CUDA graph.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -155,14 +156,27 @@ __global__ void cartpole_step_kernel(float4* __restrict__ state, const int* __re
   record_episode(stats, finished, fin_ret, fin_len);
 }
 
+// Next-step policy input: the observation as bf16, padded to 8 features
+// (one 16-byte store; the tensor-core MLP's first layer reads K = 8).
+__device__ __forceinline__ void write_obs_bf16(uint16_t* out, int i, float4 s) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(s.x, s.y), b = __floats2bfloat162_rn(s.z, s.w);
+  uint4 v;
+  v.x = *reinterpret_cast<uint32_t*>(&a);
+  v.y = *reinterpret_cast<uint32_t*>(&b);
+  v.z = 0u;
+  v.w = 0u;
+  reinterpret_cast<uint4*>(out)[i] = v;
+}
+
 // Fused PPO rollout step for CartPole with a categorical policy over A actions:
 //   action ~ Categorical(softmax(logits)) by the Gumbel-max trick,
 //   logp = logits[a] - logsumexp(logits),
 //   the pre-step observation, action, logp, value, reward and done are written
 //   to row t of the rollout storage, and `state` advances in place (it is the
 //   next step's policy input).
-__global__ void ppo_cartpole_act_step_kernel(const float* __restrict__ logits, int A,
-                                             const float* __restrict__ values, float4* __restrict__ state,
+__global__ void ppo_cartpole_act_step_kernel(const float* __restrict__ logits, int A, int ldl,
+                                             const float* __restrict__ values, int ldv, float4* __restrict__ state,
+                                             uint16_t* __restrict__ obs_bf16,
                                              int* __restrict__ ep_len, float* __restrict__ ep_ret,
                                              unsigned* __restrict__ ep_count, float* __restrict__ stats,
                                              float4* __restrict__ obs_buf, int* __restrict__ act_buf,
@@ -177,7 +191,7 @@ __global__ void ppo_cartpole_act_step_kernel(const float* __restrict__ logits, i
   int fin_len = 0;
   if (active) {
     const long long it = iter_ptr ? *iter_ptr : 0;
-    const float* l = logits + static_cast<size_t>(i) * A;
+    const float* l = logits + static_cast<size_t>(i) * ldl;
     float mx = -INFINITY;
     for (int k = 0; k < A; ++k) mx = fmaxf(mx, l[k]);
     float se = 0.f;
@@ -202,7 +216,7 @@ __global__ void ppo_cartpole_act_step_kernel(const float* __restrict__ logits, i
     obs_buf[static_cast<size_t>(t) * n + i] = s;
     act_buf[static_cast<size_t>(t) * n + i] = best;
     logp_buf[static_cast<size_t>(t) * n + i] = l[best] - lse;
-    val_buf[static_cast<size_t>(t) * n + i] = values[i];
+    val_buf[static_cast<size_t>(t) * n + i] = values[static_cast<size_t>(i) * ldv];
 
     const bool term = cartpole_physics(s, best, p);
     const int len = ep_len[i] + 1;
@@ -221,10 +235,16 @@ __global__ void ppo_cartpole_act_step_kernel(const float* __restrict__ logits, i
       ep_ret[i] = ret;
     }
     state[i] = s;
+    if (obs_bf16 != nullptr) write_obs_bf16(obs_bf16, i, s);
     rew_buf[static_cast<size_t>(t) * n + i] = 1.0f;
     done_buf[static_cast<size_t>(t) * n + i] = finished ? 1 : 0;
   }
   record_episode(stats, finished, fin_ret, fin_len);
+}
+
+__global__ void pad_obs_bf16_kernel(const float4* __restrict__ s, uint16_t* __restrict__ out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) write_obs_bf16(out, i, s[i]);
 }
 
 inline int grid_for(int n) { return (n + kBlock - 1) / kBlock; }
@@ -265,14 +285,23 @@ int tb_cartpole_step(float* state, const int* action, float* obs_out, float* rew
   return static_cast<int>(cudaGetLastError());
 }
 
-int tb_ppo_cartpole_act_step(const float* logits, int A, const float* values, float* state, int* ep_len,
+int tb_pad_obs_bf16(const float* state, void* out, int n, cudaStream_t s) {
+  if (n <= 0) return 0;
+  pad_obs_bf16_kernel<<<grid_for(n), kBlock, 0, s>>>(reinterpret_cast<const float4*>(state),
+                                                     static_cast<uint16_t*>(out), n);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_ppo_cartpole_act_step(const float* logits, int A, int ldl, const float* values, int ldv, float* state,
+                             void* obs_bf16, int* ep_len,
                              float* ep_ret, unsigned* ep_count, float* stats, float* obs_buf, int* act_buf,
                              float* logp_buf, float* val_buf, float* rew_buf, uint8_t* done_buf,
                              const long long* iter_ptr, int t, int n, unsigned long long policy_seed,
                              unsigned long long env_seed, TbCartPoleParams p, cudaStream_t s) {
   if (n <= 0) return 0;
   ppo_cartpole_act_step_kernel<<<grid_for(n), kBlock, 0, s>>>(
-      logits, A, values, reinterpret_cast<float4*>(state), ep_len, ep_ret, ep_count, stats,
+      logits, A, ldl, values, ldv, reinterpret_cast<float4*>(state), static_cast<uint16_t*>(obs_bf16), ep_len, ep_ret,
+      ep_count, stats,
       reinterpret_cast<float4*>(obs_buf), act_buf, logp_buf, val_buf, rew_buf, done_buf, iter_ptr, t, n, policy_seed,
       env_seed, p);
   return static_cast<int>(cudaGetLastError());

@@ -1,0 +1,686 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )      fp32 accumulation in TMEM
+//
+// Operands may be K-major (row-major with K contiguous: an activation X[M, K]
+// or an nn.Linear weight W[N, K]) or MN-major (row-major with M or N
+// contiguous: the transposed operands of the weight and input gradients), so
+// forward (Y = X W^T), input gradient (dX = dY W) and weight gradient
+// (dW = dY^T X) all run without materialized transposes.
+//
+// Structure: persistent CTAs (at most one per SM), 128 x BN x 64 tiles,
+// warp-specialized:
+//   warp 0      one thread issues TMA tile loads (128-byte swizzle, no
+//               multicast) into a ring of shared-memory stages;
+//   warp 1      one thread issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM
+//               accumulator and commits each stage back to the producer;
+//   warp 2      allocates / frees TMEM (two accumulators of BN columns, so the
+//               epilogue of one tile overlaps the MMAs of the next);
+//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time, fused bias /
+//               activation / tanh-backward / residual / SwiGLU, vectorized
+//               global stores, or fp32 atomic accumulation for split-K and
+//               gradient accumulation.
+// All waits are bounded (sm100_primitives.cuh): on timeout the kernel records
+// an error, drains its own in-flight copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "kernels.h"
+#include "sm100_primitives.cuh"
+
+namespace {
+
+using namespace tb::sm100;
+
+constexpr int BM = 128, BK = 64;
+constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
+constexpr int kThreads = 128 + 32 * kEpiWarps;  // warps 0-3: TMA, MMA, TMEM, spare
+
+struct DevArgs {
+  int M, N, K;
+  int m_tiles, n_tiles, splits, kb_per_split, k_blocks;
+  void* C;
+  long long ldc;
+  int c_fp32, c_atomic;
+  const float* bias;
+  const __nv_bfloat16* aux;
+  long long ld_aux;
+  int epi;
+  float alpha;
+  float* ws;      // split-K partials [splits, M, N] (null: atomics into C)
+  float* colsum;  // optional: column sums of the epilogue output, accumulated atomically
+  int* error;
+};
+
+template <int BN>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + slack for 1024-B alignment
+};
+
+// Hardware tanh approximation (relative error ~2^-11, below bf16 resolution).
+__device__ __forceinline__ float fast_tanh(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_silu(float x) { return x / (1.f + __expf(-x)); }
+
+// 16 bf16 loaded as two 16-byte vectors when aligned.
+__device__ __forceinline__ void load_bf16x16(const __nv_bfloat16* p, float* out, int valid) {
+  if (valid >= 16 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const uint4 a = reinterpret_cast<const uint4*>(p)[0], b = reinterpret_cast<const uint4*>(p)[1];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* g = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 x = __bfloat1622float2(h[j]), y = __bfloat1622float2(g[j]);
+      out[2 * j] = x.x;
+      out[2 * j + 1] = x.y;
+      out[8 + 2 * j] = y.x;
+      out[8 + 2 * j + 1] = y.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) out[j] = j < valid ? __bfloat162float(p[j]) : 0.f;
+  }
+}
+
+// Sums 32 columns over the warp's 32 rows by a butterfly transpose-reduce
+// (31 shuffles); afterwards lane L holds the sum of column L.
+__device__ __forceinline__ float warp_colsum32(float* v, int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < off; ++j) {
+      const float send = upper ? v[j] : v[j + off];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, off);
+      v[j] = (upper ? v[j + off] : v[j]) + recv;
+    }
+  }
+  return v[0];
+}
+
+// Applies the epilogue to 32 accumulator columns [c0, c0+32) of row `row`
+// (row >= M rows still join the warp-wide column sum with zeros).
+__device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane) {
+  const int N = p.N, epi = p.epi;
+  const bool row_ok = row < p.M;
+  const int valid = min(32, N - c0);
+  if (p.alpha != 1.f) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
+  }
+  if (p.ws != nullptr) {  // split-K partial: raw accumulator, no epilogue yet
+    if (row_ok) {
+      float* W = p.ws + (static_cast<long long>(ks) * p.M + row) * N + c0;
+      if (valid == 32 && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(W)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < valid) W[j] = v[j];
+      }
+    }
+    return;
+  }
+  if ((epi == TB_EPI_BIAS || epi == TB_EPI_BIAS_TANH || epi == TB_EPI_BIAS_SILU) && p.bias && ks == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += (j < valid) ? __ldg(p.bias + c0 + j) : 0.f;
+  }
+  if (epi == TB_EPI_BIAS_TANH) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fast_tanh(v[j]);
+  } else if (epi == TB_EPI_BIAS_SILU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fast_silu(v[j]);
+  } else if ((epi == TB_EPI_TANH_BWD || epi == TB_EPI_RESIDUAL) && row_ok) {
+    const __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + c0;
+    float h[32];
+    load_bf16x16(a, h, valid);
+    load_bf16x16(a + 16, h + 16, valid - 16);
+    if (epi == TB_EPI_TANH_BWD) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= 1.f - h[j] * h[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += h[j];
+    }
+  }
+  if (epi == TB_EPI_SWIGLU) {
+    // interleaved gate/up columns: out[c/2] = silu(gate) * up
+    if (!row_ok) return;
+    const int oc0 = c0 / 2;
+    const int Nout = N / 2;
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = fast_silu(v[2 * j]) * v[2 * j + 1];
+    if (p.c_fp32) {
+      float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + oc0;
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (oc0 + j < Nout) C[j] = o[j];
+    } else {
+      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + oc0;
+      if (oc0 + 16 <= Nout && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+        uint4 pk[2];
+        __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) hh[j] = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+        reinterpret_cast<uint4*>(C)[0] = pk[0];
+        reinterpret_cast<uint4*>(C)[1] = pk[1];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (oc0 + j < Nout) C[j] = __float2bfloat16_rn(o[j]);
+      }
+    }
+    return;
+  }
+  if (p.colsum != nullptr) {
+    float t[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t[j] = row_ok ? v[j] : 0.f;
+    const float cs = warp_colsum32(t, lane);
+    if (lane < valid) atomicAdd(p.colsum + c0 + lane, cs);
+  }
+  if (!row_ok) return;
+  if (p.c_atomic) {
+    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) atomicAdd(C + j, v[j]);
+    return;
+  }
+  if (p.c_fp32) {
+    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(C)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) C[j] = v[j];
+    }
+  } else {
+    __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+      uint4 pk[4];
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(pk);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) hh[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(C)[j] = pk[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) C[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
+__device__ __forceinline__ void work_coords(const DevArgs& p, int w, int& m0, int& nt, int& ks, int& kb0, int& kb1) {
+  const int mt = w % p.m_tiles;
+  const int rest = w / p.m_tiles;
+  nt = rest % p.n_tiles;
+  ks = rest / p.n_tiles;
+  m0 = mt * BM;
+  kb0 = ks * p.kb_per_split;
+  kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+}
+
+// 32 columns without the wait (callers batch loads, then wait once).
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, DevArgs p) {
+  using S = Smem<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* tfull = empty + S::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = p.m_tiles * p.n_tiles * p.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 32 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+  }
+  if (warp == 2) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
+      int m0, nt, ks, kb0, kb1;
+      work_coords(p, w, m0, nt, ks, kb0, kb1);
+      const int n0 = nt * BN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
+        uint8_t* sa = smem + stage * S::kStageBytes;
+        uint8_t* sb = sa + S::kABytes;
+        mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+        const int k0 = kb * BK;
+        if (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 64 * BK * 2, &tmA, &full[stage], m0 + 64 * j, k0);
+        } else {
+          tma_load_2d(sa, &tmA, &full[stage], k0, m0);
+        }
+        if (B_MN) {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * BK * 2, &tmB, &full[stage], n0 + 64 * j, k0);
+        } else {
+          tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+        }
+        ++issued;
+        if (++stage == S::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (*abort_flag) {
+      // drain: wait (bounded) for the loads of the last min(issued, stages) stages
+      const int n = issued < S::kStages ? issued : S::kStages;
+      int st = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < n; ++i) {
+        if (--st < 0) {
+          st = S::kStages - 1;
+          ph ^= 1;
+        }
+        const unsigned long long t0 = global_ns();
+        while (!mbar_try_wait(&full[st], ph) && global_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool any = false;
+    for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
+      int m0, nt, ks, kb0, kb1;
+      work_coords(p, w, m0, nt, ks, kb0, kb1);
+      if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem_base + acc * BN;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+        const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          // K-major: +32 bytes per K=16 step inside the 128-byte swizzle atom.
+          // MN-major: +2048 bytes (two 8-row K groups) per step; 64-wide MN
+          // blocks are 64*BK*2 bytes apart (LBO).
+          const uint64_t ad = A_MN ? smem_desc_sw128(sa + kk * 2048, 64 * BK * 2, 1024)
+                                   : smem_desc_sw128(sa + kk * 32, 16, 1024);
+          const uint64_t bd = B_MN ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
+                                   : smem_desc_sw128(sb + kk * 32, 16, 1024);
+          mma_f16(d, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[stage]);
+        any = true;
+        if (++stage == S::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      mma_commit(&tfull[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    // make sure every MMA this thread issued has finished before TMEM is freed
+    if (any) {
+      mma_commit(drain);
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 1000000000ull) {
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ epilogue: 8 warps; warp (4 + q + 4h)
+    // reads TMEM lane quarter q (rows 32q..32q+31) and column half h.
+    const int sub = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r_in_tile = sub * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+      int m0, nt, ks, kb0, kb1;
+      work_coords(p, w, m0, nt, ks, kb0, kb1);
+      const int n0 = nt * BN;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = m0 + r_in_tile;
+      const uint32_t base = tmem_base + acc * BN + (static_cast<uint32_t>(sub * 32) << 16);
+#pragma unroll 1
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 64) {
+        uint32_t r[64];
+        tmem_ld32_nowait(base + c, r);
+        tmem_ld32_nowait(base + c + 32, r + 32);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
+        if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, 2 * BN);
+  if (threadIdx.x == 0 && *abort_flag && p.error) atomicExch(p.error, TB_GEMM_ERR_TIMEOUT);
+}
+
+// C = sum over splits of the partials (+ bias, + activation).  A block owns 64
+// float4 column groups of the output; its 4 warps-groups each sum every 4th
+// partial with 4 loads in flight, then combine through shared memory, so the
+// pass streams the workspace at bandwidth instead of walking the splits
+// serially.
+constexpr int kRedItems = 64, kRedGroups = 4;
+__global__ void __launch_bounds__(kRedItems* kRedGroups) splitk_reduce_kernel(DevArgs p) {
+  __shared__ float4 part[kRedGroups][kRedItems];
+  const int n4 = (p.N + 3) / 4;
+  const long long items = static_cast<long long>(p.M) * n4;
+  const int li = threadIdx.x % kRedItems, g = threadIdx.x / kRedItems;
+  const long long item = static_cast<long long>(blockIdx.x) * kRedItems + li;
+  const bool vec = (p.N % 4) == 0;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  int row = 0, c = 0, valid = 0;
+  if (item < items) {
+    row = static_cast<int>(item / n4);
+    c = static_cast<int>(item - static_cast<long long>(row) * n4) * 4;
+    valid = min(4, p.N - c);
+    const long long stride = static_cast<long long>(p.M) * p.N;
+    const float* W = p.ws + static_cast<long long>(row) * p.N + c;
+    int k = g;
+    for (; k + 3 * kRedGroups < p.splits; k += 4 * kRedGroups) {
+      float4 x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float* q = W + (k + u * kRedGroups) * stride;
+        x[u] = vec ? *reinterpret_cast<const float4*>(q)
+                   : make_float4(q[0], valid > 1 ? q[1] : 0.f, valid > 2 ? q[2] : 0.f, valid > 3 ? q[3] : 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc.x += x[u].x;
+        acc.y += x[u].y;
+        acc.z += x[u].z;
+        acc.w += x[u].w;
+      }
+    }
+    for (; k < p.splits; k += kRedGroups) {
+      const float* q = W + k * stride;
+      const float4 x = vec ? *reinterpret_cast<const float4*>(q)
+                           : make_float4(q[0], valid > 1 ? q[1] : 0.f, valid > 2 ? q[2] : 0.f, valid > 3 ? q[3] : 0.f);
+      acc.x += x.x;
+      acc.y += x.y;
+      acc.z += x.z;
+      acc.w += x.w;
+    }
+  }
+  part[g][li] = acc;
+  __syncthreads();
+  if (g != 0 || item >= items) return;
+#pragma unroll
+  for (int q = 1; q < kRedGroups; ++q) {
+    acc.x += part[q][li].x;
+    acc.y += part[q][li].y;
+    acc.z += part[q][li].z;
+    acc.w += part[q][li].w;
+  }
+  const float s[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (j >= valid) continue;
+    float v = s[j];
+    if ((p.epi == TB_EPI_BIAS || p.epi == TB_EPI_BIAS_TANH || p.epi == TB_EPI_BIAS_SILU) && p.bias) v += p.bias[c + j];
+    if (p.epi == TB_EPI_BIAS_TANH) v = fast_tanh(v);
+    if (p.epi == TB_EPI_BIAS_SILU) v = fast_silu(v);
+    if (p.colsum) atomicAdd(p.colsum + c + j, v);
+    if (p.c_fp32) {
+      float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c + j;
+      if (p.c_atomic) atomicAdd(C, v);
+      else *C = v;
+    } else {
+      static_cast<__nv_bfloat16*>(p.C)[static_cast<long long>(row) * p.ldc + c + j] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// host side: tensor maps through the driver entry point (no libcuda link)
+// --------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// 2D bf16 row-major matrix [rows, cols] with leading dimension ld (elements);
+// box = {64 cols, box_rows}, 128-byte swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, long long ld, int box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t es[2] = {1, 1};
+  return f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch(const CUtensorMap& ta, const CUtensorMap& tbm, const DevArgs& p, int grid, cudaStream_t s) {
+  using S = Smem<BN>;
+  auto k = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+    attr = true;
+  }
+  k<<<grid, kThreads, S::kTotal, s>>>(ta, tbm, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" {
+
+int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
+  if (a->M <= 0 || a->N <= 0) return 0;
+  if (a->K <= 0) return static_cast<int>(cudaErrorInvalidValue);
+  // TMA: row strides must be multiples of 16 bytes, base 16-byte aligned.
+  if ((a->lda % 8) || (a->ldb % 8) || (reinterpret_cast<uintptr_t>(a->A) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->B) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  const bool swiglu = a->epi == TB_EPI_SWIGLU;
+  if (swiglu && ((a->N % 2) || a->colsum)) return static_cast<int>(cudaErrorInvalidValue);
+  int BN = (a->N > 128) ? 256 : 128;
+  if (a->bn_hint == 128 || a->bn_hint == 256) BN = a->bn_hint;
+  CUtensorMap ta, tbm;
+  // A: K-major -> matrix [M, K]; MN-major -> matrix [K, M]
+  const bool okA = a->a_mn ? make_map(&ta, a->A, a->K, a->M, a->lda, BK) : make_map(&ta, a->A, a->M, a->K, a->lda, BM);
+  const bool okB = a->b_mn ? make_map(&tbm, a->B, a->K, a->N, a->ldb, BK) : make_map(&tbm, a->B, a->N, a->K, a->ldb, BN);
+  if (!okA || !okB) return static_cast<int>(cudaErrorInvalidValue);
+
+  DevArgs p{};
+  p.M = a->M;
+  p.N = a->N;
+  p.K = a->K;
+  p.m_tiles = (a->M + BM - 1) / BM;
+  p.n_tiles = (a->N + BN - 1) / BN;
+  p.k_blocks = (a->K + BK - 1) / BK;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const size_t per_split = sizeof(float) * static_cast<size_t>(a->M) * a->N;
+  // split-K: partials go to the caller's workspace (then one reduce pass), or,
+  // without a workspace, atomically into an fp32 C
+  const bool ws_ok = a->workspace != nullptr && a->workspace_bytes >= 2 * per_split && !swiglu &&
+                     a->epi != TB_EPI_TANH_BWD && a->epi != TB_EPI_RESIDUAL;
+  const bool atomic_ok = a->c_fp32 && (a->epi == TB_EPI_NONE || a->epi == TB_EPI_BIAS) && !a->colsum;
+  int splits = a->split_k;
+  if (splits <= 0) {
+    splits = 1;
+    if ((ws_ok || atomic_ok) && tiles < num_sms() / 2) {
+      splits = (num_sms() + tiles - 1) / tiles;
+      const int max_s = (p.k_blocks + 3) / 4;  // keep >= 4 k-blocks per split
+      if (splits > max_s) splits = max_s;
+      if (ws_ok && static_cast<size_t>(splits) * per_split > a->workspace_bytes)
+        splits = static_cast<int>(a->workspace_bytes / per_split);  // prefer partials over atomics
+      if (splits < 1) splits = 1;
+    }
+  }
+  p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+  p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+  const bool use_ws = p.splits > 1 && ws_ok && static_cast<size_t>(p.splits) * per_split <= a->workspace_bytes;
+  if (p.splits > 1 && !use_ws && !atomic_ok) return static_cast<int>(cudaErrorInvalidValue);
+  p.C = a->C;
+  p.ldc = a->ldc;
+  p.c_fp32 = a->c_fp32;
+  p.c_atomic = (a->c_accumulate || (p.splits > 1 && !use_ws)) ? 1 : 0;
+  if (p.c_atomic && !a->c_fp32) return static_cast<int>(cudaErrorInvalidValue);
+  if (p.splits > 1 && !use_ws && !a->c_accumulate) {
+    // atomic split-K adds partial sums into a zeroed C
+    if (a->ldc == a->N) {
+      cudaMemsetAsync(a->C, 0, per_split, stream);
+    } else {
+      cudaMemset2DAsync(a->C, sizeof(float) * a->ldc, 0, sizeof(float) * a->N, a->M, stream);
+    }
+  }
+  if (a->colsum) cudaMemsetAsync(a->colsum, 0, sizeof(float) * a->N, stream);
+  p.bias = a->bias;
+  p.aux = static_cast<const __nv_bfloat16*>(a->aux);
+  p.ld_aux = a->ld_aux;
+  p.epi = a->epi;
+  p.alpha = a->alpha == 0.f ? 1.f : a->alpha;
+  p.ws = use_ws ? static_cast<float*>(a->workspace) : nullptr;
+  p.colsum = use_ws ? nullptr : a->colsum;
+  p.error = a->error;
+  const int total = tiles * p.splits;
+  const int grid = total < num_sms() ? total : num_sms();
+  const int am = a->a_mn ? 1 : 0, bm = a->b_mn ? 1 : 0;
+  int err = 0;
+#define TB_GEMM_DISPATCH(BNV)                                                          \
+  if (!am && !bm) err = launch<BNV, false, false>(ta, tbm, p, grid, stream);           \
+  else if (!am && bm) err = launch<BNV, false, true>(ta, tbm, p, grid, stream);        \
+  else if (am && !bm) err = launch<BNV, true, false>(ta, tbm, p, grid, stream);        \
+  else err = launch<BNV, true, true>(ta, tbm, p, grid, stream);
+  if (BN == 256) {
+    TB_GEMM_DISPATCH(256)
+  } else {
+    TB_GEMM_DISPATCH(128)
+  }
+#undef TB_GEMM_DISPATCH
+  if (err != 0 || !use_ws) return err;
+  DevArgs r = p;
+  r.ws = static_cast<float*>(a->workspace);
+  r.colsum = a->colsum;
+  const long long work = static_cast<long long>(a->M) * ((a->N + 3) / 4);
+  const long long g = (work + kRedItems - 1) / kRedItems;
+  splitk_reduce_kernel<<<static_cast<unsigned>(g), kRedItems * kRedGroups, 0, stream>>>(r);
+  return static_cast<int>(cudaGetLastError());
+}
+
+size_t tb_gemm_workspace_bytes(int M, int N, int K) {
+  // enough for the automatic split count of an fp32 M x N output
+  const int bn = N > 128 ? 256 : 128;  // the launcher's automatic tile width
+  const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  int splits = (148 + tiles - 1) / tiles;
+  const int max_s = ((K + BK - 1) / BK + 3) / 4;
+  if (splits > max_s) splits = max_s;
+  if (splits < 2) return 0;
+  return sizeof(float) * static_cast<size_t>(M) * N * splits;
+}
+
+}  // extern "C"

@@ -28,7 +28,10 @@ int tb_cartpole_reset(float* state, int* ep_len, float* ep_ret, unsigned* ep_cou
 int tb_cartpole_step(float* state, const int* action, float* obs_out, float* reward, uint8_t* done, int* ep_len,
                      float* ep_ret, unsigned* ep_count, float* stats, int n, unsigned long long seed,
                      TbCartPoleParams p, cudaStream_t s);
-int tb_ppo_cartpole_act_step(const float* logits, int A, const float* values, float* state, int* ep_len,
+int tb_pad_obs_bf16(const float* state, void* out, int n, cudaStream_t s);  // [n,4] f32 -> [n,8] bf16
+// logits [n, ldl] (first A used), values [n, ldv] (column 0); obs_bf16 (nullable) [n, 8]
+int tb_ppo_cartpole_act_step(const float* logits, int A, int ldl, const float* values, int ldv, float* state,
+                             void* obs_bf16, int* ep_len,
                              float* ep_ret, unsigned* ep_count, float* stats, float* obs_buf, int* act_buf,
                              float* logp_buf, float* val_buf, float* rew_buf, uint8_t* done_buf,
                              const long long* iter_ptr, int t, int n, unsigned long long policy_seed,
@@ -67,9 +70,14 @@ int tb_grpo_advantage(const float* rewards, float* adv, int groups, int G, float
 // ---------------- PPO ----------------
 int tb_ppo_gather(const float* obs, int obs_dim, const int* act, const float* logp, const float* adv, const float* ret,
                   const float* val, const double* adv_stats, float* o_obs, int* o_act, float* o_logp, float* o_adv,
-                  float* o_ret, float* o_val, int total, int mb_size, int n_mb, const long long* step_ptr,
-                  const long long* iter_ptr, long long step_imm, unsigned long long seed, int normalize,
-                  cudaStream_t s);
+                  float* o_ret, float* o_val, void* o_obs_bf16, int total, int mb_size, int n_mb,
+                  const long long* step_ptr, const long long* iter_ptr, long long step_imm, unsigned long long seed,
+                  int normalize, cudaStream_t s);
+int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, int ldv, const int* act,
+                       const float* old_logp, const float* adv, const float* ret, void* dlog_bf16, void* dval_bf16,
+                       float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
+                       float* db_val, cudaStream_t s);
+int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,
                 const float* adv, const float* ret, const float* old_val, float* dlogits, float* dvalue, float* stats,
                 int B, float clip, float vclip, float vf_coef, float ent_coef, cudaStream_t s);
@@ -93,6 +101,45 @@ int tb_rule_reward(const int* ids, const int* lens, int B, int T, int period_id,
 int tb_masked_kl(const float* lp, const float* ref, const float* mask, int B, int T, float coef, int k3, float* out,
                  cudaStream_t s);
 int tb_normalize_rewards(float* r, int B, int whiten, float eps, cudaStream_t s);
+
+// ---------------- tensor-core GEMM (tcgen05) ----------------
+enum {
+  TB_EPI_NONE = 0,
+  TB_EPI_BIAS = 1,
+  TB_EPI_BIAS_TANH = 2,
+  TB_EPI_BIAS_SILU = 3,
+  TB_EPI_TANH_BWD = 4,  // C = acc * (1 - aux^2)   (aux = saved tanh output)
+  TB_EPI_RESIDUAL = 5,  // C = acc + aux
+  TB_EPI_SWIGLU = 6,    // interleaved gate/up columns -> C[:, j] = silu(acc[2j]) * acc[2j+1]
+};
+#define TB_GEMM_ERR_TIMEOUT 2
+typedef struct {
+  const void* A;  // bf16; a_mn = 0: [M, K] (row stride lda), a_mn = 1: [K, M] (row stride lda)
+  long long lda;
+  int a_mn;
+  const void* B;  // bf16; b_mn = 0: [N, K] (row stride ldb), b_mn = 1: [K, N]
+  long long ldb;
+  int b_mn;
+  void* C;  // [M, N] row stride ldc; bf16 or fp32
+  long long ldc;
+  int c_fp32;
+  int c_accumulate;  // C += result (fp32 atomics)
+  int M, N, K;
+  const float* bias;  // [N] fp32 (EPI_BIAS*)
+  const void* aux;    // bf16 [M, N] row stride ld_aux (EPI_TANH_BWD / EPI_RESIDUAL)
+  long long ld_aux;
+  int epi;
+  float alpha;  // 0 or 1 = no scaling
+  int split_k;  // 0 = automatic (fp32 output, no nonlinear epilogue)
+  int bn_hint;  // 0 = automatic, else 128 or 256
+  int* error;   // optional device int: set to TB_GEMM_ERR_TIMEOUT if a wait ran out
+  void* workspace;         // optional fp32 scratch for split-K partials (else atomics into fp32 C)
+  size_t workspace_bytes;
+  float* colsum;           // optional [N] fp32: column sums of the output (e.g. a bias gradient)
+} TbGemmArgs;
+
+int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
+size_t tb_gemm_workspace_bytes(int M, int N, int K);
 
 #ifdef __cplusplus
 }

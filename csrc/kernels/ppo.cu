@@ -10,6 +10,7 @@
 // (2017), eq. 7 and 9.  The reference's PolicyEngine::Update
 // (turbol_vllm/src/policy/policy_engine.cpp:103-138) is REINFORCE with no clip;
 // its Gaussian mode is kept in the Python engine, this kernel is the PPO path.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -62,7 +63,8 @@ __global__ void ppo_gather_kernel(const float* __restrict__ obs, int obs_dim, co
                                   const float* __restrict__ ret, const float* __restrict__ val,
                                   const double* __restrict__ adv_stats, float* __restrict__ o_obs,
                                   int* __restrict__ o_act, float* __restrict__ o_logp, float* __restrict__ o_adv,
-                                  float* __restrict__ o_ret, float* __restrict__ o_val, int total, int bits,
+                                  float* __restrict__ o_ret, float* __restrict__ o_val, __nv_bfloat16* __restrict__ o_obs_bf16,
+                                  int total, int bits,
                                   int mb_size, int n_mb, const long long* __restrict__ step_ptr,
                                   const long long* __restrict__ iter_ptr, long long step_imm,
                                   unsigned long long seed, int normalize) {
@@ -75,8 +77,13 @@ __global__ void ppo_gather_kernel(const float* __restrict__ obs, int obs_dim, co
                              mix32(static_cast<uint32_t>(epoch) + 0x165667b1u));
   const uint32_t pos = static_cast<uint32_t>(mb) * mb_size + i;
   const uint32_t j = feistel_perm(pos, static_cast<uint32_t>(total), bits, key);
-  for (int k = 0; k < obs_dim; ++k)
-    o_obs[static_cast<size_t>(i) * obs_dim + k] = obs[static_cast<size_t>(j) * obs_dim + k];
+  for (int k = 0; k < obs_dim; ++k) {
+    const float x = obs[static_cast<size_t>(j) * obs_dim + k];
+    if (o_obs) o_obs[static_cast<size_t>(i) * obs_dim + k] = x;
+    if (o_obs_bf16) o_obs_bf16[static_cast<size_t>(i) * 8 + k] = __float2bfloat16_rn(x);
+  }
+  if (o_obs_bf16)
+    for (int k = obs_dim; k < 8; ++k) o_obs_bf16[static_cast<size_t>(i) * 8 + k] = __float2bfloat16_rn(0.f);
   o_act[i] = act[j];
   o_logp[i] = logp[j];
   float a = adv[j];
@@ -191,6 +198,111 @@ __global__ void ppo_loss_kernel(const float* __restrict__ logits, const float* _
   }
 }
 
+// Same loss, on the tensor-core MLP's padded layout: logits [B, ldl] and values
+// [B, ldv] (column 0) in fp32; writes bf16 gradients d logits [B, 8] and
+// d value [B, 8] (padding columns zero), already divided by B.
+template <int A>
+__global__ void ppo_loss_padded_kernel(const float* __restrict__ logits, int ldl, const float* __restrict__ value,
+                                       int ldv, const int* __restrict__ act, const float* __restrict__ old_logp,
+                                       const float* __restrict__ adv, const float* __restrict__ ret,
+                                       __nv_bfloat16* __restrict__ dlog, __nv_bfloat16* __restrict__ dval,
+                                       float* __restrict__ stats, int B, float clip, float vf_coef, float ent_coef,
+                                       float* __restrict__ db_log, float* __restrict__ db_val) {
+  __shared__ float red[kBlock / 32];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  float s_pg = 0.f, s_v = 0.f, s_h = 0.f, s_kl = 0.f, s_cf = 0.f;
+  float gsum[A + 1];  // column sums of the bf16 gradients (output-bias gradients)
+#pragma unroll
+  for (int k = 0; k <= A; ++k) gsum[k] = 0.f;
+  if (i < B) {
+    float l[A], p[A];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      l[k] = logits[static_cast<size_t>(i) * ldl + k];
+      mx = fmaxf(mx, l[k]);
+    }
+    float se = 0.f;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      p[k] = __expf(l[k] - mx);
+      se += p[k];
+    }
+    const float inv = 1.f / se, lse = mx + __logf(se);
+    float H = 0.f;
+#pragma unroll
+    for (int k = 0; k < A; ++k) {
+      p[k] *= inv;
+      H -= p[k] * (l[k] - lse);
+    }
+    const int a = act[i];
+    const float lp = l[a] - lse;
+    const float lr = lp - old_logp[i];
+    const float ratio = __expf(lr);
+    const float Ad = adv[i];
+    const float un = ratio * Ad;
+    const float cl = fminf(fmaxf(ratio, 1.f - clip), 1.f + clip) * Ad;
+    const bool use_unclipped = un <= cl || (ratio > 1.f - clip && ratio < 1.f + clip);
+    const float dlp = use_unclipped ? -Ad * ratio : 0.f;
+    const float V = value[static_cast<size_t>(i) * ldv], R = ret[i];
+    const float scale = 1.f / static_cast<float>(B);
+    __nv_bfloat16 g8[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float g = 0.f;
+      if (k < A) g = (dlp * ((k == a ? 1.f : 0.f) - p[k]) + ent_coef * p[k] * ((l[k] - lse) + H)) * scale;
+      g8[k] = __float2bfloat16_rn(g);
+      if (k < A) gsum[k] = __bfloat162float(g8[k]);
+    }
+    *reinterpret_cast<uint4*>(dlog + static_cast<size_t>(i) * 8) = *reinterpret_cast<uint4*>(g8);
+    __nv_bfloat16 v8[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v8[k] = __float2bfloat16_rn(k == 0 ? vf_coef * (V - R) * scale : 0.f);
+    gsum[A] = __bfloat162float(v8[0]);
+    *reinterpret_cast<uint4*>(dval + static_cast<size_t>(i) * 8) = *reinterpret_cast<uint4*>(v8);
+    s_pg = -fminf(un, cl);
+    s_v = 0.5f * (V - R) * (V - R);
+    s_h = H;
+    s_kl = (ratio - 1.f) - lr;
+    s_cf = fabsf(ratio - 1.f) > clip ? 1.f : 0.f;
+  }
+  if (stats) {
+    s_pg = tb::block_sum(s_pg, red);
+    s_v = tb::block_sum(s_v, red);
+    s_h = tb::block_sum(s_h, red);
+    s_kl = tb::block_sum(s_kl, red);
+    s_cf = tb::block_sum(s_cf, red);
+    if (threadIdx.x == 0) {
+      atomicAdd(&stats[0], s_pg);
+      atomicAdd(&stats[1], s_v);
+      atomicAdd(&stats[2], s_h);
+      atomicAdd(&stats[3], s_kl);
+      atomicAdd(&stats[4], s_cf);
+      atomicAdd(&stats[5], static_cast<float>(min(B - static_cast<int>(blockIdx.x) * kBlock, kBlock)));
+    }
+  }
+  if (db_log != nullptr) {
+#pragma unroll
+    for (int k = 0; k <= A; ++k) {
+      const float t = tb::block_sum(gsum[k], red);
+      if (threadIdx.x == 0) atomicAdd(k < A ? &db_log[k] : db_val, t);
+    }
+  }
+}
+
+// out[c] = sum over rows of x[r, c] (bf16 in, fp32 out).  Each block sums a
+// chunk of rows for a span of columns and adds its partial atomically; `out`
+// is zeroed by the launcher.
+__global__ void colsum_bf16_kernel(const __nv_bfloat16* __restrict__ x, long long ld, int rows, int cols,
+                                   int rows_per_block, float* __restrict__ out) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += __bfloat162float(x[static_cast<long long>(r) * ld + c]);
+  atomicAdd(&out[c], s);
+}
+
 __global__ void counter_add_kernel(long long* c, long long v) { *c += v; }
 
 }  // namespace
@@ -199,15 +311,17 @@ extern "C" {
 
 int tb_ppo_gather(const float* obs, int obs_dim, const int* act, const float* logp, const float* adv, const float* ret,
                   const float* val, const double* adv_stats, float* o_obs, int* o_act, float* o_logp, float* o_adv,
-                  float* o_ret, float* o_val, int total, int mb_size, int n_mb, const long long* step_ptr,
-                  const long long* iter_ptr, long long step_imm, unsigned long long seed, int normalize,
-                  cudaStream_t s) {
+                  float* o_ret, float* o_val, void* o_obs_bf16, int total, int mb_size, int n_mb,
+                  const long long* step_ptr, const long long* iter_ptr, long long step_imm, unsigned long long seed,
+                  int normalize, cudaStream_t s) {
   if (mb_size <= 0) return 0;
+  if (o_obs_bf16 != nullptr && obs_dim > 8) return static_cast<int>(cudaErrorInvalidValue);
   if (static_cast<long long>(mb_size) * n_mb > total) return static_cast<int>(cudaErrorInvalidValue);
   int bits = 1;
   while ((1LL << bits) < total) ++bits;
   ppo_gather_kernel<<<(mb_size + kBlock - 1) / kBlock, kBlock, 0, s>>>(
-      obs, obs_dim, act, logp, adv, ret, val, adv_stats, o_obs, o_act, o_logp, o_adv, o_ret, o_val, total, bits,
+      obs, obs_dim, act, logp, adv, ret, val, adv_stats, o_obs, o_act, o_logp, o_adv, o_ret, o_val,
+      static_cast<__nv_bfloat16*>(o_obs_bf16), total, bits,
       mb_size, n_mb, step_ptr, iter_ptr, step_imm, seed, normalize);
   return static_cast<int>(cudaGetLastError());
 }
@@ -233,6 +347,46 @@ int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, 
       return static_cast<int>(cudaErrorInvalidValue);
   }
 #undef TB_PPO_CASE
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, int ldv, const int* act,
+                       const float* old_logp, const float* adv, const float* ret, void* dlog_bf16, void* dval_bf16,
+                       float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
+                       float* db_val, cudaStream_t s) {
+  if (B <= 0) return 0;
+  if ((db_log == nullptr) != (db_val == nullptr)) return static_cast<int>(cudaErrorInvalidValue);
+  if (db_log) {
+    cudaMemsetAsync(db_log, 0, sizeof(float) * A, s);
+    cudaMemsetAsync(db_val, 0, sizeof(float), s);
+  }
+  const int g = (B + kBlock - 1) / kBlock;
+  auto* dl = static_cast<__nv_bfloat16*>(dlog_bf16);
+  auto* dv = static_cast<__nv_bfloat16*>(dval_bf16);
+#define TB_PPO_CASE(K)                                                                                           \
+  case K:                                                                                                        \
+    ppo_loss_padded_kernel<K><<<g, kBlock, 0, s>>>(logits, ldl, value, ldv, act, old_logp, adv, ret, dl, dv,   \
+                                                   stats, B, clip, vf_coef, ent_coef, db_log, db_val);          \
+    break;
+  switch (A) {
+    TB_PPO_CASE(2)
+    TB_PPO_CASE(3)
+    TB_PPO_CASE(4)
+    TB_PPO_CASE(6)
+    TB_PPO_CASE(8)
+    default:
+      return static_cast<int>(cudaErrorInvalidValue);
+  }
+#undef TB_PPO_CASE
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return 0;
+  cudaMemsetAsync(out, 0, sizeof(float) * cols, s);
+  const int rpb = 256;
+  dim3 grid((rows + rpb - 1) / rpb, (cols + kBlock - 1) / kBlock);
+  colsum_bf16_kernel<<<grid, kBlock, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ld, rows, cols, rpb, out);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -1,0 +1,94 @@
+"""tcgen05 GEMM vs a plain fp32 PyTorch matmul of the same bf16 operands."""
+import pytest
+import torch
+
+from turbol_b200._native import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(A, B, a_mn, b_mn):
+    a = A.float().t() if a_mn else A.float()
+    b = B.float() if b_mn else B.float().t()
+    return a @ b
+
+
+def _mk(shape, dev, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * 0.5).to(dev, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 512, 1024), (300, 200, 136), (1000, 384, 520),
+                                   (4096, 256, 256), (64, 1536, 1536)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_layouts(M, N, K, a_mn, b_mn, dev):
+    if (a_mn and M % 8) or (b_mn and N % 8):
+        pytest.skip("TMA: the contiguous dim of an MN-major operand must be a multiple of 8 (16-byte rows)")
+    A = _mk((K, M) if a_mn else (M, K), dev, M + K)
+    B = _mk((K, N) if b_mn else (N, K), dev, N + K + 1)
+    C = torch.empty(M, N, device=dev, dtype=torch.float32)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops().gemm(A, B, C, a_mn, b_mn, error=err)
+    ref = _ref(A, B, a_mn, b_mn)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.allclose(C, ref, atol=2e-2 * (K ** 0.5) / 8, rtol=1e-2), (C - ref).abs().max()
+
+
+def test_gemm_bf16_out_and_epilogues(dev):
+    M, N, K = 777, 512, 256
+    A, B = _mk((M, K), dev, 1), _mk((N, K), dev, 2)
+    bias = torch.randn(N, device=dev)
+    ref = _ref(A, B, False, False)
+    o = ops()
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    o.gemm(A, B, C, bias=bias, epi=o.EPI_BIAS_TANH)
+    assert torch.allclose(C.float(), torch.tanh(ref + bias), atol=2e-2)
+    o.gemm(A, B, C, bias=bias, epi=o.EPI_BIAS_SILU)
+    assert torch.allclose(C.float(), torch.nn.functional.silu(ref + bias), atol=5e-2, rtol=2e-2)
+    H = torch.tanh(torch.randn(M, N, device=dev)).to(torch.bfloat16)
+    Cf = torch.empty(M, N, device=dev)
+    o.gemm(A, B, Cf, aux=H, epi=o.EPI_TANH_BWD)
+    assert torch.allclose(Cf, ref * (1 - H.float() ** 2), atol=2e-2)
+    o.gemm(A, B, Cf, aux=H, epi=o.EPI_RESIDUAL)
+    assert torch.allclose(Cf, ref + H.float(), atol=2e-2)
+    S = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+    o.gemm(A, B, S, epi=o.EPI_SWIGLU)
+    exp = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+    assert torch.allclose(S.float(), exp, atol=5e-2, rtol=2e-2)
+    o.gemm(A, B, Cf, alpha=0.5)
+    assert torch.allclose(Cf, 0.5 * ref, atol=1e-2)
+
+
+def test_gemm_split_k_and_accumulate(dev):
+    # weight-gradient shape: dW[256, 256] = dY^T X over 32768 rows (both MN-major)
+    R, N, K = 32768, 256, 256
+    dY, X = _mk((R, N), dev, 3), _mk((R, K), dev, 4)
+    dW = torch.empty(N, K, device=dev)
+    ops().gemm(dY, X, dW, True, True)
+    ref = dY.float().t() @ X.float()
+    assert torch.allclose(dW, ref, atol=0.5, rtol=1e-2), (dW - ref).abs().max()
+    ops().gemm(dY, X, dW, True, True, accumulate=True)
+    assert torch.allclose(dW, 2 * ref, atol=1.0, rtol=1e-2)
+
+
+def test_gemm_splitk_workspace_and_colsum(dev):
+    o = ops()
+    R, N, K = 32768, 256, 256
+    dY, X = _mk((R, N), dev, 5), _mk((R, K), dev, 6)
+    ws = torch.empty(o.gemm_workspace_numel(N, K, R), device=dev)
+    assert ws.numel() > 0
+    dW = torch.empty(N, K, device=dev)
+    o.gemm(dY, X, dW, True, True, workspace=ws)
+    ref = dY.float().t() @ X.float()
+    assert torch.allclose(dW, ref, atol=0.5, rtol=1e-2)
+    # tanh-backward epilogue with fused column sums (a bias gradient)
+    M = 3000
+    A, B = _mk((M, 64), dev, 7), _mk((64, 256), dev, 8)  # B MN-major [K, N]
+    H = torch.tanh(torch.randn(M, 256, device=dev)).to(torch.bfloat16)
+    C = torch.empty(M, 256, device=dev, dtype=torch.bfloat16)
+    cs = torch.empty(256, device=dev)
+    o.gemm(A, B, C, False, True, aux=H, epi=o.EPI_TANH_BWD, colsum=cs)
+    exp = (A.float() @ B.float()) * (1 - H.float() ** 2)
+    assert torch.allclose(C.float(), exp, atol=3e-2, rtol=2e-2)
+    assert torch.allclose(cs, exp.sum(0), atol=0.5, rtol=2e-2)

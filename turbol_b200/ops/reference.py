@@ -15,8 +15,9 @@ def gae(rewards, values, dones, gamma: float = 0.99, lam: float = 0.95):
     """GAE over [T, N] (values [T+1, N]); recurrence of the reference's
     turbol_vllm/src/cuda/gae.cu:31-44."""
     T = rewards.shape[0]
-    adv = torch.zeros_like(rewards, dtype=torch.float32)
-    last = torch.zeros_like(rewards[0], dtype=torch.float32)
+    dt = torch.promote_types(rewards.dtype, torch.float32)
+    adv = torch.zeros_like(rewards, dtype=dt)
+    last = torch.zeros_like(rewards[0], dtype=dt)
     for t in range(T - 1, -1, -1):
         nd = 1.0 - dones[t].float()
         delta = rewards[t] + gamma * nd * values[t + 1] - values[t]

@@ -70,14 +70,17 @@ class FusedAdam:
     of the weights written in the same pass."""
 
     def __init__(self, flat_param, flat_grad, lr=3e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
-                 max_grad_norm=0.0, bf16_shadow=False):
+                 max_grad_norm=0.0, bf16_shadow=False, shadow=None):
         self.p, self.g = flat_param, flat_grad
         self.m = torch.zeros_like(flat_param)
         self.v = torch.zeros_like(flat_param)
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.step_t = torch.zeros(1, dtype=torch.int64, device=flat_param.device)
-        self.shadow = torch.empty_like(flat_param, dtype=torch.bfloat16) if bf16_shadow else None
+        if shadow is not None:
+            self.shadow = shadow
+        else:
+            self.shadow = torch.empty_like(flat_param, dtype=torch.bfloat16) if bf16_shadow else None
         self.gnorm = torch.zeros(1, dtype=torch.float32, device=flat_param.device) if max_grad_norm > 0 else None
         self._host_step = 0
 

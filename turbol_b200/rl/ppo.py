@@ -83,8 +83,27 @@ class PPOTrainer:
             raise ValueError("num_envs * rollout_steps must be a multiple of minibatch_size")
         dev = str(self.device) if self.cuda else "cpu"
         self.env = C.GPUEnvironment(N, 4, 2, dev, "cartpole", seed=cfg.seed * 7919 + rank * 104729 + 17)
-        self.policy = ActorCritic(4, 2, cfg.hidden, discrete=True, device=self.device, seed=cfg.seed)
-        self.opt = FusedAdam(self.policy.fp.flat, self.policy.fp.grad, lr=cfg.lr, max_grad_norm=cfg.max_grad_norm)
+        # tensor-core path: bf16 GEMMs with fused epilogues and a hand-written
+        # backward; otherwise PyTorch autograd (CPU, fp32 or unequal hidden sizes)
+        self.fused = (self.cuda and cfg.compute_dtype == "bf16" and len(cfg.hidden) == 2
+                      and cfg.hidden[0] == cfg.hidden[1] and cfg.hidden[0] % 64 == 0)
+        if self.fused:
+            from ..models.fused_mlp import FusedActorCritic
+
+            self.net = FusedActorCritic(4, 2, cfg.hidden, device=self.device, seed=cfg.seed)
+            self.policy = None
+            self.flat, self.flat_grad = self.net.flat, self.net.grad
+            self.opt = FusedAdam(self.net.flat, self.net.grad, lr=cfg.lr, max_grad_norm=cfg.max_grad_norm,
+                                 shadow=self.net.shadow)
+            self.obs_bf16 = torch.zeros(N, 8, device=self.device, dtype=torch.bfloat16)
+            self.mb_obs_bf16 = torch.zeros(cfg.minibatch_size, 8, device=self.device, dtype=torch.bfloat16)
+            self.ws_roll = self.net.workspace(N)
+            self.ws_mb = self.net.workspace(cfg.minibatch_size)
+        else:
+            self.policy = ActorCritic(4, 2, cfg.hidden, discrete=True, device=self.device, seed=cfg.seed)
+            self.flat, self.flat_grad = self.policy.fp.flat, self.policy.fp.grad
+            self.opt = FusedAdam(self.policy.fp.flat, self.policy.fp.grad, lr=cfg.lr,
+                                 max_grad_norm=cfg.max_grad_norm)
         self.grad_sync = grad_sync
         self.state = self.env.state()  # live [N, 4] view
         self.ep_len, self.ep_ret, self.ep_count, self.ep_stats = self.env.episode_buffers()
@@ -108,6 +127,7 @@ class PPOTrainer:
         self.iter_t = torch.zeros(1, device=self.device, dtype=torch.int64)
         self.mb_step_t = torch.zeros(1, device=self.device, dtype=torch.int64)
         self.scratch = None
+        self._empty_f32 = torch.empty(0, **f32)
         if self.cuda:
             n = _ops().gae_scratch_numel(T, N)
             self.scratch = torch.empty(max(n, 1), **f32)
@@ -127,13 +147,24 @@ class PPOTrainer:
         o = _ops()
         T = self.cfg.rollout_steps
         params = {}
-        with torch.no_grad(), self._autocast():
+        if self.fused:
+            o.pad_obs_bf16(self.state, self.obs_bf16)
+            for t in range(T):
+                logits, v = self.net.forward(self.obs_bf16, self.ws_roll)
+                o.ppo_cartpole_act_step(logits, 2, v, self.state, self.obs_bf16, self.ep_len, self.ep_ret,
+                                        self.ep_count, self.ep_stats, self.obs_buf, self.act_buf, self.logp_buf,
+                                        self.val_buf, self.rew_buf, self.done_buf, self.iter_t, t, self.policy_seed,
+                                        self.env_seed, params)
+            _, v = self.net.forward(self.obs_bf16, self.ws_roll)
+            self.val_buf[T].copy_(v[:, 0])
+        else:
+          with torch.no_grad(), self._autocast():
             for t in range(T):
                 logits, v = self.policy(self.state)
-                o.ppo_cartpole_act_step(logits.float().contiguous(), v.float().contiguous(), self.state, self.ep_len,
-                                        self.ep_ret, self.ep_count, self.ep_stats, self.obs_buf, self.act_buf,
-                                        self.logp_buf, self.val_buf, self.rew_buf, self.done_buf, self.iter_t, t,
-                                        self.policy_seed, self.env_seed, params)
+                o.ppo_cartpole_act_step(logits.float().contiguous(), 2, v.float().contiguous(), self.state, None,
+                                        self.ep_len, self.ep_ret, self.ep_count, self.ep_stats, self.obs_buf,
+                                        self.act_buf, self.logp_buf, self.val_buf, self.rew_buf, self.done_buf,
+                                        self.iter_t, t, self.policy_seed, self.env_seed, params)
             self.val_buf[T].copy_(self.policy.critic(self.state).float())
         self.adv_stats.zero_()
         gae(self.rew_buf, self.val_buf, self.done_buf, self.cfg.gamma, self.cfg.lam, stats=self.adv_stats,
@@ -145,7 +176,7 @@ class PPOTrainer:
         self._minibatch_apply_gpu(self._sync_grads())
 
     def _sync_grads(self):
-        return self.grad_sync(self.policy.fp.grad) if self.grad_sync is not None else 1.0
+        return self.grad_sync(self.flat_grad) if self.grad_sync is not None else 1.0
 
     def _minibatch_apply_gpu(self, scale):
         self.opt.step(grad_scale=scale)
@@ -154,6 +185,17 @@ class PPOTrainer:
     def _minibatch_grad_gpu(self):
         cfg = self.cfg
         o = _ops()
+        if self.fused:
+            o.ppo_gather(self.obs_buf, self.act_buf, self.logp_buf, self.adv, self.ret, self.val_buf, self.adv_stats,
+                         self._empty_f32, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, None,
+                         cfg.n_minibatches, self.mb_step_t, self.iter_t, 0, self.policy_seed ^ 0x5851F42D,
+                         cfg.norm_adv, self.mb_obs_bf16)
+            logits, v = self.net.forward(self.mb_obs_bf16, self.ws_mb)
+            o.ppo_loss_padded(logits, 2, v, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, self.ws_mb["dlog"],
+                              self.ws_mb["dval"], self.loss_stats, cfg.clip, cfg.vf_coef, cfg.ent_coef,
+                              self.net.g["b3a"], self.net.g["b3c"])
+            self.net.backward(self.mb_obs_bf16, self.ws_mb, out_bias_grads_done=True)
+            return
         o.ppo_gather(self.obs_buf, self.act_buf, self.logp_buf, self.adv, self.ret, self.val_buf, self.adv_stats,
                      self.mb_obs, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, None, cfg.n_minibatches,
                      self.mb_step_t, self.iter_t, 0, self.policy_seed ^ 0x5851F42D, cfg.norm_adv)
@@ -206,7 +248,8 @@ class PPOTrainer:
         with torch.cuda.graph(g_end, pool=pool):
             self._end_iteration_gpu()
         torch.cuda.synchronize(self.device)
-        self.policy.fp.rebind_grads()
+        if not self.fused:
+            self.policy.fp.rebind_grads()
         self._graphs = (g_roll, mb, g_end)
 
     def release_graphs(self):
@@ -308,13 +351,17 @@ class PPOTrainer:
         return self.cfg.batch
 
     def state_dict(self):
-        return {"policy": self.policy.state_dict(), "optim": self.opt.state_dict(), "iteration": self.iteration,
+        pol = self.net.state_dict() if self.fused else self.policy.state_dict()
+        return {"policy": pol, "optim": self.opt.state_dict(), "iteration": self.iteration,
                 "iter_t": self.iter_t.clone(), "env_state": self.state.clone(),
                 "ep": (self.ep_len.clone(), self.ep_ret.clone(), self.ep_count.clone())}
 
     def load_state_dict(self, sd):
         with torch.no_grad():
-            self.policy.load_state_dict(sd["policy"])
+            if self.fused:
+                self.net.load_state_dict(sd["policy"])
+            else:
+                self.policy.load_state_dict(sd["policy"])
             self.opt.load_state_dict(sd["optim"])
             self.iteration = int(sd["iteration"])
             self.iter_t.copy_(sd["iter_t"])
