@@ -149,16 +149,9 @@ def run_ours(args):
     from turbol_b200.rl.ppo import PPOConfig, PPOTrainer
 
     rank, world, local = dist_setup(args.gpus)
-    grad_sync = None
-    if world > 1:
-        from turbol_b200.parallel.dp import make_grad_sync
-
-        grad_sync = make_grad_sync(args.dp)
     cfg = PPOConfig(num_envs=args.num_envs, rollout_steps=args.rollout, hidden=HIDDEN, epochs=EPOCHS,
                     minibatch_size=MINIBATCH, lr=3e-4, clip=0.2, seed=1, compute_dtype="bf16", cuda_graphs=True)
-    tr = PPOTrainer(cfg, device=f"cuda:{local}", grad_sync=grad_sync, rank=rank)
-    if grad_sync is not None and hasattr(grad_sync, "bind"):
-        grad_sync.bind(tr.policy.fp.grad)
+    tr = PPOTrainer(cfg, device=f"cuda:{local}", rank=rank, dp=args.dp if world > 1 else "none")
     for _ in range(args.warmup):
         tr.train_iteration()
     tr.metrics()
@@ -193,9 +186,12 @@ def run_ours(args):
     steps_total = world * cfg.batch * args.steps
     value = steps_total / (ms_dev / 1e3)
     e2e_value = steps_total / e2e_s
-    launches_per_iter = cfg.rollout_steps + 1 + cfg.epochs * cfg.n_minibatches * 4 + 1
-    if grad_sync is not None:
-        launches_per_iter += cfg.epochs * cfg.n_minibatches * getattr(grad_sync, "kernels_per_call", 0)
+    tr.check_collectives()
+    # our kernels per iteration: rollout step = 5 GEMMs + act/step kernel; bootstrap
+    # 5 GEMMs + pad; GAE 1; per minibatch gather + 5 fwd GEMMs + loss + 9 bwd GEMMs
+    # + 3 split-K reduces + optimizer (Adam or the fused DP kernel) + counter; end counter
+    per_mb = 1 + 5 + 1 + 9 + 3 + 1 + 1
+    launches_per_iter = cfg.rollout_steps * 6 + 6 + 1 + cfg.epochs * cfg.n_minibatches * per_mb + 1
     out = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_dev / args.steps, "higher_is_better": True, "scaling": "weak",

@@ -1,0 +1,265 @@
+// Collective kernels over NVLink peer memory (one process per GPU; every rank
+// maps every peer's buffers through CUDA IPC, so a kernel addresses remote HBM
+// with ordinary loads and stores).
+//
+//   tb_peer_allreduce       sum (or mean) of a buffer across ranks: rank r
+//                           reduces slice r by reading it from every peer and
+//                           writes the result into every peer's output.
+//   tb_peer_allreduce_adam  the data-parallel optimizer step in one kernel:
+//                           reduce-scatter of the fp32 gradient (peer loads),
+//                           Adam on the owned shard (ZeRO-1 style: the moments
+//                           of a shard live only on its owner), all-gather of
+//                           the updated fp32 weights and their bf16 copy
+//                           (peer stores).
+//
+// Synchronization: each rank owns a flag array in its peer buffer; a release
+// store of the call's epoch into every peer's slot says "my inputs are ready",
+// and an acquire spin (bounded) on all slots gates the reads.  The last block
+// to finish (a local atomic counter) publishes the second flag ("my outputs
+// are written into you") and waits for everyone else's before the kernel ends,
+// so the next kernel on the stream sees complete weights.  Every wait gives up
+// after a time budget and sets the error word instead of hanging; the host
+// checks it.  The epoch lives in device memory so the kernel can be replayed
+// from a CUDA graph.  No TMA or multicast is involved: peer traffic is plain
+// 16-byte vector loads and stores.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "device_common.cuh"
+#include "kernels.h"
+
+namespace {
+
+constexpr int kBlock = 512;
+constexpr unsigned long long kBudgetNs = 4000000000ull;  // 4 s
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until flags[0..W) (local memory, written by peers) all reach `epoch`.
+__device__ bool wait_all(const unsigned* flags, int W, unsigned epoch, int* err, int site) {
+  const unsigned long long t0 = now_ns();
+  for (int p = 0; p < W; ++p) {
+    while (ld_acquire(flags + p) < epoch) {
+      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+      if (now_ns() - t0 > kBudgetNs) {
+        atomicCAS(err, 0, site);
+        return false;
+      }
+      __nanosleep(100);
+    }
+  }
+  return true;
+}
+
+struct Hdr {
+  unsigned flags_in[TB_MAX_PEERS];   // "peer p's inputs are ready" (epoch)
+  unsigned flags_out[TB_MAX_PEERS];  // "peer p finished writing its outputs into me" (epoch)
+};
+
+// Slice [lo, hi) of n elements owned by `rank`, rounded to multiples of 4.
+__device__ __forceinline__ void owned_slice(long long n, int rank, int W, long long& lo, long long& hi) {
+  const long long n4 = (n + 3) / 4;
+  const long long per = (n4 + W - 1) / W;
+  lo = min(n4, per * rank) * 4;
+  hi = min(n, min(n4, per * (rank + 1)) * 4);
+}
+
+__device__ void publish_and_finish(const TbPeerTable& t, unsigned epoch, unsigned* done_ctr, int* err) {
+  // every block: make this block's peer stores visible, then count in
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(done_ctr, 1u);
+    if (prev == gridDim.x - 1) {  // last block of this rank
+      *done_ctr = 0;
+      for (int p = 0; p < t.world; ++p) {
+        Hdr* h = reinterpret_cast<Hdr*>(t.hdr[p]);
+        st_release(&h->flags_out[t.rank], epoch);
+      }
+      wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_out, t.world, epoch, err, 2);
+      *t.epoch_ctr = epoch;  // next call uses epoch + 1
+    }
+  }
+}
+
+__device__ unsigned begin_call(const TbPeerTable& t, int* err, bool* ok) {
+  const unsigned epoch = *t.epoch_ctr + 1;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < t.world; ++p) st_release(&reinterpret_cast<Hdr*>(t.hdr[p])->flags_in[t.rank], epoch);
+    }
+    s_ok = wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_in, t.world, epoch, err, 1) ? 1 : 0;
+  }
+  __syncthreads();
+  *ok = s_ok != 0;
+  return epoch;
+}
+
+__global__ void __launch_bounds__(kBlock) allreduce_kernel(TbPeerTable t, long long in_off, long long out_off,
+                                                           long long n, float scale, unsigned* done_ctr, int* err) {
+  bool ok;
+  const unsigned epoch = begin_call(t, err, &ok);
+  if (ok) {
+    long long lo, hi;
+    owned_slice(n, t.rank, t.world, lo, hi);
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x * 4;
+    for (long long i = lo + (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < hi; i += stride) {
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      const bool full = i + 4 <= hi;
+      for (int p = 0; p < t.world; ++p) {
+        const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + in_off) + i;
+        if (full) {
+          const float4 x = *reinterpret_cast<const float4*>(src);
+          s.x += x.x;
+          s.y += x.y;
+          s.z += x.z;
+          s.w += x.w;
+        } else {
+          s.x += src[0];
+          if (i + 1 < hi) s.y += src[1];
+          if (i + 2 < hi) s.z += src[2];
+        }
+      }
+      s.x *= scale;
+      s.y *= scale;
+      s.z *= scale;
+      s.w *= scale;
+      for (int p = 0; p < t.world; ++p) {
+        float* dst = reinterpret_cast<float*>(static_cast<char*>(t.base[p]) + out_off) + i;
+        if (full) {
+          *reinterpret_cast<float4*>(dst) = s;
+        } else {
+          dst[0] = s.x;
+          if (i + 1 < hi) dst[1] = s.y;
+          if (i + 2 < hi) dst[2] = s.z;
+        }
+      }
+    }
+  }
+  publish_and_finish(t, epoch, done_ctr, err);
+}
+
+__device__ __forceinline__ float adam1(float& p, float g, float& m, float& v, const TbAdamParams& h, float bc1,
+                                       float bc2) {
+  m = h.beta1 * m + (1.f - h.beta1) * g;
+  v = h.beta2 * v + (1.f - h.beta2) * g * g;
+  p -= h.lr * ((m / bc1) / (sqrtf(v / bc2) + h.eps) + h.weight_decay * p);
+  return p;
+}
+
+__global__ void __launch_bounds__(kBlock) allreduce_adam_kernel(TbPeerTable t, long long grad_off,
+                                                                long long param_off, long long shadow_off,
+                                                                long long n, float* m, float* v, TbAdamParams hp,
+                                                                const long long* step_ptr, unsigned* done_ctr,
+                                                                int* err) {
+  bool ok;
+  const unsigned epoch = begin_call(t, err, &ok);
+  if (ok) {
+    const long long step = (step_ptr ? *step_ptr : hp.step) + 1;
+    const float bc1 = 1.f - powf(hp.beta1, static_cast<float>(step));
+    const float bc2 = 1.f - powf(hp.beta2, static_cast<float>(step));
+    long long lo, hi;
+    owned_slice(n, t.rank, t.world, lo, hi);
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x * 4;
+    const float gs = hp.grad_scale;
+    for (long long i = lo + (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < hi; i += stride) {
+      const int cnt = static_cast<int>(min(4LL, hi - i));
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int p = 0; p < t.world; ++p) {
+        const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + grad_off) + i;
+        if (cnt == 4) {
+          const float4 x = *reinterpret_cast<const float4*>(src);
+          g[0] += x.x;
+          g[1] += x.y;
+          g[2] += x.z;
+          g[3] += x.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < cnt) g[j] += src[j];
+        }
+      }
+      // owner's fp32 master weights (local) -> Adam -> broadcast
+      float* pl = reinterpret_cast<float*>(static_cast<char*>(t.base[t.rank]) + param_off) + i;
+      float pv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < cnt) {
+          pv[j] = pl[j];
+          float mm = m[i + j], vv = v[i + j];
+          adam1(pv[j], g[j] * gs, mm, vv, hp, bc1, bc2);
+          m[i + j] = mm;
+          v[i + j] = vv;
+        }
+      }
+      __nv_bfloat162 b01 = __floats2bfloat162_rn(pv[0], pv[1]), b23 = __floats2bfloat162_rn(pv[2], pv[3]);
+      for (int p = 0; p < t.world; ++p) {
+        float* dp = reinterpret_cast<float*>(static_cast<char*>(t.base[p]) + param_off) + i;
+        __nv_bfloat16* ds = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(t.base[p]) + shadow_off) + i;
+        if (cnt == 4) {
+          *reinterpret_cast<float4*>(dp) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+          reinterpret_cast<__nv_bfloat162*>(ds)[0] = b01;
+          reinterpret_cast<__nv_bfloat162*>(ds)[1] = b23;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (j < cnt) {
+              dp[j] = pv[j];
+              ds[j] = __float2bfloat16_rn(pv[j]);
+            }
+          }
+        }
+      }
+    }
+  }
+  publish_and_finish(t, epoch, done_ctr, err);
+}
+
+int grid_for(long long n, int world) {
+  const long long per = (n / 4 + world) / world;
+  long long g = (per + kBlock - 1) / kBlock;
+  if (g > 148) g = 148;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t tb_peer_header_bytes() { return sizeof(Hdr); }
+
+int tb_peer_allreduce(TbPeerTable t, long long in_off, long long out_off, long long n, float scale,
+                      unsigned* done_ctr, int* err, cudaStream_t s) {
+  if (t.world < 1 || t.world > TB_MAX_PEERS || (in_off & 15) || (out_off & 15)) return static_cast<int>(cudaErrorInvalidValue);
+  allreduce_kernel<<<grid_for(n, t.world), kBlock, 0, s>>>(t, in_off, out_off, n, scale, done_ctr, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_off, long long shadow_off, long long n,
+                           float* m, float* v, TbAdamParams hp, const long long* step_ptr, unsigned* done_ctr,
+                           int* err, cudaStream_t s) {
+  if (t.world < 1 || t.world > TB_MAX_PEERS || (grad_off & 15) || (param_off & 15) || (shadow_off & 7))
+    return static_cast<int>(cudaErrorInvalidValue);
+  allreduce_adam_kernel<<<grid_for(n, t.world), kBlock, 0, s>>>(t, grad_off, param_off, shadow_off, n, m, v, hp,
+                                                                step_ptr, done_ctr, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // extern "C"

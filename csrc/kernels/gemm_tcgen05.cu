@@ -64,7 +64,10 @@ struct Smem {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = BN == 256 ? 4 : 6;
   static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kTotal = kBarOffset + 256 + 1024;  // barriers + slack for 1024-B alignment
+  static constexpr int kStgOffset = kBarOffset + 256;     // per-warp store staging (bf16 outputs)
+  static constexpr int kStgWords = 20;                     // 16 words of a 32-column row + 4 pad
+  static constexpr int kStgBytes = kEpiWarps * 32 * kStgWords * 4;
+  static constexpr int kTotal = kStgOffset + kStgBytes + 1024;  // + slack for 1024-B alignment
 };
 
 // Hardware tanh approximation (relative error ~2^-11, below bf16 resolution).
@@ -113,7 +116,8 @@ __device__ __forceinline__ float warp_colsum32(float* v, int lane) {
 
 // Applies the epilogue to 32 accumulator columns [c0, c0+32) of row `row`
 // (row >= M rows still join the warp-wide column sum with zeros).
-__device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane) {
+__device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane,
+                                           uint32_t* stg, int row0) {
   const int N = p.N, epi = p.epi;
   const bool row_ok = row < p.M;
   const int valid = min(32, N - c0);
@@ -195,7 +199,7 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
     const float cs = warp_colsum32(t, lane);
     if (lane < valid) atomicAdd(p.colsum + c0 + lane, cs);
   }
-  if (!row_ok) return;
+  if (!row_ok && (p.c_atomic || p.c_fp32)) return;
   if (p.c_atomic) {
     float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
 #pragma unroll
@@ -215,14 +219,27 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
     }
   } else {
     __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
-    if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
-      uint4 pk[4];
-      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(pk);
+    if (valid == 32 && (p.ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
+      // transpose through shared memory so each store instruction writes
+      // 8 whole 64-byte row segments instead of 32 scattered 16-byte pieces
+      uint32_t* mine = stg + lane * 20;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) hh[j] = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      for (int j = 0; j < 16; ++j) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        mine[j] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      __syncwarp();
+      const int seg = lane & 3;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(C)[j] = pk[j];
-    } else {
+      for (int it = 0; it < 4; ++it) {
+        const int r = it * 8 + (lane >> 2);
+        const uint4 w = *reinterpret_cast<const uint4*>(stg + r * 20 + seg * 4);
+        if (row0 + r < p.M)
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row0 + r) * p.ldc + c0 +
+                                    seg * 8) = w;
+      }
+      __syncwarp();
+    } else if (row_ok) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (j < valid) C[j] = __float2bfloat16_rn(v[j]);
@@ -400,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = warp & 3;
     const int half = (warp - 4) >> 2;
     const int r_in_tile = sub * 32 + lane;
+    uint32_t* stg = reinterpret_cast<uint32_t*>(smem + S::kStgOffset) + (warp - 4) * 32 * S::kStgWords;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
@@ -419,10 +437,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane);
+        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
-        if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane);
+        if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32);
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);

@@ -141,6 +141,26 @@ typedef struct {
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
 size_t tb_gemm_workspace_bytes(int M, int N, int K);
 
+// ---------------- NVLink peer-memory collectives ----------------
+#define TB_MAX_PEERS 8
+typedef struct {
+  void* base[TB_MAX_PEERS];  // every rank's symmetric buffer, mapped into this process
+  void* hdr[TB_MAX_PEERS];   // every rank's flag header (inside its buffer)
+  unsigned* epoch_ctr;       // local: epoch of the last completed call
+  int rank, world;
+} TbPeerTable;
+
+size_t tb_peer_header_bytes(void);
+// out[i] = scale * sum_p in_p[i] for fp32 buffers at byte offsets in_off/out_off
+// of every rank's symmetric buffer (in-place when in_off == out_off).
+int tb_peer_allreduce(TbPeerTable t, long long in_off, long long out_off, long long n, float scale,
+                      unsigned* done_ctr, int* err, cudaStream_t s);
+// grad (fp32) reduce-scatter -> Adam on the owned shard (m, v local, full length)
+// -> fp32 weights and bf16 copy written into every rank's buffer.
+int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_off, long long shadow_off, long long n,
+                           float* m, float* v, TbAdamParams hp, const long long* step_ptr, unsigned* done_ctr,
+                           int* err, cudaStream_t s);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,18 @@
+"""Multi-GPU data-parallel tests: run dp_worker.py on 2 GPUs (skipped with fewer)."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def test_fused_dp_two_gpus():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29531", os.path.join(HERE, "dp_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "DP_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

@@ -60,6 +60,18 @@ class FusedActorCritic:
         self.reset_parameters(seed)
         self._ws = {}
 
+    def rebind_storage(self, flat: torch.Tensor, grad: torch.Tensor, shadow: torch.Tensor):
+        """Moves the weights into caller-owned buffers (e.g. NVLink peer memory)."""
+        if flat.numel() < self.numel or grad.numel() < self.numel or shadow.numel() < self.numel:
+            raise ValueError("rebind_storage: buffers too small")
+        flat[: self.numel].copy_(self.flat)
+        shadow[: self.numel].copy_(self.shadow)
+        grad[: self.numel].zero_()
+        self.flat, self.grad, self.shadow = flat[: self.numel], grad[: self.numel], shadow[: self.numel]
+        self.p = {n: self._view(self.flat, n) for n in self.offsets}
+        self.g = {n: self._view(self.grad, n) for n in self.offsets}
+        self.s = {n: self._view(self.shadow, n) for n in self.offsets}
+
     def _view(self, buf, name):
         off, shp = self.offsets[name]
         return buf[off:off + math.prod(shp)].view(shp)

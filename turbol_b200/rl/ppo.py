@@ -73,8 +73,18 @@ class PPOTrainer:
     """PPO trainer; ``grad_sync`` (optional) reduces the flat gradient across
     data-parallel ranks in place and returns the scale Adam applies."""
 
-    def __init__(self, cfg: PPOConfig, device="cuda:0", grad_sync: Optional[Callable] = None, rank: int = 0):
-        self.cfg, self.rank = cfg, rank
+    def __init__(self, cfg: PPOConfig, device="cuda:0", grad_sync: Optional[Callable] = None, rank: int = 0,
+                 dp: str = "none", group=None):
+        """dp: "none"; "nccl" (NCCL all-reduce of the gradient + local fused
+        Adam); "fused" (one NVLink peer-memory kernel: gradient reduce-scatter,
+        sharded Adam, weight all-gather)."""
+        self.cfg, self.rank, self.dp = cfg, rank, dp
+        if dp == "fused" and not (device.startswith("cuda") if isinstance(device, str) else device.type == "cuda"):
+            raise ValueError("the fused data-parallel step needs CUDA devices")
+        if dp == "nccl" and grad_sync is None:
+            from ..parallel.dp import NcclGradSync
+
+            grad_sync = NcclGradSync(group)
         self.device = torch.device(device)
         self.cuda = self.device.type == "cuda"
         C = _core()
@@ -93,8 +103,16 @@ class PPOTrainer:
             self.net = FusedActorCritic(4, 2, cfg.hidden, device=self.device, seed=cfg.seed)
             self.policy = None
             self.flat, self.flat_grad = self.net.flat, self.net.grad
-            self.opt = FusedAdam(self.net.flat, self.net.grad, lr=cfg.lr, max_grad_norm=cfg.max_grad_norm,
-                                 shadow=self.net.shadow)
+            if dp == "fused":
+                from ..parallel.peer import FusedDataParallelAdam
+
+                self.opt = FusedDataParallelAdam(self.net.numel, group, lr=cfg.lr)
+                self.net.rebind_storage(self.opt.param, self.opt.grad, self.opt.shadow)
+                self.opt.broadcast_params(0)
+                self.flat, self.flat_grad = self.net.flat, self.net.grad
+            else:
+                self.opt = FusedAdam(self.net.flat, self.net.grad, lr=cfg.lr, max_grad_norm=cfg.max_grad_norm,
+                                     shadow=self.net.shadow)
             self.obs_bf16 = torch.zeros(N, 8, device=self.device, dtype=torch.bfloat16)
             self.mb_obs_bf16 = torch.zeros(cfg.minibatch_size, 8, device=self.device, dtype=torch.bfloat16)
             self.ws_roll = self.net.workspace(N)
@@ -179,7 +197,10 @@ class PPOTrainer:
         return self.grad_sync(self.flat_grad) if self.grad_sync is not None else 1.0
 
     def _minibatch_apply_gpu(self, scale):
-        self.opt.step(grad_scale=scale)
+        if self.dp == "fused":
+            self.opt.step()  # reduce-scatter + sharded Adam + all-gather (mean over ranks)
+        else:
+            self.opt.step(grad_scale=scale)
         _ops().counter_add(self.mb_step_t, 1)
 
     def _minibatch_grad_gpu(self):
@@ -211,6 +232,12 @@ class PPOTrainer:
 
     def _sync_capturable(self) -> bool:
         return self.grad_sync is None or getattr(self.grad_sync, "capturable", False)
+
+    def check_collectives(self):
+        """Raises if a peer-memory collective timed out (reads a device word)."""
+        for obj in (self.opt, self.grad_sync):
+            if hasattr(obj, "check"):
+                obj.check()
 
     def _build_graphs(self):
         if not (self.cuda and self.cfg.cuda_graphs):
@@ -295,7 +322,7 @@ class PPOTrainer:
                 loss = ppo_categorical_loss(logits, v, act[idx], logp[idx], adv[idx], ret[idx], cfg.clip,
                                             cfg.vf_coef, cfg.ent_coef, stats=self.loss_stats)
                 loss.backward()
-                scale = self.grad_sync(self.policy.fp.grad) if self.grad_sync is not None else 1.0
+                scale = self.grad_sync(self.flat_grad) if self.grad_sync is not None else 1.0
                 self.opt.step(grad_scale=scale)
 
     # ------------------------------------------------------------------ API
@@ -319,7 +346,7 @@ class PPOTrainer:
             else:
                 for _ in range(cfg.epochs * cfg.n_minibatches):
                     mb[0].replay()
-                    self.grad_sync(self.policy.fp.grad)
+                    self.grad_sync(self.flat_grad)
                     mb[1].replay()
             g_end.replay()
         else:
