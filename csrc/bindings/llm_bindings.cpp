@@ -88,6 +88,187 @@ void register_llm_ops(py::module_& m) {
   m.def("gemm_workspace_numel", [](int M, int N, int K) {
     return static_cast<int64_t>(tb_gemm_workspace_bytes(M, N, K) / 4);
   });
+  // ---------------- transformer ops (all launch on the current stream) ----------------
+  auto bf16_2d = [](const at::Tensor& t, const char* n) {
+    chk(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1,
+        std::string(n) + ": bf16 2-D CUDA tensor with contiguous rows");
+  };
+  auto f32c = [](const at::Tensor& t, const char* n) {
+    chk(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), std::string(n) + ": contiguous fp32");
+  };
+  auto i32c = [](const at::Tensor& t, const char* n) {
+    chk(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), std::string(n) + ": contiguous int32");
+  };
+  m.def("rmsnorm_fwd", [=](at::Tensor x, at::Tensor w, at::Tensor y, py::object rstd, float eps) {
+    bf16_2d(x, "x");
+    bf16_2d(y, "y");
+    f32c(w, "w");
+    chk(x.is_contiguous() && y.is_contiguous(), "rmsnorm: contiguous rows");
+    float* r = rstd.is_none() ? nullptr : rstd.cast<at::Tensor>().data_ptr<float>();
+    cuda_ok(tb_rmsnorm_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), r, static_cast<int>(x.size(0)),
+                           static_cast<int>(x.size(1)), eps, turbol::StreamFor(x)),
+            "rmsnorm_fwd");
+  }, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("rstd") = py::none(), py::arg("eps") = 1e-6f);
+  m.def("rmsnorm_bwd", [=](at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx,
+                           py::object dx_add, at::Tensor dw) {
+    bf16_2d(dy, "dy");
+    bf16_2d(x, "x");
+    bf16_2d(dx, "dx");
+    f32c(w, "w");
+    f32c(rstd, "rstd");
+    f32c(dw, "dw");
+    const void* add = dx_add.is_none() ? nullptr : dx_add.cast<at::Tensor>().data_ptr();
+    cuda_ok(tb_rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
+                           add, dw.data_ptr<float>(), static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
+                           turbol::StreamFor(x)),
+            "rmsnorm_bwd");
+  });
+  m.def("rope", [=](at::Tensor qkv, at::Tensor pos, at::Tensor table, int n_rot_heads, int head_dim, bool inverse) {
+    bf16_2d(qkv, "qkv");
+    i32c(pos, "pos");
+    f32c(table, "table");
+    chk(pos.numel() == qkv.size(0), "rope: one position per row");
+    cuda_ok(tb_rope(qkv.data_ptr(), qkv.stride(0), pos.data_ptr<int>(), table.data_ptr<float>(),
+                    static_cast<int>(qkv.size(0)), n_rot_heads, head_dim, inverse ? 1 : 0, turbol::StreamFor(qkv)),
+            "rope");
+  }, py::arg("qkv"), py::arg("pos"), py::arg("table"), py::arg("n_rot_heads"), py::arg("head_dim"),
+     py::arg("inverse") = false);
+  m.def("embed_fwd", [=](at::Tensor ids, at::Tensor W, at::Tensor out, py::object err) {
+    i32c(ids, "ids");
+    bf16_2d(W, "W");
+    bf16_2d(out, "out");
+    int* e = err.is_none() ? nullptr : err.cast<at::Tensor>().data_ptr<int>();
+    cuda_ok(tb_embed_fwd(ids.data_ptr<int>(), W.data_ptr(), out.data_ptr(), static_cast<int>(ids.numel()),
+                         static_cast<int>(W.size(1)), static_cast<int>(W.size(0)), e, turbol::StreamFor(ids)),
+            "embed_fwd");
+  }, py::arg("ids"), py::arg("W"), py::arg("out"), py::arg("error") = py::none());
+  m.def("embed_bwd", [=](at::Tensor ids, at::Tensor dout, at::Tensor dW) {
+    i32c(ids, "ids");
+    bf16_2d(dout, "dout");
+    f32c(dW, "dW");
+    cuda_ok(tb_embed_bwd(ids.data_ptr<int>(), dout.data_ptr(), dW.data_ptr<float>(), static_cast<int>(ids.numel()),
+                         static_cast<int>(dout.size(1)), static_cast<int>(dW.size(0)), turbol::StreamFor(ids)),
+            "embed_bwd");
+  });
+  m.def("swiglu_bwd", [=](at::Tensor gu, at::Tensor dh, at::Tensor dgu) {
+    bf16_2d(gu, "gu");
+    bf16_2d(dh, "dh");
+    bf16_2d(dgu, "dgu");
+    chk(gu.is_contiguous() && dh.is_contiguous() && dgu.is_contiguous(), "swiglu_bwd: contiguous");
+    cuda_ok(tb_swiglu_bwd(gu.data_ptr(), dh.data_ptr(), dgu.data_ptr(), gu.size(0), static_cast<int>(dh.size(1)),
+                          turbol::StreamFor(gu)),
+            "swiglu_bwd");
+  });
+  m.def("swiglu_fwd", [=](at::Tensor gu, at::Tensor act) {
+    bf16_2d(gu, "gu");
+    bf16_2d(act, "act");
+    chk(gu.is_contiguous() && act.is_contiguous() && gu.size(1) == 2 * act.size(1), "swiglu_fwd: [T,2F] -> [T,F]");
+    cuda_ok(tb_swiglu_fwd(gu.data_ptr(), act.data_ptr(), gu.size(0), static_cast<int>(act.size(1)),
+                          turbol::StreamFor(gu)),
+            "swiglu_fwd");
+  });
+  m.def("kv_write", [=](at::Tensor qkv, int k_off, int v_off, at::Tensor seq_of_token, at::Tensor pos,
+                        at::Tensor block_table, at::Tensor kc, at::Tensor vc, int Hk, int D, int bs) {
+    bf16_2d(qkv, "qkv");
+    i32c(seq_of_token, "seq_of_token");
+    i32c(pos, "pos");
+    i32c(block_table, "block_table");
+    cuda_ok(tb_kv_write(qkv.data_ptr(), qkv.stride(0), k_off, v_off, seq_of_token.data_ptr<int>(), pos.data_ptr<int>(),
+                        block_table.data_ptr<int>(), static_cast<int>(block_table.size(1)), kc.data_ptr(),
+                        vc.data_ptr(), static_cast<int>(qkv.size(0)), Hk, D, bs, turbol::StreamFor(qkv)),
+            "kv_write");
+  });
+  m.def("decode_attention", [=](at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table,
+                                at::Tensor ctx_len, at::Tensor out, int Hq, int Hk, int D, int bs, float scale) {
+    bf16_2d(q, "q");
+    bf16_2d(out, "out");
+    i32c(block_table, "block_table");
+    i32c(ctx_len, "ctx_len");
+    cuda_ok(tb_decode_attention(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), block_table.data_ptr<int>(),
+                                static_cast<int>(block_table.size(1)), ctx_len.data_ptr<int>(), out.data_ptr(),
+                                out.stride(0), static_cast<int>(ctx_len.numel()), Hq, Hk, D, bs, scale,
+                                turbol::StreamFor(q)),
+            "decode_attention");
+  });
+  m.def("sample", [=](at::Tensor logits, float temperature, uint64_t seed, py::object step_ptr, int64_t step,
+                      at::Tensor out_tok, py::object out_logp, py::object tok_mat, py::object lp_mat) {
+    bf16_2d(logits, "logits");
+    i32c(out_tok, "out_tok");
+    const long long* sp = step_ptr.is_none()
+                              ? nullptr
+                              : reinterpret_cast<const long long*>(step_ptr.cast<at::Tensor>().data_ptr<int64_t>());
+    float* lp = out_logp.is_none() ? nullptr : out_logp.cast<at::Tensor>().data_ptr<float>();
+    int* tm = nullptr;
+    float* lm = nullptr;
+    int ldm = 0;
+    if (!tok_mat.is_none()) {
+      at::Tensor t = tok_mat.cast<at::Tensor>();
+      i32c(t, "tok_mat");
+      chk(t.dim() == 2 && t.size(0) == logits.size(0), "tok_mat [B, steps]");
+      tm = t.data_ptr<int>();
+      ldm = static_cast<int>(t.size(1));
+    }
+    if (!lp_mat.is_none()) {
+      at::Tensor t = lp_mat.cast<at::Tensor>();
+      f32c(t, "lp_mat");
+      chk(t.dim() == 2 && t.size(0) == logits.size(0) && (ldm == 0 || t.size(1) == ldm), "lp_mat [B, steps]");
+      lm = t.data_ptr<float>();
+      ldm = static_cast<int>(t.size(1));
+    }
+    cuda_ok(tb_sample(logits.data_ptr(), logits.stride(0), static_cast<int>(logits.size(0)),
+                      static_cast<int>(logits.size(1)), temperature, seed, sp, step, out_tok.data_ptr<int>(), lp, tm,
+                      lm, ldm, turbol::StreamFor(logits)),
+            "sample");
+  }, py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("step_ptr"), py::arg("step"),
+     py::arg("out_tok"), py::arg("out_logp") = py::none(), py::arg("tok_mat") = py::none(),
+     py::arg("lp_mat") = py::none());
+  m.def("logprob", [=](at::Tensor logits, at::Tensor target, py::object logp, py::object dlogp, float inv_temp) {
+    bf16_2d(logits, "logits");
+    i32c(target, "target");
+    float* lp = logp.is_none() ? nullptr : logp.cast<at::Tensor>().data_ptr<float>();
+    const float* dl = dlogp.is_none() ? nullptr : dlogp.cast<at::Tensor>().data_ptr<float>();
+    cuda_ok(tb_logprob(logits.data_ptr(), logits.stride(0), static_cast<int>(logits.size(0)),
+                       static_cast<int>(logits.size(1)), target.data_ptr<int>(), lp, dl, inv_temp,
+                       turbol::StreamFor(logits)),
+            "logprob");
+  }, py::arg("logits"), py::arg("target"), py::arg("logp") = py::none(), py::arg("dlogp") = py::none(),
+     py::arg("inv_temp") = 1.0f);
+  m.def("grpo_loss", [=](at::Tensor lp, at::Tensor old_lp, py::object ref_lp, at::Tensor adv, at::Tensor mask,
+                         at::Tensor dlp, py::object stats, float clip, float beta, float inv_total_seqs) {
+    f32c(lp, "lp");
+    f32c(old_lp, "old_lp");
+    f32c(adv, "adv");
+    f32c(mask, "mask");
+    f32c(dlp, "dlp");
+    chk(lp.dim() == 2, "grpo_loss: lp [B, T]");
+    const float* rl = ref_lp.is_none() ? nullptr : ref_lp.cast<at::Tensor>().data_ptr<float>();
+    float* st = stats.is_none() ? nullptr : stats.cast<at::Tensor>().data_ptr<float>();
+    cuda_ok(tb_grpo_loss(lp.data_ptr<float>(), old_lp.data_ptr<float>(), rl, adv.data_ptr<float>(),
+                         mask.data_ptr<float>(), dlp.data_ptr<float>(), st, static_cast<int>(lp.size(0)),
+                         static_cast<int>(lp.size(1)), clip, beta, inv_total_seqs, turbol::StreamFor(lp)),
+            "grpo_loss");
+  });
+  m.def("flash_attn_fwd", [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, py::object lse, int B, int T,
+                              int Hq, int Hk, float scale) {
+    bf16_2d(q, "q");
+    bf16_2d(o, "o");
+    chk(q.stride(0) == k.stride(0) && q.stride(0) == v.stride(0), "flash_attn: q/k/v share the row stride");
+    float* l = lse.is_none() ? nullptr : lse.cast<at::Tensor>().data_ptr<float>();
+    cuda_ok(tb_flash_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0), l, B,
+                              T, Hq, Hk, scale, turbol::StreamFor(q)),
+            "flash_attn_fwd");
+  });
+  m.def("flash_attn_bwd", [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
+                              at::Tensor lse, at::Tensor delta, at::Tensor dq, at::Tensor dk, at::Tensor dv, int B,
+                              int T, int Hq, int Hk, float scale) {
+    chk(dq.stride(0) == dk.stride(0) && dq.stride(0) == dv.stride(0), "flash_attn_bwd: dq/dk/dv share the stride");
+    cuda_ok(tb_flash_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0),
+                              dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
+                              dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq.stride(0), B, T, Hq, Hk, scale,
+                              turbol::StreamFor(q)),
+            "flash_attn_bwd");
+  });
+
   m.attr("EPI_NONE") = static_cast<int>(TB_EPI_NONE);
   m.attr("EPI_BIAS") = static_cast<int>(TB_EPI_BIAS);
   m.attr("EPI_BIAS_TANH") = static_cast<int>(TB_EPI_BIAS_TANH);

@@ -308,14 +308,14 @@ void register_kernel_ops(py::module_& m) {
         py::arg("ret"), py::arg("dlog"), py::arg("dval"), py::arg("stats"), py::arg("clip"), py::arg("vf_coef"),
         py::arg("ent_coef"), py::arg("db_log") = py::none(), py::arg("db_val") = py::none());
 
-  m.def("colsum_bf16", [](at::Tensor x, at::Tensor out) {
+  m.def("colsum_bf16", [](at::Tensor x, at::Tensor out, bool accumulate) {
     TB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "colsum: bf16 2-D");
     need(out, at::kFloat, "out");
     TB_CHECK(out.numel() == x.size(1), "colsum: out [cols]");
     cuda_ok(tb_colsum_bf16(x.data_ptr(), x.stride(0), static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
-                           out.data_ptr<float>(), stream_of(x)),
+                           out.data_ptr<float>(), accumulate ? 1 : 0, stream_of(x)),
             "colsum_bf16");
-  });
+  }, py::arg("x"), py::arg("out"), py::arg("accumulate") = false);
 
   m.def("ppo_loss",
         [](at::Tensor logits, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv, at::Tensor ret,

@@ -46,7 +46,7 @@ struct DevArgs {
   int m_tiles, n_tiles, splits, kb_per_split, k_blocks;
   void* C;
   long long ldc;
-  int c_fp32, c_atomic;
+  int c_fp32, c_atomic, c_add;  // atomic: split-K partials into C; add: C += result (owned elements)
   const float* bias;
   const __nv_bfloat16* aux;
   long long ld_aux;
@@ -205,6 +205,25 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < valid) atomicAdd(C + j, v[j]);
+    return;
+  }
+  if (p.c_add) {  // C += result; this thread owns these elements (no split-K)
+    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 o = reinterpret_cast<float4*>(C)[j];
+        o.x += v[4 * j];
+        o.y += v[4 * j + 1];
+        o.z += v[4 * j + 2];
+        o.w += v[4 * j + 3];
+        reinterpret_cast<float4*>(C)[j] = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) C[j] += v[j];
+    }
     return;
   }
   if (p.c_fp32) {
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(kRedItems* kRedGroups) splitk_reduce_kernel(De
     if (p.colsum) atomicAdd(p.colsum + c + j, v);
     if (p.c_fp32) {
       float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c + j;
-      if (p.c_atomic) atomicAdd(C, v);
+      if (p.c_add) *C += v;
       else *C = v;
     } else {
       static_cast<__nv_bfloat16*>(p.C)[static_cast<long long>(row) * p.ldc + c + j] = __float2bfloat16_rn(v);
@@ -646,8 +665,9 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.C = a->C;
   p.ldc = a->ldc;
   p.c_fp32 = a->c_fp32;
-  p.c_atomic = (a->c_accumulate || (p.splits > 1 && !use_ws)) ? 1 : 0;
-  if (p.c_atomic && !a->c_fp32) return static_cast<int>(cudaErrorInvalidValue);
+  p.c_atomic = (p.splits > 1 && !use_ws) ? 1 : 0;
+  p.c_add = (a->c_accumulate && !p.c_atomic && !use_ws) ? 1 : 0;
+  if ((p.c_atomic || a->c_accumulate) && !a->c_fp32) return static_cast<int>(cudaErrorInvalidValue);
   if (p.splits > 1 && !use_ws && !a->c_accumulate) {
     // atomic split-K adds partial sums into a zeroed C
     if (a->ldc == a->N) {
@@ -684,6 +704,8 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   DevArgs r = p;
   r.ws = static_cast<float*>(a->workspace);
   r.colsum = a->colsum;
+  r.c_atomic = 0;
+  r.c_add = a->c_accumulate ? 1 : 0;
   const long long work = static_cast<long long>(a->M) * ((a->N + 3) / 4);
   const long long g = (work + kRedItems - 1) / kRedItems;
   splitk_reduce_kernel<<<static_cast<unsigned>(g), kRedItems * kRedGroups, 0, stream>>>(r);

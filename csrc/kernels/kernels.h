@@ -77,7 +77,7 @@ int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, 
                        const float* old_logp, const float* adv, const float* ret, void* dlog_bf16, void* dval_bf16,
                        float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
                        float* db_val, cudaStream_t s);
-int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, cudaStream_t s);
+int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,
                 const float* adv, const float* ret, const float* old_val, float* dlogits, float* dvalue, float* stats,
                 int B, float clip, float vclip, float vf_coef, float ent_coef, cudaStream_t s);
@@ -140,6 +140,36 @@ typedef struct {
 
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
 size_t tb_gemm_workspace_bytes(int M, int N, int K);
+
+// ---------------- transformer ops ----------------
+int tb_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps, cudaStream_t s);
+int tb_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx, const void* dx_add,
+                   float* dw, int T, int D, cudaStream_t s);
+int tb_rope(void* qkv, long long ld, const int* pos, const void* table, int T, int n_rot_heads, int D, int inverse,
+            cudaStream_t s);
+int tb_embed_fwd(const int* ids, const void* W, void* out, int T, int D, int V, int* err, cudaStream_t s);
+int tb_embed_bwd(const int* ids, const void* dout, float* dW, int T, int D, int V, cudaStream_t s);
+int tb_swiglu_bwd(const void* gu, const void* dh, void* dgu, long long T, int F, cudaStream_t s);
+int tb_swiglu_fwd(const void* gu, void* act, long long T, int F, cudaStream_t s);
+int tb_kv_write(const void* qkv, long long ld, int k_off, int v_off, const int* seq_of_token, const int* pos,
+                const int* block_table, int max_blocks, void* kc, void* vc, int T, int Hk, int D, int bs,
+                cudaStream_t s);
+int tb_decode_attention(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
+                        int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk, int D,
+                        int bs, float scale, cudaStream_t s);
+int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,
+              const long long* step_ptr, long long step_imm, int* out_tok, float* out_logp, int* tok_mat,
+              float* lp_mat, int ld_mat, cudaStream_t s);
+int tb_logprob(void* logits, long long ld, int T, int V, const int* target, float* logp, const float* dlogp,
+               float inv_temp, cudaStream_t s);
+int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, const float* adv, const float* mask,
+                 float* dlp, float* stats, int B, int T, float clip, float beta, float inv_total_seqs,
+                 cudaStream_t s);
+int tb_flash_attn_fwd(const void* q, const void* k, const void* v, long long ld, void* o, long long ldo, float* lse,
+                      int B, int T, int Hq, int Hk, float scale, cudaStream_t s);
+int tb_flash_attn_bwd(const void* q, const void* k, const void* v, long long ld, const void* o, long long ldo,
+                      const void* dout, long long lddo, const float* lse, float* delta, void* dq, void* dk, void* dv,
+                      long long lddqkv, int B, int T, int Hq, int Hk, float scale, cudaStream_t s);
 
 // ---------------- NVLink peer-memory collectives ----------------
 #define TB_MAX_PEERS 8

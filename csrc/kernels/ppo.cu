@@ -381,9 +381,9 @@ int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, 
   return static_cast<int>(cudaGetLastError());
 }
 
-int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, cudaStream_t s) {
+int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, int accumulate, cudaStream_t s) {
   if (rows <= 0 || cols <= 0) return 0;
-  cudaMemsetAsync(out, 0, sizeof(float) * cols, s);
+  if (!accumulate) cudaMemsetAsync(out, 0, sizeof(float) * cols, s);
   const int rpb = 256;
   dim3 grid((rows + rpb - 1) / rpb, (cols + kBlock - 1) / kBlock);
   colsum_bf16_kernel<<<grid, kBlock, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ld, rows, cols, rpb, out);

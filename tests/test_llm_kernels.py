@@ -1,0 +1,186 @@
+"""LLM kernels vs plain fp32 PyTorch references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from turbol_b200._native import ops
+from turbol_b200.models.llm import LMConfig, rope_table
+from turbol_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def bf(x):
+    return x.to(torch.bfloat16)
+
+
+def test_rmsnorm_fwd_bwd(dev):
+    T, D = 300, 1536
+    x = bf(torch.randn(T, D, device=dev))
+    w = torch.rand(D, device=dev) + 0.5
+    y = torch.empty_like(x)
+    r = torch.empty(T, device=dev)
+    ops().rmsnorm_fwd(x, w, y, r, 1e-6)
+    xr = x.float().requires_grad_()
+    wr = w.clone().requires_grad_()
+    yr = ref.rmsnorm(xr, wr, 1e-6)
+    assert torch.allclose(y.float(), yr, atol=3e-2, rtol=2e-2)
+    dy = bf(torch.randn(T, D, device=dev))
+    add = bf(torch.randn(T, D, device=dev))
+    dx = torch.empty_like(x)
+    dw = torch.zeros(D, device=dev)
+    ops().rmsnorm_bwd(dy, x, w, r, dx, add, dw)
+    yr.backward(dy.float())
+    assert torch.allclose(dx.float(), xr.grad + add.float(), atol=5e-2, rtol=3e-2)
+    assert torch.allclose(dw, wr.grad, atol=0.5, rtol=2e-2)
+
+
+def test_rope_roundtrip(dev):
+    cfg = LMConfig.tiny()
+    tab = rope_table(cfg, dev)
+    T, Hh = 50, 6
+    qkv = bf(torch.randn(T, Hh * 128, device=dev))
+    pos = torch.randint(0, 500, (T,), device=dev, dtype=torch.int32)
+    orig = qkv.clone()
+    ops().rope(qkv, pos, tab, Hh, 128)
+    x = orig.float().view(T, Hh, 128)
+    ang = pos.double()[:, None] * (1.0 / cfg.rope_theta ** (torch.arange(0, 128, 2, device=dev).double() / 128))[None]
+    c, s = torch.cos(ang).float()[:, None], torch.sin(ang).float()[:, None]
+    e = torch.cat([x[..., :64] * c - x[..., 64:] * s, x[..., 64:] * c + x[..., :64] * s], -1)
+    assert torch.allclose(qkv.float().view(T, Hh, 128), e, atol=3e-2)
+    ops().rope(qkv, pos, tab, Hh, 128, True)
+    assert torch.allclose(qkv.float(), orig.float(), atol=5e-2)
+
+
+@pytest.mark.parametrize("B,T,Hq,Hk", [(2, 128, 4, 2), (1, 200, 12, 2), (2, 64, 8, 8)])
+def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
+    D = 128
+    ld = (Hq + 2 * Hk) * D
+    qkv = bf(torch.randn(B * T, ld, device=dev) * 0.5)
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D:(Hq + Hk) * D], qkv[:, (Hq + Hk) * D:]
+    o = torch.empty(B * T, Hq * D, device=dev, dtype=torch.bfloat16)
+    lse = torch.empty(B * Hq * T, device=dev)
+    scale = 1 / math.sqrt(D)
+    ops().flash_attn_fwd(q, k, v, o, lse, B, T, Hq, Hk, scale)
+    qr = q.float().view(B, T, Hq, D).requires_grad_()
+    kr = k.float().view(B, T, Hk, D).requires_grad_()
+    vr = v.float().view(B, T, Hk, D).requires_grad_()
+    out = ref.causal_attention(qr, kr, vr, scale)
+    assert torch.allclose(o.float().view(B, T, Hq, D), out, atol=2e-2, rtol=2e-2), (o.float().view(B, T, Hq, D) - out).abs().max()
+    do = bf(torch.randn(B * T, Hq * D, device=dev))
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(B * Hq * T, device=dev)
+    ops().flash_attn_bwd(q, k, v, o, do, lse, delta, dqkv[:, : Hq * D], dqkv[:, Hq * D:(Hq + Hk) * D],
+                         dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale)
+    out.backward(do.float().view(B, T, Hq, D))
+    for got, exp in ((dqkv[:, : Hq * D], qr.grad), (dqkv[:, Hq * D:(Hq + Hk) * D], kr.grad),
+                     (dqkv[:, (Hq + Hk) * D:], vr.grad)):
+        e = exp.reshape(B * T, -1)
+        err = (got.float() - e).abs().max() / (e.abs().max() + 1e-6)
+        assert err < 3e-2, err
+
+
+def test_decode_attention_paged(dev):
+    B, Hq, Hk, D, bs = 5, 12, 2, 128, 16
+    lens = [1, 17, 33, 100, 64]
+    nblk = 40
+    kc = bf(torch.randn(nblk, Hk, bs, D, device=dev))
+    vc = bf(torch.randn(nblk, Hk, bs, D, device=dev))
+    perm = torch.randperm(nblk)
+    table = torch.zeros(B, 8, dtype=torch.int32)
+    used = 0
+    for b in range(B):
+        nb = (lens[b] + bs - 1) // bs
+        table[b, :nb] = perm[used:used + nb].to(torch.int32)
+        used += nb
+    table = table.to(dev)
+    q = bf(torch.randn(B, Hq * D, device=dev))
+    out = torch.empty_like(q)
+    ctx = torch.tensor(lens, device=dev, dtype=torch.int32)
+    ops().decode_attention(q, kc, vc, table, ctx, out, Hq, Hk, D, bs, 1 / math.sqrt(D))
+    for b in range(B):
+        L = lens[b]
+        ks = torch.cat([kc[table[b, j]].float() for j in range((L + bs - 1) // bs)], 1)[:, :L]  # [Hk, L, D]
+        vs = torch.cat([vc[table[b, j]].float() for j in range((L + bs - 1) // bs)], 1)[:, :L]
+        qq = q[b].float().view(Hq, D)
+        kk = ks.repeat_interleave(Hq // Hk, 0)
+        vv = vs.repeat_interleave(Hq // Hk, 0)
+        p = torch.softmax((qq[:, None, :] * kk).sum(-1) / math.sqrt(D), -1)
+        e = (p[..., None] * vv).sum(1)
+        assert torch.allclose(out[b].float().view(Hq, D), e, atol=3e-2), b
+
+
+def test_sample_and_logprob(dev):
+    B, V = 7, 50000
+    logits = bf(torch.randn(B, V, device=dev) * 3)
+    tok = torch.empty(B, device=dev, dtype=torch.int32)
+    lp = torch.empty(B, device=dev)
+    ops().sample(logits, 0.0, 1, None, 0, tok, lp)  # greedy
+    assert torch.equal(tok.long(), logits.float().argmax(-1))
+    lsm = torch.log_softmax(logits.float(), -1)
+    assert torch.allclose(lp, lsm.gather(1, tok.long()[:, None])[:, 0], atol=1e-3)
+    # temperature sampling: empirical frequencies follow softmax
+    small = bf(torch.tensor([[0.0, 1.0, 2.0, -1.0]] * 4096, device=dev))
+    t = torch.empty(4096, device=dev, dtype=torch.int32)
+    ops().sample(small, 1.0, 7, None, 3, t, None)
+    freq = torch.bincount(t.long(), minlength=4).float() / 4096
+    assert torch.allclose(freq.cpu(), torch.softmax(small[0].float(), -1).cpu(), atol=0.03)
+    # log-probs and the in-place gradient
+    tgt = torch.randint(0, V, (B,), device=dev, dtype=torch.int32)
+    lg = logits.clone()
+    out = torch.empty(B, device=dev)
+    ops().logprob(lg, tgt, out)
+    assert torch.allclose(out, lsm.gather(1, tgt.long()[:, None])[:, 0], atol=2e-3)
+    g = torch.randn(B, device=dev)
+    ops().logprob(lg, tgt, None, g)
+    exp = g[:, None] * (F.one_hot(tgt.long(), V).float() - lsm.exp())
+    assert torch.allclose(lg.float(), exp, atol=2e-3, rtol=1e-2)  # gradient stored in bf16
+
+
+def test_grpo_loss_grad(dev):
+    B, T = 6, 40
+    lp = (-torch.rand(B, T, device=dev) * 3).requires_grad_()
+    old = lp.detach() + 0.1 * torch.randn(B, T, device=dev)
+    refl = lp.detach() + 0.2 * torch.randn(B, T, device=dev)
+    adv = torch.randn(B, device=dev)
+    mask = (torch.rand(B, T, device=dev) < 0.8).float()
+    clip, beta = 0.2, 0.04
+    r = torch.exp(lp - old)
+    pg = -torch.min(r * adv[:, None], r.clamp(1 - clip, 1 + clip) * adv[:, None])
+    d = refl - lp
+    kl = torch.exp(d) - d - 1
+    loss = (((pg + beta * kl) * mask).sum(1) / mask.sum(1)).sum() / B
+    loss.backward()
+    dlp = torch.empty(B, T, device=dev)
+    stats = torch.zeros(4, device=dev)
+    ops().grpo_loss(lp.detach().contiguous(), old, refl, adv, mask, dlp, stats, clip, beta, 1.0 / B)
+    assert torch.allclose(dlp, lp.grad, atol=1e-6)
+    assert abs(float(stats[0] + beta * stats[1]) - float(loss)) < 1e-4
+
+
+def test_swiglu_and_embedding(dev):
+    T, F_ = 33, 64
+    gu = bf(torch.randn(T, 2 * F_, device=dev))
+    act = torch.empty(T, F_, device=dev, dtype=torch.bfloat16)
+    ops().swiglu_fwd(gu, act)
+    g, u = gu.float()[:, 0::2].requires_grad_(), gu.float()[:, 1::2].requires_grad_()
+    e = F.silu(g) * u
+    assert torch.allclose(act.float(), e, atol=2e-2)
+    dh = bf(torch.randn(T, F_, device=dev))
+    dgu = torch.empty_like(gu)
+    ops().swiglu_bwd(gu, dh, dgu)
+    e.backward(dh.float())
+    assert torch.allclose(dgu.float()[:, 0::2], g.grad, atol=3e-2)
+    assert torch.allclose(dgu.float()[:, 1::2], u.grad, atol=3e-2)
+    V, D = 100, 256
+    W = bf(torch.randn(V, D, device=dev))
+    ids = torch.randint(0, V, (77,), device=dev, dtype=torch.int32)
+    out = torch.empty(77, D, device=dev, dtype=torch.bfloat16)
+    ops().embed_fwd(ids, W, out)
+    assert torch.equal(out, W[ids.long()])
+    dW = torch.zeros(V, D, device=dev)
+    ops().embed_bwd(ids, out, dW)
+    exp = torch.zeros(V, D, device=dev).index_add_(0, ids.long(), out.float())
+    assert torch.allclose(dW, exp, atol=1e-3)

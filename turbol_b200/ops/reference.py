@@ -124,3 +124,38 @@ def causal_attention(q, k, v, scale=None):
     s = s.masked_fill(~mask, float("-inf"))
     p = s.softmax(-1)
     return torch.einsum("bhqk,bkhd->bqhd", p, vf)
+
+
+def lm_forward_ref(model, ids, params=None):
+    """fp32 forward of a DecoderLM (all layers, embed and head) from its bf16
+    weights; returns logits [B, T, V].  ``params`` (name -> tensor) overrides the
+    weights, e.g. with leaf tensors for autograd."""
+    cfg = model.cfg
+    P = params if params is not None else {n: model.s[n].float() for n in model.offsets}
+    if params is None and model.flat is not None:
+        for n in P:
+            if n.endswith(("ln1", "ln2", "norm", "bqkv")):
+                P[n] = model.p[n].float()
+    B, T = ids.shape
+    H, D, F = cfg.hidden, cfg.head_dim, cfg.ffn
+    x = P["embed"][ids.long()]
+    pos = torch.arange(T, device=ids.device)
+    for i in model.layers:
+        p = f"l{i}."
+        h = rmsnorm(x, P[p + "ln1"], cfg.rms_eps)
+        qkv = h @ P[p + "wqkv"].t()
+        if cfg.qkv_bias:
+            qkv = qkv + P[p + "bqkv"]
+        q = qkv[..., : cfg.q_dim].view(B, T, cfg.n_heads, D)
+        k = qkv[..., cfg.q_dim:cfg.q_dim + cfg.kv_dim].view(B, T, cfg.n_kv_heads, D)
+        v = qkv[..., cfg.q_dim + cfg.kv_dim:].view(B, T, cfg.n_kv_heads, D)
+        q, k = rope(q, pos, cfg.rope_theta), rope(k, pos, cfg.rope_theta)
+        a = causal_attention(q, k, v).reshape(B, T, cfg.q_dim)
+        x = x + a @ P[p + "wo"].t()
+        h = rmsnorm(x, P[p + "ln2"], cfg.rms_eps)
+        gu = h @ P[p + "wgu"].t()
+        act = torch.nn.functional.silu(gu[..., 0::2]) * gu[..., 1::2]
+        x = x + act @ P[p + "wdown"].t()
+    h = rmsnorm(x, P["norm"], cfg.rms_eps)
+    W = P["embed"] if cfg.tie_embeddings else P["lm_head"]
+    return h @ W.t()

@@ -1,0 +1,181 @@
+"""GRPO (Shao et al. 2024, "DeepSeekMath", group relative policy optimization)
+for a decoder-only policy on the turbol_b200 kernels.
+
+One step:
+  1. rollout   P prompts x G samples, ``response_len`` tokens each, temperature
+               sampling (LLMGenerator: own paged-KV decode loop, CUDA graph);
+  2. reward    R = (FNV-1a-64(response ids) mod 1000) / 1000 (hash reward
+               kernel) -> group-normalized advantages (GRPO kernel);
+  3. reference log-probs of the sampled responses under the frozen initial
+               policy (forward only);
+  4. update    micro-batched forward with saved activations -> LM-head logits
+               of the response positions -> log-probs -> GRPO loss kernel
+               (clipped ratio, k3 KL to the reference, per-sequence token mean)
+               -> logits gradient in place -> hand-written backward -> fp32
+               gradient accumulation -> one fused Adam launch over all weights.
+With one update per rollout the behaviour policy equals the current policy,
+so the ratio is 1 and the clip is inactive (the GRPO setting with mu = 1).
+
+Train tokens per step = P * G * (prompt_len + response_len).
+
+The reference's grpo_example.py (turbol_vllm/examples/py/grpo_example.py:124-151)
+echoes prompts and updates a linear policy on an uninitialised batch; this
+module is the algorithm it names.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from .._native import ops as _ops
+from ..models.llm import DecoderLM, LMConfig
+from ..ops.rl import FusedAdam
+from .rollout import LLMGenerator
+
+
+@dataclass
+class GRPOConfig:
+    model: LMConfig = field(default_factory=LMConfig.qwen2_1p5b)
+    num_prompts: int = 64
+    group_size: int = 8
+    prompt_len: int = 256
+    response_len: int = 512
+    temperature: float = 1.0
+    lr: float = 1e-6
+    clip: float = 0.2
+    kl_coef: float = 0.04
+    micro_batch: int = 8  # sequences per forward/backward
+    seed: int = 0
+
+    @property
+    def batch(self) -> int:
+        return self.num_prompts * self.group_size
+
+    @property
+    def seq_len(self) -> int:
+        return self.prompt_len + self.response_len
+
+
+class GRPOTrainer:
+    def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = DecoderLM(cfg.model, self.device, seed=cfg.seed)
+        self.ref = self.model.frozen_copy()
+        self.opt = optimizer or FusedAdam(self.model.flat, self.model.grad, lr=cfg.lr, betas=(0.9, 0.95),
+                                          shadow=self.model.shadow)
+        self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17)
+        self.stats = torch.zeros(4, device=self.device)
+        self.step_count = 0
+        self.last_times = {}
+
+    # ------------------------------------------------------------------ helpers
+    def _prompts(self) -> torch.Tensor:
+        g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count)
+        return torch.randint(0, self.cfg.model.vocab, (self.cfg.num_prompts, self.cfg.prompt_len),
+                             generator=g, device=self.device, dtype=torch.int32)
+
+    def _response_rows(self, m: int) -> torch.Tensor:
+        """Indices of the hidden rows that predict the response tokens of m sequences."""
+        T, Lp, Lr = self.cfg.seq_len, self.cfg.prompt_len, self.cfg.response_len
+        base = torch.arange(m, device=self.device) * T
+        return (base[:, None] + torch.arange(Lp - 1, Lp - 1 + Lr, device=self.device)[None, :]).reshape(-1)
+
+    @torch.no_grad()
+    def ref_logprobs(self, seqs: torch.Tensor) -> torch.Tensor:
+        """Log-probs of the response tokens under the frozen reference model."""
+        cfg = self.cfg
+        o = _ops()
+        B, T, Lr = seqs.shape[0], cfg.seq_len, cfg.response_len
+        out = torch.empty(B, Lr, device=self.device)
+        mb = cfg.micro_batch
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
+        for s0 in range(0, B, mb):
+            ids = seqs[s0:s0 + mb].contiguous()
+            m = ids.shape[0]
+            x = self.ref.embed(ids)
+            x, _ = self.ref.forward(x, m, T, pos[: m * T], save=False)
+            hf = self.ref.final_norm(x)
+            rows = hf.index_select(0, self._response_rows(m))
+            logits = self.ref.logits(rows)
+            tgt = ids[:, cfg.prompt_len:].reshape(-1).contiguous()
+            o.logprob(logits, tgt, out[s0:s0 + m].view(-1))
+        return out
+
+    # ------------------------------------------------------------------ step
+    def step(self) -> dict:
+        cfg = self.cfg
+        o = _ops()
+        dev = self.device
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        # 1. rollout
+        seqs, roll_lp = self.gen.generate(self._prompts(), cfg.group_size, cfg.response_len, cfg.temperature)
+        torch.cuda.synchronize(dev)
+        t1 = time.perf_counter()
+        # 2. rewards and group-normalized advantages
+        resp = seqs[:, cfg.prompt_len:].contiguous()
+        lens = torch.full((cfg.batch,), cfg.response_len, device=dev, dtype=torch.int32)
+        rewards = o.hash_reward(resp, lens)
+        adv = o.grpo_advantage(rewards, cfg.group_size, 1e-4, True)
+        # 3. reference log-probs
+        ref_lp = self.ref_logprobs(seqs)
+        torch.cuda.synchronize(dev)
+        t2 = time.perf_counter()
+        # 4. update
+        self.model.zero_grad()
+        self.stats.zero_()
+        self._train(seqs, ref_lp, adv)
+        self.opt.step()
+        torch.cuda.synchronize(dev)
+        t3 = time.perf_counter()
+        self.step_count += 1
+        st = self.stats.cpu().tolist()
+        self.last_times = {"rollout_s": t1 - t0, "reward_ref_s": t2 - t1, "train_s": t3 - t2, "step_s": t3 - t0}
+        return {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()),
+                "pg_loss": st[0], "kl": st[1], "clipped_tokens": st[2], "tokens": st[3],
+                "rollout_logp_mean": float(roll_lp.mean()), **self.last_times,
+                "train_tokens": cfg.batch * cfg.seq_len}
+
+    def _train(self, seqs, ref_lp, adv):
+        cfg = self.cfg
+        o = _ops()
+        m_ = self.model
+        T, Lp, Lr = cfg.seq_len, cfg.prompt_len, cfg.response_len
+        mb = cfg.micro_batch
+        H = cfg.model.hidden
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
+        mask = torch.ones(mb, Lr, device=self.device)
+        for s0 in range(0, cfg.batch, mb):
+            ids = seqs[s0:s0 + mb].contiguous()
+            m = ids.shape[0]
+            N = m * T
+            x0 = m_.embed(ids)
+            x, saved = m_.forward(x0, m, T, pos[:N], save=True)
+            rstd = torch.empty(N, device=self.device)
+            hf = m_.final_norm(x, rstd)
+            rows = self._response_rows(m)
+            hr = hf.index_select(0, rows)
+            logits = m_.logits(hr)                                      # [m*Lr, V] bf16
+            tgt = ids[:, Lp:].reshape(-1).contiguous()
+            lp = torch.empty(m * Lr, device=self.device)
+            o.logprob(logits, tgt, lp)
+            old = lp.detach().clone()                                   # behaviour policy == current
+            dlp = torch.empty_like(lp)
+            o.grpo_loss(lp.view(m, Lr), old.view(m, Lr), ref_lp[s0:s0 + m].contiguous(), adv[s0:s0 + m].contiguous(),
+                        mask[:m], dlp.view(m, Lr), self.stats, cfg.clip, cfg.kl_coef, 1.0 / cfg.batch)
+            o.logprob(logits, tgt, None, dlp)                          # logits <- d loss / d logits
+            dhr = torch.empty(m * Lr, H, device=self.device, dtype=torch.bfloat16)
+            o.gemm(logits, m_.head_weight(), dhr, False, True)          # d h = dLogits W_head
+            o.gemm(logits, hr, m_.head_grad(), True, True, accumulate=True, split_k=1)  # dW_head += dLogits^T h
+            dhf = torch.zeros(N, H, device=self.device, dtype=torch.bfloat16)
+            dhf.index_copy_(0, rows, dhr)
+            dx = torch.empty_like(x)
+            o.rmsnorm_bwd(dhf, x, m_.f32["norm"], rstd, dx, None, m_.g["norm"])
+            dx = m_.backward(dx, saved, m, T, pos[:N])
+            m_.embed_backward(ids, dx)
+            del saved, logits

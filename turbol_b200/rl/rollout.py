@@ -1,0 +1,291 @@
+"""Rollout engines: the token-level LLM generator and the reference's
+string-level ``RolloutEngine``.
+
+:class:`LLMGenerator` runs its own decode loop on the turbol_b200 kernels (no
+vLLM): a paged KV cache (16-token blocks, block tables from the native
+``KVBlockManager``), prompt-prefix sharing (the G samples of a prompt point
+their first block-table entries at the prompt's blocks), prefill through the
+flash-attention kernel, and a decode step — embedding, per layer RMSNorm, QKV
+GEMM (+bias), RoPE, KV write, paged GQA decode attention, output GEMM
+(+residual), RMSNorm, gate/up GEMM with fused SwiGLU, down GEMM (+residual),
+final norm, LM-head GEMM, temperature sampling — captured once as a CUDA graph
+and replayed per token.  The sampled tokens and their log-probabilities land
+in [B, max_new] device matrices (the column comes from a device counter).
+
+:class:`RolloutEngine` keeps the reference's API
+(turbol_vllm/include/turbol/rollout/rollout_engine.hpp:8-36:
+RolloutConfig{inference_backend, model_path, tensor_parallel_size,
+max_new_tokens, temperature, top_p, top_k, max_batch_size}; initialize,
+shutdown, generate, generate_batch, is_vllm_available).  Backends: "native"
+(LLMGenerator over a byte-level tokenizer; with random weights the text is
+noise, the API and throughput are real), "echo" (the reference's fallback,
+turbol_vllm/src/rollout/rollout_engine.cpp:42-44) and "vllm" (optional, via
+``turbol_b200.vllm_inference``).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from .._native import core as _core, ops as _ops
+from ..models.llm import DecoderLM, LMConfig
+
+
+class LLMGenerator:
+    def __init__(self, model: DecoderLM, max_batch: int, max_len: int, block_size: int = 16, seed: int = 0,
+                 cuda_graph: bool = True):
+        self.m = model
+        self.cfg = model.cfg
+        self.device = model.device
+        self.max_batch, self.max_len, self.bs = max_batch, max_len, block_size
+        self.seed = seed
+        self.cuda_graph = cuda_graph
+        cfg = self.cfg
+        self.blocks_per_seq = (max_len + block_size - 1) // block_size
+        # worst case: every sequence private (no sharing) -> max_batch * blocks
+        self.num_blocks = max_batch * self.blocks_per_seq + 1
+        self.kv = _core().KVBlockManager(self.num_blocks, block_size)
+        shape = (self.num_blocks, cfg.n_kv_heads, block_size, cfg.head_dim)
+        self.kc = [torch.empty(shape, device=self.device, dtype=torch.bfloat16) for _ in model.layers]
+        self.vc = [torch.empty(shape, device=self.device, dtype=torch.bfloat16) for _ in model.layers]
+        self._graph = None
+        self._graph_B = None
+        self.calls = 0
+
+    # ------------------------------------------------------------ block tables
+    def _tables(self, P: int, G: int, Lp: int, steps: int):
+        """Block tables with the prompt blocks shared by the G samples of a prompt."""
+        self.kv.reset()
+        bs = self.bs
+        n_prompt_blocks = Lp // bs  # full prompt blocks are shared; a partial one is copied per sample
+        tail = Lp - n_prompt_blocks * bs
+        B = P * G
+        table = torch.zeros(B, self.blocks_per_seq, dtype=torch.int32)
+        pre_table = torch.zeros(P, self.blocks_per_seq, dtype=torch.int32)
+        for p in range(P):
+            st = self.kv.allocate(p, max(Lp, 1))
+            if not st.ok():
+                raise RuntimeError(f"KV cache: {st}")
+            pblocks = self.kv.block_table(p)
+            pre_table[p, : len(pblocks)] = torch.tensor(pblocks, dtype=torch.int32)
+            for g in range(G):
+                s = p * G + g
+                sid = P + s
+                need = Lp + steps - n_prompt_blocks * bs
+                st = self.kv.allocate(sid, max(need, 1))
+                if not st.ok():
+                    raise RuntimeError(f"KV cache: {st}")
+                own = self.kv.block_table(sid)
+                row = pblocks[:n_prompt_blocks] + own
+                table[s, : len(row)] = torch.tensor(row[: self.blocks_per_seq], dtype=torch.int32)
+        return table.to(self.device), pre_table.to(self.device), n_prompt_blocks, tail
+
+    # ------------------------------------------------------------ decode step
+    def _decode_step(self, B: int):
+        o = _ops()
+        cfg, m = self.cfg, self.m
+        H, D = cfg.hidden, cfg.head_dim
+        st = self.state
+        x = st["x"]
+        o.embed_fwd(st["tok"], m.s["embed"], x)
+        h, qkv, attn, x2, act = st["h"], st["qkv"], st["attn"], st["x2"], st["act"]
+        scale = 1.0 / math.sqrt(D)
+        for li, i in enumerate(m.layers):
+            P = f"l{i}."
+            o.rmsnorm_fwd(x, m.f32[P + "ln1"], h, None, cfg.rms_eps)
+            if cfg.qkv_bias:
+                o.gemm(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS)
+            else:
+                o.gemm(h, m.s[P + "wqkv"], qkv)
+            o.rope(qkv, st["pos"], m.table, cfg.n_heads + cfg.n_kv_heads, D)
+            o.kv_write(qkv, cfg.q_dim, cfg.q_dim + cfg.kv_dim, st["seq"], st["pos"], st["table"], self.kc[li],
+                       self.vc[li], cfg.n_kv_heads, D, self.bs)
+            o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], attn, cfg.n_heads,
+                               cfg.n_kv_heads, D, self.bs, scale)
+            o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL)
+            o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
+            o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
+            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
+        o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
+        o.gemm(h, m.head_weight(), st["logits"])
+        o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls, st["step"], 0, st["tok"], None,
+                 st["tok_mat"], st["lp_mat"])
+        st["pos"].add_(1)
+        st["ctx"].add_(1)
+        o.counter_add(st["step"], 1)
+
+    def _alloc_state(self, B: int, steps: int):
+        cfg = self.cfg
+        dev = self.device
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        return {
+            "x": torch.empty(B, cfg.hidden, **bf), "h": torch.empty(B, cfg.hidden, **bf),
+            "qkv": torch.empty(B, cfg.qkv_dim, **bf), "attn": torch.empty(B, cfg.q_dim, **bf),
+            "x2": torch.empty(B, cfg.hidden, **bf), "act": torch.empty(B, cfg.ffn, **bf),
+            "logits": torch.empty(B, cfg.vocab, **bf),
+            "tok": torch.zeros(B, device=dev, dtype=torch.int32),
+            "pos": torch.zeros(B, device=dev, dtype=torch.int32),
+            "ctx": torch.zeros(B, device=dev, dtype=torch.int32),
+            "seq": torch.arange(B, device=dev, dtype=torch.int32),
+            "table": torch.zeros(B, self.blocks_per_seq, device=dev, dtype=torch.int32),
+            "step": torch.zeros(1, device=dev, dtype=torch.int64),
+            "tok_mat": torch.zeros(B, steps, device=dev, dtype=torch.int32),
+            "lp_mat": torch.zeros(B, steps, device=dev, dtype=torch.float32),
+        }
+
+    # ------------------------------------------------------------ generate
+    @torch.no_grad()
+    def generate(self, prompts: torch.Tensor, group: int = 1, max_new: int = 16, temperature: float = 1.0):
+        """prompts [P, Lp] int -> (sequences [P*G, Lp+max_new] int32, logp [P*G, max_new] fp32)."""
+        o = _ops()
+        cfg, m = self.cfg, self.m
+        P, Lp = prompts.shape
+        G = group
+        B = P * G
+        if B > self.max_batch or Lp + max_new > self.max_len:
+            raise ValueError("generate: batch or length beyond the engine's capacity")
+        self.temperature = float(temperature)
+        self.calls += 1
+        table, pre_table, n_shared, tail = self._tables(P, G, Lp, max_new)
+        prompts = prompts.to(self.device, torch.int32).contiguous()
+        # ---- prefill the P prompts once; K/V land in the shared prompt blocks
+        pos = torch.arange(Lp, device=self.device, dtype=torch.int32).repeat(P)
+        seq_of_tok = torch.arange(P, device=self.device, dtype=torch.int32).repeat_interleave(Lp)
+        kcs, vcs = self.kc, self.vc
+
+        def hook(i, qkv):
+            li = m.layers.index(i)
+            o.kv_write(qkv, cfg.q_dim, cfg.q_dim + cfg.kv_dim, seq_of_tok, pos, pre_table, kcs[li], vcs[li],
+                       cfg.n_kv_heads, cfg.head_dim, self.bs)
+
+        x = m.embed(prompts)
+        x, _ = m.forward(x, P, Lp, pos, save=False, kv_hook=hook)
+        last = x.view(P, Lp, -1)[:, -1, :].contiguous()
+        # a partially filled last prompt block is private: copy it to each sample's own block
+        if tail:
+            src_blocks = pre_table[:, n_shared].long()
+            dst_blocks = table[:, n_shared].long()
+            for li in range(len(m.layers)):
+                kcs[li][dst_blocks] = kcs[li][src_blocks.repeat_interleave(G)]
+                vcs[li][dst_blocks] = vcs[li][src_blocks.repeat_interleave(G)]
+        # ---- decode state: first token sampled from the prompt's last position
+        if self._graph is None or self._graph_B != (B, max_new):
+            self.state = self._alloc_state(B, max_new)
+            self._graph = None
+        st = self.state
+        st["table"].copy_(table)
+        h = torch.empty(P, cfg.hidden, device=self.device, dtype=torch.bfloat16)
+        o.rmsnorm_fwd(last, m.f32["norm"], h, None, cfg.rms_eps)
+        hB = h.repeat_interleave(G, 0).contiguous()
+        o.gemm(hB, m.head_weight(), st["logits"])
+        st["step"].zero_()
+        o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls + 1, st["step"], 0, st["tok"], None,
+                 st["tok_mat"], st["lp_mat"])
+        o.counter_add(st["step"], 1)
+        st["pos"].fill_(Lp)
+        st["ctx"].fill_(Lp + 1)
+        steps = max_new - 1
+        if steps > 0:
+            if self.cuda_graph:
+                # capture one decode step (re-captured per call: the sampling
+                # seed is a launch parameter), then replay it per token
+                saved = {k: v.clone() for k, v in st.items() if k in ("tok", "pos", "ctx", "step")}
+                if self._graph is None:
+                    s = torch.cuda.Stream(device=self.device)
+                    s.wait_stream(torch.cuda.current_stream(self.device))
+                    with torch.cuda.stream(s):  # first call: warm-up outside capture
+                        self._decode_step(B)
+                    torch.cuda.current_stream(self.device).wait_stream(s)
+                    for k, v in saved.items():
+                        st[k].copy_(v)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._decode_step(B)
+                for k, v in saved.items():
+                    st[k].copy_(v)
+                self._graph, self._graph_B = g, (B, max_new)
+                for _ in range(steps):
+                    self._graph.replay()
+            else:
+                for _ in range(steps):
+                    self._decode_step(B)
+        seqs = torch.cat([prompts.repeat_interleave(G, 0), st["tok_mat"]], 1)
+        return seqs, st["lp_mat"].clone()
+
+
+# ---------------------------------------------------------------------------
+@dataclass
+class RolloutConfig:
+    inference_backend: str = "native"  # "native" | "echo" | "vllm"
+    model_path: str = ""
+    tensor_parallel_size: int = 1
+    max_new_tokens: int = 2048
+    temperature: float = 1.0
+    top_p: float = 1.0
+    top_k: int = -1
+    max_batch_size: int = 256
+    model: str = "tiny"  # "tiny" | "qwen2-1.5b" | "llama3-8b" (random-init architectures)
+    device: str = "cuda:0"
+    seed: int = 0
+
+
+class RolloutEngine:
+    def __init__(self, config: Optional[RolloutConfig] = None):
+        self.config = config or RolloutConfig()
+        self.initialized = False
+        self._gen: Optional[LLMGenerator] = None
+        self._vllm = None
+        self._tok = None
+
+    def initialize(self):
+        c = self.config
+        self._tok = _core().ByteTokenizer()
+        Status = _core().Status
+        if c.inference_backend == "native" and torch.cuda.is_available():
+            cfg = {"tiny": LMConfig.tiny(vocab=512), "qwen2-1.5b": LMConfig.qwen2_1p5b(),
+                   "llama3-8b": LMConfig.llama3_8b()}[c.model]
+            model = DecoderLM(cfg, c.device, seed=c.seed, master=False)
+            self._gen = LLMGenerator(model, c.max_batch_size, min(cfg.max_seq, 4096), seed=c.seed)
+        elif c.inference_backend == "vllm":
+            from ..vllm_inference import VLLMInferenceConfig, VLLMInferenceEngine
+
+            self._vllm = VLLMInferenceEngine(VLLMInferenceConfig(model=c.model_path, max_tokens=c.max_new_tokens,
+                                                                 temperature=c.temperature, top_p=c.top_p))
+        self.initialized = True
+        return Status()
+
+    def shutdown(self):
+        self._gen = None
+        self._vllm = None
+        self.initialized = False
+        return _core().Status()
+
+    def is_vllm_available(self) -> bool:
+        from ..vllm_inference import vllm_available
+
+        return vllm_available()
+
+    def generate(self, prompt: str) -> str:
+        return self.generate_batch([prompt])[0]
+
+    def generate_batch(self, prompts: List[str]) -> List[str]:
+        if not self.initialized:
+            raise RuntimeError("RolloutEngine not initialized")
+        if self._vllm is not None:
+            return self._vllm.generate_batch(prompts)
+        if self._gen is None:
+            return ["[RolloutEngine] " + p for p in prompts]  # echo fallback (no GPU / no model)
+        tok = self._tok
+        vocab = self._gen.cfg.vocab
+        enc = [[t % vocab for t in tok.encode(p, True, False)] for p in prompts]
+        L = max(len(e) for e in enc)
+        ids = torch.full((len(enc), L), tok.pad_id % vocab, dtype=torch.int32)
+        for i, e in enumerate(enc):
+            ids[i, L - len(e):] = torch.tensor(e, dtype=torch.int32)  # left pad
+        new = max(1, min(self.config.max_new_tokens, self._gen.max_len - L))
+        seqs, _ = self._gen.generate(ids, 1, new, self.config.temperature)
+        out = seqs[:, L:].cpu().tolist()
+        return [tok.decode([t for t in row if t < 256]) for row in out]
