@@ -77,6 +77,7 @@ PYBIND11_MODULE(turbol_core, m) {
 
   py::class_<Status>(m, "Status")
       .def(py::init<>())
+      .def(py::init<StatusCode, std::string>(), py::arg("code"), py::arg("message") = "")
       .def("ok", &Status::ok)
       .def("code", [](const Status& s) { return static_cast<int>(s.code()); })
       .def("message", &Status::message)

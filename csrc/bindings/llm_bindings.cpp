@@ -191,7 +191,8 @@ void register_llm_ops(py::module_& m) {
             "decode_attention");
   });
   m.def("sample", [=](at::Tensor logits, float temperature, uint64_t seed, py::object step_ptr, int64_t step,
-                      at::Tensor out_tok, py::object out_logp, py::object tok_mat, py::object lp_mat) {
+                      at::Tensor out_tok, py::object out_logp, py::object tok_mat, py::object lp_mat,
+                      py::object seed_t, py::object temp_t) {
     bf16_2d(logits, "logits");
     i32c(out_tok, "out_tok");
     const long long* sp = step_ptr.is_none()
@@ -215,13 +216,25 @@ void register_llm_ops(py::module_& m) {
       lm = t.data_ptr<float>();
       ldm = static_cast<int>(t.size(1));
     }
+    const unsigned long long* sd = nullptr;
+    const float* tp = nullptr;
+    if (!seed_t.is_none()) {
+      at::Tensor t = seed_t.cast<at::Tensor>();
+      chk(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() >= 1, "seed_t: int64 CUDA tensor");
+      sd = reinterpret_cast<const unsigned long long*>(t.data_ptr<int64_t>());
+    }
+    if (!temp_t.is_none()) {
+      at::Tensor t = temp_t.cast<at::Tensor>();
+      f32c(t, "temp_t");
+      tp = t.data_ptr<float>();
+    }
     cuda_ok(tb_sample(logits.data_ptr(), logits.stride(0), static_cast<int>(logits.size(0)),
                       static_cast<int>(logits.size(1)), temperature, seed, sp, step, out_tok.data_ptr<int>(), lp, tm,
-                      lm, ldm, turbol::StreamFor(logits)),
+                      lm, ldm, sd, tp, turbol::StreamFor(logits)),
             "sample");
   }, py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("step_ptr"), py::arg("step"),
      py::arg("out_tok"), py::arg("out_logp") = py::none(), py::arg("tok_mat") = py::none(),
-     py::arg("lp_mat") = py::none());
+     py::arg("lp_mat") = py::none(), py::arg("seed_t") = py::none(), py::arg("temp_t") = py::none());
   m.def("logprob", [=](at::Tensor logits, at::Tensor target, py::object logp, py::object dlogp, float inv_temp) {
     bf16_2d(logits, "logits");
     i32c(target, "target");

@@ -17,6 +17,7 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "device_common.cuh"
 #include "kernels.h"
 
 namespace {
@@ -505,11 +506,7 @@ int tb_flash_attn_fwd(const void* q, const void* k, const void* v, long long ld,
   if (B <= 0 || T <= 0) return 0;
   if (Hq % Hk || (ld % 8) || (ldo % 8)) return static_cast<int>(cudaErrorInvalidValue);
   const int smem = 5 * 64 * ROWB;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  tb::ensure_dyn_smem(reinterpret_cast<const void*>(fa_fwd_kernel), smem);
   dim3 grid((T + BMQ - 1) / BMQ, B * Hq);
   fa_fwd_kernel<<<grid, NT, smem, s>>>(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
                                        static_cast<const bf16*>(v), ld, static_cast<bf16*>(o), ldo, lse, T, Hq, Hk,
@@ -526,12 +523,8 @@ int tb_flash_attn_bwd(const void* q, const void* k, const void* v, long long ld,
   fa_bwd_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
       static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, delta, B, T, Hq);
   const int smem = 6 * 64 * ROWB;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(fa_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(fa_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  tb::ensure_dyn_smem(reinterpret_cast<const void*>(fa_bwd_dkdv_kernel), smem);
+  tb::ensure_dyn_smem(reinterpret_cast<const void*>(fa_bwd_dq_kernel), smem);
   dim3 g1((T + BNK - 1) / BNK, B * Hk);
   fa_bwd_dkdv_kernel<<<g1, NT, smem, s>>>(static_cast<const bf16*>(q), static_cast<const bf16*>(k),
                                           static_cast<const bf16*>(v), ld, static_cast<const bf16*>(dout), lddo, lse,

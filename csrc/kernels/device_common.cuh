@@ -5,7 +5,28 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 namespace tb {
+
+// Raises a kernel's dynamic shared memory limit above the 48 KB default.  The
+// attribute belongs to the function in the current device's context, so it is
+// set once per (function, device) pair.
+inline cudaError_t ensure_dyn_smem(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (d.first == fn && d.second == dev) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.emplace_back(fn, dev);
+  return e;
+}
 
 // ---------------------------------------------------------------------------
 // Philox4x32-10 counter-based generator (Salmon, Moraes, Dror, Shaw, "Parallel

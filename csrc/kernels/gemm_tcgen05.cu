@@ -31,6 +31,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "device_common.cuh"
 #include "sm100_primitives.cuh"
 
 namespace {
@@ -53,16 +54,24 @@ struct DevArgs {
   int epi;
   float alpha;
   float* ws;      // split-K partials [splits, M, N] (null: atomics into C)
+  int* slot_cnt;  // in-kernel split-K fix-up: one arrival counter per (tile, epilogue warp); null: reduce pass
   float* colsum;  // optional: column sums of the epilogue output, accumulated atomically
   int* error;
 };
+
+// Workspace layout for split-K: [kCntBytes of fix-up counters][partials].
+constexpr int kCntSlots = 8192;
+constexpr size_t kCntBytes = kCntSlots * sizeof(int);
+// With at most this many splits the last warp to finish a slice sums the
+// partials itself; more splits go through the bandwidth-parallel reduce pass.
+constexpr int kMaxFixupSplits = 4;
 
 template <int BN>
 struct Smem {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kStgOffset = kBarOffset + 256;     // per-warp store staging (bf16 outputs)
   static constexpr int kStgWords = 20;                     // 16 words of a 32-column row + 4 pad
@@ -116,16 +125,20 @@ __device__ __forceinline__ float warp_colsum32(float* v, int lane) {
 
 // Applies the epilogue to 32 accumulator columns [c0, c0+32) of row `row`
 // (row >= M rows still join the warp-wide column sum with zeros).
+// mode kEpiFull: scale by alpha and run the epilogue; kEpiPartial: scale and
+// store the split-K partial; kEpiFinal: epilogue of already-scaled summed partials.
+enum { kEpiFull = 0, kEpiPartial = 1, kEpiFinal = 2 };
 __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane,
-                                           uint32_t* stg, int row0) {
+                                           uint32_t* stg, int row0, int mode) {
   const int N = p.N, epi = p.epi;
   const bool row_ok = row < p.M;
   const int valid = min(32, N - c0);
-  if (p.alpha != 1.f) {
+  const bool partial = mode == kEpiPartial;
+  if (p.alpha != 1.f && mode != kEpiFinal) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] *= p.alpha;
   }
-  if (p.ws != nullptr) {  // split-K partial: raw accumulator, no epilogue yet
+  if (partial) {  // split-K partial: raw accumulator, no epilogue yet
     if (row_ok) {
       float* W = p.ws + (static_cast<long long>(ks) * p.M + row) * N + c0;
       if (valid == 32 && (reinterpret_cast<uintptr_t>(W) & 15) == 0) {
@@ -263,6 +276,132 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
       for (int j = 0; j < 32; ++j)
         if (j < valid) C[j] = __float2bfloat16_rn(v[j]);
     }
+  }
+}
+
+// Split-K fix-up of one warp slice: rows [row0, row0+32) x columns
+// [col0, col0+COLS), summed over the splits' partials (in split order) with
+// the epilogue applied.  Lanes run along columns (float4 each), so every load
+// and store instruction covers whole 256- or 512-byte row segments, and the
+// partial loads of a block of rows are all issued before they are used.
+template <int COLS>
+__device__ __forceinline__ void fixup_slice(const DevArgs& p, int row0, int col0, int lane) {
+  constexpr int LPR = COLS / 4;   // lanes per row
+  constexpr int RPI = 32 / LPR;   // rows per instruction
+  constexpr int RB = 4;           // rows per load batch (per lane)
+  const int c = col0 + (lane % LPR) * 4;
+  const int nvalid = min(4, p.N - c);  // <= 0: a lane past the last column (still joins the shuffles)
+  const bool vec = nvalid == 4 && (p.N % 4) == 0;
+  const int epi = p.epi;
+  float b[4] = {0.f, 0.f, 0.f, 0.f};
+  if ((epi == TB_EPI_BIAS || epi == TB_EPI_BIAS_TANH || epi == TB_EPI_BIAS_SILU) && p.bias) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b[j] = j < nvalid ? __ldg(p.bias + c + j) : 0.f;
+  }
+  float cs[4] = {0.f, 0.f, 0.f, 0.f};
+  const long long plane = static_cast<long long>(p.M) * p.N;
+#pragma unroll 1
+  for (int r0 = lane / LPR; nvalid > 0 && r0 < 32; r0 += RPI * RB) {
+    float v[RB][4];
+#pragma unroll
+    for (int u = 0; u < RB; ++u) v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxFixupSplits; ++sp) {
+      if (sp >= p.splits) break;
+#pragma unroll
+      for (int u = 0; u < RB; ++u) {
+        const int row = row0 + r0 + u * RPI;
+        if (row >= p.M) continue;
+        const float* W = p.ws + sp * plane + static_cast<long long>(row) * p.N + c;
+        if (vec) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(W));
+          v[u][0] += x.x;
+          v[u][1] += x.y;
+          v[u][2] += x.z;
+          v[u][3] += x.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nvalid) v[u][j] += __ldcg(W + j);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RB; ++u) {
+      const int row = row0 + r0 + u * RPI;
+      if (row >= p.M) continue;
+      float* x = v[u];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[j] += b[j];
+      if (epi == TB_EPI_BIAS_TANH) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = fast_tanh(x[j]);
+      } else if (epi == TB_EPI_BIAS_SILU) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = fast_silu(x[j]);
+      } else if (epi == TB_EPI_RESIDUAL || epi == TB_EPI_TANH_BWD) {
+        const __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + c;
+        float h[4];
+        if (nvalid == 4 && (reinterpret_cast<uintptr_t>(a) & 7) == 0) {
+          const uint2 u2 = *reinterpret_cast<const uint2*>(a);
+          const float2 h0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.x));
+          const float2 h1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u2.y));
+          h[0] = h0.x;
+          h[1] = h0.y;
+          h[2] = h1.x;
+          h[3] = h1.y;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) h[j] = j < nvalid ? __bfloat162float(a[j]) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) x[j] = epi == TB_EPI_RESIDUAL ? x[j] + h[j] : x[j] * (1.f - h[j] * h[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cs[j] += x[j];
+      if (p.c_fp32) {
+        float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c;
+        if (nvalid == 4 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+          float4 o = make_float4(x[0], x[1], x[2], x[3]);
+          if (p.c_add) {
+            const float4 q = *reinterpret_cast<const float4*>(C);
+            o.x += q.x;
+            o.y += q.y;
+            o.z += q.z;
+            o.w += q.w;
+          }
+          *reinterpret_cast<float4*>(C) = o;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nvalid) C[j] = p.c_add ? C[j] + x[j] : x[j];
+        }
+      } else {
+        __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + c;
+        if (nvalid == 4 && (reinterpret_cast<uintptr_t>(C) & 7) == 0) {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+          uint2 o;
+          o.x = *reinterpret_cast<uint32_t*>(&lo);
+          o.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(C) = o;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nvalid) C[j] = __float2bfloat16_rn(x[j]);
+        }
+      }
+    }
+  }
+  if (p.colsum != nullptr) {
+    // lanes with the same columns hold different rows: fold them, then one atomic per column
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cs[j] += __shfl_xor_sync(0xffffffffu, cs[j], off);
+    if (lane < LPR)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < nvalid) atomicAdd(p.colsum + c + j, cs[j]);
   }
 }
 
@@ -439,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* stg = reinterpret_cast<uint32_t*>(smem + S::kStgOffset) + (warp - 4) * 32 * S::kStgWords;
     int acc = 0;
     uint32_t acc_phase = 0;
+    const int mode = p.ws != nullptr ? kEpiPartial : kEpiFull;
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
       int m0, nt, ks, kb0, kb1;
       work_coords(p, w, m0, nt, ks, kb0, kb1);
@@ -447,25 +587,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = m0 + r_in_tile;
       const uint32_t base = tmem_base + acc * BN + (static_cast<uint32_t>(sub * 32) << 16);
+      constexpr int kStep = BN / 2 >= 64 ? 64 : 32;  // columns per TMEM load batch
 #pragma unroll 1
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 64) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kStep) {
         uint32_t r[64];
         tmem_ld32_nowait(base + c, r);
-        tmem_ld32_nowait(base + c + 32, r + 32);
+        if constexpr (kStep == 64) tmem_ld32_nowait(base + c + 32, r + 32);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32);
+        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode);
+        if constexpr (kStep == 64) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
-        if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
+          if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode);
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
+      }
+      if (p.slot_cnt != nullptr) {
+        // In-kernel split-K fix-up, per warp slice (32 rows x BN/2 columns):
+        // publish this split's partial, count arrivals, and let the last of
+        // the `splits` warps that own the slice sum every partial (in split
+        // order, so the result does not depend on arrival order) and run the
+        // full epilogue.  Warp-local: no barrier across warps, no waiting.
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          const int slot = (w % (p.m_tiles * p.n_tiles)) * kEpiWarps + (warp - 4);
+          last = atomicAdd(p.slot_cnt + slot, 1) == p.splits - 1;
+          if (last) atomicExch(p.slot_cnt + slot, 0);  // leave the counter zero for the next launch
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          fixup_slice<BN / 2>(p, m0 + sub * 32, n0 + half * (BN / 2), lane);
+        }
       }
     }
   }
@@ -476,7 +639,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && *abort_flag && p.error) atomicExch(p.error, TB_GEMM_ERR_TIMEOUT);
 }
 
-// C = sum over splits of the partials (+ bias, + activation).  A block owns 64
+// C = sum over splits of the partials, then the epilogue (bias, activation,
+// residual add or tanh backward).  A block owns 64
 // float4 column groups of the output; its 4 warps-groups each sum every 4th
 // partial with 4 loads in flight, then combine through shared memory, so the
 // pass streams the workspace at bandwidth instead of walking the splits
@@ -542,6 +706,10 @@ __global__ void __launch_bounds__(kRedItems* kRedGroups) splitk_reduce_kernel(De
     if ((p.epi == TB_EPI_BIAS || p.epi == TB_EPI_BIAS_TANH || p.epi == TB_EPI_BIAS_SILU) && p.bias) v += p.bias[c + j];
     if (p.epi == TB_EPI_BIAS_TANH) v = fast_tanh(v);
     if (p.epi == TB_EPI_BIAS_SILU) v = fast_silu(v);
+    if (p.epi == TB_EPI_RESIDUAL || p.epi == TB_EPI_TANH_BWD) {
+      const float h = __bfloat162float(p.aux[static_cast<long long>(row) * p.ld_aux + c + j]);
+      v = p.epi == TB_EPI_RESIDUAL ? v + h : v * (1.f - h * h);
+    }
     if (p.colsum) atomicAdd(p.colsum + c + j, v);
     if (p.c_fp32) {
       float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c + j;
@@ -598,15 +766,59 @@ int num_sms() {
   return n;
 }
 
+// Tile width and split count.  When K may be split (a workspace or atomics
+// are available), BN = 256 and K is split if the tiles cover less than half
+// the SMs, into as many splits as fit in one wave, each keeping at least 4
+// k-blocks.  Otherwise BN = 256 unless the 256-wide tiles would not cover the
+// SMs once; then 128, or 64 if 128-wide tiles would not cover half of them
+// (narrow tiles multiply the CTAs that stream operands, which is what bounds
+// GEMMs with few rows such as decode-time projections).
+struct Plan {
+  int BN, m_tiles, n_tiles, k_blocks, splits;
+};
+Plan make_plan(int M, int N, int K, int bn_hint, int split_k, bool can_split, size_t ws_bytes) {
+  Plan pl{};
+  const int sms = num_sms();
+  pl.m_tiles = (M + BM - 1) / BM;
+  pl.k_blocks = (K + BK - 1) / BK;
+  if (bn_hint == 64 || bn_hint == 128 || bn_hint == 256) {
+    pl.BN = bn_hint;
+  } else {
+    pl.BN = N > 128 ? 256 : 128;
+    // narrow tiles only where K will not be split (splitting keeps the wide,
+    // more efficient tiles busy instead)
+    const bool may_split = split_k > 1 || (split_k <= 0 && can_split);
+    if (!may_split) {
+      if (pl.BN == 256 && pl.m_tiles * ((N + 255) / 256) < sms) pl.BN = 128;
+      if (pl.BN == 128 && N > 64 && pl.m_tiles * ((N + 127) / 128) < sms / 2) pl.BN = 64;
+    }
+  }
+  pl.n_tiles = (N + pl.BN - 1) / pl.BN;
+  const int tiles = pl.m_tiles * pl.n_tiles;
+  int splits = split_k;
+  if (splits <= 0) {
+    splits = 1;
+    if (can_split && tiles < sms / 2) {
+      splits = sms / tiles;
+      const int max_s = (pl.k_blocks + 3) / 4;
+      if (splits > max_s) splits = max_s;
+      const size_t per_split = sizeof(float) * static_cast<size_t>(M) * N;
+      if (ws_bytes != 0 && ws_bytes != static_cast<size_t>(-1)) {
+        const size_t fit = ws_bytes > kCntBytes ? (ws_bytes - kCntBytes) / per_split : 0;
+        if (static_cast<size_t>(splits) > fit && fit >= 2) splits = static_cast<int>(fit);  // prefer partials over atomics
+      }
+      if (splits < 1) splits = 1;
+    }
+  }
+  pl.splits = splits;
+  return pl;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 int launch(const CUtensorMap& ta, const CUtensorMap& tbm, const DevArgs& p, int grid, cudaStream_t s) {
   using S = Smem<BN>;
   auto k = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
-    attr = true;
-  }
+  tb::ensure_dyn_smem(reinterpret_cast<const void*>(k), S::kTotal);
   k<<<grid, kThreads, S::kTotal, s>>>(ta, tbm, p);
   return static_cast<int>(cudaGetLastError());
 }
@@ -624,8 +836,13 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
     return static_cast<int>(cudaErrorInvalidValue);
   const bool swiglu = a->epi == TB_EPI_SWIGLU;
   if (swiglu && ((a->N % 2) || a->colsum)) return static_cast<int>(cudaErrorInvalidValue);
-  int BN = (a->N > 128) ? 256 : 128;
-  if (a->bn_hint == 128 || a->bn_hint == 256) BN = a->bn_hint;
+  const bool ws_epi_ok = !swiglu;
+  const bool atomic_ok = a->c_fp32 && (a->epi == TB_EPI_NONE || a->epi == TB_EPI_BIAS) && !a->colsum;
+  const bool have_ws = a->workspace != nullptr && ws_epi_ok &&
+                       a->workspace_bytes >= kCntBytes + 2 * sizeof(float) * static_cast<size_t>(a->M) * a->N;
+  const Plan pl = make_plan(a->M, a->N, a->K, a->bn_hint, a->split_k, have_ws || atomic_ok,
+                            have_ws ? a->workspace_bytes : 0);
+  const int BN = pl.BN;
   CUtensorMap ta, tbm;
   // A: K-major -> matrix [M, K]; MN-major -> matrix [K, M]
   const bool okA = a->a_mn ? make_map(&ta, a->A, a->K, a->M, a->lda, BK) : make_map(&ta, a->A, a->M, a->K, a->lda, BM);
@@ -636,37 +853,24 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.M = a->M;
   p.N = a->N;
   p.K = a->K;
-  p.m_tiles = (a->M + BM - 1) / BM;
-  p.n_tiles = (a->N + BN - 1) / BN;
-  p.k_blocks = (a->K + BK - 1) / BK;
+  p.m_tiles = pl.m_tiles;
+  p.n_tiles = pl.n_tiles;
+  p.k_blocks = pl.k_blocks;
   const int tiles = p.m_tiles * p.n_tiles;
   const size_t per_split = sizeof(float) * static_cast<size_t>(a->M) * a->N;
-  // split-K: partials go to the caller's workspace (then one reduce pass), or,
-  // without a workspace, atomically into an fp32 C
-  const bool ws_ok = a->workspace != nullptr && a->workspace_bytes >= 2 * per_split && !swiglu &&
-                     a->epi != TB_EPI_TANH_BWD && a->epi != TB_EPI_RESIDUAL;
-  const bool atomic_ok = a->c_fp32 && (a->epi == TB_EPI_NONE || a->epi == TB_EPI_BIAS) && !a->colsum;
-  int splits = a->split_k;
-  if (splits <= 0) {
-    splits = 1;
-    if ((ws_ok || atomic_ok) && tiles < num_sms() / 2) {
-      splits = (num_sms() + tiles - 1) / tiles;
-      const int max_s = (p.k_blocks + 3) / 4;  // keep >= 4 k-blocks per split
-      if (splits > max_s) splits = max_s;
-      if (ws_ok && static_cast<size_t>(splits) * per_split > a->workspace_bytes)
-        splits = static_cast<int>(a->workspace_bytes / per_split);  // prefer partials over atomics
-      if (splits < 1) splits = 1;
-    }
-  }
-  p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+  p.kb_per_split = (p.k_blocks + pl.splits - 1) / pl.splits;
   p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
-  const bool use_ws = p.splits > 1 && ws_ok && static_cast<size_t>(p.splits) * per_split <= a->workspace_bytes;
+  // split-K: partials go to the caller's workspace (summed in-kernel by the
+  // last warp to finish a slice, or by one reduce pass for many splits), or,
+  // without a workspace, atomically into an fp32 C
+  const bool use_ws = p.splits > 1 && have_ws && kCntBytes + static_cast<size_t>(p.splits) * per_split <= a->workspace_bytes;
+  const bool fixup = use_ws && p.splits <= kMaxFixupSplits && tiles * kEpiWarps <= kCntSlots;
   if (p.splits > 1 && !use_ws && !atomic_ok) return static_cast<int>(cudaErrorInvalidValue);
   p.C = a->C;
   p.ldc = a->ldc;
   p.c_fp32 = a->c_fp32;
   p.c_atomic = (p.splits > 1 && !use_ws) ? 1 : 0;
-  p.c_add = (a->c_accumulate && !p.c_atomic && !use_ws) ? 1 : 0;
+  p.c_add = (a->c_accumulate && !p.c_atomic && (!use_ws || fixup)) ? 1 : 0;
   if ((p.c_atomic || a->c_accumulate) && !a->c_fp32) return static_cast<int>(cudaErrorInvalidValue);
   if (p.splits > 1 && !use_ws && !a->c_accumulate) {
     // atomic split-K adds partial sums into a zeroed C
@@ -682,8 +886,9 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.ld_aux = a->ld_aux;
   p.epi = a->epi;
   p.alpha = a->alpha == 0.f ? 1.f : a->alpha;
-  p.ws = use_ws ? static_cast<float*>(a->workspace) : nullptr;
-  p.colsum = use_ws ? nullptr : a->colsum;
+  p.ws = use_ws ? reinterpret_cast<float*>(static_cast<char*>(a->workspace) + kCntBytes) : nullptr;
+  p.slot_cnt = fixup ? static_cast<int*>(a->workspace) : nullptr;
+  p.colsum = (use_ws && !fixup) ? nullptr : a->colsum;
   p.error = a->error;
   const int total = tiles * p.splits;
   const int grid = total < num_sms() ? total : num_sms();
@@ -696,13 +901,14 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   else err = launch<BNV, true, true>(ta, tbm, p, grid, stream);
   if (BN == 256) {
     TB_GEMM_DISPATCH(256)
-  } else {
+  } else if (BN == 128) {
     TB_GEMM_DISPATCH(128)
+  } else {
+    TB_GEMM_DISPATCH(64)
   }
 #undef TB_GEMM_DISPATCH
-  if (err != 0 || !use_ws) return err;
+  if (err != 0 || !use_ws || fixup) return err;
   DevArgs r = p;
-  r.ws = static_cast<float*>(a->workspace);
   r.colsum = a->colsum;
   r.c_atomic = 0;
   r.c_add = a->c_accumulate ? 1 : 0;
@@ -713,14 +919,11 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
 }
 
 size_t tb_gemm_workspace_bytes(int M, int N, int K) {
-  // enough for the automatic split count of an fp32 M x N output
-  const int bn = N > 128 ? 256 : 128;  // the launcher's automatic tile width
-  const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-  int splits = (148 + tiles - 1) / tiles;
-  const int max_s = ((K + BK - 1) / BK + 3) / 4;
-  if (splits > max_s) splits = max_s;
-  if (splits < 2) return 0;
-  return sizeof(float) * static_cast<size_t>(M) * N * splits;
+  // enough for the automatic tile width and split count of this shape
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const Plan pl = make_plan(M, N, K, 0, 0, true, static_cast<size_t>(-1));
+  if (pl.splits < 2) return 0;
+  return kCntBytes + sizeof(float) * static_cast<size_t>(M) * N * pl.splits;
 }
 
 }  // extern "C"

@@ -131,9 +131,13 @@ typedef struct {
   int epi;
   float alpha;  // 0 or 1 = no scaling
   int split_k;  // 0 = automatic (fp32 output, no nonlinear epilogue)
-  int bn_hint;  // 0 = automatic, else 128 or 256
+  int bn_hint;  // 0 = automatic, else 64, 128 or 256
   int* error;   // optional device int: set to TB_GEMM_ERR_TIMEOUT if a wait ran out
-  void* workspace;         // optional fp32 scratch for split-K partials (else atomics into fp32 C)
+  // Optional split-K scratch (else atomics into an fp32 C).  Layout: 32 KB of
+  // arrival counters, then the fp32 partials.  Zero-fill it before its first
+  // use; every call that completes leaves the counters zero again.  Calls that
+  // may overlap on the GPU need separate workspaces.
+  void* workspace;
   size_t workspace_bytes;
   float* colsum;           // optional [N] fp32: column sums of the output (e.g. a bias gradient)
 } TbGemmArgs;
@@ -157,9 +161,11 @@ int tb_kv_write(const void* qkv, long long ld, int k_off, int v_off, const int* 
 int tb_decode_attention(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
                         int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk, int D,
                         int bs, float scale, cudaStream_t s);
+// seed_ptr / temp_ptr (optional) override seed / temperature from device
+// memory, so a captured CUDA graph can be replayed with new values.
 int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,
               const long long* step_ptr, long long step_imm, int* out_tok, float* out_logp, int* tok_mat,
-              float* lp_mat, int ld_mat, cudaStream_t s);
+              float* lp_mat, int ld_mat, const unsigned long long* seed_ptr, const float* temp_ptr, cudaStream_t s);
 int tb_logprob(void* logits, long long ld, int T, int V, const int* target, float* logp, const float* dlogp,
                float inv_temp, cudaStream_t s);
 int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, const float* adv, const float* mask,

@@ -347,83 +347,347 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const bf16* __restrict
   }
 }
 
+// Tensor-core decode attention (block_size 16, head_dim 128).  CTA = (sequence,
+// kv head); the G query heads of the group are the rows of a 16-row MMA tile
+// (rows >= G are zero).  Warp w walks KV blocks w, w+4, ...: each 16-token K
+// and V block is staged into the warp's shared memory with cp.async (double
+// buffered), S = Q K^T and O += P V run as bf16 mma.sync m16n8k16, the online
+// softmax runs on the accumulator fragments, and the four warps merge their
+// (max, sum, O) partials at the end.
+namespace dtc {
+__device__ __forceinline__ uint32_t saddr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ int swz(int row, int chunk) { return row * 256 + ((chunk ^ (row & 7)) << 4); }
+__device__ __forceinline__ void mma(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack(float x, float y) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// 16 token rows x 128 dims of one KV block -> swizzled smem tile (8 x 16 B per lane)
+__device__ __forceinline__ void stage(uint8_t* tile, const bf16* src, int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i, r = e >> 4, c = e & 15;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(tile + swz(r, c))), "l"(src + r * 128 + c * 8)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+}  // namespace dtc
+
+constexpr int kDecTcSmem = 4 * 2 * 2 * 16 * 256;  // warps x stages x {K, V} x 16 tokens x 256 B
+
+__global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restrict__ q, long long ldq,
+                                                            const bf16* __restrict__ kc, const bf16* __restrict__ vc,
+                                                            const int* __restrict__ block_table, int max_blocks,
+                                                            const int* __restrict__ ctx_len, bf16* __restrict__ out,
+                                                            long long ldo, int Hk, int G, float scale) {
+  constexpr int D = 128, BS = 16, NW = 4;
+  extern __shared__ __align__(128) uint8_t dyn_smem[];
+  auto sKV = reinterpret_cast<uint8_t(*)[2][2][BS * 256]>(dyn_smem);  // [warp][stage][K/V]
+  // after the main loop the staging area is reused for the partial outputs
+  auto sm_o = reinterpret_cast<float(*)[16][D + 4]>(dyn_smem);
+  __shared__ float sm_m[NW][16], sm_l[NW][16];
+  const int s = blockIdx.x / Hk, hk = blockIdx.x % Hk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+  const int L = ctx_len[s];
+  const int nblk = (L + BS - 1) / BS;
+  // Q fragments for the G query heads (rows g < G), pre-scaled into log2 units
+  const float qs = scale * 1.4426950408889634f;
+  uint32_t qa[8][4];
+  const bf16* qrow = q + static_cast<long long>(s) * ldq + static_cast<long long>(hk * G + g) * D;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    uint32_t lo = 0u, hi = 0u;
+    if (g < G) {
+      const __nv_bfloat162 x0 = *reinterpret_cast<const __nv_bfloat162*>(qrow + kk * 16 + 2 * t4);
+      const __nv_bfloat162 x1 = *reinterpret_cast<const __nv_bfloat162*>(qrow + kk * 16 + 8 + 2 * t4);
+      const float2 f0 = __bfloat1622float2(x0), f1 = __bfloat1622float2(x1);
+      lo = dtc::pack(f0.x * qs, f0.y * qs);
+      hi = dtc::pack(f1.x * qs, f1.y * qs);
+    }
+    qa[kk][0] = lo;
+    qa[kk][1] = 0u;  // rows g + 8 >= 8 >= G: padding
+    qa[kk][2] = hi;
+    qa[kk][3] = 0u;
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  const int* bt = block_table + static_cast<long long>(s) * max_blocks;
+  auto src_k = [&](int j) { return kc + (static_cast<long long>(bt[j]) * Hk + hk) * BS * D; };
+  auto src_v = [&](int j) { return vc + (static_cast<long long>(bt[j]) * Hk + hk) * BS * D; };
+  int st = 0;
+  if (warp < nblk) {
+    dtc::stage(sKV[warp][0][0], src_k(warp), lane);
+    dtc::stage(sKV[warp][0][1], src_v(warp), lane);
+  }
+  for (int j = warp; j < nblk; j += NW) {
+    const int jn = j + NW;
+    if (jn < nblk) {
+      dtc::stage(sKV[warp][st ^ 1][0], src_k(jn), lane);
+      dtc::stage(sKV[warp][st ^ 1][1], src_v(jn), lane);
+      asm volatile("cp.async.wait_group 2;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncwarp();
+    const uint8_t* tk = sKV[warp][st][0];
+    const uint8_t* tv = sKV[warp][st][1];
+    if ((j + 1) * BS > L) {
+      // slots past the context hold stale (possibly non-finite) values: zero
+      // their V rows so that p = 0 contributes exactly 0 (K rows are masked below)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i, r = e >> 4, c = e & 15;
+        if (j * BS + r >= L) *reinterpret_cast<uint4*>(sKV[warp][st][1] + dtc::swz(r, c)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      __syncwarp();
+    }
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t b[4];
+      const int row = (lane & 7) + 8 * (lane >> 4);
+      const int chunk = kk * 2 + ((lane >> 3) & 1);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                   : "r"(dtc::saddr(tk + dtc::swz(row, chunk))));
+      dtc::mma(sc[0], qa[kk], b[0], b[1]);
+      dtc::mma(sc[1], qa[kk], b[2], b[3]);
+    }
+    // row g of the tile: tokens n*8 + 2*t4 + {0,1}
+    const int base = j * BS;
+    float mx = m;
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        if (base + n * 8 + 2 * t4 + e >= L) sc[n][e] = -INFINITY;
+        mx = fmaxf(mx, sc[n][e]);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float corr = (m == -INFINITY) ? 0.f : exp2f(m - mx);
+    float p[2][2], rs = 0.f;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[n][e] = sc[n][e] == -INFINITY ? 0.f : exp2f(sc[n][e] - mx);
+        rs += p[n][e];
+      }
+    l = l * corr + rs;
+    m = mx;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) {
+      o[d][0] *= corr;
+      o[d][1] *= corr;
+    }
+    const uint32_t pa[4] = {dtc::pack(p[0][0], p[0][1]), 0u, dtc::pack(p[1][0], p[1][1]), 0u};
+#pragma unroll
+    for (int d = 0; d < 16; d += 2) {
+      uint32_t b[4];
+      const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+      const int chunk = d + (lane >> 4);
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3])
+                   : "r"(dtc::saddr(tv + dtc::swz(row, chunk))));
+      dtc::mma(o[d], pa, b[0], b[1]);
+      dtc::mma(o[d + 1], pa, b[2], b[3]);
+    }
+    __syncwarp();
+    st ^= 1;
+  }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  __syncthreads();  // every warp is done reading its staging tiles
+  if (t4 == 0) {
+    sm_m[warp][g] = m;
+    sm_l[warp][g] = l;
+  }
+#pragma unroll
+  for (int d = 0; d < 16; ++d) {
+    sm_o[warp][g][d * 8 + 2 * t4] = o[d][0];
+    sm_o[warp][g][d * 8 + 2 * t4 + 1] = o[d][1];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm_m[w][r]);
+    float Ls = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (sm_m[w][r] == -INFINITY) continue;
+      const float c = exp2f(sm_m[w][r] - M);
+      Ls += sm_l[w][r] * c;
+      acc += sm_o[w][r][d] * c;
+    }
+    out[static_cast<long long>(s) * ldo + static_cast<long long>(hk * G + r) * D + d] =
+        __float2bfloat16_rn(Ls > 0.f ? acc / Ls : 0.f);
+  }
+}
+
 // ------------------------------------------------------------------ sampling
-// One CTA per row of logits [B, V] (bf16): token = argmax(logit/T + Gumbel)
-// with Philox noise keyed by (seed, row, step); also returns the token's
-// log-probability under softmax(logit / T).  temperature <= 0: greedy.
+// One CTA per row of logits [B, V] (bf16), temperature T (<= 0: greedy).
+// Sampling is exact inverse-CDF sampling from softmax(logit / T), done with
+// one exp per element:
+//   pass 1  each thread keeps an online (max, sum of exp) over its elements
+//           (16-byte loads of 8 logits, interleaved across threads) and the
+//           argmax; the block combines them into the row max M and S.
+//   pick    one Philox uniform u per (seed, row, step); the threads' scaled
+//           sums, scanned in thread order, locate the thread whose elements
+//           hold the quantile u * S; that thread re-walks its own elements
+//           (the same order) to find the token.  Any fixed order of the
+//           categories gives the same distribution.
+// Also returns the token's log-probability z_tok / T - (M + log S), and with
+// tok_mat / lp_mat writes both into column `step` (a device counter).
+__device__ __forceinline__ void online_add(float& m, float& s, float z) {
+  if (z > m) {
+    s = s * __expf(m - z) + 1.f;
+    m = z;
+  } else if (z != -INFINITY) {
+    s += __expf(z - m);
+  }
+}
+
 __global__ void __launch_bounds__(1024) sample_kernel(const bf16* __restrict__ logits, long long ld, int V,
                                                      float temperature, unsigned long long seed,
                                                      const long long* __restrict__ step_ptr, long long step_imm,
                                                      int* __restrict__ out_tok, float* __restrict__ out_logp,
                                                      int* __restrict__ tok_mat, float* __restrict__ lp_mat,
-                                                     int ld_mat) {
+                                                     int ld_mat, const unsigned long long* __restrict__ seed_ptr,
+                                                     const float* __restrict__ temp_ptr) {
   const int row = blockIdx.x;
   const bf16* x = logits + static_cast<long long>(row) * ld;
+  if (seed_ptr) seed = *seed_ptr;
+  if (temp_ptr) temperature = *temp_ptr;
   const float inv_t = temperature > 0.f ? 1.f / temperature : 1.f;
   const bool greedy = temperature <= 0.f;
   const long long step = step_ptr ? *step_ptr : step_imm;
-  float mx = -INFINITY, best = -INFINITY;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  const int nv = vec ? V / 8 : 0;
+  float m = -INFINITY, sm = 0.f, best = -INFINITY;
   int best_i = 0;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+  for (int c = tid; c < nv; c += nt) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + c * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      const float z0 = f.x * inv_t, z1 = f.y * inv_t;
+      if (z0 > best) { best = z0; best_i = c * 8 + 2 * k; }
+      if (z1 > best) { best = z1; best_i = c * 8 + 2 * k + 1; }
+      online_add(m, sm, z0);
+      online_add(m, sm, z1);
+    }
+  }
+  for (int i = nv * 8 + tid; i < V; i += nt) {
     const float z = bf(x[i]) * inv_t;
-    mx = fmaxf(mx, z);
-    float key = z;
-    if (!greedy) {
-      const uint4 r = tb::Philox::gen(seed, static_cast<uint32_t>(i), static_cast<uint32_t>(row),
-                                      static_cast<uint32_t>(step), static_cast<uint32_t>(step >> 32));
-      key = z - __logf(-__logf(tb::u01_open(r.x)));
-    }
-    if (key > best) {
-      best = key;
-      best_i = i;
-    }
+    if (z > best) { best = z; best_i = i; }
+    online_add(m, sm, z);
   }
-  __shared__ float s_m[32], s_b[32];
+  // ---- block max / argmax, then the sum rescaled to the block max
+  __shared__ float s_a[32], s_b[32];
   __shared__ int s_i[32];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  __shared__ float s_M, s_S, s_target;
+  __shared__ int s_tok, s_owner;
+  const int lane = tid & 31, w = tid >> 5, nw = nt >> 5;
+  float bm = m, bb = best;
+  int bi = best_i;
   for (int o = 16; o > 0; o >>= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-    if (ob > best || (ob == best && oi < best_i)) {
-      best = ob;
-      best_i = oi;
-    }
+    bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+    const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > bb || (ob == bb && oi < bi)) { bb = ob; bi = oi; }
   }
-  if (lane == 0) {
-    s_m[w] = mx;
-    s_b[w] = best;
-    s_i[w] = best_i;
-  }
+  if (lane == 0) { s_a[w] = bm; s_b[w] = bb; s_i[w] = bi; }
   __syncthreads();
   if (w == 0) {
-    const int nw = blockDim.x >> 5;
-    mx = lane < nw ? s_m[lane] : -INFINITY;
-    best = lane < nw ? s_b[lane] : -INFINITY;
-    best_i = lane < nw ? s_i[lane] : 0;
+    bm = lane < nw ? s_a[lane] : -INFINITY;
+    bb = lane < nw ? s_b[lane] : -INFINITY;
+    bi = lane < nw ? s_i[lane] : 0;
     for (int o = 16; o > 0; o >>= 1) {
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-      if (ob > best || (ob == best && oi < best_i)) {
-        best = ob;
-        best_i = oi;
-      }
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      const float ob = __shfl_xor_sync(0xffffffffu, bb, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > bb || (ob == bb && oi < bi)) { bb = ob; bi = oi; }
     }
-    if (lane == 0) {
-      s_m[0] = mx;
-      s_i[0] = best_i;
+    if (lane == 0) { s_M = bm; s_tok = bi; }
+  }
+  __syncthreads();
+  const float M = s_M;
+  const float wt = (m == -INFINITY) ? 0.f : sm * __expf(m - M);  // this thread's share of S
+  // inclusive scan of wt in thread order (warp scans + a scan of warp totals)
+  float inc = wt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  __syncthreads();
+  if (lane == 31) s_a[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    float t = lane < nw ? s_a[lane] : 0.f;
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < nw) s_b[lane] = t;  // inclusive warp-total prefix
+    if (lane == 31) {
+      s_S = t;
+      const uint4 r = tb::Philox::gen(seed, 0x53414D50u, static_cast<uint32_t>(row), static_cast<uint32_t>(step),
+                                      static_cast<uint32_t>(step >> 32));
+      s_target = tb::u01_open(r.x) * t;
+      s_owner = -1;
     }
   }
   __syncthreads();
-  mx = s_m[0];
-  float se = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) se += __expf(bf(x[i]) * inv_t - mx);
-  __shared__ float s_red[32];
-  se = tb::block_sum(se, s_red);
-  if (threadIdx.x == 0) {
-    const int tok = s_i[0];
-    const float lp = bf(x[tok]) * inv_t - (mx + __logf(se));
+  const float S = s_S;
+  if (!greedy) {
+    const float excl = inc - wt + (w > 0 ? s_b[w - 1] : 0.f);
+    const float target = s_target;
+    // the owner: excl <= target < excl + wt; rounding past the end falls to the last thread with mass
+    if (wt > 0.f && excl <= target && (target < excl + wt)) atomicMax(&s_owner, tid);
+    __syncthreads();
+    if (s_owner < 0) {
+      if (wt > 0.f) atomicMax(&s_owner, tid);
+      __syncthreads();
+    }
+    if (tid == s_owner) {
+      float acc = excl;
+      int tok = -1, last_i = -1;
+      for (int c = tid; c < nv; c += nt) {
+        const uint4 u = *reinterpret_cast<const uint4*>(x + c * 8);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          const float z0 = f.x * inv_t, z1 = f.y * inv_t;
+          if (z0 != -INFINITY) { acc += __expf(z0 - M); last_i = c * 8 + 2 * k; if (tok < 0 && acc > target) tok = last_i; }
+          if (z1 != -INFINITY) { acc += __expf(z1 - M); last_i = c * 8 + 2 * k + 1; if (tok < 0 && acc > target) tok = last_i; }
+        }
+      }
+      for (int i = nv * 8 + tid; i < V; i += nt) {
+        const float z = bf(x[i]) * inv_t;
+        if (z != -INFINITY) { acc += __expf(z - M); last_i = i; if (tok < 0 && acc > target) tok = i; }
+      }
+      s_tok = tok >= 0 ? tok : last_i;
+    }
+    __syncthreads();
+  }
+  if (tid == 0) {
+    const int tok = s_tok;
+    const float lp = bf(x[tok]) * inv_t - (M + __logf(S));
     out_tok[row] = tok;
     if (out_logp) out_logp[row] = lp;
     // generation matrices [B, ld_mat]: column = the decode step (device counter)
@@ -643,6 +907,13 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
   auto* k = static_cast<const bf16*>(kc);
   auto* v = static_cast<const bf16*>(vc);
   auto* o = static_cast<bf16*>(out);
+  if (bs == 16 && G <= 8) {
+    const cudaError_t e = tb::ensure_dyn_smem(reinterpret_cast<const void*>(decode_attn_tc_kernel), kDecTcSmem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    decode_attn_tc_kernel<<<grid, 128, kDecTcSmem, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk,
+                                                        G, scale);
+    return static_cast<int>(cudaGetLastError());
+  }
   switch (G) {
     case 1: decode_attn_kernel<1><<<grid, 128, 0, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk, bs, scale); break;
     case 2: decode_attn_kernel<2><<<grid, 128, 0, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk, bs, scale); break;
@@ -656,10 +927,11 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
 
 int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,
               const long long* step_ptr, long long step_imm, int* out_tok, float* out_logp, int* tok_mat,
-              float* lp_mat, int ld_mat, cudaStream_t s) {
+              float* lp_mat, int ld_mat, const unsigned long long* seed_ptr, const float* temp_ptr,
+              cudaStream_t s) {
   if (B <= 0) return 0;
   sample_kernel<<<B, 1024, 0, s>>>(static_cast<const bf16*>(logits), ld, V, temperature, seed, step_ptr, step_imm,
-                                    out_tok, out_logp, tok_mat, lp_mat, ld_mat);
+                                    out_tok, out_logp, tok_mat, lp_mat, ld_mat, seed_ptr, temp_ptr);
   return static_cast<int>(cudaGetLastError());
 }
 

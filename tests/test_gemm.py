@@ -76,7 +76,7 @@ def test_gemm_splitk_workspace_and_colsum(dev):
     o = ops()
     R, N, K = 32768, 256, 256
     dY, X = _mk((R, N), dev, 5), _mk((R, K), dev, 6)
-    ws = torch.empty(o.gemm_workspace_numel(N, K, R), device=dev)
+    ws = torch.zeros(o.gemm_workspace_numel(N, K, R), device=dev)
     assert ws.numel() > 0
     dW = torch.empty(N, K, device=dev)
     o.gemm(dY, X, dW, True, True, workspace=ws)
@@ -92,3 +92,84 @@ def test_gemm_splitk_workspace_and_colsum(dev):
     exp = (A.float() @ B.float()) * (1 - H.float() ** 2)
     assert torch.allclose(C.float(), exp, atol=3e-2, rtol=2e-2)
     assert torch.allclose(cs, exp.sum(0), atol=0.5, rtol=2e-2)
+
+
+@pytest.mark.parametrize("epi", ["residual", "tanh_bwd", "bias"])
+def test_gemm_splitk_workspace_epilogues(epi, dev):
+    # decode-shaped projection: few output tiles, long K -> split-K through the
+    # workspace, with the epilogue applied by the reduce pass (bf16 output)
+    o = ops()
+    M, N, K = 512, 1536, 8960
+    A, B = _mk((M, K), dev, 11), _mk((N, K), dev, 12)
+    ref = _ref(A, B, False, False)
+    H = torch.tanh(torch.randn(M, N, device=dev)).to(torch.bfloat16)
+    bias = torch.randn(N, device=dev)
+    ws = torch.zeros(o.gemm_workspace_numel(M, N, K), device=dev)
+    assert ws.numel() >= 2 * M * N
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    # 3 splits: in-kernel fix-up; 7 splits (the automatic count): reduce pass
+    for sk in (3, 0):
+        if epi == "residual":
+            o.gemm(A, B, C, aux=H, epi=o.EPI_RESIDUAL, workspace=ws, split_k=sk)
+            exp = ref + H.float()
+        elif epi == "tanh_bwd":
+            o.gemm(A, B, C, aux=H, epi=o.EPI_TANH_BWD, workspace=ws, split_k=sk)
+            exp = ref * (1 - H.float() ** 2)
+        else:
+            o.gemm(A, B, C, bias=bias, epi=o.EPI_BIAS, workspace=ws, split_k=sk)
+            exp = ref + bias
+        tol = 2e-2 * exp.abs().max().item()
+        assert (C.float() - exp).abs().max().item() < tol, sk
+
+
+def test_gemm_splitk_inkernel_fixup_accumulate(dev):
+    # three splits: the last warp to finish each slice sums the partials in-kernel;
+    # fp32 accumulate + alpha + fused column sums, twice in a row (the arrival
+    # counters must be left zero by the first call)
+    o = ops()
+    M, N, K = 300, 200, 4096
+    A, B = _mk((M, K), dev, 21), _mk((N, K), dev, 22)
+    ref = _ref(A, B, False, False)
+    ws = torch.zeros(2 * 1024 * 1024, device=dev)
+    C0 = torch.randn(M, N, device=dev)
+    C = C0.clone()
+    cs = torch.empty(N, device=dev)
+    for call in range(2):
+        o.gemm(A, B, C, accumulate=True, alpha=0.5, split_k=3, workspace=ws, colsum=cs)
+        exp = C0 + 0.5 * ref * (call + 1)
+        assert torch.allclose(C, exp, atol=0.05, rtol=1e-2), (call, (C - exp).abs().max())
+        assert torch.allclose(cs, 0.5 * ref.sum(0), atol=1.0, rtol=1e-2), call
+    assert int(ws[:8192].view(torch.int32).abs().sum()) == 0  # counters back at zero
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tile_widths(a_mn, b_mn, bn, dev):
+    M, N, K = 384, 448, 320
+    A = _mk((K, M) if a_mn else (M, K), dev, 31)
+    B = _mk((K, N) if b_mn else (N, K), dev, 32)
+    C = torch.empty(M, N, device=dev, dtype=torch.float32)
+    ops().gemm(A, B, C, a_mn, b_mn, bn=bn)
+    ref = _ref(A, B, a_mn, b_mn)
+    assert torch.allclose(C, ref, atol=5e-2, rtol=1e-2), (C - ref).abs().max()
+
+
+def test_gemm_bn64_epilogues(dev):
+    # decode-shaped (few rows): the automatic tile width is 64
+    o = ops()
+    M, N, K = 512, 1536, 1536
+    A, B = _mk((M, K), dev, 41), _mk((N, K), dev, 42)
+    ref = _ref(A, B, False, False)
+    H = torch.randn(M, N, device=dev).to(torch.bfloat16)
+    C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    o.gemm(A, B, C, aux=H, epi=o.EPI_RESIDUAL)
+    exp = ref + H.float()
+    assert (C.float() - exp).abs().max().item() < 2e-2 * exp.abs().max().item()
+    S = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16)
+    o.gemm(A, B, S, epi=o.EPI_SWIGLU, bn=64)
+    exp = torch.nn.functional.silu(ref[:, 0::2]) * ref[:, 1::2]
+    assert (S.float() - exp).abs().max().item() < 2e-2 * exp.abs().max().item()
+    cs = torch.empty(N, device=dev)
+    Cf = torch.empty(M, N, device=dev)
+    o.gemm(A, B, Cf, bn=64, colsum=cs)
+    assert torch.allclose(cs, ref.sum(0), atol=1.0, rtol=1e-2)

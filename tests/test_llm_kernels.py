@@ -82,26 +82,35 @@ def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
         assert err < 3e-2, err
 
 
-def test_decode_attention_paged(dev):
-    B, Hq, Hk, D, bs = 5, 12, 2, 128, 16
+@pytest.mark.parametrize("Hq,Hk,bs", [(12, 2, 16), (32, 8, 16), (8, 1, 16), (4, 4, 16), (12, 2, 8)])
+def test_decode_attention_paged(dev, Hq, Hk, bs):
+    # bs 16 with up to 8 query heads per kv head runs the tensor-core kernel; bs 8 the CUDA-core one
+    B, D = 5, 128
     lens = [1, 17, 33, 100, 64]
-    nblk = 40
+    nblk = 80
     kc = bf(torch.randn(nblk, Hk, bs, D, device=dev))
     vc = bf(torch.randn(nblk, Hk, bs, D, device=dev))
     perm = torch.randperm(nblk)
-    table = torch.zeros(B, 8, dtype=torch.int32)
+    table = torch.zeros(B, 16, dtype=torch.int32)
     used = 0
     for b in range(B):
         nb = (lens[b] + bs - 1) // bs
         table[b, :nb] = perm[used:used + nb].to(torch.int32)
         used += nb
     table = table.to(dev)
+    # slots past each context hold garbage in a real cache: make it non-finite here
+    for b in range(B):
+        L = lens[b]
+        if L % bs:
+            kc[table[b, L // bs], :, L % bs:] = float("nan")
+            vc[table[b, L // bs], :, L % bs:] = float("inf")
     q = bf(torch.randn(B, Hq * D, device=dev))
     out = torch.empty_like(q)
     ctx = torch.tensor(lens, device=dev, dtype=torch.int32)
     ops().decode_attention(q, kc, vc, table, ctx, out, Hq, Hk, D, bs, 1 / math.sqrt(D))
     for b in range(B):
         L = lens[b]
+        assert torch.isfinite(out[b].float()).all(), b
         ks = torch.cat([kc[table[b, j]].float() for j in range((L + bs - 1) // bs)], 1)[:, :L]  # [Hk, L, D]
         vs = torch.cat([vc[table[b, j]].float() for j in range((L + bs - 1) // bs)], 1)[:, :L]
         qq = q[b].float().view(Hq, D)
@@ -127,6 +136,15 @@ def test_sample_and_logprob(dev):
     ops().sample(small, 1.0, 7, None, 3, t, None)
     freq = torch.bincount(t.long(), minlength=4).float() / 4096
     assert torch.allclose(freq.cpu(), torch.softmax(small[0].float(), -1).cpu(), atol=0.03)
+    # vectorized rows (V % 8 == 0), temperature 0.7, log-probs of the sampled tokens
+    row = torch.randn(1, 96) * 2
+    wide = bf(row.repeat(16384, 1).to(dev))
+    t2, lp2 = torch.empty(16384, device=dev, dtype=torch.int32), torch.empty(16384, device=dev)
+    ops().sample(wide, 0.7, 11, None, 5, t2, lp2)
+    p = torch.softmax(wide[0].float() / 0.7, -1)
+    freq = torch.bincount(t2.long(), minlength=96).float() / 16384
+    assert (freq - p).abs().max().item() < 0.02
+    assert torch.allclose(lp2, p.log()[t2.long()], atol=1e-3)
     # log-probs and the in-place gradient
     tgt = torch.randint(0, V, (B,), device=dev, dtype=torch.int32)
     lg = logits.clone()

@@ -139,7 +139,9 @@ class FusedActorCritic:
             o = _ops()
             n = max(o.gemm_workspace_numel(H, H, B), o.gemm_workspace_numel(PAD, H, B),
                     o.gemm_workspace_numel(2 * H, PAD, B), 1)
-            ws["splitk"] = torch.empty(n, **f32)  # split-K partials of the weight-gradient GEMMs
+            # split-K partials of the weight-gradient GEMMs (zero-filled: its
+            # head holds arrival counters that every call leaves zero)
+            ws["splitk"] = torch.zeros(n, **f32)
             self._ws[B] = ws
         return ws
 

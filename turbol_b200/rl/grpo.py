@@ -73,6 +73,23 @@ class GRPOTrainer:
         self.step_count = 0
         self.last_times = {}
 
+    # ------------------------------------------------------------------ checkpoint
+    def state_dict(self) -> dict:
+        """Master weights (fp32), the frozen reference weights, optimizer state and
+        the step counter (which also keys the prompt and sampling streams)."""
+        return {"policy": {"flat": self.model.flat, "shadow": self.model.shadow},
+                "optim": self.opt.state_dict(), "ref_shadow": self.ref.shadow,
+                "step_count": self.step_count, "gen_calls": self.gen.calls}
+
+    def load_state_dict(self, sd: dict):
+        with torch.no_grad():
+            self.model.flat.copy_(sd["policy"]["flat"])
+            self.model.shadow.copy_(sd["policy"]["shadow"])
+            self.ref.shadow.copy_(sd["ref_shadow"])
+            self.opt.load_state_dict(sd["optim"])
+        self.step_count = int(sd["step_count"])
+        self.gen.calls = int(sd["gen_calls"])
+
     # ------------------------------------------------------------------ helpers
     def _prompts(self) -> torch.Tensor:
         g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count)

@@ -381,7 +381,8 @@ class PPOTrainer:
         pol = self.net.state_dict() if self.fused else self.policy.state_dict()
         return {"policy": pol, "optim": self.opt.state_dict(), "iteration": self.iteration,
                 "iter_t": self.iter_t.clone(), "env_state": self.state.clone(),
-                "ep": (self.ep_len.clone(), self.ep_ret.clone(), self.ep_count.clone())}
+                "ep": (self.ep_len.clone(), self.ep_ret.clone(), self.ep_count.clone()),
+                "cpu_rng": self._cpu_gen.get_state()}
 
     def load_state_dict(self, sd):
         with torch.no_grad():
@@ -395,3 +396,5 @@ class PPOTrainer:
             self.state.copy_(sd["env_state"])
             for dst, src in zip((self.ep_len, self.ep_ret, self.ep_count), sd["ep"]):
                 dst.copy_(src)
+            if "cpu_rng" in sd:
+                self._cpu_gen.set_state(sd["cpu_rng"])

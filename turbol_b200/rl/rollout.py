@@ -55,6 +55,12 @@ class LLMGenerator:
         self._graph_B = None
         self.calls = 0
 
+    def reset_graph(self):
+        """Drops the captured decode step.  The capture holds the model's weight
+        and KV-cache addresses: call this after rebinding the model's storage."""
+        self._graph = None
+        self._graph_B = None
+
     # ------------------------------------------------------------ block tables
     def _tables(self, P: int, G: int, Lp: int, steps: int):
         """Block tables with the prompt blocks shared by the G samples of a prompt."""
@@ -111,8 +117,8 @@ class LLMGenerator:
             o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
-        o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls, st["step"], 0, st["tok"], None,
-                 st["tok_mat"], st["lp_mat"])
+        o.sample(st["logits"], 1.0, 0, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
+                 seed_t=st["seed_t"], temp_t=st["temp_t"])
         st["pos"].add_(1)
         st["ctx"].add_(1)
         o.counter_add(st["step"], 1)
@@ -134,6 +140,10 @@ class LLMGenerator:
             "step": torch.zeros(1, device=dev, dtype=torch.int64),
             "tok_mat": torch.zeros(B, steps, device=dev, dtype=torch.int32),
             "lp_mat": torch.zeros(B, steps, device=dev, dtype=torch.float32),
+            # sampling seed and temperature live on the device so that one
+            # captured decode step serves every generate call
+            "seed_t": torch.zeros(1, device=dev, dtype=torch.int64),
+            "temp_t": torch.ones(1, device=dev, dtype=torch.float32),
         }
 
     # ------------------------------------------------------------ generate
@@ -182,6 +192,8 @@ class LLMGenerator:
         hB = h.repeat_interleave(G, 0).contiguous()
         o.gemm(hB, m.head_weight(), st["logits"])
         st["step"].zero_()
+        st["seed_t"].fill_(self.seed + 7919 * self.calls)
+        st["temp_t"].fill_(self.temperature)
         o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls + 1, st["step"], 0, st["tok"], None,
                  st["tok_mat"], st["lp_mat"])
         o.counter_add(st["step"], 1)
@@ -190,23 +202,25 @@ class LLMGenerator:
         steps = max_new - 1
         if steps > 0:
             if self.cuda_graph:
-                # capture one decode step (re-captured per call: the sampling
-                # seed is a launch parameter), then replay it per token
-                saved = {k: v.clone() for k, v in st.items() if k in ("tok", "pos", "ctx", "step")}
+                # capture one decode step once per (batch, length) shape, then
+                # replay it per token; everything that changes between calls
+                # (tokens, positions, block tables, seed, temperature) is read
+                # from device memory
                 if self._graph is None:
+                    saved = {k: v.clone() for k, v in st.items() if k in ("tok", "pos", "ctx", "step")}
                     s = torch.cuda.Stream(device=self.device)
                     s.wait_stream(torch.cuda.current_stream(self.device))
-                    with torch.cuda.stream(s):  # first call: warm-up outside capture
+                    with torch.cuda.stream(s):  # warm-up outside capture
                         self._decode_step(B)
                     torch.cuda.current_stream(self.device).wait_stream(s)
                     for k, v in saved.items():
                         st[k].copy_(v)
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    self._decode_step(B)
-                for k, v in saved.items():
-                    st[k].copy_(v)
-                self._graph, self._graph_B = g, (B, max_new)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._decode_step(B)
+                    for k, v in saved.items():
+                        st[k].copy_(v)
+                    self._graph, self._graph_B = g, (B, max_new)
                 for _ in range(steps):
                     self._graph.replay()
             else:
@@ -252,8 +266,10 @@ class RolloutEngine:
         elif c.inference_backend == "vllm":
             from ..vllm_inference import VLLMInferenceConfig, VLLMInferenceEngine
 
-            self._vllm = VLLMInferenceEngine(VLLMInferenceConfig(model=c.model_path, max_tokens=c.max_new_tokens,
-                                                                 temperature=c.temperature, top_p=c.top_p))
+            self._vllm = VLLMInferenceEngine(VLLMInferenceConfig(
+                model=c.model_path or VLLMInferenceConfig.model, tensor_parallel_size=c.tensor_parallel_size,
+                max_new_tokens=c.max_new_tokens, temperature=c.temperature, top_p=c.top_p, top_k=c.top_k,
+                max_batch_size=c.max_batch_size))
         self.initialized = True
         return Status()
 
@@ -262,6 +278,10 @@ class RolloutEngine:
         self._vllm = None
         self.initialized = False
         return _core().Status()
+
+    def is_native_available(self) -> bool:
+        """True when generation runs on this package's own decode engine (not the echo fallback)."""
+        return self._gen is not None
 
     def is_vllm_available(self) -> bool:
         from ..vllm_inference import vllm_available
@@ -288,4 +308,5 @@ class RolloutEngine:
         new = max(1, min(self.config.max_new_tokens, self._gen.max_len - L))
         seqs, _ = self._gen.generate(ids, 1, new, self.config.temperature)
         out = seqs[:, L:].cpu().tolist()
-        return [tok.decode([t for t in row if t < 256]) for row in out]
+        # random-init weights emit arbitrary bytes: decode leniently
+        return [bytes(t for t in row if t < 256).decode("utf-8", errors="replace") for row in out]
