@@ -15,9 +15,57 @@ void cuda_ok(int e, const char* what) {
   if (e != 0) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(static_cast<cudaError_t>(e)));
 }
 cudaStream_t cur_stream(int dev) { return c10::cuda::getCurrentCUDAStream(dev).stream(); }
+
+// Counters of one tensor-parallel communicator (int32 CUDA tensor [8]):
+// [0] all-gather epoch, [1] all-gather CTA counter, [2] reduce-scatter epoch,
+// [3] reduce-scatter CTA counter, [4..5] reduce-scatter arrival targets,
+// [6] error word.
+extern "C" void tb_tp_set_trace(void* p);
+TbTpComm tp_comm(const PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, int rows_per_rank,
+                 const at::Tensor& ctr, bool rs) {
+  if (!ctr.is_cuda() || ctr.scalar_type() != at::kInt || ctr.numel() < 8 || !ctr.is_contiguous())
+    throw std::invalid_argument("tp: counters must be a contiguous int32 CUDA tensor [8]");
+  const TbPeerTable t = p.Table();
+  TbTpComm c{};
+  c.rank = t.rank;
+  c.world = t.world;
+  c.rows_per_rank = rows_per_rank;
+  auto* u = reinterpret_cast<unsigned*>(ctr.data_ptr<int>());
+  c.epoch_ctr = rs ? u + 2 : u;
+  c.done_ctr = rs ? u + 3 : u + 1;
+  c.rs_target = u + 4;
+  c.err = ctr.data_ptr<int>() + 6;
+  for (int r = 0; r < t.world; ++r) {
+    c.hdr[r] = static_cast<char*>(t.base[r]) + hdr_off;
+    c.data[r] = static_cast<char*>(t.base[r]) + data_off;
+  }
+  c.parity_bytes = parity_bytes;
+  return c;
+}
+
+TbGemmArgs tp_gemm_args(const at::Tensor& A, const at::Tensor& B, bool b_mn, int bn) {
+  if (!A.is_cuda() || !B.is_cuda() || A.scalar_type() != at::kBFloat16 || B.scalar_type() != at::kBFloat16 ||
+      A.dim() != 2 || B.dim() != 2 || A.stride(1) != 1 || B.stride(1) != 1)
+    throw std::invalid_argument("tp gemm: A and B must be 2-D bf16 CUDA tensors with a contiguous last dim");
+  TbGemmArgs a{};
+  a.A = A.data_ptr();
+  a.lda = A.stride(0);
+  a.B = B.data_ptr();
+  a.ldb = B.stride(0);
+  a.b_mn = b_mn;
+  a.K = static_cast<int>(A.size(1));
+  a.N = static_cast<int>(b_mn ? B.size(1) : B.size(0));
+  if ((b_mn ? B.size(0) : B.size(1)) != A.size(1)) throw std::invalid_argument("tp gemm: K mismatch");
+  a.bn_hint = bn;
+  return a;
+}
 }  // namespace
 
 void register_comm_ops(py::module_& m) {
+  m.def("tp_header_bytes", []() { return static_cast<int64_t>(tb_tp_header_bytes()); });
+  m.def("tp_set_trace", [](py::object t) {
+    tb_tp_set_trace(t.is_none() ? nullptr : t.cast<at::Tensor>().data_ptr());
+  });
   py::class_<PeerMemory>(m, "PeerMemory")
       .def(py::init<size_t, int>(), py::arg("payload_bytes"), py::arg("device"))
       .def("handle", [](const PeerMemory& p) { return py::bytes(p.Handle()); })
@@ -55,6 +103,80 @@ void register_comm_ops(py::module_& m) {
                      "peer_allreduce");
            },
            py::arg("in_offset"), py::arg("out_offset"), py::arg("numel"), py::arg("scale") = 1.0f)
+      .def("payload_ptrs",
+           [](const PeerMemory& p) {
+             const TbPeerTable t = p.Table();
+             std::vector<int64_t> v;
+             for (int r = 0; r < t.world; ++r) v.push_back(reinterpret_cast<int64_t>(t.base[r]));
+             return v;
+           })
+      // all-gather -> GEMM: out[M, N] = gather_rows(shard) . W^T  (+ epilogue)
+      .def("tp_ag_gemm",
+           [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr,
+              at::Tensor shard, at::Tensor W, at::Tensor out, bool b_mn, py::object bias, py::object aux, int epi,
+              int bn) {
+             TbGemmArgs a = tp_gemm_args(shard, W, b_mn, bn);
+             const int rows = static_cast<int>(shard.size(0));
+             a.M = rows * p.world();
+             if (!out.is_cuda() || out.dim() != 2 || out.stride(1) != 1 || out.size(0) != a.M ||
+                 out.size(1) != (epi == TB_EPI_SWIGLU ? a.N / 2 : a.N))
+               throw std::invalid_argument("tp_ag_gemm: out must be [world * rows, N]");
+             a.C = out.data_ptr();
+             a.ldc = out.stride(0);
+             a.c_fp32 = out.scalar_type() == at::kFloat;
+             a.epi = epi;
+             at::Tensor b, x;
+             if (!bias.is_none()) {
+               b = bias.cast<at::Tensor>();
+               a.bias = b.data_ptr<float>();
+             }
+             if (!aux.is_none()) {
+               x = aux.cast<at::Tensor>();
+               a.aux = x.data_ptr();
+               a.ld_aux = x.stride(0);
+             }
+             TbTpComm c = tp_comm(p, hdr_off, data_off, parity_bytes, rows, ctr, false);
+             a.error = c.err;
+             cuda_ok(tb_tp_ag_gemm(&c, &a, cur_stream(p.device())), "tp_ag_gemm");
+           },
+           py::arg("hdr_off"), py::arg("data_off"), py::arg("parity_bytes"), py::arg("ctr"), py::arg("shard"),
+           py::arg("W"), py::arg("out"), py::arg("b_mn") = false, py::arg("bias") = py::none(),
+           py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0)
+      // GEMM -> reduce-scatter: out[M / world, N] = rows of sum_r(A_r . W_r^T) (+ bias) (+ residual)
+      .def("tp_gemm_rs",
+           [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr, at::Tensor A,
+              at::Tensor W, at::Tensor out, bool b_mn, py::object bias, py::object residual, int bn) {
+             TbGemmArgs a = tp_gemm_args(A, W, b_mn, bn);
+             a.M = static_cast<int>(A.size(0));
+             if (a.M % p.world()) throw std::invalid_argument("tp_gemm_rs: rows must divide by the world size");
+             const int rows = a.M / p.world();
+             if (!out.is_cuda() || out.scalar_type() != at::kBFloat16 || out.dim() != 2 || out.stride(1) != 1 ||
+                 out.size(0) != rows || out.size(1) != a.N)
+               throw std::invalid_argument("tp_gemm_rs: out must be bf16 [M / world, N]");
+             a.epi = TB_EPI_NONE;
+             at::Tensor b, r;
+             const float* bp = nullptr;
+             const void* rp = nullptr;
+             int64_t ldr = 0;
+             if (!bias.is_none()) {
+               b = bias.cast<at::Tensor>();
+               bp = b.data_ptr<float>();
+             }
+             if (!residual.is_none()) {
+               r = residual.cast<at::Tensor>();
+               if (r.scalar_type() != at::kBFloat16 || r.size(0) != rows || r.size(1) != a.N || r.stride(1) != 1)
+                 throw std::invalid_argument("tp_gemm_rs: residual must be bf16 [M / world, N]");
+               rp = r.data_ptr();
+               ldr = r.stride(0);
+             }
+             TbTpComm c = tp_comm(p, hdr_off, data_off, parity_bytes, rows, ctr, true);
+             a.error = c.err;
+             cuda_ok(tb_tp_gemm_rs(&c, &a, out.data_ptr(), out.stride(0), bp, rp, ldr, cur_stream(p.device())),
+                     "tp_gemm_rs");
+           },
+           py::arg("hdr_off"), py::arg("data_off"), py::arg("parity_bytes"), py::arg("ctr"), py::arg("A"),
+           py::arg("W"), py::arg("out"), py::arg("b_mn") = false, py::arg("bias") = py::none(),
+           py::arg("residual") = py::none(), py::arg("bn") = 0)
       .def("allreduce_adam",
            [](PeerMemory& p, int64_t grad_off, int64_t param_off, int64_t shadow_off, int64_t n, at::Tensor m1,
               at::Tensor m2, float lr, float b1, float b2, float eps, float wd, float grad_scale, at::Tensor step) {

@@ -42,6 +42,30 @@ constexpr int BM = 128, BK = 64;
 constexpr int kEpiWarps = 8;                    // two per TMEM lane quarter
 constexpr int kThreads = 128 + 32 * kEpiWarps;  // warps 0-3: TMA, MMA, TMEM, spare
 
+// Tensor-parallel collectives fused into the GEMM (see the TP section below).
+constexpr int kTpMaxRanks = TB_MAX_PEERS;
+constexpr int kTpSubRows = 8;    // rows per all-gather push unit (one ready flag each)
+constexpr int kTpMaxSub = 2048;  // push units per source rank (rows per rank <= 16384)
+struct TpHdr {                    // one per rank, at the start of its symmetric buffer
+  unsigned ready[2][kTpMaxRanks][kTpMaxSub];  // AG: [parity][src][unit] arrivals of the src's push warps
+                                              // (zeroed again by this rank once consumed)
+  unsigned consumed[kTpMaxRanks];             // AG: rank p has finished reading its staging (epoch)
+  unsigned rs_arrivals[2];                    // RS: [parity] CTA arrivals from every source (monotonic)
+  unsigned rs_consumed[kTpMaxRanks];          // RS: rank p has finished reading its receive slots (epoch)
+};
+struct TpArgs {
+  int rank, world, rows_per_rank;  // rows_per_rank (Mloc): a multiple of 128
+  unsigned* epoch_ctr;             // epoch of this op's previous call (local device memory)
+  unsigned* done_ctr;              // local CTA counter
+  TpHdr* hdr[kTpMaxRanks];         // every rank's header
+  char* data[kTpMaxRanks];         // every rank's data region (AG staging or RS receive slots)
+  long long parity_bytes;          // bytes per parity half of a data region
+  const __nv_bfloat16* shard;      // AG: this rank's rows [Mloc, K]
+  long long ld_shard;
+  int* err;
+  unsigned long long* trace;  // optional [grid][8] timestamps (diagnostics)
+};
+
 struct DevArgs {
   int M, N, K;
   int m_tiles, n_tiles, splits, kb_per_split, k_blocks;
@@ -57,6 +81,7 @@ struct DevArgs {
   int* slot_cnt;  // in-kernel split-K fix-up: one arrival counter per (tile, epilogue warp); null: reduce pass
   float* colsum;  // optional: column sums of the epilogue output, accumulated atomically
   int* error;
+  TpArgs tp;
 };
 
 // Workspace layout for split-K: [kCntBytes of fix-up counters][partials].
@@ -129,7 +154,7 @@ __device__ __forceinline__ float warp_colsum32(float* v, int lane) {
 // store the split-K partial; kEpiFinal: epilogue of already-scaled summed partials.
 enum { kEpiFull = 0, kEpiPartial = 1, kEpiFinal = 2 };
 __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane,
-                                           uint32_t* stg, int row0, int mode) {
+                                           uint32_t* stg, int row0, int mode, void* cbase) {
   const int N = p.N, epi = p.epi;
   const bool row_ok = row < p.M;
   const int valid = min(32, N - c0);
@@ -184,12 +209,12 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j] = fast_silu(v[2 * j]) * v[2 * j + 1];
     if (p.c_fp32) {
-      float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + oc0;
+      float* C = static_cast<float*>(cbase) + static_cast<long long>(row) * p.ldc + oc0;
 #pragma unroll
       for (int j = 0; j < 16; ++j)
         if (oc0 + j < Nout) C[j] = o[j];
     } else {
-      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + oc0;
+      __nv_bfloat16* C = static_cast<__nv_bfloat16*>(cbase) + static_cast<long long>(row) * p.ldc + oc0;
       if (oc0 + 16 <= Nout && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
         uint4 pk[2];
         __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(pk);
@@ -214,14 +239,14 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
   }
   if (!row_ok && (p.c_atomic || p.c_fp32)) return;
   if (p.c_atomic) {
-    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    float* C = static_cast<float*>(cbase) + static_cast<long long>(row) * p.ldc + c0;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < valid) atomicAdd(C + j, v[j]);
     return;
   }
   if (p.c_add) {  // C += result; this thread owns these elements (no split-K)
-    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    float* C = static_cast<float*>(cbase) + static_cast<long long>(row) * p.ldc + c0;
     if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -240,7 +265,7 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
     return;
   }
   if (p.c_fp32) {
-    float* C = static_cast<float*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
+    float* C = static_cast<float*>(cbase) + static_cast<long long>(row) * p.ldc + c0;
     if (valid == 32 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) reinterpret_cast<float4*>(C)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -250,8 +275,8 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
         if (j < valid) C[j] = v[j];
     }
   } else {
-    __nv_bfloat16* C = static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row) * p.ldc + c0;
-    if (valid == 32 && (p.ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
+    __nv_bfloat16* C = static_cast<__nv_bfloat16*>(cbase) + static_cast<long long>(row) * p.ldc + c0;
+    if (valid == 32 && (p.ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(cbase) & 15) == 0) {
       // transpose through shared memory so each store instruction writes
       // 8 whole 64-byte row segments instead of 32 scattered 16-byte pieces
       uint32_t* mine = stg + lane * 20;
@@ -267,7 +292,7 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
         const int r = it * 8 + (lane >> 2);
         const uint4 w = *reinterpret_cast<const uint4*>(stg + r * 20 + seg * 4);
         if (row0 + r < p.M)
-          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.C) + static_cast<long long>(row0 + r) * p.ldc + c0 +
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(cbase) + static_cast<long long>(row0 + r) * p.ldc + c0 +
                                     seg * 8) = w;
       }
       __syncwarp();
@@ -427,9 +452,53 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
-template <int BN, bool A_MN, bool B_MN>
+// ---------------------------------------------------------------- TP helpers
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* q) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(q) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* q, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(q), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* q, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(q), "r"(v) : "memory");
+}
+// Bounded wait until *q >= target (epochs compared wrap-safe).  On timeout
+// records `site` in the error word, raises the CTA's abort flag and returns false.
+__device__ __forceinline__ bool tp_wait_geq(const unsigned* q, unsigned target, int* err, int site,
+                                            volatile int* abort_flag) {
+  const unsigned long long t0 = global_ns();
+  while (static_cast<int>(ld_acquire_sys(q) - target) < 0) {
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitBudgetNs) {
+      if (err) atomicCAS(err, 0, site);
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+// All-gather push split: the (peer, row, 16-byte vector) space of one rank's
+// pushes, T_all = (world - 1) * rows * vpr vectors, is cut into `nw` equal
+// contiguous ranges, one per push warp.  A unit of kTpSubRows rows is complete
+// when every warp whose range overlaps it has arrived.
+__device__ __forceinline__ long long push_begin(long long w, long long nw, long long T_all) { return w * T_all / nw; }
+__device__ __forceinline__ long long push_worker_of(long long i, long long nw, long long T_all) {
+  return ((i + 1) * nw - 1) / T_all;
+}
+
+// TP = 0: plain GEMM.  TP = 1: all-gather -> GEMM (rows of A are sharded over
+// the ranks; remote shards arrive by peer stores into local staging).  TP = 2:
+// GEMM -> reduce-scatter (each output tile is stored into the receive slot of
+// the rank that owns its rows; tp_rs_finish_kernel sums the slots).
+template <int BN, bool A_MN, bool B_MN, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, DevArgs p) {
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmA3,
+                        DevArgs p) {
   using S = Smem<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -443,6 +512,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.m_tiles * p.n_tiles * p.splits;
+  if (TP != 0 && p.tp.trace && threadIdx.x == 0) p.tp.trace[blockIdx.x * 8 + 0] = global_ns();
+  const unsigned epoch = TP ? *p.tp.epoch_ctr + 1u : 0u;
+  const unsigned parity = epoch & 1u;
+  const int mloc = TP ? p.tp.rows_per_rank : 0;
+  // all-gather: start with this rank's own row tiles while the remote shards arrive
+  // all-gather: own rows first (they need no transfer); reduce-scatter: the
+  // next rank's rows first, own rows last, so the peer stores of the first
+  // wave of tiles overlap the MMAs of the later ones
+  const int first_mt = TP == 1 ? (p.tp.rank * mloc) / BM
+                       : TP == 2 ? (((p.tp.rank + 1) % p.tp.world) * mloc) / BM : 0;
+  auto tile_m0 = [&](int m0) { return TP != 0 ? ((m0 / BM + first_mt) % p.m_tiles) * BM : m0; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -458,6 +538,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch(&tmA);
     tma_prefetch(&tmB);
+    if (TP == 1) {
+      tma_prefetch(&tmA2);
+      tma_prefetch(&tmA3);
+    }
   }
   if (warp == 2) tmem_alloc(tmem_slot, 2 * BN);
   tc_fence_before();
@@ -473,7 +557,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total && !*abort_flag; w += gridDim.x) {
       int m0, nt, ks, kb0, kb1;
       work_coords(p, w, m0, nt, ks, kb0, kb1);
+      m0 = tile_m0(m0);
       const int n0 = nt * BN;
+      int a_src = 0;  // TP == 1: rank that owns these rows
+      if constexpr (TP == 1) {
+        a_src = m0 / mloc;
+        if (a_src != p.tp.rank) {
+          // the push units of this tile: complete once every push warp of
+          // rank a_src whose range overlaps a unit has arrived
+          const int sub0 = (m0 - a_src * mloc) / kTpSubRows;
+          const unsigned* rdy = p.tp.hdr[p.tp.rank]->ready[parity][a_src];
+          if (p.tp.trace && p.tp.trace[blockIdx.x * 8 + 3] == 0) p.tp.trace[blockIdx.x * 8 + 3] = global_ns();
+          const long long vpr = p.K / 8, T = static_cast<long long>(mloc) * vpr;
+          const long long T_all = (p.tp.world - 1) * T, nw = 2ll * gridDim.x;  // every rank runs the same grid
+          const int pi = p.tp.rank < a_src ? p.tp.rank : p.tp.rank - 1;     // this rank's index among a_src's peers
+          bool ok = true;
+          for (int j = 0; j < BM / kTpSubRows && ok; ++j) {
+            const long long lo = pi * T + static_cast<long long>(sub0 + j) * kTpSubRows * vpr;
+            const long long hi = lo + kTpSubRows * vpr - 1;
+            const unsigned need = static_cast<unsigned>(push_worker_of(hi, nw, T_all) - push_worker_of(lo, nw, T_all) + 1);
+            ok = tp_wait_geq(rdy + sub0 + j, need, p.tp.err, 11, abort_flag);
+          }
+          if (!ok) break;
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // peer stores -> TMA reads
+          if (p.tp.trace && p.tp.trace[blockIdx.x * 8 + 4] == 0) p.tp.trace[blockIdx.x * 8 + 4] = global_ns();
+        }
+      }
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
         uint8_t* sa = smem + stage * S::kStageBytes;
@@ -483,6 +592,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (A_MN) {
 #pragma unroll
           for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 64 * BK * 2, &tmA, &full[stage], m0 + 64 * j, k0);
+        } else if (TP == 1) {
+          if (a_src == p.tp.rank) tma_load_2d(sa, &tmA, &full[stage], k0, m0 - a_src * mloc);
+          else tma_load_2d(sa, parity ? &tmA3 : &tmA2, &full[stage], k0, m0);
         } else {
           tma_load_2d(sa, &tmA, &full[stage], k0, m0);
         }
@@ -569,6 +681,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 1000000000ull) {
       }
     }
+  } else if (TP == 1 && (warp == 2 || warp == 3)) {
+    // ------------------------------------------------ all-gather push (warps 2, 3)
+    // Unit u (8 rows of this rank's shard, for one peer) goes into that peer's
+    // staging by peer stores over NVLink (16 16-byte loads in flight per lane),
+    // then one release flag per unit.
+    if constexpr (TP == 1) {
+      const int W = p.tp.world, r = p.tp.rank, K = p.K;
+      const long long vpr = K / 8, T = static_cast<long long>(mloc) * vpr, T_all = (W - 1) * T;
+      const long long nw = 2ll * gridDim.x, wk = 2ll * blockIdx.x + (warp - 2);
+      const long long b0 = push_begin(wk, nw, T_all), b1 = push_begin(wk + 1, nw, T_all);
+      if (b1 > b0) {
+        // the peers have finished reading this parity's staging from two calls ago
+        int ok = 1;
+        if (lane == 0 && epoch > 2u)
+          for (int o = 0; o < W && ok; ++o)
+            if (o != r) ok = tp_wait_geq(&p.tp.hdr[r]->consumed[o], epoch - 2u, p.tp.err, 12, abort_flag) ? 1 : 0;
+        if (__shfl_sync(0xffffffffu, ok, 0)) {
+          const char* src_base = reinterpret_cast<const char*>(p.tp.shard);
+          constexpr int kDepth = 16;
+          for (long long e0 = b0 + lane; e0 < b1; e0 += 32 * kDepth) {
+            uint4 v[kDepth];
+            uint32_t pk[kDepth], rw[kDepth], cc[kDepth];  // peer index, row, vector column (32-bit: T_all < 2^31)
+#pragma unroll
+            for (int q = 0; q < kDepth; ++q) {
+              const uint32_t e = static_cast<uint32_t>(e0 + q * 32);
+              pk[q] = e / static_cast<uint32_t>(T);
+              const uint32_t within = e - pk[q] * static_cast<uint32_t>(T);
+              rw[q] = within / static_cast<uint32_t>(vpr);
+              cc[q] = within - rw[q] * static_cast<uint32_t>(vpr);
+              if (e0 + q * 32 < b1)
+                v[q] = *reinterpret_cast<const uint4*>(src_base + (rw[q] * p.tp.ld_shard + cc[q] * 8ll) * 2);
+            }
+#pragma unroll
+            for (int q = 0; q < kDepth; ++q) {
+              if (e0 + q * 32 < b1) {
+                const int peer = static_cast<int>(pk[q]) >= r ? static_cast<int>(pk[q]) + 1 : static_cast<int>(pk[q]);
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.tp.data[peer] + parity * p.tp.parity_bytes);
+                *reinterpret_cast<uint4*>(dst + (static_cast<long long>(r) * mloc + rw[q]) * K + cc[q] * 8) = v[q];
+              }
+            }
+          }
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          __syncwarp();
+          // one arrival per unit this range touched
+          const long long u_first = b0 / (kTpSubRows * vpr), u_last = (b1 - 1) / (kTpSubRows * vpr);
+          for (long long u = u_first + lane; u <= u_last; u += 32) {  // u indexes (peer, unit) pairs
+            const int nsub = mloc / kTpSubRows;
+            const int pi = static_cast<int>(u / nsub), sub = static_cast<int>(u % nsub);
+            const int peer = pi >= r ? pi + 1 : pi;
+            red_release_sys_add(&p.tp.hdr[peer]->ready[parity][r][sub], 1u);
+          }
+        }
+      }
+      if (p.tp.trace && lane == 0) p.tp.trace[blockIdx.x * 8 + 1 + (warp - 2)] = global_ns();
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------ epilogue: 8 warps; warp (4 + q + 4h)
     // reads TMEM lane quarter q (rows 32q..32q+31) and column half h.
@@ -579,10 +746,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const int mode = p.ws != nullptr ? kEpiPartial : kEpiFull;
+    unsigned rs_ready = epoch <= 2u ? 0xffffffffu : 0u;  // bit o: rank o's slots may be written
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
       int m0, nt, ks, kb0, kb1;
       work_coords(p, w, m0, nt, ks, kb0, kb1);
+      m0 = tile_m0(m0);
       const int n0 = nt * BN;
+      void* cbase = p.C;
+      if constexpr (TP == 2) {
+        // this tile's rows belong to rank `o`: store into o's receive slot for
+        // this source rank, addressed so that the global row index applies
+        const int o = m0 / mloc;
+        if (!((rs_ready >> o) & 1u)) {  // o has finished reading this parity's slots from two calls ago
+          int ok = 1;
+          if (lane == 0) ok = tp_wait_geq(&p.tp.hdr[p.tp.rank]->rs_consumed[o], epoch - 2u, p.tp.err, 13, abort_flag);
+          if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+          rs_ready |= 1u << o;
+        }
+        cbase = p.tp.data[o] + parity * p.tp.parity_bytes +
+                (static_cast<long long>(p.tp.rank) - o) * mloc * p.N * 2;
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int row = m0 + r_in_tile;
@@ -597,11 +780,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode);
+        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode, cbase);
         if constexpr (kStep == 64) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
-          if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode);
+          if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode, cbase);
         }
       }
       tc_fence_before();
@@ -632,11 +815,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (TP == 2 && warp >= 4) __threadfence_system();  // this thread's peer stores, before the arrival below
+  if (TP != 0 && p.tp.trace && threadIdx.x == 128) p.tp.trace[blockIdx.x * 8 + 5] = global_ns();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, 2 * BN);
-  if (threadIdx.x == 0 && *abort_flag && p.error) atomicExch(p.error, TB_GEMM_ERR_TIMEOUT);
+  if (threadIdx.x == 0 && *abort_flag && p.error) atomicCAS(p.error, 0, TB_GEMM_ERR_TIMEOUT);  // keeps a site code
+  if constexpr (TP == 1) {
+    if (threadIdx.x == 0) {
+      // the last CTA: every CTA has finished reading staging -> tell the peers
+      __threadfence();
+      if (atomicAdd(p.tp.done_ctr, 1u) == gridDim.x - 1) {
+        *p.tp.done_ctr = 0;
+        // reset this parity's arrival counters (every CTA has consumed them)
+        const int nsub = mloc / kTpSubRows;
+        for (int o = 0; o < p.tp.world; ++o)
+          if (o != p.tp.rank)
+            for (int u = 0; u < nsub; ++u) p.tp.hdr[p.tp.rank]->ready[parity][o][u] = 0u;
+        __threadfence();
+        for (int o = 0; o < p.tp.world; ++o)
+          if (o != p.tp.rank) st_release_sys(&p.tp.hdr[o]->consumed[p.tp.rank], epoch);
+        *p.tp.epoch_ctr = epoch;
+      }
+    }
+  } else if constexpr (TP == 2) {
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int o = 0; o < p.tp.world; ++o) red_release_sys_add(&p.tp.hdr[o]->rs_arrivals[parity], 1u);
+    }
+  }
 }
 
 // C = sum over splits of the partials, then the epilogue (bias, activation,
@@ -814,13 +1022,105 @@ Plan make_plan(int M, int N, int K, int bn_hint, int split_k, bool can_split, si
   return pl;
 }
 
-template <int BN, bool A_MN, bool B_MN>
-int launch(const CUtensorMap& ta, const CUtensorMap& tbm, const DevArgs& p, int grid, cudaStream_t s) {
+template <int BN, bool A_MN, bool B_MN, int TP = 0>
+int launch(const CUtensorMap& ta, const CUtensorMap& tbm, const DevArgs& p, int grid, cudaStream_t s,
+           const CUtensorMap* ta2 = nullptr, const CUtensorMap* ta3 = nullptr) {
   using S = Smem<BN>;
-  auto k = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
+  auto k = gemm_tcgen05_kernel<BN, A_MN, B_MN, TP>;
   tb::ensure_dyn_smem(reinterpret_cast<const void*>(k), S::kTotal);
-  k<<<grid, kThreads, S::kTotal, s>>>(ta, tbm, p);
+  k<<<grid, kThreads, S::kTotal, s>>>(ta, tbm, ta2 ? *ta2 : ta, ta3 ? *ta3 : ta, p);
   return static_cast<int>(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------------------
+// Reduce-scatter finish: out[Mloc, N] = sum over source ranks of this rank's
+// receive slots (+ bias, + residual), once every CTA of every rank's GEMM has
+// arrived.  Then tells the peers that the slots of this parity may be reused.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) tp_rs_finish_kernel(TpArgs t, int N, const float* __restrict__ bias,
+                                                           const __nv_bfloat16* __restrict__ res, long long ld_res,
+                                                           __nv_bfloat16* __restrict__ out, long long ldo,
+                                                           unsigned* tgt, unsigned add) {
+  const unsigned epoch = *t.epoch_ctr + 1u, parity = epoch & 1u;
+  const unsigned target = tgt[parity] + add;
+  __shared__ int s_ok;
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    s_ok = tp_wait_geq(&t.hdr[t.rank]->rs_arrivals[parity], target, t.err, 14,
+                       reinterpret_cast<volatile int*>(&s_abort)) ? 1 : 0;
+  }
+  __syncthreads();
+  const int W = t.world, mloc = t.rows_per_rank;
+  if (s_ok) {
+    const char* base = t.data[t.rank] + parity * t.parity_bytes;
+    const long long slot = static_cast<long long>(mloc) * N;  // elements per source slot
+    const long long nvec = slot / 8;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < nvec;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      const long long e = i * 8;
+      const int row = static_cast<int>(e / N), col = static_cast<int>(e - static_cast<long long>(row) * N);
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < W; ++src) {
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(base) + src * (slot / 8) + i);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
+        }
+      }
+      if (bias) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += bias[col + k];
+      }
+      if (res) {
+        const uint4 u = *reinterpret_cast<const uint4*>(res + row * ld_res + col);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(h[k]);
+          acc[2 * k] += f.x;
+          acc[2 * k + 1] += f.y;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) oh[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+      *reinterpret_cast<uint4*>(out + row * ldo + col) = o;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(t.done_ctr, 1u) == gridDim.x - 1) {
+      *t.done_ctr = 0;
+      for (int o = 0; o < W; ++o) st_release_sys(&t.hdr[o]->rs_consumed[t.rank], epoch);  // self included
+      tgt[parity] = target;
+      *t.epoch_ctr = epoch;
+    }
+  }
+}
+
+unsigned long long* g_tp_trace = nullptr;
+
+bool fill_tp(TpArgs* tp, const TbTpComm* c) {
+  if (c->world < 1 || c->world > kTpMaxRanks || c->rank < 0 || c->rank >= c->world) return false;
+  tp->rank = c->rank;
+  tp->world = c->world;
+  tp->rows_per_rank = c->rows_per_rank;
+  tp->epoch_ctr = c->epoch_ctr;
+  tp->done_ctr = c->done_ctr;
+  for (int i = 0; i < kTpMaxRanks; ++i) {
+    tp->hdr[i] = static_cast<TpHdr*>(c->hdr[i]);
+    tp->data[i] = static_cast<char*>(c->data[i]);
+  }
+  tp->parity_bytes = c->parity_bytes;
+  tp->err = c->err;
+  tp->trace = g_tp_trace;
+  return true;
 }
 
 }  // namespace
@@ -925,5 +1225,117 @@ size_t tb_gemm_workspace_bytes(int M, int N, int K) {
   if (pl.splits < 2) return 0;
   return kCntBytes + sizeof(float) * static_cast<size_t>(M) * N * pl.splits;
 }
+
+size_t tb_tp_header_bytes(void) { return (sizeof(TpHdr) + 4095) / 4096 * 4096; }
+
+#define TB_TP_DISPATCH(TPV, BNV, BMN)                                                                \
+  (BMN ? launch<BNV, false, true, TPV>(ta, tbm, p, grid, stream, &ta2, &ta3)                       \
+       : launch<BNV, false, false, TPV>(ta, tbm, p, grid, stream, &ta2, &ta3))
+
+int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t stream) {
+  const int W = c->world, mloc = c->rows_per_rank;
+  if (a->M <= 0 || a->N <= 0) return 0;
+  if (a->a_mn || a->K <= 0 || a->K % 8 || a->lda % 8 || a->ldb % 8 || mloc % BM || a->M != W * mloc ||
+      mloc / kTpSubRows > kTpMaxSub || a->workspace || a->colsum || a->c_accumulate ||
+      c->parity_bytes < 2ll * a->M * a->K || c->parity_bytes % 16 || (reinterpret_cast<uintptr_t>(a->A) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->B) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  const Plan pl = make_plan(a->M, a->N, a->K, a->bn_hint, 1, false, 0);
+  const int BN = pl.BN;
+  if (g_tp_trace) cudaMemsetAsync(g_tp_trace, 0, 148 * 8 * 8, stream);
+  CUtensorMap ta, ta2, ta3, tbm;
+  const bool ok = make_map(&ta, a->A, mloc, a->K, a->lda, BM) &&
+                  make_map(&ta2, c->data[c->rank], a->M, a->K, a->K, BM) &&
+                  make_map(&ta3, static_cast<char*>(c->data[c->rank]) + c->parity_bytes, a->M, a->K, a->K, BM) &&
+                  (a->b_mn ? make_map(&tbm, a->B, a->K, a->N, a->ldb, BK) : make_map(&tbm, a->B, a->N, a->K, a->ldb, BN));
+  if (!ok) return static_cast<int>(cudaErrorInvalidValue);
+  DevArgs p{};
+  p.M = a->M;
+  p.N = a->N;
+  p.K = a->K;
+  p.m_tiles = pl.m_tiles;
+  p.n_tiles = pl.n_tiles;
+  p.k_blocks = pl.k_blocks;
+  p.splits = 1;
+  p.kb_per_split = pl.k_blocks;
+  p.C = a->C;
+  p.ldc = a->ldc;
+  p.c_fp32 = a->c_fp32;
+  p.bias = a->bias;
+  p.aux = static_cast<const __nv_bfloat16*>(a->aux);
+  p.ld_aux = a->ld_aux;
+  p.epi = a->epi;
+  p.alpha = a->alpha == 0.f ? 1.f : a->alpha;
+  p.error = a->error;
+  if (!fill_tp(&p.tp, c)) return static_cast<int>(cudaErrorInvalidValue);
+  p.tp.shard = static_cast<const __nv_bfloat16*>(a->A);
+  p.tp.ld_shard = a->lda;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const bool bmn = a->b_mn != 0;
+  if (BN == 256) return TB_TP_DISPATCH(1, 256, bmn);
+  if (BN == 128) return TB_TP_DISPATCH(1, 128, bmn);
+  return TB_TP_DISPATCH(1, 64, bmn);
+}
+
+int tb_tp_gemm_rs(const TbTpComm* c, const TbGemmArgs* a, void* out, long long ldo, const float* bias,
+                  const void* residual, long long ld_res, cudaStream_t stream) {
+  const int W = c->world, mloc = c->rows_per_rank;
+  if (a->M <= 0 || a->N <= 0) return 0;
+  if (a->a_mn || a->K <= 0 || a->lda % 8 || a->ldb % 8 || a->N % 8 || ldo % 8 || (residual && ld_res % 8) ||
+      mloc % BM || a->M != W * mloc || a->epi != TB_EPI_NONE || a->workspace || a->colsum || a->c_accumulate ||
+      c->parity_bytes < 2ll * W * mloc * a->N || (reinterpret_cast<uintptr_t>(a->A) & 15) ||
+      (reinterpret_cast<uintptr_t>(a->B) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(residual) & 15) || c->rs_target == nullptr)
+    return static_cast<int>(cudaErrorInvalidValue);
+  const Plan pl = make_plan(a->M, a->N, a->K, a->bn_hint, 1, false, 0);
+  const int BN = pl.BN;
+  CUtensorMap ta, tbm;
+  const bool ok = make_map(&ta, a->A, a->M, a->K, a->lda, BM) &&
+                  (a->b_mn ? make_map(&tbm, a->B, a->K, a->N, a->ldb, BK) : make_map(&tbm, a->B, a->N, a->K, a->ldb, BN));
+  if (!ok) return static_cast<int>(cudaErrorInvalidValue);
+  const CUtensorMap& ta2 = ta;
+  const CUtensorMap& ta3 = ta;
+  DevArgs p{};
+  p.M = a->M;
+  p.N = a->N;
+  p.K = a->K;
+  p.m_tiles = pl.m_tiles;
+  p.n_tiles = pl.n_tiles;
+  p.k_blocks = pl.k_blocks;
+  p.splits = 1;
+  p.kb_per_split = pl.k_blocks;
+  p.C = nullptr;
+  p.ldc = a->N;
+  p.c_fp32 = 0;
+  p.epi = TB_EPI_NONE;
+  p.alpha = a->alpha == 0.f ? 1.f : a->alpha;
+  p.error = a->error;
+  if (!fill_tp(&p.tp, c)) return static_cast<int>(cudaErrorInvalidValue);
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const bool bmn = a->b_mn != 0;
+  int err;
+  if (BN == 256) err = TB_TP_DISPATCH(2, 256, bmn);
+  else if (BN == 128) err = TB_TP_DISPATCH(2, 128, bmn);
+  else err = TB_TP_DISPATCH(2, 64, bmn);
+  if (err) return err;
+  TpArgs t = p.tp;
+  t.epoch_ctr = c->epoch_ctr;
+  const long long nvec = static_cast<long long>(mloc) * a->N / 8;
+  long long g = (nvec + 255) / 256;
+  if (g > 4ll * num_sms()) g = 4ll * num_sms();
+  if (g < 1) g = 1;
+  tp_rs_finish_kernel<<<static_cast<unsigned>(g), 256, 0, stream>>>(
+      t, a->N, bias, static_cast<const __nv_bfloat16*>(residual), ld_res, static_cast<__nv_bfloat16*>(out), ldo,
+      c->rs_target, static_cast<unsigned>(W * grid));
+  return static_cast<int>(cudaGetLastError());
+}
+#undef TB_TP_DISPATCH
+
+// Diagnostics: with a device buffer of at least 148 * 8 uint64, later
+// all-gather GEMMs record per-CTA globaltimer stamps (start, push end of warps
+// 2 and 3, first remote wait begin / end, main loop end).  nullptr turns it off.
+void tb_tp_set_trace(void* p) { g_tp_trace = static_cast<unsigned long long*>(p); }
 
 }  // extern "C"

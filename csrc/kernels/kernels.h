@@ -187,6 +187,32 @@ typedef struct {
 } TbPeerTable;
 
 size_t tb_peer_header_bytes(void);
+
+// ---- tensor parallelism: collectives fused into the tcgen05 GEMM -----------
+// Symmetric layout per rank (mapped into every peer): a header of
+// tb_tp_header_bytes() (flags) and a data region of two parity halves.
+typedef struct {
+  int rank, world, rows_per_rank;  // rows_per_rank: a multiple of 128
+  unsigned* epoch_ctr;             // device counter: epoch of this op's previous call (one per op)
+  unsigned* done_ctr;              // device counter, zero-initialized (one per op)
+  void* hdr[TB_MAX_PEERS];         // every rank's header
+  void* data[TB_MAX_PEERS];        // every rank's data region
+  long long parity_bytes;          // bytes of one parity half of a data region
+  int* err;                        // device error word (a nonzero site after a timed-out wait)
+  unsigned* rs_target;             // reduce-scatter only: device [2] arrival targets, zero-initialized
+} TbTpComm;
+size_t tb_tp_header_bytes(void);
+// C[M, N] = gather_rows(A) . B^T with A this rank's rows [rows_per_rank, K]
+// (a->A, a->lda) and M = world * rows_per_rank; the other ranks' rows arrive by
+// peer stores into this rank's data region (needs 2 * M * K * 2 bytes) while
+// the tiles of the local rows are computed.  Epilogues as tb_gemm_bf16.
+int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t s);
+// out[rows_per_rank, N] = (sum over ranks of A_r . B_r^T)[this rank's rows]
+// (+ bias) (+ residual): each GEMM tile is stored (bf16) into the receive slot
+// of the rank that owns its rows; a finishing kernel sums the slots.  The
+// data region needs 2 * M * N * 2 bytes.
+int tb_tp_gemm_rs(const TbTpComm* c, const TbGemmArgs* a, void* out, long long ldo, const float* bias,
+                  const void* residual, long long ld_res, cudaStream_t s);
 // out[i] = scale * sum_p in_p[i] for fp32 buffers at byte offsets in_off/out_off
 // of every rank's symmetric buffer (in-place when in_off == out_off).
 int tb_peer_allreduce(TbPeerTable t, long long in_off, long long out_off, long long n, float scale,
