@@ -16,3 +16,12 @@ def test_fused_dp_two_gpus():
            "--master-addr=127.0.0.1", "--master-port=29531", os.path.join(HERE, "dp_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "DP_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_grpo_data_parallel_two_gpus():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "500", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29535",
+           os.path.join(HERE, "grpo_dp_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "GRPO_DP_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

@@ -61,14 +61,46 @@ class GRPOConfig:
 
 
 class GRPOTrainer:
-    def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None):
+    """GRPO on one GPU, or data-parallel over a process group.
+
+    dp: "none"; "fused" (gradient reduce-scatter, sharded Adam and weight
+    all-gather in one NVLink peer-memory kernel; the model's fp32 weights,
+    gradient and bf16 copy live in symmetric memory); "nccl" (NCCL all-reduce
+    of the gradient + local fused Adam; the baseline).  With data parallelism
+    ``cfg.num_prompts`` is per rank and every rank samples its own prompts."""
+
+    def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None, dp: str = "none", group=None):
         self.cfg = cfg
         self.device = torch.device(device)
+        self.dp, self.group = dp, group
+        self.rank, self.world = 0, 1
+        if dp != "none":
+            import torch.distributed as dist
+
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.model = DecoderLM(cfg.model, self.device, seed=cfg.seed)
+        self.grad_sync = None
+        if dp == "fused":
+            from ..parallel.peer import FusedDataParallelAdam
+
+            self.opt = FusedDataParallelAdam(self.model.numel, group, lr=cfg.lr, betas=(0.9, 0.95))
+            self.model.rebind_storage(self.opt.param, self.opt.grad, self.opt.shadow)
+            self.opt.broadcast_params(0)
+        else:
+            self.opt = optimizer or FusedAdam(self.model.flat, self.model.grad, lr=cfg.lr, betas=(0.9, 0.95),
+                                              shadow=self.model.shadow)
+            if dp == "nccl":
+                import torch.distributed as dist
+
+                from ..parallel.dp import NcclGradSync
+
+                dist.broadcast(self.model.flat, src=0, group=group)
+                self.model.sync_shadow()
+                self.grad_sync = NcclGradSync(group)
+            elif dp != "none":
+                raise ValueError(f"unknown data-parallel mode {dp!r}")
         self.ref = self.model.frozen_copy()
-        self.opt = optimizer or FusedAdam(self.model.flat, self.model.grad, lr=cfg.lr, betas=(0.9, 0.95),
-                                          shadow=self.model.shadow)
-        self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17)
+        self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.rank)
         self.stats = torch.zeros(4, device=self.device)
         self.step_count = 0
         self.last_times = {}
@@ -92,7 +124,8 @@ class GRPOTrainer:
 
     # ------------------------------------------------------------------ helpers
     def _prompts(self) -> torch.Tensor:
-        g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count)
+        g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count +
+                                                            104729 * self.rank)
         return torch.randint(0, self.cfg.model.vocab, (self.cfg.num_prompts, self.cfg.prompt_len),
                              generator=g, device=self.device, dtype=torch.int32)
 
@@ -147,7 +180,10 @@ class GRPOTrainer:
         self.model.zero_grad()
         self.stats.zero_()
         self._train(seqs, ref_lp, adv)
-        self.opt.step()
+        if self.grad_sync is not None:
+            self.opt.step(grad_scale=self.grad_sync(self.model.grad))
+        else:
+            self.opt.step()  # the fused data-parallel step averages over ranks itself
         torch.cuda.synchronize(dev)
         t3 = time.perf_counter()
         self.step_count += 1
