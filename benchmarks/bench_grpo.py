@@ -24,6 +24,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1, help="data-parallel ranks (launch with torchrun for > 1)")
     ap.add_argument("--dp", choices=["fused", "nccl"], default="fused")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel rollout group size (training stays data parallel)")
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--prompts", type=int, default=64, help="prompts per rank")
@@ -55,7 +56,9 @@ def main():
     cfg = GRPOConfig(model=LMConfig.tiny() if a.tiny else LMConfig.qwen2_1p5b(), num_prompts=a.prompts,
                      group_size=a.group, prompt_len=a.prompt_len, response_len=a.response_len,
                      micro_batch=a.micro_batch)
-    tr = GRPOTrainer(cfg, str(dev), dp=dp)
+    if a.tp > 1 and (world < 2 or world % a.tp):
+        raise SystemExit("--tp needs a world size that is a multiple of it")
+    tr = GRPOTrainer(cfg, str(dev), dp=dp, tp=a.tp)
     for _ in range(a.warmup):
         tr.step()
     times, last = [], None
@@ -74,16 +77,18 @@ def main():
         times.append(ms.item() / 1e3)
     sec = sum(times) / len(times)
     if rank == 0:
-        out = {"metric": "GRPO train tokens/s", "value": world * cfg.batch * cfg.seq_len / sec, "unit": "tokens/s",
+        groups = world // a.tp  # each tensor-parallel group trains on its own prompts
+        out = {"metric": "GRPO train tokens/s", "value": groups * cfg.batch * cfg.seq_len / sec, "unit": "tokens/s",
                "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "s_per_step": sec,
                "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
                "data": "synthetic (random prompt ids, random-init weights)",
                "phases_s": {k: last[k] for k in ("rollout_s", "reward_ref_s", "train_s")},
-               "decode_tokens_per_s": world * cfg.batch * cfg.response_len / last["rollout_s"],
-               "config": {"model": "qwen2-1.5b-shape" if not a.tiny else "tiny", "prompts_per_gpu": cfg.num_prompts,
+               "decode_tokens_per_s": groups * cfg.batch * cfg.response_len / last["rollout_s"],
+               "config": {"model": "qwen2-1.5b-shape" if not a.tiny else "tiny", "prompts_per_group": cfg.num_prompts,
                           "group": cfg.group_size, "prompt_len": cfg.prompt_len, "response_len": cfg.response_len,
                           "micro_batch": cfg.micro_batch, "params": cfg.model.param_count(),
-                          "parallelism": f"dp{world}" + (f" ({dp})" if world > 1 else "")},
+                          "parallelism": (f"tp{a.tp}xdp{groups} rollout, dp{world} training" if a.tp > 1
+                                          else f"dp{world}") + (f" ({dp})" if world > 1 else "")},
                "timing": "CUDA events around each step, max over ranks",
                "reward_mean": last["reward_mean"], "kl": last["kl"],
                "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 2**30}

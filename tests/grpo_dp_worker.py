@@ -39,6 +39,22 @@ def main():
         del tr
     err = (finals["fused"] - finals["nccl"]).abs().max().item()
     assert err < 1e-5, err
+    # tensor-parallel rollout (tp = world) + data-parallel training
+    # (row shards of the fused kernels are multiples of 128: 256 sequences per group)
+    tcfg = GRPOConfig(model=LMConfig.tiny(), num_prompts=32, group_size=8, prompt_len=32, response_len=16,
+                      micro_batch=16, lr=1e-4)
+    tr = GRPOTrainer(tcfg, f"cuda:{local}", dp="fused", tp=world)
+    for _ in range(2):
+        st = tr.step()
+        assert st["tokens"] == tcfg.batch // world * tcfg.response_len
+    w = tr.model.flat.detach().clone()
+    ws = [torch.empty_like(w) for _ in range(world)]
+    dist.all_gather(ws, w)
+    assert all(torch.equal(x, ws[0]) for x in ws), "tp: weights differ across ranks"
+    # the rollout shard was re-sliced from the updated weights
+    assert torch.equal(tr.tpm.w["l0.wo"], tr.model.s["l0.wo"][:, rank * tr.tpm.q_dim:(rank + 1) * tr.tpm.q_dim])
+    tr.comm.check()
+    del tr
     if rank == 0:
         print("GRPO_DP_WORKER_OK", err)
     dist.barrier()

@@ -19,3 +19,14 @@ def test_tp_fused_kernels_two_gpus():
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "tp_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=500)
     assert r.returncode == 0 and "TP_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_tp_model_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29537",
+           os.path.join(HERE, "tp_llm_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=500)
+    assert r.returncode == 0 and "TP_LLM_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

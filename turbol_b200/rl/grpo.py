@@ -67,9 +67,18 @@ class GRPOTrainer:
     all-gather in one NVLink peer-memory kernel; the model's fp32 weights,
     gradient and bf16 copy live in symmetric memory); "nccl" (NCCL all-reduce
     of the gradient + local fused Adam; the baseline).  With data parallelism
-    ``cfg.num_prompts`` is per rank and every rank samples its own prompts."""
+    ``cfg.num_prompts`` is per rank and every rank samples its own prompts.
 
-    def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None, dp: str = "none", group=None):
+    tp > 1 (with dp over all ranks): the rollout runs tensor-parallel over
+    groups of ``tp`` consecutive ranks (TPDecoderLM + TPLLMGenerator on the
+    fused all-gather->GEMM / GEMM->reduce-scatter kernels); the ranks of a
+    group generate ``cfg.num_prompts`` prompts together and each trains on its
+    1/tp share of the group's sequences; after the optimizer step every rank
+    re-slices its rollout shard from the updated weights (the trainer ->
+    rollout weight sync)."""
+
+    def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None, dp: str = "none", group=None,
+                 tp: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dp, self.group = dp, group
@@ -100,7 +109,25 @@ class GRPOTrainer:
             elif dp != "none":
                 raise ValueError(f"unknown data-parallel mode {dp!r}")
         self.ref = self.model.frozen_copy()
-        self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.rank)
+        self.tp = tp
+        self.tp_rank, self.group_index = 0, self.rank
+        if tp > 1:
+            from ..models.tp_llm import TPDecoderLM
+            from ..parallel.dist import build_mesh
+            from ..parallel.tp import TensorParallelComm
+            from .rollout import TPLLMGenerator
+
+            if dp == "none":
+                raise ValueError("tensor-parallel rollout needs a process group (dp='fused' or 'nccl')")
+            mesh = build_mesh(self.world, self.rank, tp=tp)
+            self.tp_rank, self.group_index = mesh.tp_rank, self.rank // tp
+            rows = max(cfg.num_prompts * cfg.prompt_len, cfg.batch)
+            self.comm = TensorParallelComm(rows, cfg.model.hidden, cfg.model.hidden, group=mesh.tp_group,
+                                           device=self.device.index)
+            self.tpm = TPDecoderLM(self.model, self.comm)
+            self.gen = TPLLMGenerator(self.tpm, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.group_index)
+        else:
+            self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.rank)
         self.stats = torch.zeros(4, device=self.device)
         self.step_count = 0
         self.last_times = {}
@@ -125,7 +152,7 @@ class GRPOTrainer:
     # ------------------------------------------------------------------ helpers
     def _prompts(self) -> torch.Tensor:
         g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count +
-                                                            104729 * self.rank)
+                                                            104729 * self.group_index)
         return torch.randint(0, self.cfg.model.vocab, (self.cfg.num_prompts, self.cfg.prompt_len),
                              generator=g, device=self.device, dtype=torch.int32)
 
@@ -172,6 +199,10 @@ class GRPOTrainer:
         lens = torch.full((cfg.batch,), cfg.response_len, device=dev, dtype=torch.int32)
         rewards = o.hash_reward(resp, lens)
         adv = o.grpo_advantage(rewards, cfg.group_size, 1e-4, True)
+        if self.tp > 1:  # this rank trains on its share of the tensor-parallel group's sequences
+            share = cfg.batch // self.tp
+            lo = self.tp_rank * share
+            seqs, adv = seqs[lo:lo + share].contiguous(), adv[lo:lo + share].contiguous()
         # 3. reference log-probs
         ref_lp = self.ref_logprobs(seqs)
         torch.cuda.synchronize(dev)
@@ -184,6 +215,8 @@ class GRPOTrainer:
             self.opt.step(grad_scale=self.grad_sync(self.model.grad))
         else:
             self.opt.step()  # the fused data-parallel step averages over ranks itself
+        if self.tp > 1:
+            self.tpm.load_from(self.model)  # trainer -> rollout weight sync
         torch.cuda.synchronize(dev)
         t3 = time.perf_counter()
         self.step_count += 1
@@ -192,7 +225,7 @@ class GRPOTrainer:
         return {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()),
                 "pg_loss": st[0], "kl": st[1], "clipped_tokens": st[2], "tokens": st[3],
                 "rollout_logp_mean": float(roll_lp.mean()), **self.last_times,
-                "train_tokens": cfg.batch * cfg.seq_len}
+                "train_tokens": seqs.shape[0] * cfg.seq_len}
 
     def _train(self, seqs, ref_lp, adv):
         cfg = self.cfg
@@ -203,7 +236,8 @@ class GRPOTrainer:
         H = cfg.model.hidden
         pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
         mask = torch.ones(mb, Lr, device=self.device)
-        for s0 in range(0, cfg.batch, mb):
+        nb = seqs.shape[0]
+        for s0 in range(0, nb, mb):
             ids = seqs[s0:s0 + mb].contiguous()
             m = ids.shape[0]
             N = m * T
@@ -220,7 +254,7 @@ class GRPOTrainer:
             old = lp.detach().clone()                                   # behaviour policy == current
             dlp = torch.empty_like(lp)
             o.grpo_loss(lp.view(m, Lr), old.view(m, Lr), ref_lp[s0:s0 + m].contiguous(), adv[s0:s0 + m].contiguous(),
-                        mask[:m], dlp.view(m, Lr), self.stats, cfg.clip, cfg.kl_coef, 1.0 / cfg.batch)
+                        mask[:m], dlp.view(m, Lr), self.stats, cfg.clip, cfg.kl_coef, 1.0 / nb)
             o.logprob(logits, tgt, None, dlp)                          # logits <- d loss / d logits
             dhr = torch.empty(m * Lr, H, device=self.device, dtype=torch.bfloat16)
             o.gemm(logits, m_.head_weight(), dhr, False, True)          # d h = dLogits W_head

@@ -310,3 +310,161 @@ class RolloutEngine:
         out = seqs[:, L:].cpu().tolist()
         # random-init weights emit arbitrary bytes: decode leniently
         return [bytes(t for t in row if t < 256).decode("utf-8", errors="replace") for row in out]
+
+
+# ---------------------------------------------------------------------------
+class TPLLMGenerator(LLMGenerator):
+    """LLMGenerator over a tensor-parallel model (:class:`TPDecoderLM`).
+
+    Every rank holds the KV cache of its own KV heads for all sequences and
+    runs attention for its own heads; sequences are split by rows for the
+    embedding, the LM head and sampling (rank r samples sequences
+    [r*B/tp, (r+1)*B/tp)).  The projections are the fused all-gather -> GEMM
+    and GEMM -> reduce-scatter kernels, so the decode step (captured once as a
+    CUDA graph, replayed in lockstep on all ranks) contains no NCCL call.  The
+    sampled tokens are all-gathered once at the end."""
+
+    def __init__(self, model, max_batch: int, max_len: int, block_size: int = 16, seed: int = 0,
+                 cuda_graph: bool = True):
+        self.tpm = model
+        self.m = model.full
+        self.cfg = model.cfg
+        self.device = model.device
+        self.max_batch, self.max_len, self.bs = max_batch, max_len, block_size
+        self.seed = seed
+        self.cuda_graph = cuda_graph
+        self.blocks_per_seq = (max_len + block_size - 1) // block_size
+        self.num_blocks = max_batch * self.blocks_per_seq + 1
+        self.kv = _core().KVBlockManager(self.num_blocks, block_size)
+        shape = (self.num_blocks, model.hk, block_size, self.cfg.head_dim)
+        self.kc = [torch.empty(shape, device=self.device, dtype=torch.bfloat16) for _ in model.layers]
+        self.vc = [torch.empty(shape, device=self.device, dtype=torch.bfloat16) for _ in model.layers]
+        self._graph = None
+        self._graph_B = None
+        self.calls = 0
+
+    def _alloc_state(self, B: int, steps: int):
+        st = super()._alloc_state(B, steps)
+        tpm = self.tpm
+        b = B // tpm.tp
+        bf = dict(device=self.device, dtype=torch.bfloat16)
+        st.update({"x": torch.empty(b, self.cfg.hidden, **bf), "h": torch.empty(b, self.cfg.hidden, **bf),
+                   "tok": torch.zeros(b, device=self.device, dtype=torch.int32),
+                   "logits": torch.empty(b, self.cfg.vocab, **bf),
+                   "tok_mat": torch.zeros(b, steps, device=self.device, dtype=torch.int32),
+                   "lp_mat": torch.zeros(b, steps, device=self.device, dtype=torch.float32)})
+        return st
+
+    def _decode_step(self, B: int):
+        o = _ops()
+        cfg, tpm = self.cfg, self.tpm
+        st = self.state
+        D = cfg.head_dim
+        scale = 1.0 / math.sqrt(D)
+        o.embed_fwd(st["tok"], self.m.s["embed"], st["x"])
+        x = st["x"]
+        for li, i in enumerate(tpm.layers):
+            def attn_fn(qkv, out, li=li):
+                o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], out, tpm.hq, tpm.hk, D,
+                                   self.bs, scale)
+
+            def hook(i_, qkv, li=li):
+                o.kv_write(qkv, tpm.q_dim, tpm.q_dim + tpm.kv_dim, st["seq"], st["pos"], st["table"], self.kc[li],
+                           self.vc[li], tpm.hk, D, self.bs)
+
+            x = tpm.layer(i, x, st["pos"], B, 1, attn_fn, hook)
+        o.rmsnorm_fwd(x, self.m.f32["norm"], st["h"], None, cfg.rms_eps)
+        o.gemm(st["h"], self.m.head_weight(), st["logits"])
+        o.sample(st["logits"], 1.0, 0, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
+                 seed_t=st["seed_t"], temp_t=st["temp_t"])
+        st["pos"].add_(1)
+        st["ctx"].add_(1)
+        o.counter_add(st["step"], 1)
+
+    @torch.no_grad()
+    def generate(self, prompts: torch.Tensor, group: int = 1, max_new: int = 16, temperature: float = 1.0):
+        """Same contract as LLMGenerator.generate; every rank passes the same
+        prompts and receives the full sequences and log-probs."""
+        import torch.distributed as dist
+
+        o = _ops()
+        cfg, tpm = self.cfg, self.tpm
+        tp, r = tpm.tp, tpm.rank
+        P, Lp = prompts.shape
+        G = group
+        B = P * G
+        if B > self.max_batch or Lp + max_new > self.max_len:
+            raise ValueError("generate: batch or length beyond the engine's capacity")
+        if P % tp:
+            raise ValueError("generate: the prompt count must divide by the tensor-parallel size")
+        self.temperature = float(temperature)
+        self.calls += 1
+        table, pre_table, n_shared, tail = self._tables(P, G, Lp, max_new)
+        prompts = prompts.to(self.device, torch.int32).contiguous()
+        pos = torch.arange(Lp, device=self.device, dtype=torch.int32).repeat(P)
+        seq_of_tok = torch.arange(P, device=self.device, dtype=torch.int32).repeat_interleave(Lp)
+        kcs, vcs = self.kc, self.vc
+
+        def hook(i, qkv):
+            li = tpm.layers.index(i)
+            o.kv_write(qkv, tpm.q_dim, tpm.q_dim + tpm.kv_dim, seq_of_tok, pos, pre_table, kcs[li], vcs[li],
+                       tpm.hk, cfg.head_dim, self.bs)
+
+        x = tpm.embed_rows(prompts.reshape(-1))
+        x = tpm.forward(x, P, Lp, pos, kv_hook=hook)
+        p_loc = P // tp
+        last = x.view(p_loc, Lp, -1)[:, -1, :].contiguous()  # this rank's prompts' last positions
+        if tail:
+            src_blocks = pre_table[:, n_shared].long()
+            dst_blocks = table[:, n_shared].long()
+            for li in range(len(tpm.layers)):
+                kcs[li][dst_blocks] = kcs[li][src_blocks.repeat_interleave(G)]
+                vcs[li][dst_blocks] = vcs[li][src_blocks.repeat_interleave(G)]
+        if self._graph is None or self._graph_B != (B, max_new):
+            self.state = self._alloc_state(B, max_new)
+            self._graph = None
+        st = self.state
+        st["table"].copy_(table)
+        h = torch.empty(p_loc, cfg.hidden, device=self.device, dtype=torch.bfloat16)
+        o.rmsnorm_fwd(last, self.m.f32["norm"], h, None, cfg.rms_eps)
+        hB = h.repeat_interleave(G, 0).contiguous()
+        o.gemm(hB, self.m.head_weight(), st["logits"])
+        st["step"].zero_()
+        # per-rank sampling streams: rank r samples different sequences
+        st["seed_t"].fill_(self.seed + 7919 * self.calls + 104729 * r)
+        st["temp_t"].fill_(self.temperature)
+        o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls + 104729 * r + 1, st["step"], 0,
+                 st["tok"], None, st["tok_mat"], st["lp_mat"])
+        o.counter_add(st["step"], 1)
+        st["pos"].fill_(Lp)
+        st["ctx"].fill_(Lp + 1)
+        steps = max_new - 1
+        if steps > 0:
+            if self.cuda_graph:
+                if self._graph is None:
+                    saved = {k: v.clone() for k, v in st.items() if k in ("tok", "pos", "ctx", "step")}
+                    s = torch.cuda.Stream(device=self.device)
+                    s.wait_stream(torch.cuda.current_stream(self.device))
+                    with torch.cuda.stream(s):
+                        self._decode_step(B)
+                    torch.cuda.current_stream(self.device).wait_stream(s)
+                    for k, v in saved.items():
+                        st[k].copy_(v)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        self._decode_step(B)
+                    for k, v in saved.items():
+                        st[k].copy_(v)
+                    self._graph, self._graph_B = g, (B, max_new)
+                for _ in range(steps):
+                    self._graph.replay()
+            else:
+                for _ in range(steps):
+                    self._decode_step(B)
+        group_pg = getattr(tpm.comm, "group", None)
+        tok_all = torch.empty(B, max_new, device=self.device, dtype=torch.int32)
+        lp_all = torch.empty(B, max_new, device=self.device, dtype=torch.float32)
+        dist.all_gather_into_tensor(tok_all, st["tok_mat"], group=group_pg)
+        dist.all_gather_into_tensor(lp_all, st["lp_mat"], group=group_pg)
+        seqs = torch.cat([prompts.repeat_interleave(G, 0), tok_all], 1)
+        return seqs, lp_all
