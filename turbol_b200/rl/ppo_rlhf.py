@@ -1,0 +1,273 @@
+"""PPO-RLHF on a pipeline-parallel decoder policy with a value head.
+
+One step (every rank is one pipeline stage of the trainer and also holds a
+bf16 rollout copy of the whole policy):
+
+  1. weight sync   each stage broadcasts its bf16 weights into every rank's
+                   rollout copy (NCCL broadcast per tensor);
+  2. rollout       each rank samples responses for its share of the prompts
+                   with its own paged-KV decode loop; the sequences are
+                   all-gathered;
+  3. scoring       a forward-only pipeline pass of the policy gives the
+                   behaviour log-probs and values of the response tokens; one
+                   of the frozen reference policy gives reference log-probs;
+                   the last stage forms per-token rewards (KL penalty
+                   -beta * (logp - logp_ref), plus the sequence reward
+                   (hash(response) mod 1000) / 1000 on the last token) and
+                   GAE(gamma, lambda) advantages (the GAE kernel), whitened;
+  4. update        one 1F1B pipeline pass (NCCL send/recv between stages)
+                   with the clipped PPO policy loss and the clipped value loss
+                   on the last stage; Adam on every stage.
+
+The reference has no RLHF trainer or pipeline execution
+(turbol_vllm/src/distributed/pipeline_trainer.cpp:67-113 is a serial stub).
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from .._native import ops as _ops
+from ..models.llm import DecoderLM, LMConfig
+from ..ops.rl import gae
+from ..parallel import pipeline as pp
+from .rollout import LLMGenerator
+
+
+@dataclass
+class RLHFConfig:
+    model: LMConfig = field(default_factory=LMConfig.llama3_8b)
+    num_prompts: int = 32       # sequences per step (the whole pipeline)
+    prompt_len: int = 512
+    response_len: int = 1024
+    micro_batch: int = 4        # sequences per pipeline micro-batch
+    lr: float = 1e-6
+    clip: float = 0.2
+    vclip: float = 0.2
+    vf_coef: float = 0.1
+    kl_coef: float = 0.05
+    gamma: float = 1.0
+    lam: float = 0.95
+    temperature: float = 1.0
+    seed: int = 0
+
+    @property
+    def seq_len(self) -> int:
+        return self.prompt_len + self.response_len
+
+
+class _Frozen:
+    """Forward-only stand-in for a pipeline stage (the reference policy)."""
+
+    def __init__(self, stage: pp.PipelineStage):
+        self.model = stage.model.frozen_copy()
+        self.cfg, self.device = stage.cfg, stage.device
+        self.stage, self.num_stages = stage.stage, stage.num_stages
+        self.first, self.last = stage.first, stage.last
+
+
+class PPORLHFTrainer:
+    def __init__(self, cfg: RLHFConfig, device, group=None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.ranks = list(range(self.world)) if group is None else dist.get_process_group_ranks(group)
+        if cfg.num_prompts % cfg.micro_batch or cfg.num_prompts % self.world:
+            raise ValueError("num_prompts must divide by micro_batch and by the pipeline size")
+        self.stage = pp.PipelineStage(cfg.model, self.rank, self.world, self.device, seed=cfg.seed, value_head=True,
+                                      lr=cfg.lr)
+        # a tied embedding lives on the first and the last stage: same initial
+        # weights, and the two gradients are summed after every backward pass
+        self.tied = cfg.model.tie_embeddings and self.world > 1
+        self.embed_group = dist.new_group([self.ranks[0], self.ranks[-1]]) if self.tied else None
+        if self.tied and (self.stage.first or self.stage.last):
+            dist.broadcast(self.stage.model.p["embed"], src=self.ranks[0], group=self.embed_group)
+            self.stage.model.sync_shadow()
+        self.ref = _Frozen(self.stage)
+        # bf16 rollout copy of the whole policy on every rank
+        self.rollout = DecoderLM(cfg.model, self.device, seed=cfg.seed, master=False)
+        self.gen = LLMGenerator(self.rollout, cfg.num_prompts // self.world, cfg.seq_len,
+                                seed=cfg.seed + 31 + 7919 * self.rank)
+        self.step_count = 0
+        self.sync_weights()
+
+    # ------------------------------------------------------------ weight sync
+    @torch.no_grad()
+    def sync_weights(self):
+        """Every stage's bf16 weights -> every rank's rollout copy."""
+        for src in range(self.world):
+            for name in self._stage_names(src):
+                t = self.rollout.s[name]
+                if src == self.rank:
+                    t.copy_(self.stage.model.s[name])
+                dist.broadcast(t, src=self.ranks[src], group=self.group)
+        # fp32 norm weights / biases in place: the captured decode graph keeps their addresses
+        for n, t in self.rollout.f32.items():
+            t.copy_(self.rollout.s[n].float())
+
+    def _stage_names(self, s: int):
+        cfg = self.cfg.model
+        names = []
+        if s == 0:
+            names.append("embed")
+        for i in pp.stage_layers(cfg.n_layers, self.world, s):
+            names += [n for n in self.rollout.offsets if n.startswith(f"l{i}.")]
+        if s == self.world - 1:
+            names.append("norm")
+            if not cfg.tie_embeddings:
+                names.append("lm_head")
+        return names
+
+    # ------------------------------------------------------------ helpers
+    def _resp_rows(self, m: int) -> torch.Tensor:
+        T, Lp, Lr = self.cfg.seq_len, self.cfg.prompt_len, self.cfg.response_len
+        base = torch.arange(m, device=self.device) * T
+        return (base[:, None] + torch.arange(Lp - 1, Lp - 1 + Lr, device=self.device)[None, :]).reshape(-1)
+
+    def _head(self, model: DecoderLM, x_out: torch.Tensor, m: int, ids: torch.Tensor):
+        """Final norm, response-row logits and log-probs of the target tokens."""
+        o = _ops()
+        N = x_out.shape[0]
+        rstd = torch.empty(N, device=self.device)
+        hf = model.final_norm(x_out, rstd)
+        rows = self._resp_rows(m)
+        hr = hf.index_select(0, rows)
+        logits = model.logits(hr)
+        tgt = ids[:, self.cfg.prompt_len:].reshape(-1).contiguous()
+        lp = torch.empty(m * self.cfg.response_len, device=self.device)
+        o.logprob(logits, tgt, lp)
+        return hf, rstd, rows, hr, logits, tgt, lp
+
+    def _pass(self, stage, seqs: torch.Tensor, train: bool, on_last):
+        cfg = self.cfg
+        mb, T = cfg.micro_batch, cfg.seq_len
+        M = seqs.shape[0] // mb
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
+        pp.set_micro_geometry(mb, T, pos)
+
+        def first(i):
+            return stage.model.embed(seqs[i * mb:(i + 1) * mb])
+
+        def back_first(i, dx):
+            stage.model.embed_backward(seqs[i * mb:(i + 1) * mb], dx)
+
+        pp.run_1f1b(stage, self.ranks, M, mb * T, first, on_last, back_first, group=self.group,
+                    forward_only=not train)
+
+    # ------------------------------------------------------------ step
+    def step(self) -> dict:
+        cfg = self.cfg
+        o = _ops()
+        dev = self.device
+        B, Lr = cfg.num_prompts, cfg.response_len
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        # 1. weight sync (after the previous update)
+        if self.step_count > 0:
+            self.sync_weights()
+        torch.cuda.synchronize(dev)
+        t_sync = time.perf_counter()
+        # 2. rollout
+        g = torch.Generator(device=dev).manual_seed(cfg.seed * 1000003 + self.step_count * 131 + self.rank)
+        prompts = torch.randint(0, cfg.model.vocab, (B // self.world, cfg.prompt_len), generator=g, device=dev,
+                                dtype=torch.int32)
+        seqs_local, _ = self.gen.generate(prompts, 1, Lr, cfg.temperature)
+        seqs = torch.empty(B, cfg.seq_len, device=dev, dtype=torch.int32)
+        dist.all_gather_into_tensor(seqs, seqs_local.contiguous(), group=self.group)
+        torch.cuda.synchronize(dev)
+        t_roll = time.perf_counter()
+        # 3. behaviour log-probs / values, reference log-probs, rewards, advantages
+        mb = cfg.micro_batch
+        old_lp = torch.zeros(B, Lr, device=dev)
+        old_v = torch.zeros(B, Lr, device=dev)
+        ref_lp = torch.zeros(B, Lr, device=dev)
+        st = self.stage
+
+        def score_policy(i, x_out):
+            ids = seqs[i * mb:(i + 1) * mb]
+            hf, _, rows, hr, logits, tgt, lp = self._head(st.model, x_out, mb, ids)
+            old_lp[i * mb:(i + 1) * mb] = lp.view(mb, Lr)
+            old_v[i * mb:(i + 1) * mb] = st.values(hr).view(mb, Lr)
+
+        def score_ref(i, x_out):
+            ids = seqs[i * mb:(i + 1) * mb]
+            *_, lp = self._head(self.ref.model, x_out, mb, ids)
+            ref_lp[i * mb:(i + 1) * mb] = lp.view(mb, Lr)
+
+        with torch.no_grad():
+            self._pass(st, seqs, False, score_policy)
+            self._pass(self.ref, seqs, False, score_ref)
+        adv = ret = None
+        seq_reward = None
+        if st.last:
+            resp = seqs[:, cfg.prompt_len:].contiguous()
+            seq_reward = o.hash_reward(resp, torch.full((B,), Lr, device=dev, dtype=torch.int32))
+            r = -cfg.kl_coef * (old_lp - ref_lp)
+            r[:, -1] += seq_reward
+            vals = torch.cat([old_v.t(), torch.zeros(1, B, device=dev)], 0).contiguous()  # [Lr + 1, B]
+            a_t, ret_t = gae(r.t().contiguous(), vals, torch.zeros(Lr, B, device=dev, dtype=torch.uint8),
+                             cfg.gamma, cfg.lam)
+            adv, ret = a_t.t().contiguous(), ret_t.t().contiguous()
+            adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        torch.cuda.synchronize(dev)
+        t_score = time.perf_counter()
+        # 4. PPO update through the pipeline (1F1B)
+        st.zero_grad()
+        stats = torch.zeros(4, device=dev)
+        norm = 1.0 / (B * Lr)
+
+        def loss_last(i, x_out):
+            sl = slice(i * mb, (i + 1) * mb)
+            ids = seqs[sl]
+            hf, rstd, rows, hr, logits, tgt, lp = self._head(st.model, x_out, mb, ids)
+            v = st.values(hr)
+            lp_t = lp.view(mb, Lr).detach().requires_grad_()
+            v_t = v.view(mb, Lr).detach().requires_grad_()
+            with torch.enable_grad():
+                ratio = torch.exp(lp_t - old_lp[sl])
+                A = adv[sl]
+                pg = -torch.min(ratio * A, torch.clamp(ratio, 1 - cfg.clip, 1 + cfg.clip) * A)
+                v_clip = old_v[sl] + torch.clamp(v_t - old_v[sl], -cfg.vclip, cfg.vclip)
+                vf = 0.5 * torch.max((v_t - ret[sl]) ** 2, (v_clip - ret[sl]) ** 2)
+                loss = (pg.sum() + cfg.vf_coef * vf.sum()) * norm
+                loss.backward()
+            stats[0] += pg.detach().sum() * norm
+            stats[1] += vf.detach().sum() * norm
+            stats[2] += ((ratio.detach() - 1).abs() > cfg.clip).float().sum()
+            stats[3] += mb * Lr
+            H = cfg.model.hidden
+            o.logprob(logits, tgt, None, lp_t.grad.reshape(-1).contiguous())       # logits <- d loss / d logits
+            dhr = torch.empty(mb * Lr, H, device=dev, dtype=torch.bfloat16)
+            o.gemm(logits, st.model.head_weight(), dhr, False, True)              # d h = dLogits W_head
+            o.gemm(logits, hr, st.model.head_grad(), True, True, accumulate=True, split_k=1)
+            st.values_backward(hr, v_t.grad.reshape(-1), dhr)
+            dhf = torch.zeros(mb * cfg.seq_len, H, device=dev, dtype=torch.bfloat16)
+            dhf.index_copy_(0, rows, dhr)
+            dx = torch.empty_like(x_out)
+            o.rmsnorm_bwd(dhf, x_out, st.model.f32["norm"], rstd, dx, None, st.model.g["norm"])
+            return dx
+
+        self._pass(st, seqs, True, loss_last)
+        if self.tied and (st.first or st.last):
+            dist.all_reduce(st.model.g["embed"], group=self.embed_group)
+        st.step()
+        torch.cuda.synchronize(dev)
+        t_end = time.perf_counter()
+        self.step_count += 1
+        out = {"sync_s": t_sync - t0, "rollout_s": t_roll - t_sync, "score_s": t_score - t_roll,
+               "train_s": t_end - t_score, "step_s": t_end - t0, "train_tokens": B * cfg.seq_len}
+        # the last stage owns the losses and rewards: share them
+        vec = torch.zeros(6, device=dev)
+        if st.last:
+            vec[:4] = stats
+            vec[4] = seq_reward.mean()
+            vec[5] = (old_lp - ref_lp).mean()
+        dist.broadcast(vec, src=self.ranks[-1], group=self.group)
+        v = vec.tolist()
+        out.update({"pg_loss": v[0], "vf_loss": v[1], "clipfrac": v[2] / max(v[3], 1.0), "reward_mean": v[4],
+                    "kl": v[5]})
+        return out
