@@ -98,23 +98,28 @@ class LLMGenerator:
         x = st["x"]
         o.embed_fwd(st["tok"], m.s["embed"], x)
         h, qkv, attn, x2, act = st["h"], st["qkv"], st["attn"], st["x2"], st["act"]
+        # few sequences: the projections have few output tiles and long K, so
+        # split K over the SMs (partials in this workspace); many sequences:
+        # the narrow-tile plan without splitting is faster
+        ws = st.get("ws")
+        kw = {"workspace": ws} if ws is not None else {}
         scale = 1.0 / math.sqrt(D)
         for li, i in enumerate(m.layers):
             P = f"l{i}."
             o.rmsnorm_fwd(x, m.f32[P + "ln1"], h, None, cfg.rms_eps)
             if cfg.qkv_bias:
-                o.gemm(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS)
+                o.gemm(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS, **kw)
             else:
-                o.gemm(h, m.s[P + "wqkv"], qkv)
+                o.gemm(h, m.s[P + "wqkv"], qkv, **kw)
             o.rope(qkv, st["pos"], m.table, cfg.n_heads + cfg.n_kv_heads, D)
             o.kv_write(qkv, cfg.q_dim, cfg.q_dim + cfg.kv_dim, st["seq"], st["pos"], st["table"], self.kc[li],
                        self.vc[li], cfg.n_kv_heads, D, self.bs)
             o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], attn, cfg.n_heads,
                                cfg.n_kv_heads, D, self.bs, scale)
-            o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL)
+            o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL, **kw)
             o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
             o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
-            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
+            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
         o.sample(st["logits"], 1.0, 0, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
@@ -144,7 +149,16 @@ class LLMGenerator:
             # captured decode step serves every generate call
             "seed_t": torch.zeros(1, device=dev, dtype=torch.int64),
             "temp_t": torch.ones(1, device=dev, dtype=torch.float32),
+            **self._split_workspace(B),
         }
+
+    def _split_workspace(self, B: int) -> dict:
+        if B > 64:
+            return {}
+        o, cfg = _ops(), self.cfg
+        n = max(o.gemm_workspace_numel(B, cfg.qkv_dim, cfg.hidden), o.gemm_workspace_numel(B, cfg.hidden, cfg.q_dim),
+                o.gemm_workspace_numel(B, cfg.hidden, cfg.ffn), 1)
+        return {"ws": torch.zeros(n, device=self.device)}
 
     # ------------------------------------------------------------ generate
     @torch.no_grad()
