@@ -317,6 +317,37 @@ void register_kernel_ops(py::module_& m) {
             "colsum_bf16");
   }, py::arg("x"), py::arg("out"), py::arg("accumulate") = false);
 
+  m.def("dense_k8_fwd", [](at::Tensor x, at::Tensor W, py::object bias, at::Tensor y, bool tanh_act) {
+    TB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(1) == 8 && x.stride(1) == 1,
+             "dense_k8_fwd: x bf16 [M, 8]");
+    TB_CHECK(W.scalar_type() == at::kBFloat16 && W.is_contiguous() && W.dim() == 2 && W.size(1) == 8,
+             "dense_k8_fwd: W bf16 [N, 8] contiguous");
+    TB_CHECK(y.scalar_type() == at::kBFloat16 && y.dim() == 2 && y.size(0) == x.size(0) && y.size(1) == W.size(0) &&
+                 y.stride(1) == 1, "dense_k8_fwd: y bf16 [M, N]");
+    const float* bp = nullptr;
+    at::Tensor bt;
+    if (!bias.is_none()) {
+      bt = bias.cast<at::Tensor>();
+      need(bt, at::kFloat, "bias");
+      bp = bt.data_ptr<float>();
+    }
+    cuda_ok(tb_dense_k8_fwd(x.data_ptr(), x.stride(0), W.data_ptr(), bp, y.data_ptr(), y.stride(0),
+                            static_cast<int>(x.size(0)), static_cast<int>(W.size(0)), tanh_act ? 1 : 0, stream_of(x)),
+            "dense_k8_fwd");
+  }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true);
+  m.def("dense_k8_wgrad", [](at::Tensor dz, at::Tensor x, at::Tensor dW, bool accumulate) {
+    TB_CHECK(dz.is_cuda() && dz.scalar_type() == at::kBFloat16 && dz.dim() == 2 && dz.stride(1) == 1,
+             "dense_k8_wgrad: dz bf16 [M, N]");
+    TB_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(1) == 8 && x.size(0) == dz.size(0) &&
+                 x.stride(1) == 1, "dense_k8_wgrad: x bf16 [M, 8]");
+    need(dW, at::kFloat, "dW");
+    TB_CHECK(dW.numel() == dz.size(1) * 8, "dense_k8_wgrad: dW fp32 [N, 8]");
+    cuda_ok(tb_dense_k8_wgrad(dz.data_ptr(), dz.stride(0), x.data_ptr(), x.stride(0), dW.data_ptr<float>(),
+                              static_cast<int>(dz.size(0)), static_cast<int>(dz.size(1)), accumulate ? 1 : 0,
+                              stream_of(dz)),
+            "dense_k8_wgrad");
+  }, py::arg("dz"), py::arg("x"), py::arg("dW"), py::arg("accumulate") = false);
+
   m.def("ppo_loss",
         [](at::Tensor logits, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv, at::Tensor ret,
            py::object old_val, at::Tensor dlogits, at::Tensor dvalue, py::object stats, float clip, float vclip,

@@ -493,7 +493,9 @@ __device__ __forceinline__ long long push_worker_of(long long i, long long nw, l
 // TP = 0: plain GEMM.  TP = 1: all-gather -> GEMM (rows of A are sharded over
 // the ranks; remote shards arrive by peer stores into local staging).  TP = 2:
 // GEMM -> reduce-scatter (each output tile is stored into the receive slot of
-// the rank that owns its rows; tp_rs_finish_kernel sums the slots).
+// the rank that owns its rows; tp_rs_finish_kernel sums the slots).  TP = 3:
+// split-K with the in-kernel fix-up (a separate instantiation keeps that code
+// out of the other variants' epilogue).
 template <int BN, bool A_MN, bool B_MN, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -512,17 +514,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total = p.m_tiles * p.n_tiles * p.splits;
-  if (TP != 0 && p.tp.trace && threadIdx.x == 0) p.tp.trace[blockIdx.x * 8 + 0] = global_ns();
-  const unsigned epoch = TP ? *p.tp.epoch_ctr + 1u : 0u;
+  constexpr bool kTp = TP == 1 || TP == 2;  // a tensor-parallel collective variant
+  if (kTp && p.tp.trace && threadIdx.x == 0) p.tp.trace[blockIdx.x * 8 + 0] = global_ns();
+  const unsigned epoch = kTp ? *p.tp.epoch_ctr + 1u : 0u;
   const unsigned parity = epoch & 1u;
-  const int mloc = TP ? p.tp.rows_per_rank : 0;
+  const int mloc = kTp ? p.tp.rows_per_rank : 0;
   // all-gather: start with this rank's own row tiles while the remote shards arrive
   // all-gather: own rows first (they need no transfer); reduce-scatter: the
   // next rank's rows first, own rows last, so the peer stores of the first
   // wave of tiles overlap the MMAs of the later ones
   const int first_mt = TP == 1 ? (p.tp.rank * mloc) / BM
                        : TP == 2 ? (((p.tp.rank + 1) % p.tp.world) * mloc) / BM : 0;
-  auto tile_m0 = [&](int m0) { return TP != 0 ? ((m0 / BM + first_mt) % p.m_tiles) * BM : m0; };
+  auto tile_m0 = [&](int m0) { return kTp ? ((m0 / BM + first_mt) % p.m_tiles) * BM : m0; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::kStages; ++s) {
@@ -793,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc = 0;
         acc_phase ^= 1;
       }
-      if (p.slot_cnt != nullptr) {
+      if constexpr (TP == 3) {
         // In-kernel split-K fix-up, per warp slice (32 rows x BN/2 columns):
         // publish this split's partial, count arrivals, and let the last of
         // the `splits` warps that own the slice sum every partial (in split
@@ -816,7 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (TP == 2 && warp >= 4) __threadfence_system();  // this thread's peer stores, before the arrival below
-  if (TP != 0 && p.tp.trace && threadIdx.x == 128) p.tp.trace[blockIdx.x * 8 + 5] = global_ns();
+  if (kTp && p.tp.trace && threadIdx.x == 128) p.tp.trace[blockIdx.x * 8 + 5] = global_ns();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1194,11 +1197,17 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   const int grid = total < num_sms() ? total : num_sms();
   const int am = a->a_mn ? 1 : 0, bm = a->b_mn ? 1 : 0;
   int err = 0;
-#define TB_GEMM_DISPATCH(BNV)                                                          \
-  if (!am && !bm) err = launch<BNV, false, false>(ta, tbm, p, grid, stream);           \
-  else if (!am && bm) err = launch<BNV, false, true>(ta, tbm, p, grid, stream);        \
-  else if (am && !bm) err = launch<BNV, true, false>(ta, tbm, p, grid, stream);        \
-  else err = launch<BNV, true, true>(ta, tbm, p, grid, stream);
+#define TB_GEMM_DISPATCH2(BNV, MODE)                                                   \
+  if (!am && !bm) err = launch<BNV, false, false, MODE>(ta, tbm, p, grid, stream);     \
+  else if (!am && bm) err = launch<BNV, false, true, MODE>(ta, tbm, p, grid, stream);  \
+  else if (am && !bm) err = launch<BNV, true, false, MODE>(ta, tbm, p, grid, stream);  \
+  else err = launch<BNV, true, true, MODE>(ta, tbm, p, grid, stream);
+#define TB_GEMM_DISPATCH(BNV)              \
+  if (fixup) {                             \
+    TB_GEMM_DISPATCH2(BNV, 3)              \
+  } else {                                 \
+    TB_GEMM_DISPATCH2(BNV, 0)              \
+  }
   if (BN == 256) {
     TB_GEMM_DISPATCH(256)
   } else if (BN == 128) {
@@ -1207,6 +1216,7 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
     TB_GEMM_DISPATCH(64)
   }
 #undef TB_GEMM_DISPATCH
+#undef TB_GEMM_DISPATCH2
   if (err != 0 || !use_ws || fixup) return err;
   DevArgs r = p;
   r.colsum = a->colsum;

@@ -78,6 +78,13 @@ int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, 
                        float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
                        float* db_val, cudaStream_t s);
 int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, int accumulate, cudaStream_t s);
+// First MLP layer with 8 (padded) input features: y = act(x . W^T + b), act 0
+// none / 1 tanh; x bf16 [M, 8], W bf16 [N, 8] (N % 8 == 0, N <= 1024), y bf16.
+int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
+                    int N, int act, cudaStream_t s);
+// dW[N, 8] (fp32) = (or += with accumulate) dz[M, N]^T . x[M, 8] (bf16 inputs).
+int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
+                      int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,
                 const float* adv, const float* ret, const float* old_val, float* dlogits, float* dvalue, float* stats,
                 int B, float clip, float vclip, float vf_coef, float ent_coef, cudaStream_t s);

@@ -305,6 +305,111 @@ __global__ void colsum_bf16_kernel(const __nv_bfloat16* __restrict__ x, long lon
 
 __global__ void counter_add_kernel(long long* c, long long v) { *c += v; }
 
+// ---------------------------------------------------------------- small-K dense layer
+// y[M, N] = act(x[M, 8] . W[N, 8]^T + b) for the first layer of an MLP whose
+// input has at most 8 features (bf16 in, fp32 accumulation, bf16 out).  A
+// tensor-core tile would be 87% zero padding in K and bound by its epilogue.
+// Here a thread owns 4 output columns: their 32 weights and 4 biases live in
+// registers (few registers: many resident warps to hide the load latency), and
+// it walks a chunk of rows, 4 rows in flight; the lanes of a warp share each
+// row's 16-byte input (one broadcast load) and write 32 neighbouring 8-byte
+// column groups (256 contiguous bytes).
+constexpr int kDenseCols = 4;  // output columns per thread (W slice in 32 registers)
+__global__ void __launch_bounds__(256) dense_k8_fwd_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                           const __nv_bfloat16* __restrict__ W,
+                                                           const float* __restrict__ bias,
+                                                           __nv_bfloat16* __restrict__ y, long long ldy, int M, int N,
+                                                           int act, int rows_per_block) {
+  constexpr int C = kDenseCols;
+  const int groups = N / C;
+  const int g = threadIdx.x % groups;           // column group of this thread
+  const int rsub = threadIdx.x / groups;        // row offset within a block step
+  const int rstep = blockDim.x / groups;
+  if (rsub >= rstep) return;
+  float w[C][8], b[C];
+#pragma unroll
+  for (int j = 0; j < C; ++j) {
+    const uint4 u = *reinterpret_cast<const uint4*>(W + (g * C + j) * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      w[j][2 * k] = f.x;
+      w[j][2 * k + 1] = f.y;
+    }
+    b[j] = bias ? bias[g * C + j] : 0.f;
+  }
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(M, r0 + rows_per_block);
+  constexpr int kR = 4;  // rows in flight per thread
+  for (int rb = r0 + rsub; rb < r1; rb += kR * rstep) {
+    uint4 xu[kR];
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      const int r = rb + q * rstep;
+      xu[q] = r < r1 ? *reinterpret_cast<const uint4*>(x + r * ldx) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < kR; ++q) {
+      const int r = rb + q * rstep;
+      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&xu[q]);
+      float xv[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(xh[k]);
+        xv[2 * k] = f.x;
+        xv[2 * k + 1] = f.y;
+      }
+      float o[C];
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        float acc = b[j];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(xv[k], w[j][k], acc);
+        if (act == 1) {
+          float t;
+          asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(acc));
+          acc = t;
+        }
+        o[j] = acc;
+      }
+      uint2 ou;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ou);
+      oh[0] = __floats2bfloat162_rn(o[0], o[1]);
+      oh[1] = __floats2bfloat162_rn(o[2], o[3]);
+      if (r < r1) *reinterpret_cast<uint2*>(y + r * ldy + g * C) = ou;
+    }
+  }
+}
+
+// dW[N, 8] += dz[M, N]^T . x[M, 8]: thread = one output column j over a chunk
+// of rows (coalesced dz reads, x rows broadcast), 8 partial sums reduced with
+// one atomic each per thread.
+constexpr int kWgRows = 256;
+__global__ void __launch_bounds__(256) dense_k8_wgrad_kernel(const __nv_bfloat16* __restrict__ dz, long long ldz,
+                                                             const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                             float* __restrict__ dW, int M, int N) {
+  __shared__ float sx[kWgRows][8];
+  const int r0 = blockIdx.y * kWgRows;
+  const int nr = min(kWgRows, M - r0);
+  for (int i = threadIdx.x; i < nr * 8; i += blockDim.x) {
+    const int r = i / 8, k = i % 8;
+    sx[r][k] = __bfloat162float(x[(r0 + r) * ldx + k]);
+  }
+  __syncthreads();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= N) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const __nv_bfloat16* col = dz + static_cast<long long>(r0) * ldz + j;
+  for (int r = 0; r < nr; ++r) {
+    const float d = __bfloat162float(col[static_cast<long long>(r) * ldz]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = fmaf(d, sx[r][k], acc[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) atomicAdd(dW + j * 8 + k, acc[k]);
+}
+
 }  // namespace
 
 extern "C" {
@@ -392,6 +497,35 @@ int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, 
 
 int tb_counter_add(long long* counter, long long v, cudaStream_t s) {
   counter_add_kernel<<<1, 1, 0, s>>>(counter, v);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
+                    int N, int act, cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (N % 8 || N > 1024 || ldx % 8 || ldy % 8 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(y) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  // one thread per column group (N / 4 <= 256 threads), as many row lanes as fit in 256 threads
+  const int groups = N / kDenseCols;
+  if (groups > 256) return static_cast<int>(cudaErrorInvalidValue);
+  const int rstep = 256 / groups;
+  int rows = 32;
+  while (rows > rstep && (static_cast<long long>(M) + rows - 1) / rows < 4 * 148) rows /= 2;
+  const unsigned grid = static_cast<unsigned>((M + rows - 1) / rows);
+  dense_k8_fwd_kernel<<<grid, rstep * groups, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx,
+                                                      static_cast<const __nv_bfloat16*>(W), bias,
+                                                      static_cast<__nv_bfloat16*>(y), ldy, M, N, act, rows);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
+                      int accumulate, cudaStream_t s) {
+  if (!accumulate) cudaMemsetAsync(dW, 0, sizeof(float) * 8 * static_cast<size_t>(N), s);
+  if (M <= 0) return 0;
+  dim3 grid((N + 255) / 256, (M + kWgRows - 1) / kWgRows);
+  dense_k8_wgrad_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(dz), ldz,
+                                             static_cast<const __nv_bfloat16*>(x), ldx, dW, M, N);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -47,3 +47,26 @@ def test_fused_mlp_matches_autograd(H, B, dev):
     # padding stays untouched by the gradients
     assert float(net.g["w1"][:, 4:].abs().max()) == 0.0
     assert float(net.g["w3a"][2:].abs().max()) == 0.0
+
+
+def test_dense_k8_kernels(dev):
+    from turbol_b200._native import ops
+    o = ops()
+    g = torch.Generator().manual_seed(4)
+    M, N = 5000, 512
+    x = torch.zeros(M, 8)
+    x[:, :4] = torch.randn(M, 4, generator=g)
+    x = x.to(dev, torch.bfloat16)
+    W = (torch.randn(N, 8, generator=g) * 0.5).to(dev, torch.bfloat16)
+    b = torch.randn(N, generator=g).to(dev)
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    o.dense_k8_fwd(x, W, b, y, True)
+    ref = torch.tanh(x.float() @ W.float().t() + b)
+    assert (y.float() - ref).abs().max().item() < 1e-2
+    dz = torch.randn(M, N, generator=g).to(dev, torch.bfloat16)
+    dW = torch.full((N, 8), 7.0, device=dev)
+    o.dense_k8_wgrad(dz, x, dW)
+    exp = dz.float().t() @ x.float()
+    assert torch.allclose(dW, exp, atol=1e-2, rtol=1e-3)
+    o.dense_k8_wgrad(dz, x, dW, True)
+    assert torch.allclose(dW, 2 * exp, atol=2e-2, rtol=1e-3)

@@ -154,7 +154,7 @@ class FusedActorCritic:
         S, P = self.s, self.p
         H = self.H
         h1 = ws["h1"]
-        o.gemm(x_bf16, S["w1"], h1, bias=P["b1"], epi=o.EPI_BIAS_TANH)
+        o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], h1, True)                 # 8 input features: CUDA cores
         o.gemm(h1[:, :H], S["w2a"], ws["h2a"], bias=P["b2a"], epi=o.EPI_BIAS_TANH)
         o.gemm(h1[:, H:], S["w2c"], ws["h2c"], bias=P["b2c"], epi=o.EPI_BIAS_TANH)
         o.gemm(ws["h2a"], S["w3a"], ws["logits"], bias=P["b3a"], epi=o.EPI_BIAS)
