@@ -30,6 +30,14 @@ void need(const at::Tensor& t, at::ScalarType dt, const char* name) {
 
 cudaStream_t stream_of(const at::Tensor& t) { return turbol::StreamFor(t); }
 
+// A row-major 2-D block (unit column stride, any row stride), e.g. a column
+// block of a wider buffer; 1-D tensors must be contiguous.
+void need_rows(const at::Tensor& t, at::ScalarType dt, const char* name) {
+  TB_CHECK(t.defined() && t.is_cuda() && t.scalar_type() == dt, std::string(name) + ": wrong device or dtype");
+  TB_CHECK((t.dim() == 2 && t.stride(1) == 1) || (t.dim() == 1 && t.is_contiguous()),
+           std::string(name) + " must have unit column stride");
+}
+
 TbCartPoleParams cp_params(py::dict d) {
   TbCartPoleParams p{9.8f, 1.0f, 0.1f, 0.5f, 10.0f, 0.02f, 2.4f, 12.0f * 2.0f * 3.14159265358979f / 360.0f, 0.05f, 500};
   if (d.contains("gravity")) p.gravity = d["gravity"].cast<float>();
@@ -80,8 +88,8 @@ void register_kernel_ops(py::module_& m) {
            at::Tensor ep_ret, at::Tensor ep_count, at::Tensor stats, at::Tensor obs_buf, at::Tensor act_buf,
            at::Tensor logp_buf, at::Tensor val_buf, at::Tensor rew_buf, at::Tensor done_buf, py::object iter_ptr,
            int t, uint64_t policy_seed, uint64_t env_seed, py::dict params) {
-          need(logits, at::kFloat, "logits");
-          need(values, at::kFloat, "values");
+          need_rows(logits, at::kFloat, "logits");
+          need_rows(values, at::kFloat, "values");
           need(state, at::kFloat, "state");
           need(obs_buf, at::kFloat, "obs_buf");
           need(act_buf, at::kInt, "act_buf");
@@ -90,10 +98,11 @@ void register_kernel_ops(py::module_& m) {
           need(rew_buf, at::kFloat, "rew_buf");
           TB_CHECK(done_buf.is_cuda() && done_buf.element_size() == 1 && done_buf.is_contiguous(), "done_buf u8");
           const int n = static_cast<int>(state.size(0));
-          TB_CHECK(logits.dim() == 2 && logits.size(0) == n && logits.size(1) >= A, "logits [N, >=A]");
-          TB_CHECK(values.size(0) == n, "values batch mismatch");
+          TB_CHECK(logits.dim() == 2 && logits.size(0) == n && logits.size(1) >= A && logits.stride(1) == 1,
+                   "logits [N, >=A]");
+          TB_CHECK(values.size(0) == n && (values.dim() == 1 || values.stride(1) == 1), "values batch mismatch");
           TB_CHECK(obs_buf.dim() == 3 && obs_buf.size(1) == n && t >= 0 && t < obs_buf.size(0), "obs_buf [T, N, 4]");
-          const int ldv = values.dim() == 2 ? static_cast<int>(values.size(1)) : 1;
+          const int ldv = values.dim() == 2 ? static_cast<int>(values.stride(0)) : 1;
           void* ob = nullptr;
           if (!obs_bf16.is_none()) {
             at::Tensor x = obs_bf16.cast<at::Tensor>();
@@ -108,7 +117,7 @@ void register_kernel_ops(py::module_& m) {
             ip = reinterpret_cast<const long long*>(it.data_ptr<int64_t>());
           }
           cuda_ok(tb_ppo_cartpole_act_step(
-                      logits.data_ptr<float>(), A, static_cast<int>(logits.size(1)), values.data_ptr<float>(), ldv,
+                      logits.data_ptr<float>(), A, static_cast<int>(logits.stride(0)), values.data_ptr<float>(), ldv,
                       state.data_ptr<float>(), ob, ep_len.data_ptr<int>(), ep_ret.data_ptr<float>(),
                       reinterpret_cast<unsigned*>(ep_count.data_ptr<int>()), stats.data_ptr<float>(),
                       obs_buf.data_ptr<float>(), act_buf.data_ptr<int>(), logp_buf.data_ptr<float>(),
@@ -287,18 +296,24 @@ void register_kernel_ops(py::module_& m) {
         [](at::Tensor logits, int A, at::Tensor value, at::Tensor act, at::Tensor old_logp, at::Tensor adv,
            at::Tensor ret, at::Tensor dlog, at::Tensor dval, py::object stats, float clip, float vf_coef,
            float ent_coef, py::object db_log, py::object db_val) {
-          need(logits, at::kFloat, "logits");
-          need(value, at::kFloat, "value");
+          // logits / value / dlog / dval may be column blocks of wider row-major buffers
+          auto rows = [](const at::Tensor& t, at::ScalarType dt, const char* n) {
+            TB_CHECK(t.is_cuda() && t.scalar_type() == dt && t.dim() == 2 && t.stride(1) == 1, n);
+          };
+          rows(logits, at::kFloat, "logits: fp32 [B, >=A] with unit column stride");
+          rows(value, at::kFloat, "value: fp32 [B, >=1] with unit column stride");
+          rows(dlog, at::kBFloat16, "dlog: bf16 [B, 8] with unit column stride");
+          rows(dval, at::kBFloat16, "dval: bf16 [B, 8] with unit column stride");
           need(act, at::kInt, "act");
-          need(dlog, at::kBFloat16, "dlog");
-          need(dval, at::kBFloat16, "dval");
           const int B = static_cast<int>(act.numel());
-          TB_CHECK(logits.size(0) == B && dlog.numel() == 8LL * B && dval.numel() == 8LL * B, "padded loss shapes");
+          TB_CHECK(logits.size(0) == B && dlog.size(0) == B && dval.size(0) == B && dlog.size(1) >= 8 &&
+                       dval.size(1) >= 8 && dlog.stride(0) == dval.stride(0), "padded loss shapes");
           float* sp = stats.is_none() ? nullptr : stats.cast<at::Tensor>().data_ptr<float>();
-          cuda_ok(tb_ppo_loss_padded(logits.data_ptr<float>(), static_cast<int>(logits.size(1)), A,
-                                     value.data_ptr<float>(), static_cast<int>(value.size(1)), act.data_ptr<int>(),
+          cuda_ok(tb_ppo_loss_padded(logits.data_ptr<float>(), static_cast<int>(logits.stride(0)), A,
+                                     value.data_ptr<float>(), static_cast<int>(value.stride(0)), act.data_ptr<int>(),
                                      old_logp.data_ptr<float>(), adv.data_ptr<float>(), ret.data_ptr<float>(),
-                                     dlog.data_ptr(), dval.data_ptr(), sp, B, clip, vf_coef, ent_coef,
+                                     dlog.data_ptr(), dval.data_ptr(), static_cast<int>(dlog.stride(0)), sp, B, clip,
+                                     vf_coef, ent_coef,
                                      db_log.is_none() ? nullptr : db_log.cast<at::Tensor>().data_ptr<float>(),
                                      db_val.is_none() ? nullptr : db_val.cast<at::Tensor>().data_ptr<float>(),
                                      stream_of(logits)),

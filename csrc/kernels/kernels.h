@@ -75,7 +75,7 @@ int tb_ppo_gather(const float* obs, int obs_dim, const int* act, const float* lo
                   int normalize, cudaStream_t s);
 int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, int ldv, const int* act,
                        const float* old_logp, const float* adv, const float* ret, void* dlog_bf16, void* dval_bf16,
-                       float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
+                       int ldd, float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
                        float* db_val, cudaStream_t s);
 int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, int accumulate, cudaStream_t s);
 // First MLP layer with 8 (padded) input features: y = act(x . W^T + b), act 0

@@ -199,13 +199,13 @@ __global__ void ppo_loss_kernel(const float* __restrict__ logits, const float* _
 }
 
 // Same loss, on the tensor-core MLP's padded layout: logits [B, ldl] and values
-// [B, ldv] (column 0) in fp32; writes bf16 gradients d logits [B, 8] and
-// d value [B, 8] (padding columns zero), already divided by B.
+// [B, ldv] (column 0) in fp32; writes bf16 gradients d logits and d value, 8
+// columns each with row stride ldd (padding columns zero), already divided by B.
 template <int A>
 __global__ void ppo_loss_padded_kernel(const float* __restrict__ logits, int ldl, const float* __restrict__ value,
                                        int ldv, const int* __restrict__ act, const float* __restrict__ old_logp,
                                        const float* __restrict__ adv, const float* __restrict__ ret,
-                                       __nv_bfloat16* __restrict__ dlog, __nv_bfloat16* __restrict__ dval,
+                                       __nv_bfloat16* __restrict__ dlog, __nv_bfloat16* __restrict__ dval, int ldd,
                                        float* __restrict__ stats, int B, float clip, float vf_coef, float ent_coef,
                                        float* __restrict__ db_log, float* __restrict__ db_val) {
   __shared__ float red[kBlock / 32];
@@ -254,12 +254,12 @@ __global__ void ppo_loss_padded_kernel(const float* __restrict__ logits, int ldl
       g8[k] = __float2bfloat16_rn(g);
       if (k < A) gsum[k] = __bfloat162float(g8[k]);
     }
-    *reinterpret_cast<uint4*>(dlog + static_cast<size_t>(i) * 8) = *reinterpret_cast<uint4*>(g8);
+    *reinterpret_cast<uint4*>(dlog + static_cast<size_t>(i) * ldd) = *reinterpret_cast<uint4*>(g8);
     __nv_bfloat16 v8[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) v8[k] = __float2bfloat16_rn(k == 0 ? vf_coef * (V - R) * scale : 0.f);
     gsum[A] = __bfloat162float(v8[0]);
-    *reinterpret_cast<uint4*>(dval + static_cast<size_t>(i) * 8) = *reinterpret_cast<uint4*>(v8);
+    *reinterpret_cast<uint4*>(dval + static_cast<size_t>(i) * ldd) = *reinterpret_cast<uint4*>(v8);
     s_pg = -fminf(un, cl);
     s_v = 0.5f * (V - R) * (V - R);
     s_h = H;
@@ -457,9 +457,11 @@ int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, 
 
 int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, int ldv, const int* act,
                        const float* old_logp, const float* adv, const float* ret, void* dlog_bf16, void* dval_bf16,
-                       float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
+                       int ldd, float* stats, int B, float clip, float vf_coef, float ent_coef, float* db_log,
                        float* db_val, cudaStream_t s) {
   if (B <= 0) return 0;
+  if (ldd % 8 || (reinterpret_cast<uintptr_t>(dlog_bf16) & 15) || (reinterpret_cast<uintptr_t>(dval_bf16) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
   if ((db_log == nullptr) != (db_val == nullptr)) return static_cast<int>(cudaErrorInvalidValue);
   if (db_log) {
     cudaMemsetAsync(db_log, 0, sizeof(float) * A, s);
@@ -470,7 +472,7 @@ int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, 
   auto* dv = static_cast<__nv_bfloat16*>(dval_bf16);
 #define TB_PPO_CASE(K)                                                                                           \
   case K:                                                                                                        \
-    ppo_loss_padded_kernel<K><<<g, kBlock, 0, s>>>(logits, ldl, value, ldv, act, old_logp, adv, ret, dl, dv,   \
+    ppo_loss_padded_kernel<K><<<g, kBlock, 0, s>>>(logits, ldl, value, ldv, act, old_logp, adv, ret, dl, dv, ldd, \
                                                    stats, B, clip, vf_coef, ent_coef, db_log, db_val);          \
     break;
   switch (A) {

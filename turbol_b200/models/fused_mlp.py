@@ -1,16 +1,20 @@
 """Tensor-core actor-critic MLP with hand-written forward and backward.
 
 Two tanh MLPs (actor obs -> H -> H -> A logits, critic obs -> H -> H -> 1)
-run on the tcgen05 GEMM (:func:`turbol_b200.ops.gemm`) with the pointwise work
-fused into the GEMM epilogues:
+run as one network with block-diagonal layers: the actor and the critic are
+the two diagonal blocks of W2 [2H, 2H] and W3 [16, 2H] (the off-diagonal
+blocks are zero and receive no gradient, so they stay zero), so every layer is
+a single launch for both heads.  The 8-feature first layer runs on CUDA cores
+(a tensor-core tile would be mostly K padding); the rest on the tcgen05 GEMM
+(:func:`turbol_b200.ops.gemm`) with the pointwise work fused into the GEMM
+epilogues:
 
-  forward   H1 = tanh(X W1^T + b1)          one GEMM for actor and critic (W1 stacked)
-            H2 = tanh(H1 W2^T + b2)         per head
-            out = H2 W3^T + b3              per head (fp32)
-  backward  dZ2 = (dOut W3) * (1 - H2^2)    GEMM + tanh-backward epilogue
-            dZ1 = (dZ2 W2) * (1 - H1^2)     GEMM + tanh-backward epilogue
-            dW  = dZ^T H                    MN-major x MN-major GEMM, split-K, fp32
-            db  = column sums of dZ
+  forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
+            H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM
+            out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
+  backward  dZ2 = (dOut W3) * (1 - H2^2)    one GEMM + tanh-backward epilogue (+ db2 column sums)
+            dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM + tanh-backward epilogue (+ db1 column sums)
+            dW  = dZ^T H                    per diagonal block: MN-major x MN-major GEMM, split-K, fp32
 No transposes are materialized and no [B, H] fp32 intermediates exist:
 activations and activation gradients are bf16, weights are the bf16 shadow
 that the fused Adam writes next to the fp32 master copy, and weight gradients
@@ -43,9 +47,8 @@ class FusedActorCritic:
         self.obs_dim, self.act_dim, self.H = obs_dim, act_dim, H
         self.device = torch.device(device)
         # parameter layout in the flat buffer; every offset 64-element aligned
-        shapes = [("w1", (2 * H, PAD)), ("b1", (2 * H,)),
-                  ("w2a", (H, H)), ("b2a", (H,)), ("w3a", (PAD, H)), ("b3a", (PAD,)),
-                  ("w2c", (H, H)), ("b2c", (H,)), ("w3c", (PAD, H)), ("b3c", (PAD,))]
+        shapes = [("w1", (2 * H, PAD)), ("b1", (2 * H,)), ("w2", (2 * H, 2 * H)), ("b2", (2 * H,)),
+                  ("w3", (2 * PAD, 2 * H)), ("b3", (2 * PAD,))]
         self.offsets, off = {}, 0
         for name, shp in shapes:
             self.offsets[name] = (off, shp)
@@ -54,9 +57,7 @@ class FusedActorCritic:
         self.flat = torch.zeros(off, device=self.device, dtype=torch.float32)
         self.grad = torch.zeros(off, device=self.device, dtype=torch.float32)
         self.shadow = torch.zeros(off, device=self.device, dtype=torch.bfloat16)
-        self.p = {n: self._view(self.flat, n) for n in self.offsets}
-        self.g = {n: self._view(self.grad, n) for n in self.offsets}
-        self.s = {n: self._view(self.shadow, n) for n in self.offsets}
+        self._make_views()
         self.reset_parameters(seed)
         self._ws = {}
 
@@ -68,13 +69,26 @@ class FusedActorCritic:
         shadow[: self.numel].copy_(self.shadow)
         grad[: self.numel].zero_()
         self.flat, self.grad, self.shadow = flat[: self.numel], grad[: self.numel], shadow[: self.numel]
-        self.p = {n: self._view(self.flat, n) for n in self.offsets}
-        self.g = {n: self._view(self.grad, n) for n in self.offsets}
-        self.s = {n: self._view(self.shadow, n) for n in self.offsets}
+        self._make_views()
 
     def _view(self, buf, name):
         off, shp = self.offsets[name]
         return buf[off:off + math.prod(shp)].view(shp)
+
+    def _make_views(self):
+        """Whole parameters plus per-head views of the diagonal blocks
+        (w2a / w2c, b2a / b2c, w3a / w3c, b3a / b3c)."""
+        H = self.H
+
+        def views(buf):
+            d = {n: self._view(buf, n) for n in self.offsets}
+            d["w2a"], d["w2c"] = d["w2"][:H, :H], d["w2"][H:, H:]
+            d["b2a"], d["b2c"] = d["b2"][:H], d["b2"][H:]
+            d["w3a"], d["w3c"] = d["w3"][:PAD, :H], d["w3"][PAD:, H:]
+            d["b3a"], d["b3c"] = d["b3"][:PAD], d["b3"][PAD:]
+            return d
+
+        self.p, self.g, self.s = views(self.flat), views(self.grad), views(self.shadow)
 
     # ------------------------------------------------------------ init / io
     def reset_parameters(self, seed: int = 0):
@@ -124,17 +138,15 @@ class FusedActorCritic:
             bf = dict(device=self.device, dtype=torch.bfloat16)
             f32 = dict(device=self.device, dtype=torch.float32)
             H = self.H
+            out = torch.empty(B, 2 * PAD, **f32)       # logits | value
+            dout = torch.empty(B, 2 * PAD, **bf)       # d logits | d value
             ws = {
                 "h1": torch.empty(B, 2 * H, **bf),
-                "h2a": torch.empty(B, H, **bf),
-                "h2c": torch.empty(B, H, **bf),
-                "logits": torch.empty(B, PAD, **f32),
-                "value": torch.empty(B, PAD, **f32),
-                "dz2a": torch.empty(B, H, **bf),
-                "dz2c": torch.empty(B, H, **bf),
+                "h2": torch.empty(B, 2 * H, **bf),
+                "out": out, "logits": out[:, :PAD], "value": out[:, PAD:],
+                "dz2": torch.empty(B, 2 * H, **bf),
                 "dz1": torch.empty(B, 2 * H, **bf),
-                "dlog": torch.empty(B, PAD, **bf),
-                "dval": torch.empty(B, PAD, **bf),
+                "dout": dout, "dlog": dout[:, :PAD], "dval": dout[:, PAD:],
             }
             o = _ops()
             n = max(o.gemm_workspace_numel(H, H, B), o.gemm_workspace_numel(PAD, H, B),
@@ -147,38 +159,35 @@ class FusedActorCritic:
 
     # ------------------------------------------------------------ compute
     def forward(self, x_bf16: torch.Tensor, ws=None):
-        """x_bf16 [B, 8] -> (logits fp32 [B, 8], value fp32 [B, 8] (column 0))."""
+        """x_bf16 [B, 8] -> (logits fp32 [B, 8], value fp32 [B, 8] (column 0)), views of ws['out']."""
         o = _ops()
         B = x_bf16.shape[0]
         ws = ws or self.workspace(B)
         S, P = self.s, self.p
-        H = self.H
-        h1 = ws["h1"]
-        o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], h1, True)                 # 8 input features: CUDA cores
-        o.gemm(h1[:, :H], S["w2a"], ws["h2a"], bias=P["b2a"], epi=o.EPI_BIAS_TANH)
-        o.gemm(h1[:, H:], S["w2c"], ws["h2c"], bias=P["b2c"], epi=o.EPI_BIAS_TANH)
-        o.gemm(ws["h2a"], S["w3a"], ws["logits"], bias=P["b3a"], epi=o.EPI_BIAS)
-        o.gemm(ws["h2c"], S["w3c"], ws["value"], bias=P["b3c"], epi=o.EPI_BIAS)
+        o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], ws["h1"], True)                 # 8 input features: CUDA cores
+        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH)    # both heads' hidden layer
+        o.gemm(ws["h2"], S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)        # logits | value
         return ws["logits"], ws["value"]
 
     def backward(self, x_bf16: torch.Tensor, ws, out_bias_grads_done: bool = False):
-        """Weight gradients into self.grad from ws['dlog'] / ws['dval'] (bf16 [B, 8]).
+        """Weight gradients into self.grad from ws['dout'] = (d logits | d value)
+        (bf16 [B, 16]).
 
         The hidden-layer bias gradients come out of the tanh-backward GEMM
         epilogues (column sums); the output-layer bias gradients come from the
-        loss kernel when ``out_bias_grads_done`` (else a column-sum kernel)."""
+        loss kernel when ``out_bias_grads_done`` (else a column-sum kernel).
+        Weight gradients are computed for the diagonal blocks only, so the
+        off-diagonal gradient (and weights) stay zero."""
         o = _ops()
         S, G = self.s, self.g
         H = self.H
-        h1, wsk = ws["h1"], ws["splitk"]
-        for head, dout, h2, dz2, w2, w3, cols in (("a", ws["dlog"], ws["h2a"], ws["dz2a"], S["w2a"], S["w3a"], slice(0, H)),
-                                                   ("c", ws["dval"], ws["h2c"], ws["dz2c"], S["w2c"], S["w3c"], slice(H, 2 * H))):
-            o.gemm(dout, h2, G["w3" + head], True, True, workspace=wsk)          # dW3 = dOut^T H2
-            if not out_bias_grads_done:
-                o.colsum_bf16(dout, G["b3" + head])                                # db3
-            o.gemm(dout, w3, dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD,        # dZ2 = (dOut W3)(1 - H2^2)
-                   colsum=G["b2" + head])                                          #   db2 = sum dZ2
-            o.gemm(dz2, h1[:, cols], G["w2" + head], True, True, workspace=wsk)   # dW2 = dZ2^T H1
-            o.gemm(dz2, w2, ws["dz1"][:, cols], False, True, aux=h1[:, cols],     # dZ1 = (dZ2 W2)(1 - H1^2)
-                   epi=o.EPI_TANH_BWD, colsum=G["b1"][cols])                       #   db1 = sum dZ1
-        o.gemm(ws["dz1"], x_bf16, G["w1"], True, True, workspace=wsk)             # dW1 = dZ1^T X
+        h1, h2, dz2, dz1, dout, wsk = ws["h1"], ws["h2"], ws["dz2"], ws["dz1"], ws["dout"], ws["splitk"]
+        for head, rows, cols in (("a", slice(0, PAD), slice(0, H)), ("c", slice(PAD, 2 * PAD), slice(H, 2 * H))):
+            o.gemm(dout[:, rows], h2[:, cols], G["w3" + head], True, True, workspace=wsk)   # dW3 block = dOut^T H2
+        if not out_bias_grads_done:
+            o.colsum_bf16(dout, G["b3"])
+        o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])  # dZ2, db2
+        for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
+            o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk)      # dW2 block = dZ2^T H1
+        o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
+        o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
