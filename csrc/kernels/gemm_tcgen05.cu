@@ -153,8 +153,25 @@ __device__ __forceinline__ float warp_colsum32(float* v, int lane) {
 // mode kEpiFull: scale by alpha and run the epilogue; kEpiPartial: scale and
 // store the split-K partial; kEpiFinal: epilogue of already-scaled summed partials.
 enum { kEpiFull = 0, kEpiPartial = 1, kEpiFinal = 2 };
+__device__ __forceinline__ void unpack_bf16x32(uint4 q0, uint4 q1, uint4 q2, uint4 q3, float* out) {
+  const uint4 q[4] = {q0, q1, q2, q3};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      out[8 * i + 2 * j] = f.x;
+      out[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+// pre: a0..a3 hold the row's 32 aux values, already loaded (16 bytes each).
 __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane,
-                                           uint32_t* stg, int row0, int mode, void* cbase) {
+                                           uint32_t* stg, int row0, int mode, void* cbase, bool pre = false,
+                                           uint4 a0 = uint4{}, uint4 a1 = uint4{}, uint4 a2 = uint4{},
+                                           uint4 a3 = uint4{}) {
   const int N = p.N, epi = p.epi;
   const bool row_ok = row < p.M;
   const int valid = min(32, N - c0);
@@ -188,10 +205,14 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = fast_silu(v[j]);
   } else if ((epi == TB_EPI_TANH_BWD || epi == TB_EPI_RESIDUAL) && row_ok) {
-    const __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + c0;
     float h[32];
-    load_bf16x16(a, h, valid);
-    load_bf16x16(a + 16, h + 16, valid - 16);
+    if (pre) {
+      unpack_bf16x32(a0, a1, a2, a3, h);
+    } else {
+      const __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + c0;
+      load_bf16x16(a, h, valid);
+      load_bf16x16(a + 16, h + 16, valid - 16);
+    }
     if (epi == TB_EPI_TANH_BWD) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= 1.f - h[j] * h[j];
@@ -430,11 +451,20 @@ __device__ __forceinline__ void fixup_slice(const DevArgs& p, int row0, int col0
   }
 }
 
+// Work unit w -> (tile, K split).  Tiles run in panels of kPanel m-tiles:
+// within a panel the m-tile index moves fastest, so a wave of ~148 tiles
+// covers ~16 row blocks x ~9 column blocks and re-reads far less of A and B
+// from DRAM than sweeping all row blocks per column block.
+constexpr int kPanel = 16;
 __device__ __forceinline__ void work_coords(const DevArgs& p, int w, int& m0, int& nt, int& ks, int& kb0, int& kb1) {
-  const int mt = w % p.m_tiles;
-  const int rest = w / p.m_tiles;
-  nt = rest % p.n_tiles;
-  ks = rest / p.n_tiles;
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int t = w % tiles;
+  ks = w / tiles;
+  const int panel = t / (kPanel * p.n_tiles);
+  const int within = t - panel * kPanel * p.n_tiles;
+  const int gm = min(kPanel, p.m_tiles - panel * kPanel);
+  const int mt = panel * kPanel + within % gm;
+  nt = within / gm;
   m0 = mt * BM;
   kb0 = ks * p.kb_per_split;
   kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
@@ -774,8 +804,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + r_in_tile;
       const uint32_t base = tmem_base + acc * BN + (static_cast<uint32_t>(sub * 32) << 16);
       constexpr int kStep = BN / 2 >= 64 ? 64 : 32;  // columns per TMEM load batch
+      // epilogues that read an aux matrix: issue this row's aux loads before
+      // the TMEM loads so the two latencies overlap
+      const bool aux_rows = (p.epi == TB_EPI_TANH_BWD || p.epi == TB_EPI_RESIDUAL) && mode != kEpiPartial &&
+                            row < p.M;
 #pragma unroll 1
       for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += kStep) {
+        uint4 ax[kStep / 8];
+        bool pre = false;
+        if (aux_rows && n0 + c + kStep <= p.N) {
+          const __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + n0 + c;
+          if ((reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+            pre = true;
+#pragma unroll
+            for (int q = 0; q < kStep / 8; ++q) ax[q] = reinterpret_cast<const uint4*>(a)[q];
+          }
+        }
         uint32_t r[64];
         tmem_ld32_nowait(base + c, r);
         if constexpr (kStep == 64) tmem_ld32_nowait(base + c + 32, r + 32);
@@ -783,11 +827,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (n0 + c < p.N) epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode, cbase);
+        if (n0 + c < p.N)
+          epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[0], ax[1], ax[2], ax[3]);
         if constexpr (kStep == 64) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
-          if (n0 + c + 32 < p.N) epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode, cbase);
+          if (n0 + c + 32 < p.N)
+            epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[kStep / 8 - 4],
+                       ax[kStep / 8 - 3], ax[kStep / 8 - 2], ax[kStep / 8 - 1]);
         }
       }
       tc_fence_before();
