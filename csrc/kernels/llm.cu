@@ -117,14 +117,21 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __re
       }
     }
   }
+  // weight gradient: the block's warps combine in shared memory, then one
+  // global atomic per column per block (not per warp)
+  __shared__ float sdw[MAXV * 32];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
 #pragma unroll
   for (int s = 0; s < MAXV / 8; ++s) {
     const int c = s * 256 + lane * 8;
     if (c < D) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) atomicAdd(dw + c + i, dwp[s * 8 + i]);
+      for (int i = 0; i < 8; ++i) atomicAdd(sdw + c + i, dwp[s * 8 + i]);
     }
   }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(dw + c, sdw[c]);
 }
 
 // ------------------------------------------------------------------ RoPE
@@ -706,15 +713,20 @@ __global__ void __launch_bounds__(1024) logprob_kernel(bf16* __restrict__ logits
   const int row = blockIdx.x;
   bf16* x = logits + static_cast<long long>(row) * ld;
   float m = -INFINITY, s = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float z = bf(x[i]) * inv_temp;
-    if (z > m) {
-      s = s * __expf(m - z) + 1.f;
-      m = z;
-    } else {
-      s += __expf(z - m);
+  // 16-byte loads of 8 logits where the row allows it
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  const int nv = vec ? V / 8 : 0;
+  for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + c * 8);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      online_add(m, s, f.x * inv_temp);
+      online_add(m, s, f.y * inv_temp);
     }
   }
+  for (int i = nv * 8 + threadIdx.x; i < V; i += blockDim.x) online_add(m, s, bf(x[i]) * inv_temp);
   // merge (m, s) pairs across the block
   __shared__ float sm[32], ss[32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -752,7 +764,20 @@ __global__ void __launch_bounds__(1024) logprob_kernel(bf16* __restrict__ logits
   if (threadIdx.x == 0 && logp) logp[row] = zt - lse;
   if (dlogp != nullptr) {
     const float g = dlogp[row];
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    for (int c = threadIdx.x; c < nv; c += blockDim.x) {
+      uint4 u = *reinterpret_cast<const uint4*>(x + c * 8);
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(h[k]);
+        const int i0 = c * 8 + 2 * k;
+        const float p0 = __expf(f.x * inv_temp - lse), p1 = __expf(f.y * inv_temp - lse);
+        h[k] = __floats2bfloat162_rn(g * inv_temp * ((i0 == tgt ? 1.f : 0.f) - p0),
+                                     g * inv_temp * ((i0 + 1 == tgt ? 1.f : 0.f) - p1));
+      }
+      *reinterpret_cast<uint4*>(x + c * 8) = u;
+    }
+    for (int i = nv * 8 + threadIdx.x; i < V; i += blockDim.x) {
       const float p = __expf(bf(x[i]) * inv_temp - lse);
       x[i] = __float2bfloat16_rn(g * inv_temp * ((i == tgt ? 1.f : 0.f) - p));
     }
@@ -831,7 +856,9 @@ int tb_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* r
                    float* dw, int T, int D, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 256 || D > 8192) return static_cast<int>(cudaErrorInvalidValue);
-  const int rpb = 64;
+  // ~2 blocks per SM; more rows per block means fewer global atomics on dw
+  int rpb = (T + 2 * 148 - 1) / (2 * 148);
+  if (rpb < 8) rpb = 8;
   const unsigned g = (T + rpb - 1) / rpb;
   auto* a = static_cast<const bf16*>(dy);
   auto* b = static_cast<const bf16*>(x);
