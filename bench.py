@@ -11,7 +11,10 @@ Workload (weak scaling: every rank owns its own 65,536 envs):
 One step = one full PPO iteration (rollout + GAE + 1,024 minibatch updates).
 value = N * 65,536 * 128 * K / (max over ranks of the device time of K steps).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--grpo-steps G]
+
+The JSON line also carries a secondary "grpo" measurement: GRPO train
+tokens/s (1.5B-shape policy, 64 prompts x 8 per GPU, data parallel).
 
 For N > 1 run under torch.distributed.run (one process per GPU).
 ``--impl reference`` runs the reference build's own Python API (installed in
@@ -47,7 +50,49 @@ def parse():
     p.add_argument("--rollout", type=int, default=ROLLOUT)
     p.add_argument("--dp", choices=["fused", "nccl"], default="fused",
                    help="gradient reduction for N > 1: fused peer-memory kernel or NCCL all-reduce")
+    p.add_argument("--grpo-steps", type=int, default=None,
+                   help="timed steps of the GRPO secondary measurement (0: skip; default 2 on one GPU, "
+                        "0 on several so the scaling run stays short); 3 warm-up steps")
     return p.parse_args()
+
+
+def run_grpo(args, world, rank, local):
+    """Secondary measurement: GRPO train tokens/s on the 1.5B-shape policy
+    (64 prompts x 8 samples per GPU, 256 + 512 tokens, data parallel with the
+    fused peer-memory optimizer step for N > 1), device-timed, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from turbol_b200.rl.grpo import GRPOConfig, GRPOTrainer
+
+    cfg = GRPOConfig(num_prompts=64, group_size=8, prompt_len=256, response_len=512, micro_batch=8)
+    tr = GRPOTrainer(cfg, f"cuda:{local}", dp=args.dp if world > 1 else "none")
+    warm = 3
+    for _ in range(warm):
+        tr.step()
+    times = []
+    last = None
+    for _ in range(args.grpo_steps):
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        last = tr.step()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(max_over_ranks(e0.elapsed_time(e1) / 1e3, world))
+    sec = sum(times) / len(times)
+    if world > 1:
+        tr.opt.check()
+    out = {"metric": "GRPO train tokens/s", "value": world * cfg.batch * cfg.seq_len / sec, "unit": "tokens/s",
+           "steps": args.grpo_steps, "warmup": warm, "s_per_step": sec,
+           "phases_s": {k: last[k] for k in ("rollout_s", "reward_ref_s", "train_s")},
+           "config": {"model": "qwen2-1.5b-shape decoder (28 layers, hidden 1536, 12q/2kv heads, ffn 8960, "
+                               "vocab 151936)", "prompts_per_gpu": 64, "group": 8, "prompt_len": 256,
+                      "response_len": 512, "parallelism": f"dp{world}" + (f" ({args.dp})" if world > 1 else "")},
+           "timing": "CUDA events around each step, max over ranks"}
+    del tr
+    torch.cuda.empty_cache()
+    return out
 
 
 class ClockSampler:
@@ -207,9 +252,18 @@ def run_ours(args):
         "gpu_launches": launches_per_iter * args.steps,
         "final_mean_return": m.get("mean_return"),
     }
+    tr.release_graphs()
+    del tr
+    torch.cuda.empty_cache()
+    if args.grpo_steps is None:
+        args.grpo_steps = 2 if world == 1 else 0
+    if args.grpo_steps > 0:
+        try:
+            out["grpo"] = run_grpo(args, world, rank, local)
+        except Exception as e:  # the headline line is printed regardless
+            out["grpo"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if rank == 0:
         print(json.dumps(out), flush=True)
-    tr.release_graphs()
     if world > 1:
         import torch.distributed as dist
 

@@ -63,6 +63,15 @@ TbGemmArgs tp_gemm_args(const at::Tensor& A, const at::Tensor& B, bool b_mn, int
 
 void register_comm_ops(py::module_& m) {
   m.def("tp_header_bytes", []() { return static_cast<int64_t>(tb_tp_header_bytes()); });
+  m.def("bounded_wait_probe", [](at::Tensor flags, int64_t expect, double budget_s, at::Tensor err) {
+    if (!flags.is_cuda() || flags.scalar_type() != at::kInt || !err.is_cuda() || err.scalar_type() != at::kInt)
+      throw std::invalid_argument("bounded_wait_probe: int32 CUDA tensors");
+    cuda_ok(tb_bounded_wait_probe(reinterpret_cast<const unsigned*>(flags.data_ptr<int>()),
+                                  static_cast<int>(flags.numel()), static_cast<unsigned>(expect),
+                                  static_cast<unsigned long long>(budget_s * 1e9), err.data_ptr<int>(),
+                                  cur_stream(flags.device().index())),
+            "bounded_wait_probe");
+  }, py::arg("flags"), py::arg("expect"), py::arg("budget_s"), py::arg("err"));
   m.def("tp_set_trace", [](py::object t) {
     tb_tp_set_trace(t.is_none() ? nullptr : t.cast<at::Tensor>().data_ptr());
   });

@@ -50,12 +50,13 @@ __device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
 }
 
 // Waits until flags[0..W) (local memory, written by peers) all reach `epoch`.
-__device__ bool wait_all(const unsigned* flags, int W, unsigned epoch, int* err, int site) {
+__device__ bool wait_all(const unsigned* flags, int W, unsigned epoch, int* err, int site,
+                         unsigned long long budget_ns = kBudgetNs) {
   const unsigned long long t0 = now_ns();
   for (int p = 0; p < W; ++p) {
     while (ld_acquire(flags + p) < epoch) {
       if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (now_ns() - t0 > kBudgetNs) {
+      if (now_ns() - t0 > budget_ns) {
         atomicCAS(err, 0, site);
         return false;
       }
@@ -100,10 +101,11 @@ __device__ unsigned begin_call(const TbPeerTable& t, int* err, bool* ok) {
   const unsigned epoch = *t.epoch_ctr + 1;
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) {
-      __threadfence_system();
-      for (int p = 0; p < t.world; ++p) st_release(&reinterpret_cast<Hdr*>(t.hdr[p])->flags_in[t.rank], epoch);
-    }
+    // every block publishes "this rank's inputs are ready" (the same epoch,
+    // idempotent), so no block waits on another block of its own grid being
+    // scheduled: the only waits are on other ranks
+    __threadfence_system();
+    for (int p = 0; p < t.world; ++p) st_release(&reinterpret_cast<Hdr*>(t.hdr[p])->flags_in[t.rank], epoch);
     s_ok = wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_in, t.world, epoch, err, 1) ? 1 : 0;
   }
   __syncthreads();
@@ -239,6 +241,16 @@ int grid_for(long long n, int world) {
   return static_cast<int>(g);
 }
 
+// The collectives' bounded wait on its own: one thread waits for flags[0..n)
+// to reach `expect` for at most budget_ns, then records `site` in the error
+// word and returns.  Lets a test make a wait run out (a flag that nothing
+// sets) and check that the kernel ends with an error status instead of
+// hanging, without a second rank.
+__global__ void bounded_wait_probe_kernel(const unsigned* flags, int n, unsigned expect,
+                                          unsigned long long budget_ns, int* err) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) wait_all(flags, n, expect, err, 99, budget_ns);
+}
+
 }  // namespace
 
 extern "C" {
@@ -259,6 +271,13 @@ int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_of
     return static_cast<int>(cudaErrorInvalidValue);
   allreduce_adam_kernel<<<grid_for(n, t.world), kBlock, 0, s>>>(t, grad_off, param_off, shadow_off, n, m, v, hp,
                                                                 step_ptr, done_ctr, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_bounded_wait_probe(const unsigned* flags, int n, unsigned expect, unsigned long long budget_ns, int* err,
+                          cudaStream_t s) {
+  if (n <= 0 || n > TB_MAX_PEERS) return static_cast<int>(cudaErrorInvalidValue);
+  bounded_wait_probe_kernel<<<1, 32, 0, s>>>(flags, n, expect, budget_ns, err);
   return static_cast<int>(cudaGetLastError());
 }
 

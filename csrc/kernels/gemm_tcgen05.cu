@@ -300,11 +300,16 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
     if (valid == 32 && (p.ldc % 8) == 0 && (reinterpret_cast<uintptr_t>(cbase) & 15) == 0) {
       // transpose through shared memory so each store instruction writes
       // 8 whole 64-byte row segments instead of 32 scattered 16-byte pieces
-      uint32_t* mine = stg + lane * 20;
+      // four 16-byte stores per lane: with the 80-byte row pitch the 8 lanes
+      // of each store phase hit disjoint banks
+      uint4* mine = reinterpret_cast<uint4*>(stg + lane * 20);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-        mine[j] = *reinterpret_cast<uint32_t*>(&h2);
+      for (int q = 0; q < 4; ++q) {
+        uint4 pk;
+        __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(v[8 * q + 2 * j], v[8 * q + 2 * j + 1]);
+        mine[q] = pk;
       }
       __syncwarp();
       const int seg = lane & 3;

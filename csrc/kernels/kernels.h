@@ -194,6 +194,10 @@ typedef struct {
 } TbPeerTable;
 
 size_t tb_peer_header_bytes(void);
+// The peer collectives' bounded flag wait, alone: waits up to budget_ns for
+// flags[0..n) >= expect, then sets *err = 99 (site code) and returns.
+int tb_bounded_wait_probe(const unsigned* flags, int n, unsigned expect, unsigned long long budget_ns, int* err,
+                          cudaStream_t s);
 
 // ---- tensor parallelism: collectives fused into the tcgen05 GEMM -----------
 // Symmetric layout per rank (mapped into every peer): a header of
