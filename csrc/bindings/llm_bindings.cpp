@@ -261,16 +261,28 @@ void register_llm_ops(py::module_& m) {
                          static_cast<int>(lp.size(1)), clip, beta, inv_total_seqs, turbol::StreamFor(lp)),
             "grpo_loss");
   });
-  m.def("flash_attn_fwd", [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, py::object lse, int B, int T,
-                              int Hq, int Hk, float scale) {
-    bf16_2d(q, "q");
-    bf16_2d(o, "o");
-    chk(q.stride(0) == k.stride(0) && q.stride(0) == v.stride(0), "flash_attn: q/k/v share the row stride");
-    float* l = lse.is_none() ? nullptr : lse.cast<at::Tensor>().data_ptr<float>();
-    cuda_ok(tb_flash_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0), l, B,
-                              T, Hq, Hk, scale, turbol::StreamFor(q)),
-            "flash_attn_fwd");
-  });
+  m.def(
+      "flash_attn_fwd",
+      [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, py::object lse, int B, int T, int Hq, int Hk,
+          float scale, const std::string& impl, py::object err) {
+        bf16_2d(q, "q");
+        bf16_2d(o, "o");
+        chk(q.stride(0) == k.stride(0) && q.stride(0) == v.stride(0), "flash_attn: q/k/v share the row stride");
+        float* l = lse.is_none() ? nullptr : lse.cast<at::Tensor>().data_ptr<float>();
+        if (impl == "tc") {
+          int* e = err.is_none() ? nullptr : err.cast<at::Tensor>().data_ptr<int>();
+          cuda_ok(tb_flash_attn_fwd_tc(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(),
+                                       o.stride(0), l, B, T, Hq, Hk, scale, e, turbol::StreamFor(q)),
+                  "flash_attn_fwd");
+        } else {
+          chk(impl == "mma", "flash_attn_fwd: impl is 'tc' (tcgen05) or 'mma' (mma.sync)");
+          cuda_ok(tb_flash_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0),
+                                    l, B, T, Hq, Hk, scale, turbol::StreamFor(q)),
+                  "flash_attn_fwd");
+        }
+      },
+      py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("B"), py::arg("T"),
+      py::arg("Hq"), py::arg("Hk"), py::arg("scale"), py::arg("impl") = "tc", py::arg("err") = py::none());
   m.def("flash_attn_bwd", [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
                               at::Tensor lse, at::Tensor delta, at::Tensor dq, at::Tensor dk, at::Tensor dv, int B,
                               int T, int Hq, int Hk, float scale) {

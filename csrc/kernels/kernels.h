@@ -180,6 +180,10 @@ int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, cons
                  cudaStream_t s);
 int tb_flash_attn_fwd(const void* q, const void* k, const void* v, long long ld, void* o, long long ldo, float* lse,
                       int B, int T, int Hq, int Hk, float scale, cudaStream_t s);
+// Same contract on tcgen05 tensor cores (TMA + TMEM); err (nullable) gets site
+// 21 when a bounded wait ran out.
+int tb_flash_attn_fwd_tc(const void* q, const void* k, const void* v, long long ld, void* o, long long ldo, float* lse,
+                         int B, int T, int Hq, int Hk, float scale, int* err, cudaStream_t s);
 int tb_flash_attn_bwd(const void* q, const void* k, const void* v, long long ld, const void* o, long long ldo,
                       const void* dout, long long lddo, const float* lse, float* delta, void* dq, void* dk, void* dv,
                       long long lddqkv, int B, int T, int Hq, int Hk, float scale, cudaStream_t s);

@@ -82,6 +82,41 @@ def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
         assert err < 3e-2, err
 
 
+@pytest.mark.parametrize("B,T,Hq,Hk,amp", [(1, 64, 4, 2, 1.0), (2, 200, 12, 2, 1.0), (3, 333, 8, 8, 1.0),
+                                          (1, 768, 12, 2, 3.0), (2, 300, 32, 8, 6.0)])
+def test_flash_attention_fwd_tcgen05(B, T, Hq, Hk, amp, dev):
+    """tcgen05 forward vs an fp32 reference and vs the mma.sync kernel (same LSE).
+    amp > 1 makes the scores large and uneven, so the lazily updated row max
+    moves mid-sequence and the O accumulator in TMEM gets rescaled."""
+    D = 128
+    ld = (Hq + 2 * Hk) * D
+    g = torch.Generator(device=dev).manual_seed(T + Hq)
+    qkv = bf(torch.randn(B * T, ld, device=dev, generator=g) * 0.5)
+    qkv[:, : Hq * D] *= amp
+    # a ramp on the keys: later keys score higher, so the running max keeps growing
+    ramp = torch.linspace(0, amp, T, device=dev).repeat(B)[:, None]
+    qkv[:, Hq * D:(Hq + Hk) * D] = bf(qkv[:, Hq * D:(Hq + Hk) * D].float() + ramp)
+    q, k, v = qkv[:, : Hq * D], qkv[:, Hq * D:(Hq + Hk) * D], qkv[:, (Hq + Hk) * D:]
+    scale = 1 / math.sqrt(D)
+    o_tc = torch.full((B * T, Hq * D), float("nan"), device=dev, dtype=torch.bfloat16)
+    lse_tc = torch.full((B * Hq * T,), float("nan"), device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops().flash_attn_fwd(q, k, v, o_tc, lse_tc, B, T, Hq, Hk, scale, impl="tc", err=err)
+    o_mma = torch.empty_like(o_tc)
+    lse_mma = torch.empty_like(lse_tc)
+    ops().flash_attn_fwd(q, k, v, o_mma, lse_mma, B, T, Hq, Hk, scale, impl="mma")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    out = ref.causal_attention(q.float().view(B, T, Hq, D), k.float().view(B, T, Hk, D),
+                               v.float().view(B, T, Hk, D), scale)
+    got = o_tc.float().view(B, T, Hq, D)
+    assert torch.isfinite(got).all()
+    assert (got - out).abs().max() < 3e-2 * max(1.0, out.abs().max().item())
+    assert (got - o_mma.float().view(B, T, Hq, D)).abs().max() < 3e-2 * max(1.0, out.abs().max().item())
+    assert torch.isfinite(lse_tc).all()
+    assert torch.allclose(lse_tc, lse_mma, atol=2e-2, rtol=1e-3)
+
+
 @pytest.mark.parametrize("Hq,Hk,bs", [(12, 2, 16), (32, 8, 16), (8, 1, 16), (4, 4, 16), (12, 2, 8)])
 def test_decode_attention_paged(dev, Hq, Hk, bs):
     # bs 16 with up to 8 query heads per kv head runs the tensor-core kernel; bs 8 the CUDA-core one
