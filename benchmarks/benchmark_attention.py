@@ -4,7 +4,7 @@
 The reference's benchmark_attention (turbol_vllm/benchmarks/benchmark_attention.cpp:45-87)
 prints the sizes of a (4, 8, 512, 64) problem and never launches a kernel.
 This one times the framework's causal GQA flash attention (forward on
-tcgen05 and on mma.sync, backward on mma.sync; bf16, head_dim 128) at the
+tcgen05 and on mma.sync, backward likewise; bf16, head_dim 128) at the
 model shapes it serves, against
 PyTorch's scaled_dot_product_attention on the same tensors (a library
 kernel, for comparison only):
@@ -62,10 +62,16 @@ def bench_shape(name, B, T, Hq, Hk, steps):
     scale = 1 / math.sqrt(D)
     fwd = lambda: o.flash_attn_fwd(q, k, v, out, lse, B, T, Hq, Hk, scale, impl="tc")  # noqa: E731
     fwd_mma = lambda: o.flash_attn_fwd(q, k, v, out, lse, B, T, Hq, Hk, scale, impl="mma")  # noqa: E731
+    ws = torch.empty(o.flash_attn_bwd_ws_numel(B, T, Hk), device=dev)
     bwd = lambda: o.flash_attn_bwd(q, k, v, out, dout, lse, delta, dqkv[:, : Hq * D],  # noqa: E731
-                                   dqkv[:, Hq * D:(Hq + Hk) * D], dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale)
+                                   dqkv[:, Hq * D:(Hq + Hk) * D], dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale,
+                                   impl="tc", ws=ws)
+    bwd_mma = lambda: o.flash_attn_bwd(q, k, v, out, dout, lse, delta, dqkv[:, : Hq * D],  # noqa: E731
+                                       dqkv[:, Hq * D:(Hq + Hk) * D], dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale,
+                                       impl="mma")
     t_fm = timed(fwd_mma, steps)
     fwd()
+    t_bm = timed(bwd_mma, steps)
     t_f, t_b = timed(fwd, steps), timed(bwd, steps)
     # PyTorch SDPA on [B, H, T, D] views (GQA by repeating K/V heads)
     qt = q.reshape(B, T, Hq, D).transpose(1, 2).contiguous()
@@ -80,10 +86,10 @@ def bench_shape(name, B, T, Hq, Hk, steps):
            F.scaled_dot_product_attention(qt, kt, vt, is_causal=True).float()).abs().max().item()
     fl = 2.0 * B * Hq * T * T * D
     r = {"shape": name, "B": B, "T": T, "Hq": Hq, "Hk": Hk, "D": D,
-         "fwd_ms": t_f, "fwd_tflops": fl / t_f / 1e9, "fwd_mma_sync_ms": t_fm, "bwd_ms": t_b, "bwd_tflops": 2.5 * fl / t_b / 1e9,
+         "fwd_ms": t_f, "fwd_tflops": fl / t_f / 1e9, "fwd_mma_sync_ms": t_fm, "bwd_mma_sync_ms": t_bm, "bwd_ms": t_b, "bwd_tflops": 2.5 * fl / t_b / 1e9,
          "sdpa_fwd_ms": t_sdpa, "sdpa_bwd_ms": t_sdpa_b, "max_abs_diff_vs_sdpa": err}
     print(f"{name:22s} fwd {t_f * 1e3:8.1f} us {r['fwd_tflops']:6.0f} TF/s (mma.sync {t_fm * 1e3:.1f} us) | bwd {t_b * 1e3:8.1f} us "
-          f"{r['bwd_tflops']:6.0f} TF/s | torch SDPA fwd {t_sdpa * 1e3:8.1f} us bwd {t_sdpa_b * 1e3:8.1f} us "
+          f"{r['bwd_tflops']:6.0f} TF/s (mma.sync {t_bm * 1e3:.1f} us) | torch SDPA fwd {t_sdpa * 1e3:8.1f} us bwd {t_sdpa_b * 1e3:8.1f} us "
           f"| max|diff| {err:.3g}")
     return r
 

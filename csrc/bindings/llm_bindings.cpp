@@ -283,15 +283,41 @@ void register_llm_ops(py::module_& m) {
       },
       py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"), py::arg("B"), py::arg("T"),
       py::arg("Hq"), py::arg("Hk"), py::arg("scale"), py::arg("impl") = "tc", py::arg("err") = py::none());
-  m.def("flash_attn_bwd", [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
-                              at::Tensor lse, at::Tensor delta, at::Tensor dq, at::Tensor dk, at::Tensor dv, int B,
-                              int T, int Hq, int Hk, float scale) {
-    chk(dq.stride(0) == dk.stride(0) && dq.stride(0) == dv.stride(0), "flash_attn_bwd: dq/dk/dv share the stride");
-    cuda_ok(tb_flash_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0),
-                              dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
-                              dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq.stride(0), B, T, Hq, Hk, scale,
-                              turbol::StreamFor(q)),
-            "flash_attn_bwd");
+  m.def(
+      "flash_attn_bwd",
+      [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout, at::Tensor lse, at::Tensor delta,
+          at::Tensor dq, at::Tensor dk, at::Tensor dv, int B, int T, int Hq, int Hk, float scale,
+          const std::string& impl, py::object ws, py::object err) {
+        chk(dq.stride(0) == dk.stride(0) && dq.stride(0) == dv.stride(0), "flash_attn_bwd: dq/dk/dv share the stride");
+        if (impl == "tc") {
+          float* w = nullptr;
+          size_t wb = 0;
+          if (!ws.is_none()) {
+            at::Tensor wt = ws.cast<at::Tensor>();
+            chk(wt.is_cuda() && wt.scalar_type() == at::kFloat && wt.is_contiguous(), "flash_attn_bwd: ws fp32");
+            w = wt.data_ptr<float>();
+            wb = static_cast<size_t>(wt.numel()) * sizeof(float);
+          }
+          int* e = err.is_none() ? nullptr : err.cast<at::Tensor>().data_ptr<int>();
+          cuda_ok(tb_flash_attn_bwd_tc(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(),
+                                       o.stride(0), dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(),
+                                       delta.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                       dq.stride(0), B, T, Hq, Hk, scale, w, wb, e, turbol::StreamFor(q)),
+                  "flash_attn_bwd");
+        } else {
+          chk(impl == "mma", "flash_attn_bwd: impl is 'tc' (tcgen05) or 'mma' (mma.sync)");
+          cuda_ok(tb_flash_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), o.data_ptr(), o.stride(0),
+                                    dout.data_ptr(), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(),
+                                    dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dq.stride(0), B, T, Hq, Hk, scale,
+                                    turbol::StreamFor(q)),
+                  "flash_attn_bwd");
+        }
+      },
+      py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("dout"), py::arg("lse"), py::arg("delta"),
+      py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("B"), py::arg("T"), py::arg("Hq"), py::arg("Hk"),
+      py::arg("scale"), py::arg("impl") = "tc", py::arg("ws") = py::none(), py::arg("err") = py::none());
+  m.def("flash_attn_bwd_ws_numel", [](int B, int T, int Hk) {
+    return static_cast<int64_t>(tb_flash_attn_bwd_ws_bytes(B, T, Hk) / sizeof(float));
   });
 
   m.attr("EPI_NONE") = static_cast<int>(TB_EPI_NONE);

@@ -514,6 +514,15 @@ int tb_flash_attn_fwd(const void* q, const void* k, const void* v, long long ld,
   return static_cast<int>(cudaGetLastError());
 }
 
+int tb_flash_attn_delta(const void* o, long long ldo, const void* dout, long long lddo, float* delta, int B, int T,
+                        int Hq, cudaStream_t s) {
+  if (B <= 0 || T <= 0) return 0;
+  const long long rows = static_cast<long long>(B) * T * Hq;
+  fa_bwd_delta_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
+      static_cast<const bf16*>(o), ldo, static_cast<const bf16*>(dout), lddo, delta, B, T, Hq);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int tb_flash_attn_bwd(const void* q, const void* k, const void* v, long long ld, const void* o, long long ldo,
                       const void* dout, long long lddo, const float* lse, float* delta, void* dq, void* dk, void* dv,
                       long long lddqkv, int B, int T, int Hq, int Hk, float scale, cudaStream_t s) {

@@ -187,6 +187,17 @@ int tb_flash_attn_fwd_tc(const void* q, const void* k, const void* v, long long 
 int tb_flash_attn_bwd(const void* q, const void* k, const void* v, long long ld, const void* o, long long ldo,
                       const void* dout, long long lddo, const float* lse, float* delta, void* dq, void* dk, void* dv,
                       long long lddqkv, int B, int T, int Hq, int Hk, float scale, cudaStream_t s);
+// delta[b, h, t] = sum_d dO[t, h, d] * O[t, h, d] (the backward's row term)
+int tb_flash_attn_delta(const void* o, long long ldo, const void* dout, long long lddo, float* delta, int B, int T,
+                        int Hq, cudaStream_t s);
+// Backward on tcgen05: delta, dK/dV (KV tile outer) and dQ (query tile outer).
+// ws (nullable, tb_flash_attn_bwd_ws_bytes) lets the dK/dV pass split a GQA
+// group over CTAs and sum in fp32; err (nullable) gets site 22/23 on a timeout.
+size_t tb_flash_attn_bwd_ws_bytes(int B, int T, int Hk);
+int tb_flash_attn_bwd_tc(const void* q, const void* k, const void* v, long long ld, const void* o, long long ldo,
+                         const void* dout, long long lddo, const float* lse, float* delta, void* dq, void* dk,
+                         void* dv, long long lddqkv, int B, int T, int Hq, int Hk, float scale, float* ws,
+                         size_t ws_bytes, int* err, cudaStream_t s);
 
 // ---------------- NVLink peer-memory collectives ----------------
 #define TB_MAX_PEERS 8

@@ -54,8 +54,13 @@ def test_rope_roundtrip(dev):
     assert torch.allclose(qkv.float(), orig.float(), atol=5e-2)
 
 
-@pytest.mark.parametrize("B,T,Hq,Hk", [(2, 128, 4, 2), (1, 200, 12, 2), (2, 64, 8, 8)])
-def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
+@pytest.mark.parametrize("impl,use_ws", [("tc", True), ("tc", False), ("mma", False)])
+@pytest.mark.parametrize("B,T,Hq,Hk", [(2, 128, 4, 2), (1, 200, 12, 2), (2, 64, 8, 8), (1, 777, 12, 2),
+                                       (2, 320, 32, 8)])
+def test_flash_attention_fwd_bwd(B, T, Hq, Hk, impl, use_ws, dev):
+    """Forward + backward vs fp32 autograd.  impl 'tc' runs the tcgen05
+    kernels (with a workspace the dK/dV pass splits GQA groups over CTAs and
+    sums in fp32); 'mma' the mma.sync ones."""
     D = 128
     ld = (Hq + 2 * Hk) * D
     qkv = bf(torch.randn(B * T, ld, device=dev) * 0.5)
@@ -63,7 +68,7 @@ def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
     o = torch.empty(B * T, Hq * D, device=dev, dtype=torch.bfloat16)
     lse = torch.empty(B * Hq * T, device=dev)
     scale = 1 / math.sqrt(D)
-    ops().flash_attn_fwd(q, k, v, o, lse, B, T, Hq, Hk, scale)
+    ops().flash_attn_fwd(q, k, v, o, lse, B, T, Hq, Hk, scale, impl=impl)
     qr = q.float().view(B, T, Hq, D).requires_grad_()
     kr = k.float().view(B, T, Hk, D).requires_grad_()
     vr = v.float().view(B, T, Hk, D).requires_grad_()
@@ -72,8 +77,14 @@ def test_flash_attention_fwd_bwd(B, T, Hq, Hk, dev):
     do = bf(torch.randn(B * T, Hq * D, device=dev))
     dqkv = torch.empty_like(qkv)
     delta = torch.empty(B * Hq * T, device=dev)
+    ws = torch.empty(ops().flash_attn_bwd_ws_numel(B, T, Hk), device=dev) if use_ws else None
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    dqkv.fill_(float("nan"))
     ops().flash_attn_bwd(q, k, v, o, do, lse, delta, dqkv[:, : Hq * D], dqkv[:, Hq * D:(Hq + Hk) * D],
-                         dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale)
+                         dqkv[:, (Hq + Hk) * D:], B, T, Hq, Hk, scale, impl=impl, ws=ws,
+                         err=err if impl == "tc" else None)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
     out.backward(do.float().view(B, T, Hq, D))
     for got, exp in ((dqkv[:, : Hq * D], qr.grad), (dqkv[:, Hq * D:(Hq + Hk) * D], kr.grad),
                      (dqkv[:, (Hq + Hk) * D:], vr.grad)):

@@ -305,6 +305,7 @@ class DecoderLM:
         d_attn = self._buf("d_attn", (N, cfg.q_dim))
         d_qkv = self._buf("d_qkv", (N, cfg.qkv_dim))
         delta = self._buf("delta", (B * cfg.n_heads * T,), torch.float32)
+        attn_ws = self._buf("attn_ws", (o.flash_attn_bwd_ws_numel(B, T, cfg.n_kv_heads),), torch.float32)
         for i, a in zip(reversed(self.layers), reversed(saved)):
             P = f"l{i}."
             # ---- MLP
@@ -324,7 +325,7 @@ class DecoderLM:
             dk = d_qkv[:, cfg.q_dim:cfg.q_dim + cfg.kv_dim]
             dv = d_qkv[:, cfg.q_dim + cfg.kv_dim:]
             o.flash_attn_bwd(q, k, v, a["attn"], d_attn, a["lse"], delta, dq, dk, dv, B, T, cfg.n_heads,
-                             cfg.n_kv_heads, scale)
+                             cfg.n_kv_heads, scale, ws=attn_ws)
             o.rope(d_qkv, pos, self.table, cfg.n_heads + cfg.n_kv_heads, D, True)   # inverse rotation
             o.gemm(d_qkv, self.s[P + "wqkv"], dh, False, True)                      # dh1 = dQKV Wqkv
             o.gemm(d_qkv, a["h1"], G[P + "wqkv"], True, True, accumulate=True, split_k=1)  # dWqkv += dQKV^T h1
