@@ -79,6 +79,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Order in which the forward streams K/V tiles through the ring: K_0, then
+// (K_{j+1}, V_j) for every j, so the scores of the next tile can be computed
+// while the softmax of the current one runs.
+__device__ __forceinline__ void fwd_tile_order(int i, int n, bool& is_v, int& j) {
+  if (i == 0) {
+    is_v = false;
+    j = 0;
+    return;
+  }
+  const int t = i - 1;
+  j = t >> 1;
+  is_v = (t & 1) || j + 1 >= n;
+  if (!is_v) j += 1;
+}
+
 __global__ void __launch_bounds__(kThreads, 2)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, bf16* __restrict__ ob, long long ldo,
@@ -89,11 +104,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* q_full = bars;
   uint64_t* ring_full = bars + 1;   // [kSlots]
   uint64_t* ring_empty = bars + 4;  // [kSlots]
-  uint64_t* s_full = bars + 7;
-  uint64_t* p_full = bars + 8;
-  uint64_t* o_full = bars + 9;
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* s_full = bars + 7;  // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* p_empty = bars + 10;
+  uint64_t* o_full = bars + 11;
+  uint64_t* drain = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,8 +125,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], 1);
     }
-    mbar_init(s_full, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
     mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -136,8 +154,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t ph = static_cast<uint32_t>(i / kSlots) & 1u;
       if (!mbar_wait(&ring_empty[slot], ph ^ 1u, abort_flag)) break;
       uint8_t* dst = smem + kOffRing + slot * kTileBytes;
-      const CUtensorMap* m = (i & 1) ? &tmV : &tmK;
-      const int y = row_base + (i >> 1) * BKV;
+      bool is_v;
+      int jt;
+      fwd_tile_order(i, n_kv, is_v, jt);
+      const CUtensorMap* m = is_v ? &tmV : &tmK;
+      const int y = row_base + jt * BKV;
       mbar_arrive_expect_tx(&ring_full[slot], kTileBytes);
       tma_load_2d(dst, m, &ring_full[slot], hk * D, y);
       tma_load_2d(dst + kTileBytes / 2, m, &ring_full[slot], hk * D + 64, y);
@@ -163,37 +184,49 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t sq = smem_u32(smem), sp = smem_u32(smem + kOffP);
     bool ok = mbar_wait(q_full, 0, abort_flag), any = false;
     if (ok) tc_fence_after();
-    for (int j = 0; ok && j < n_kv; ++j) {
-      int i = 2 * j, slot = i % kSlots;
-      if (!mbar_wait(&ring_full[slot], static_cast<uint32_t>(i / kSlots) & 1u, abort_flag)) {
-        ok = false;
-        break;
-      }
+    int ci = 0;  // ring tiles consumed, in the producer's order
+    auto take = [&](uint32_t& saddr, int& slot) -> bool {
+      slot = ci % kSlots;
+      if (!mbar_wait(&ring_full[slot], static_cast<uint32_t>(ci / kSlots) & 1u, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t sk = smem_u32(smem + kOffRing + slot * kTileBytes);
+      saddr = smem_u32(smem + kOffRing + slot * kTileBytes);
+      ++ci;
+      return true;
+    };
+    auto issue_s = [&](int j) -> bool {  // S_j = Q K_j^T into score buffer j & 1
+      uint32_t sk;
+      int slot;
+      if (!take(sk, slot)) return false;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint64_t ad = smem_desc_sw128(sq + (kk >> 2) * (kQBytes / 2) + (kk & 3) * 32, 16, 1024);
         const uint64_t bd = smem_desc_sw128(sk + (kk >> 2) * (kTileBytes / 2) + (kk & 3) * 32, 16, 1024);
-        mma_f16(t_s, ad, bd, id_s, kk > 0 ? 1u : 0u);
+        mma_f16(t_s + 64 * (j & 1), ad, bd, id_s, kk > 0 ? 1u : 0u);
       }
       any = true;
       mma_commit(&ring_empty[slot]);
-      mma_commit(s_full);
+      mma_commit(&s_full[j & 1]);
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    for (int j = 0; ok && j < n_kv; ++j) {
+      // the next tile's scores overlap this tile's softmax (its buffer was read by softmax j-1)
+      if (j + 1 < n_kv && !issue_s(j + 1)) {
+        ok = false;
+        break;
+      }
       // P_j written (and S_j read, O rescaled) by the softmax warpgroup
       if (!mbar_wait(p_full, static_cast<uint32_t>(j) & 1u, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      i = 2 * j + 1;
-      slot = i % kSlots;
-      if (!mbar_wait(&ring_full[slot], static_cast<uint32_t>(i / kSlots) & 1u, abort_flag)) {
+      uint32_t sv;
+      int slot;
+      if (!take(sv, slot)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const uint32_t sv = smem_u32(smem + kOffRing + slot * kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; ++kk) {
         const uint64_t ad = smem_desc_sw128(sp + kk * 32, 16, 1024);
@@ -201,6 +234,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         mma_f16(t_o, ad, bd, id_o, (j > 0 || kk > 0) ? 1u : 0u);
       }
       mma_commit(&ring_empty[slot]);
+      mma_commit(p_empty);
     }
     if (ok) mma_commit(o_full);
     if (any) {
@@ -221,26 +255,31 @@ __global__ void __launch_bounds__(kThreads, 2)
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full, static_cast<uint32_t>(j) & 1u, abort_flag));
+      const uint32_t t_sj = t_s + 64 * (j & 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag));
       if (!ok) break;
       tc_fence_after();
       const int k0 = j * BKV;
       const bool diag = k0 + BKV - 1 > q0;  // a key of this tile may lie past some row of the query tile
       // pass 1: the tile's row max (S is read twice from TMEM rather than held in registers)
-      float mt = -INFINITY;
+      // (four independent max chains: one warp per SM sub-partition leaves little latency hiding)
+      float mx[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mx[e] = -INFINITY;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t sv[32];
-        tmem_ld_x32(t_s + half * 32, sv);
+        tmem_ld_x32(t_sj + half * 32, sv);
         tmem_wait_ld();
         after_wait<32>(sv);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          float x = __uint_as_float(sv[c]) * scale_log2;
+          float x = __uint_as_float(sv[c]);
           if (diag && k0 + half * 32 + c > row) x = -INFINITY;
-          mt = fmaxf(mt, x);
+          mx[c & 3] = fmaxf(mx[c & 3], x);
         }
       }
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
       const bool need = mt > m_ref + kRescaleThreshold;  // always true on the first tile (col 0 <= row)
       float alpha = 1.f;
       if (need) {
@@ -248,8 +287,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         m_ref = mt;
         l *= alpha;
       }
+      if (j > 0) {
+        // P_{j-1} V_{j-1} has finished reading the P tile and accumulating into O
+        ok = __all_sync(0xffffffffu, mbar_wait(p_empty, static_cast<uint32_t>(j - 1) & 1u, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+      }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O_{j-1} is complete (the commit behind s_full covers the previous P.V)
 #pragma unroll 1
         for (int cc = 0; cc < D / 32; ++cc) {
           uint32_t ov[32];
@@ -263,11 +307,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         tmem_wait_st();
       }
       // pass 2: P = exp2(S - m) as bf16 into the swizzled P tile
-      float sum = 0.f;
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t sv[32];
-        tmem_ld_x32(t_s + half * 32, sv);
+        tmem_ld_x32(t_sj + half * 32, sv);
         tmem_wait_ld();
         after_wait<32>(sv);
 #pragma unroll
@@ -276,18 +320,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int col = half * 32 + 8 * c + 2 * e;
-            float x0 = __uint_as_float(sv[8 * c + 2 * e]) * scale_log2;
-            float x1 = __uint_as_float(sv[8 * c + 2 * e + 1]) * scale_log2;
+            float x0 = __uint_as_float(sv[8 * c + 2 * e]) * scale_log2 - m_ref;
+            float x1 = __uint_as_float(sv[8 * c + 2 * e + 1]) * scale_log2 - m_ref;
             if (diag && k0 + col > row) x0 = -INFINITY;
             if (diag && k0 + col + 1 > row) x1 = -INFINITY;
-            const float p0 = ex2(x0 - m_ref), p1 = ex2(x1 - m_ref);
-            sum += p0 + p1;
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            sm[e] += p0 + p1;
             w[e] = pack_bf16(p0, p1);
           }
           *reinterpret_cast<uint4*>(prow + (((half * 4 + c) ^ sw) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      l += sum;
+      l += (sm[0] + sm[1]) + (sm[2] + sm[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -361,11 +405,15 @@ __device__ __forceinline__ void red_add_v4(float* p, float a, float b, float c, 
                : "memory");
 }
 
-// smem layout of the dK/dV pass (offsets from the 1024-aligned base)
-constexpr int kKvOffK = 0, kKvOffV = 32768, kKvOffRing = 65536;  // ring: 2 x (Q 16 KB + dO 16 KB)
-constexpr int kKvOffP = kKvOffRing + 2 * 32768;                   // 2 x 16 KB
-constexpr int kKvOffDS = kKvOffP + 2 * 16384;                     // 2 x 16 KB
-constexpr int kKvOffLsd = kKvOffDS + 2 * 16384;                   // 8 warps x (32 lse2 + 32 delta) floats
+// smem layout of the dK/dV pass (offsets from the 1024-aligned base): the
+// (Q, dO) ring is three steps deep so the loads of step s+2 are in flight
+// while step s runs; P^T and dS^T are single tiles (the elementwise warps of
+// step s+1 write them once the gradient MMAs of step s have read them).
+constexpr int kKvSlots = 3;
+constexpr int kKvOffK = 0, kKvOffV = 32768, kKvOffRing = 65536;  // ring: 3 x (Q 16 KB + dO 16 KB)
+constexpr int kKvOffP = kKvOffRing + kKvSlots * 32768;            // 16 KB
+constexpr int kKvOffDS = kKvOffP + 16384;                         // 16 KB
+constexpr int kKvOffLsd = kKvOffDS + 16384;                       // 8 warps x (32 lse2 + 32 delta) floats
 constexpr int kKvOffBar = kKvOffLsd + 8 * 64 * 4;
 constexpr int kKvSmem = kKvOffBar + 128 + 1024;
 
@@ -380,11 +428,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kKvOffBar);
   uint64_t* kv_full = bars;
-  uint64_t* ring_full = bars + 1;   // [2]
-  uint64_t* ring_empty = bars + 3;  // [2]
-  uint64_t* st_full = bars + 5;     // [2]
-  uint64_t* pd_full = bars + 7;     // [2]
-  uint64_t* pd_empty = bars + 9;    // [2]
+  uint64_t* ring_full = bars + 1;   // [3]
+  uint64_t* ring_empty = bars + 4;  // [3]
+  uint64_t* st_full = bars + 7;     // [2]
+  uint64_t* pd_full = bars + 9;
+  uint64_t* pd_empty = bars + 10;
   uint64_t* acc_full = bars + 11;
   uint64_t* drain = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
@@ -400,13 +448,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKvSlots; ++i) {
       mbar_init(&ring_full[i], 1);
       mbar_init(&ring_empty[i], 1);
-      mbar_init(&st_full[i], 1);
-      mbar_init(&pd_full[i], 8);
-      mbar_init(&pd_empty[i], 1);
     }
+    mbar_init(&st_full[0], 1);
+    mbar_init(&st_full[1], 1);
+    mbar_init(pd_full, 8);
+    mbar_init(pd_empty, 1);
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -431,8 +480,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     int issued = 0;
     for (int s = 0; s < n_steps && !*abort_flag; ++s) {
-      const int slot = s & 1;
-      if (!mbar_wait(&ring_empty[slot], (static_cast<uint32_t>(s >> 1) & 1u) ^ 1u, abort_flag)) break;
+      const int slot = s % kKvSlots;
+      if (!mbar_wait(&ring_empty[slot], (static_cast<uint32_t>(s / kKvSlots) & 1u) ^ 1u, abort_flag)) break;
       const int h = h_first + s / n_q, q0 = (i_lo + s % n_q) * 64;
       uint8_t* dst = smem + kKvOffRing + slot * 32768;
       mbar_arrive_expect_tx(&ring_full[slot], 32768);
@@ -446,9 +495,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const unsigned long long t0 = global_ns();
       while (!mbar_try_wait(kv_full, 0) && global_ns() - t0 < 100000000ull) {
       }
-      for (int s = issued - (issued < 2 ? issued : 2); s < issued; ++s) {
+      for (int s = issued - (issued < kKvSlots ? issued : kKvSlots); s < issued; ++s) {
         const unsigned long long t1 = global_ns();
-        while (!mbar_try_wait(&ring_full[s & 1], static_cast<uint32_t>(s >> 1) & 1u) &&
+        while (!mbar_try_wait(&ring_full[s % kKvSlots], static_cast<uint32_t>(s / kKvSlots) & 1u) &&
                global_ns() - t1 < 100000000ull) {
         }
       }
@@ -460,11 +509,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t sk = smem_u32(smem + kKvOffK), sv = smem_u32(smem + kKvOffV);
     bool ok = mbar_wait(kv_full, 0, abort_flag), any = false;
     auto grads = [&](int t) -> bool {
-      const int bt = t & 1;
-      if (!mbar_wait(&pd_full[bt], static_cast<uint32_t>(t >> 1) & 1u, abort_flag)) return false;
+      const int slot = t % kKvSlots;
+      if (!mbar_wait(pd_full, static_cast<uint32_t>(t) & 1u, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t sq = smem_u32(smem + kKvOffRing + bt * 32768), sdo = sq + 16384;
-      const uint32_t sp = smem_u32(smem + kKvOffP + bt * 16384), sds = smem_u32(smem + kKvOffDS + bt * 16384);
+      const uint32_t sq = smem_u32(smem + kKvOffRing + slot * 32768), sdo = sq + 16384;
+      const uint32_t sp = smem_u32(smem + kKvOffP), sds = smem_u32(smem + kKvOffDS);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
@@ -473,19 +522,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mma_f16(tmem_base + 384, smem_desc_sw128(sds + kk * 32, 16, 1024),
                 smem_desc_sw128(sq + kk * 2048, 8192, 1024), id_g, acc);
       }
-      mma_commit(&ring_empty[bt]);
-      mma_commit(&pd_empty[bt]);
+      mma_commit(&ring_empty[slot]);
+      mma_commit(pd_empty);
       return true;
     };
     if (ok) tc_fence_after();
     for (int s = 0; ok && s < n_steps; ++s) {
-      const int bs = s & 1;
-      if (!mbar_wait(&ring_full[bs], static_cast<uint32_t>(s >> 1) & 1u, abort_flag)) {
+      const int bs = s & 1, slot = s % kKvSlots;
+      if (!mbar_wait(&ring_full[slot], static_cast<uint32_t>(s / kKvSlots) & 1u, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sq = smem_u32(smem + kKvOffRing + bs * 32768), sdo = sq + 16384;
+      const uint32_t sq = smem_u32(smem + kKvOffRing + slot * 32768), sdo = sq + 16384;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t ao = (kk >> 2) * 16384 + (kk & 3) * 32, bo = (kk >> 2) * 8192 + (kk & 3) * 32;
@@ -513,18 +562,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     float* L = reinterpret_cast<float*>(smem + kKvOffLsd) + (warp - 4) * 64;
     bool ok = true;
+    // lse / delta of this warp's 32 query columns, loaded one step ahead
+    auto fetch = [&](int s, float& fl, float& fd) {
+      const int h = h_first + s / n_q, q = (i_lo + s % n_q) * 64 + half * 32 + lane;
+      const long long idx = (static_cast<long long>(b) * Hq + h) * T + q;
+      fl = q < T ? lse[idx] * l2e : __int_as_float(0x7f800000);
+      fd = q < T ? delta[idx] : 0.f;
+    };
+    float nl = 0.f, nd = 0.f;
+    if (n_steps > 0) fetch(0, nl, nd);
     for (int s = 0; s < n_steps; ++s) {
       const int bs = s & 1;
-      const int h = h_first + s / n_q, q0 = (i_lo + s % n_q) * 64;
-      // this warp's 32 query columns: lse (log2 units) at L[0, 32), delta at L[32, 64)
+      const int q0 = (i_lo + s % n_q) * 64;
+      // L[0, 32): lse in log2 units, L[32, 64): delta
       __syncwarp();
-      {
-        const int q = q0 + half * 32 + lane;
-        const long long idx = (static_cast<long long>(b) * Hq + h) * T + q;
-        L[lane] = q < T ? lse[idx] * l2e : __int_as_float(0x7f800000);
-        L[32 + lane] = q < T ? delta[idx] : 0.f;
-      }
+      L[lane] = nl;
+      L[32 + lane] = nd;
       __syncwarp();
+      if (s + 1 < n_steps) fetch(s + 1, nl, nd);
       ok = __all_sync(0xffffffffu, mbar_wait(&st_full[bs], static_cast<uint32_t>(s >> 1) & 1u, abort_flag));
       if (!ok) break;
       tc_fence_after();
@@ -548,11 +603,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         pw[c >> 1] = pack_bf16(p0, p1);
         dw[c >> 1] = pack_bf16(d0, d1);
       }
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(&pd_empty[bs], (static_cast<uint32_t>(s >> 1) & 1u) ^ 1u, abort_flag));
+      // the gradient MMAs of step s-1 have read the P^T / dS^T tiles
+      ok = __all_sync(0xffffffffu, mbar_wait(pd_empty, (static_cast<uint32_t>(s) & 1u) ^ 1u, abort_flag));
       if (!ok) break;
-      uint8_t* prow = smem + kKvOffP + bs * 16384 + r * 128;
-      uint8_t* drow = smem + kKvOffDS + bs * 16384 + r * 128;
+      uint8_t* prow = smem + kKvOffP + r * 128;
+      uint8_t* drow = smem + kKvOffDS + r * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int chunk = ((half * 4 + c) ^ sw) << 4;
@@ -562,7 +617,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pd_full[bs]);
+      if (lane == 0) mbar_arrive(pd_full);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort_flag));
     if (ok) {
