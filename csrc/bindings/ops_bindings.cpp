@@ -332,6 +332,39 @@ void register_kernel_ops(py::module_& m) {
             "colsum_bf16");
   }, py::arg("x"), py::arg("out"), py::arg("accumulate") = false);
 
+  m.def(
+      "lin_gauss_act",
+      [](at::Tensor x, at::Tensor params, at::Tensor act, at::Tensor logp, int O, int A, float stdv, uint64_t seed,
+         uint32_t counter) {
+        need(x, at::kFloat, "x");
+        need(params, at::kFloat, "params");
+        need(act, at::kFloat, "act");
+        need(logp, at::kFloat, "logp");
+        TB_CHECK(x.numel() % O == 0 && act.numel() == x.numel() / O * A && logp.numel() == x.numel() / O,
+                 "lin_gauss_act: shapes");
+        cuda_ok(tb_lin_gauss_act(x.data_ptr<float>(), params.data_ptr<float>(), act.data_ptr<float>(),
+                                 logp.data_ptr<float>(), static_cast<int>(x.numel() / O), O, A, stdv, seed, counter,
+                                 stream_of(x)),
+                "lin_gauss_act");
+      },
+      py::arg("x"), py::arg("params"), py::arg("act"), py::arg("logp"), py::arg("O"), py::arg("A"), py::arg("std"),
+      py::arg("seed"), py::arg("counter"));
+  m.def(
+      "lin_gauss_grad",
+      [](at::Tensor batch, at::Tensor params, at::Tensor grad, int O, int A, float stdv, float clip, float vf_coef,
+         bool has_old) {
+        need(batch, at::kFloat, "batch");
+        need(params, at::kFloat, "params");
+        need(grad, at::kFloat, "grad");
+        TB_CHECK(batch.dim() == 2, "lin_gauss_grad: batch [N, row]");
+        cuda_ok(tb_lin_gauss_grad(batch.data_ptr<float>(), static_cast<int>(batch.size(1)), params.data_ptr<float>(),
+                                  grad.data_ptr<float>(), static_cast<int>(batch.size(0)), O, A, stdv, clip, vf_coef,
+                                  has_old ? 1 : 0, stream_of(batch)),
+                "lin_gauss_grad");
+      },
+      py::arg("batch"), py::arg("params"), py::arg("grad"), py::arg("O"), py::arg("A"), py::arg("std"),
+      py::arg("clip"), py::arg("vf_coef"), py::arg("has_old"));
+
   m.def("dense_k8_fwd", [](at::Tensor x, at::Tensor W, py::object bias, at::Tensor y, bool tanh_act) {
     TB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(1) == 8 && x.stride(1) == 1,
              "dense_k8_fwd: x bf16 [M, 8]");

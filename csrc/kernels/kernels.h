@@ -80,6 +80,13 @@ int tb_ppo_loss_padded(const float* logits, int ldl, int A, const float* value, 
 int tb_colsum_bf16(const void* x, long long ld, int rows, int cols, float* out, int accumulate, cudaStream_t s);
 // First MLP layer with 8 (padded) input features: y = act(x . W^T + b), act 0
 // none / 1 tanh; x bf16 [M, 8], W bf16 [N, 8] (N % 8 == 0, N <= 1024), y bf16.
+// Linear Gaussian actor-critic (params: W_a [A, O], b_a [A], W_c [O], b_c):
+// sampling with log-density, and the PPO + value-loss gradient accumulated
+// into grad (caller zeroes it).  O <= 64, A <= 16.
+int tb_lin_gauss_act(const float* x, const float* params, float* act, float* logp, int N, int O, int A, float stdv,
+                     uint64_t seed, uint32_t counter, cudaStream_t s);
+int tb_lin_gauss_grad(const float* batch, int row_w, const float* params, float* grad, int N, int O, int A,
+                      float stdv, float clip, float vf_coef, int has_old, cudaStream_t s);
 int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
                     int N, int act, cudaStream_t s);
 // dW[N, 8] (fp32) = (or += with accumulate) dz[M, N]^T . x[M, 8] (bf16 inputs).

@@ -133,3 +133,41 @@ def test_ppo_gpu_learns(graphs, dev):
     tr.release_graphs()
     assert m["mean_return"] > 2 * first and m["mean_return"] > 80, (first, m)
     assert 0 <= m["clipfrac"] <= 1 and m["entropy"] > 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("has_old", [False, True])
+def test_policy_engine_fused_linear_gaussian_matches_autograd(has_old, dev):
+    """The fused act / gradient kernels of the linear Gaussian model give the
+    same update as the autograd path, and consistent samples."""
+    O, A, N = 16, 4, 300
+    fused = turbol.PolicyEngine(obs_dim=O, act_dim=A, device=dev, seed=3)
+    eager = turbol.PolicyEngine(obs_dim=O, act_dim=A, device=dev, seed=3)
+    fused.initialize()
+    eager.initialize()
+    eager._fused = lambda: False
+    assert fused._fused()
+    g = torch.Generator().manual_seed(5)
+    obs = torch.randn(N, O, generator=g)
+    act = (torch.rand(N, A, generator=g) * 2 - 1) * 0.9
+    adv, ret = torch.randn(N, 1, generator=g), torch.randn(N, 1, generator=g)
+    cols = [obs, act, adv, ret]
+    if has_old:
+        cols.append(torch.randn(N, 1, generator=g) * 0.3 - 4.0)
+    batch = torch.cat(cols, 1).to(dev)
+    for _ in range(3):
+        assert fused.update(batch).ok() and eager.update(batch).ok()
+    torch.cuda.synchronize()
+    assert torch.allclose(fused.net.fp.flat, eager.net.fp.flat, atol=2e-5, rtol=1e-4), \
+        (fused.net.fp.flat - eager.net.fp.flat).abs().max()
+    x = torch.randn(4096, O, device=dev)
+    a, lp = fused.act(x)
+    assert a.shape == (4096, A) and lp.shape == (4096,)
+    assert float(a.abs().max()) <= 1.0
+    mean = fused.net.actor(x)
+    assert torch.allclose(lp, fused.net.gaussian_logprob(mean, a), atol=1e-4, rtol=1e-4)
+    # the noise is standard normal where no clamp applies
+    z = ((a - mean) / fused.std)[(a.abs() < 0.999)]
+    assert abs(float(z.mean())) < 0.05 and abs(float(z.std()) - 1.0) < 0.05
+    a2, _ = fused.act(x)
+    assert not torch.equal(a, a2)

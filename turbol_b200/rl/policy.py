@@ -15,6 +15,11 @@ Here:
     without it the ratio is 1 and the gradient equals the reference's
     policy-gradient loss;
   * parameters live in one flat buffer updated by the fused Adam kernel;
+  * on a GPU the reference's model (linear Gaussian, ``hidden=()``) acts and
+    computes its gradient in one fused kernel each (``lin_gauss_act`` /
+    ``lin_gauss_grad``: Philox noise, clipped-PPO + value loss, block-reduced
+    parameter gradients), so a step is four launches instead of an autograd
+    graph;
   * ``forward(obs)`` without out-parameters returns ``(action, logprob)``,
     the form the reference README documents (README.md:149).
 """
@@ -51,6 +56,7 @@ class PolicyEngine:
         self.net: Optional[ActorCritic] = None
         self.opt: Optional[FusedAdam] = None
         self._gen = None
+        self._calls = 0  # Philox counter of the fused sampler
 
     # -------------------------------------------------------------- lifecycle
     def initialize(self):
@@ -65,6 +71,11 @@ class PolicyEngine:
         if self.net is None:
             raise RuntimeError("PolicyEngine not initialized")
 
+    def _fused(self) -> bool:
+        """The fused kernels serve the linear Gaussian model on a GPU."""
+        return (self.device.type == "cuda" and not self.hidden and not self.discrete and self.obs_dim <= 64
+                and self.act_dim <= 16)
+
     # -------------------------------------------------------------- acting
     @torch.no_grad()
     def act(self, obs: torch.Tensor):
@@ -76,6 +87,15 @@ class PolicyEngine:
             logp_all = F.log_softmax(logits, -1)
             a = torch.multinomial(logp_all.exp(), 1, generator=self._gen).squeeze(1)
             return a.to(torch.int32), logp_all.gather(1, a[:, None]).squeeze(1)
+        if self._fused():
+            from .._native import ops as _ops
+            x = obs.reshape(-1, self.obs_dim).contiguous()
+            a = torch.empty(x.shape[0], self.act_dim, device=self.device)
+            lp = torch.empty(x.shape[0], device=self.device)
+            self._calls += 1
+            _ops().lin_gauss_act(x, self.net.fp.flat, a, lp, self.obs_dim, self.act_dim, self.std,
+                                 self.seed + 12345, self._calls & 0xFFFFFFFF)
+            return a, lp
         mean = self.net.actor(obs)
         noise = torch.randn(mean.shape, device=self.device, generator=self._gen)
         a = (mean + self.std * noise).clamp(-1.0, 1.0)
@@ -116,6 +136,13 @@ class PolicyEngine:
             raise ValueError("batch size must be a multiple of obs+act+adv+ret(+old_logp)")
         has_old = b.dim() == 2 and b.shape[1] == row + 1
         b = b.reshape(-1, row + 1 if has_old else row)
+        if self._fused():
+            from .._native import ops as _ops
+            self.net.fp.grad.zero_()
+            _ops().lin_gauss_grad(b.contiguous(), self.net.fp.flat, self.net.fp.grad, self.obs_dim, self.act_dim,
+                                  self.std, self.clip, self.vf_coef, has_old)
+            self.opt.step()
+            return _core().Status()
         obs = b[:, : self.obs_dim]
         act = b[:, self.obs_dim:self.obs_dim + aw]
         adv = b[:, self.obs_dim + aw]
