@@ -8,8 +8,8 @@ step.  Prints one JSON line: train tokens/s = 512 * 768 tokens / step time,
 with the rollout / reward+reference / train phase times.
 
   python benchmarks/bench_grpo.py [--steps K] [--warmup W] [--prompts P] [--tiny]
-  torchrun --nproc-per-node N benchmarks/bench_grpo.py --gpus N [--dp fused|nccl]   (data parallel,
-      --prompts per GPU; tokens/s is the whole job's)
+  torchrun --nproc-per-node N benchmarks/bench_grpo.py --gpus N [--dp fused|nccl] [--tp T [--tp-mode M]]
+      (data parallel: --prompts per GPU; with --tp, per tensor-parallel group; tokens/s is the whole job's)
 """
 import argparse
 import json
@@ -24,7 +24,9 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1, help="data-parallel ranks (launch with torchrun for > 1)")
     ap.add_argument("--dp", choices=["fused", "nccl"], default="fused")
-    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel rollout group size (training stays data parallel)")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size")
+    ap.add_argument("--tp-mode", choices=["train", "rollout"], default="train",
+                    help="train: TP rollout and TP training (TP x DP); rollout: TP rollout, data-parallel training")
     ap.add_argument("--steps", type=int, default=2)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--prompts", type=int, default=64, help="prompts per rank")
@@ -58,7 +60,7 @@ def main():
                      micro_batch=a.micro_batch)
     if a.tp > 1 and (world < 2 or world % a.tp):
         raise SystemExit("--tp needs a world size that is a multiple of it")
-    tr = GRPOTrainer(cfg, str(dev), dp=dp, tp=a.tp)
+    tr = GRPOTrainer(cfg, str(dev), dp=dp, tp=a.tp, tp_mode=a.tp_mode)
     for _ in range(a.warmup):
         tr.step()
     times, last = [], None
@@ -87,7 +89,8 @@ def main():
                "config": {"model": "qwen2-1.5b-shape" if not a.tiny else "tiny", "prompts_per_group": cfg.num_prompts,
                           "group": cfg.group_size, "prompt_len": cfg.prompt_len, "response_len": cfg.response_len,
                           "micro_batch": cfg.micro_batch, "params": cfg.model.param_count(),
-                          "parallelism": (f"tp{a.tp}xdp{groups} rollout, dp{world} training" if a.tp > 1
+                          "parallelism": ((f"tp{a.tp}xdp{groups} rollout and training" if a.tp_mode == "train"
+                                           else f"tp{a.tp}xdp{groups} rollout, dp{world} training") if a.tp > 1
                                           else f"dp{world}") + (f" ({dp})" if world > 1 else "")},
                "timing": "CUDA events around each step, max over ranks",
                "reward_mean": last["reward_mean"], "kl": last["kl"],

@@ -8,7 +8,9 @@ responses per step, pipeline micro-batches of 4 sequences (8 micro-batches,
 1F1B over NCCL send/recv), weights synced from the trainer stages to every
 rank's rollout copy before each step.
 
-    torchrun --nproc-per-node N benchmarks/bench_rlhf_pp.py --gpus N [--steps K] [--warmup W] [--tiny]
+    torchrun --nproc-per-node N benchmarks/bench_rlhf_pp.py --gpus N [--tp T] [--steps K] [--warmup W] [--tiny]
+
+With --tp T the N ranks form N / T pipeline stages of T tensor-parallel ranks.
 
 Prints one JSON line: train tokens/s = 32 * 1536 / step time (CUDA events,
 max over ranks), with the phase times.
@@ -31,6 +33,7 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=512)
     ap.add_argument("--response-len", type=int, default=1024)
     ap.add_argument("--micro-batch", type=int, default=4)
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel ranks per pipeline stage (PP x TP)")
     ap.add_argument("--tiny", action="store_true")
     a = ap.parse_args()
     import torch
@@ -52,7 +55,7 @@ def main():
     rank = dist.get_rank()
     cfg = RLHFConfig(model=LMConfig.tiny(n_layers=4) if a.tiny else LMConfig.llama3_8b(), num_prompts=a.prompts,
                      prompt_len=a.prompt_len, response_len=a.response_len, micro_batch=a.micro_batch)
-    tr = PPORLHFTrainer(cfg, dev)
+    tr = PPORLHFTrainer(cfg, dev, tp=a.tp)
     for _ in range(a.warmup):
         tr.step()
     times, last = [], None
@@ -76,7 +79,8 @@ def main():
             "phases_s": {k: last[k] for k in ("sync_s", "rollout_s", "score_s", "train_s")},
             "config": {"model": "llama3-8b-shape" if not a.tiny else "tiny", "prompts": cfg.num_prompts,
                        "prompt_len": cfg.prompt_len, "response_len": cfg.response_len,
-                       "micro_batch": cfg.micro_batch, "parallelism": f"pp{world} (1F1B, NCCL p2p)",
+                       "micro_batch": cfg.micro_batch, "parallelism": f"pp{world // a.tp} (1F1B, NCCL p2p)" + (
+                           f" x tp{a.tp} (fused AG-GEMM / GEMM-RS)" if a.tp > 1 else ""),
                        "params": cfg.model.param_count()},
             "timing": "CUDA events around each step, max over ranks",
             "peak_mem_gb": torch.cuda.max_memory_allocated(dev) / 2**30}), flush=True)

@@ -123,7 +123,7 @@ void register_comm_ops(py::module_& m) {
       .def("tp_ag_gemm",
            [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr,
               at::Tensor shard, at::Tensor W, at::Tensor out, bool b_mn, py::object bias, py::object aux, int epi,
-              int bn) {
+              int bn, py::object gather_out) {
              TbGemmArgs a = tp_gemm_args(shard, W, b_mn, bn);
              const int rows = static_cast<int>(shard.size(0));
              a.M = rows * p.world();
@@ -145,12 +145,21 @@ void register_comm_ops(py::module_& m) {
                a.ld_aux = x.stride(0);
              }
              TbTpComm c = tp_comm(p, hdr_off, data_off, parity_bytes, rows, ctr, false);
+             at::Tensor g;
+             if (!gather_out.is_none()) {
+               g = gather_out.cast<at::Tensor>();
+               if (!g.is_cuda() || g.scalar_type() != at::kBFloat16 || g.dim() != 2 || g.stride(1) != 1 ||
+                   g.size(0) != a.M || g.size(1) != a.K)
+                 throw std::invalid_argument("tp_ag_gemm: gather_out must be bf16 [world * rows, K]");
+               c.gather_out = g.data_ptr();
+               c.ld_gather = g.stride(0);
+             }
              a.error = c.err;
              cuda_ok(tb_tp_ag_gemm(&c, &a, cur_stream(p.device())), "tp_ag_gemm");
            },
            py::arg("hdr_off"), py::arg("data_off"), py::arg("parity_bytes"), py::arg("ctr"), py::arg("shard"),
            py::arg("W"), py::arg("out"), py::arg("b_mn") = false, py::arg("bias") = py::none(),
-           py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0)
+           py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("gather_out") = py::none())
       // GEMM -> reduce-scatter: out[M / world, N] = rows of sum_r(A_r . W_r^T) (+ bias) (+ residual)
       .def("tp_gemm_rs",
            [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr, at::Tensor A,

@@ -62,6 +62,8 @@ struct TpArgs {
   long long parity_bytes;          // bytes per parity half of a data region
   const __nv_bfloat16* shard;      // AG: this rank's rows [Mloc, K]
   long long ld_shard;
+  __nv_bfloat16* gather_out;       // AG, optional: the gathered A [M, K] is also written here
+  long long ld_gather;
   int* err;
   unsigned long long* trace;  // optional [grid][8] timestamps (diagnostics)
 };
@@ -878,6 +880,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) tmem_dealloc(tmem_base, 2 * BN);
   if (threadIdx.x == 0 && *abort_flag && p.error) atomicCAS(p.error, 0, TB_GEMM_ERR_TIMEOUT);  // keeps a site code
   if constexpr (TP == 1) {
+    if (p.tp.gather_out != nullptr) {
+      // Copy-out of the gathered A (a training backward needs it for the weight
+      // gradient): each warp copies whole push units, own rows from the shard,
+      // remote rows from this rank's staging once the unit's arrivals are
+      // complete.  It runs before this CTA counts itself done, so no peer can
+      // refill this parity's staging underneath it.
+      const int W = p.tp.world, r = p.tp.rank, K = p.K;
+      const long long vpr = K / 8, T = static_cast<long long>(mloc) * vpr;
+      const long long T_all = (W - 1) * T, nw = 2ll * gridDim.x;
+      constexpr int kWarps = kThreads / 32;
+      const int units = p.M / kTpSubRows;
+      const __nv_bfloat16* staged =
+          reinterpret_cast<const __nv_bfloat16*>(p.tp.data[r] + parity * p.tp.parity_bytes);
+      for (int u = blockIdx.x * kWarps + warp; u < units; u += gridDim.x * kWarps) {
+        int go = lane == 0 ? (*abort_flag ? 0 : 1) : 0;
+        const int row0 = u * kTpSubRows, src = row0 / mloc;
+        const __nv_bfloat16* from = staged + static_cast<long long>(row0) * K;
+        long long ld = K;
+        if (src == r) {
+          from = p.tp.shard + static_cast<long long>(row0 - r * mloc) * p.tp.ld_shard;
+          ld = p.tp.ld_shard;
+        } else if (lane == 0 && go) {
+          const int sub = (row0 - src * mloc) / kTpSubRows;
+          const int pi = r < src ? r : r - 1;  // this rank's index among src's peers
+          const long long lo = pi * T + static_cast<long long>(sub) * kTpSubRows * vpr;
+          const long long hi = lo + kTpSubRows * vpr - 1;
+          const unsigned need = static_cast<unsigned>(push_worker_of(hi, nw, T_all) - push_worker_of(lo, nw, T_all) + 1);
+          go = tp_wait_geq(&p.tp.hdr[r]->ready[parity][src][sub], need, p.tp.err, 15, abort_flag) ? 1 : 0;
+        }
+        if (!__shfl_sync(0xffffffffu, go, 0)) break;
+        for (long long e = lane; e < kTpSubRows * vpr; e += 32) {
+          const long long i = e / vpr, c = e - i * vpr;
+          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(from + i * ld + c * 8));
+          *reinterpret_cast<uint4*>(p.tp.gather_out + (row0 + i) * p.tp.ld_gather + c * 8) = v;
+        }
+      }
+      __syncthreads();
+    }
     if (threadIdx.x == 0) {
       // the last CTA: every CTA has finished reading staging -> tell the peers
       __threadfence();
@@ -1175,6 +1215,8 @@ bool fill_tp(TpArgs* tp, const TbTpComm* c) {
   tp->parity_bytes = c->parity_bytes;
   tp->err = c->err;
   tp->trace = g_tp_trace;
+  tp->gather_out = static_cast<__nv_bfloat16*>(c->gather_out);
+  tp->ld_gather = c->ld_gather;
   return true;
 }
 
@@ -1300,7 +1342,8 @@ int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t stream) {
   if (a->a_mn || a->K <= 0 || a->K % 8 || a->lda % 8 || a->ldb % 8 || mloc % BM || a->M != W * mloc ||
       mloc / kTpSubRows > kTpMaxSub || a->workspace || a->colsum || a->c_accumulate ||
       c->parity_bytes < 2ll * a->M * a->K || c->parity_bytes % 16 || (reinterpret_cast<uintptr_t>(a->A) & 15) ||
-      (reinterpret_cast<uintptr_t>(a->B) & 15))
+      (reinterpret_cast<uintptr_t>(a->B) & 15) ||
+      (c->gather_out && ((reinterpret_cast<uintptr_t>(c->gather_out) & 15) || c->ld_gather % 8 || c->ld_gather < a->K)))
     return static_cast<int>(cudaErrorInvalidValue);
   const Plan pl = make_plan(a->M, a->N, a->K, a->bn_hint, 1, false, 0);
   const int BN = pl.BN;

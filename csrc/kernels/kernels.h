@@ -233,12 +233,17 @@ typedef struct {
   long long parity_bytes;          // bytes of one parity half of a data region
   int* err;                        // device error word (a nonzero site after a timed-out wait)
   unsigned* rs_target;             // reduce-scatter only: device [2] arrival targets, zero-initialized
+  void* gather_out;                // all-gather only, optional: bf16 [M, K] receives the gathered A
+  long long ld_gather;             // its row stride (elements, a multiple of 8)
 } TbTpComm;
 size_t tb_tp_header_bytes(void);
 // C[M, N] = gather_rows(A) . B^T with A this rank's rows [rows_per_rank, K]
 // (a->A, a->lda) and M = world * rows_per_rank; the other ranks' rows arrive by
 // peer stores into this rank's data region (needs 2 * M * K * 2 bytes) while
 // the tiles of the local rows are computed.  Epilogues as tb_gemm_bf16.
+// With c->gather_out set, the gathered A [M, K] is also written there (for the
+// weight gradient of a column-parallel layer, or of a row-parallel layer's
+// backward), at the end of the same kernel.
 int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t s);
 // out[rows_per_rank, N] = (sum over ranks of A_r . B_r^T)[this rank's rows]
 // (+ bias) (+ residual): each GEMM tile is stored (bf16) into the receive slot

@@ -30,3 +30,15 @@ def test_tp_model_two_gpus():
            os.path.join(HERE, "tp_llm_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=500)
     assert r.returncode == 0 and "TP_LLM_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+
+
+def test_tp_training_two_gpus():
+    """TP forward + backward == single-GPU gradients; GRPO with TP training."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29541",
+           os.path.join(HERE, "tp_train_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=500)
+    assert r.returncode == 0 and "TP_TRAIN_WORKER_OK" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]

@@ -72,8 +72,9 @@ class FusedDataParallelAdam:
         self.scale = 1.0 / self.world
 
     def broadcast_params(self, src: int = 0):
-        """Makes every rank start from rank src's weights."""
-        dist.broadcast(self.param, src=src, group=self.pb.group)
+        """Makes every rank start from the weights of rank ``src`` of the group."""
+        g = self.pb.group
+        dist.broadcast(self.param, src=dist.get_global_rank(g, src) if g is not None else src, group=g)
         self.shadow.copy_(self.param)
         torch.cuda.synchronize()
 

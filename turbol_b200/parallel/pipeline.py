@@ -11,7 +11,8 @@ Model Training on GPU Clusters Using Megatron-LM", SC'21): each stage does
 one backward, then drains the remaining backwards, so at most
 ``num_stages - stage`` micro-batches of activations are alive per stage.
 Activations go forward and their gradients backward with
-``torch.distributed`` NCCL send/recv; a send to the next stage and the receive
+``torch.distributed`` NCCL send/recv (with tensor parallelism inside the
+stages, every rank sends its rows to the same TP rank of the next stage); a send to the next stage and the receive
 from it are posted as one batched operation so the two directions never wait
 on each other, and NCCL runs them on its own stream, overlapped with the next
 micro-batch's compute.
@@ -43,12 +44,26 @@ class PipelineStage:
     VH_ROWS = 8  # the value head is a [1, H] linear layer stored as 8 rows (tile-friendly); row 0 is used
 
     def __init__(self, cfg: LMConfig, stage: int, num_stages: int, device, seed: int = 0, value_head: bool = False,
-                 lr: float = 1e-5, betas=(0.9, 0.95)):
+                 lr: float = 1e-5, betas=(0.9, 0.95), tp_comm=None):
+        """tp_comm: a :class:`TensorParallelComm` over this stage's
+        tensor-parallel group; the stage then holds this rank's shard of its
+        layers (:class:`TPTrainLM`) and its micro-batch rows are split over the
+        group (each rank exchanges its rows with the same TP rank of the
+        neighbouring stages)."""
         self.cfg, self.stage, self.num_stages = cfg, stage, num_stages
         self.first, self.last = stage == 0, stage == num_stages - 1
         self.device = torch.device(device)
-        self.model = DecoderLM(cfg, self.device, layers=stage_layers(cfg.n_layers, num_stages, stage),
-                               embed=self.first, head=self.last, seed=seed + 1009 * stage)
+        self.tp_comm = tp_comm
+        self.tp = tp_comm.world if tp_comm is not None else 1
+        base = DecoderLM(cfg, self.device, layers=stage_layers(cfg.n_layers, num_stages, stage),
+                         embed=self.first, head=self.last, seed=seed + 1009 * stage, master=tp_comm is None)
+        if tp_comm is not None:
+            from ..models.tp_llm import TPTrainLM
+
+            self.model = TPTrainLM(base, tp_comm)
+            del base
+        else:
+            self.model = base
         self.opt = FusedAdam(self.model.flat, self.model.grad, lr=lr, betas=betas, shadow=self.model.shadow)
         self.value_head = value_head and self.last
         if self.value_head:
@@ -68,6 +83,9 @@ class PipelineStage:
     @torch.no_grad()
     def load_from_full(self, full: DecoderLM):
         """Copies this stage's tensors (by name) from a full model (fp32 when it has master weights)."""
+        if self.tp > 1:
+            self.model.load_from(full)
+            return
         src = full.p if full.flat is not None else full.s
         for name in self.model.offsets:
             self.model.p[name].copy_(src[name])
@@ -79,6 +97,10 @@ class PipelineStage:
             self.vh_grad.zero_()
 
     def step(self, grad_scale: float = 1.0):
+        if self.tp > 1:  # replicated parameters saw only this rank's rows
+            self.model.reduce_replicated_grads()
+            if self.value_head:
+                dist.all_reduce(self.vh_grad, group=self.tp_comm.group)
         self.opt.step(grad_scale)
         if self.value_head:
             self.vh_opt.step(grad_scale)
@@ -239,6 +261,8 @@ def set_micro_geometry(B: int, T: int, pos: torch.Tensor):
 
 def stage_forward(stage: PipelineStage, i: int, x_in: torch.Tensor, save: bool):
     B, T, pos = _GEOM["B"], _GEOM["T"], _GEOM["pos"]
+    if getattr(stage, "tp", 1) > 1:
+        return stage.model.forward_train(x_in, B, T, pos, save=save)
     return stage.model.forward(x_in, B, T, pos, save=save)
 
 

@@ -69,16 +69,22 @@ class GRPOTrainer:
     of the gradient + local fused Adam; the baseline).  With data parallelism
     ``cfg.num_prompts`` is per rank and every rank samples its own prompts.
 
-    tp > 1 (with dp over all ranks): the rollout runs tensor-parallel over
-    groups of ``tp`` consecutive ranks (TPDecoderLM + TPLLMGenerator on the
-    fused all-gather->GEMM / GEMM->reduce-scatter kernels); the ranks of a
-    group generate ``cfg.num_prompts`` prompts together and each trains on its
-    1/tp share of the group's sequences; after the optimizer step every rank
-    re-slices its rollout shard from the updated weights (the trainer ->
-    rollout weight sync)."""
+    tp > 1: groups of ``tp`` consecutive ranks generate ``cfg.num_prompts``
+    prompts together with a tensor-parallel rollout (TPLLMGenerator on the
+    fused all-gather->GEMM / GEMM->reduce-scatter kernels).  ``tp_mode``:
+
+    * "train" (default): training is tensor parallel too (TPTrainLM: each rank
+      owns 1/tp of every projection, forward and backward on the fused
+      kernels); the TP group trains on all of its sequences, each micro-batch
+      split by rows over the ranks; data parallelism (``dp``) runs over the
+      ranks that hold the same shard (TP x DP).  Rollout and trainer share the
+      weights, so the trainer -> rollout sync is free.
+    * "rollout": every rank keeps the full model and trains data parallel on
+      its 1/tp share of the group's sequences; after the optimizer step every
+      rank re-slices its rollout shard from the updated weights."""
 
     def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None, dp: str = "none", group=None,
-                 tp: int = 1):
+                 tp: int = 1, tp_mode: str = "train"):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dp, self.group = dp, group
@@ -87,8 +93,15 @@ class GRPOTrainer:
             import torch.distributed as dist
 
             self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
-        self.model = DecoderLM(cfg.model, self.device, seed=cfg.seed)
+        self.tp, self.tp_mode = tp, tp_mode if tp > 1 else "none"
+        self.tp_rank, self.group_index = 0, self.rank
         self.grad_sync = None
+        if tp > 1 and tp_mode == "train":
+            self._init_tp_train(cfg, dp)
+            return
+        if tp > 1 and tp_mode != "rollout":
+            raise ValueError(f"unknown tensor-parallel mode {tp_mode!r}")
+        self.model = DecoderLM(cfg.model, self.device, seed=cfg.seed)
         if dp == "fused":
             from ..parallel.peer import FusedDataParallelAdam
 
@@ -109,8 +122,6 @@ class GRPOTrainer:
             elif dp != "none":
                 raise ValueError(f"unknown data-parallel mode {dp!r}")
         self.ref = self.model.frozen_copy()
-        self.tp = tp
-        self.tp_rank, self.group_index = 0, self.rank
         if tp > 1:
             from ..models.tp_llm import TPDecoderLM
             from ..parallel.dist import build_mesh
@@ -128,6 +139,53 @@ class GRPOTrainer:
             self.gen = TPLLMGenerator(self.tpm, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.group_index)
         else:
             self.gen = LLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.rank)
+        self.stats = torch.zeros(4, device=self.device)
+        self.step_count = 0
+        self.last_times = {}
+
+    def _init_tp_train(self, cfg: GRPOConfig, dp: str):
+        """TP x DP training: the model is this rank's shard (TPTrainLM)."""
+        import torch.distributed as dist
+
+        from ..models.tp_llm import TPTrainLM
+        from ..parallel.dist import build_mesh
+        from ..parallel.tp import TensorParallelComm
+        from .rollout import TPLLMGenerator
+
+        tp = self.tp
+        if dp == "none":
+            raise ValueError("tensor-parallel training needs a process group (dp='fused' or 'nccl')")
+        if cfg.micro_batch % tp or (cfg.micro_batch // tp * cfg.seq_len) % 128 or cfg.batch % cfg.micro_batch:
+            raise ValueError("tensor-parallel training: micro_batch must divide the batch, split over the TP ranks "
+                             "into whole sequences, and give each rank a multiple of 128 rows")
+        mesh = build_mesh(self.world, self.rank, tp=tp)
+        self.mesh = mesh
+        self.tp_rank, self.group_index = mesh.tp_rank, self.rank // tp
+        H = cfg.model.hidden
+        rows = max(cfg.num_prompts * cfg.prompt_len, cfg.batch, cfg.micro_batch * cfg.seq_len)
+        self.comm = TensorParallelComm(rows, H, H, group=mesh.tp_group, device=self.device.index)
+        full = DecoderLM(cfg.model, self.device, seed=cfg.seed, master=False)  # bf16 only, sliced below
+        self.model = TPTrainLM(full, self.comm)
+        del full
+        dp_world = mesh.dp
+        if dp_world > 1 and dp == "fused":
+            from ..parallel.peer import FusedDataParallelAdam
+
+            self.opt = FusedDataParallelAdam(self.model.numel, mesh.dp_group, lr=cfg.lr, betas=(0.9, 0.95))
+            self.model.rebind_storage(self.opt.param, self.opt.grad, self.opt.shadow)
+            self.opt.broadcast_params(0)
+        else:
+            self.opt = FusedAdam(self.model.flat, self.model.grad, lr=cfg.lr, betas=(0.9, 0.95),
+                                 shadow=self.model.shadow)
+            if dp_world > 1:
+                from ..parallel.dp import NcclGradSync
+
+                dist.broadcast(self.model.flat, src=dist.get_global_rank(mesh.dp_group, 0), group=mesh.dp_group)
+                self.model.shadow.copy_(self.model.flat)
+                self.grad_sync = NcclGradSync(mesh.dp_group)
+        self.ref = self.model.frozen_copy()
+        self.tpm = self.model
+        self.gen = TPLLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.group_index)
         self.stats = torch.zeros(4, device=self.device)
         self.step_count = 0
         self.last_times = {}
@@ -199,24 +257,38 @@ class GRPOTrainer:
         lens = torch.full((cfg.batch,), cfg.response_len, device=dev, dtype=torch.int32)
         rewards = o.hash_reward(resp, lens)
         adv = o.grpo_advantage(rewards, cfg.group_size, 1e-4, True)
-        if self.tp > 1:  # this rank trains on its share of the tensor-parallel group's sequences
+        if self.tp_mode == "rollout":  # this rank trains on its share of the tensor-parallel group's sequences
             share = cfg.batch // self.tp
             lo = self.tp_rank * share
             seqs, adv = seqs[lo:lo + share].contiguous(), adv[lo:lo + share].contiguous()
+        train_tokens = seqs.shape[0] * cfg.seq_len // (self.tp if self.tp_mode == "train" else 1)
         # 3. reference log-probs
-        ref_lp = self.ref_logprobs(seqs)
+        if self.tp_mode == "train":
+            own = self._tp_own(seqs.shape[0])
+            adv = adv.index_select(0, own).contiguous()
+            ref_lp = self._tp_ref_logprobs(seqs)
+        else:
+            ref_lp = self.ref_logprobs(seqs)
         torch.cuda.synchronize(dev)
         t2 = time.perf_counter()
         # 4. update
         self.model.zero_grad()
         self.stats.zero_()
-        self._train(seqs, ref_lp, adv)
+        if self.tp_mode == "train":
+            self._train_tp(seqs, ref_lp, adv)
+            self.model.reduce_replicated_grads()
+            import torch.distributed as dist
+
+            dist.all_reduce(self.stats, group=self.mesh.tp_group)
+        else:
+            self._train(seqs, ref_lp, adv)
         if self.grad_sync is not None:
             self.opt.step(grad_scale=self.grad_sync(self.model.grad))
         else:
             self.opt.step()  # the fused data-parallel step averages over ranks itself
-        if self.tp > 1:
+        if self.tp_mode == "rollout":
             self.tpm.load_from(self.model)  # trainer -> rollout weight sync
+        # (tp_mode "train": the rollout reads the weights the optimizer just wrote)
         torch.cuda.synchronize(dev)
         t3 = time.perf_counter()
         self.step_count += 1
@@ -225,7 +297,7 @@ class GRPOTrainer:
         return {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()),
                 "pg_loss": st[0], "kl": st[1], "clipped_tokens": st[2], "tokens": st[3],
                 "rollout_logp_mean": float(roll_lp.mean()), **self.last_times,
-                "train_tokens": seqs.shape[0] * cfg.seq_len}
+                "train_tokens": train_tokens}
 
     def _train(self, seqs, ref_lp, adv):
         cfg = self.cfg
@@ -265,4 +337,77 @@ class GRPOTrainer:
             o.rmsnorm_bwd(dhf, x, m_.f32["norm"], rstd, dx, None, m_.g["norm"])
             dx = m_.backward(dx, saved, m, T, pos[:N])
             m_.embed_backward(ids, dx)
+            del saved, logits
+
+    # ------------------------------------------------------------------ tensor-parallel training
+    def _tp_own(self, nb: int) -> torch.Tensor:
+        """Indices of the sequences whose rows this rank holds: in every
+        micro-batch of ``micro_batch`` sequences, rank r holds the r-th 1/tp."""
+        mb, tp, r = self.cfg.micro_batch, self.tp, self.tp_rank
+        ml = mb // tp
+        base = torch.arange(0, nb, mb, device=self.device)
+        return (base[:, None] + r * ml + torch.arange(ml, device=self.device)[None, :]).reshape(-1)
+
+    @torch.no_grad()
+    def _tp_ref_logprobs(self, seqs: torch.Tensor) -> torch.Tensor:
+        """Reference log-probs of this rank's sequences (TP forward of the frozen shard)."""
+        cfg = self.cfg
+        o = _ops()
+        ref = self.ref
+        B, T, Lp, Lr = seqs.shape[0], cfg.seq_len, cfg.prompt_len, cfg.response_len
+        mb, tp, r = cfg.micro_batch, self.tp, self.tp_rank
+        ml = mb // tp
+        out = torch.empty(B // tp, Lr, device=self.device)
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
+        rows = self._response_rows(ml)
+        for j, s0 in enumerate(range(0, B, mb)):
+            ids = seqs[s0:s0 + mb].contiguous()
+            x = ref.embed_rows(ids.reshape(-1))
+            x = ref.forward(x, mb, T, pos)
+            hf = ref.final_norm(x)
+            logits = ref.logits(hf.index_select(0, rows))
+            tgt = ids[r * ml:(r + 1) * ml, Lp:].reshape(-1).contiguous()
+            o.logprob(logits, tgt, out[j * ml:(j + 1) * ml].view(-1))
+        return out
+
+    def _train_tp(self, seqs, ref_lp, adv):
+        """Micro-batched TP forward/backward; every rank of the group runs the
+        same micro-batches, each on its rows (whole sequences)."""
+        cfg = self.cfg
+        o = _ops()
+        M = self.model
+        T, Lp, Lr = cfg.seq_len, cfg.prompt_len, cfg.response_len
+        mb, tp, r = cfg.micro_batch, self.tp, self.tp_rank
+        ml = mb // tp
+        H = cfg.model.hidden
+        nb = seqs.shape[0]
+        pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
+        mask = torch.ones(ml, Lr, device=self.device)
+        rows = self._response_rows(ml)
+        for j, s0 in enumerate(range(0, nb, mb)):
+            ids = seqs[s0:s0 + mb].contiguous()
+            x0 = M.embed_rows(ids.reshape(-1))
+            x, saved = M.forward_train(x0, mb, T, pos, save=True)
+            rstd = torch.empty(ml * T, device=self.device)
+            hf = M.full.final_norm(x, rstd)
+            hr = hf.index_select(0, rows)
+            logits = M.full.logits(hr)                                  # [ml*Lr, V] bf16
+            tgt = ids[r * ml:(r + 1) * ml, Lp:].reshape(-1).contiguous()
+            lp = torch.empty(ml * Lr, device=self.device)
+            o.logprob(logits, tgt, lp)
+            old = lp.detach().clone()                                   # behaviour policy == current
+            dlp = torch.empty_like(lp)
+            sl = slice(j * ml, (j + 1) * ml)
+            o.grpo_loss(lp.view(ml, Lr), old.view(ml, Lr), ref_lp[sl].contiguous(), adv[sl].contiguous(), mask,
+                        dlp.view(ml, Lr), self.stats, cfg.clip, cfg.kl_coef, 1.0 / nb)
+            o.logprob(logits, tgt, None, dlp)                          # logits <- d loss / d logits
+            dhr = torch.empty(ml * Lr, H, device=self.device, dtype=torch.bfloat16)
+            o.gemm(logits, M.full.head_weight(), dhr, False, True)      # d h = dLogits W_head
+            o.gemm(logits, hr, M.full.head_grad(), True, True, accumulate=True, split_k=1)
+            dhf = torch.zeros(ml * T, H, device=self.device, dtype=torch.bfloat16)
+            dhf.index_copy_(0, rows, dhr)
+            dx = torch.empty_like(x)
+            o.rmsnorm_bwd(dhf, x, M.f32["norm"], rstd, dx, None, M.g["norm"])
+            dx = M.backward(dx, saved, mb, T, pos)
+            M.embed_backward_rows(ids.reshape(-1), dx)
             del saved, logits

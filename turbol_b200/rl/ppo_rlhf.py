@@ -67,25 +67,63 @@ class _Frozen:
         self.cfg, self.device = stage.cfg, stage.device
         self.stage, self.num_stages = stage.stage, stage.num_stages
         self.first, self.last = stage.first, stage.last
+        self.tp = getattr(stage, "tp", 1)
 
 
 class PPORLHFTrainer:
-    def __init__(self, cfg: RLHFConfig, device, group=None):
+    """tp > 1: the world is split into ``world / tp`` pipeline stages of ``tp``
+    consecutive ranks; each stage's layers are tensor parallel (TPTrainLM on
+    the fused all-gather->GEMM / GEMM->reduce-scatter kernels, forward and
+    backward), every micro-batch's rows are split over the stage's TP ranks,
+    and rank t of a stage exchanges its rows with rank t of the neighbouring
+    stages (PP x TP)."""
+
+    def __init__(self, cfg: RLHFConfig, device, group=None, tp: int = 1):
         self.cfg = cfg
         self.device = torch.device(device)
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.ranks = list(range(self.world)) if group is None else dist.get_process_group_ranks(group)
         if cfg.num_prompts % cfg.micro_batch or cfg.num_prompts % self.world:
-            raise ValueError("num_prompts must divide by micro_batch and by the pipeline size")
-        self.stage = pp.PipelineStage(cfg.model, self.rank, self.world, self.device, seed=cfg.seed, value_head=True,
-                                      lr=cfg.lr)
+            raise ValueError("num_prompts must divide by micro_batch and by the world size")
+        self.tp, self.tp_rank = tp, 0
+        comm = None
+        if tp > 1:
+            from ..parallel.dist import build_mesh
+            from ..parallel.tp import TensorParallelComm
+
+            if group is not None:
+                raise ValueError("pipeline x tensor parallel runs on the world group")
+            if self.world % tp or cfg.micro_batch % tp or (cfg.micro_batch // tp * cfg.seq_len) % 128:
+                raise ValueError("tp must divide the world size and the micro-batch, with a multiple of 128 rows "
+                                 "per rank")
+            mesh = build_mesh(self.world, self.rank, tp=tp, pp=self.world // tp)
+            self.mesh, self.tp_rank = mesh, mesh.tp_rank
+            self.pp_ranks, self.pp_group, self.tp_group = mesh.pp_ranks, mesh.pp_group, mesh.tp_group
+            stage_idx, n_stages = mesh.pp_rank, mesh.pp
+            H = cfg.model.hidden
+            comm = TensorParallelComm(cfg.micro_batch * cfg.seq_len, H, H, group=mesh.tp_group,
+                                      device=self.device.index)
+            self.tp_comm = comm
+        else:
+            self.pp_ranks, self.pp_group, self.tp_group = self.ranks, group, None
+            stage_idx, n_stages = self.rank, self.world
+        self.n_stages = n_stages
+        self.stage = pp.PipelineStage(cfg.model, stage_idx, n_stages, self.device, seed=cfg.seed, value_head=True,
+                                      lr=cfg.lr, tp_comm=comm)
         # a tied embedding lives on the first and the last stage: same initial
         # weights, and the two gradients are summed after every backward pass
-        self.tied = cfg.model.tie_embeddings and self.world > 1
-        self.embed_group = dist.new_group([self.ranks[0], self.ranks[-1]]) if self.tied else None
+        # (one group per TP rank: the first- and last-stage ranks holding it)
+        self.tied = cfg.model.tie_embeddings and n_stages > 1
+        self.embed_group = None
+        if self.tied:
+            for t in range(tp):
+                ends = [self.ranks[t], self.ranks[(n_stages - 1) * tp + t]]
+                g = dist.new_group(ends)
+                if self.rank in ends:
+                    self.embed_group = g
         if self.tied and (self.stage.first or self.stage.last):
-            dist.broadcast(self.stage.model.p["embed"], src=self.ranks[0], group=self.embed_group)
+            dist.broadcast(self.stage.model.p["embed"], src=self.pp_ranks[0], group=self.embed_group)
             self.stage.model.sync_shadow()
         self.ref = _Frozen(self.stage)
         # bf16 rollout copy of the whole policy on every rank
@@ -99,6 +137,8 @@ class PPORLHFTrainer:
     @torch.no_grad()
     def sync_weights(self):
         """Every stage's bf16 weights -> every rank's rollout copy."""
+        if self.tp > 1:
+            return self._sync_weights_tp()
         for src in range(self.world):
             for name in self._stage_names(src):
                 t = self.rollout.s[name]
@@ -108,6 +148,27 @@ class PPORLHFTrainer:
         # fp32 norm weights / biases in place: the captured decode graph keeps their addresses
         for n, t in self.rollout.f32.items():
             t.copy_(self.rollout.s[n].float())
+
+    @torch.no_grad()
+    def _sync_weights_tp(self):
+        """PP x TP: every rank's bf16 shard buffer is broadcast once (the
+        replicated tensors only from TP rank 0) and written into the matching
+        slices of every rank's full rollout copy."""
+        from ..models.tp_llm import TPTrainLM
+
+        cfg, tp = self.cfg.model, self.tp
+        if not hasattr(self, "_sync_buf"):
+            most = max(TPTrainLM.layout(cfg, pp.stage_layers(cfg.n_layers, self.n_stages, s), s == 0,
+                                        s == self.n_stages - 1, tp)[2] for s in range(self.n_stages))
+            self._sync_buf = torch.empty(most, device=self.device, dtype=torch.bfloat16)
+        for src in range(self.world):
+            s, t = src // tp, src % tp
+            offs, rep, numel = TPTrainLM.layout(cfg, pp.stage_layers(cfg.n_layers, self.n_stages, s), s == 0,
+                                                s == self.n_stages - 1, tp)
+            buf = self.stage.model.shadow if src == self.rank else self._sync_buf[:numel]
+            lo = 0 if t == 0 else rep
+            dist.broadcast(buf[lo:numel], src=self.ranks[src], group=self.group)
+            TPTrainLM.unshard_into(self.rollout, buf, offs, tp, t, shards_only=t > 0)
 
     def _stage_names(self, s: int):
         cfg = self.cfg.model
@@ -149,14 +210,28 @@ class PPORLHFTrainer:
         pos = torch.arange(T, device=self.device, dtype=torch.int32).repeat(mb)
         pp.set_micro_geometry(mb, T, pos)
 
-        def first(i):
-            return stage.model.embed(seqs[i * mb:(i + 1) * mb])
+        if self.tp > 1:
+            def first(i):
+                return stage.model.embed_rows(seqs[i * mb:(i + 1) * mb].reshape(-1))
 
-        def back_first(i, dx):
-            stage.model.embed_backward(seqs[i * mb:(i + 1) * mb], dx)
+            def back_first(i, dx):
+                stage.model.embed_backward_rows(seqs[i * mb:(i + 1) * mb].reshape(-1), dx)
+        else:
+            def first(i):
+                return stage.model.embed(seqs[i * mb:(i + 1) * mb])
 
-        pp.run_1f1b(stage, self.ranks, M, mb * T, first, on_last, back_first, group=self.group,
+            def back_first(i, dx):
+                stage.model.embed_backward(seqs[i * mb:(i + 1) * mb], dx)
+
+        pp.run_1f1b(stage, self.pp_ranks, M, mb * T // self.tp, first, on_last, back_first, group=self.pp_group,
                     forward_only=not train)
+
+    def _own(self, i: int) -> slice:
+        """The sequences of micro-batch i whose rows this rank holds (all of
+        them without TP; the tp_rank-th 1/tp with it)."""
+        mb = self.cfg.micro_batch
+        ml = mb // self.tp
+        return slice(i * mb + self.tp_rank * ml, i * mb + (self.tp_rank + 1) * ml)
 
     # ------------------------------------------------------------ step
     def step(self) -> dict:
@@ -187,20 +262,25 @@ class PPORLHFTrainer:
         ref_lp = torch.zeros(B, Lr, device=dev)
         st = self.stage
 
+        ml = mb // self.tp
+
         def score_policy(i, x_out):
-            ids = seqs[i * mb:(i + 1) * mb]
-            hf, _, rows, hr, logits, tgt, lp = self._head(st.model, x_out, mb, ids)
-            old_lp[i * mb:(i + 1) * mb] = lp.view(mb, Lr)
-            old_v[i * mb:(i + 1) * mb] = st.values(hr).view(mb, Lr)
+            sl = self._own(i)
+            hf, _, rows, hr, logits, tgt, lp = self._head(st.model, x_out, ml, seqs[sl])
+            old_lp[sl] = lp.view(ml, Lr)
+            old_v[sl] = st.values(hr).view(ml, Lr)
 
         def score_ref(i, x_out):
-            ids = seqs[i * mb:(i + 1) * mb]
-            *_, lp = self._head(self.ref.model, x_out, mb, ids)
-            ref_lp[i * mb:(i + 1) * mb] = lp.view(mb, Lr)
+            sl = self._own(i)
+            *_, lp = self._head(self.ref.model, x_out, ml, seqs[sl])
+            ref_lp[sl] = lp.view(ml, Lr)
 
         with torch.no_grad():
             self._pass(st, seqs, False, score_policy)
             self._pass(self.ref, seqs, False, score_ref)
+            if self.tp > 1 and st.last:  # every TP rank of the last stage scored its own sequences
+                for t_ in (old_lp, old_v, ref_lp):
+                    dist.all_reduce(t_, group=self.tp_group)
         adv = ret = None
         seq_reward = None
         if st.last:
@@ -221,12 +301,12 @@ class PPORLHFTrainer:
         norm = 1.0 / (B * Lr)
 
         def loss_last(i, x_out):
-            sl = slice(i * mb, (i + 1) * mb)
+            sl = self._own(i)
             ids = seqs[sl]
-            hf, rstd, rows, hr, logits, tgt, lp = self._head(st.model, x_out, mb, ids)
+            hf, rstd, rows, hr, logits, tgt, lp = self._head(st.model, x_out, ml, ids)
             v = st.values(hr)
-            lp_t = lp.view(mb, Lr).detach().requires_grad_()
-            v_t = v.view(mb, Lr).detach().requires_grad_()
+            lp_t = lp.view(ml, Lr).detach().requires_grad_()
+            v_t = v.view(ml, Lr).detach().requires_grad_()
             with torch.enable_grad():
                 ratio = torch.exp(lp_t - old_lp[sl])
                 A = adv[sl]
@@ -238,14 +318,14 @@ class PPORLHFTrainer:
             stats[0] += pg.detach().sum() * norm
             stats[1] += vf.detach().sum() * norm
             stats[2] += ((ratio.detach() - 1).abs() > cfg.clip).float().sum()
-            stats[3] += mb * Lr
+            stats[3] += ml * Lr
             H = cfg.model.hidden
             o.logprob(logits, tgt, None, lp_t.grad.reshape(-1).contiguous())       # logits <- d loss / d logits
-            dhr = torch.empty(mb * Lr, H, device=dev, dtype=torch.bfloat16)
+            dhr = torch.empty(ml * Lr, H, device=dev, dtype=torch.bfloat16)
             o.gemm(logits, st.model.head_weight(), dhr, False, True)              # d h = dLogits W_head
             o.gemm(logits, hr, st.model.head_grad(), True, True, accumulate=True, split_k=1)
             st.values_backward(hr, v_t.grad.reshape(-1), dhr)
-            dhf = torch.zeros(mb * cfg.seq_len, H, device=dev, dtype=torch.bfloat16)
+            dhf = torch.zeros(ml * cfg.seq_len, H, device=dev, dtype=torch.bfloat16)
             dhf.index_copy_(0, rows, dhr)
             dx = torch.empty_like(x_out)
             o.rmsnorm_bwd(dhf, x_out, st.model.f32["norm"], rstd, dx, None, st.model.g["norm"])
@@ -263,6 +343,8 @@ class PPORLHFTrainer:
         # the last stage owns the losses and rewards: share them
         vec = torch.zeros(6, device=dev)
         if st.last:
+            if self.tp > 1:
+                dist.all_reduce(stats, group=self.tp_group)
             vec[:4] = stats
             vec[4] = seq_reward.mean()
             vec[5] = (old_lp - ref_lp).mean()
