@@ -1,0 +1,197 @@
+// Host-side race and memory checks of the native core (built with
+// -fsanitize=address,undefined and, separately, -fsanitize=thread by
+// tests/test_sanitizers.py; no GPU is used).  Each section drives one
+// component the way the Python bindings do, with the concurrency the
+// framework allows: the profiler from several threads with exports running
+// alongside (the reference's ExportJSON re-locked its own mutex,
+// turbol_vllm/src/profiler/profiler.cpp:192-200), the TCP rendezvous store
+// with a server thread per client, the KV block allocator through many
+// allocate/append/free cycles, and the file formats (Config, TFRecord event
+// files, Prometheus text, JSONL datasets) through write/read round trips.
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "kernels.h"
+#include "turbol/config.hpp"
+#include "turbol/observability.hpp"
+#include "turbol/runtime.hpp"
+
+// The host core's only kernel dependency (TensorUtils on CUDA tensors); the
+// sanitizer build links no kernels, and CPU tensors never reach it.
+extern "C" int tb_elementwise(float*, const float*, const float*, long long, float, int, cudaStream_t) {
+  return static_cast<int>(cudaErrorNotSupported);
+}
+
+using namespace turbol;
+
+static int g_fail = 0;
+#define EXPECT(c)                                                   \
+  do {                                                             \
+    if (!(c)) {                                                    \
+      std::fprintf(stderr, "EXPECT failed %s:%d: %s\n", __FILE__, __LINE__, #c); \
+      ++g_fail;                                                    \
+    }                                                              \
+  } while (0)
+
+static void config_roundtrip(const std::string& dir) {
+  Config c;
+  c.SetString("model", "qwen2-1.5b");
+  c.SetInt("num_envs", 65536);
+  c.SetFloat("lr", 3e-4);
+  c.SetBool("fused", true);
+  const std::string p = dir + "/cfg.txt";
+  EXPECT(c.Save(p).ok());
+  Config d;
+  EXPECT(d.Load(p).ok());
+  EXPECT(d.GetInt("num_envs", 0) == 65536 && d.GetBool("fused", false) && d.GetString("model", "") == "qwen2-1.5b");
+}
+
+static void profiler_threads(const std::string& dir) {
+  ProfilerConfig pc;
+  pc.enable_cuda_timing = false;
+  Profiler prof(pc);
+  prof.Enable();
+  std::atomic<bool> done{false};
+  std::vector<std::thread> ts;
+  for (int t = 0; t < 4; ++t)
+    ts.emplace_back([&prof, t] {
+      for (int i = 0; i < 300; ++i) {
+        SpanID a = prof.BeginSpan("outer" + std::to_string(t));
+        SpanID b = prof.BeginSpan("inner");
+        prof.RecordComm("allreduce", 1 << 20, 0.01);
+        prof.EndSpan(b);
+        prof.EndSpan(a);
+      }
+    });
+  std::thread exporter([&] {
+    int n = 0;
+    while (!done.load()) {
+      EXPECT(prof.ExportJSON(dir + "/stats.json").ok());
+      (void)prof.GetStats();
+      (void)prof.Summary();
+      ++n;
+    }
+    EXPECT(n > 0);
+  });
+  for (auto& t : ts) t.join();
+  done = true;
+  exporter.join();
+  EXPECT(prof.GetAllSpans().size() == 4u * 300u * 2u);
+  EXPECT(prof.ExportChromeTrace(dir + "/trace.json").ok());
+  prof.Disable();
+}
+
+static void writers(const std::string& dir) {
+  {
+    TensorBoardWriter tb(dir);
+    std::vector<float> h(1000);
+    for (int i = 0; i < 1000; ++i) h[i] = static_cast<float>(i % 37) * 0.5f;
+    std::vector<std::thread> ts;
+    for (int t = 0; t < 3; ++t)
+      ts.emplace_back([&tb, &h, t] {
+        for (int s = 0; s < 200; ++s) tb.AddScalar("loss/" + std::to_string(t), 1.0f / (s + 1), s);
+        tb.AddHistogram("h", h.data(), static_cast<int64_t>(h.size()), t);
+        tb.AddText("note", "step text", t);
+      });
+    for (auto& t : ts) t.join();
+    tb.Flush();
+  }
+  PrometheusWriter pw(dir + "/metrics.prom");
+  for (int i = 0; i < 50; ++i) {
+    Labels l;
+    l.kv["rank"] = "0";
+    pw.WriteCounter("env_steps_total", 1000.0 * i, l);
+    pw.WriteGauge("reward_mean", 0.5);
+  }
+  pw.Flush();
+}
+
+static void tcp_store() {
+  TcpStore server("127.0.0.1", 0, true, 5000);
+  const int port = server.port();
+  EXPECT(port > 0);
+  const int world = 4;
+  std::vector<std::thread> ts;
+  std::atomic<int> ok{0};
+  for (int r = 0; r < world; ++r)
+    ts.emplace_back([&, r] {
+      TcpStore c("127.0.0.1", port, false, 5000);
+      bool good = c.Set("key" + std::to_string(r), "v" + std::to_string(r)).ok();
+      int64_t res = 0;
+      for (int i = 0; i < 20; ++i) good = good && c.Add("counter", 1, &res).ok();
+      good = good && c.Barrier("b0", world, 5000).ok();
+      std::string v;
+      good = good && c.Get("key" + std::to_string((r + 1) % world), &v, 5000).ok() &&
+             v == "v" + std::to_string((r + 1) % world);
+      good = good && c.Barrier("b1", world, 5000).ok();
+      if (good) ok.fetch_add(1);
+    });
+  for (auto& t : ts) t.join();
+  EXPECT(ok.load() == world);
+  std::string v;
+  EXPECT(server.Get("counter", &v, 1000).ok() && v == "80");
+  // a missing key times out with a status, not a hang
+  EXPECT(server.Get("never_set", &v, 50).code() == StatusCode::kTimeout);
+}
+
+static void kv_blocks() {
+  KVBlockManager kv(257, 16);
+  for (int round = 0; round < 20; ++round) {
+    for (int s = 0; s < 16; ++s) EXPECT(kv.Allocate(round * 100 + s, 200).ok());
+    for (int s = 0; s < 16; ++s)
+      for (int t = 0; t < 20; ++t) EXPECT(kv.AppendToken(round * 100 + s).ok());
+    EXPECT(kv.BlockTable(round * 100 + 3).size() == static_cast<size_t>(kv.BlocksFor(220)));
+    for (int s = 0; s < 16; ++s) EXPECT(kv.Free(round * 100 + s).ok());
+    EXPECT(kv.NumFree() == 257);
+  }
+  EXPECT(!kv.Allocate(1, 257 * 16 + 1).ok());  // more than the pool: refused
+}
+
+static void schedules_tokenizer_dataset(const std::string& dir) {
+  for (int S = 1; S <= 8; ++S)
+    for (int s = 0; s < S; ++s) {
+      auto ops = PipelineSchedule::OneFOneB(S, s, 8);
+      EXPECT(ops.size() == 16u);
+      EXPECT(PipelineSchedule::PeakActivations(ops) <= S - s);
+    }
+  ByteTokenizer tok;
+  const std::string text = "GRPO on B200: \xce\xbb = 0.95 \xe2\x9c\x93";
+  EXPECT(tok.Decode(tok.Encode(text, true, true)) == text);
+  const std::string p = dir + "/data.jsonl";
+  {
+    std::ofstream f(p);
+    for (int i = 0; i < 64; ++i)
+      f << "{\"prompt\": \"question " << i << " \\\"quoted\\\"\", \"chosen\": \"yes\", \"rejected\": \"no\"}\n";
+  }
+  DatasetConfig dc;
+  dc.data_paths = {p};
+  dc.batch_size = 8;
+  dc.max_seq_length = 32;
+  Dataset ds(dc);
+  EXPECT(ds.Initialize().ok());
+  int batches = 0;
+  PreprocessedBatch b;
+  while (ds.HasNext() && ds.NextBatch(&b).ok()) ++batches;
+  EXPECT(batches == 8);
+}
+
+int main(int argc, char** argv) {
+  const std::string dir = argc > 1 ? argv[1] : "/tmp";
+  config_roundtrip(dir);
+  profiler_threads(dir);
+  writers(dir);
+  tcp_store();
+  kv_blocks();
+  schedules_tokenizer_dataset(dir);
+  if (g_fail) {
+    std::fprintf(stderr, "%d checks failed\n", g_fail);
+    return 1;
+  }
+  std::printf("HOST_SANITIZE_OK\n");
+  return 0;
+}
