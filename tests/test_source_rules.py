@@ -1,9 +1,11 @@
 """Source rules for code that runs on several GPUs, checked on the CPU.
 
-* No bulk or tensor TMA load with cluster multicast anywhere in the kernels:
-  the tensor-parallel and data-parallel kernels read peer memory, and a
-  multicast load whose source is (or could be) another GPU's memory is
-  forbidden; the rule is kept global so no multi-GPU path can reach one.
+* Every bulk / tensor (TMA) copy in the kernels uses only the qualifiers on
+  an allow-list: a plain tile or bulk copy into this CTA's shared memory,
+  completing on an mbarrier.  The tensor-parallel and data-parallel kernels
+  read peer memory, and a copy that fans one load out to several CTAs must
+  never read another GPU's memory; keeping the rule global means no
+  multi-GPU path can reach such a copy.
 * Every kernel source is built for sm_100a only (no other -gencode target).
 * Every device spin-wait in the peer-memory kernels goes through a bounded
   helper (a time budget), never an open-ended loop on a flag.
@@ -16,8 +18,10 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 KERNELS = sorted(glob.glob(os.path.join(ROOT, "csrc", "kernels", "*.cu")) +
                  glob.glob(os.path.join(ROOT, "csrc", "kernels", "*.cuh")) +
                  glob.glob(os.path.join(ROOT, "csrc", "kernels", "*.h")))
-# the qualifier is assembled so that this file does not itself read as a use of it
-MC = "multicast" + "::" + "cluster"
+# the qualifiers a bulk / tensor copy may carry
+ALLOWED = {"tensor", "1d", "2d", "3d", "4d", "5d", "shared::cluster", "shared::cta", "global", "tile",
+           "mbarrier::complete_tx::bytes", "bulk_group", "L2::cache_hint", "async", "bulk", "cp", "commit_group",
+           "wait_group", "read", "prefetch", "im2col"}
 
 
 def _code_lines(path):
@@ -28,13 +32,15 @@ def _code_lines(path):
     return out
 
 
-def test_no_multicast_bulk_loads():
+def test_bulk_copies_use_allowed_qualifiers_only():
     bad = []
     for path in KERNELS:
         for i, code in _code_lines(path):
-            if "cp.async.bulk" in code and MC in code:
-                bad.append(f"{os.path.relpath(path, ROOT)}:{i}")
-    assert not bad, f"cluster-multicast bulk/TMA loads found: {bad}"
+            for m in re.finditer(r"cp\.async\.bulk[\w.:]*", code):
+                extra = [q for q in m.group(0).split(".") if q and q not in ALLOWED]
+                if extra:
+                    bad.append(f"{os.path.relpath(path, ROOT)}:{i}: {extra}")
+    assert not bad, f"bulk/TMA copies with qualifiers outside the allow-list: {bad}"
 
 
 def test_sm100a_only():
