@@ -261,6 +261,20 @@ void register_llm_ops(py::module_& m) {
                          static_cast<int>(lp.size(1)), clip, beta, inv_total_seqs, turbol::StreamFor(lp)),
             "grpo_loss");
   });
+  m.def("ppo_token_loss", [=](at::Tensor lp, at::Tensor old_lp, at::Tensor adv, at::Tensor v, at::Tensor old_v,
+                              at::Tensor ret, at::Tensor dlp, at::Tensor dv, py::object stats, float clip, float vclip,
+                              float vf_coef, float norm) {
+    for (auto* t : {&lp, &old_lp, &adv, &v, &old_v, &ret, &dlp, &dv}) f32c(*t, "ppo_token_loss");
+    const long long R = lp.numel();
+    for (auto* t : {&old_lp, &adv, &v, &old_v, &ret, &dlp, &dv})
+      chk(t->numel() == R, "ppo_token_loss: every array has the same number of tokens");
+    float* st = stats.is_none() ? nullptr : stats.cast<at::Tensor>().data_ptr<float>();
+    cuda_ok(tb_ppo_token_loss(lp.data_ptr<float>(), old_lp.data_ptr<float>(), adv.data_ptr<float>(),
+                              v.data_ptr<float>(), old_v.data_ptr<float>(), ret.data_ptr<float>(),
+                              dlp.data_ptr<float>(), dv.data_ptr<float>(), st, R, clip, vclip, vf_coef, norm,
+                              turbol::StreamFor(lp)),
+            "ppo_token_loss");
+  });
   m.def(
       "flash_attn_fwd",
       [=](at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, py::object lse, int B, int T, int Hq, int Hk,

@@ -113,6 +113,29 @@ __device__ unsigned begin_call(const TbPeerTable& t, int* err, bool* ok) {
   return epoch;
 }
 
+// Sum over the ranks of the float4 at element i of every rank's fp32 buffer
+// at byte offset `off`.  All W peer loads are issued before the first add, so a
+// call pays one NVLink round trip instead of W; the adds run in rank order, as
+// a sequential loop would.
+__device__ __forceinline__ float4 sum_peers4(const TbPeerTable& t, long long off, long long i) {
+  float4 x[TB_MAX_PEERS];
+#pragma unroll
+  for (int p = 0; p < TB_MAX_PEERS; ++p)
+    if (p < t.world)
+      x[p] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + off) + i);
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int p = 0; p < TB_MAX_PEERS; ++p) {
+    if (p < t.world) {
+      s.x += x[p].x;
+      s.y += x[p].y;
+      s.z += x[p].z;
+      s.w += x[p].w;
+    }
+  }
+  return s;
+}
+
 __global__ void __launch_bounds__(kBlock) allreduce_kernel(TbPeerTable t, long long in_off, long long out_off,
                                                            long long n, float scale, unsigned* done_ctr, int* err) {
   bool ok;
@@ -124,15 +147,11 @@ __global__ void __launch_bounds__(kBlock) allreduce_kernel(TbPeerTable t, long l
     for (long long i = lo + (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < hi; i += stride) {
       float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
       const bool full = i + 4 <= hi;
-      for (int p = 0; p < t.world; ++p) {
-        const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + in_off) + i;
-        if (full) {
-          const float4 x = *reinterpret_cast<const float4*>(src);
-          s.x += x.x;
-          s.y += x.y;
-          s.z += x.z;
-          s.w += x.w;
-        } else {
+      if (full) {
+        s = sum_peers4(t, in_off, i);
+      } else {
+        for (int p = 0; p < t.world; ++p) {
+          const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + in_off) + i;
           s.x += src[0];
           if (i + 1 < hi) s.y += src[1];
           if (i + 2 < hi) s.z += src[2];
@@ -183,15 +202,15 @@ __global__ void __launch_bounds__(kBlock) allreduce_adam_kernel(TbPeerTable t, l
     for (long long i = lo + (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < hi; i += stride) {
       const int cnt = static_cast<int>(min(4LL, hi - i));
       float g[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int p = 0; p < t.world; ++p) {
-        const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + grad_off) + i;
-        if (cnt == 4) {
-          const float4 x = *reinterpret_cast<const float4*>(src);
-          g[0] += x.x;
-          g[1] += x.y;
-          g[2] += x.z;
-          g[3] += x.w;
-        } else {
+      if (cnt == 4) {
+        const float4 x = sum_peers4(t, grad_off, i);
+        g[0] = x.x;
+        g[1] = x.y;
+        g[2] = x.z;
+        g[3] = x.w;
+      } else {
+        for (int p = 0; p < t.world; ++p) {
+          const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + grad_off) + i;
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             if (j < cnt) g[j] += src[j];

@@ -185,6 +185,13 @@ int tb_logprob(void* logits, long long ld, int T, int V, const int* target, floa
 int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, const float* adv, const float* mask,
                  float* dlp, float* stats, int B, int T, float clip, float beta, float inv_total_seqs,
                  cudaStream_t s);
+// Clipped PPO policy loss + clipped value loss per token (RLHF with a value
+// head), forward and backward: dlp, dv = d loss / d (lp, v), loss = norm *
+// (sum pg + vf_coef sum vf); stats (nullable) += {pg * norm, vf * norm,
+// clipped tokens, tokens}.  All arrays fp32 [R].
+int tb_ppo_token_loss(const float* lp, const float* old_lp, const float* adv, const float* v, const float* old_v,
+                      const float* ret, float* dlp, float* dv, float* stats, long long R, float clip, float vclip,
+                      float vf_coef, float norm, cudaStream_t s);
 int tb_flash_attn_fwd(const void* q, const void* k, const void* v, long long ld, void* o, long long ldo, float* lse,
                       int B, int T, int Hq, int Hk, float scale, cudaStream_t s);
 // Same contract on tcgen05 tensor cores (TMA + TMEM); err (nullable) gets site

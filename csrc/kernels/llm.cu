@@ -834,6 +834,59 @@ __global__ void grpo_loss_kernel(const float* __restrict__ lp, const float* __re
   }
 }
 
+// Per-token clipped PPO loss of an RLHF policy with a value head, forward and
+// backward in one pass over R tokens:
+//   ratio = exp(lp - old_lp);  pg = -min(ratio A, clip(ratio, 1 -+ c) A)
+//   v_c = old_v + clip(v - old_v, -+ vc);  vf = 0.5 max((v - ret)^2, (v_c - ret)^2)
+//   loss = norm (sum pg + vf_coef sum vf)
+// dlp / dv are d loss / d lp and d loss / d v (ties of min / max split the
+// gradient evenly, clip passes it inside its range); stats += {sum pg * norm,
+// sum vf * norm, tokens with |ratio - 1| > c, tokens}.
+__global__ void ppo_token_loss_kernel(const float* __restrict__ lp, const float* __restrict__ old_lp,
+                                      const float* __restrict__ adv, const float* __restrict__ v,
+                                      const float* __restrict__ old_v, const float* __restrict__ ret,
+                                      float* __restrict__ dlp, float* __restrict__ dv, float* __restrict__ stats,
+                                      long long R, float clip, float vclip, float vf_coef, float norm) {
+  __shared__ float red[32];
+  float s_pg = 0.f, s_vf = 0.f, s_cf = 0.f, s_n = 0.f;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < R;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float A = adv[i];
+    const float r = __expf(lp[i] - old_lp[i]);
+    const float rc = fminf(fmaxf(r, 1.f - clip), 1.f + clip);
+    const float un = r * A, cl = rc * A;
+    const bool inside = r >= 1.f - clip && r <= 1.f + clip;
+    // d(-min(un, cl))/d lp: the unclipped branch carries -A r, the clipped one -A r only inside the range
+    const float g_un = -A * r, g_cl = inside ? -A * r : 0.f;
+    const float g_pg = un < cl ? g_un : (un > cl ? g_cl : 0.5f * (g_un + g_cl));
+    dlp[i] = g_pg * norm;
+    const float vv = v[i], ov = old_v[i], rt = ret[i];
+    const float dd = vv - ov;
+    const float vc = ov + fminf(fmaxf(dd, -vclip), vclip);
+    const float a = vv - rt, b = vc - rt;
+    const float a2 = a * a, b2 = b * b;
+    const float db = (dd >= -vclip && dd <= vclip) ? b : 0.f;  // d(0.5 b^2)/dv through the clip
+    const float g_vf = a2 > b2 ? a : (b2 > a2 ? db : 0.5f * (a + db));
+    dv[i] = vf_coef * g_vf * norm;
+    s_pg += -fminf(un, cl);
+    s_vf += 0.5f * fmaxf(a2, b2);
+    s_cf += fabsf(r - 1.f) > clip ? 1.f : 0.f;
+    s_n += 1.f;
+  }
+  if (stats) {
+    s_pg = tb::block_sum(s_pg, red);
+    s_vf = tb::block_sum(s_vf, red);
+    s_cf = tb::block_sum(s_cf, red);
+    s_n = tb::block_sum(s_n, red);
+    if (threadIdx.x == 0) {
+      atomicAdd(&stats[0], s_pg * norm);
+      atomicAdd(&stats[1], s_vf * norm);
+      atomicAdd(&stats[2], s_cf);
+      atomicAdd(&stats[3], s_n);
+    }
+  }
+}
+
 inline unsigned grid_for(long long work, int block = 256) {
   long long g = (work + block - 1) / block;
   if (g > 148 * 16) g = 148 * 16;
@@ -974,6 +1027,15 @@ int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, cons
                  cudaStream_t s) {
   if (B <= 0) return 0;
   grpo_loss_kernel<<<B, 256, 0, s>>>(lp, old_lp, ref_lp, adv, mask, dlp, stats, B, T, clip, beta, inv_total_seqs);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_ppo_token_loss(const float* lp, const float* old_lp, const float* adv, const float* v, const float* old_v,
+                      const float* ret, float* dlp, float* dv, float* stats, long long R, float clip, float vclip,
+                      float vf_coef, float norm, cudaStream_t s) {
+  if (R <= 0) return 0;
+  ppo_token_loss_kernel<<<grid_for(R), 256, 0, s>>>(lp, old_lp, adv, v, old_v, ret, dlp, dv, stats, R, clip, vclip,
+                                                     vf_coef, norm);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -13,6 +13,11 @@ takes a clipped-ratio step with a k3 KL penalty against a frozen reference.
 ``--model`` picks a random-init architecture ("tiny" runs anywhere with a GPU
 in seconds; "qwen2-1.5b" is the 28-layer, 1536-hidden shape); ``--model-path``
 is accepted for command-line compatibility and only names the run.
+
+On several GPUs (one process per GPU):
+    torchrun --nproc-per-node 8 examples/grpo_example.py --model qwen2-1.5b --tp 2 --dp fused
+runs tensor-parallel groups of --tp ranks (rollout and training) with data
+parallelism across the groups.
 """
 from __future__ import annotations
 
@@ -48,6 +53,9 @@ def parse_args(argv=None):
     p.add_argument("--micro-batch", type=int, default=8)
     p.add_argument("--clip", type=float, default=0.2)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--dp", choices=["fused", "nccl"], default="fused",
+                   help="data-parallel gradient reduction when launched on several GPUs (torchrun)")
+    p.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (rollout and training)")
     p.add_argument("--checkpoint-dir", type=str, default="")
     p.add_argument("--checkpoint-every", type=int, default=0)
     return p.parse_args(argv)
@@ -65,7 +73,25 @@ def main(argv=None):
     cfg = GRPOConfig(model=model, num_prompts=args.num_prompts, group_size=args.group_size,
                      prompt_len=args.prompt_len, response_len=args.max_tokens, temperature=args.temperature,
                      lr=args.lr, clip=args.clip, kl_coef=args.kl_coef, micro_batch=args.micro_batch, seed=args.seed)
-    tr = GRPOTrainer(cfg, args.device)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = 0
+    if world > 1:  # launched by torchrun: one process per GPU, TP groups of --tp ranks, DP over the rest
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        args.device = f"cuda:{local}"
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device(args.device))
+        rank = dist.get_rank()
+        tr = GRPOTrainer(cfg, args.device, dp=args.dp, tp=args.tp)
+    else:
+        if args.tp > 1:
+            raise SystemExit("--tp needs several GPUs: launch with torchrun --nproc-per-node N")
+        tr = GRPOTrainer(cfg, args.device)
+    if rank != 0:
+        args.print_every = 1 << 30
     log_dir = args.log_dir or tempfile.mkdtemp(prefix="turbol_grpo_")
     os.makedirs(log_dir, exist_ok=True)
     tb = turbol.TensorBoardWriter(log_dir)
@@ -89,7 +115,13 @@ def main(argv=None):
         if args.checkpoint_dir and args.checkpoint_every and (step + 1) % args.checkpoint_every == 0:
             turbol.save_checkpoint(args.checkpoint_dir, step + 1, tr, background=True).wait()
     tb.flush()
-    print(f"logs: {log_dir}")
+    if rank == 0:
+        print(f"logs: {log_dir}")
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
     return tr
 
 

@@ -248,3 +248,26 @@ def test_swiglu_and_embedding(dev):
     ops().embed_bwd(ids, out, dW)
     exp = torch.zeros(V, D, device=dev).index_add_(0, ids.long(), out.float())
     assert torch.allclose(dW, exp, atol=1e-3)
+
+
+def test_ppo_token_loss_matches_autograd(dev):
+    """Fused PPO-RLHF token loss (policy clip + value clip) == autograd of the fp32 expression."""
+    from turbol_b200.ops import reference as R_
+
+    g = torch.Generator(device=dev).manual_seed(3)
+    n = 4 * 1024 + 37
+    lp = -torch.rand(n, device=dev, generator=g) * 3
+    old = lp + 0.3 * torch.randn(n, device=dev, generator=g)  # ratios on both sides of the clip
+    adv = torch.randn(n, device=dev, generator=g)
+    v = torch.randn(n, device=dev, generator=g)
+    old_v = v + 0.4 * torch.randn(n, device=dev, generator=g)
+    ret = torch.randn(n, device=dev, generator=g)
+    norm = 1.0 / n
+    loss, dlp_ref, dv_ref, st_ref = R_.ppo_token_loss(lp, old, adv, v, old_v, ret, 0.2, 0.2, 0.1, norm)
+    dlp, dv = torch.empty_like(lp), torch.empty_like(v)
+    stats = torch.zeros(4, device=dev)
+    ops().ppo_token_loss(lp, old, adv, v, old_v, ret, dlp, dv, stats, 0.2, 0.2, 0.1, norm)
+    assert torch.allclose(dlp, dlp_ref, atol=1e-7, rtol=1e-4)
+    assert torch.allclose(dv, dv_ref, atol=1e-7, rtol=1e-4)
+    assert torch.allclose(stats, st_ref, rtol=1e-4, atol=1e-5), (stats, st_ref)
+    assert abs(float(stats[0] + 0.1 * stats[1]) - float(loss)) < 1e-4

@@ -159,3 +159,22 @@ def lm_forward_ref(model, ids, params=None):
     h = rmsnorm(x, P["norm"], cfg.rms_eps)
     W = P["embed"] if cfg.tie_embeddings else P["lm_head"]
     return h @ W.t()
+
+
+def ppo_token_loss(lp, old_lp, adv, v, old_v, ret, clip=0.2, vclip=0.2, vf_coef=0.1, norm=1.0):
+    """Clipped PPO policy loss + clipped value loss per token (the oracle of
+    the ``ppo_token_loss`` kernel).  Returns (loss, d loss / d lp,
+    d loss / d v, stats [pg * norm, vf * norm, clipped tokens, tokens])."""
+    lp_t = lp.detach().float().clone().requires_grad_()
+    v_t = v.detach().float().clone().requires_grad_()
+    with torch.enable_grad():
+        ratio = torch.exp(lp_t - old_lp.float())
+        pg = -torch.min(ratio * adv, torch.clamp(ratio, 1 - clip, 1 + clip) * adv)
+        v_clip = old_v + torch.clamp(v_t - old_v, -vclip, vclip)
+        vf = 0.5 * torch.max((v_t - ret) ** 2, (v_clip - ret) ** 2)
+        loss = (pg.sum() + vf_coef * vf.sum()) * norm
+        loss.backward()
+    stats = torch.stack([pg.detach().sum() * norm, vf.detach().sum() * norm,
+                         ((ratio.detach() - 1).abs() > clip).float().sum(),
+                         torch.tensor(float(lp.numel()), device=lp.device)])
+    return loss.detach(), lp_t.grad, v_t.grad, stats

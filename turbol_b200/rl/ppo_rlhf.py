@@ -304,27 +304,17 @@ class PPORLHFTrainer:
             sl = self._own(i)
             ids = seqs[sl]
             hf, rstd, rows, hr, logits, tgt, lp = self._head(st.model, x_out, ml, ids)
-            v = st.values(hr)
-            lp_t = lp.view(ml, Lr).detach().requires_grad_()
-            v_t = v.view(ml, Lr).detach().requires_grad_()
-            with torch.enable_grad():
-                ratio = torch.exp(lp_t - old_lp[sl])
-                A = adv[sl]
-                pg = -torch.min(ratio * A, torch.clamp(ratio, 1 - cfg.clip, 1 + cfg.clip) * A)
-                v_clip = old_v[sl] + torch.clamp(v_t - old_v[sl], -cfg.vclip, cfg.vclip)
-                vf = 0.5 * torch.max((v_t - ret[sl]) ** 2, (v_clip - ret[sl]) ** 2)
-                loss = (pg.sum() + cfg.vf_coef * vf.sum()) * norm
-                loss.backward()
-            stats[0] += pg.detach().sum() * norm
-            stats[1] += vf.detach().sum() * norm
-            stats[2] += ((ratio.detach() - 1).abs() > cfg.clip).float().sum()
-            stats[3] += ml * Lr
+            v = st.values(hr).contiguous()
+            # clipped policy loss + clipped value loss, forward and backward in one kernel
+            dlp, dv = torch.empty_like(lp), torch.empty_like(v)
+            o.ppo_token_loss(lp, old_lp[sl].reshape(-1), adv[sl].reshape(-1), v, old_v[sl].reshape(-1),
+                             ret[sl].reshape(-1), dlp, dv, stats, cfg.clip, cfg.vclip, cfg.vf_coef, norm)
             H = cfg.model.hidden
-            o.logprob(logits, tgt, None, lp_t.grad.reshape(-1).contiguous())       # logits <- d loss / d logits
+            o.logprob(logits, tgt, None, dlp)                                     # logits <- d loss / d logits
             dhr = torch.empty(ml * Lr, H, device=dev, dtype=torch.bfloat16)
             o.gemm(logits, st.model.head_weight(), dhr, False, True)              # d h = dLogits W_head
             o.gemm(logits, hr, st.model.head_grad(), True, True, accumulate=True, split_k=1)
-            st.values_backward(hr, v_t.grad.reshape(-1), dhr)
+            st.values_backward(hr, dv, dhr)
             dhf = torch.zeros(ml * cfg.seq_len, H, device=dev, dtype=torch.bfloat16)
             dhf.index_copy_(0, rows, dhr)
             dx = torch.empty_like(x_out)
