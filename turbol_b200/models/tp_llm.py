@@ -38,6 +38,12 @@ every activation row over NVLink once per direction and calls no NCCL
 collective inside a layer.  The rollout engine can run on the same object
 (``TPLLMGenerator``): the optimizer writes the bf16 weights it reads, so the
 trainer -> rollout weight sync needs no copy at all.
+
+Reference parity: the reference names tensor parallelism only in its
+specification (docs/SPECIFICATION.md:1890-1900, a TENSOR_PARALLEL strategy and
+a tensor_parallel_size field) and forwards tensor_parallel_size to vLLM
+(turbol_vllm/python/turbol/vllm_inference.py:98,176); it has no tensor-parallel
+model or training code.
 """
 from __future__ import annotations
 
