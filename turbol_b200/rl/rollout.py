@@ -103,6 +103,7 @@ class LLMGenerator:
         # the narrow-tile plan without splitting is faster
         ws = st.get("ws")
         kw = {"workspace": ws} if ws is not None else {}
+        kw_down = {"workspace": st["ws_down"]} if "ws_down" in st else kw
         scale = 1.0 / math.sqrt(D)
         for li, i in enumerate(m.layers):
             P = f"l{i}."
@@ -119,7 +120,7 @@ class LLMGenerator:
             o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL, **kw)
             o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
             o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
-            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw)
+            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw_down)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
         o.sample(st["logits"], 1.0, 0, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
@@ -153,9 +154,11 @@ class LLMGenerator:
         }
 
     def _split_workspace(self, B: int) -> dict:
-        if B > 64:
-            return {}
         o, cfg = _ops(), self.cfg
+        if B > 64:
+            # many sequences: only the down projection (long K = ffn, few output
+            # tiles) gains from splitting K; the others keep the narrow-tile plan
+            return {"ws_down": torch.zeros(max(o.gemm_workspace_numel(B, cfg.hidden, cfg.ffn), 1), device=self.device)}
         n = max(o.gemm_workspace_numel(B, cfg.qkv_dim, cfg.hidden), o.gemm_workspace_numel(B, cfg.hidden, cfg.q_dim),
                 o.gemm_workspace_numel(B, cfg.hidden, cfg.ffn), 1)
         return {"ws": torch.zeros(n, device=self.device)}
