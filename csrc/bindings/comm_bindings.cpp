@@ -123,7 +123,7 @@ void register_comm_ops(py::module_& m) {
       .def("tp_ag_gemm",
            [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr,
               at::Tensor shard, at::Tensor W, at::Tensor out, bool b_mn, py::object bias, py::object aux, int epi,
-              int bn, py::object gather_out) {
+              int bn, py::object gather_out, py::object c2) {
              TbGemmArgs a = tp_gemm_args(shard, W, b_mn, bn);
              const int rows = static_cast<int>(shard.size(0));
              a.M = rows * p.world();
@@ -154,12 +154,22 @@ void register_comm_ops(py::module_& m) {
                c.gather_out = g.data_ptr();
                c.ld_gather = g.stride(0);
              }
+             at::Tensor raw;
+             if (!c2.is_none()) {
+               raw = c2.cast<at::Tensor>();
+               if (epi != TB_EPI_SWIGLU || !raw.is_cuda() || raw.scalar_type() != at::kBFloat16 || raw.dim() != 2 ||
+                   raw.stride(1) != 1 || raw.size(0) != a.M || raw.size(1) != a.N)
+                 throw std::invalid_argument("tp_ag_gemm: c2 (EPI_SWIGLU only) must be bf16 [world * rows, N]");
+               a.C2 = raw.data_ptr();
+               a.ldc2 = raw.stride(0);
+             }
              a.error = c.err;
              cuda_ok(tb_tp_ag_gemm(&c, &a, cur_stream(p.device())), "tp_ag_gemm");
            },
            py::arg("hdr_off"), py::arg("data_off"), py::arg("parity_bytes"), py::arg("ctr"), py::arg("shard"),
            py::arg("W"), py::arg("out"), py::arg("b_mn") = false, py::arg("bias") = py::none(),
-           py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("gather_out") = py::none())
+           py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("gather_out") = py::none(),
+           py::arg("c2") = py::none())
       // GEMM -> reduce-scatter: out[M / world, N] = rows of sum_r(A_r . W_r^T) (+ bias) (+ residual)
       .def("tp_gemm_rs",
            [](PeerMemory& p, int64_t hdr_off, int64_t data_off, int64_t parity_bytes, at::Tensor ctr, at::Tensor A,

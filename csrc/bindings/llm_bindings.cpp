@@ -19,7 +19,7 @@ void cuda_ok(int e, const char* what) {
 // C = epi(A . B^T) with A [M,K] (a_mn=0) or [K,M] (a_mn=1), B [N,K] (b_mn=0) or [K,N] (b_mn=1).
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, bool b_mn, py::object bias,
           py::object aux, int epi, bool accumulate, float alpha, int split_k, int bn, py::object err,
-          py::object workspace, py::object colsum) {
+          py::object workspace, py::object colsum, py::object c2) {
   chk(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   chk(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: A and B must be bfloat16");
   chk(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D operands");
@@ -29,7 +29,8 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   const int64_t N = b_mn ? B.size(1) : B.size(0);
   const int64_t Kb = b_mn ? B.size(0) : B.size(1);
   chk(K == Kb, "gemm: K mismatch");
-  chk(C.size(0) == M && C.size(1) == (epi == TB_EPI_SWIGLU ? N / 2 : N), "gemm: C shape mismatch");
+  const int64_t nc = epi == TB_EPI_SWIGLU ? N / 2 : (epi == TB_EPI_SWIGLU_BWD ? 2 * N : N);
+  chk(C.size(0) == M && C.size(1) == nc, "gemm: C shape mismatch");
   chk(C.scalar_type() == at::kFloat || C.scalar_type() == at::kBFloat16, "gemm: C must be fp32 or bf16");
   TbGemmArgs a{};
   a.A = A.data_ptr();
@@ -53,8 +54,9 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   }
   if (!aux.is_none()) {
     x = aux.cast<at::Tensor>();
-    chk(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && x.size(0) == M && x.size(1) == N,
-        "gemm: aux must be bf16 [M, N]");
+    chk(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1 && x.size(0) == M &&
+            x.size(1) == (epi == TB_EPI_SWIGLU_BWD ? 2 * N : N),
+        "gemm: aux must be bf16 [M, N] ([M, 2N] interleaved gate/up for EPI_SWIGLU_BWD)");
     a.aux = x.data_ptr();
     a.ld_aux = x.stride(0);
   }
@@ -75,6 +77,15 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
     chk(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.numel() == N, "gemm: colsum must be fp32 [N]");
     a.colsum = cs.data_ptr<float>();
   }
+  at::Tensor raw;
+  if (!c2.is_none()) {
+    raw = c2.cast<at::Tensor>();
+    chk(epi == TB_EPI_SWIGLU && raw.is_cuda() && raw.scalar_type() == at::kBFloat16 && raw.dim() == 2 &&
+            raw.stride(1) == 1 && raw.size(0) == M && raw.size(1) == N,
+        "gemm: c2 (EPI_SWIGLU only) must be bf16 [M, N]");
+    a.C2 = raw.data_ptr();
+    a.ldc2 = raw.stride(0);
+  }
   cuda_ok(tb_gemm_bf16(&a, turbol::StreamFor(C)), "gemm_bf16");
 }
 
@@ -84,7 +95,7 @@ void register_llm_ops(py::module_& m) {
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn") = false, py::arg("b_mn") = false,
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0f, py::arg("split_k") = 0, py::arg("bn") = 0, py::arg("error") = py::none(),
-        py::arg("workspace") = py::none(), py::arg("colsum") = py::none());
+        py::arg("workspace") = py::none(), py::arg("colsum") = py::none(), py::arg("c2") = py::none());
   m.def("gemm_workspace_numel", [](int M, int N, int K) {
     return static_cast<int64_t>(tb_gemm_workspace_bytes(M, N, K) / 4);
   });
@@ -341,4 +352,5 @@ void register_llm_ops(py::module_& m) {
   m.attr("EPI_TANH_BWD") = static_cast<int>(TB_EPI_TANH_BWD);
   m.attr("EPI_RESIDUAL") = static_cast<int>(TB_EPI_RESIDUAL);
   m.attr("EPI_SWIGLU") = static_cast<int>(TB_EPI_SWIGLU);
+  m.attr("EPI_SWIGLU_BWD") = static_cast<int>(TB_EPI_SWIGLU_BWD);
 }

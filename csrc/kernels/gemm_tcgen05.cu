@@ -83,6 +83,8 @@ struct DevArgs {
   int* slot_cnt;  // in-kernel split-K fix-up: one arrival counter per (tile, epilogue warp); null: reduce pass
   float* colsum;  // optional: column sums of the epilogue output, accumulated atomically
   int* error;
+  __nv_bfloat16* c2;  // EPI_SWIGLU, optional: the raw gate/up accumulator [M, N] (bf16), row stride ldc2
+  long long ldc2;
   TpArgs tp;
 };
 
@@ -169,7 +171,43 @@ __device__ __forceinline__ void unpack_bf16x32(uint4 q0, uint4 q1, uint4 q2, uin
   }
 }
 
+// Stores 32 bf16 columns [c0, c0 + valid) of this lane's row into base (row
+// stride ld): when whole and aligned, transposed through the warp's shared
+// staging so each store instruction writes 8 whole 64-byte row segments.
+// Every lane of the warp calls it (rows >= M are masked).
+__device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* base, long long ld, int M, int row0, int row, int c0,
+                                                 const float* v, int valid, int lane, uint32_t* stg) {
+  if (valid == 32 && (ld % 8) == 0 && (c0 % 8) == 0 && (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+    uint4* mine = reinterpret_cast<uint4*>(stg + lane * 20);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 pk;
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) hh[j] = __floats2bfloat162_rn(v[8 * q + 2 * j], v[8 * q + 2 * j + 1]);
+      mine[q] = pk;
+    }
+    __syncwarp();
+    const int seg = lane & 3;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int r = it * 8 + (lane >> 2);
+      const uint4 w = *reinterpret_cast<const uint4*>(stg + r * 20 + seg * 4);
+      if (row0 + r < M) *reinterpret_cast<uint4*>(base + static_cast<long long>(row0 + r) * ld + c0 + seg * 8) = w;
+    }
+    __syncwarp();
+  } else if (row < M) {
+    __nv_bfloat16* C = base + static_cast<long long>(row) * ld + c0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) C[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
 // pre: a0..a3 hold the row's 32 aux values, already loaded (16 bytes each).
+// kSwBwd: the instantiation that runs the SwiGLU-backward epilogue (kept out
+// of the others, whose register budget it would otherwise take).
+template <bool kSwBwd = false>
 __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, float* v, int ks, int lane,
                                            uint32_t* stg, int row0, int mode, void* cbase, bool pre = false,
                                            uint4 a0 = uint4{}, uint4 a1 = uint4{}, uint4 a2 = uint4{},
@@ -223,8 +261,38 @@ __device__ __forceinline__ void epilogue32(const DevArgs& p, int row, int c0, fl
       for (int j = 0; j < 32; ++j) v[j] += h[j];
     }
   }
+  if constexpr (kSwBwd) {
+    // acc = d out[:, c0..c0+32) of out = silu(gate) * up; aux holds the
+    // interleaved (gate, up) columns [M, 2N]; C receives d(gate, up) [M, 2N].
+    // Two halves of 16 output columns, each giving 32 interleaved columns.
+    __nv_bfloat16* C = static_cast<__nv_bfloat16*>(cbase);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int vh = valid - 16 * h;  // valid output columns in this half (may be <= 0)
+      if (vh <= 0) break;             // uniform across the warp
+      float d[32];
+      if (row_ok) {
+        const __nv_bfloat16* g = p.aux + static_cast<long long>(row) * p.ld_aux + 2 * (c0 + 16 * h);
+        load_bf16x16(g, d, 2 * vh);
+        load_bf16x16(g + 16, d + 16, 2 * vh - 16);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float x = d[2 * j], u = d[2 * j + 1], dy = v[16 * h + j];
+          const float sg = 1.f / (1.f + __expf(-x));
+          d[2 * j] = dy * u * (sg * (1.f + x * (1.f - sg)));
+          d[2 * j + 1] = dy * x * sg;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) d[j] = 0.f;
+      }
+      store_bf16_row32(C, p.ldc, p.M, row0, row, 2 * (c0 + 16 * h), d, vh >= 16 ? 32 : 2 * vh, lane, stg);
+    }
+    return;
+  }
   if (epi == TB_EPI_SWIGLU) {
     // interleaved gate/up columns: out[c/2] = silu(gate) * up
+    if (p.c2 != nullptr) store_bf16_row32(p.c2, p.ldc2, p.M, row0, row, c0, v, valid, lane, stg);
     if (!row_ok) return;
     const int oc0 = c0 / 2;
     const int Nout = N / 2;
@@ -532,7 +600,8 @@ __device__ __forceinline__ long long push_worker_of(long long i, long long nw, l
 // GEMM -> reduce-scatter (each output tile is stored into the receive slot of
 // the rank that owns its rows; tp_rs_finish_kernel sums the slots).  TP = 3:
 // split-K with the in-kernel fix-up (a separate instantiation keeps that code
-// out of the other variants' epilogue).
+// out of the other variants' epilogue).  TP = 4: plain GEMM with the
+// SwiGLU-backward epilogue (also a separate instantiation, for the same reason).
 template <int BN, bool A_MN, bool B_MN, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -835,12 +904,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
         if (n0 + c < p.N)
-          epilogue32(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[0], ax[1], ax[2], ax[3]);
+          epilogue32<TP == 4>(p, row, n0 + c, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[0], ax[1], ax[2],
+                              ax[3]);
         if constexpr (kStep == 64) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[32 + j]);
           if (n0 + c + 32 < p.N)
-            epilogue32(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[kStep / 8 - 4],
+            epilogue32<TP == 4>(p, row, n0 + c + 32, v, ks, lane, stg, m0 + sub * 32, mode, cbase, pre, ax[kStep / 8 - 4],
                        ax[kStep / 8 - 3], ax[kStep / 8 - 2], ax[kStep / 8 - 1]);
         }
       }
@@ -1232,8 +1302,14 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
       (reinterpret_cast<uintptr_t>(a->B) & 15))
     return static_cast<int>(cudaErrorInvalidValue);
   const bool swiglu = a->epi == TB_EPI_SWIGLU;
+  const bool swiglu_bwd = a->epi == TB_EPI_SWIGLU_BWD;
   if (swiglu && ((a->N % 2) || a->colsum)) return static_cast<int>(cudaErrorInvalidValue);
-  const bool ws_epi_ok = !swiglu;
+  if (swiglu_bwd && (a->a_mn || a->c_fp32 || a->aux == nullptr || a->colsum || a->c_accumulate || (a->ld_aux % 8) ||
+                     (reinterpret_cast<uintptr_t>(a->aux) & 15)))
+    return static_cast<int>(cudaErrorInvalidValue);
+  if (a->C2 && (!swiglu || (a->ldc2 % 8) || (reinterpret_cast<uintptr_t>(a->C2) & 15)))
+    return static_cast<int>(cudaErrorInvalidValue);
+  const bool ws_epi_ok = !swiglu && !swiglu_bwd;
   const bool atomic_ok = a->c_fp32 && (a->epi == TB_EPI_NONE || a->epi == TB_EPI_BIAS) && !a->colsum;
   const bool have_ws = a->workspace != nullptr && ws_epi_ok &&
                        a->workspace_bytes >= kCntBytes + 2 * sizeof(float) * static_cast<size_t>(a->M) * a->N;
@@ -1287,6 +1363,8 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.slot_cnt = fixup ? static_cast<int*>(a->workspace) : nullptr;
   p.colsum = (use_ws && !fixup) ? nullptr : a->colsum;
   p.error = a->error;
+  p.c2 = static_cast<__nv_bfloat16*>(a->C2);
+  p.ldc2 = a->ldc2;
   const int total = tiles * p.splits;
   const int grid = total < num_sms() ? total : num_sms();
   const int am = a->a_mn ? 1 : 0, bm = a->b_mn ? 1 : 0;
@@ -1296,11 +1374,15 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   else if (!am && bm) err = launch<BNV, false, true, MODE>(ta, tbm, p, grid, stream);  \
   else if (am && !bm) err = launch<BNV, true, false, MODE>(ta, tbm, p, grid, stream);  \
   else err = launch<BNV, true, true, MODE>(ta, tbm, p, grid, stream);
-#define TB_GEMM_DISPATCH(BNV)              \
-  if (fixup) {                             \
-    TB_GEMM_DISPATCH2(BNV, 3)              \
-  } else {                                 \
-    TB_GEMM_DISPATCH2(BNV, 0)              \
+#define TB_GEMM_DISPATCH(BNV)                                                      \
+  if (swiglu_bwd) {                                                                \
+    if (am) return static_cast<int>(cudaErrorInvalidValue);                        \
+    err = bm ? launch<BNV, false, true, 4>(ta, tbm, p, grid, stream)               \
+             : launch<BNV, false, false, 4>(ta, tbm, p, grid, stream);             \
+  } else if (fixup) {                                                              \
+    TB_GEMM_DISPATCH2(BNV, 3)                                                      \
+  } else {                                                                         \
+    TB_GEMM_DISPATCH2(BNV, 0)                                                      \
   }
   if (BN == 256) {
     TB_GEMM_DISPATCH(256)
@@ -1339,6 +1421,8 @@ size_t tb_tp_header_bytes(void) { return (sizeof(TpHdr) + 4095) / 4096 * 4096; }
 int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t stream) {
   const int W = c->world, mloc = c->rows_per_rank;
   if (a->M <= 0 || a->N <= 0) return 0;
+  if (a->epi == TB_EPI_SWIGLU_BWD || (a->C2 && a->epi != TB_EPI_SWIGLU))
+    return static_cast<int>(cudaErrorInvalidValue);
   if (a->a_mn || a->K <= 0 || a->K % 8 || a->lda % 8 || a->ldb % 8 || mloc % BM || a->M != W * mloc ||
       mloc / kTpSubRows > kTpMaxSub || a->workspace || a->colsum || a->c_accumulate ||
       c->parity_bytes < 2ll * a->M * a->K || c->parity_bytes % 16 || (reinterpret_cast<uintptr_t>(a->A) & 15) ||
@@ -1372,6 +1456,8 @@ int tb_tp_ag_gemm(const TbTpComm* c, const TbGemmArgs* a, cudaStream_t stream) {
   p.epi = a->epi;
   p.alpha = a->alpha == 0.f ? 1.f : a->alpha;
   p.error = a->error;
+  p.c2 = static_cast<__nv_bfloat16*>(a->C2);
+  p.ldc2 = a->ldc2;
   if (!fill_tp(&p.tp, c)) return static_cast<int>(cudaErrorInvalidValue);
   p.tp.shard = static_cast<const __nv_bfloat16*>(a->A);
   p.tp.ld_shard = a->lda;

@@ -125,6 +125,9 @@ enum {
   TB_EPI_TANH_BWD = 4,  // C = acc * (1 - aux^2)   (aux = saved tanh output)
   TB_EPI_RESIDUAL = 5,  // C = acc + aux
   TB_EPI_SWIGLU = 6,    // interleaved gate/up columns -> C[:, j] = silu(acc[2j]) * acc[2j+1]
+                        // (C2, optional: the raw interleaved gate/up accumulator, bf16 [M, N])
+  TB_EPI_SWIGLU_BWD = 7,  // acc = d out of out = silu(g) * u; aux = interleaved (g, u) bf16 [M, 2N];
+                          // C = interleaved (d g, d u) bf16 [M, 2N]
 };
 #define TB_GEMM_ERR_TIMEOUT 2
 typedef struct {
@@ -154,6 +157,8 @@ typedef struct {
   void* workspace;
   size_t workspace_bytes;
   float* colsum;           // optional [N] fp32: column sums of the output (e.g. a bias gradient)
+  void* C2;                // EPI_SWIGLU, optional bf16 [M, N]: also receives the raw gate/up accumulator
+  long long ldc2;
 } TbGemmArgs;
 
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);

@@ -173,3 +173,34 @@ def test_gemm_bn64_epilogues(dev):
     Cf = torch.empty(M, N, device=dev)
     o.gemm(A, B, Cf, bn=64, colsum=cs)
     assert torch.allclose(cs, ref.sum(0), atol=1.0, rtol=1e-2)
+
+
+@pytest.mark.parametrize("M,N,K,b_mn,bn", [(777, 512, 256, False, 0), (512, 8960, 1536, True, 0),
+                                            (300, 272, 320, True, 64), (256, 1024, 512, False, 128)])
+def test_gemm_swiglu_save_and_backward_epilogues(M, N, K, b_mn, bn, dev):
+    """SwiGLU forward writing the raw gate/up product too (c2), and the
+    SwiGLU-backward epilogue (d act -> interleaved d gate, d up), against fp32
+    autograd of silu(gate) * up."""
+    o = ops()
+    A = _mk((M, K), dev, 11)
+    B = _mk((K, 2 * N) if b_mn else (2 * N, K), dev, 12)
+    ref = _ref(A, B, False, b_mn)                               # [M, 2N] interleaved gate/up
+    act = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * N, device=dev, dtype=torch.bfloat16)
+    o.gemm(A, B, act, False, b_mn, epi=o.EPI_SWIGLU, c2=gu, bn=bn)
+    assert torch.allclose(gu.float(), ref, atol=3e-2, rtol=1e-2), (gu.float() - ref).abs().max()
+    g_, u_ = gu.float()[:, 0::2], gu.float()[:, 1::2]
+    assert torch.allclose(act.float(), torch.nn.functional.silu(g_) * u_, atol=5e-2, rtol=2e-2)
+    # backward: d act = dY . W (the down projection's input gradient), fused into d(gate, up)
+    Kd = 384
+    dY = _mk((M, Kd), dev, 13)
+    Wd = _mk((Kd, N) if b_mn else (N, Kd), dev, 14)       # W stored [K, N] (MN-major) or [N, K]
+    d_act = _ref(dY, Wd, False, b_mn)                           # [M, N]
+    d_gu = torch.empty(M, 2 * N, device=dev, dtype=torch.bfloat16)
+    o.gemm(dY, Wd, d_gu, False, b_mn, aux=gu, epi=o.EPI_SWIGLU_BWD, bn=bn)
+    g = g_.clone().requires_grad_()
+    u = u_.clone().requires_grad_()
+    (torch.nn.functional.silu(g) * u).backward(d_act)
+    exp = torch.stack([g.grad, u.grad], -1).reshape(M, 2 * N)
+    tol = 3e-2 * max(1.0, float(exp.abs().max()))
+    assert torch.allclose(d_gu.float(), exp, atol=tol, rtol=2e-2), (d_gu.float() - exp).abs().max()

@@ -261,9 +261,8 @@ class DecoderLM:
             o.flash_attn_fwd(q, k, v, a["attn"], a["lse"], B, T, cfg.n_heads, cfg.n_kv_heads, scale)
             o.gemm(a["attn"], self.s[P + "wo"], a["x2"], aux=x, epi=o.EPI_RESIDUAL)
             o.rmsnorm_fwd(a["x2"], self.f32[P + "ln2"], a["h2"], a["r2"], cfg.rms_eps)
-            if save:
-                o.gemm(a["h2"], self.s[P + "wgu"], a["gu"])
-                o.swiglu_fwd(a["gu"], a["act"])
+            if save:  # SwiGLU in the epilogue; the raw gate/up product is kept for the backward
+                o.gemm(a["h2"], self.s[P + "wgu"], a["act"], epi=o.EPI_SWIGLU, c2=a["gu"])
             else:
                 o.gemm(a["h2"], self.s[P + "wgu"], a["act"], epi=o.EPI_SWIGLU)
             xo = torch.empty(N, H, device=self.device, dtype=torch.bfloat16) if save else \
@@ -299,7 +298,6 @@ class DecoderLM:
         H, F, D = cfg.hidden, cfg.ffn, cfg.head_dim
         scale = 1.0 / math.sqrt(D)
         G = self.g
-        d_act = self._buf("d_act", (N, F))
         d_gu = self._buf("d_gu", (N, 2 * F))
         dh = self._buf("dh", (N, H))
         d_attn = self._buf("d_attn", (N, cfg.q_dim))
@@ -309,9 +307,9 @@ class DecoderLM:
         for i, a in zip(reversed(self.layers), reversed(saved)):
             P = f"l{i}."
             # ---- MLP
-            o.gemm(dx, self.s[P + "wdown"], d_act, False, True)                      # d act = dX Wdown
+            # d act = dX Wdown, turned into d(gate, up) by the SwiGLU-backward epilogue
+            o.gemm(dx, self.s[P + "wdown"], d_gu, False, True, aux=a["gu"], epi=o.EPI_SWIGLU_BWD)
             o.gemm(dx, a["act"], G[P + "wdown"], True, True, accumulate=True, split_k=1)  # dWdown += dX^T act
-            o.swiglu_bwd(a["gu"], d_act, d_gu)
             o.gemm(d_gu, self.s[P + "wgu"], dh, False, True)                        # dh2 = dGU Wgu
             o.gemm(d_gu, a["h2"], G[P + "wgu"], True, True, accumulate=True, split_k=1)  # dWgu += dGU^T h2
             dx2 = torch.empty(N, H, device=self.device, dtype=torch.bfloat16)

@@ -447,8 +447,8 @@ class TPTrainLM(TPDecoderLM):
             o.flash_attn_fwd(q, k, v, a["attn"], a["lse"], B, T, self.hq, self.hk, scale)
             a["x2"] = c.gemm_reduce_scatter(a["attn"], w[P + "wo"], residual=x)
             o.rmsnorm_fwd(a["x2"], w[P + "ln2"], a["h2"], a["r2"], cfg.rms_eps)
-            c.all_gather_gemm(a["h2"], w[P + "wgu"], out=a["gu"], gather_out=a["h2f"])
-            o.swiglu_fwd(a["gu"], a["act"])
+            c.all_gather_gemm(a["h2"], w[P + "wgu"], out=a["act"], epi=o.EPI_SWIGLU, gather_out=a["h2f"],
+                              c2=a["gu"])
             x = c.gemm_reduce_scatter(a["act"], w[P + "wdown"], residual=a["x2"])
             saved.append(a)
         return x, saved

@@ -63,10 +63,12 @@ class TensorParallelComm:
 
     # ------------------------------------------------------------------ ops
     def all_gather_gemm(self, shard: torch.Tensor, W: torch.Tensor, out: torch.Tensor = None, b_mn: bool = False,
-                        bias=None, aux=None, epi: int = 0, bn: int = 0, gather_out: torch.Tensor = None
-                        ) -> torch.Tensor:
+                        bias=None, aux=None, epi: int = 0, bn: int = 0, gather_out: torch.Tensor = None,
+                        c2: torch.Tensor = None) -> torch.Tensor:
         """gather_out (optional, bf16 [M, K]): also receives the gathered rows
-        (what the weight gradient of this projection needs in training)."""
+        (what the weight gradient of this projection needs in training).
+        c2 (optional, bf16 [M, N], with the SwiGLU epilogue): also receives the
+        raw gate/up product, which the SwiGLU backward needs."""
         M = shard.shape[0] * self.world
         K = shard.shape[1]
         N = W.shape[1] if b_mn else W.shape[0]
@@ -76,7 +78,7 @@ class TensorParallelComm:
             ncols = N // 2 if epi == _ops().EPI_SWIGLU else N
             out = torch.empty(M, ncols, device=shard.device, dtype=torch.bfloat16)
         self.pb.mem.tp_ag_gemm(0, self.ag_off, self.ag_half, self.ctr, shard, W, out, b_mn, bias, aux, epi, bn,
-                               gather_out)
+                               gather_out, c2)
         return out
 
     def gemm_reduce_scatter(self, A: torch.Tensor, W: torch.Tensor, out: torch.Tensor = None, b_mn: bool = False,
