@@ -1,0 +1,61 @@
+#!/usr/bin/env python
+"""The PPO actor-critic MLP's forward and backward alone (one GPU): the
+minibatch GEMMs of bench.py's headline workload (32,768 rows, hidden 256 per
+head, block-diagonal actor | critic) without the rest of the PPO step.
+
+  python benchmarks/bench_mlp_step.py [--rows 32768] [--reps 50]
+
+Prints the CUDA-event time of one forward + backward (the upstream gradient
+is a fixed random tensor), and its bytes/FLOPs; a small, self-contained
+command for ncu captures of these kernels.
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from turbol_b200.models.fused_mlp import PAD, FusedActorCritic  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", type=int, default=32768)
+    ap.add_argument("--hidden", type=int, default=256)
+    ap.add_argument("--reps", type=int, default=50)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    net = FusedActorCritic(4, 2, (a.hidden, a.hidden), device=dev, seed=0)
+    B = a.rows
+    ws = net.workspace(B)
+    x = torch.zeros(B, PAD, device=dev, dtype=torch.bfloat16)
+    x[:, :4] = torch.randn(B, 4, device=dev).to(torch.bfloat16)
+    dout = (torch.randn(B, 2 * PAD, device=dev) * 1e-3).to(torch.bfloat16)
+
+    def step():
+        net.forward(x, ws)
+        ws["dout"].copy_(dout)
+        net.grad.zero_()
+        net.backward(x, ws)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(a.reps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.reps
+    H2 = 2 * a.hidden
+    flops = 2 * B * (PAD * H2 + H2 * H2 + H2 * 2 * PAD) * 3
+    print(json.dumps({"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "us": us, "tflops": flops / us / 1e6,
+                      "activation_bytes_per_layer": B * H2 * 2}))
+
+
+if __name__ == "__main__":
+    main()
