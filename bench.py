@@ -233,9 +233,10 @@ def run_ours(args):
     e2e_value = steps_total / e2e_s
     tr.check_collectives()
     # our kernels per iteration: rollout step = 5 GEMMs + act/step kernel; bootstrap
-    # 5 GEMMs + pad; GAE 1; per minibatch gather + 5 fwd GEMMs + loss + 9 bwd GEMMs
-    # + 3 split-K reduces + optimizer (Adam or the fused DP kernel) + counter; end counter
-    per_mb = 1 + 5 + 1 + 9 + 3 + 1 + 1
+    # 5 GEMMs + pad; GAE 1; per minibatch: gather, first layer, 2 forward GEMMs, loss,
+    # 2 eight-wide weight-gradient passes, 4 backward GEMMs + 2 split-K reduces,
+    # optimizer (Adam or the fused DP kernel), counter; end counter
+    per_mb = 1 + 1 + 2 + 1 + 2 + 4 + 2 + 1 + 1
     launches_per_iter = cfg.rollout_steps * 6 + 6 + 1 + cfg.epochs * cfg.n_minibatches * per_mb + 1
     out = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,

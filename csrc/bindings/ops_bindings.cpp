@@ -383,6 +383,27 @@ void register_kernel_ops(py::module_& m) {
                             static_cast<int>(x.size(0)), static_cast<int>(W.size(0)), tanh_act ? 1 : 0, stream_of(x)),
             "dense_k8_fwd");
   }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true);
+  // out (fp32, contiguous) += A^T X for 8-wide X blocks; zeroed first unless accumulate
+  m.def("skinny8_wgrad", [](at::Tensor A, at::Tensor X, at::Tensor out, int xblock, int64_t os_j, int64_t os_k,
+                            int64_t os_blk, bool accumulate) {
+    TB_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
+             "skinny8_wgrad: A bf16 [M, N]");
+    TB_CHECK(X.is_cuda() && X.scalar_type() == at::kBFloat16 && X.dim() == 2 && X.stride(1) == 1 &&
+                 X.size(0) == A.size(0) && xblock > 0 && A.size(1) % xblock == 0 &&
+                 X.size(1) >= 8 * (A.size(1) / xblock),
+             "skinny8_wgrad: X bf16 [M, 8 * N / xblock]");
+    need(out, at::kFloat, "out");
+    TB_CHECK(out.is_contiguous(), "skinny8_wgrad: out must be contiguous");
+    const int64_t N = A.size(1), nb = N / xblock;
+    const int64_t last = (N - 1) * os_j + 7 * os_k + (nb - 1) * os_blk;
+    TB_CHECK(os_j >= 0 && os_k >= 0 && os_blk >= 0 && last < out.numel(), "skinny8_wgrad: out too small");
+    if (!accumulate) cuda_ok(static_cast<int>(cudaMemsetAsync(out.data_ptr(), 0, out.nbytes(), stream_of(A))),
+                             "skinny8_wgrad memset");
+    cuda_ok(tb_skinny8_wgrad(A.data_ptr(), A.stride(0), X.data_ptr(), X.stride(0), xblock, out.data_ptr<float>(), os_j,
+                             os_k, os_blk, static_cast<int>(A.size(0)), static_cast<int>(N), stream_of(A)),
+            "skinny8_wgrad");
+  }, py::arg("A"), py::arg("X"), py::arg("out"), py::arg("xblock"), py::arg("os_j"), py::arg("os_k"),
+     py::arg("os_blk") = 0, py::arg("accumulate") = false);
   m.def("dense_k8_wgrad", [](at::Tensor dz, at::Tensor x, at::Tensor dW, bool accumulate) {
     TB_CHECK(dz.is_cuda() && dz.scalar_type() == at::kBFloat16 && dz.dim() == 2 && dz.stride(1) == 1,
              "dense_k8_wgrad: dz bf16 [M, N]");

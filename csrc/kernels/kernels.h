@@ -90,6 +90,12 @@ int tb_lin_gauss_grad(const float* batch, int row_w, const float* params, float*
 int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
                     int N, int act, cudaStream_t s);
 // dW[N, 8] (fp32) = (or += with accumulate) dz[M, N]^T . x[M, 8] (bf16 inputs).
+// out = A^T X over M rows for 8-wide X (the weight gradient of a layer with 8
+// input or output features), A bf16 [M, N<=512], X bf16 [M, 8 * N/xblock]:
+// A's column block b pairs with X's columns [8b, 8b+8); out[(j, k)] at
+// j*os_j + k*os_k + b*os_blk, fp32, accumulated atomically (zero it first).
+int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
+                     long long os_j, long long os_k, long long os_blk, int M, int N, cudaStream_t s);
 int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
                       int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,

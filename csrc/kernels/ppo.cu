@@ -410,6 +410,66 @@ __global__ void __launch_bounds__(256) dense_k8_wgrad_kernel(const __nv_bfloat16
   for (int k = 0; k < 8; ++k) atomicAdd(dW + j * 8 + k, acc[k]);
 }
 
+// Weight gradient of a layer with 8 features on one side, out = A^T X summed
+// over M rows, with A bf16 [M, N] (N <= 512, N % 8 == 0) and X bf16 [M, 8]
+// per column block: columns [b*xblock, (b+1)*xblock) of A pair with X's
+// columns [8b, 8b+8) (block-diagonal heads).  out[(j, k)] at j*os_j + k*os_k
+// + b*os_blk (fp32, accumulated atomically: the caller zeroes it).  Each
+// thread owns 8 columns and keeps 64 products; 16-byte loads, 4 rows in flight
+// per thread, one CTA per SM, so the pass runs at memory bandwidth instead of
+// through a mostly-padding tensor-core tile plus a split-K reduce pass.
+constexpr int kSkThreads = 512, kSkUnroll = 4;
+__global__ void __launch_bounds__(kSkThreads) skinny8_wgrad_kernel(
+    const __nv_bfloat16* __restrict__ A, long long lda, const __nv_bfloat16* __restrict__ X, long long ldx,
+    int xblock, float* __restrict__ out, long long os_j, long long os_k, long long os_blk, int M, int N,
+    int rows_per_block) {
+  const int tpr = N / 8;  // threads per row
+  const int lanes = kSkThreads / tpr;
+  const int t = threadIdx.x % tpr, rl = threadIdx.x / tpr;
+  if (rl >= lanes) return;
+  const int j0 = 8 * t, blk = j0 / xblock;
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
+  float acc[8][8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[c][k] = 0.f;
+  for (int rb = r0 + rl; rb < r1; rb += lanes * kSkUnroll) {
+    uint4 a[kSkUnroll], x[kSkUnroll];
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const int r = rb + u * lanes;
+      const bool ok = r < r1;
+      a[u] = ok ? *reinterpret_cast<const uint4*>(A + static_cast<long long>(r) * lda + j0) : make_uint4(0u, 0u, 0u, 0u);
+      x[u] = ok ? *reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * ldx + 8 * blk)
+                : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
+      float av[8], xv[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fa = __bfloat1622float2(ah[q]), fx = __bfloat1622float2(xh[q]);
+        av[2 * q] = fa.x;
+        av[2 * q + 1] = fa.y;
+        xv[2 * q] = fx.x;
+        xv[2 * q + 1] = fx.y;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[c][k] = fmaf(av[c], xv[k], acc[c][k]);
+    }
+  }
+  float* o = out + blk * os_blk;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) atomicAdd(o + (j0 + c) * os_j + k * os_k, acc[c][k]);
+}
+
 }  // namespace
 
 extern "C" {
@@ -518,6 +578,23 @@ int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bi
   dense_k8_fwd_kernel<<<grid, rstep * groups, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx,
                                                       static_cast<const __nv_bfloat16*>(W), bias,
                                                       static_cast<__nv_bfloat16*>(y), ldy, M, N, act, rows);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
+                     long long os_j, long long os_k, long long os_blk, int M, int N, cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || lda % 8 || ldx % 8 ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(X) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int per = (M + sms - 1) / sms;
+  const int grid = (M + per - 1) / per;
+  skinny8_wgrad_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
+                                                    static_cast<const __nv_bfloat16*>(X), ldx, xblock, out, os_j,
+                                                    os_k, os_blk, M, N, per);
   return static_cast<int>(cudaGetLastError());
 }
 

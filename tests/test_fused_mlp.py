@@ -70,3 +70,26 @@ def test_dense_k8_kernels(dev):
     assert torch.allclose(dW, exp, atol=1e-2, rtol=1e-3)
     o.dense_k8_wgrad(dz, x, dW, True)
     assert torch.allclose(dW, 2 * exp, atol=2e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("N,xblock", [(512, 256), (512, 512), (128, 64), (256, 256)])
+def test_skinny8_wgrad(N, xblock, dev):
+    """out = A^T X per column block against fp32 torch, both output layouts."""
+    o = ops()
+    g = torch.Generator().manual_seed(N + xblock)
+    M = 33333
+    nb = N // xblock
+    A = torch.randn(M, N, generator=g).to(dev, torch.bfloat16)
+    X = torch.randn(M, 8 * nb, generator=g).to(dev, torch.bfloat16)
+    exp = torch.zeros(8 * nb, N)  # [k + 8b, j]
+    for b in range(nb):
+        cols = slice(b * xblock, (b + 1) * xblock)
+        exp[8 * b:8 * b + 8, cols] = X.float().cpu()[:, 8 * b:8 * b + 8].t() @ A.float().cpu()[:, cols]
+    out = torch.full((8 * nb, N), 3.0, device=dev)          # rows k + 8b, columns j (the w3 layout)
+    o.skinny8_wgrad(A, X, out, xblock, 1, N, 8 * N)
+    assert torch.allclose(out.cpu(), exp, atol=0.5, rtol=1e-3), (out.cpu() - exp).abs().max()
+    if nb == 1:
+        out2 = torch.zeros(N, 8, device=dev)                # [j, k] (the w1 layout)
+        o.skinny8_wgrad(A, X, out2, xblock, 8, 1)
+        o.skinny8_wgrad(A, X, out2, xblock, 8, 1, 0, True)  # accumulate
+        assert torch.allclose(out2.cpu(), 2 * exp.t(), atol=1.0, rtol=1e-3)
