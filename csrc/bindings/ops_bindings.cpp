@@ -404,6 +404,26 @@ void register_kernel_ops(py::module_& m) {
             "skinny8_wgrad");
   }, py::arg("A"), py::arg("X"), py::arg("out"), py::arg("xblock"), py::arg("os_j"), py::arg("os_k"),
      py::arg("os_blk") = 0, py::arg("accumulate") = false);
+  // dz = (dout W per head) * (1 - h^2); db (fp32 [N]) zeroed first unless accumulate, then += column sums
+  m.def("mlp_head_dz", [](at::Tensor dout, at::Tensor h, at::Tensor W, int xblock, at::Tensor dz, at::Tensor db,
+                          bool accumulate) {
+    for (auto* t : {&dout, &h, &W, &dz})
+      TB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
+               "mlp_head_dz: bf16 2-D CUDA tensors with a contiguous last dim");
+    const int64_t M = h.size(0), N = h.size(1);
+    TB_CHECK(xblock > 0 && N % xblock == 0 && dz.size(0) == M && dz.size(1) == N && dout.size(0) == M &&
+                 dout.size(1) >= 8 * (N / xblock) && W.size(0) >= 8 * (N / xblock) && W.size(1) == N,
+             "mlp_head_dz: shapes (dout [M, 8 heads], h/dz [M, N], W [8 heads, N])");
+    need(db, at::kFloat, "db");
+    TB_CHECK(db.is_contiguous() && db.numel() == N, "mlp_head_dz: db fp32 [N]");
+    if (!accumulate) cuda_ok(static_cast<int>(cudaMemsetAsync(db.data_ptr(), 0, db.nbytes(), stream_of(h))),
+                             "mlp_head_dz memset");
+    cuda_ok(tb_mlp_head_dz(dout.data_ptr(), dout.stride(0), h.data_ptr(), h.stride(0), W.data_ptr(), W.stride(0),
+                           xblock, dz.data_ptr(), dz.stride(0), db.data_ptr<float>(), static_cast<int>(M),
+                           static_cast<int>(N), stream_of(h)),
+            "mlp_head_dz");
+  }, py::arg("dout"), py::arg("h"), py::arg("W"), py::arg("xblock"), py::arg("dz"), py::arg("db"),
+     py::arg("accumulate") = false);
   m.def("dense_k8_wgrad", [](at::Tensor dz, at::Tensor x, at::Tensor dW, bool accumulate) {
     TB_CHECK(dz.is_cuda() && dz.scalar_type() == at::kBFloat16 && dz.dim() == 2 && dz.stride(1) == 1,
              "dense_k8_wgrad: dz bf16 [M, N]");

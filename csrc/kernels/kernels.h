@@ -96,6 +96,11 @@ int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bi
 // j*os_j + k*os_k + b*os_blk, fp32, accumulated atomically (zero it first).
 int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
                      long long os_j, long long os_k, long long os_blk, int M, int N, cudaStream_t s);
+// dZ = (dOut_b W_b) * (1 - H^2) per head b (8 outputs per head, xblock hidden
+// columns per head) and db += column sums of dZ: the backward of an output
+// layer with 8 outputs per head into a tanh layer.  db accumulates atomically.
+int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh, const void* W, long long ldw,
+                   int xblock, void* dz, long long ldz, float* db, int M, int N, cudaStream_t s);
 int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
                       int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,

@@ -470,6 +470,86 @@ __global__ void __launch_bounds__(kSkThreads) skinny8_wgrad_kernel(
     for (int k = 0; k < 8; ++k) atomicAdd(o + (j0 + c) * os_j + k * os_k, acc[c][k]);
 }
 
+// Backward through an output layer with 8 outputs per head into a tanh hidden
+// layer: dZ[r, j] = (sum_k dOut[r, 8b + k] W[8b + k, j]) * (1 - H[r, j]^2) for
+// the head b = j / xblock owning column j, and db[j] += sum_r dZ[r, j].
+// dOut bf16 [M, 8 * heads], H bf16 [M, N], W bf16 [8 * heads, N] (row
+// stride ldw), dZ bf16 [M, N]; db fp32 [N] (accumulated atomically: zeroed by
+// the caller).  Each thread keeps its 8 columns' 8 x 8 weights in registers and
+// streams rows with 16-byte loads, 4 rows in flight: a bandwidth-bound pass
+// instead of a K = 16 tensor-core GEMM whose time goes to its epilogue.
+__global__ void __launch_bounds__(kSkThreads) mlp_head_dz_kernel(
+    const __nv_bfloat16* __restrict__ dout, long long ldd, const __nv_bfloat16* __restrict__ H, long long ldh,
+    const __nv_bfloat16* __restrict__ W, long long ldw, int xblock, __nv_bfloat16* __restrict__ dz, long long ldz,
+    float* __restrict__ db, int M, int N, int rows_per_block) {
+  const int tpr = N / 8;
+  const int lanes = kSkThreads / tpr;
+  const int t = threadIdx.x % tpr, rl = threadIdx.x / tpr;
+  if (rl >= lanes) return;
+  const int j0 = 8 * t, blk = j0 / xblock;
+  float w[8][8];  // w[k][c] = W[8 blk + k, j0 + c]
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 u = *reinterpret_cast<const uint4*>(W + static_cast<long long>(8 * blk + k) * ldw + j0);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(h[q]);
+      w[k][2 * q] = f.x;
+      w[k][2 * q + 1] = f.y;
+    }
+  }
+  float dbs[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) dbs[c] = 0.f;
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
+  for (int rb = r0 + rl; rb < r1; rb += lanes * kSkUnroll) {
+    uint4 hu[kSkUnroll], du[kSkUnroll];
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const int r = rb + u * lanes;
+      const bool ok = r < r1;
+      hu[u] = ok ? *reinterpret_cast<const uint4*>(H + static_cast<long long>(r) * ldh + j0) : make_uint4(0u, 0u, 0u, 0u);
+      du[u] = ok ? *reinterpret_cast<const uint4*>(dout + static_cast<long long>(r) * ldd + 8 * blk)
+                 : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const int r = rb + u * lanes;
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&hu[u]);
+      const __nv_bfloat162* dh = reinterpret_cast<const __nv_bfloat162*>(&du[u]);
+      float hv[8], dv[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 fh = __bfloat1622float2(hh[q]), fd = __bfloat1622float2(dh[q]);
+        hv[2 * q] = fh.x;
+        hv[2 * q + 1] = fh.y;
+        dv[2 * q] = fd.x;
+        dv[2 * q + 1] = fd.y;
+      }
+      float o[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(dv[k], w[k][c], acc);
+        o[c] = acc * (1.f - hv[c] * hv[c]);
+      }
+      if (r < r1) {
+        uint4 pk;
+        __nv_bfloat162* ph = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ph[q] = __floats2bfloat162_rn(o[2 * q], o[2 * q + 1]);
+        *reinterpret_cast<uint4*>(dz + static_cast<long long>(r) * ldz + j0) = pk;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) dbs[c] += o[c];
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c) atomicAdd(db + j0 + c, dbs[c]);
+}
+
 }  // namespace
 
 extern "C" {
@@ -595,6 +675,25 @@ int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx,
   skinny8_wgrad_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
                                                     static_cast<const __nv_bfloat16*>(X), ldx, xblock, out, os_j,
                                                     os_k, os_blk, M, N, per);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh, const void* W, long long ldw,
+                   int xblock, void* dz, long long ldz, float* db, int M, int N, cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || ldd % 8 || ldh % 8 || ldw % 8 ||
+      ldz % 8 || (reinterpret_cast<uintptr_t>(dout) & 15) || (reinterpret_cast<uintptr_t>(H) & 15) ||
+      (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(dz) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int per = (M + sms - 1) / sms;
+  const int grid = (M + per - 1) / per;
+  mlp_head_dz_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(dout), ldd,
+                                                  static_cast<const __nv_bfloat16*>(H), ldh,
+                                                  static_cast<const __nv_bfloat16*>(W), ldw, xblock,
+                                                  static_cast<__nv_bfloat16*>(dz), ldz, db, M, N, per);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -93,3 +93,24 @@ def test_skinny8_wgrad(N, xblock, dev):
         o.skinny8_wgrad(A, X, out2, xblock, 8, 1)
         o.skinny8_wgrad(A, X, out2, xblock, 8, 1, 0, True)  # accumulate
         assert torch.allclose(out2.cpu(), 2 * exp.t(), atol=1.0, rtol=1e-3)
+
+
+@pytest.mark.parametrize("N,xblock", [(512, 256), (128, 64), (256, 256)])
+def test_mlp_head_dz(N, xblock, dev):
+    """dZ = (dOut_head W_head) * (1 - H^2) and db = column sums, against fp32 torch."""
+    o = ops()
+    g = torch.Generator().manual_seed(N)
+    M, nb = 20001, N // xblock
+    dout = (torch.randn(M, 8 * nb, generator=g) * 0.1).to(dev, torch.bfloat16)
+    h = torch.tanh(torch.randn(M, N, generator=g)).to(dev, torch.bfloat16)
+    W = (torch.randn(8 * nb, N, generator=g) * 0.2).to(dev, torch.bfloat16)
+    dz = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    db = torch.full((N,), 5.0, device=dev)
+    o.mlp_head_dz(dout, h, W, xblock, dz, db)
+    pre = torch.zeros(M, N, device=dev)
+    for b in range(nb):
+        cols = slice(b * xblock, (b + 1) * xblock)
+        pre[:, cols] = dout.float()[:, 8 * b:8 * b + 8] @ W.float()[8 * b:8 * b + 8, cols]
+    exp = pre * (1 - h.float() ** 2)
+    assert torch.allclose(dz.float(), exp, atol=1e-2, rtol=1e-2), (dz.float() - exp).abs().max()
+    assert torch.allclose(db, exp.sum(0), atol=0.05, rtol=1e-3), (db - exp.sum(0)).abs().max()

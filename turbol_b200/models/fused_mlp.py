@@ -12,7 +12,7 @@ epilogues:
   forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
             H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
-  backward  dZ2 = (dOut W3) * (1 - H2^2)    one GEMM + tanh-backward epilogue (+ db2 column sums)
+  backward  dZ2 = (dOut W3) * (1 - H2^2)    one bandwidth-bound CUDA-core pass (K = 8 per head) + db2
             dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM + tanh-backward epilogue (+ db1 column sums)
             dW2 = dZ2^T H1                  per diagonal block: MN-major x MN-major GEMM, split-K, fp32
             dW3, dW1                        8-wide side: one bandwidth-bound CUDA-core pass each
@@ -188,7 +188,7 @@ class FusedActorCritic:
         o.skinny8_wgrad(h2, dout, G["w3"], H, 1, 2 * H, PAD * 2 * H)
         if not out_bias_grads_done:
             o.colsum_bf16(dout, G["b3"])
-        o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])  # dZ2, db2
+        o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"])     # dZ2 = (dOut W3) * (1 - H2^2), db2: CUDA cores
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
             o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk)      # dW2 block = dZ2^T H1
         o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
