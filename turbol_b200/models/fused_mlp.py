@@ -12,10 +12,9 @@ epilogues:
   forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
             H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
-  backward  dZ2 = (dOut W3) * (1 - H2^2)    one bandwidth-bound CUDA-core pass (K = 8 per head) + db2
+  backward  dZ2 = (dOut W3) * (1 - H2^2)    one GEMM + tanh-backward epilogue (+ db2 column sums)
             dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM + tanh-backward epilogue (+ db1 column sums)
-            dW2 = dZ2^T H1                  per diagonal block: MN-major x MN-major GEMM, split-K, fp32
-            dW3, dW1                        8-wide side: one bandwidth-bound CUDA-core pass each
+            dW  = dZ^T H                    per diagonal block: MN-major x MN-major GEMM, split-K, fp32
 No transposes are materialized and no [B, H] fp32 intermediates exist:
 activations and activation gradients are bf16, weights are the bf16 shadow
 that the fused Adam writes next to the fp32 master copy, and weight gradients
@@ -183,13 +182,12 @@ class FusedActorCritic:
         S, G = self.s, self.g
         H = self.H
         h1, h2, dz2, dz1, dout, wsk = ws["h1"], ws["h2"], ws["dz2"], ws["dz1"], ws["dout"], ws["splitk"]
-        # dW3 diagonal blocks = dOut_head^T H2_head: 8 output rows per head, so a
-        # bandwidth-bound CUDA-core pass over H2 (no mostly-padding tensor-core tile)
-        o.skinny8_wgrad(h2, dout, G["w3"], H, 1, 2 * H, PAD * 2 * H)
+        for head, rows, cols in (("a", slice(0, PAD), slice(0, H)), ("c", slice(PAD, 2 * PAD), slice(H, 2 * H))):
+            o.gemm(dout[:, rows], h2[:, cols], G["w3" + head], True, True, workspace=wsk)   # dW3 block = dOut^T H2
         if not out_bias_grads_done:
             o.colsum_bf16(dout, G["b3"])
-        o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"])     # dZ2 = (dOut W3) * (1 - H2^2), db2: CUDA cores
+        o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])  # dZ2, db2
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
             o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk)      # dW2 block = dZ2^T H1
         o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
-        o.skinny8_wgrad(dz1, x_bf16, G["w1"], 2 * H, PAD, 1)                                  # dW1 = dZ1^T X
+        o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
