@@ -53,8 +53,40 @@ def main():
     us = e0.elapsed_time(e1) * 1e3 / a.reps
     H2 = 2 * a.hidden
     flops = 2 * B * (PAD * H2 + H2 * H2 + H2 * 2 * PAD) * 3
-    print(json.dumps({"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "us": us, "tflops": flops / us / 1e6,
-                      "activation_bytes_per_layer": B * H2 * 2}))
+    res = {"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "us": us, "tflops": flops / us / 1e6,
+           "activation_bytes_per_layer": B * H2 * 2}
+    # the three 8-wide pieces of the backward: tensor-core GEMM (+ split-K reduce)
+    # against the CUDA-core two-pass kernels
+    from turbol_b200._native import ops
+
+    o = ops()
+    S, G, H = net.s, net.g, a.hidden
+    h2, h1, dz2, dz1, wsk = ws["h2"], ws["h1"], ws["dz2"], ws["dz1"], ws["splitk"]
+    sc = torch.empty(o.skinny8_scratch_numel(H2), device=dev)
+
+    def t(fn, reps=50):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / reps
+
+    def dw3_gemm():
+        for head, rows, cols in (("a", slice(0, PAD), slice(0, H)), ("c", slice(PAD, 2 * PAD), slice(H, 2 * H))):
+            o.gemm(dout[:, rows], h2[:, cols], G["w3" + head], True, True, workspace=wsk)
+
+    res["dW3_us"] = {"gemm": t(dw3_gemm), "cuda_core": t(lambda: o.skinny8_wgrad(h2, dout, G["w3"], H, 1, H2,
+                                                                                 PAD * H2, False, sc))}
+    res["dZ2_us"] = {"gemm": t(lambda: o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD,
+                                              colsum=G["b2"])),
+                     "cuda_core": t(lambda: o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"], False, sc))}
+    res["dW1_us"] = {"gemm": t(lambda: o.gemm(dz1, x, G["w1"], True, True, workspace=wsk)),
+                     "cuda_core": t(lambda: o.skinny8_wgrad(dz1, x, G["w1"], H2, PAD, 1, 0, False, sc))}
+    print(json.dumps(res))
 
 
 if __name__ == "__main__":

@@ -383,9 +383,10 @@ void register_kernel_ops(py::module_& m) {
                             static_cast<int>(x.size(0)), static_cast<int>(W.size(0)), tanh_act ? 1 : 0, stream_of(x)),
             "dense_k8_fwd");
   }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true);
-  // out (fp32, contiguous) += A^T X for 8-wide X blocks; zeroed first unless accumulate
+  m.def("skinny8_scratch_numel", [](int N) { return static_cast<int64_t>(tb_skinny8_scratch_floats(N)); });
+  // out (fp32, contiguous) = A^T X for 8-wide X blocks (+= with accumulate); scratch fp32 per-CTA partials
   m.def("skinny8_wgrad", [](at::Tensor A, at::Tensor X, at::Tensor out, int xblock, int64_t os_j, int64_t os_k,
-                            int64_t os_blk, bool accumulate) {
+                            int64_t os_blk, bool accumulate, at::Tensor scratch) {
     TB_CHECK(A.is_cuda() && A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(1) == 1,
              "skinny8_wgrad: A bf16 [M, N]");
     TB_CHECK(X.is_cuda() && X.scalar_type() == at::kBFloat16 && X.dim() == 2 && X.stride(1) == 1 &&
@@ -393,20 +394,20 @@ void register_kernel_ops(py::module_& m) {
                  X.size(1) >= 8 * (A.size(1) / xblock),
              "skinny8_wgrad: X bf16 [M, 8 * N / xblock]");
     need(out, at::kFloat, "out");
-    TB_CHECK(out.is_contiguous(), "skinny8_wgrad: out must be contiguous");
+    need(scratch, at::kFloat, "scratch");
+    TB_CHECK(out.is_contiguous() && scratch.is_contiguous(), "skinny8_wgrad: contiguous out and scratch");
     const int64_t N = A.size(1), nb = N / xblock;
     const int64_t last = (N - 1) * os_j + 7 * os_k + (nb - 1) * os_blk;
     TB_CHECK(os_j >= 0 && os_k >= 0 && os_blk >= 0 && last < out.numel(), "skinny8_wgrad: out too small");
-    if (!accumulate) cuda_ok(static_cast<int>(cudaMemsetAsync(out.data_ptr(), 0, out.nbytes(), stream_of(A))),
-                             "skinny8_wgrad memset");
     cuda_ok(tb_skinny8_wgrad(A.data_ptr(), A.stride(0), X.data_ptr(), X.stride(0), xblock, out.data_ptr<float>(), os_j,
-                             os_k, os_blk, static_cast<int>(A.size(0)), static_cast<int>(N), stream_of(A)),
+                             os_k, os_blk, static_cast<int>(A.size(0)), static_cast<int>(N), accumulate ? 1 : 0,
+                             scratch.data_ptr<float>(), static_cast<size_t>(scratch.numel()), stream_of(A)),
             "skinny8_wgrad");
   }, py::arg("A"), py::arg("X"), py::arg("out"), py::arg("xblock"), py::arg("os_j"), py::arg("os_k"),
-     py::arg("os_blk") = 0, py::arg("accumulate") = false);
-  // dz = (dout W per head) * (1 - h^2); db (fp32 [N]) zeroed first unless accumulate, then += column sums
+     py::arg("os_blk"), py::arg("accumulate"), py::arg("scratch"));
+  // dz = (dout W per head) * (1 - h^2); db (fp32 [N]) = column sums of dz (+= with accumulate)
   m.def("mlp_head_dz", [](at::Tensor dout, at::Tensor h, at::Tensor W, int xblock, at::Tensor dz, at::Tensor db,
-                          bool accumulate) {
+                          bool accumulate, at::Tensor scratch) {
     for (auto* t : {&dout, &h, &W, &dz})
       TB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
                "mlp_head_dz: bf16 2-D CUDA tensors with a contiguous last dim");
@@ -415,15 +416,15 @@ void register_kernel_ops(py::module_& m) {
                  dout.size(1) >= 8 * (N / xblock) && W.size(0) >= 8 * (N / xblock) && W.size(1) == N,
              "mlp_head_dz: shapes (dout [M, 8 heads], h/dz [M, N], W [8 heads, N])");
     need(db, at::kFloat, "db");
-    TB_CHECK(db.is_contiguous() && db.numel() == N, "mlp_head_dz: db fp32 [N]");
-    if (!accumulate) cuda_ok(static_cast<int>(cudaMemsetAsync(db.data_ptr(), 0, db.nbytes(), stream_of(h))),
-                             "mlp_head_dz memset");
+    need(scratch, at::kFloat, "scratch");
+    TB_CHECK(db.is_contiguous() && db.numel() == N && scratch.is_contiguous(), "mlp_head_dz: db fp32 [N]");
     cuda_ok(tb_mlp_head_dz(dout.data_ptr(), dout.stride(0), h.data_ptr(), h.stride(0), W.data_ptr(), W.stride(0),
                            xblock, dz.data_ptr(), dz.stride(0), db.data_ptr<float>(), static_cast<int>(M),
-                           static_cast<int>(N), stream_of(h)),
+                           static_cast<int>(N), accumulate ? 1 : 0, scratch.data_ptr<float>(),
+                           static_cast<size_t>(scratch.numel()), stream_of(h)),
             "mlp_head_dz");
   }, py::arg("dout"), py::arg("h"), py::arg("W"), py::arg("xblock"), py::arg("dz"), py::arg("db"),
-     py::arg("accumulate") = false);
+     py::arg("accumulate"), py::arg("scratch"));
   m.def("dense_k8_wgrad", [](at::Tensor dz, at::Tensor x, at::Tensor dW, bool accumulate) {
     TB_CHECK(dz.is_cuda() && dz.scalar_type() == at::kBFloat16 && dz.dim() == 2 && dz.stride(1) == 1,
              "dense_k8_wgrad: dz bf16 [M, N]");

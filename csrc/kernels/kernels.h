@@ -93,14 +93,18 @@ int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bi
 // out = A^T X over M rows for 8-wide X (the weight gradient of a layer with 8
 // input or output features), A bf16 [M, N<=512], X bf16 [M, 8 * N/xblock]:
 // A's column block b pairs with X's columns [8b, 8b+8); out[(j, k)] at
-// j*os_j + k*os_k + b*os_blk, fp32, accumulated atomically (zero it first).
+// j*os_j + k*os_k + b*os_blk, fp32, stored (or added with accumulate).
+// scratch: tb_skinny8_scratch_floats(N) floats for the per-CTA partials.
+size_t tb_skinny8_scratch_floats(int N);
 int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
-                     long long os_j, long long os_k, long long os_blk, int M, int N, cudaStream_t s);
+                     long long os_j, long long os_k, long long os_blk, int M, int N, int accumulate, float* scratch,
+                     size_t scratch_floats, cudaStream_t s);
 // dZ = (dOut_b W_b) * (1 - H^2) per head b (8 outputs per head, xblock hidden
-// columns per head) and db += column sums of dZ: the backward of an output
-// layer with 8 outputs per head into a tanh layer.  db accumulates atomically.
+// columns per head) and db (+)= column sums of dZ: the backward of an output
+// layer with 8 outputs per head into a tanh layer.  scratch as above.
 int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh, const void* W, long long ldw,
-                   int xblock, void* dz, long long ldz, float* db, int M, int N, cudaStream_t s);
+                   int xblock, void* dz, long long ldz, float* db, int M, int N, int accumulate, float* scratch,
+                   size_t scratch_floats, cudaStream_t s);
 int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
                       int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,

@@ -413,61 +413,81 @@ __global__ void __launch_bounds__(256) dense_k8_wgrad_kernel(const __nv_bfloat16
 // Weight gradient of a layer with 8 features on one side, out = A^T X summed
 // over M rows, with A bf16 [M, N] (N <= 512, N % 8 == 0) and X bf16 [M, 8]
 // per column block: columns [b*xblock, (b+1)*xblock) of A pair with X's
-// columns [8b, 8b+8) (block-diagonal heads).  out[(j, k)] at j*os_j + k*os_k
-// + b*os_blk (fp32, accumulated atomically: the caller zeroes it).  Each
-// thread owns 8 columns and keeps 64 products; 16-byte loads, 4 rows in flight
-// per thread, one CTA per SM, so the pass runs at memory bandwidth instead of
-// through a mostly-padding tensor-core tile plus a split-K reduce pass.
+// columns [8b, 8b+8) (block-diagonal heads).  Two passes, no global atomics:
+// each CTA streams a slice of the rows (every thread owns 8 columns and keeps
+// 64 products; 16-byte loads, 4 rows in flight), sums its row-lanes in shared
+// memory and writes one partial [N * 8] to `part`; skinny8_reduce_kernel adds
+// the CTAs' partials and writes out[(j, k)] at j*os_j + k*os_k + b*os_blk.
 constexpr int kSkThreads = 512, kSkUnroll = 4;
-__global__ void __launch_bounds__(kSkThreads) skinny8_wgrad_kernel(
+__global__ void __launch_bounds__(kSkThreads) skinny8_partial_kernel(
     const __nv_bfloat16* __restrict__ A, long long lda, const __nv_bfloat16* __restrict__ X, long long ldx,
-    int xblock, float* __restrict__ out, long long os_j, long long os_k, long long os_blk, int M, int N,
-    int rows_per_block) {
+    int xblock, float* __restrict__ part, int M, int N, int rows_per_block) {
+  __shared__ float red[512 * 8];
   const int tpr = N / 8;  // threads per row
   const int lanes = kSkThreads / tpr;
   const int t = threadIdx.x % tpr, rl = threadIdx.x / tpr;
-  if (rl >= lanes) return;
-  const int j0 = 8 * t, blk = j0 / xblock;
-  const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
-  float acc[8][8];
+  for (int i = threadIdx.x; i < N * 8; i += blockDim.x) red[i] = 0.f;
+  __syncthreads();
+  if (rl < lanes) {
+    const int j0 = 8 * t, blk = j0 / xblock;
+    const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
+    float acc[8][8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c)
+    for (int c = 0; c < 8; ++c)
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc[c][k] = 0.f;
-  for (int rb = r0 + rl; rb < r1; rb += lanes * kSkUnroll) {
-    uint4 a[kSkUnroll], x[kSkUnroll];
+      for (int k = 0; k < 8; ++k) acc[c][k] = 0.f;
+    for (int rb = r0 + rl; rb < r1; rb += lanes * kSkUnroll) {
+      uint4 a[kSkUnroll], x[kSkUnroll];
 #pragma unroll
-    for (int u = 0; u < kSkUnroll; ++u) {
-      const int r = rb + u * lanes;
-      const bool ok = r < r1;
-      a[u] = ok ? *reinterpret_cast<const uint4*>(A + static_cast<long long>(r) * lda + j0) : make_uint4(0u, 0u, 0u, 0u);
-      x[u] = ok ? *reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * ldx + 8 * blk)
-                : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int u = 0; u < kSkUnroll; ++u) {
-      const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
-      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
-      float av[8], xv[8];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 fa = __bfloat1622float2(ah[q]), fx = __bfloat1622float2(xh[q]);
-        av[2 * q] = fa.x;
-        av[2 * q + 1] = fa.y;
-        xv[2 * q] = fx.x;
-        xv[2 * q + 1] = fx.y;
+      for (int u = 0; u < kSkUnroll; ++u) {
+        const int r = rb + u * lanes;
+        const bool ok = r < r1;
+        a[u] = ok ? *reinterpret_cast<const uint4*>(A + static_cast<long long>(r) * lda + j0)
+                  : make_uint4(0u, 0u, 0u, 0u);
+        x[u] = ok ? *reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * ldx + 8 * blk)
+                  : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
+      for (int u = 0; u < kSkUnroll; ++u) {
+        const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
+        float av[8], xv[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[c][k] = fmaf(av[c], xv[k], acc[c][k]);
+        for (int q = 0; q < 4; ++q) {
+          const float2 fa = __bfloat1622float2(ah[q]), fx = __bfloat1622float2(xh[q]);
+          av[2 * q] = fa.x;
+          av[2 * q + 1] = fa.y;
+          xv[2 * q] = fx.x;
+          xv[2 * q + 1] = fx.y;
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[c][k] = fmaf(av[c], xv[k], acc[c][k]);
+      }
     }
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) atomicAdd(&red[(j0 + c) * 8 + k], acc[c][k]);  // shared memory
   }
-  float* o = out + blk * os_blk;
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) atomicAdd(o + (j0 + c) * os_j + k * os_k, acc[c][k]);
+  __syncthreads();
+  float* dst = part + static_cast<long long>(blockIdx.x) * N * 8;
+  for (int i = threadIdx.x; i < N * 8; i += blockDim.x) dst[i] = red[i];
+}
+
+// Sums `parts` partials [parts, N * 8] and stores (or adds) them at the
+// caller's layout (see skinny8_partial_kernel).
+__global__ void skinny8_reduce_kernel(const float* __restrict__ part, int parts, int N, int xblock,
+                                      float* __restrict__ out, long long os_j, long long os_k, long long os_blk,
+                                      int accumulate) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N * 8) return;
+  float s = 0.f;
+  for (int b = 0; b < parts; ++b) s += part[static_cast<long long>(b) * N * 8 + i];
+  const int j = i / 8, k = i % 8;
+  float* o = out + (j / xblock) * os_blk + j * os_j + k * os_k;
+  *o = accumulate ? *o + s : s;
 }
 
 // Backward through an output layer with 8 outputs per head into a tanh hidden
@@ -481,12 +501,15 @@ __global__ void __launch_bounds__(kSkThreads) skinny8_wgrad_kernel(
 __global__ void __launch_bounds__(kSkThreads) mlp_head_dz_kernel(
     const __nv_bfloat16* __restrict__ dout, long long ldd, const __nv_bfloat16* __restrict__ H, long long ldh,
     const __nv_bfloat16* __restrict__ W, long long ldw, int xblock, __nv_bfloat16* __restrict__ dz, long long ldz,
-    float* __restrict__ db, int M, int N, int rows_per_block) {
+    float* __restrict__ part, int M, int N, int rows_per_block) {
+  __shared__ float red[512];
   const int tpr = N / 8;
   const int lanes = kSkThreads / tpr;
   const int t = threadIdx.x % tpr, rl = threadIdx.x / tpr;
-  if (rl >= lanes) return;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) red[i] = 0.f;
+  __syncthreads();
   const int j0 = 8 * t, blk = j0 / xblock;
+  if (rl < lanes) {
   float w[8][8];  // w[k][c] = W[8 blk + k, j0 + c]
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
@@ -547,7 +570,20 @@ __global__ void __launch_bounds__(kSkThreads) mlp_head_dz_kernel(
     }
   }
 #pragma unroll
-  for (int c = 0; c < 8; ++c) atomicAdd(db + j0 + c, dbs[c]);
+  for (int c = 0; c < 8; ++c) atomicAdd(&red[j0 + c], dbs[c]);  // shared memory
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += blockDim.x) part[static_cast<long long>(blockIdx.x) * N + i] = red[i];
+}
+
+// db[j] (+)= sum over the CTAs' partials [parts, N].
+__global__ void colsum_parts_kernel(const float* __restrict__ part, int parts, int N, float* __restrict__ db,
+                                    int accumulate) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= N) return;
+  float s = 0.f;
+  for (int b = 0; b < parts; ++b) s += part[static_cast<long long>(b) * N + j];
+  db[j] = accumulate ? db[j] + s : s;
 }
 
 }  // namespace
@@ -661,39 +697,53 @@ int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bi
   return static_cast<int>(cudaGetLastError());
 }
 
-int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
-                     long long os_j, long long os_k, long long os_blk, int M, int N, cudaStream_t s) {
-  if (M <= 0) return 0;
-  if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || lda % 8 || ldx % 8 ||
-      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(X) & 15))
-    return static_cast<int>(cudaErrorInvalidValue);
-  int sms = 148;
-  int dev = 0;
+static int sk_grid(int M, int* per) {  // one CTA per SM, each a contiguous slice of rows
+  int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int per = (M + sms - 1) / sms;
-  const int grid = (M + per - 1) / per;
-  skinny8_wgrad_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
-                                                    static_cast<const __nv_bfloat16*>(X), ldx, xblock, out, os_j,
-                                                    os_k, os_blk, M, N, per);
+  *per = (M + sms - 1) / sms;
+  return (M + *per - 1) / *per;
+}
+
+size_t tb_skinny8_scratch_floats(int N) {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return static_cast<size_t>(sms) * 8 * static_cast<size_t>(N > 0 ? N : 0);
+}
+
+int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
+                     long long os_j, long long os_k, long long os_blk, int M, int N, int accumulate, float* scratch,
+                     size_t scratch_floats, cudaStream_t s) {
+  if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || lda % 8 || ldx % 8 ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) || M < 0)
+    return static_cast<int>(cudaErrorInvalidValue);
+  int per = 1;
+  const int grid = M > 0 ? sk_grid(M, &per) : 0;
+  if (static_cast<size_t>(grid) * N * 8 > scratch_floats) return static_cast<int>(cudaErrorInvalidValue);
+  if (grid > 0)
+    skinny8_partial_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
+                                                        static_cast<const __nv_bfloat16*>(X), ldx, xblock, scratch,
+                                                        M, N, per);
+  skinny8_reduce_kernel<<<(N * 8 + 255) / 256, 256, 0, s>>>(scratch, grid, N, xblock, out, os_j, os_k, os_blk,
+                                                             accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 
 int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh, const void* W, long long ldw,
-                   int xblock, void* dz, long long ldz, float* db, int M, int N, cudaStream_t s) {
-  if (M <= 0) return 0;
+                   int xblock, void* dz, long long ldz, float* db, int M, int N, int accumulate, float* scratch,
+                   size_t scratch_floats, cudaStream_t s) {
   if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || ldd % 8 || ldh % 8 || ldw % 8 ||
       ldz % 8 || (reinterpret_cast<uintptr_t>(dout) & 15) || (reinterpret_cast<uintptr_t>(H) & 15) ||
-      (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(dz) & 15))
+      (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(dz) & 15) || M < 0)
     return static_cast<int>(cudaErrorInvalidValue);
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int per = (M + sms - 1) / sms;
-  const int grid = (M + per - 1) / per;
-  mlp_head_dz_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(dout), ldd,
-                                                  static_cast<const __nv_bfloat16*>(H), ldh,
-                                                  static_cast<const __nv_bfloat16*>(W), ldw, xblock,
-                                                  static_cast<__nv_bfloat16*>(dz), ldz, db, M, N, per);
+  int per = 1;
+  const int grid = M > 0 ? sk_grid(M, &per) : 0;
+  if (static_cast<size_t>(grid) * N > scratch_floats) return static_cast<int>(cudaErrorInvalidValue);
+  if (grid > 0)
+    mlp_head_dz_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(dout), ldd,
+                                                    static_cast<const __nv_bfloat16*>(H), ldh,
+                                                    static_cast<const __nv_bfloat16*>(W), ldw, xblock,
+                                                    static_cast<__nv_bfloat16*>(dz), ldz, scratch, M, N, per);
+  colsum_parts_kernel<<<(N + 255) / 256, 256, 0, s>>>(scratch, grid, N, db, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -85,13 +85,14 @@ def test_skinny8_wgrad(N, xblock, dev):
     for b in range(nb):
         cols = slice(b * xblock, (b + 1) * xblock)
         exp[8 * b:8 * b + 8, cols] = X.float().cpu()[:, 8 * b:8 * b + 8].t() @ A.float().cpu()[:, cols]
+    sc = torch.empty(o.skinny8_scratch_numel(N), device=dev)
     out = torch.full((8 * nb, N), 3.0, device=dev)          # rows k + 8b, columns j (the w3 layout)
-    o.skinny8_wgrad(A, X, out, xblock, 1, N, 8 * N)
+    o.skinny8_wgrad(A, X, out, xblock, 1, N, 8 * N, False, sc)
     assert torch.allclose(out.cpu(), exp, atol=0.5, rtol=1e-3), (out.cpu() - exp).abs().max()
     if nb == 1:
         out2 = torch.zeros(N, 8, device=dev)                # [j, k] (the w1 layout)
-        o.skinny8_wgrad(A, X, out2, xblock, 8, 1)
-        o.skinny8_wgrad(A, X, out2, xblock, 8, 1, 0, True)  # accumulate
+        o.skinny8_wgrad(A, X, out2, xblock, 8, 1, 0, False, sc)
+        o.skinny8_wgrad(A, X, out2, xblock, 8, 1, 0, True, sc)  # accumulate
         assert torch.allclose(out2.cpu(), 2 * exp.t(), atol=1.0, rtol=1e-3)
 
 
@@ -106,7 +107,8 @@ def test_mlp_head_dz(N, xblock, dev):
     W = (torch.randn(8 * nb, N, generator=g) * 0.2).to(dev, torch.bfloat16)
     dz = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
     db = torch.full((N,), 5.0, device=dev)
-    o.mlp_head_dz(dout, h, W, xblock, dz, db)
+    sc = torch.empty(o.skinny8_scratch_numel(N), device=dev)
+    o.mlp_head_dz(dout, h, W, xblock, dz, db, False, sc)
     pre = torch.zeros(M, N, device=dev)
     for b in range(nb):
         cols = slice(b * xblock, (b + 1) * xblock)
