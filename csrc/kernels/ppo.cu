@@ -411,83 +411,111 @@ __global__ void __launch_bounds__(256) dense_k8_wgrad_kernel(const __nv_bfloat16
 }
 
 // Weight gradient of a layer with 8 features on one side, out = A^T X summed
-// over M rows, with A bf16 [M, N] (N <= 512, N % 8 == 0) and X bf16 [M, 8]
+// over M rows, with A bf16 [M, N] (N <= 512, N % 32 == 0) and X bf16 [M, 8]
 // per column block: columns [b*xblock, (b+1)*xblock) of A pair with X's
-// columns [8b, 8b+8) (block-diagonal heads).  Two passes, no global atomics:
-// each CTA streams a slice of the rows (every thread owns 8 columns and keeps
-// 64 products; 16-byte loads, 4 rows in flight), sums its row-lanes in shared
-// memory and writes one partial [N * 8] to `part`; skinny8_reduce_kernel adds
+// columns [8b, 8b+8) (block-diagonal heads).  Two passes, no atomics: in
+// skinny8_partial_kernel a warp covers 32 columns (4 threads of 8 columns) x 8
+// row-lanes, streams a slice of the rows with 16-byte loads (4 rows in flight
+// per thread, 64 products per thread), folds its row-lanes with shuffles and
+// writes one partial [N * 8] per CTA to `part`; skinny8_reduce_kernel adds
 // the CTAs' partials and writes out[(j, k)] at j*os_j + k*os_k + b*os_blk.
-constexpr int kSkThreads = 512, kSkUnroll = 4;
-__global__ void __launch_bounds__(kSkThreads) skinny8_partial_kernel(
+constexpr int kSkUnroll = 4;
+constexpr int kSkThreads = 512;  // mlp_head_dz_kernel
+__global__ void __launch_bounds__(512) skinny8_partial_kernel(
     const __nv_bfloat16* __restrict__ A, long long lda, const __nv_bfloat16* __restrict__ X, long long ldx,
     int xblock, float* __restrict__ part, int M, int N, int rows_per_block) {
-  __shared__ float red[512 * 8];
-  const int tpr = N / 8;  // threads per row
-  const int lanes = kSkThreads / tpr;
-  const int t = threadIdx.x % tpr, rl = threadIdx.x / tpr;
-  for (int i = threadIdx.x; i < N * 8; i += blockDim.x) red[i] = 0.f;
-  __syncthreads();
-  if (rl < lanes) {
-    const int j0 = 8 * t, blk = j0 / xblock;
-    const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
-    float acc[8][8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int tc = lane & 3, rl = lane >> 2;  // column thread within the warp's 32 columns, row-lane 0..7
+  const int j0 = warp * 32 + tc * 8, blk = j0 / xblock;
+  const int r0 = blockIdx.x * rows_per_block, r1 = min(M, r0 + rows_per_block);
+  float acc[8][8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
+  for (int c = 0; c < 8; ++c)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) acc[c][k] = 0.f;
-    for (int rb = r0 + rl; rb < r1; rb += lanes * kSkUnroll) {
-      uint4 a[kSkUnroll], x[kSkUnroll];
+    for (int k = 0; k < 8; ++k) acc[c][k] = 0.f;
+  for (int rb = r0 + rl; rb < r1; rb += 8 * kSkUnroll) {
+    uint4 a[kSkUnroll], x[kSkUnroll];
 #pragma unroll
-      for (int u = 0; u < kSkUnroll; ++u) {
-        const int r = rb + u * lanes;
-        const bool ok = r < r1;
-        a[u] = ok ? *reinterpret_cast<const uint4*>(A + static_cast<long long>(r) * lda + j0)
-                  : make_uint4(0u, 0u, 0u, 0u);
-        x[u] = ok ? *reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * ldx + 8 * blk)
-                  : make_uint4(0u, 0u, 0u, 0u);
-      }
-#pragma unroll
-      for (int u = 0; u < kSkUnroll; ++u) {
-        const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
-        const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
-        float av[8], xv[8];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 fa = __bfloat1622float2(ah[q]), fx = __bfloat1622float2(xh[q]);
-          av[2 * q] = fa.x;
-          av[2 * q + 1] = fa.y;
-          xv[2 * q] = fx.x;
-          xv[2 * q + 1] = fx.y;
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-#pragma unroll
-          for (int k = 0; k < 8; ++k) acc[c][k] = fmaf(av[c], xv[k], acc[c][k]);
-      }
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const int r = rb + 8 * u;
+      const bool ok = r < r1;
+      a[u] = ok ? *reinterpret_cast<const uint4*>(A + static_cast<long long>(r) * lda + j0) : make_uint4(0u, 0u, 0u, 0u);
+      x[u] = ok ? *reinterpret_cast<const uint4*>(X + static_cast<long long>(r) * ldx + 8 * blk)
+                : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
+    for (int u = 0; u < kSkUnroll; ++u) {
+      const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+      const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
+      float av[8], xv[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) atomicAdd(&red[(j0 + c) * 8 + k], acc[c][k]);  // shared memory
+      for (int q = 0; q < 4; ++q) {
+        const float2 fa = __bfloat1622float2(ah[q]), fx = __bfloat1622float2(xh[q]);
+        av[2 * q] = fa.x;
+        av[2 * q + 1] = fa.y;
+        xv[2 * q] = fx.x;
+        xv[2 * q + 1] = fx.y;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[c][k] = fmaf(av[c], xv[k], acc[c][k]);
+    }
   }
-  __syncthreads();
-  float* dst = part + static_cast<long long>(blockIdx.x) * N * 8;
-  for (int i = threadIdx.x; i < N * 8; i += blockDim.x) dst[i] = red[i];
+  // fold the 8 row-lanes (lane bits 2..4); every lane of a column thread ends with the sums
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float v = acc[c][k];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      acc[c][k] = v;
+    }
+  // row-lane rl stores column j0 + rl's 8 values
+  float* dst = part + static_cast<long long>(blockIdx.x) * N * 8 + (j0 + rl) * 8;
+  float outv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float v = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) v = (c == rl) ? acc[c][k] : v;
+    outv[k] = v;
+  }
+  reinterpret_cast<float4*>(dst)[0] = make_float4(outv[0], outv[1], outv[2], outv[3]);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(outv[4], outv[5], outv[6], outv[7]);
 }
 
-// Sums `parts` partials [parts, N * 8] and stores (or adds) them at the
-// caller's layout (see skinny8_partial_kernel).
-__global__ void skinny8_reduce_kernel(const float* __restrict__ part, int parts, int N, int xblock,
-                                      float* __restrict__ out, long long os_j, long long os_k, long long os_blk,
-                                      int accumulate) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= N * 8) return;
+// Sum of `parts` partials part[b * n + i] for n outputs: 32 outputs per CTA,
+// 32 thread groups each summing every 32nd partial, then a shared-memory fold.
+// Element i goes to out[map(i)] (store, or add with accumulate).
+template <typename Map>
+__device__ __forceinline__ void reduce_parts(const float* __restrict__ part, int parts, int n, int accumulate,
+                                             Map map) {
+  __shared__ float sm[32][33];
+  const int oi = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + oi;
   float s = 0.f;
-  for (int b = 0; b < parts; ++b) s += part[static_cast<long long>(b) * N * 8 + i];
-  const int j = i / 8, k = i % 8;
-  float* o = out + (j / xblock) * os_blk + j * os_j + k * os_k;
-  *o = accumulate ? *o + s : s;
+  if (i < n)
+    for (int b = g; b < parts; b += 32) s += part[static_cast<long long>(b) * n + i];
+  sm[g][oi] = s;
+  __syncthreads();
+  if (g == 0 && i < n) {
+    float t = 0.f;
+    for (int q = 0; q < 32; ++q) t += sm[q][oi];
+    float* o = map(i);
+    *o = accumulate ? *o + t : t;
+  }
+}
+
+__global__ void __launch_bounds__(1024) skinny8_reduce_kernel(const float* __restrict__ part, int parts, int N,
+                                                              int xblock, float* __restrict__ out, long long os_j,
+                                                              long long os_k, long long os_blk, int accumulate) {
+  reduce_parts(part, parts, N * 8, accumulate, [&](int i) {
+    const int j = i / 8, k = i % 8;
+    return out + (j / xblock) * os_blk + j * os_j + k * os_k;
+  });
 }
 
 // Backward through an output layer with 8 outputs per head into a tanh hidden
@@ -577,13 +605,9 @@ __global__ void __launch_bounds__(kSkThreads) mlp_head_dz_kernel(
 }
 
 // db[j] (+)= sum over the CTAs' partials [parts, N].
-__global__ void colsum_parts_kernel(const float* __restrict__ part, int parts, int N, float* __restrict__ db,
-                                    int accumulate) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= N) return;
-  float s = 0.f;
-  for (int b = 0; b < parts; ++b) s += part[static_cast<long long>(b) * N + j];
-  db[j] = accumulate ? db[j] + s : s;
+__global__ void __launch_bounds__(1024) colsum_parts_kernel(const float* __restrict__ part, int parts, int N,
+                                                            float* __restrict__ db, int accumulate) {
+  reduce_parts(part, parts, N, accumulate, [&](int j) { return db + j; });
 }
 
 }  // namespace
@@ -713,18 +737,17 @@ size_t tb_skinny8_scratch_floats(int N) {
 int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx, int xblock, float* out,
                      long long os_j, long long os_k, long long os_blk, int M, int N, int accumulate, float* scratch,
                      size_t scratch_floats, cudaStream_t s) {
-  if (N <= 0 || N > 512 || N % 8 || xblock <= 0 || xblock % 8 || N % xblock || lda % 8 || ldx % 8 ||
+  if (N <= 0 || N > 512 || N % 32 || xblock <= 0 || xblock % 8 || N % xblock || lda % 8 || ldx % 8 ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) || M < 0)
     return static_cast<int>(cudaErrorInvalidValue);
   int per = 1;
   const int grid = M > 0 ? sk_grid(M, &per) : 0;
   if (static_cast<size_t>(grid) * N * 8 > scratch_floats) return static_cast<int>(cudaErrorInvalidValue);
   if (grid > 0)
-    skinny8_partial_kernel<<<grid, kSkThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
-                                                        static_cast<const __nv_bfloat16*>(X), ldx, xblock, scratch,
-                                                        M, N, per);
-  skinny8_reduce_kernel<<<(N * 8 + 255) / 256, 256, 0, s>>>(scratch, grid, N, xblock, out, os_j, os_k, os_blk,
-                                                             accumulate);
+    skinny8_partial_kernel<<<grid, N, 0, s>>>(static_cast<const __nv_bfloat16*>(A), lda,
+                                               static_cast<const __nv_bfloat16*>(X), ldx, xblock, scratch, M, N, per);
+  skinny8_reduce_kernel<<<(N * 8 + 31) / 32, 1024, 0, s>>>(scratch, grid, N, xblock, out, os_j, os_k, os_blk,
+                                                            accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -743,7 +766,7 @@ int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh
                                                     static_cast<const __nv_bfloat16*>(H), ldh,
                                                     static_cast<const __nv_bfloat16*>(W), ldw, xblock,
                                                     static_cast<__nv_bfloat16*>(dz), ldz, scratch, M, N, per);
-  colsum_parts_kernel<<<(N + 255) / 256, 256, 0, s>>>(scratch, grid, N, db, accumulate);
+  colsum_parts_kernel<<<(N + 31) / 32, 1024, 0, s>>>(scratch, grid, N, db, accumulate);
   return static_cast<int>(cudaGetLastError());
 }
 
