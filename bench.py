@@ -234,9 +234,9 @@ def run_ours(args):
     tr.check_collectives()
     # our kernels per iteration: rollout step = 5 GEMMs + act/step kernel; bootstrap
     # 5 GEMMs + pad; GAE 1; per minibatch: gather, first layer, 2 forward GEMMs, loss,
-    # 7 backward GEMMs + 5 split-K reduces,
+    # dW3 and dZ2 passes (2 kernels each), 4 backward GEMMs + 3 split-K reduces,
     # optimizer (Adam or the fused DP kernel), counter; end counter
-    per_mb = 1 + 1 + 2 + 1 + 7 + 5 + 1 + 1
+    per_mb = 1 + 1 + 2 + 1 + 4 + 4 + 3 + 1 + 1
     launches_per_iter = cfg.rollout_steps * 6 + 6 + 1 + cfg.epochs * cfg.n_minibatches * per_mb + 1
     out = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,

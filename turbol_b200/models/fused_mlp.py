@@ -12,9 +12,10 @@ epilogues:
   forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
             H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
-  backward  dZ2 = (dOut W3) * (1 - H2^2)    one GEMM + tanh-backward epilogue (+ db2 column sums)
+  backward  dZ2 = (dOut W3) * (1 - H2^2)    one CUDA-core pass (8 outputs per head) + db2 column sums
+            dW3 = dOut^T H2                 one CUDA-core pass (8 rows per head, 18.6 vs 36.8 us as GEMMs)
             dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM + tanh-backward epilogue (+ db1 column sums)
-            dW  = dZ^T H                    per diagonal block: MN-major x MN-major GEMM, split-K, fp32
+            dW2, dW1 = dZ^T H               MN-major x MN-major GEMMs, split-K, fp32
 No transposes are materialized and no [B, H] fp32 intermediates exist:
 activations and activation gradients are bf16, weights are the bf16 shadow
 that the fused Adam writes next to the fp32 master copy, and weight gradients
@@ -154,6 +155,8 @@ class FusedActorCritic:
             # split-K partials of the weight-gradient GEMMs (zero-filled: its
             # head holds arrival counters that every call leaves zero)
             ws["splitk"] = torch.zeros(n, **f32)
+            # per-CTA partial sums of the 8-wide CUDA-core passes
+            ws["parts"] = torch.empty(o.skinny8_scratch_numel(min(2 * H, 512)), **f32)
             self._ws[B] = ws
         return ws
 
@@ -182,11 +185,20 @@ class FusedActorCritic:
         S, G = self.s, self.g
         H = self.H
         h1, h2, dz2, dz1, dout, wsk = ws["h1"], ws["h2"], ws["dz2"], ws["dz1"], ws["dout"], ws["splitk"]
-        for head, rows, cols in (("a", slice(0, PAD), slice(0, H)), ("c", slice(PAD, 2 * PAD), slice(H, 2 * H))):
-            o.gemm(dout[:, rows], h2[:, cols], G["w3" + head], True, True, workspace=wsk)   # dW3 block = dOut^T H2
+        narrow = 2 * H <= 512  # the CUDA-core passes keep a whole row of H2 in one CTA's column threads
+        if narrow:
+            # dW3 diagonal blocks = dOut_head^T H2_head (8 rows per head): one CUDA-core
+            # pass over H2 (a tensor-core tile would be 15/16 padding)
+            o.skinny8_wgrad(h2, dout, G["w3"], H, 1, 2 * H, PAD * 2 * H, False, ws["parts"])
+        else:
+            for head, rows, cols in (("a", slice(0, PAD), slice(0, H)), ("c", slice(PAD, 2 * PAD), slice(H, 2 * H))):
+                o.gemm(dout[:, rows], h2[:, cols], G["w3" + head], True, True, workspace=wsk)  # dW3 = dOut^T H2
         if not out_bias_grads_done:
             o.colsum_bf16(dout, G["b3"])
-        o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])  # dZ2, db2
+        if narrow:  # dZ2 = (dOut W3) * (1 - H2^2), db2: K = 8 per head, one CUDA-core pass
+            o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"], False, ws["parts"])
+        else:
+            o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
             o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk)      # dW2 block = dZ2^T H1
         o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
