@@ -84,6 +84,9 @@ def main():
     res["dZ2_us"] = {"gemm": t(lambda: o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD,
                                               colsum=G["b2"])),
                      "cuda_core": t(lambda: o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"], False, sc))}
+    P = net.p
+    res["out_fwd_us"] = {"gemm": t(lambda: o.gemm(h2, S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)),
+                         "cuda_core": t(lambda: o.mlp_head_fwd(h2, S["w3"], P["b3"], H, ws["out"]))}
     res["dW1_us"] = {"gemm": t(lambda: o.gemm(dz1, x, G["w1"], True, True, workspace=wsk)),
                      "cuda_core": t(lambda: o.skinny8_wgrad(dz1, x, G["w1"], H2, PAD, 1, 0, False, sc))}
     print(json.dumps(res))

@@ -425,6 +425,29 @@ void register_kernel_ops(py::module_& m) {
             "mlp_head_dz");
   }, py::arg("dout"), py::arg("h"), py::arg("W"), py::arg("xblock"), py::arg("dz"), py::arg("db"),
      py::arg("accumulate"), py::arg("scratch"));
+  // out (fp32 [M, >= 8 heads]) = h W^T + bias per head (8 outputs per head, xblock hidden columns each)
+  m.def("mlp_head_fwd", [](at::Tensor h, at::Tensor W, py::object bias, int xblock, at::Tensor out) {
+    TB_CHECK(h.is_cuda() && h.scalar_type() == at::kBFloat16 && h.dim() == 2 && h.stride(1) == 1 &&
+                 W.scalar_type() == at::kBFloat16 && W.dim() == 2 && W.stride(1) == 1 && W.size(1) == h.size(1) &&
+                 xblock > 0 && h.size(1) % xblock == 0,
+             "mlp_head_fwd: h bf16 [M, N], W bf16 [8 heads, N]");
+    const int heads = static_cast<int>(h.size(1) / xblock);
+    TB_CHECK(W.size(0) >= 8 * heads, "mlp_head_fwd: W needs 8 rows per head");
+    need(out, at::kFloat, "out");
+    TB_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == h.size(0) && out.size(1) >= 8 * heads,
+             "mlp_head_fwd: out fp32 [M, 8 heads]");
+    const float* b = nullptr;
+    at::Tensor bt;
+    if (!bias.is_none()) {
+      bt = bias.cast<at::Tensor>();
+      need(bt, at::kFloat, "bias");
+      TB_CHECK(bt.numel() >= 8 * heads, "mlp_head_fwd: bias fp32 [8 heads]");
+      b = bt.data_ptr<float>();
+    }
+    cuda_ok(tb_mlp_head_fwd(h.data_ptr(), h.stride(0), W.data_ptr(), W.stride(0), b, out.data_ptr<float>(),
+                            out.stride(0), xblock, heads, static_cast<int>(h.size(0)), stream_of(h)),
+            "mlp_head_fwd");
+  }, py::arg("h"), py::arg("W"), py::arg("bias"), py::arg("xblock"), py::arg("out"));
   m.def("dense_k8_wgrad", [](at::Tensor dz, at::Tensor x, at::Tensor dW, bool accumulate) {
     TB_CHECK(dz.is_cuda() && dz.scalar_type() == at::kBFloat16 && dz.dim() == 2 && dz.stride(1) == 1,
              "dense_k8_wgrad: dz bf16 [M, N]");

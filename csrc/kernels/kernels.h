@@ -105,6 +105,11 @@ int tb_skinny8_wgrad(const void* A, long long lda, const void* X, long long ldx,
 int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh, const void* W, long long ldw,
                    int xblock, void* dz, long long ldz, float* db, int M, int N, int accumulate, float* scratch,
                    size_t scratch_floats, cudaStream_t s);
+// out[r, 8b + k] = bias[8b + k] + H[r, head b's xblock columns] . W[8b + k, same]:
+// an output layer with 8 outputs per head (fp32 out, row stride ldo); xblock a
+// power of two in [64, 256].
+int tb_mlp_head_fwd(const void* H, long long ldh, const void* W, long long ldw, const float* bias, float* out,
+                    long long ldo, int xblock, int heads, int M, cudaStream_t s);
 int tb_dense_k8_wgrad(const void* dz, long long ldz, const void* x, long long ldx, float* dW, int M, int N,
                       int accumulate, cudaStream_t s);
 int tb_ppo_loss(const float* logits, int A, const float* value, const int* act, const float* old_logp,

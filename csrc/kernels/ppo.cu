@@ -610,6 +610,75 @@ __global__ void __launch_bounds__(1024) colsum_parts_kernel(const float* __restr
   reduce_parts(part, parts, N, accumulate, [&](int j) { return db + j; });
 }
 
+// Output layer with 8 outputs per head: out[r, 8b + k] = b[8b + k] + sum over
+// the head's columns j of H[r, j] W[8b + k, j] (fp32 out).  A sub-warp of
+// xblock / 8 lanes covers one row of one head (8 columns per lane, the head's
+// 8 x 8 weights per lane in registers), sums across its lanes with shuffles,
+// and every warp keeps one head; rows stream with 16-byte loads, 4 in flight.
+__global__ void __launch_bounds__(256) mlp_head_fwd_kernel(const __nv_bfloat16* __restrict__ H, long long ldh,
+                                                           const __nv_bfloat16* __restrict__ W, long long ldw,
+                                                           const float* __restrict__ bias, float* __restrict__ out,
+                                                           long long ldo, int xblock, int heads, int M) {
+  const int lane = threadIdx.x & 31;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+  const int L = xblock / 8, G = 32 / L;  // lanes per row, rows per warp step
+  const int head = gw % heads;
+  const int c0 = head * xblock + (lane % L) * 8;
+  float w[8][8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 u = *reinterpret_cast<const uint4*>(W + static_cast<long long>(8 * head + k) * ldw + c0);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(h[q]);
+      w[k][2 * q] = f.x;
+      w[k][2 * q + 1] = f.y;
+    }
+  }
+  const int kk = lane % L;  // the output this lane writes (lanes 0..7 of a row group)
+  const float bk = (kk < 8 && bias) ? bias[8 * head + kk] : 0.f;
+  const int step = (nw / heads) * G;
+  // the loop bound is uniform across the warp (the shuffles below need every lane)
+  for (int wb = (gw / heads) * G; wb < M; wb += 4 * step) {
+    const int rb = wb + lane / L;
+    uint4 hu[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = rb + u * step;
+      hu[u] = r < M ? *reinterpret_cast<const uint4*>(H + static_cast<long long>(r) * ldh + c0)
+                    : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int r = rb + u * step;
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&hu[u]);
+      float hv[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(hh[q]);
+        hv[2 * q] = f.x;
+        hv[2 * q + 1] = f.y;
+      }
+      float acc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float a = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) a = fmaf(hv[c], w[k][c], a);
+        acc[k] = a;
+      }
+      for (int off = L / 2; off >= 1; off >>= 1)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+      float v = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v = (k == kk) ? acc[k] : v;
+      if (r < M && kk < 8) out[static_cast<long long>(r) * ldo + 8 * head + kk] = v + bk;
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -767,6 +836,22 @@ int tb_mlp_head_dz(const void* dout, long long ldd, const void* H, long long ldh
                                                     static_cast<const __nv_bfloat16*>(W), ldw, xblock,
                                                     static_cast<__nv_bfloat16*>(dz), ldz, scratch, M, N, per);
   colsum_parts_kernel<<<(N + 31) / 32, 1024, 0, s>>>(scratch, grid, N, db, accumulate);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_mlp_head_fwd(const void* H, long long ldh, const void* W, long long ldw, const float* bias, float* out,
+                    long long ldo, int xblock, int heads, int M, cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (xblock < 64 || xblock > 256 || (xblock & (xblock - 1)) || heads < 1 || ldh % 8 || ldw % 8 ||
+      (reinterpret_cast<uintptr_t>(H) & 15) || (reinterpret_cast<uintptr_t>(W) & 15) || ldo < 8 * heads)
+    return static_cast<int>(cudaErrorInvalidValue);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // 8 warps per CTA, an even number of warps per head
+  const int grid = sms * 4;
+  mlp_head_fwd_kernel<<<grid, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(H), ldh,
+                                            static_cast<const __nv_bfloat16*>(W), ldw, bias, out, ldo, xblock, heads,
+                                            M);
   return static_cast<int>(cudaGetLastError());
 }
 

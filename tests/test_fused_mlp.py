@@ -117,3 +117,18 @@ def test_mlp_head_dz(N, xblock, dev):
     exp = pre * (1 - h.float() ** 2)
     assert torch.allclose(dz.float(), exp, atol=1e-2, rtol=1e-2), (dz.float() - exp).abs().max()
     assert torch.allclose(db, exp.sum(0), atol=0.05, rtol=1e-3), (db - exp.sum(0)).abs().max()
+
+
+@pytest.mark.parametrize("H", [256, 128, 64])
+def test_mlp_head_fwd(H, dev):
+    """out[:, 8b + k] = bias + H2_head . W3[8b + k] per head, against fp32 torch (row count not a multiple of 32)."""
+    o = ops()
+    g = torch.Generator().manual_seed(H)
+    M = 10007
+    h = torch.tanh(torch.randn(M, 2 * H, generator=g)).to(dev, torch.bfloat16)
+    W = (torch.randn(16, 2 * H, generator=g) * 0.1).to(dev, torch.bfloat16)
+    b = torch.randn(16, generator=g).to(dev)
+    out = torch.full((M, 16), 7.0, device=dev)
+    o.mlp_head_fwd(h, W, b, H, out)
+    exp = torch.cat([h.float()[:, :H] @ W.float()[:8, :H].t(), h.float()[:, H:] @ W.float()[8:, H:].t()], 1) + b
+    assert torch.allclose(out, exp, atol=2e-3, rtol=1e-3), (out - exp).abs().max()
