@@ -233,7 +233,7 @@ def run_ours(args):
     e2e_value = steps_total / e2e_s
     tr.check_collectives()
     # our kernels per iteration: rollout step = 5 GEMMs + act/step kernel; bootstrap
-    # 5 GEMMs + pad; GAE 1; per minibatch: gather, first layer, hidden GEMM, output layer, loss,
+    # 5 GEMMs + pad; GAE 1; per minibatch: gather, first layer, 2 forward GEMMs, loss,
     # dW3 and dZ2 passes (2 kernels each), 4 backward GEMMs + 3 split-K reduces,
     # optimizer (Adam or the fused DP kernel), counter; end counter
     per_mb = 1 + 1 + 2 + 1 + 4 + 4 + 3 + 1 + 1
