@@ -87,6 +87,20 @@ def main():
     P = net.p
     res["out_fwd_us"] = {"gemm": t(lambda: o.gemm(h2, S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)),
                          "cuda_core": t(lambda: o.mlp_head_fwd(h2, S["w3"], P["b3"], H, ws["out"]))}
+    # tile widths of the two K = 512 GEMMs and of the hidden-layer weight gradient
+    for bn in (64, 128, 256):
+        res[f"h2_fwd_bn{bn}_us"] = t(lambda: o.gemm(h1, S["w2"], h2, bias=P["b2"], epi=o.EPI_BIAS_TANH, bn=bn))
+        res[f"dZ1_bn{bn}_us"] = t(lambda: o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD,
+                                                 colsum=G["b1"], bn=bn))
+    for bn in (128, 256):
+        for sk in (0, 8, 16, 32):
+            def dw2():
+                for cols in (slice(0, H), slice(H, 2 * H)):
+                    o.gemm(dz2[:, cols], h1[:, cols], G["w2a"], True, True, workspace=wsk, bn=bn, split_k=sk)
+            try:
+                res[f"dW2_bn{bn}_s{sk}_us"] = t(dw2)
+            except Exception:
+                res[f"dW2_bn{bn}_s{sk}_us"] = None
     res["dW1_us"] = {"gemm": t(lambda: o.gemm(dz1, x, G["w1"], True, True, workspace=wsk)),
                      "cuda_core": t(lambda: o.skinny8_wgrad(dz1, x, G["w1"], H2, PAD, 1, 0, False, sc))}
     print(json.dumps(res))
