@@ -43,7 +43,7 @@ def main():
     # (row shards of the fused kernels are multiples of 128: 256 sequences per group)
     tcfg = GRPOConfig(model=LMConfig.tiny(), num_prompts=32, group_size=8, prompt_len=32, response_len=16,
                       micro_batch=16, lr=1e-4)
-    tr = GRPOTrainer(tcfg, f"cuda:{local}", dp="fused", tp=world)
+    tr = GRPOTrainer(tcfg, f"cuda:{local}", dp="fused", tp=world, tp_mode="rollout")
     for _ in range(2):
         st = tr.step()
         assert st["tokens"] == tcfg.batch // world * tcfg.response_len
