@@ -168,7 +168,8 @@ class FusedActorCritic:
         ws = ws or self.workspace(B)
         S, P = self.s, self.p
         o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], ws["h1"], True)                 # 8 input features: CUDA cores
-        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH)    # both heads' hidden layer
+        # both heads' hidden layer (128-wide tiles: 34.2 vs 37.3 us at 32,768 rows)
+        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH, bn=128)
         # (the CUDA-core mlp_head_fwd measured slower here: 26.7 vs 16.5 us at 32,768 rows)
         o.gemm(ws["h2"], S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)        # logits | value
         return ws["logits"], ws["value"]
@@ -200,7 +201,8 @@ class FusedActorCritic:
             o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"], False, ws["parts"])
         else:
             o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])
+        # dW2 block = dZ2^T H1 (128-wide tiles, 32 K splits: 35.1 vs 42.9 us for both heads at 32,768 rows)
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
-            o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk)      # dW2 block = dZ2^T H1
+            o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk, bn=128, split_k=32)
         o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
         o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
