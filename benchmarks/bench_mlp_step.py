@@ -101,6 +101,8 @@ def main():
                 res[f"dW2_bn{bn}_s{sk}_us"] = t(dw2)
             except Exception:
                 res[f"dW2_bn{bn}_s{sk}_us"] = None
+    for rows in (0, 64, 128, 256, 512):  # first layer: rows per CTA (0 = automatic)
+        res[f"first_layer_rows{rows}_us"] = t(lambda: o.dense_k8_fwd(x, S["w1"], P["b1"], h1, True, rows))
     res["dW1_us"] = {"gemm": t(lambda: o.gemm(dz1, x, G["w1"], True, True, workspace=wsk)),
                      "cuda_core": t(lambda: o.skinny8_wgrad(dz1, x, G["w1"], H2, PAD, 1, 0, False, sc))}
     print(json.dumps(res))

@@ -365,7 +365,7 @@ void register_kernel_ops(py::module_& m) {
       py::arg("batch"), py::arg("params"), py::arg("grad"), py::arg("O"), py::arg("A"), py::arg("std"),
       py::arg("clip"), py::arg("vf_coef"), py::arg("has_old"));
 
-  m.def("dense_k8_fwd", [](at::Tensor x, at::Tensor W, py::object bias, at::Tensor y, bool tanh_act) {
+  m.def("dense_k8_fwd", [](at::Tensor x, at::Tensor W, py::object bias, at::Tensor y, bool tanh_act, int rows) {
     TB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(1) == 8 && x.stride(1) == 1,
              "dense_k8_fwd: x bf16 [M, 8]");
     TB_CHECK(W.scalar_type() == at::kBFloat16 && W.is_contiguous() && W.dim() == 2 && W.size(1) == 8,
@@ -379,10 +379,11 @@ void register_kernel_ops(py::module_& m) {
       need(bt, at::kFloat, "bias");
       bp = bt.data_ptr<float>();
     }
-    cuda_ok(tb_dense_k8_fwd(x.data_ptr(), x.stride(0), W.data_ptr(), bp, y.data_ptr(), y.stride(0),
-                            static_cast<int>(x.size(0)), static_cast<int>(W.size(0)), tanh_act ? 1 : 0, stream_of(x)),
+    cuda_ok(tb_dense_k8_fwd_rows(x.data_ptr(), x.stride(0), W.data_ptr(), bp, y.data_ptr(), y.stride(0),
+                                 static_cast<int>(x.size(0)), static_cast<int>(W.size(0)), tanh_act ? 1 : 0, rows,
+                                 stream_of(x)),
             "dense_k8_fwd");
-  }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true);
+  }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true, py::arg("rows") = 0);
   m.def("skinny8_scratch_numel", [](int N) { return static_cast<int64_t>(tb_skinny8_scratch_floats(N)); });
   // out (fp32, contiguous) = A^T X for 8-wide X blocks (+= with accumulate); scratch fp32 per-CTA partials
   m.def("skinny8_wgrad", [](at::Tensor A, at::Tensor X, at::Tensor out, int xblock, int64_t os_j, int64_t os_k,

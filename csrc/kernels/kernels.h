@@ -89,6 +89,9 @@ int tb_lin_gauss_grad(const float* batch, int row_w, const float* params, float*
                       float stdv, float clip, float vf_coef, int has_old, cudaStream_t s);
 int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
                     int N, int act, cudaStream_t s);
+// Same, with the rows per CTA given (0: automatic).
+int tb_dense_k8_fwd_rows(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy,
+                         int M, int N, int act, int rows_hint, cudaStream_t s);
 // dW[N, 8] (fp32) = (or += with accumulate) dz[M, N]^T . x[M, 8] (bf16 inputs).
 // out = A^T X over M rows for 8-wide X (the weight gradient of a layer with 8
 // input or output features), A bf16 [M, N<=512], X bf16 [M, 8 * N/xblock]:

@@ -773,6 +773,11 @@ int tb_counter_add(long long* counter, long long v, cudaStream_t s) {
 
 int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy, int M,
                     int N, int act, cudaStream_t s) {
+  return tb_dense_k8_fwd_rows(x, ldx, W, bias, y, ldy, M, N, act, 0, s);
+}
+
+int tb_dense_k8_fwd_rows(const void* x, long long ldx, const void* W, const float* bias, void* y, long long ldy,
+                         int M, int N, int act, int rows_hint, cudaStream_t s) {
   if (M <= 0) return 0;
   if (N % 8 || N > 1024 || ldx % 8 || ldy % 8 || (reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
       (reinterpret_cast<uintptr_t>(y) & 15))
@@ -782,7 +787,11 @@ int tb_dense_k8_fwd(const void* x, long long ldx, const void* W, const float* bi
   if (groups > 256) return static_cast<int>(cudaErrorInvalidValue);
   const int rstep = 256 / groups;
   int rows = 32;
-  while (rows > rstep && (static_cast<long long>(M) + rows - 1) / rows < 4 * 148) rows /= 2;
+  if (rows_hint > 0) {
+    rows = rows_hint < rstep ? rstep : rows_hint;  // rows per CTA (each CTA loads its weight slice once)
+  } else {
+    while (rows > rstep && (static_cast<long long>(M) + rows - 1) / rows < 4 * 148) rows /= 2;
+  }
   const unsigned grid = static_cast<unsigned>((M + rows - 1) / rows);
   dense_k8_fwd_kernel<<<grid, rstep * groups, 0, s>>>(static_cast<const __nv_bfloat16*>(x), ldx,
                                                       static_cast<const __nv_bfloat16*>(W), bias,
