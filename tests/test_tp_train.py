@@ -95,3 +95,22 @@ def test_unshard_inverts_load(master):
         assert torch.equal(got[n], ref[n].to(got[n].dtype)), n
     for n in dst.f32:
         assert torch.allclose(dst.f32[n], src.p[n], atol=1e-2), n
+
+
+def test_grpo_tp_rejects_shapes_the_fused_kernels_cannot_tile(tmp_path):
+    """Tensor-parallel GRPO checks its row counts before building anything."""
+    import torch.distributed as dist
+
+    from turbol_b200.rl.grpo import GRPOConfig, GRPOTrainer
+
+    own = not dist.is_initialized()
+    if own:
+        dist.init_process_group("gloo", init_method=f"file://{tmp_path}/pg", rank=0, world_size=1)
+    try:
+        cfg = GRPOConfig(model=LMConfig.tiny(), num_prompts=4, group_size=2, prompt_len=64, response_len=64,
+                         micro_batch=2)
+        with pytest.raises(ValueError, match="multiple of 128"):
+            GRPOTrainer(cfg, "cpu", dp="nccl", tp=2)
+    finally:
+        if own:
+            dist.destroy_process_group()

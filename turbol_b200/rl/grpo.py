@@ -158,6 +158,12 @@ class GRPOTrainer:
         if cfg.micro_batch % tp or (cfg.micro_batch // tp * cfg.seq_len) % 128 or cfg.batch % cfg.micro_batch:
             raise ValueError("tensor-parallel training: micro_batch must divide the batch, split over the TP ranks "
                              "into whole sequences, and give each rank a multiple of 128 rows")
+        # the fused TP kernels work on 128-row tiles of each rank's share: prefill
+        # rows (prompts x prompt_len) and decode rows (sequences) per rank
+        if (cfg.num_prompts * cfg.prompt_len // tp) % 128 or (cfg.batch // tp) % 128 or cfg.num_prompts % tp:
+            raise ValueError("tensor-parallel rollout: each rank needs a multiple of 128 prompt tokens and of 128 "
+                             f"sequences (num_prompts={cfg.num_prompts}, prompt_len={cfg.prompt_len}, "
+                             f"batch={cfg.batch}, tp={tp})")
         mesh = build_mesh(self.world, self.rank, tp=tp)
         self.mesh = mesh
         self.tp_rank, self.group_index = mesh.tp_rank, self.rank // tp
