@@ -232,12 +232,13 @@ def run_ours(args):
     value = steps_total / (ms_dev / 1e3)
     e2e_value = steps_total / e2e_s
     tr.check_collectives()
-    # our kernels per iteration: rollout step = 5 GEMMs + act/step kernel; bootstrap
-    # 5 GEMMs + pad; GAE 1; per minibatch: gather, first layer, 2 forward GEMMs, loss,
+    # our kernels per iteration: rollout step = MLP forward (first layer + 2 GEMMs)
+    # + fused act/env-step kernel; observation pad + bootstrap forward (3); GAE 1;
+    # per minibatch: gather, first layer, 2 forward GEMMs, loss,
     # dW3 and dZ2 passes (2 kernels each), 4 backward GEMMs + 3 split-K reduces,
     # optimizer (Adam or the fused DP kernel), counter; end counter
     per_mb = 1 + 1 + 2 + 1 + 4 + 4 + 3 + 1 + 1
-    launches_per_iter = cfg.rollout_steps * 6 + 6 + 1 + cfg.epochs * cfg.n_minibatches * per_mb + 1
+    launches_per_iter = cfg.rollout_steps * 4 + 1 + 3 + 1 + cfg.epochs * cfg.n_minibatches * per_mb + 1
     out = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_dev / args.steps, "higher_is_better": True, "scaling": "weak",
