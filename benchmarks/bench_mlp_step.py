@@ -26,6 +26,7 @@ def main():
     ap.add_argument("--rows", type=int, default=32768)
     ap.add_argument("--hidden", type=int, default=256)
     ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--no-variants", action="store_true", help="time the MLP step only (short runs for ncu)")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     net = FusedActorCritic(4, 2, (a.hidden, a.hidden), device=dev, seed=0)
@@ -55,6 +56,9 @@ def main():
     flops = 2 * B * (PAD * H2 + H2 * H2 + H2 * 2 * PAD) * 3
     res = {"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "us": us, "tflops": flops / us / 1e6,
            "activation_bytes_per_layer": B * H2 * 2}
+    if a.no_variants:
+        print(json.dumps(res))
+        return
     # the three 8-wide pieces of the backward: tensor-core GEMM (+ split-K reduce)
     # against the CUDA-core two-pass kernels
     from turbol_b200._native import ops
