@@ -120,8 +120,10 @@ void register_llm_ops(py::module_& m) {
                            static_cast<int>(x.size(1)), eps, turbol::StreamFor(x)),
             "rmsnorm_fwd");
   }, py::arg("x"), py::arg("w"), py::arg("y"), py::arg("rstd") = py::none(), py::arg("eps") = 1e-6f);
+  m.def("rmsnorm_bwd_ws_numel", [](int D) { return static_cast<int64_t>(tb_rmsnorm_bwd_ws_floats(D)); });
+  // ws (optional fp32, rmsnorm_bwd_ws_numel(D)): weight-gradient partials summed by a second pass
   m.def("rmsnorm_bwd", [=](at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx,
-                           py::object dx_add, at::Tensor dw) {
+                           py::object dx_add, at::Tensor dw, py::object ws) {
     bf16_2d(dy, "dy");
     bf16_2d(x, "x");
     bf16_2d(dx, "dx");
@@ -129,11 +131,21 @@ void register_llm_ops(py::module_& m) {
     f32c(rstd, "rstd");
     f32c(dw, "dw");
     const void* add = dx_add.is_none() ? nullptr : dx_add.cast<at::Tensor>().data_ptr();
-    cuda_ok(tb_rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(), dx.data_ptr(),
-                           add, dw.data_ptr<float>(), static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
-                           turbol::StreamFor(x)),
+    float* wsp = nullptr;
+    size_t wsn = 0;
+    at::Tensor wst;
+    if (!ws.is_none()) {
+      wst = ws.cast<at::Tensor>();
+      f32c(wst, "ws");
+      wsp = wst.data_ptr<float>();
+      wsn = static_cast<size_t>(wst.numel());
+    }
+    cuda_ok(tb_rmsnorm_bwd_ws(dy.data_ptr(), x.data_ptr(), w.data_ptr<float>(), rstd.data_ptr<float>(),
+                              dx.data_ptr(), add, dw.data_ptr<float>(), static_cast<int>(x.size(0)),
+                              static_cast<int>(x.size(1)), wsp, wsn, turbol::StreamFor(x)),
             "rmsnorm_bwd");
-  });
+  }, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dx"), py::arg("dx_add"), py::arg("dw"),
+     py::arg("ws") = py::none());
   m.def("rope", [=](at::Tensor qkv, at::Tensor pos, at::Tensor table, int n_rot_heads, int head_dim, bool inverse) {
     bf16_2d(qkv, "qkv");
     i32c(pos, "pos");

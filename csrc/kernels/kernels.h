@@ -191,6 +191,12 @@ size_t tb_gemm_workspace_bytes(int M, int N, int K);
 int tb_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps, cudaStream_t s);
 int tb_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx, const void* dx_add,
                    float* dw, int T, int D, cudaStream_t s);
+// Same; with a workspace of tb_rmsnorm_bwd_ws_floats(D) floats the blocks'
+// weight-gradient partials are summed by a second pass instead of contended
+// global atomics (dw still accumulates: dw += sum).
+size_t tb_rmsnorm_bwd_ws_floats(int D);
+int tb_rmsnorm_bwd_ws(const void* dy, const void* x, const float* w, const float* rstd, void* dx, const void* dx_add,
+                      float* dw, int T, int D, float* ws, size_t ws_floats, cudaStream_t s);
 int tb_rope(void* qkv, long long ld, const int* pos, const void* table, int T, int n_rot_heads, int D, int inverse,
             cudaStream_t s);
 int tb_embed_fwd(const int* ids, const void* W, void* out, int T, int D, int V, int* err, cudaStream_t s);

@@ -76,7 +76,7 @@ template <int MAXV>
 __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
                                    const float* __restrict__ w, const float* __restrict__ rstd,
                                    bf16* __restrict__ dx, const bf16* __restrict__ dx_add, float* __restrict__ dw,
-                                   int T, int D, int rows_per_block) {
+                                   float* __restrict__ part, int T, int D, int rows_per_block) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   float dwp[MAXV];
 #pragma unroll
@@ -131,7 +131,30 @@ __global__ void rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __re
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(dw + c, sdw[c]);
+  if (part) {  // one partial row per block, summed by rms_parts_add_kernel (no contended atomics)
+    for (int c = threadIdx.x; c < D; c += blockDim.x) part[static_cast<long long>(blockIdx.x) * D + c] = sdw[c];
+  } else {
+    for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(dw + c, sdw[c]);
+  }
+}
+
+// dw[c] += sum over `parts` block partials [parts, D]: 32 columns per CTA, 32
+// thread groups each summing every 32nd partial, then a shared-memory fold.
+__global__ void __launch_bounds__(1024) rms_parts_add_kernel(const float* __restrict__ part, int parts, int D,
+                                                             float* __restrict__ dw) {
+  __shared__ float sm[32][33];
+  const int ci = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + ci;
+  float s = 0.f;
+  if (c < D)
+    for (int b = g; b < parts; b += 32) s += part[static_cast<long long>(b) * D + c];
+  sm[g][ci] = s;
+  __syncthreads();
+  if (g == 0 && c < D) {
+    float t = 0.f;
+    for (int q = 0; q < 32; ++q) t += sm[q][ci];
+    dw[c] += t;
+  }
 }
 
 // ------------------------------------------------------------------ RoPE
@@ -905,24 +928,33 @@ int tb_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, i
   return static_cast<int>(cudaGetLastError());
 }
 
+size_t tb_rmsnorm_bwd_ws_floats(int D) { return static_cast<size_t>(2 * 148) * (D > 0 ? D : 0); }
+
 int tb_rmsnorm_bwd(const void* dy, const void* x, const float* w, const float* rstd, void* dx, const void* dx_add,
                    float* dw, int T, int D, cudaStream_t s) {
+  return tb_rmsnorm_bwd_ws(dy, x, w, rstd, dx, dx_add, dw, T, D, nullptr, 0, s);
+}
+
+int tb_rmsnorm_bwd_ws(const void* dy, const void* x, const float* w, const float* rstd, void* dx, const void* dx_add,
+                      float* dw, int T, int D, float* ws, size_t ws_floats, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 256 || D > 8192) return static_cast<int>(cudaErrorInvalidValue);
-  // ~2 blocks per SM; more rows per block means fewer global atomics on dw
+  // ~2 blocks per SM
   int rpb = (T + 2 * 148 - 1) / (2 * 148);
   if (rpb < 8) rpb = 8;
   const unsigned g = (T + rpb - 1) / rpb;
+  float* part = (ws && static_cast<size_t>(g) * D <= ws_floats) ? ws : nullptr;
   auto* a = static_cast<const bf16*>(dy);
   auto* b = static_cast<const bf16*>(x);
   auto* o = static_cast<bf16*>(dx);
   auto* ad = static_cast<const bf16*>(dx_add);
   if (D <= 2048)
-    rmsnorm_bwd_kernel<64><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, T, D, rpb);
+    rmsnorm_bwd_kernel<64><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, part, T, D, rpb);
   else if (D <= 4096)
-    rmsnorm_bwd_kernel<128><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, T, D, rpb);
+    rmsnorm_bwd_kernel<128><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, part, T, D, rpb);
   else
-    rmsnorm_bwd_kernel<256><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, T, D, rpb);
+    rmsnorm_bwd_kernel<256><<<g, 256, 0, s>>>(a, b, w, rstd, o, ad, dw, part, T, D, rpb);
+  if (part) rms_parts_add_kernel<<<(D + 31) / 32, 1024, 0, s>>>(part, static_cast<int>(g), D, dw);
   return static_cast<int>(cudaGetLastError());
 }
 

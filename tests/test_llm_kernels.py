@@ -35,6 +35,13 @@ def test_rmsnorm_fwd_bwd(dev):
     yr.backward(dy.float())
     assert torch.allclose(dx.float(), xr.grad + add.float(), atol=5e-2, rtol=3e-2)
     assert torch.allclose(dw, wr.grad, atol=0.5, rtol=2e-2)
+    # the two-pass weight gradient (workspace) accumulates the same sum
+    ws = torch.empty(ops().rmsnorm_bwd_ws_numel(D), device=dev)
+    dw2 = torch.full((D,), 1.0, device=dev)
+    dx2 = torch.empty_like(x)
+    ops().rmsnorm_bwd(dy, x, w, r, dx2, add, dw2, ws)
+    assert torch.equal(dx2, dx)
+    assert torch.allclose(dw2 - 1.0, dw, atol=1e-2, rtol=1e-4)
 
 
 def test_rope_roundtrip(dev):
