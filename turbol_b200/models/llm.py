@@ -304,7 +304,6 @@ class DecoderLM:
         d_qkv = self._buf("d_qkv", (N, cfg.qkv_dim))
         delta = self._buf("delta", (B * cfg.n_heads * T,), torch.float32)
         attn_ws = self._buf("attn_ws", (o.flash_attn_bwd_ws_numel(B, T, cfg.n_kv_heads),), torch.float32)
-        rms_ws = self._buf("rms_ws", (o.rmsnorm_bwd_ws_numel(H),), torch.float32)
         for i, a in zip(reversed(self.layers), reversed(saved)):
             P = f"l{i}."
             # ---- MLP
@@ -314,7 +313,7 @@ class DecoderLM:
             o.gemm(d_gu, self.s[P + "wgu"], dh, False, True)                        # dh2 = dGU Wgu
             o.gemm(d_gu, a["h2"], G[P + "wgu"], True, True, accumulate=True, split_k=1)  # dWgu += dGU^T h2
             dx2 = torch.empty(N, H, device=self.device, dtype=torch.bfloat16)
-            o.rmsnorm_bwd(dh, a["x2"], self.f32[P + "ln2"], a["r2"], dx2, dx, G[P + "ln2"], rms_ws)
+            o.rmsnorm_bwd(dh, a["x2"], self.f32[P + "ln2"], a["r2"], dx2, dx, G[P + "ln2"])
             # ---- attention
             o.gemm(dx2, self.s[P + "wo"], d_attn, False, True)                      # d attn = dX2 Wo
             o.gemm(dx2, a["attn"], G[P + "wo"], True, True, accumulate=True, split_k=1)  # dWo += dX2^T attn
@@ -331,7 +330,7 @@ class DecoderLM:
             if cfg.qkv_bias:
                 o.colsum_bf16(d_qkv, G[P + "bqkv"], True)
             dxi = torch.empty(N, H, device=self.device, dtype=torch.bfloat16)
-            o.rmsnorm_bwd(dh, a["x"], self.f32[P + "ln1"], a["r1"], dxi, dx2, G[P + "ln1"], rms_ws)
+            o.rmsnorm_bwd(dh, a["x"], self.f32[P + "ln1"], a["r1"], dxi, dx2, G[P + "ln1"])
             dx = dxi
         return dx
 

@@ -470,7 +470,6 @@ class TPTrainLM(TPDecoderLM):
         d_qkv = self._buf("d_qkv", (N, self.qkv_dim))
         delta = self._buf("delta", (B * self.hq * T,), torch.float32)
         attn_ws = self._buf("attn_ws", (o.flash_attn_bwd_ws_numel(B, T, self.hk),), torch.float32)
-        rms_ws = self._buf("rms_ws", (o.rmsnorm_bwd_ws_numel(H),), torch.float32)
         for i, a in zip(reversed(self.layers), reversed(saved)):
             P = f"l{i}."
             # ---- MLP: row-parallel down projection, column-parallel gate/up
@@ -480,7 +479,7 @@ class TPTrainLM(TPDecoderLM):
             dh2 = c.gemm_reduce_scatter(d_gu, w[P + "wgu"], b_mn=True)                     # dh2_r = RS(dGU Wgu_r)
             o.gemm(d_gu, a["h2f"], G[P + "wgu"], True, True, accumulate=True, split_k=1)   # dWgu_r += dGU^T h2
             dx2 = torch.empty(m, H, device=self.device, dtype=torch.bfloat16)
-            o.rmsnorm_bwd(dh2, a["x2"], w[P + "ln2"], a["r2"], dx2, dx, G[P + "ln2"], rms_ws)
+            o.rmsnorm_bwd(dh2, a["x2"], w[P + "ln2"], a["r2"], dx2, dx, G[P + "ln2"])
             # ---- attention: row-parallel output projection, column-parallel QKV
             c.all_gather_gemm(dx2, w[P + "wo"], out=d_attn, b_mn=True, gather_out=dfull)   # d attn = dX2 Wo_r
             o.gemm(dfull, a["attn"], G[P + "wo"], True, True, accumulate=True, split_k=1)  # dWo_r += dX2^T attn
@@ -497,7 +496,7 @@ class TPTrainLM(TPDecoderLM):
             if cfg.qkv_bias:
                 o.colsum_bf16(d_qkv, G[P + "bqkv"], True)
             dxi = torch.empty(m, H, device=self.device, dtype=torch.bfloat16)
-            o.rmsnorm_bwd(dh1, a["x"], w[P + "ln1"], a["r1"], dxi, dx2, G[P + "ln1"], rms_ws)
+            o.rmsnorm_bwd(dh1, a["x"], w[P + "ln1"], a["r1"], dxi, dx2, G[P + "ln1"])
             dx = dxi
         return dx
 
