@@ -2,14 +2,19 @@
 # Builds the unmodified reference (DeRuiChen258/Turbol, turbol_vllm tree) with
 # its own CMake for sm_100 and installs its Python package + benchmark binaries
 # into baseline/_ref (git-ignored).  The reference ships no setup.py or
-# pyproject.toml at its root, so `pip install /root/reference` cannot work;
+# pyproject.toml at its root, so a plain `pip install` of it cannot work;
 # this runs the build the reference's own CMakeLists.txt defines, from a copy
 # (the source tree is read-only).  Tests are off (GoogleTest is not installed)
 # and NCCL is off (its NCCL build calls a function NCCL does not have).
 # Its CMakeLists.txt pins libtorch's arch list to 12.0 (sm_120 only), so an
 # sm_100 -gencode is added through CMAKE_CUDA_FLAGS (appended to, not replaced).
+#
+#   REF=<path to the reference checkout> baseline/build_reference.sh
 set -euo pipefail
-REF=${REF:-/root/reference}
+if [ -z "${REF:-}" ] || [ ! -d "$REF/turbol_vllm" ]; then
+  echo "set REF to the reference checkout (the directory holding turbol_vllm/)" >&2
+  exit 2
+fi
 HERE=$(cd "$(dirname "$0")" && pwd)
 SRC=$(mktemp -d /tmp/ref_src.XXXX)
 BLD=$(mktemp -d /tmp/ref_build.XXXX)

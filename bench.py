@@ -13,8 +13,10 @@ value = N * 65,536 * 128 * K / (max over ranks of the device time of K steps).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--grpo-steps G]
 
-The JSON line also carries a secondary "grpo" measurement: GRPO train
-tokens/s (1.5B-shape policy, 64 prompts x 8 per GPU, data parallel).
+The JSON line also carries the second half of the headline metric under
+"grpo": GRPO train tokens/s/box on the 1.5B-shape policy, 64 prompts x 8 per
+model replica; on one GPU the whole model, on N >= 2 GPUs tensor parallel
+over rank pairs x data parallel over the N/2 pairs (TP2 x DP4 at N = 8).
 
 For N > 1 run under torch.distributed.run (one process per GPU).
 ``--impl reference`` runs the reference build's own Python API (installed in
@@ -50,23 +52,32 @@ def parse():
     p.add_argument("--rollout", type=int, default=ROLLOUT)
     p.add_argument("--dp", choices=["fused", "nccl"], default="fused",
                    help="gradient reduction for N > 1: fused peer-memory kernel or NCCL all-reduce")
-    p.add_argument("--grpo-steps", type=int, default=None,
-                   help="timed steps of the GRPO secondary measurement (0: skip; default 2 on one GPU, "
-                        "0 on several so the scaling run stays short); 3 warm-up steps")
+    p.add_argument("--grpo-steps", type=int, default=2,
+                   help="timed steps of the GRPO measurement (0: skip); 3 warm-up steps")
     return p.parse_args()
 
 
 def run_grpo(args, world, rank, local):
     """Secondary measurement: GRPO train tokens/s on the 1.5B-shape policy
-    (64 prompts x 8 samples per GPU, 256 + 512 tokens, data parallel with the
-    fused peer-memory optimizer step for N > 1), device-timed, max over ranks."""
+    (64 prompts x 8 samples per model replica, 256 + 512 tokens), device-timed,
+    max over ranks.  One GPU: the whole model on the GPU.  N >= 2 GPUs: the
+    layout of the TP2 x DP4 workload, tensor parallel over rank pairs (rollout
+    and training on the fused all-gather->GEMM / GEMM->reduce-scatter kernels)
+    x data parallel over the N/2 pairs (fused peer-memory optimizer step)."""
     import torch
     import torch.distributed as dist
 
     from turbol_b200.rl.grpo import GRPOConfig, GRPOTrainer
 
     cfg = GRPOConfig(num_prompts=64, group_size=8, prompt_len=256, response_len=512, micro_batch=8)
-    tr = GRPOTrainer(cfg, f"cuda:{local}", dp=args.dp if world > 1 else "none")
+    tp = 2 if world >= 2 else 1
+    if world % tp:
+        raise ValueError(f"GRPO layout TP{tp} needs an even GPU count, got {world}")
+    if tp > 1:
+        tr = GRPOTrainer(cfg, f"cuda:{local}", dp="fused", tp=tp, tp_mode="train")
+    else:
+        tr = GRPOTrainer(cfg, f"cuda:{local}", dp="none")
+    replicas = world // tp
     warm = 3
     for _ in range(warm):
         tr.step()
@@ -81,15 +92,19 @@ def run_grpo(args, world, rank, local):
         torch.cuda.synchronize()
         times.append(max_over_ranks(e0.elapsed_time(e1) / 1e3, world))
     sec = sum(times) / len(times)
-    if world > 1:
+    if hasattr(tr.opt, "check"):
         tr.opt.check()
-    out = {"metric": "GRPO train tokens/s", "value": world * cfg.batch * cfg.seq_len / sec, "unit": "tokens/s",
-           "steps": args.grpo_steps, "warmup": warm, "s_per_step": sec,
+    if tp > 1:
+        tr.comm.check()
+    par = "dp1" if tp == 1 else f"tp{tp}xdp{replicas} (fused TP collectives, fused DP optimizer step)"
+    out = {"metric": "GRPO train tokens/s/box", "value": replicas * cfg.batch * cfg.seq_len / sec,
+           "unit": "tokens/s", "n_gpus": world, "steps": args.grpo_steps, "warmup": warm, "s_per_step": sec,
            "phases_s": {k: last[k] for k in ("rollout_s", "reward_ref_s", "train_s")},
            "config": {"model": "qwen2-1.5b-shape decoder (28 layers, hidden 1536, 12q/2kv heads, ffn 8960, "
-                               "vocab 151936)", "prompts_per_gpu": 64, "group": 8, "prompt_len": 256,
-                      "response_len": 512, "parallelism": f"dp{world}" + (f" ({args.dp})" if world > 1 else "")},
-           "timing": "CUDA events around each step, max over ranks"}
+                               "vocab 151936)", "prompts_per_replica": cfg.num_prompts, "group": cfg.group_size,
+                      "prompt_len": cfg.prompt_len, "response_len": cfg.response_len,
+                      "global_batch_sequences": replicas * cfg.batch, "parallelism": par},
+           "scaling": "weak", "timing": "CUDA events around each step, max over ranks"}
     del tr
     torch.cuda.empty_cache()
     return out
@@ -257,8 +272,6 @@ def run_ours(args):
     tr.release_graphs()
     del tr
     torch.cuda.empty_cache()
-    if args.grpo_steps is None:
-        args.grpo_steps = 2 if world == 1 else 0
     if args.grpo_steps > 0:
         try:
             out["grpo"] = run_grpo(args, world, rank, local)

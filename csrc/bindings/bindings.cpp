@@ -68,12 +68,15 @@ PYBIND11_MODULE(turbol_core, m) {
       .value("kInvalidArgument", StatusCode::kInvalidArgument)
       .value("kNotFound", StatusCode::kNotFound)
       .value("kAlreadyExists", StatusCode::kAlreadyExists)
-      .value("kOutOfMemory", StatusCode::kOutOfMemory)
+      .value("kResourceExhausted", StatusCode::kResourceExhausted)
+      .value("kUnimplemented", StatusCode::kUnimplemented)
       .value("kInternalError", StatusCode::kInternalError)
-      .value("kNotImplemented", StatusCode::kNotImplemented)
       .value("kUnavailable", StatusCode::kUnavailable)
       .value("kTimeout", StatusCode::kTimeout)
       .value("kCudaError", StatusCode::kCudaError);
+  // this library's earlier names for codes 4 and 5
+  m.attr("StatusCode").attr("kOutOfMemory") = StatusCode::kResourceExhausted;
+  m.attr("StatusCode").attr("kNotImplemented") = StatusCode::kUnimplemented;
 
   py::class_<Status>(m, "Status")
       .def(py::init<>())

@@ -62,6 +62,11 @@ TbGemmArgs tp_gemm_args(const at::Tensor& A, const at::Tensor& B, bool b_mn, int
 }  // namespace
 
 void register_comm_ops(py::module_& m) {
+  m.def("peer_owned_slice", [](int64_t n, int rank, int world) {
+    long long lo = 0, hi = 0;
+    tb_peer_owned_slice(n, rank, world, &lo, &hi);
+    return py::make_tuple(static_cast<int64_t>(lo), static_cast<int64_t>(hi));
+  });
   m.def("tp_header_bytes", []() { return static_cast<int64_t>(tb_tp_header_bytes()); });
   m.def("bounded_wait_probe", [](at::Tensor flags, int64_t expect, double budget_s, at::Tensor err) {
     if (!flags.is_cuda() || flags.scalar_type() != at::kInt || !err.is_cuda() || err.scalar_type() != at::kInt)
@@ -208,9 +213,11 @@ void register_comm_ops(py::module_& m) {
       .def("allreduce_adam",
            [](PeerMemory& p, int64_t grad_off, int64_t param_off, int64_t shadow_off, int64_t n, at::Tensor m1,
               at::Tensor m2, float lr, float b1, float b2, float eps, float wd, float grad_scale, at::Tensor step) {
-             if (!m1.is_cuda() || m1.scalar_type() != at::kFloat || m1.numel() < n || !m2.is_cuda() ||
-                 m2.numel() < n || step.scalar_type() != at::kLong)
-               throw std::invalid_argument("allreduce_adam: bad state tensors");
+             long long lo = 0, hi = 0;
+             tb_peer_owned_slice(n, p.rank(), p.world(), &lo, &hi);
+             if (!m1.is_cuda() || m1.scalar_type() != at::kFloat || m1.numel() < hi - lo || !m2.is_cuda() ||
+                 m2.scalar_type() != at::kFloat || m2.numel() < hi - lo || step.scalar_type() != at::kLong)
+               throw std::invalid_argument("allreduce_adam: m and v must be fp32 CUDA tensors of the owned shard");
              TbAdamParams hp{lr, b1, b2, eps, wd, grad_scale, 0.f, 0};
              cuda_ok(tb_peer_allreduce_adam(p.Table(), grad_off, param_off, shadow_off, n, m1.data_ptr<float>(),
                                             m2.data_ptr<float>(), hp,

@@ -258,6 +258,72 @@ void register_llm_ops(py::module_& m) {
   }, py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("step_ptr"), py::arg("step"),
      py::arg("out_tok"), py::arg("out_logp") = py::none(), py::arg("tok_mat") = py::none(),
      py::arg("lp_mat") = py::none(), py::arg("seed_t") = py::none(), py::arg("temp_t") = py::none());
+  m.def("sample_filtered", [=](at::Tensor logits, float temperature, int top_k, float top_p, uint64_t seed,
+                               py::object step_ptr, int64_t step, at::Tensor out_tok, py::object out_logp,
+                               py::object tok_mat, py::object lp_mat, py::object seed_t, py::object temp_t,
+                               int eos_id, int pad_id, py::object done, py::object lengths, py::object n_done) {
+    bf16_2d(logits, "logits");
+    i32c(out_tok, "out_tok");
+    const int B = static_cast<int>(logits.size(0));
+    auto ptr_i64 = [](py::object o) -> const long long* {
+      return o.is_none() ? nullptr : reinterpret_cast<const long long*>(o.cast<at::Tensor>().data_ptr<int64_t>());
+    };
+    float* lp = out_logp.is_none() ? nullptr : out_logp.cast<at::Tensor>().data_ptr<float>();
+    int* tm = nullptr;
+    float* lm = nullptr;
+    int ldm = 0;
+    if (!tok_mat.is_none()) {
+      at::Tensor t = tok_mat.cast<at::Tensor>();
+      i32c(t, "tok_mat");
+      chk(t.dim() == 2 && t.size(0) == B, "tok_mat [B, steps]");
+      tm = t.data_ptr<int>();
+      ldm = static_cast<int>(t.size(1));
+    }
+    if (!lp_mat.is_none()) {
+      at::Tensor t = lp_mat.cast<at::Tensor>();
+      f32c(t, "lp_mat");
+      chk(t.dim() == 2 && t.size(0) == B && (ldm == 0 || t.size(1) == ldm), "lp_mat [B, steps]");
+      lm = t.data_ptr<float>();
+      ldm = static_cast<int>(t.size(1));
+    }
+    const float* tp = nullptr;
+    if (!temp_t.is_none()) {
+      at::Tensor t = temp_t.cast<at::Tensor>();
+      f32c(t, "temp_t");
+      tp = t.data_ptr<float>();
+    }
+    unsigned char* dn = nullptr;
+    int* len = nullptr;
+    int* nd = nullptr;
+    if (eos_id >= 0) {
+      chk(!done.is_none() && !n_done.is_none(), "sample_filtered: eos_id needs done and n_done tensors");
+      at::Tensor d = done.cast<at::Tensor>();
+      chk(d.is_cuda() && d.scalar_type() == at::kByte && d.numel() >= B && d.is_contiguous(), "done: uint8 [B]");
+      dn = d.data_ptr<uint8_t>();
+      at::Tensor c = n_done.cast<at::Tensor>();
+      i32c(c, "n_done");
+      nd = c.data_ptr<int>();
+      if (!lengths.is_none()) {
+        at::Tensor l = lengths.cast<at::Tensor>();
+        i32c(l, "lengths");
+        chk(l.numel() >= B, "lengths [B]");
+        len = l.data_ptr<int>();
+      }
+    }
+    if (!seed_t.is_none()) {
+      at::Tensor t = seed_t.cast<at::Tensor>();
+      chk(t.is_cuda() && t.scalar_type() == at::kLong && t.numel() >= 1, "seed_t: int64 CUDA tensor");
+    }
+    cuda_ok(tb_sample_filtered(logits.data_ptr(), logits.stride(0), B, static_cast<int>(logits.size(1)), temperature,
+                               top_k, top_p, seed, ptr_i64(step_ptr), step, out_tok.data_ptr<int>(), lp, tm, lm, ldm,
+                               reinterpret_cast<const unsigned long long*>(ptr_i64(seed_t)), tp, eos_id, pad_id, dn,
+                               len, nd, turbol::StreamFor(logits)),
+            "sample_filtered");
+  }, py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"), py::arg("seed"),
+     py::arg("step_ptr"), py::arg("step"), py::arg("out_tok"), py::arg("out_logp") = py::none(),
+     py::arg("tok_mat") = py::none(), py::arg("lp_mat") = py::none(), py::arg("seed_t") = py::none(),
+     py::arg("temp_t") = py::none(), py::arg("eos_id") = -1, py::arg("pad_id") = 0, py::arg("done") = py::none(),
+     py::arg("lengths") = py::none(), py::arg("n_done") = py::none());
   m.def("logprob", [=](at::Tensor logits, at::Tensor target, py::object logp, py::object dlogp, float inv_temp) {
     bf16_2d(logits, "logits");
     i32c(target, "target");

@@ -18,9 +18,9 @@ std::string Status::ToString() const {
     case StatusCode::kInvalidArgument: name = "InvalidArgument"; break;
     case StatusCode::kNotFound: name = "NotFound"; break;
     case StatusCode::kAlreadyExists: name = "AlreadyExists"; break;
-    case StatusCode::kOutOfMemory: name = "OutOfMemory"; break;
+    case StatusCode::kResourceExhausted: name = "ResourceExhausted"; break;
+    case StatusCode::kUnimplemented: name = "Unimplemented"; break;
     case StatusCode::kInternalError: name = "InternalError"; break;
-    case StatusCode::kNotImplemented: name = "NotImplemented"; break;
     case StatusCode::kUnavailable: name = "Unavailable"; break;
     case StatusCode::kTimeout: name = "Timeout"; break;
     case StatusCode::kCudaError: name = "CudaError"; break;

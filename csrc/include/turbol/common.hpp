@@ -27,12 +27,15 @@ enum class StatusCode : int {
   kInvalidArgument = 1,
   kNotFound = 2,
   kAlreadyExists = 3,
-  kOutOfMemory = 4,
-  kInternalError = 5,
-  kNotImplemented = 6,
+  kResourceExhausted = 4,
+  kUnimplemented = 5,
+  kInternalError = 6,
   kUnavailable = 7,
   kTimeout = 8,
   kCudaError = 100,
+  // Older names of this library, kept as aliases of the same values.
+  kOutOfMemory = kResourceExhausted,
+  kNotImplemented = kUnimplemented,
 };
 
 class Status {
@@ -43,9 +46,11 @@ class Status {
   static Status InvalidArgument(const std::string& m) { return {StatusCode::kInvalidArgument, m}; }
   static Status NotFound(const std::string& m) { return {StatusCode::kNotFound, m}; }
   static Status AlreadyExists(const std::string& m) { return {StatusCode::kAlreadyExists, m}; }
-  static Status OutOfMemory(const std::string& m) { return {StatusCode::kOutOfMemory, m}; }
+  static Status ResourceExhausted(const std::string& m) { return {StatusCode::kResourceExhausted, m}; }
+  static Status OutOfMemory(const std::string& m) { return ResourceExhausted(m); }
+  static Status Unimplemented(const std::string& m) { return {StatusCode::kUnimplemented, m}; }
+  static Status NotImplemented(const std::string& m) { return Unimplemented(m); }
   static Status InternalError(const std::string& m) { return {StatusCode::kInternalError, m}; }
-  static Status NotImplemented(const std::string& m) { return {StatusCode::kNotImplemented, m}; }
   static Status Unavailable(const std::string& m) { return {StatusCode::kUnavailable, m}; }
   static Status Timeout(const std::string& m) { return {StatusCode::kTimeout, m}; }
   static Status CudaError(const std::string& m) { return {StatusCode::kCudaError, m}; }

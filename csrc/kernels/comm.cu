@@ -7,8 +7,9 @@
 //                           writes the result into every peer's output.
 //   tb_peer_allreduce_adam  the data-parallel optimizer step in one kernel:
 //                           reduce-scatter of the fp32 gradient (peer loads),
-//                           Adam on the owned shard (ZeRO-1 style: the moments
-//                           of a shard live only on its owner), all-gather of
+//                           Adam on the owned shard (ZeRO-1: the Adam moments
+//                           are shard-sized arrays that exist only on the
+//                           shard's owner), all-gather of
 //                           the updated fp32 weights and their bf16 copy
 //                           (peer stores).
 //
@@ -71,12 +72,15 @@ struct Hdr {
   unsigned flags_out[TB_MAX_PEERS];  // "peer p finished writing its outputs into me" (epoch)
 };
 
-// Slice [lo, hi) of n elements owned by `rank`, rounded to multiples of 4.
-__device__ __forceinline__ void owned_slice(long long n, int rank, int W, long long& lo, long long& hi) {
+// Slice [lo, hi) of n elements owned by `rank`, rounded to multiples of 4
+// (the host computes the same split in tb_peer_owned_slice).
+__host__ __device__ __forceinline__ void owned_slice(long long n, int rank, int W, long long& lo, long long& hi) {
   const long long n4 = (n + 3) / 4;
   const long long per = (n4 + W - 1) / W;
-  lo = min(n4, per * rank) * 4;
-  hi = min(n, min(n4, per * (rank + 1)) * 4);
+  const long long a = per * rank, b = per * (rank + 1);
+  lo = (a < n4 ? a : n4) * 4;
+  const long long h4 = (b < n4 ? b : n4) * 4;
+  hi = h4 < n ? h4 : n;
 }
 
 __device__ void publish_and_finish(const TbPeerTable& t, unsigned epoch, unsigned* done_ctr, int* err) {
@@ -223,10 +227,10 @@ __global__ void __launch_bounds__(kBlock) allreduce_adam_kernel(TbPeerTable t, l
       for (int j = 0; j < 4; ++j) {
         if (j < cnt) {
           pv[j] = pl[j];
-          float mm = m[i + j], vv = v[i + j];
+          float mm = m[i - lo + j], vv = v[i - lo + j];  // moments: this rank's shard only
           adam1(pv[j], g[j] * gs, mm, vv, hp, bc1, bc2);
-          m[i + j] = mm;
-          v[i + j] = vv;
+          m[i - lo + j] = mm;
+          v[i - lo + j] = vv;
         }
       }
       __nv_bfloat162 b01 = __floats2bfloat162_rn(pv[0], pv[1]), b23 = __floats2bfloat162_rn(pv[2], pv[3]);
@@ -275,6 +279,10 @@ __global__ void bounded_wait_probe_kernel(const unsigned* flags, int n, unsigned
 extern "C" {
 
 size_t tb_peer_header_bytes() { return sizeof(Hdr); }
+
+void tb_peer_owned_slice(long long n, int rank, int world, long long* lo, long long* hi) {
+  owned_slice(n, rank, world, *lo, *hi);
+}
 
 int tb_peer_allreduce(TbPeerTable t, long long in_off, long long out_off, long long n, float scale,
                       unsigned* done_ctr, int* err, cudaStream_t s) {

@@ -214,6 +214,15 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
 int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,
               const long long* step_ptr, long long step_imm, int* out_tok, float* out_logp, int* tok_mat,
               float* lp_mat, int ld_mat, const unsigned long long* seed_ptr, const float* temp_ptr, cudaStream_t s);
+// Sampling with top-k (k <= 0: off), top-p (p >= 1: off) and an end-of-sequence
+// stop (eos_id < 0: off; then done [B] flags, lengths [B] and the n_done
+// counter are updated).  The returned log-prob is under the full tempered
+// softmax.
+int tb_sample_filtered(const void* logits, long long ld, int B, int V, float temperature, int top_k, float top_p,
+                       unsigned long long seed, const long long* step_ptr, long long step_imm, int* out_tok,
+                       float* out_logp, int* tok_mat, float* lp_mat, int ld_mat, const unsigned long long* seed_ptr,
+                       const float* temp_ptr, int eos_id, int pad_id, unsigned char* done, int* lengths, int* n_done,
+                       cudaStream_t s);
 int tb_logprob(void* logits, long long ld, int T, int V, const int* target, float* logp, const float* dlogp,
                float inv_temp, cudaStream_t s);
 int tb_grpo_loss(const float* lp, const float* old_lp, const float* ref_lp, const float* adv, const float* mask,
@@ -296,8 +305,10 @@ int tb_tp_gemm_rs(const TbTpComm* c, const TbGemmArgs* a, void* out, long long l
 // of every rank's symmetric buffer (in-place when in_off == out_off).
 int tb_peer_allreduce(TbPeerTable t, long long in_off, long long out_off, long long n, float scale,
                       unsigned* done_ctr, int* err, cudaStream_t s);
-// grad (fp32) reduce-scatter -> Adam on the owned shard (m, v local, full length)
-// -> fp32 weights and bf16 copy written into every rank's buffer.
+// grad (fp32) reduce-scatter -> Adam on the owned shard -> fp32 weights and
+// bf16 copy written into every rank's buffer.  m and v hold the owned shard
+// only: element i of the owned slice [lo, hi) is m[i - lo].
+void tb_peer_owned_slice(long long n, int rank, int world, long long* lo, long long* hi);
 int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_off, long long shadow_off, long long n,
                            float* m, float* v, TbAdamParams hp, const long long* step_ptr, unsigned* done_ctr,
                            int* err, cudaStream_t s);

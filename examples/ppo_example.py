@@ -131,7 +131,8 @@ def main(argv=None):
                 prom.write_gauge("turbol_ppo_mean_return",
                                  float(m["mean_return"]) if m["mean_return"] == m["mean_return"] else 0.0)
                 prom.flush()
-        if args.checkpoint_dir and args.checkpoint_every and (it + 1) % args.checkpoint_every == 0 and rank == 0:
+        if args.checkpoint_dir and args.checkpoint_every and (it + 1) % args.checkpoint_every == 0:
+            # every rank writes its own files (environments, RNG, optimizer shard)
             turbol.save_checkpoint(args.checkpoint_dir, it + 1, tr, background=False, keep_last=3)
     if rank == 0:
         tb.flush()

@@ -53,7 +53,7 @@ ext = CUDAExtension(
 setup(
     name="turbol_b200",
     version="0.1.0",
-    packages=["turbol_b200"],
+    packages=["turbol_b200", "turbol"],
     ext_modules=[ext],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
 )

@@ -56,6 +56,16 @@ def test_status_and_shape():
         sh[5]
 
 
+def test_status_codes_match_reference_values():
+    # turbol_vllm/include/turbol/common.hpp:97-108: the integer codes and names
+    sc = turbol.StatusCode
+    expect = {"kOk": 0, "kInvalidArgument": 1, "kNotFound": 2, "kAlreadyExists": 3, "kResourceExhausted": 4,
+              "kUnimplemented": 5, "kInternalError": 6, "kUnavailable": 7, "kTimeout": 8, "kCudaError": 100}
+    for name, val in expect.items():
+        assert int(getattr(sc, name)) == val, name
+    assert int(sc.kOutOfMemory) == 4 and int(sc.kNotImplemented) == 5  # aliases
+
+
 def test_config_roundtrip(tmp_path):
     c = turbol.Config()
     c.set("lr", 3e-4)

@@ -7,7 +7,8 @@ HBM directly over NVLink.
 
 :class:`FusedDataParallelAdam` keeps a model's flat fp32 weights, flat fp32
 gradient and bf16 weight copy inside that symmetric memory; one kernel per step
-reduces the gradient across ranks, runs Adam on the shard each rank owns and
+reduces the gradient across ranks, runs Adam on the shard each rank owns (the
+Adam moments are allocated for that shard only: ZeRO-1) and
 writes the updated weights (fp32 and bf16) into every rank.  It replaces
 "NCCL all-reduce + local Adam" with a single launch that is replayable inside a
 CUDA graph.  :class:`FusedGradSync` is the gradient-only variant (sum/mean
@@ -65,8 +66,11 @@ class FusedDataParallelAdam:
         self.grad = self.pb.tensor(self.off_grad, self.numel, torch.float32)
         self.shadow = self.pb.tensor(self.off_shadow, self.numel, torch.bfloat16)
         dev = self.param.device
-        self.m = torch.zeros(self.numel, device=dev)
-        self.v = torch.zeros(self.numel, device=dev)
+        # ZeRO-1: the Adam moments exist only for the slice this rank updates
+        self.shard_lo, self.shard_hi = _ops().peer_owned_slice(self.numel, self.pb.rank, self.world)
+        shard = max(1, self.shard_hi - self.shard_lo)
+        self.m = torch.zeros(shard, device=dev)
+        self.v = torch.zeros(shard, device=dev)
         self.step_t = torch.zeros(1, dtype=torch.int64, device=dev)
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.scale = 1.0 / self.world
@@ -85,9 +89,16 @@ class FusedDataParallelAdam:
         _ops().counter_add(self.step_t, 1)
 
     def state_dict(self):
-        return {"m": self.m, "v": self.v, "step": self.step_t.clone()}
+        """This rank's optimizer shard: the moments of elements [lo, hi) of the
+        flat parameter vector (each data-parallel rank saves its own)."""
+        return {"m": self.m, "v": self.v, "step": self.step_t.clone(), "shard": (self.shard_lo, self.shard_hi),
+                "numel": self.numel, "world": self.world}
 
     def load_state_dict(self, sd):
+        shard = tuple(sd.get("shard", (self.shard_lo, self.shard_hi)))
+        if shard != (self.shard_lo, self.shard_hi) or sd["m"].numel() != self.m.numel():
+            raise ValueError(f"optimizer shard {shard} does not match this rank's slice "
+                             f"({self.shard_lo}, {self.shard_hi}); load the file saved by the same data-parallel rank")
         self.m.copy_(sd["m"])
         self.v.copy_(sd["v"])
         self.step_t.copy_(sd["step"])

@@ -197,6 +197,18 @@ class GRPOTrainer:
         self.last_times = {}
 
     # ------------------------------------------------------------------ checkpoint
+    def checkpoint_ranks(self) -> dict:
+        """Place of this rank in a checkpoint.  Tensor-parallel training: one
+        policy file per TP shard (``_tp<t>_pp0``), optimizer and trainer state
+        per data-parallel rank of that shard.  Full-model data parallelism: one
+        policy file, optimizer/trainer state per rank."""
+        if self.tp_mode == "train":
+            return {"tp_rank": self.tp_rank, "pp_rank": 0, "dp_rank": self.mesh.dp_rank,
+                    "layout": {"tp": self.tp, "pp": 1, "dp": self.mesh.dp}}
+        if self.dp != "none":
+            return {"dp_rank": self.rank, "layout": {"tp": 1, "pp": 1, "dp": self.world}}
+        return {}
+
     def state_dict(self) -> dict:
         """Master weights (fp32), the frozen reference weights, optimizer state and
         the step counter (which also keys the prompt and sampling streams)."""
@@ -210,6 +222,8 @@ class GRPOTrainer:
             self.model.shadow.copy_(sd["policy"]["shadow"])
             self.ref.shadow.copy_(sd["ref_shadow"])
             self.opt.load_state_dict(sd["optim"])
+            if self.tp_mode == "rollout":
+                self.tpm.load_from(self.model)  # the rollout shard follows the loaded weights
         self.step_count = int(sd["step_count"])
         self.gen.calls = int(sd["gen_calls"])
 

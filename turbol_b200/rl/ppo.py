@@ -78,7 +78,7 @@ class PPOTrainer:
         """dp: "none"; "nccl" (NCCL all-reduce of the gradient + local fused
         Adam); "fused" (one NVLink peer-memory kernel: gradient reduce-scatter,
         sharded Adam, weight all-gather)."""
-        self.cfg, self.rank, self.dp = cfg, rank, dp
+        self.cfg, self.rank, self.dp, self.group = cfg, rank, dp, group
         if dp == "fused" and not (device.startswith("cuda") if isinstance(device, str) else device.type == "cuda"):
             raise ValueError("the fused data-parallel step needs CUDA devices")
         if dp == "nccl" and grad_sync is None:
@@ -376,6 +376,16 @@ class PPOTrainer:
 
     def env_steps_per_iteration(self) -> int:
         return self.cfg.batch
+
+    def checkpoint_ranks(self) -> dict:
+        """Place of this rank in a checkpoint: with data parallelism every rank
+        saves its own environments, RNG and (fused step) optimizer shard; the
+        policy is the same on every rank and is written by rank 0."""
+        if self.dp == "none":
+            return {}
+        import torch.distributed as dist
+
+        return {"dp_rank": dist.get_rank(self.group), "layout": {"tp": 1, "pp": 1, "dp": dist.get_world_size(self.group)}}
 
     def state_dict(self):
         pol = self.net.state_dict() if self.fused else self.policy.state_dict()

@@ -8,8 +8,9 @@ their first block-table entries at the prompt's blocks), prefill through the
 flash-attention kernel, and a decode step — embedding, per layer RMSNorm, QKV
 GEMM (+bias), RoPE, KV write, paged GQA decode attention, output GEMM
 (+residual), RMSNorm, gate/up GEMM with fused SwiGLU, down GEMM (+residual),
-final norm, LM-head GEMM, temperature sampling — captured once as a CUDA graph
-and replayed per token.  The sampled tokens and their log-probabilities land
+final norm, LM-head GEMM, sampling (temperature; top-k, top-p and an
+end-of-sequence stop through the filtered sampler) — captured once as a CUDA
+graph and replayed per token.  The sampled tokens and their log-probabilities land
 in [B, max_new] device matrices (the column comes from a device counter).
 
 :class:`RolloutEngine` keeps the reference's API
@@ -123,11 +124,33 @@ class LLMGenerator:
             o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw_down)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
-        o.sample(st["logits"], 1.0, 0, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
-                 seed_t=st["seed_t"], temp_t=st["temp_t"])
+        self._sample(st)
         st["pos"].add_(1)
         st["ctx"].add_(1)
         o.counter_add(st["step"], 1)
+
+    # ------------------------------------------------------------ sampling
+    sampling = (-1, 1.0, -1, 0)  # (top_k, top_p, eos_id, pad_id): plain temperature sampling
+
+    def _filtered(self) -> bool:
+        k, p, eos, _ = self.sampling
+        return k > 0 or p < 1.0 or eos >= 0
+
+    def _sample(self, st, seed: Optional[int] = None, temperature: Optional[float] = None):
+        """Samples st["tok"] from st["logits"] into column st["step"] of the
+        generation matrices.  Without explicit seed / temperature they are read
+        from device memory (the captured decode step)."""
+        o = _ops()
+        dev_args = {} if seed is not None else {"seed_t": st["seed_t"], "temp_t": st["temp_t"]}
+        t = 1.0 if temperature is None else temperature
+        sd = 0 if seed is None else seed
+        if self._filtered():
+            k, p, eos, pad = self.sampling
+            o.sample_filtered(st["logits"], t, k, p, sd, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"],
+                              eos_id=eos, pad_id=pad, done=st["done"], lengths=st["lengths"], n_done=st["n_done"],
+                              **dev_args)
+        else:
+            o.sample(st["logits"], t, sd, st["step"], 0, st["tok"], None, st["tok_mat"], st["lp_mat"], **dev_args)
 
     def _alloc_state(self, B: int, steps: int):
         cfg = self.cfg
@@ -150,6 +173,10 @@ class LLMGenerator:
             # captured decode step serves every generate call
             "seed_t": torch.zeros(1, device=dev, dtype=torch.int64),
             "temp_t": torch.ones(1, device=dev, dtype=torch.float32),
+            # end-of-sequence state (used when an eos_id is given)
+            "done": torch.zeros(B, device=dev, dtype=torch.uint8),
+            "lengths": torch.full((B,), steps, device=dev, dtype=torch.int32),
+            "n_done": torch.zeros(1, device=dev, dtype=torch.int32),
             **self._split_workspace(B),
         }
 
@@ -165,8 +192,16 @@ class LLMGenerator:
 
     # ------------------------------------------------------------ generate
     @torch.no_grad()
-    def generate(self, prompts: torch.Tensor, group: int = 1, max_new: int = 16, temperature: float = 1.0):
-        """prompts [P, Lp] int -> (sequences [P*G, Lp+max_new] int32, logp [P*G, max_new] fp32)."""
+    def generate(self, prompts: torch.Tensor, group: int = 1, max_new: int = 16, temperature: float = 1.0,
+                 top_k: int = -1, top_p: float = 1.0, eos_id: int = -1, pad_id: int = 0, stop_check: int = 16):
+        """prompts [P, Lp] int -> (sequences [P*G, Lp+max_new] int32, logp [P*G, max_new] fp32).
+
+        top_k > 0 keeps the k most likely tokens, top_p < 1 the smallest set
+        of them holding probability p (nucleus); temperature <= 0 is greedy.
+        With eos_id >= 0 a sequence stops at its first eos_id (later columns
+        hold pad_id and log-prob 0), ``self.last_lengths`` [P*G] gives each
+        response's length (eos included) and decoding ends as soon as every
+        sequence has stopped (checked every ``stop_check`` tokens)."""
         o = _ops()
         cfg, m = self.cfg, self.m
         P, Lp = prompts.shape
@@ -174,6 +209,10 @@ class LLMGenerator:
         B = P * G
         if B > self.max_batch or Lp + max_new > self.max_len:
             raise ValueError("generate: batch or length beyond the engine's capacity")
+        sampling = (int(top_k), float(top_p), int(eos_id), int(pad_id))
+        if sampling != self.sampling:
+            self.sampling = sampling
+            self._graph = None  # the captured step holds the sampler's kind
         self.temperature = float(temperature)
         self.calls += 1
         table, pre_table, n_shared, tail = self._tables(P, G, Lp, max_new)
@@ -211,8 +250,14 @@ class LLMGenerator:
         st["step"].zero_()
         st["seed_t"].fill_(self.seed + 7919 * self.calls)
         st["temp_t"].fill_(self.temperature)
-        o.sample(st["logits"], self.temperature, self.seed + 7919 * self.calls + 1, st["step"], 0, st["tok"], None,
-                 st["tok_mat"], st["lp_mat"])
+        eos = self.sampling[2] >= 0
+        if eos:
+            st["done"].zero_()
+            st["n_done"].zero_()
+            st["lengths"].fill_(max_new)
+            st["tok_mat"].fill_(self.sampling[3])
+            st["lp_mat"].zero_()
+        self._sample(st, seed=self.seed + 7919 * self.calls + 1, temperature=self.temperature)
         o.counter_add(st["step"], 1)
         st["pos"].fill_(Lp)
         st["ctx"].fill_(Lp + 1)
@@ -238,11 +283,19 @@ class LLMGenerator:
                     for k, v in saved.items():
                         st[k].copy_(v)
                     self._graph, self._graph_B = g, (B, max_new)
-                for _ in range(steps):
-                    self._graph.replay()
+                step_fn = self._graph.replay
             else:
-                for _ in range(steps):
+                def step_fn():
                     self._decode_step(B)
+            done_steps = 0
+            while done_steps < steps:
+                n = min(stop_check if eos else steps, steps - done_steps)
+                for _ in range(n):
+                    step_fn()
+                done_steps += n
+                if eos and int(st["n_done"].item()) >= B:  # every sequence has stopped
+                    break
+        self.last_lengths = st["lengths"].clone() if eos else None
         seqs = torch.cat([prompts.repeat_interleave(G, 0), st["tok_mat"]], 1)
         return seqs, st["lp_mat"].clone()
 
@@ -315,18 +368,34 @@ class RolloutEngine:
             return self._vllm.generate_batch(prompts)
         if self._gen is None:
             return ["[RolloutEngine] " + p for p in prompts]  # echo fallback (no GPU / no model)
-        tok = self._tok
+        out: List[str] = []
+        cap = max(1, min(self.config.max_batch_size, self._gen.max_batch))
+        for i in range(0, len(prompts), cap):  # batches of at most max_batch_size prompts
+            out.extend(self._generate_native(prompts[i:i + cap]))
+        return out
+
+    def _generate_native(self, prompts: List[str]) -> List[str]:
+        c, tok = self.config, self._tok
         vocab = self._gen.cfg.vocab
         enc = [[t % vocab for t in tok.encode(p, True, False)] for p in prompts]
         L = max(len(e) for e in enc)
         ids = torch.full((len(enc), L), tok.pad_id % vocab, dtype=torch.int32)
         for i, e in enumerate(enc):
             ids[i, L - len(e):] = torch.tensor(e, dtype=torch.int32)  # left pad
-        new = max(1, min(self.config.max_new_tokens, self._gen.max_len - L))
-        seqs, _ = self._gen.generate(ids, 1, new, self.config.temperature)
+        new = max(1, min(c.max_new_tokens, self._gen.max_len - L))
+        eos = tok.eos_id % vocab
+        seqs, _ = self._gen.generate(ids, 1, new, c.temperature, top_k=c.top_k, top_p=c.top_p, eos_id=eos,
+                                     pad_id=tok.pad_id % vocab)
+        lens = self._gen.last_lengths.cpu().tolist()
         out = seqs[:, L:].cpu().tolist()
-        # random-init weights emit arbitrary bytes: decode leniently
-        return [bytes(t for t in row if t < 256).decode("utf-8", errors="replace") for row in out]
+        texts = []
+        for row, n in zip(out, lens):
+            row = row[:n]
+            if row and row[-1] == eos:
+                row = row[:-1]  # the stop token is not part of the text
+            # random-init weights emit arbitrary bytes: decode leniently
+            texts.append(bytes(t for t in row if t < 256).decode("utf-8", errors="replace"))
+        return texts
 
 
 # ---------------------------------------------------------------------------

@@ -16,8 +16,20 @@ This module defines the format:
         replay.pt                 optional replay-buffer contents
         config.cfg                configuration, ``key=value`` (readable by
                                   ``turbol_b200.Config.load``)
-        COMPLETE                  written last: a directory without it is an
-                                  interrupted save and is ignored by ``latest_step``
+        COMPLETE<sfx>             written last by each saving rank, with the
+                                  layout of the save (tp, pp and dp sizes).  A
+                                  step counts as complete only when the marker
+                                  of every rank of that layout is present; an
+                                  interrupted or partial save is ignored by
+                                  ``latest_step`` and refused by ``load_checkpoint``.
+
+File suffixes: ``_tp<t>_pp<p>`` when the layout has more than one tensor- or
+pipeline-parallel rank (the model is sharded), and ``_dp<d>`` on the files of
+state that differs between data-parallel ranks (sharded optimizer moments,
+each rank's environments and RNG).  The policy of a (tp, pp) shard is written
+once, by data-parallel rank 0.  A trainer reports its place in the layout with
+``checkpoint_ranks()`` (``tp_rank``, ``pp_rank``, ``dp_rank``, ``layout``);
+explicit arguments override it.
 
 A trainer participates through ``state_dict()`` returning a dict whose
 ``"policy"`` and ``"optim"`` entries go to their own files and whose other
@@ -29,6 +41,7 @@ thread writes the files.
 """
 from __future__ import annotations
 
+import json
 import os
 import re
 import shutil
@@ -100,13 +113,68 @@ def read_config(path: str) -> Dict[str, str]:
     return out
 
 
-def _suffix(tp: int, pp: int, dp: Optional[int]) -> str:
+def _suffix(tp: int, pp: int, dp: Optional[int], sharded: bool) -> str:
     s = ""
     if dp is not None:
         s += f"_dp{dp}"
-    if tp or pp:
+    if sharded:
         s += f"_tp{tp}_pp{pp}"
     return s
+
+
+def _resolve_ranks(trainer, tp_rank, pp_rank, dp_rank, layout):
+    """Fills unset rank arguments from ``trainer.checkpoint_ranks()``."""
+    auto = {}
+    if trainer is not None and hasattr(trainer, "checkpoint_ranks"):
+        auto = trainer.checkpoint_ranks() or {}
+    tp_rank = auto.get("tp_rank", 0) if tp_rank is None else tp_rank
+    pp_rank = auto.get("pp_rank", 0) if pp_rank is None else pp_rank
+    if dp_rank is None:
+        dp_rank = auto.get("dp_rank")
+    lay = dict(auto.get("layout") or {})
+    lay.update(layout or {})
+    tp = int(lay.get("tp", max(1, tp_rank + 1)))
+    pp = int(lay.get("pp", max(1, pp_rank + 1)))
+    dp = int(lay.get("dp", 0 if dp_rank is None else dp_rank + 1))
+    if dp_rank is not None and dp < 1:
+        raise ValueError("a per-data-parallel-rank save needs layout['dp'] >= 1")
+    return int(tp_rank), int(pp_rank), dp_rank, {"tp": tp, "pp": pp, "dp": dp if dp_rank is not None else 0}
+
+
+def _marker_names(layout) -> set:
+    sharded = layout["tp"] * layout["pp"] > 1
+    dps = [None] if layout["dp"] == 0 else list(range(layout["dp"]))
+    return {f"COMPLETE{_suffix(t, p, d, sharded)}" for t in range(layout["tp"]) for p in range(layout["pp"])
+            for d in dps}
+
+
+def _read_marker(path: str):
+    try:
+        with open(path) as f:
+            text = f.read().strip()
+        d = json.loads(text)
+        if isinstance(d, dict) and {"tp", "pp", "dp"} <= set(d):
+            return {"tp": int(d["tp"]), "pp": int(d["pp"]), "dp": int(d["dp"])}
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def step_complete(path: str) -> bool:
+    """True when every rank of the save's layout wrote its marker in ``path``."""
+    if not os.path.isdir(path):
+        return False
+    names = {f for f in os.listdir(path) if f.startswith("COMPLETE")}
+    if not names:
+        return False
+    for n in sorted(names):
+        lay = _read_marker(os.path.join(path, n))
+        if lay is None:
+            if n == "COMPLETE":  # a single-process save of the first format
+                return True
+            continue
+        return _marker_names(lay) <= names
+    return False
 
 
 class SaveHandle:
@@ -128,13 +196,21 @@ class SaveHandle:
 
 
 def save_checkpoint(directory: str, step: int, trainer=None, *, state: Optional[Dict[str, Any]] = None,
-                    config=None, replay: Optional[Dict[str, Any]] = None, tp_rank: int = 0, pp_rank: int = 0,
-                    dp_rank: Optional[int] = None, write_config: bool = True, background: bool = False,
+                    config=None, replay: Optional[Dict[str, Any]] = None, tp_rank: Optional[int] = None,
+                    pp_rank: Optional[int] = None, dp_rank: Optional[int] = None, layout: Optional[dict] = None,
+                    write_config: bool = True, background: bool = False,
                     keep_last: Optional[int] = None) -> SaveHandle:
-    """Writes ``<directory>/step_<step>/``.  ``state`` defaults to
-    ``trainer.state_dict()``; ``config`` defaults to ``trainer.cfg``.  With
-    ``background=True`` returns at once after the host snapshot; call
-    ``.wait()`` on the handle before relying on the files."""
+    """Writes this rank's files of ``<directory>/step_<step>/``.  Every rank of
+    a parallel job calls it (each writes its own shards and marker).
+    ``state`` defaults to ``trainer.state_dict()``; ``config`` to
+    ``trainer.cfg``; the ranks and ``layout`` ({"tp", "pp", "dp"} sizes) to
+    ``trainer.checkpoint_ranks()``.  With ``background=True`` returns at once
+    after the host snapshot; call ``.wait()`` on the handle before relying on
+    the files.  ``keep_last`` (applied by the lead rank) deletes all but the
+    newest ``keep_last`` complete steps; an incomplete newer step that other
+    ranks may still be writing is never counted or touched."""
+    tp_rank, pp_rank, dp_rank, lay = _resolve_ranks(trainer, tp_rank, pp_rank, dp_rank, layout)
+    lead = tp_rank == 0 and pp_rank == 0 and not dp_rank
     if state is None:
         if trainer is None:
             raise ValueError("save_checkpoint needs a trainer or a state dict")
@@ -146,8 +222,10 @@ def save_checkpoint(directory: str, step: int, trainer=None, *, state: Optional[
     snap = _to_host(dict(state))
     rep = _to_host(replay) if replay is not None else None
     path = os.path.join(directory, f"step_{int(step)}")
-    sfx = _suffix(tp_rank, pp_rank, None)
-    osfx = _suffix(tp_rank, pp_rank, dp_rank)
+    sharded = lay["tp"] * lay["pp"] > 1
+    sfx = _suffix(tp_rank, pp_rank, None, sharded)
+    osfx = _suffix(tp_rank, pp_rank, dp_rank, sharded)
+    marker = json.dumps({"step": int(step), **lay})
 
     def write():
         os.makedirs(path, exist_ok=True)
@@ -160,13 +238,16 @@ def save_checkpoint(directory: str, step: int, trainer=None, *, state: Optional[
         torch.save(snap, os.path.join(path, f"trainer{osfx}.pt"))
         if rep is not None:
             torch.save(rep, os.path.join(path, f"replay{osfx}.pt"))
-        if write_config and config is not None and tp_rank == 0 and pp_rank == 0 and not dp_rank:
+        if write_config and config is not None and lead:
             _write_config(os.path.join(path, "config.cfg"), config)
-        with open(os.path.join(path, f"COMPLETE{osfx}"), "w") as f:
-            f.write(str(int(step)) + "\n")
-        if keep_last is not None and tp_rank == 0 and pp_rank == 0 and not dp_rank:
+        tmp = os.path.join(path, f".COMPLETE{osfx}.tmp")
+        with open(tmp, "w") as f:
+            f.write(marker + "\n")
+        os.replace(tmp, os.path.join(path, f"COMPLETE{osfx}"))
+        if keep_last is not None and lead:
             for old in list_steps(directory)[:-keep_last]:
-                shutil.rmtree(os.path.join(directory, f"step_{old}"), ignore_errors=True)
+                if old < int(step):
+                    shutil.rmtree(os.path.join(directory, f"step_{old}"), ignore_errors=True)
 
     if not background:
         write()
@@ -194,8 +275,7 @@ def list_steps(directory: str):
         m = _STEP_RE.match(name)
         if not m:
             continue
-        d = os.path.join(directory, name)
-        if any(f.startswith("COMPLETE") for f in os.listdir(d)):
+        if step_complete(os.path.join(directory, name)):
             steps.append(int(m.group(1)))
     return sorted(steps)
 
@@ -206,22 +286,33 @@ def latest_step(directory: str) -> Optional[int]:
 
 
 def load_checkpoint(directory: str, step: Optional[int] = None, trainer=None, *, map_location="cpu",
-                    tp_rank: int = 0, pp_rank: int = 0, dp_rank: Optional[int] = None, config=None,
-                    strict_config: bool = True) -> Dict[str, Any]:
-    """Reads ``<directory>/step_<step>`` (the latest completed one by default)
-    and returns the state dict (``policy``, ``optim`` and the trainer entries,
-    plus ``replay`` and ``config`` when present).  With ``trainer`` the state
-    is also loaded into it.  With ``config`` (or ``trainer.cfg``) the saved
-    configuration must match key for key unless ``strict_config=False``."""
+                    tp_rank: Optional[int] = None, pp_rank: Optional[int] = None, dp_rank: Optional[int] = None,
+                    layout: Optional[dict] = None, config=None, strict_config: bool = True) -> Dict[str, Any]:
+    """Reads this rank's files of ``<directory>/step_<step>`` (the latest
+    complete one by default) and returns the state dict (``policy``, ``optim``
+    and the trainer entries, plus ``replay`` and ``config`` when present).
+    With ``trainer`` the state is also loaded into it, and the ranks default
+    to ``trainer.checkpoint_ranks()``.  The step must be complete for its
+    layout and must hold this rank's marker.  With ``config`` (or
+    ``trainer.cfg``) the saved configuration must match key for key unless
+    ``strict_config=False``."""
+    tp_rank, pp_rank, dp_rank, lay = _resolve_ranks(trainer, tp_rank, pp_rank, dp_rank, layout)
     if step is None:
         step = latest_step(directory)
         if step is None:
             raise FileNotFoundError(f"no completed checkpoint under {directory}")
     path = os.path.join(directory, f"step_{int(step)}")
-    sfx = _suffix(tp_rank, pp_rank, None)
-    osfx = _suffix(tp_rank, pp_rank, dp_rank)
-    if not any(f.startswith("COMPLETE") for f in os.listdir(path)):
-        raise FileNotFoundError(f"{path} is not a completed checkpoint")
+    sharded = lay["tp"] * lay["pp"] > 1
+    sfx = _suffix(tp_rank, pp_rank, None, sharded)
+    osfx = _suffix(tp_rank, pp_rank, dp_rank, sharded)
+    if not step_complete(path):
+        raise FileNotFoundError(f"{path} is not a complete checkpoint (a rank's marker is missing)")
+    own = os.path.join(path, f"COMPLETE{osfx}")
+    if not os.path.exists(own) and not (osfx == "" and os.path.exists(os.path.join(path, "COMPLETE"))):
+        raise FileNotFoundError(f"{path} has no files of this rank (marker COMPLETE{osfx} missing)")
+    saved_lay = _read_marker(own)
+    if saved_lay is not None and saved_lay != lay:
+        raise ValueError(f"checkpoint layout {saved_lay} differs from this job's {lay}")
     state: Dict[str, Any] = torch.load(os.path.join(path, f"trainer{osfx}.pt"), map_location=map_location,
                                        weights_only=False)
     pol = os.path.join(path, f"policy{sfx}.pt")
@@ -249,4 +340,5 @@ def load_checkpoint(directory: str, step: Optional[int] = None, trainer=None, *,
     return state
 
 
-__all__ = ["save_checkpoint", "load_checkpoint", "latest_step", "list_steps", "read_config", "SaveHandle"]
+__all__ = ["save_checkpoint", "load_checkpoint", "latest_step", "list_steps", "read_config", "SaveHandle",
+           "step_complete"]
