@@ -19,7 +19,7 @@ void cuda_ok(int e, const char* what) {
 // C = epi(A . B^T) with A [M,K] (a_mn=0) or [K,M] (a_mn=1), B [N,K] (b_mn=0) or [K,N] (b_mn=1).
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, bool b_mn, py::object bias,
           py::object aux, int epi, bool accumulate, float alpha, int split_k, int bn, py::object err,
-          py::object workspace, py::object colsum, py::object c2) {
+          py::object workspace, py::object colsum, py::object c2, int kgroup) {
   chk(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors required");
   chk(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: A and B must be bfloat16");
   chk(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D operands");
@@ -64,6 +64,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   a.alpha = alpha;
   a.split_k = split_k;
   a.bn_hint = bn;
+  a.kgroup = kgroup;
   if (!err.is_none()) a.error = err.cast<at::Tensor>().data_ptr<int>();
   at::Tensor ws, cs;
   if (!workspace.is_none()) {
@@ -95,7 +96,8 @@ void register_llm_ops(py::module_& m) {
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn") = false, py::arg("b_mn") = false,
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0f, py::arg("split_k") = 0, py::arg("bn") = 0, py::arg("error") = py::none(),
-        py::arg("workspace") = py::none(), py::arg("colsum") = py::none(), py::arg("c2") = py::none());
+        py::arg("workspace") = py::none(), py::arg("colsum") = py::none(), py::arg("c2") = py::none(),
+        py::arg("kgroup") = 0);
   m.def("gemm_workspace_numel", [](int M, int N, int K) {
     return static_cast<int64_t>(tb_gemm_workspace_bytes(M, N, K) / 4);
   });

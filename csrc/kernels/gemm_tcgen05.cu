@@ -85,6 +85,7 @@ struct DevArgs {
   int* error;
   __nv_bfloat16* c2;  // EPI_SWIGLU, optional: the raw gate/up accumulator [M, N] (bf16), row stride ldc2
   long long ldc2;
+  int kg_ntiles;      // block-diagonal B: n-tiles per diagonal block (0 = off); k_blocks is then per block
   TpArgs tp;
 };
 
@@ -543,6 +544,11 @@ __device__ __forceinline__ void work_coords(const DevArgs& p, int w, int& m0, in
   m0 = mt * BM;
   kb0 = ks * p.kb_per_split;
   kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+  if (p.kg_ntiles > 0) {  // block-diagonal B: only the K range of this tile's diagonal block
+    const int g = nt / p.kg_ntiles;
+    kb0 += g * p.k_blocks;
+    kb1 += g * p.k_blocks;
+  }
 }
 
 // 32 columns without the wait (callers batch loads, then wait once).
@@ -1313,7 +1319,13 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   const bool atomic_ok = a->c_fp32 && (a->epi == TB_EPI_NONE || a->epi == TB_EPI_BIAS) && !a->colsum;
   const bool have_ws = a->workspace != nullptr && ws_epi_ok &&
                        a->workspace_bytes >= kCntBytes + 2 * sizeof(float) * static_cast<size_t>(a->M) * a->N;
-  const Plan pl = make_plan(a->M, a->N, a->K, a->bn_hint, a->split_k, have_ws || atomic_ok,
+  const int kg = a->kgroup;
+  if (kg != 0 && (kg < 0 || kg % 64 || a->N % kg || a->K != a->N || swiglu || swiglu_bwd))
+    return static_cast<int>(cudaErrorInvalidValue);
+  // block-diagonal B: the tile width must divide the block, K is one block
+  int bn_hint = a->bn_hint;
+  if (kg && (bn_hint == 0 || kg % bn_hint)) bn_hint = kg % 256 == 0 ? 256 : (kg % 128 == 0 ? 128 : 64);
+  const Plan pl = make_plan(a->M, a->N, kg ? kg : a->K, bn_hint, a->split_k, have_ws || atomic_ok,
                             have_ws ? a->workspace_bytes : 0);
   const int BN = pl.BN;
   CUtensorMap ta, tbm;
@@ -1365,6 +1377,7 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.error = a->error;
   p.c2 = static_cast<__nv_bfloat16*>(a->C2);
   p.ldc2 = a->ldc2;
+  p.kg_ntiles = kg ? kg / BN : 0;
   const int total = tiles * p.splits;
   const int grid = total < num_sms() ? total : num_sms();
   const int am = a->a_mn ? 1 : 0, bm = a->b_mn ? 1 : 0;

@@ -182,6 +182,11 @@ typedef struct {
   float* colsum;           // optional [N] fp32: column sums of the output (e.g. a bias gradient)
   void* C2;                // EPI_SWIGLU, optional bf16 [M, N]: also receives the raw gate/up accumulator
   long long ldc2;
+  // Block-diagonal B (0 = off): B holds N / kgroup square diagonal blocks of
+  // kgroup x kgroup (zeros elsewhere), so output column n only needs the K range
+  // [g * kgroup, (g + 1) * kgroup) with g = n / kgroup; the kernel skips the rest.
+  // Needs K == N and kgroup a multiple of 64 that divides N.
+  int kgroup;
 } TbGemmArgs;
 
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);

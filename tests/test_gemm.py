@@ -204,3 +204,30 @@ def test_gemm_swiglu_save_and_backward_epilogues(M, N, K, b_mn, bn, dev):
     exp = torch.stack([g.grad, u.grad], -1).reshape(M, 2 * N)
     tol = 3e-2 * max(1.0, float(exp.abs().max()))
     assert torch.allclose(d_gu.float(), exp, atol=tol, rtol=2e-2), (d_gu.float() - exp).abs().max()
+
+
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("kg,bn", [(256, 128), (256, 0), (128, 64)])
+def test_gemm_block_diagonal_k_range(b_mn, kg, bn, dev):
+    """kgroup: output column n reads only the K range of its diagonal block of B.
+    B's off-diagonal blocks hold garbage here, so a kernel that still read them
+    would not match the fp32 product with the masked (block-diagonal) B."""
+    M, N = 1000, 512
+    A = _mk((M, N), dev, 3)
+    B = _mk((N, N), dev, 4)
+    mask = torch.zeros(N, N, device=dev, dtype=torch.bool)
+    for g in range(N // kg):
+        mask[g * kg:(g + 1) * kg, g * kg:(g + 1) * kg] = True
+    Bm = torch.where(mask, B, torch.zeros_like(B))
+    aux = _mk((M, N), dev, 5)
+    bias = torch.randn(N, device=dev)
+    for epi, kw in ((0, {}), (ops().EPI_BIAS_TANH, {"bias": bias}), (ops().EPI_TANH_BWD, {"aux": aux})):
+        C = torch.empty(M, N, device=dev, dtype=torch.bfloat16 if epi else torch.float32)
+        ops().gemm(A, B, C, False, b_mn, epi=epi, bn=bn, kgroup=kg, **kw)
+        acc = _ref(A, Bm, False, b_mn)
+        if epi == ops().EPI_BIAS_TANH:
+            acc = torch.tanh(acc + bias)
+        elif epi == ops().EPI_TANH_BWD:
+            acc = acc * (1 - aux.float() ** 2)
+        torch.cuda.synchronize()
+        assert torch.allclose(C.float(), acc, atol=3e-2 * (kg ** 0.5) / 8 + 2e-2, rtol=2e-2), (epi, (C.float() - acc).abs().max())

@@ -10,11 +10,14 @@ a single launch for both heads.  The 8-feature first layer runs on CUDA cores
 epilogues:
 
   forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
-            H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM
+            H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM over the diagonal
+                                            blocks only (kgroup: each output tile
+                                            iterates over its head's K range)
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
   backward  dZ2 = (dOut W3) * (1 - H2^2)    one CUDA-core pass (8 outputs per head) + db2 column sums
             dW3 = dOut^T H2                 one CUDA-core pass (8 rows per head, 18.6 vs 36.8 us as GEMMs)
-            dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM + tanh-backward epilogue (+ db1 column sums)
+            dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM (diagonal blocks only) + tanh-backward
+                                            epilogue (+ db1 column sums)
             dW2, dW1 = dZ^T H               MN-major x MN-major GEMMs, split-K, fp32
 No transposes are materialized and no [B, H] fp32 intermediates exist:
 activations and activation gradients are bf16, weights are the bf16 shadow
@@ -168,8 +171,9 @@ class FusedActorCritic:
         ws = ws or self.workspace(B)
         S, P = self.s, self.p
         o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], ws["h1"], True)                 # 8 input features: CUDA cores
-        # both heads' hidden layer (128-wide tiles: 34.2 vs 37.3 us at 32,768 rows)
-        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH, bn=128)
+        # both heads' hidden layer (128-wide tiles: 34.2 vs 37.3 us at 32,768 rows); kgroup=H: each
+        # output tile reads only its head's diagonal block of W2 (half the MMAs and operand loads)
+        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH, bn=128, kgroup=self.H)
         # (the CUDA-core mlp_head_fwd measured slower here: 26.7 vs 16.5 us at 32,768 rows)
         o.gemm(ws["h2"], S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)        # logits | value
         return ws["logits"], ws["value"]
@@ -204,5 +208,6 @@ class FusedActorCritic:
         # dW2 block = dZ2^T H1 (128-wide tiles, 32 K splits: 35.1 vs 42.9 us for both heads at 32,768 rows)
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
             o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk, bn=128, split_k=32)
-        o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"])   # dZ1, db1
+        o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"],   # dZ1, db1
+               kgroup=self.H)                                                    # (diagonal blocks of W2 only)
         o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
