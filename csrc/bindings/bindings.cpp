@@ -651,10 +651,16 @@ PYBIND11_MODULE(turbol_core, m) {
           return d;
         },
         py::arg("device_id") = 0);
+#if TURBOL_CUDA
   m.def("built_for", []() { return std::string("sm_100a"); });
+#else
+  m.def("built_for", []() { return std::string("cpu"); });
+#endif
 
+#if TURBOL_CUDA
   py::module_ ops = m.def_submodule("ops", "raw sm_100a kernel launchers on torch tensors");
   register_kernel_ops(ops);
   register_llm_ops(ops);
   register_comm_ops(ops);
+#endif
 }

@@ -1,7 +1,6 @@
 // Implementation of the foundation types declared in turbol/common.hpp.
 #include "turbol/common.hpp"
 
-#include <c10/cuda/CUDAGuard.h>
 
 #include <algorithm>
 #include <cctype>

@@ -1,6 +1,12 @@
 #include "turbol/observability.hpp"
 
+#if TURBOL_CUDA
 #include <nvtx3/nvToolsExt.h>
+#else  // CPU-only build: no NVTX (it ships with the CUDA toolkit)
+#define nvtxRangePushA(name) ((void)(name))
+#define nvtxRangePop() ((void)0)
+#define nvtxMarkA(name) ((void)(name))
+#endif
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -117,7 +123,7 @@ EventID Profiler::BeginEvent(const std::string& name, int device_id) {
   e.device_id = device_id;
   cudaEventCreate(&e.start);
   cudaEventCreate(&e.end);
-  cudaStream_t st = c10::cuda::getCurrentCUDAStream(device_id).stream();
+  cudaStream_t st = CurrentStream(device_id);
   cudaEventRecord(e.start, st);
   e.cpu_start_ns = NowNs();
   events_.push_back(e);
@@ -128,7 +134,7 @@ void Profiler::EndEvent(EventID id) {
   std::lock_guard<std::mutex> g(mu_);
   for (auto& e : events_) {
     if (e.id == id.id && !e.ended) {
-      cudaStream_t st = c10::cuda::getCurrentCUDAStream(e.device_id).stream();
+      cudaStream_t st = CurrentStream(e.device_id);
       cudaEventRecord(e.end, st);
       e.ended = true;
       return;

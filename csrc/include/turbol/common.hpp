@@ -12,8 +12,8 @@
 #pragma once
 
 #include <ATen/ATen.h>
-#include <c10/cuda/CUDAStream.h>
-#include <cuda_runtime.h>
+
+#include "turbol/cuda_compat.hpp"
 
 #include <cstdint>
 #include <string>
@@ -173,8 +173,6 @@ struct CudaMemoryInfo {
 CudaMemoryInfo GetCudaMemoryInfo(int device_id);
 
 // Current torch CUDA stream of the tensor's device (kernels launch there).
-inline cudaStream_t StreamFor(const at::Tensor& t) {
-  return c10::cuda::getCurrentCUDAStream(t.device().index()).stream();
-}
+inline cudaStream_t StreamFor(const at::Tensor& t) { return CurrentStream(t.device().index()); }
 
 }  // namespace turbol

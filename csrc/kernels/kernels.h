@@ -5,7 +5,11 @@
 // kernel needs it, is passed in by the caller.
 #pragma once
 
+#if !defined(TURBOL_CUDA) || TURBOL_CUDA
 #include <cuda_runtime.h>
+#else
+#include "turbol/cuda_compat.hpp"  // CPU-only build of the host core: runtime types only
+#endif
 #include <stddef.h>
 #include <stdint.h>
 

@@ -1,6 +1,14 @@
 """Build the native core of turbol_b200 in-tree.
 
     python setup.py build_ext --inplace
+    TURBOL_CPU_ONLY=1 python setup.py build_ext --build-lib <dir>   # host core only
+
+CPU-only build (TURBOL_CPU_ONLY=1): the host runtime (Tensor/Config/engines on
+CPU tensors/profiler/writers/tokenizer/dataset/store/schedules/KV allocator and
+the pybind11 module) compiled with the C++ compiler alone against torch's CPU
+headers: no nvcc, no CUDA runtime, no kernels (the ``ops`` submodule is absent
+and ``built_for()`` returns "cpu").  It is for machines without a GPU and for
+CI; write it to its own --build-lib so it does not replace the CUDA build.
 
 One extension, ``turbol_b200.turbol_core``, holds both the C++ host runtime
 (Tensor/Config/engines/profiler/writers/bootstrap store/pybind11 bindings) and
@@ -13,7 +21,7 @@ import glob
 import os
 
 from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -37,7 +45,27 @@ nvcc_flags = ARCH + [
 ]
 cxx_flags = ["-O3", "-std=c++17", "-DTURBOL_CUDA=1", "-Wno-unused-function"]
 
-ext = CUDAExtension(
+CPU_ONLY = os.environ.get("TURBOL_CPU_ONLY", "") not in ("", "0")
+
+
+def cpu_sources():
+    pats = ["csrc/core/*.cpp", "csrc/engines/*.cpp", "csrc/bindings/bindings.cpp", "csrc/cpu_only/*.cpp"]
+    out = []
+    for p in pats:
+        out += sorted(glob.glob(os.path.join(ROOT, p)))
+    out = [s for s in out if os.path.basename(s) != "peer.cpp"]  # NVLink peer memory: CUDA only
+    return [os.path.relpath(s, ROOT) for s in out]
+
+
+cpu_ext = CppExtension(
+    name="turbol_b200.turbol_core",
+    sources=cpu_sources(),
+    include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")],
+    extra_compile_args=["-O3", "-std=c++17", "-DTURBOL_CUDA=0", "-Wno-unused-function", "-Wno-unused-parameter"],
+    extra_link_args=["-l:libstdc++.so.6"],
+)
+
+ext = cpu_ext if CPU_ONLY else CUDAExtension(
     name="turbol_b200.turbol_core",
     sources=sources(),
     include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")],
