@@ -96,7 +96,11 @@ def run_grpo(args, world, rank, local):
         tr.opt.check()
     if tp > 1:
         tr.comm.check()
-    par = "dp1" if tp == 1 else f"tp{tp}xdp{replicas} (fused TP collectives, fused DP optimizer step)"
+    if tr.sync is not None:
+        tr.sync.check()
+    par = "dp1" if tp == 1 else (f"tp{tp}xdp{replicas}: tensor-parallel training on the fused TP collectives, "
+                                 f"fused DP optimizer step over the {replicas} replicas, rollout on a full bf16 "
+                                 f"replica per GPU refreshed by the fused weight all-gather")
     out = {"metric": "GRPO train tokens/s/box", "value": replicas * cfg.batch * cfg.seq_len / sec,
            "unit": "tokens/s", "n_gpus": world, "steps": args.grpo_steps, "warmup": warm, "s_per_step": sec,
            "phases_s": {k: last[k] for k in ("rollout_s", "reward_ref_s", "train_s")},

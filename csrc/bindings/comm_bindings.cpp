@@ -117,6 +117,19 @@ void register_comm_ops(py::module_& m) {
                      "peer_allreduce");
            },
            py::arg("in_offset"), py::arg("out_offset"), py::arg("numel"), py::arg("scale") = 1.0f)
+      .def("scatter_copy",
+           [](PeerMemory& p, at::Tensor src0, at::Tensor src1, at::Tensor segs, int64_t total_vecs, int64_t dst_base) {
+             static_assert(sizeof(TbCopySeg) == 8 * sizeof(int64_t), "TbCopySeg layout");
+             if (!src0.is_cuda() || !src1.is_cuda() || !segs.is_cuda() || segs.scalar_type() != at::kLong ||
+                 segs.dim() != 2 || segs.size(1) != 8 || !segs.is_contiguous())
+               throw std::invalid_argument("scatter_copy: CUDA sources and int64 segments [n, 8] on the device");
+             cuda_ok(tb_peer_scatter_copy(p.Table(), src0.data_ptr(), src1.data_ptr(),
+                                          reinterpret_cast<const TbCopySeg*>(segs.data_ptr<int64_t>()),
+                                          static_cast<int>(segs.size(0)), total_vecs, dst_base, p.DoneCounter(),
+                                          p.ErrorWord(), cur_stream(p.device())),
+                     "peer_scatter_copy");
+           },
+           py::arg("src0"), py::arg("src1"), py::arg("segs"), py::arg("total_vecs"), py::arg("dst_base") = 0)
       .def("payload_ptrs",
            [](const PeerMemory& p) {
              const TbPeerTable t = p.Table();

@@ -384,6 +384,62 @@ void register_kernel_ops(py::module_& m) {
                                  stream_of(x)),
             "dense_k8_fwd");
   }, py::arg("x"), py::arg("W"), py::arg("bias"), py::arg("y"), py::arg("tanh") = true, py::arg("rows") = 0);
+  m.def("ppo_head_parts", [](int H, int A) { return tb_ppo_head_default_parts(H, A); });
+  m.def("ppo_head_part_numel", [](int H, int A, int parts) { return static_cast<int64_t>(tb_ppo_head_part_numel(H, A, parts)); });
+  // fused output layer + clipped PPO loss + output-layer backward (see ppo_head.cu)
+  m.def("ppo_head", [](at::Tensor h2, at::Tensor W3, at::Tensor b3, int crow, int A, at::Tensor act, at::Tensor old_logp,
+                       at::Tensor adv, at::Tensor ret, at::Tensor dz, at::Tensor g_w3, at::Tensor g_b3, at::Tensor g_b2,
+                       py::object stats, at::Tensor part, int parts, float clip, float vf_coef, float ent_coef) {
+    for (auto* t : {&h2, &W3, &dz})
+      TB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1,
+               "ppo_head: h2, W3, dz must be bf16 2-D CUDA tensors with a contiguous last dim");
+    const int64_t M = h2.size(0), N = h2.size(1);
+    TB_CHECK(N % 2 == 0 && dz.size(0) == M && dz.size(1) == N && W3.size(1) == N && W3.size(0) > crow,
+             "ppo_head: h2/dz [M, 2H], W3 [> crow, 2H]");
+    for (auto* t : {&b3, &g_w3, &g_b3, &g_b2, &old_logp, &adv, &ret, &part}) need(*t, at::kFloat, "ppo_head fp32 operand");
+    need(act, at::kInt, "act");
+    TB_CHECK(g_w3.dim() == 2 && g_w3.size(1) == N && g_w3.size(0) > crow && g_w3.stride(1) == 1 && g_b2.numel() == N &&
+                 g_b3.numel() > crow && b3.numel() > crow && act.numel() >= M && old_logp.numel() >= M &&
+                 adv.numel() >= M && ret.numel() >= M,
+             "ppo_head: gradient / input shapes");
+    TB_CHECK(part.numel() >= tb_ppo_head_part_numel(static_cast<int>(N / 2), A, parts), "ppo_head: part too small");
+    float* sp = nullptr;
+    if (!stats.is_none()) {
+      at::Tensor st = stats.cast<at::Tensor>();
+      need(st, at::kFloat, "stats");
+      TB_CHECK(st.numel() >= 6, "ppo_head: stats [>= 6]");
+      sp = st.data_ptr<float>();
+    }
+    TbPpoHeadArgs a{};
+    a.H2 = h2.data_ptr();
+    a.ldh = h2.stride(0);
+    a.W3 = W3.data_ptr();
+    a.ldw = W3.stride(0);
+    a.b3 = b3.data_ptr<float>();
+    a.crow = crow;
+    a.act = act.data_ptr<int>();
+    a.old_logp = old_logp.data_ptr<float>();
+    a.adv = adv.data_ptr<float>();
+    a.ret = ret.data_ptr<float>();
+    a.dz = dz.data_ptr();
+    a.ldz = dz.stride(0);
+    a.g_w3 = g_w3.data_ptr<float>();
+    a.ldgw = g_w3.stride(0);
+    a.g_b3 = g_b3.data_ptr<float>();
+    a.g_b2 = g_b2.data_ptr<float>();
+    a.stats = sp;
+    a.part = part.data_ptr<float>();
+    a.parts = parts;
+    a.M = static_cast<int>(M);
+    a.H = static_cast<int>(N / 2);
+    a.A = A;
+    a.clip = clip;
+    a.vf_coef = vf_coef;
+    a.ent_coef = ent_coef;
+    cuda_ok(tb_ppo_head(&a, stream_of(h2)), "ppo_head");
+  }, py::arg("h2"), py::arg("W3"), py::arg("b3"), py::arg("crow"), py::arg("A"), py::arg("act"), py::arg("old_logp"),
+     py::arg("adv"), py::arg("ret"), py::arg("dz"), py::arg("g_w3"), py::arg("g_b3"), py::arg("g_b2"),
+     py::arg("stats"), py::arg("part"), py::arg("parts"), py::arg("clip"), py::arg("vf_coef"), py::arg("ent_coef"));
   m.def("skinny8_scratch_numel", [](int N) { return static_cast<int64_t>(tb_skinny8_scratch_floats(N)); });
   // out (fp32, contiguous) = A^T X for 8-wide X blocks (+= with accumulate); scratch fp32 per-CTA partials
   m.def("skinny8_wgrad", [](at::Tensor A, at::Tensor X, at::Tensor out, int xblock, int64_t os_j, int64_t os_k,

@@ -5,6 +5,10 @@
 //   tb_peer_allreduce       sum (or mean) of a buffer across ranks: rank r
 //                           reduces slice r by reading it from every peer and
 //                           writes the result into every peer's output.
+//   tb_peer_scatter_copy    all-gather with a layout change: every rank writes
+//                           row segments of its buffers into every rank's
+//                           payload (the trainer -> rollout weight sync of a
+//                           tensor-parallel trainer into full-model copies).
 //   tb_peer_allreduce_adam  the data-parallel optimizer step in one kernel:
 //                           reduce-scatter of the fp32 gradient (peer loads),
 //                           Adam on the owned shard (ZeRO-1: the Adam moments
@@ -256,6 +260,68 @@ __global__ void __launch_bounds__(kBlock) allreduce_adam_kernel(TbPeerTable t, l
   publish_and_finish(t, epoch, done_ctr, err);
 }
 
+// Scatter all-gather with a layout change (the trainer -> rollout weight sync
+// of a tensor-parallel trainer with a full-model rollout copy on every rank).
+// Segment k copies `rows` rows of `row_bytes` from this rank's source buffer
+// (src[sel] + src_off, row stride src_ld) into the payload of every rank
+// (peers != 0) or of this rank only (peers == 0, e.g. replicated tensors that
+// every rank holds already), at dst_off with row stride dst_ld.  Work is
+// flattened over the 16-byte vectors of all segments (vec_begin: exclusive
+// prefix over the segments); a thread finds its segment by binary search and
+// issues one local load and one store per destination rank, 4 vectors in
+// flight.  The begin/finish handshakes are those of the other collectives
+// here: no rank writes into a peer's copy before that peer has entered the
+// call (its previous readers of the copy are done, by stream order), and no
+// rank leaves before every peer's writes into its copy are complete.
+__global__ void __launch_bounds__(kBlock) scatter_copy_kernel(TbPeerTable t, const char* __restrict__ src0,
+                                                              const char* __restrict__ src1,
+                                                              const TbCopySeg* __restrict__ segs, int nseg,
+                                                              long long total_vecs, long long dst_base,
+                                                              unsigned* done_ctr, int* err) {
+  bool ok;
+  const unsigned epoch = begin_call(t, err, &ok);
+  if (ok) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    constexpr int kU = 4;
+    for (long long v0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v0 < total_vecs;
+         v0 += stride * kU) {
+      uint4 val[kU];
+      long long dst[kU];
+      int all[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long long v = v0 + u * stride;
+        dst[u] = -1;
+        if (v >= total_vecs) continue;
+        int lo = 0, hi = nseg - 1;  // last segment with vec_begin <= v
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (segs[mid].vec_begin <= v) lo = mid;
+          else hi = mid - 1;
+        }
+        const TbCopySeg& g = segs[lo];
+        const long long vpr = g.row_bytes >> 4;
+        const long long e = v - g.vec_begin, row = e / vpr, col = e - row * vpr;
+        const char* sp = (g.src_sel ? src1 : src0) + g.src_off + row * g.src_ld + col * 16;
+        val[u] = *reinterpret_cast<const uint4*>(sp);
+        dst[u] = dst_base + g.dst_off + row * g.dst_ld + col * 16;
+        all[u] = g.peers;
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (dst[u] < 0) continue;
+        if (all[u]) {
+          for (int p = 0; p < t.world; ++p)
+            *reinterpret_cast<uint4*>(static_cast<char*>(t.base[p]) + dst[u]) = val[u];
+        } else {
+          *reinterpret_cast<uint4*>(static_cast<char*>(t.base[t.rank]) + dst[u]) = val[u];
+        }
+      }
+    }
+  }
+  publish_and_finish(t, epoch, done_ctr, err);
+}
+
 int grid_for(long long n, int world) {
   const long long per = (n / 4 + world) / world;
   long long g = (per + kBlock - 1) / kBlock;
@@ -298,6 +364,20 @@ int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_of
     return static_cast<int>(cudaErrorInvalidValue);
   allreduce_adam_kernel<<<grid_for(n, t.world), kBlock, 0, s>>>(t, grad_off, param_off, shadow_off, n, m, v, hp,
                                                                 step_ptr, done_ctr, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_peer_scatter_copy(TbPeerTable t, const void* src0, const void* src1, const TbCopySeg* segs, int nseg,
+                         long long total_vecs, long long dst_base, unsigned* done_ctr, int* err, cudaStream_t s) {
+  if (t.world < 1 || t.world > TB_MAX_PEERS || nseg <= 0 || total_vecs < 0 || (dst_base & 15) ||
+      (reinterpret_cast<uintptr_t>(src0) & 15) || (reinterpret_cast<uintptr_t>(src1) & 15))
+    return static_cast<int>(cudaErrorInvalidValue);
+  long long g = (total_vecs + kBlock * 4 - 1) / (kBlock * 4);
+  if (g > 4 * 148) g = 4 * 148;
+  if (g < 1) g = 1;
+  scatter_copy_kernel<<<static_cast<int>(g), kBlock, 0, s>>>(t, static_cast<const char*>(src0),
+                                                              static_cast<const char*>(src1), segs, nseg, total_vecs,
+                                                              dst_base, done_ctr, err);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -194,6 +194,40 @@ typedef struct {
 } TbGemmArgs;
 
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
+// PPO output layer + clipped loss + output-layer backward in one pass over the
+// hidden activations H2 = [H2a | H2c] (bf16 [M, 2H]); categorical actor with A
+// actions.  W3 bf16 [>= crow + 1, 2H] (actor rows 0..A-1 over columns [0, H),
+// the critic row `crow` over [H, 2H)), b3 fp32.  Writes dZ2 (bf16 [M, 2H]),
+// the gradients of b2, W3 (actor rows and the critic row) and b3 (written, not
+// accumulated), and adds [pg, v, entropy, kl, clipfrac, rows] into stats.
+// part: scratch of tb_ppo_head_part_numel(H, A, parts) floats.
+typedef struct {
+  const void* H2;
+  long long ldh;
+  const void* W3;
+  long long ldw;
+  const float* b3;
+  int crow;
+  const int* act;
+  const float* old_logp;
+  const float* adv;
+  const float* ret;
+  void* dz;
+  long long ldz;
+  float* g_w3;
+  long long ldgw;
+  float* g_b3;
+  float* g_b2;
+  float* stats;
+  float* part;
+  int parts;  // CTAs (each writes one partial row)
+  int M, H, A;
+  float clip, vf_coef, ent_coef;
+} TbPpoHeadArgs;
+int tb_ppo_head(const TbPpoHeadArgs* args, cudaStream_t s);
+long long tb_ppo_head_part_numel(int H, int A, int parts);
+int tb_ppo_head_default_parts(int H, int A);  // CTAs for one resident wave on this device
+
 size_t tb_gemm_workspace_bytes(int M, int N, int K);
 
 // ---------------- transformer ops ----------------
@@ -275,6 +309,21 @@ typedef struct {
 } TbPeerTable;
 
 size_t tb_peer_header_bytes(void);
+// One row-segment copy of tb_peer_scatter_copy (all sizes and offsets in bytes,
+// multiples of 16).
+typedef struct {
+  long long vec_begin;  // first 16-byte vector of this segment in the flattened work (exclusive prefix)
+  long long src_off, src_ld;
+  long long dst_off, dst_ld;  // relative to dst_base in every rank's payload
+  long long rows, row_bytes;
+  int src_sel;  // 0: src0, 1: src1
+  int peers;    // 1: write into every rank, 0: this rank only
+} TbCopySeg;
+// Every rank copies its segments (segs: device array, sorted by vec_begin) from
+// its local src0 / src1 into the payloads of all ranks (or only its own),
+// between the begin / finish handshakes of the peer collectives.
+int tb_peer_scatter_copy(TbPeerTable t, const void* src0, const void* src1, const TbCopySeg* segs, int nseg,
+                         long long total_vecs, long long dst_base, unsigned* done_ctr, int* err, cudaStream_t s);
 // The peer collectives' bounded flag wait, alone: waits up to budget_ns for
 // flags[0..n) >= expect, then sets *err = 99 (site code) and returns.
 int tb_bounded_wait_probe(const unsigned* flags, int n, unsigned expect, unsigned long long budget_ns, int* err,

@@ -79,6 +79,16 @@ def main():
         err = (a - b).abs().max().item() / (b.abs().max().item() + 1e-12)
         worst = max(worst, err)
     assert worst < 1e-4, ("pipeline gradients", worst)
+    # ---- 1b. activation recompute: the same gradients
+    ref_g = st.model.grad.clone()
+    st.zero_grad()
+    pp.run_1f1b(st, list(range(world)), M, mb * T,
+                lambda i: st.model.embed(ids[i * mb:(i + 1) * mb]),
+                lambda i, x: head_loss_grad(st.model, x, ids[i * mb:(i + 1) * mb]),
+                lambda i, dx: st.model.embed_backward(ids[i * mb:(i + 1) * mb], dx), recompute=True)
+    torch.cuda.synchronize()
+    rel = (st.model.grad - ref_g).abs().max().item() / (ref_g.abs().max().item() + 1e-12)
+    assert rel < 1e-5, ("recompute gradients", rel)
     # ---- 2. PPO-RLHF through the pipeline
     rcfg = RLHFConfig(model=LMConfig.tiny(n_layers=4), num_prompts=8, prompt_len=32, response_len=32,
                       micro_batch=2, lr=1e-4)

@@ -132,3 +132,50 @@ def test_mlp_head_fwd(H, dev):
     o.mlp_head_fwd(h, W, b, H, out)
     exp = torch.cat([h.float()[:, :H] @ W.float()[:8, :H].t(), h.float()[:, H:] @ W.float()[8:, H:].t()], 1) + b
     assert torch.allclose(out, exp, atol=2e-3, rtol=1e-3), (out - exp).abs().max()
+
+
+@pytest.mark.parametrize("H,B", [(256, 3000), (128, 4099)])
+def test_fused_ppo_head_matches_autograd(H, B, dev):
+    """Hidden layers + the one-pass output layer / clipped PPO loss / output-layer
+    backward (ppo_head.cu) + the hidden backward, against fp32 autograd of the
+    same actor-critic and the reference loss expression: every parameter's
+    gradient and the loss statistics."""
+    from turbol_b200.ops import reference as refops
+
+    net = FusedActorCritic(4, 2, (H, H), device=dev, seed=5)
+    ref = ActorCritic(4, 2, (H, H), discrete=True, device="cpu", seed=5)
+    g = torch.Generator().manual_seed(B + H)
+    obs = torch.randn(B, 4, generator=g) * 0.5
+    x = torch.zeros(B, 8, device=dev, dtype=torch.bfloat16)
+    ops().pad_obs_bf16(obs.to(dev).contiguous(), x)
+    xo = x[:, :4].float().cpu().requires_grad_()
+    rl, rv = ref(xo)
+    act = torch.randint(0, 2, (B,), generator=g, dtype=torch.int32)
+    # behaviour log-probs near the current ones: some ratios fall outside the clip range
+    old = (torch.log_softmax(rl.detach(), -1).gather(1, act.long()[:, None])[:, 0]
+           + 0.3 * torch.randn(B, generator=g))
+    adv = torch.randn(B, generator=g)
+    ret = torch.randn(B, generator=g)
+    loss, st_ref = refops.ppo_categorical_loss(rl, rv, act, old, adv, ret, 0.2, 0.5, 0.01)
+    loss.backward()
+    ws = net.workspace(B)
+    stats = torch.zeros(8, device=dev)
+    net.grad.fill_(0.0)
+    net.forward_hidden(x, ws)
+    net.loss_backward(x, ws, act.to(dev), old.to(dev), adv.to(dev), ret.to(dev), stats, 0.2, 0.5, 0.01)
+    torch.cuda.synchronize()
+    ga = [net.g["w1"][:H, :4], net.g["b1"][:H], net.g["w2a"], net.g["b2a"], net.g["w3a"][:2], net.g["b3a"][:2]]
+    gc = [net.g["w1"][H:, :4], net.g["b1"][H:], net.g["w2c"], net.g["b2c"], net.g["w3c"][:1], net.g["b3c"][:1]]
+    for got, p in zip(ga + gc, ref.actor_params + ref.critic_params):
+        exp = p.grad
+        scale = float(exp.abs().max()) + 1e-8
+        err = float((got.cpu() - exp).abs().max()) / scale
+        assert err < 5e-2, (p.shape, err)
+    # gradients of the padding and of the off-diagonal blocks stay zero
+    assert float(net.g["w3a"][2:].abs().max()) == 0.0 and float(net.g["w3c"][1:].abs().max()) == 0.0
+    assert float(net.g["w3"][:8, H:].abs().max()) == 0.0 and float(net.g["w3"][8:, :H].abs().max()) == 0.0
+    # statistics: [pg, v, entropy, kl, clipfrac] sums and the row count
+    st = stats.cpu()
+    assert st[5].item() == B
+    for k in range(5):
+        assert abs(st[k].item() - st_ref[k].item()) <= 2e-2 * max(1.0, abs(st_ref[k].item())), (k, st, st_ref)

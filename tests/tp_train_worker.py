@@ -5,9 +5,13 @@
    hand-written backward: outputs and input gradients on each rank's rows,
    the sharded weight gradients against the matching slices of the full
    gradients, the replicated ones (norms, embedding) after the TP all-reduce.
-2. GRPO with tensor-parallel training (tp=2, tp_mode="train") runs two steps:
-   finite statistics, replicated weights stay identical on both ranks, the
-   shards move."""
+2. The fused trainer -> rollout weight sync (TPReplicaSync): every rank's
+   full-model replica equals the source model, and after the shards move it
+   equals the un-sharded shards of both ranks (bit for bit).
+3. GRPO with tensor-parallel training (tp=2, tp_mode="train") runs two steps
+   with the full-replica rollout and with the TP rollout: finite statistics,
+   replicated weights stay identical on both ranks, the shards move, and the
+   replica follows the trainer."""
 import datetime
 import os
 import sys
@@ -78,23 +82,67 @@ def main():
         errs["embed"] = rel(tpm.g["embed"], full.g["embed"])
         bad = {k: v for k, v in errs.items() if not v < 3e-2}
         assert not bad, ("tp train", rep, bad)
-    # ---- GRPO with tensor-parallel training
+    # ---- fused trainer -> rollout weight sync: the full replica on every rank
+    from turbol_b200.parallel.weight_sync import TPReplicaSync
+
+    sync = TPReplicaSync(tpm)
+    sync()
+    torch.cuda.synchronize()
+    sync.check()
+    for name in full.offsets:
+        assert torch.equal(sync.full.s[name], full.s[name]), ("replica bf16", name)
+    for name, t in sync.full.f32.items():
+        assert torch.equal(t, full.p[name]), ("replica fp32", name)
+    with torch.no_grad():  # move the shards (rank-dependent), sync, compare with the un-sharded shards
+        tpm.flat.add_(torch.randn(tpm.numel, generator=torch.Generator(device=dev).manual_seed(7 + rank),
+                                  device=dev) * 1e-2)
+        rep = tpm.flat[: tpm.rep_numel].clone()
+        dist.broadcast(rep, src=0)  # replicated tensors stay identical across the group
+        tpm.flat[: tpm.rep_numel].copy_(rep)
+        tpm.shadow.copy_(tpm.flat)
+    sync()
+    torch.cuda.synchronize()
+    sync.check()
+    flats = [torch.empty_like(tpm.flat) for _ in range(world)]
+    dist.all_gather(flats, tpm.flat)
+    want = DecoderLM(cfg, dev, seed=3)
+    for t, f in enumerate(flats):
+        TPTrainLM.unshard_into(want, f, tpm.offsets, world, t, shards_only=t > 0)
+    want.sync_shadow()
+    for name in full.offsets:
+        assert torch.equal(sync.full.s[name], want.s[name]), ("replica after sync", name)
+    for name, t in sync.full.f32.items():
+        assert torch.equal(t, want.p[name]), ("replica fp32 after sync", name)
+    # ---- GRPO with tensor-parallel training: full-replica rollout (default) and TP rollout
     # (the TP decode step needs a multiple of 128 sequences per rank)
     gcfg = GRPOConfig(model=cfg, num_prompts=32, group_size=8, prompt_len=64, response_len=64, micro_batch=8,
                       lr=1e-3)
-    tr = GRPOTrainer(gcfg, str(dev), dp="fused", tp=2, tp_mode="train")
-    before = tr.model.flat.clone()
-    for _ in range(2):
-        st = tr.step()
-        assert all(v == v for v in st.values() if isinstance(v, float)), st
-    torch.cuda.synchronize()
-    tr.comm.check()
-    moved = (tr.model.flat - before).abs().max().item()
-    assert moved > 0, "weights did not move"
-    rep_sum = tr.model.flat[: tr.model.rep_numel].double().sum().reshape(1)
-    sums = [torch.zeros_like(rep_sum) for _ in range(world)]
-    dist.all_gather(sums, rep_sum)
-    assert float(sums[0]) == float(sums[1]), ("replicated weights diverged", [float(s) for s in sums])
+    for mode in ("replica", "tp"):
+        tr = GRPOTrainer(gcfg, str(dev), dp="fused", tp=2, tp_mode="train", rollout=mode)
+        before = tr.model.flat.clone()
+        for _ in range(2):
+            st = tr.step()
+            assert all(v == v for v in st.values() if isinstance(v, float)), (mode, st)
+        torch.cuda.synchronize()
+        tr.comm.check()
+        if tr.sync is not None:
+            tr.sync.check()
+            # the replica holds the trainer's latest weights
+            flats = [torch.empty_like(tr.model.flat) for _ in range(world)]
+            dist.all_gather(flats, tr.model.flat)
+            chk = DecoderLM(cfg, dev, seed=3)
+            for t, f in enumerate(flats):
+                TPTrainLM.unshard_into(chk, f, tr.model.offsets, world, t, shards_only=t > 0)
+            chk.sync_shadow()
+            for name in chk.offsets:
+                assert torch.equal(tr.sync.full.s[name], chk.s[name]), ("GRPO replica", name)
+        moved = (tr.model.flat - before).abs().max().item()
+        assert moved > 0, "weights did not move"
+        rep_sum = tr.model.flat[: tr.model.rep_numel].double().sum().reshape(1)
+        sums = [torch.zeros_like(rep_sum) for _ in range(world)]
+        dist.all_gather(sums, rep_sum)
+        assert float(sums[0]) == float(sums[1]), ("replicated weights diverged", [float(s) for s in sums])
+        del tr
     if rank == 0:
         print("TP_TRAIN_WORKER_OK", {k: round(v, 5) for k, v in errs.items()}, st["kl"], moved)
     dist.barrier()

@@ -14,6 +14,9 @@ epilogues:
                                             blocks only (kgroup: each output tile
                                             iterates over its head's K range)
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
+  training  with 2 actions and H in {128, 256}: output layer + clipped PPO loss +
+            dZ2, dW3, db3, db2 in ONE CUDA-core pass over H2 (ppo_head.cu:
+            :meth:`forward_hidden` + :meth:`loss_backward`), then dW2, dZ1, dW1
   backward  dZ2 = (dOut W3) * (1 - H2^2)    one CUDA-core pass (8 outputs per head) + db2 column sums
             dW3 = dOut^T H2                 one CUDA-core pass (8 rows per head, 18.6 vs 36.8 us as GEMMs)
             dZ1 = (dZ2 W2) * (1 - H1^2)     one GEMM (diagonal blocks only) + tanh-backward
@@ -50,6 +53,8 @@ class FusedActorCritic:
             raise ValueError("hidden must be a multiple of 64, obs_dim and act_dim at most 8")
         self.obs_dim, self.act_dim, self.H = obs_dim, act_dim, H
         self.device = torch.device(device)
+        # the one-pass output layer + loss + output-layer backward (ppo_head.cu)
+        self.fused_head = act_dim == 2 and H in (128, 256)
         # parameter layout in the flat buffer; every offset 64-element aligned
         shapes = [("w1", (2 * H, PAD)), ("b1", (2 * H,)), ("w2", (2 * H, 2 * H)), ("b2", (2 * H,)),
                   ("w3", (2 * PAD, 2 * H)), ("b3", (2 * PAD,))]
@@ -160,6 +165,9 @@ class FusedActorCritic:
             ws["splitk"] = torch.zeros(n, **f32)
             # per-CTA partial sums of the 8-wide CUDA-core passes
             ws["parts"] = torch.empty(o.skinny8_scratch_numel(min(2 * H, 512)), **f32)
+            if self.fused_head:
+                ws["head_parts"] = o.ppo_head_parts(H, self.act_dim)
+                ws["head_part"] = torch.empty(o.ppo_head_part_numel(H, self.act_dim, ws["head_parts"]), **f32)
             self._ws[B] = ws
         return ws
 
@@ -177,6 +185,38 @@ class FusedActorCritic:
         # (the CUDA-core mlp_head_fwd measured slower here: 26.7 vs 16.5 us at 32,768 rows)
         o.gemm(ws["h2"], S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)        # logits | value
         return ws["logits"], ws["value"]
+
+    def forward_hidden(self, x_bf16: torch.Tensor, ws):
+        """The two hidden layers only: ws['h1'], ws['h2'] (the input of :meth:`loss_backward`)."""
+        o = _ops()
+        S, P = self.s, self.p
+        o.dense_k8_fwd(x_bf16, S["w1"], P["b1"], ws["h1"], True)
+        o.gemm(ws["h1"], S["w2"], ws["h2"], bias=P["b2"], epi=o.EPI_BIAS_TANH, bn=128, kgroup=self.H)
+
+    def loss_backward(self, x_bf16: torch.Tensor, ws, act, old_logp, adv, ret, stats, clip: float, vf_coef: float,
+                      ent_coef: float):
+        """Output layer, clipped PPO loss and the whole backward after
+        :meth:`forward_hidden`: one pass over H2 computes the logits and values,
+        the loss (statistics added into ``stats``), dZ2 and the gradients of W3,
+        b3 and b2 (ppo_head.cu); then the GEMMs for dW2, dZ1 (+ db1) and dW1."""
+        o = _ops()
+        S, G, P = self.s, self.g, self.p
+        o.ppo_head(ws["h2"], S["w3"], P["b3"], PAD, self.act_dim, act, old_logp, adv, ret, ws["dz2"], G["w3"], G["b3"],
+                   G["b2"], stats, ws["head_part"], ws["head_parts"], clip, vf_coef, ent_coef)
+        self._hidden_backward(x_bf16, ws)
+
+    def _hidden_backward(self, x_bf16: torch.Tensor, ws):
+        """dW2 (per head), dZ1 + db1 and dW1 from ws['dz2']."""
+        o = _ops()
+        S, G = self.s, self.g
+        H = self.H
+        h1, dz2, dz1, wsk = ws["h1"], ws["dz2"], ws["dz1"], ws["splitk"]
+        # dW2 block = dZ2^T H1 (128-wide tiles, 32 K splits: 35.1 vs 42.9 us for both heads at 32,768 rows)
+        for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
+            o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk, bn=128, split_k=32)
+        o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"],   # dZ1, db1
+               kgroup=self.H)                                                    # (diagonal blocks of W2 only)
+        o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
 
     def backward(self, x_bf16: torch.Tensor, ws, out_bias_grads_done: bool = False):
         """Weight gradients into self.grad from ws['dout'] = (d logits | d value)
@@ -205,9 +245,4 @@ class FusedActorCritic:
             o.mlp_head_dz(dout, h2, S["w3"], H, dz2, G["b2"], False, ws["parts"])
         else:
             o.gemm(dout, S["w3"], dz2, False, True, aux=h2, epi=o.EPI_TANH_BWD, colsum=G["b2"])
-        # dW2 block = dZ2^T H1 (128-wide tiles, 32 K splits: 35.1 vs 42.9 us for both heads at 32,768 rows)
-        for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
-            o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk, bn=128, split_k=32)
-        o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"],   # dZ1, db1
-               kgroup=self.H)                                                    # (diagonal blocks of W2 only)
-        o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
+        self._hidden_backward(x_bf16, ws)

@@ -44,13 +44,16 @@ class PipelineStage:
     VH_ROWS = 8  # the value head is a [1, H] linear layer stored as 8 rows (tile-friendly); row 0 is used
 
     def __init__(self, cfg: LMConfig, stage: int, num_stages: int, device, seed: int = 0, value_head: bool = False,
-                 lr: float = 1e-5, betas=(0.9, 0.95), tp_comm=None):
+                 lr: float = 1e-5, betas=(0.9, 0.95), tp_comm=None, recompute: bool = False):
         """tp_comm: a :class:`TensorParallelComm` over this stage's
         tensor-parallel group; the stage then holds this rank's shard of its
         layers (:class:`TPTrainLM`) and its micro-batch rows are split over the
         group (each rank exchanges its rows with the same TP rank of the
-        neighbouring stages)."""
+        neighbouring stages).  recompute: activation recomputation in
+        :func:`run_1f1b` (keep stage inputs only, re-run the forward before
+        each backward)."""
         self.cfg, self.stage, self.num_stages = cfg, stage, num_stages
+        self.recompute = recompute
         self.first, self.last = stage == 0, stage == num_stages - 1
         self.device = torch.device(device)
         self.tp_comm = tp_comm
@@ -153,9 +156,19 @@ class _P2P:
 
 def run_1f1b(stage: PipelineStage, ranks: Sequence[int], num_micro: int, micro_rows: int,
              forward_first: Callable[[int], torch.Tensor], loss_last: Callable[[int, torch.Tensor], torch.Tensor],
-             backward_first: Callable[[int, torch.Tensor], None], group=None, forward_only: bool = False):
+             backward_first: Callable[[int, torch.Tensor], None], group=None, forward_only: bool = False,
+             recompute: Optional[bool] = None):
     """One pipeline pass over ``num_micro`` micro-batches of ``micro_rows``
     hidden rows each.
+
+    recompute (default ``stage.recompute``): activation recomputation.  The
+    forward keeps only each micro-batch's stage input; its backward first
+    re-runs the stage forward from that input to rebuild the saved
+    activations, then runs the backward.  A stage then holds one [rows, H]
+    input per micro-batch in flight instead of every layer's activations, for
+    one extra forward per micro-batch (the reference's
+    ``PipelineConfig::activation_checkpointing``,
+    turbol_vllm/include/turbol/distributed/pipeline_trainer.hpp:47).
 
     forward_first(i) -> x: the first stage's input rows of micro-batch i
     (the embedding).  loss_last(i, x_out) -> dx_out: on the last stage,
@@ -174,14 +187,22 @@ def run_1f1b(stage: PipelineStage, ranks: Sequence[int], num_micro: int, micro_r
     def new():
         return torch.empty(shape, device=dev, dtype=torch.bfloat16)
 
+    if recompute is None:
+        recompute = getattr(stage, "recompute", False)
+
     def fwd(i, x_in):
+        # with recompute the forward still saves (the same code path as the
+        # recomputation, so the output sent on equals the rebuilt one) and drops
+        # the activations at once: one micro-batch's worth exists at a time
         x_out, sv = stage_forward(stage, i, x_in, save=not forward_only)
         if not forward_only:
-            saved[i] = (x_in, sv)
+            saved[i] = (x_in, None if recompute else sv)
         return x_out
 
     def bwd(i, dx_out):
         x_in, sv = saved.pop(i)
+        if sv is None:  # recompute: rebuild this micro-batch's activations from its input
+            _, sv = stage_forward(stage, i, x_in, save=True)
         return stage_backward(stage, i, dx_out, sv)
 
     if forward_only:

@@ -84,8 +84,18 @@ class GRPOTrainer:
       rank re-slices its rollout shard from the updated weights."""
 
     def __init__(self, cfg: GRPOConfig, device="cuda:0", optimizer=None, dp: str = "none", group=None,
-                 tp: int = 1, tp_mode: str = "train"):
+                 tp: int = 1, tp_mode: str = "train", rollout: str = "replica"):
+        """rollout (tp_mode "train"): "replica" - each rank decodes its share of
+        the group's sequences on a full bf16 copy of the model that a fused
+        all-gather kernel refreshes after every optimizer step
+        (:class:`~turbol_b200.parallel.weight_sync.TPReplicaSync`); "tp" - the
+        tensor-parallel decode on the trainer's own shards (no copy, two fused
+        collectives per layer per token)."""
         self.cfg = cfg
+        self.rollout_mode = rollout if tp > 1 and tp_mode == "train" else "local"
+        if self.rollout_mode not in ("replica", "tp", "local"):
+            raise ValueError(f"unknown rollout mode {rollout!r}")
+        self.sync = None
         self.device = torch.device(device)
         self.dp, self.group = dp, group
         self.rank, self.world = 0, 1
@@ -191,7 +201,16 @@ class GRPOTrainer:
                 self.grad_sync = NcclGradSync(mesh.dp_group)
         self.ref = self.model.frozen_copy()
         self.tpm = self.model
-        self.gen = TPLLMGenerator(self.model, cfg.batch, cfg.seq_len, seed=cfg.seed + 17 + 7919 * self.group_index)
+        if self.rollout_mode == "replica":
+            from ..parallel.weight_sync import TPReplicaSync
+
+            self.sync = TPReplicaSync(self.model, mesh.tp_group)
+            self.sync()
+            self.gen = LLMGenerator(self.sync.full, cfg.batch // tp, cfg.seq_len,
+                                    seed=cfg.seed + 17 + 7919 * self.group_index + 104729 * self.tp_rank)
+        else:
+            self.gen = TPLLMGenerator(self.model, cfg.batch, cfg.seq_len,
+                                      seed=cfg.seed + 17 + 7919 * self.group_index)
         self.stats = torch.zeros(4, device=self.device)
         self.step_count = 0
         self.last_times = {}
@@ -224,10 +243,29 @@ class GRPOTrainer:
             self.opt.load_state_dict(sd["optim"])
             if self.tp_mode == "rollout":
                 self.tpm.load_from(self.model)  # the rollout shard follows the loaded weights
+            elif self.sync is not None:
+                self.sync()  # and the rollout replicas
         self.step_count = int(sd["step_count"])
         self.gen.calls = int(sd["gen_calls"])
 
     # ------------------------------------------------------------------ helpers
+    def _replica_rollout(self):
+        """Rank r of the TP group decodes prompts [r P/tp, (r+1) P/tp) (x G
+        samples) on its replica; the group then shares all sequences (in
+        prompt order) for the tensor-parallel update."""
+        import torch.distributed as dist
+
+        cfg, tp, r = self.cfg, self.tp, self.tp_rank
+        P = cfg.num_prompts // tp
+        prompts = self._prompts()[r * P:(r + 1) * P].contiguous()
+        seqs, lp = self.gen.generate(prompts, cfg.group_size, cfg.response_len, cfg.temperature)
+        g = self.mesh.tp_group
+        all_seqs = torch.empty((tp,) + tuple(seqs.shape), device=self.device, dtype=seqs.dtype)
+        all_lp = torch.empty((tp,) + tuple(lp.shape), device=self.device, dtype=lp.dtype)
+        dist.all_gather_into_tensor(all_seqs, seqs.contiguous(), group=g)
+        dist.all_gather_into_tensor(all_lp, lp.contiguous(), group=g)
+        return all_seqs.view(-1, seqs.shape[1]), all_lp.view(-1, lp.shape[1])
+
     def _prompts(self) -> torch.Tensor:
         g = torch.Generator(device=self.device).manual_seed(self.cfg.seed * 1000003 + self.step_count +
                                                             104729 * self.group_index)
@@ -269,7 +307,10 @@ class GRPOTrainer:
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
         # 1. rollout
-        seqs, roll_lp = self.gen.generate(self._prompts(), cfg.group_size, cfg.response_len, cfg.temperature)
+        if self.rollout_mode == "replica":
+            seqs, roll_lp = self._replica_rollout()
+        else:
+            seqs, roll_lp = self.gen.generate(self._prompts(), cfg.group_size, cfg.response_len, cfg.temperature)
         torch.cuda.synchronize(dev)
         t1 = time.perf_counter()
         # 2. rewards and group-normalized advantages
@@ -308,7 +349,9 @@ class GRPOTrainer:
             self.opt.step()  # the fused data-parallel step averages over ranks itself
         if self.tp_mode == "rollout":
             self.tpm.load_from(self.model)  # trainer -> rollout weight sync
-        # (tp_mode "train": the rollout reads the weights the optimizer just wrote)
+        elif self.sync is not None:
+            self.sync()  # fused all-gather of the new shards into every rank's rollout replica
+        # (rollout "tp": the rollout reads the weights the optimizer just wrote)
         torch.cuda.synchronize(dev)
         t3 = time.perf_counter()
         self.step_count += 1

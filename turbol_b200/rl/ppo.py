@@ -10,10 +10,11 @@ GPU path (everything stays on the device, no host round trip per step):
                  the transition at row t, step CartPole with auto-reset;
   advantages     one GAE kernel that also accumulates the advantage moments;
   minibatch      gather through an on-device Feistel permutation (fused with
-                 advantage normalization) -> forward -> fused PPO loss
-                 forward+backward kernel -> autograd backward into one flat
-                 gradient buffer -> [data-parallel gradient reduction] -> one
-                 fused Adam launch.
+                 advantage normalization) -> hidden layers -> one kernel for
+                 the output layer, the clipped loss and the output-layer
+                 backward -> weight-gradient GEMMs into one flat gradient
+                 buffer -> [data-parallel gradient reduction] -> one fused
+                 Adam launch.
 The rollout, the advantage pass and one minibatch step are each captured as a
 CUDA graph; the minibatch graph is replayed epochs * n_minibatches times and
 reads its (epoch, minibatch) position from a device counter.
@@ -211,6 +212,11 @@ class PPOTrainer:
                          self._empty_f32, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, None,
                          cfg.n_minibatches, self.mb_step_t, self.iter_t, 0, self.policy_seed ^ 0x5851F42D,
                          cfg.norm_adv, self.mb_obs_bf16)
+            if self.net.fused_head:  # output layer + loss + output-layer backward in one pass over H2
+                self.net.forward_hidden(self.mb_obs_bf16, self.ws_mb)
+                self.net.loss_backward(self.mb_obs_bf16, self.ws_mb, self.mb_act, self.mb_logp, self.mb_adv,
+                                       self.mb_ret, self.loss_stats, cfg.clip, cfg.vf_coef, cfg.ent_coef)
+                return
             logits, v = self.net.forward(self.mb_obs_bf16, self.ws_mb)
             o.ppo_loss_padded(logits, 2, v, self.mb_act, self.mb_logp, self.mb_adv, self.mb_ret, self.ws_mb["dlog"],
                               self.ws_mb["dval"], self.loss_stats, cfg.clip, cfg.vf_coef, cfg.ent_coef,

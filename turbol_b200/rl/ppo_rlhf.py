@@ -53,6 +53,7 @@ class RLHFConfig:
     lam: float = 0.95
     temperature: float = 1.0
     seed: int = 0
+    recompute: bool = False     # activation recomputation in the pipeline stages
 
     @property
     def seq_len(self) -> int:
@@ -110,7 +111,7 @@ class PPORLHFTrainer:
             stage_idx, n_stages = self.rank, self.world
         self.n_stages = n_stages
         self.stage = pp.PipelineStage(cfg.model, stage_idx, n_stages, self.device, seed=cfg.seed, value_head=True,
-                                      lr=cfg.lr, tp_comm=comm)
+                                      lr=cfg.lr, tp_comm=comm, recompute=cfg.recompute)
         # a tied embedding lives on the first and the last stage: same initial
         # weights, and the two gradients are summed after every backward pass
         # (one group per TP rank: the first- and last-stage ranks holding it)
