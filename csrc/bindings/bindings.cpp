@@ -28,6 +28,7 @@ using namespace turbol;
 void register_kernel_ops(py::module_& ops);  // ops_bindings.cpp
 void register_llm_ops(py::module_& ops);      // llm_bindings.cpp
 void register_comm_ops(py::module_& ops);     // comm_bindings.cpp
+void register_dist(py::module_& m);           // dist_bindings.cpp
 
 namespace {
 
@@ -662,5 +663,8 @@ PYBIND11_MODULE(turbol_core, m) {
   register_kernel_ops(ops);
   register_llm_ops(ops);
   register_comm_ops(ops);
+  py::module_ dist = m.def_submodule("dist", "C++ distributed runtime: NcclCommunicator, DistributedTrainer, "
+                                               "PipelineTrainer (turbol/distributed.hpp)");
+  register_dist(dist);
 #endif
 }

@@ -1,7 +1,7 @@
 // Native C++ demo of the framework's core (the counterpart of the reference's
 // turbol_vllm/examples/main.cpp:9-59): builds the runtime, tensors, an
-// environment, a replay buffer, the reward engine, the config store and the
-// profiler from C++ only, steps the environment through its public API and
+// environment, a replay buffer, the reward engine, the config store, the
+// profiler and the distributed trainer from C++ only, steps the environment through its public API and
 // prints what it did.  Runs on CPU, or on the GPU when one is present.
 //
 //   make -C examples/cpp && ./examples/cpp/turbol_demo [cpu|cuda]
@@ -10,6 +10,7 @@
 
 #include "turbol/common.hpp"
 #include "turbol/config.hpp"
+#include "turbol/distributed.hpp"
 #include "turbol/engines.hpp"
 #include "turbol/observability.hpp"
 #include "turbol/runtime.hpp"
@@ -88,6 +89,16 @@ int main(int argc, char** argv) {
     Profiler::Guard g(&prof, "demo_span", "demo");
   }
   std::printf("   config num_envs=%lld, profiler spans=%zu\n", cfg.GetInt("num_envs", 0), prof.GetAllSpans().size());
+
+  std::printf("\n7. Distributed trainer (one process: a group of one)\n");
+  distributed::DistributedConfig dcfg;
+  distributed::DistributedTrainer dist(dcfg);
+  s = dist.Initialize();
+  if (!s.ok()) return fail("DistributedTrainer::Initialize", s);
+  s = dist.AllReduce(&t, "mean");
+  if (!s.ok()) return fail("DistributedTrainer::AllReduce", s);
+  std::printf("   rank %d of %d, all-reduce(mean) ok\n", dist.GetRank(), dist.GetWorldSize());
+  dist.Shutdown();
 
   if (want_cuda) {
     const auto mem = GetCudaMemoryInfo(0);

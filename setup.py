@@ -27,6 +27,24 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
+def nccl_dirs():
+    """Headers and library of the NCCL that torch loads (the nvidia-nccl wheel
+    next to torch), so the C++ communicators share torch's libnccl.so.2."""
+    try:
+        import nvidia.nccl  # namespace package: no __file__
+
+        base = list(nvidia.nccl.__path__)[0]
+    except ImportError:
+        return None, None
+    inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
+    if os.path.exists(os.path.join(inc, "nccl.h")) and os.path.exists(os.path.join(lib, "libnccl.so.2")):
+        return inc, lib
+    return None, None
+
+
+NCCL_INC, NCCL_LIB = nccl_dirs()
+
+
 def sources():
     pats = ["csrc/core/*.cpp", "csrc/engines/*.cpp", "csrc/bindings/*.cpp", "csrc/kernels/*.cu"]
     out = []
@@ -53,7 +71,8 @@ def cpu_sources():
     out = []
     for p in pats:
         out += sorted(glob.glob(os.path.join(ROOT, p)))
-    out = [s for s in out if os.path.basename(s) != "peer.cpp"]  # NVLink peer memory: CUDA only
+    # NVLink peer memory and the NCCL communicators: CUDA build only
+    out = [s for s in out if os.path.basename(s) not in ("peer.cpp", "distributed.cpp")]
     return [os.path.relpath(s, ROOT) for s in out]
 
 
@@ -68,14 +87,17 @@ cpu_ext = CppExtension(
 ext = cpu_ext if CPU_ONLY else CUDAExtension(
     name="turbol_b200.turbol_core",
     sources=sources(),
-    include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")],
+    include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")] + ([NCCL_INC] if NCCL_INC else []),
     extra_compile_args={"cxx": cxx_flags, "nvcc": nvcc_flags},
-    libraries=["nccl"] if os.environ.get("TURBOL_LINK_NCCL") else [],
     # Link the C++ runtime dynamically: a toolchain whose libstdc++.so link is
     # missing falls back to libstdc++.a, and a private static copy of the
     # iostream/locale machinery inside this library crashes on the first
     # number it formats (its facet ids differ from the process's libstdc++).
-    extra_link_args=["-l:libstdc++.so.6"],
+    # (an RPATH, not a RUNPATH, for NCCL's directory: a RUNPATH here would stop a
+    # native program that links this library from resolving torch's libraries
+    # through its own RPATH)
+    extra_link_args=["-l:libstdc++.so.6"] + ([f"-L{NCCL_LIB}", "-l:libnccl.so.2", "-Wl,--disable-new-dtags",
+                                              f"-Wl,-rpath,{NCCL_LIB}"] if NCCL_LIB else ["-lnccl"]),
 )
 
 setup(

@@ -19,3 +19,4 @@ def test_cpp_demo_builds_and_runs():
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     out = r.stdout
     assert "200 steps x 1024 envs" in out and "sampled 256 rows" in out and "demo finished" in out
+    assert "rank 0 of 1, all-reduce(mean) ok" in out
