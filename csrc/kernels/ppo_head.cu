@@ -140,7 +140,8 @@ __global__ void __launch_bounds__(kThreads) ppo_head_kernel(
       const float other = __shfl_xor_sync(0xffffffffu, s[k], 16);
       l[k] = (critic ? other : s[k]) + bl[k];
     }
-    const float V = (critic ? s[0] : __shfl_xor_sync(0xffffffffu, s[0], 16)) + bv;
+    const float vs = __shfl_xor_sync(0xffffffffu, s[0], 16);  // every lane takes part in the exchange
+    const float V = (critic ? s[0] : vs) + bv;
     // ---- loss (every lane, same values)
     float mx = l[0];
 #pragma unroll
