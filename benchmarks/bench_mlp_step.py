@@ -27,6 +27,9 @@ def main():
     ap.add_argument("--hidden", type=int, default=256)
     ap.add_argument("--reps", type=int, default=50)
     ap.add_argument("--no-variants", action="store_true", help="time the MLP step only (short runs for ncu)")
+    ap.add_argument("--fused-head", action="store_true",
+                    help="the PPO training step's path: hidden layers, then the one-pass output layer + clipped "
+                         "loss + output-layer backward (ppo_head.cu), then the hidden backward")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     net = FusedActorCritic(4, 2, (a.hidden, a.hidden), device=dev, seed=0)
@@ -36,7 +39,17 @@ def main():
     x[:, :4] = torch.randn(B, 4, device=dev).to(torch.bfloat16)
     dout = (torch.randn(B, 2 * PAD, device=dev) * 1e-3).to(torch.bfloat16)
 
+    act = torch.randint(0, 2, (B,), device=dev, dtype=torch.int32)
+    old = torch.full((B,), -0.69, device=dev)
+    adv = torch.randn(B, device=dev)
+    ret = torch.randn(B, device=dev)
+    stats = torch.zeros(8, device=dev)
+
     def step():
+        if a.fused_head:
+            net.forward_hidden(x, ws)
+            net.loss_backward(x, ws, act, old, adv, ret, stats, 0.2, 0.5, 0.0)
+            return
         net.forward(x, ws)
         ws["dout"].copy_(dout)
         net.grad.zero_()
@@ -54,8 +67,8 @@ def main():
     us = e0.elapsed_time(e1) * 1e3 / a.reps
     H2 = 2 * a.hidden
     flops = 2 * B * (PAD * H2 + H2 * H2 + H2 * 2 * PAD) * 3
-    res = {"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "us": us, "tflops": flops / us / 1e6,
-           "activation_bytes_per_layer": B * H2 * 2}
+    res = {"benchmark": "ppo_mlp_fwd_bwd", "rows": B, "fused_head": a.fused_head, "us": us,
+           "tflops": flops / us / 1e6, "activation_bytes_per_layer": B * H2 * 2}
     if a.no_variants:
         print(json.dumps(res))
         return

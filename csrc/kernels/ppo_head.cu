@@ -52,19 +52,52 @@ __device__ __forceinline__ void load_row(const bf16* p, float* h) {
   }
 }
 
+// Rows in flight per warp: a ring of shared-memory slots filled by cp.async,
+// so a warp keeps kRing row loads outstanding (the pass is bound by how many
+// bytes are in flight per SM, not by arithmetic).
+constexpr int kRing = 4;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Shared memory of one CTA (bytes): per warp a ring of kRing slots of (one
+// H2 row, 4 row scalars); the final fold reuses the same area.
+template <int A, int CPL>
+struct HeadSmem {
+  static constexpr int H = 16 * CPL;
+  static constexpr int kSlot = 2 * H * 2 + 16;  // bf16 row + act, old logp, adv, ret
+  static constexpr int kRingBytes = kWarps * kRing * kSlot;
+  static constexpr int kFold = kWarps * (2 * H + A * H + H + A + 1 + kStats) * 4;
+  static constexpr int kTotal = kRingBytes > kFold ? kRingBytes : kFold;
+};
+
 // CPL = H / 16 columns per lane; A actions (categorical).
 template <int A, int CPL>
-__global__ void __launch_bounds__(kThreads) ppo_head_kernel(
+__global__ void __launch_bounds__(kThreads, 2) ppo_head_kernel(
     const bf16* __restrict__ H2, long long ldh, const bf16* __restrict__ W3, long long ldw,
     const float* __restrict__ b3, int crow, const int* __restrict__ act, const float* __restrict__ old_logp,
     const float* __restrict__ adv, const float* __restrict__ ret, bf16* __restrict__ dz, long long ldz,
     float* __restrict__ part, int M, float clip, float vf_coef, float ent_coef) {
-  constexpr int H = 16 * CPL;
-  extern __shared__ float red[];  // [kWarps][part_len]
+  using S = HeadSmem<A, CPL>;
+  constexpr int H = S::H;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* ring_base = smem;
+  float* red = reinterpret_cast<float*>(smem);  // the fold, after the loop
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const bool critic = lane >= 16;
   const int col = (critic ? H : 0) + (lane & 15) * CPL;  // first column of this lane in H2 / dZ2
-  // output-layer weights of this lane's columns: actor rows 0..A-1, or the critic row
+  // output-layer weights of this lane's columns, in registers for the whole
+  // pass: actor rows 0..A-1, or the critic row
   float wt[A][CPL];
 #pragma unroll
   for (int k = 0; k < A; ++k) {
@@ -94,31 +127,41 @@ __global__ void __launch_bounds__(kThreads) ppo_head_kernel(
   float st_pg = 0.f, st_v = 0.f, st_h = 0.f, st_kl = 0.f, st_cf = 0.f, st_n = 0.f;
 
   const int gw_id = blockIdx.x * kWarps + w, n_warps = gridDim.x * kWarps;
-  // the next row's inputs are loaded before the current row is processed
-  float hn[CPL];
-  int an = 0;
-  float oldn = 0.f, Adn = 0.f, Rn = 0.f;
-  if (gw_id < M) {
-    load_row<CPL>(H2 + static_cast<long long>(gw_id) * ldh + col, hn);
-    an = act[gw_id];
-    oldn = old_logp[gw_id];
-    Adn = adv[gw_id];
-    Rn = ret[gw_id];
-  }
-  for (int r = gw_id; r < M; r += n_warps) {
-    float h[CPL];
+  uint8_t* ring = ring_base + w * kRing * S::kSlot;
+  // Lane l stages bytes [l * 2 CPL, (l + 1) * 2 CPL) of a row: exactly the
+  // columns it reads back, so its own cp.async wait covers them; lanes 0-3
+  // stage the row's action, old log-prob, advantage and return.
+  auto issue = [&](int slot, int r) {
+    if (r < M) {
+      uint8_t* dst = ring + slot * S::kSlot;
+      const bf16* src = H2 + static_cast<long long>(r) * ldh + col;
 #pragma unroll
-    for (int c = 0; c < CPL; ++c) h[c] = hn[c];
-    const int a = an;
-    const float old = oldn, Ad = Adn, R = Rn;
-    const int rn = r + n_warps;
-    if (rn < M) {
-      load_row<CPL>(H2 + static_cast<long long>(rn) * ldh + col, hn);
-      an = act[rn];
-      oldn = old_logp[rn];
-      Adn = adv[rn];
-      Rn = ret[rn];
+      for (int q = 0; q < CPL / 8; ++q) cp_async16(dst + (col + 8 * q) * 2, src + 8 * q);
+      if (lane < 4) {
+        const void* sp = lane == 0 ? static_cast<const void*>(act + r)
+                         : lane == 1 ? static_cast<const void*>(old_logp + r)
+                         : lane == 2 ? static_cast<const void*>(adv + r)
+                                     : static_cast<const void*>(ret + r);
+        cp_async4(dst + 2 * H * 2 + 4 * lane, sp);
+      }
     }
+    cp_async_commit();  // one group per slot, empty past the end
+  };
+#pragma unroll
+  for (int q = 0; q < kRing; ++q) issue(q, gw_id + q * n_warps);
+  int slot = 0;
+  for (int r = gw_id; r < M; r += n_warps) {
+    cp_async_wait<kRing - 1>();  // this lane's copies of the oldest slot are done
+    const uint8_t* cur = ring + slot * S::kSlot;
+    float h[CPL];
+    load_row<CPL>(reinterpret_cast<const bf16*>(cur) + col, h);
+    float scal = lane < 4 ? *reinterpret_cast<const float*>(cur + 2 * H * 2 + 4 * lane) : 0.f;
+    const int a = __float_as_int(__shfl_sync(0xffffffffu, scal, 0));
+    const float old = __shfl_sync(0xffffffffu, scal, 1), Ad = __shfl_sync(0xffffffffu, scal, 2),
+                R = __shfl_sync(0xffffffffu, scal, 3);
+    __syncwarp();
+    issue(slot, r + kRing * n_warps);  // refill the slot just read
+    slot = slot + 1 == kRing ? 0 : slot + 1;
     // ---- forward: partial dot products, then sums over the 16 lanes of a half
     float s[A];
 #pragma unroll
@@ -215,6 +258,8 @@ __global__ void __launch_bounds__(kThreads) ppo_head_kernel(
     }
   }
   // ---- this warp's sums into its shared-memory row, then a fixed-order fold
+  cp_async_wait<0>();
+  __syncthreads();  // every warp is done with its ring (the fold reuses it)
   const int L = part_len(H, A);
   float* row = red + w * L;
 #pragma unroll
@@ -283,7 +328,7 @@ __global__ void __launch_bounds__(1024) ppo_head_reduce_kernel(const float* __re
 template <int A, int CPL>
 int launch_head(const TbPpoHeadArgs* a, cudaStream_t s) {
   const int L = part_len(16 * CPL, A);
-  const size_t smem = sizeof(float) * kWarps * L;
+  const size_t smem = HeadSmem<A, CPL>::kTotal;
   auto k = ppo_head_kernel<A, CPL>;
   tb::ensure_dyn_smem(reinterpret_cast<const void*>(k), static_cast<int>(smem));
   k<<<a->parts, kThreads, smem, s>>>(static_cast<const bf16*>(a->H2), a->ldh, static_cast<const bf16*>(a->W3),
@@ -310,10 +355,16 @@ int tb_ppo_head_default_parts(int H, int A) {
   // one partial row per resident CTA: SMs x CTAs that fit on an SM
   int dev = 0, sms = 148, per_sm = 1;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const size_t smem = sizeof(float) * kWarps * part_len(H, A);
+  size_t smem = 0;
   const void* fn = nullptr;
-  if (A == 2 && H == 256) fn = reinterpret_cast<const void*>(ppo_head_kernel<2, 16>);
-  if (A == 2 && H == 128) fn = reinterpret_cast<const void*>(ppo_head_kernel<2, 8>);
+  if (A == 2 && H == 256) {
+    fn = reinterpret_cast<const void*>(ppo_head_kernel<2, 16>);
+    smem = HeadSmem<2, 16>::kTotal;
+  }
+  if (A == 2 && H == 128) {
+    fn = reinterpret_cast<const void*>(ppo_head_kernel<2, 8>);
+    smem = HeadSmem<2, 8>::kTotal;
+  }
   if (fn != nullptr) {
     tb::ensure_dyn_smem(fn, static_cast<int>(smem));
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) != cudaSuccess || per_sm < 1)
