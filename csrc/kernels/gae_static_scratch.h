@@ -16,12 +16,18 @@
 //     (zero them first if you want this call's moments alone).
 //   * The workspace holds TB_GAE_STATIC_SCRATCH_FLOATS floats (1 MiB).  A call
 //     whose chunked scan needs more returns cudaErrorInvalidValue and does
-//     nothing; tb_gae_static_scratch_fits(T, N) says in advance.  (N >= 32768
-//     needs no workspace at all; smaller N needs about 2 * 65536 floats.)
+//     nothing; tb_gae_static_scratch_fits(T, N) says in advance.  Under the
+//     current chunk rule no shape needs more: N >= 32768 needs no workspace,
+//     and smaller N uses at most min(64, T, ceil(65536 / N)) chunks of
+//     2 * N floats, i.e. below 2 * (65536 + N) < 196,608 floats; the check
+//     guards a future change of that rule.
 //   * Set-up: the first call on a device resolves the array's device address
 //     with cudaGetSymbolAddress for the current device and caches it; make
 //     that first call (or tb_gae_static_scratch_init) before any stream
-//     capture, with the target device current.
+//     capture, with the target device current.  The cached address belongs
+//     to the device's current context: after cudaDeviceReset on that device
+//     it is stale and the entry point must not be called again in the same
+//     process.
 //   * Every call on a device shares the one array and leaves its contents
 //     behind; every element a call reads it first writes, so nothing needs
 //     clearing between calls.  Calls that overlap on the GPU (different

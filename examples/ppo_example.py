@@ -10,8 +10,11 @@ auto-reset), an actor-critic MLP (tanh, orthogonal init), GAE(0.99, 0.95),
 clipped PPO for 4 epochs of minibatches, Adam.  Every rollout step is also
 pushed into a RingBuffer (capacity 8192 by default) as the reference does.
 
-On a GPU the trainer runs the fused sm_100a path (bf16 tensor-core MLP,
-on-device environment, CUDA graphs); on CPU the same math in PyTorch.
+The default compute dtype is fp32 (the 256-env workload's precision): on a
+GPU the environment, sampling, GAE, minibatch gather, loss and Adam run as
+sm_100a kernels under CUDA graphs with an fp32 MLP; ``--dtype bf16`` switches
+the MLP to the tensor-core path of the large-batch benchmark; on CPU the same
+math in PyTorch.
 Multi-GPU data parallel: ``torchrun --nproc-per-node N examples/ppo_example.py --dp fused``.
 """
 from __future__ import annotations
@@ -47,7 +50,9 @@ def parse_args(argv=None):
     p.add_argument("--hidden", type=int, nargs="+", default=[64, 64])
     p.add_argument("--epochs", type=int, default=4)
     p.add_argument("--buffer-capacity", type=int, default=8192)
-    p.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16", help="GPU compute dtype")
+    p.add_argument("--dtype", choices=["bf16", "fp32"], default="fp32",
+                   help="compute dtype: fp32 (the default, as in the 256-env CartPole workload) or bf16 (the "
+                        "tensor-core path of the large-batch benchmark)")
     p.add_argument("--dp", choices=["none", "nccl", "fused"], default="none",
                    help="data parallel gradient reduction (launch with torchrun)")
     p.add_argument("--checkpoint-dir", type=str, default="")

@@ -60,3 +60,25 @@ def test_grpo_kernel(G, dev):
     got = grpo_advantage(r.to(dev), G).cpu()
     exp = ref.grpo_advantage(r, G)
     assert torch.allclose(got, exp, atol=1e-5)
+
+
+def test_static_scratch_gae_bound_cpu():
+    """The allocation-free GAE entry point's size check (host arithmetic, no
+    GPU): fits() agrees with the 1 MiB array for every shape probed, and under
+    the chunk rule no shape needs more than 196,608 floats, so the rejection
+    branch only guards a future change of that rule."""
+    import ctypes
+
+    import turbol_b200
+    from turbol_b200._native import ops
+
+    lib = ctypes.CDLL(turbol_b200.turbol_core.__file__)
+    fits = lib.tb_gae_static_scratch_fits
+    fits.restype, fits.argtypes = ctypes.c_int, [ctypes.c_int, ctypes.c_int]
+    worst = 0
+    for N in list(range(1, 300)) + [511, 513, 1000, 4095, 4097, 16383, 32767, 32768, 65536]:
+        for T in (1, 2, 7, 64, 65, 256, 4096):
+            need = ops().gae_scratch_numel(T, N)
+            worst = max(worst, need)
+            assert fits(T, N) == (1 if need <= 256 * 1024 else 0), (T, N, need)
+    assert worst < 196608, worst
