@@ -65,7 +65,6 @@ def run_grpo(args, world, rank, local):
     and training on the fused all-gather->GEMM / GEMM->reduce-scatter kernels)
     x data parallel over the N/2 pairs (fused peer-memory optimizer step)."""
     import torch
-    import torch.distributed as dist
 
     from turbol_b200.rl.grpo import GRPOConfig, GRPOTrainer
 

@@ -38,7 +38,6 @@ import datetime
 import json
 import math
 import os
-import time
 
 import torch
 import torch.distributed as dist

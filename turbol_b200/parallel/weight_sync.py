@@ -29,7 +29,6 @@ import math
 from typing import List
 
 import torch
-import torch.distributed as dist
 
 from ..models.llm import ALIGN, DecoderLM
 from .peer import PeerBuffers

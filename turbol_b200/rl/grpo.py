@@ -24,11 +24,8 @@ module is the algorithm it names.
 """
 from __future__ import annotations
 
-import math
 import time
 from dataclasses import dataclass, field
-from typing import Optional
-
 import torch
 
 from .._native import ops as _ops
