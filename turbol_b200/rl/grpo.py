@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import time
 from dataclasses import dataclass, field
+
 import torch
 
 from .._native import ops as _ops
@@ -74,8 +75,9 @@ class GRPOTrainer:
       owns 1/tp of every projection, forward and backward on the fused
       kernels); the TP group trains on all of its sequences, each micro-batch
       split by rows over the ranks; data parallelism (``dp``) runs over the
-      ranks that hold the same shard (TP x DP).  Rollout and trainer share the
-      weights, so the trainer -> rollout sync is free.
+      ranks that hold the same shard (TP x DP).  The rollout and the frozen
+      reference model are per-rank full copies by default (``rollout``
+      below), so decoding and reference scoring need no collective.
     * "rollout": every rank keeps the full model and trains data parallel on
       its 1/tp share of the group's sequences; after the optimizer step every
       rank re-slices its rollout shard from the updated weights."""
@@ -179,7 +181,6 @@ class GRPOTrainer:
         self.comm = TensorParallelComm(rows, H, H, group=mesh.tp_group, device=self.device.index)
         full = DecoderLM(cfg.model, self.device, seed=cfg.seed, master=False)  # bf16 only, sliced below
         self.model = TPTrainLM(full, self.comm)
-        del full
         dp_world = mesh.dp
         if dp_world > 1 and dp == "fused":
             from ..parallel.peer import FusedDataParallelAdam
@@ -196,7 +197,13 @@ class GRPOTrainer:
                 dist.broadcast(self.model.flat, src=dist.get_global_rank(mesh.dp_group, 0), group=mesh.dp_group)
                 self.model.shadow.copy_(self.model.flat)
                 self.grad_sync = NcclGradSync(mesh.dp_group)
-        self.ref = self.model.frozen_copy()
+        if self.rollout_mode == "replica":
+            # the frozen reference stays a whole bf16 model (the initial
+            # weights): each rank scores its own sequences with it, no collective
+            self.ref = full
+        else:
+            self.ref = self.model.frozen_copy()
+        del full
         self.tpm = self.model
         if self.rollout_mode == "replica":
             from ..parallel.weight_sync import TPReplicaSync
@@ -237,6 +244,7 @@ class GRPOTrainer:
             self.model.flat.copy_(sd["policy"]["flat"])
             self.model.shadow.copy_(sd["policy"]["shadow"])
             self.ref.shadow.copy_(sd["ref_shadow"])
+            self.ref._make_views()  # a bf16-only model keeps fp32 copies of its norms and biases: refresh them
             self.opt.load_state_dict(sd["optim"])
             if self.tp_mode == "rollout":
                 self.tpm.load_from(self.model)  # the rollout shard follows the loaded weights
@@ -324,7 +332,8 @@ class GRPOTrainer:
         if self.tp_mode == "train":
             own = self._tp_own(seqs.shape[0])
             adv = adv.index_select(0, own).contiguous()
-            ref_lp = self._tp_ref_logprobs(seqs)
+            ref_lp = (self.ref_logprobs(seqs.index_select(0, own).contiguous()) if self.rollout_mode == "replica"
+                      else self._tp_ref_logprobs(seqs))
         else:
             ref_lp = self.ref_logprobs(seqs)
         torch.cuda.synchronize(dev)
