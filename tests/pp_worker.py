@@ -102,6 +102,27 @@ def main():
     tr.sync_weights()
     for name in tr._stage_names(rank):
         assert torch.equal(tr.rollout.s[name], tr.stage.model.s[name]), name
+    # ---- 3. checkpoint of the pipeline shards: each stage saves policy_tp0_pp<s>, a fresh trainer loads it
+    import tempfile
+
+    from turbol_b200.utils.checkpoint import load_checkpoint, save_checkpoint
+
+    base = os.path.join(tempfile.gettempdir(), f"tb_pp_ckpt_{os.environ.get('MASTER_PORT', '0')}")
+    save_checkpoint(base, 3, tr)
+    dist.barrier()
+    names = set(os.listdir(os.path.join(base, "step_3")))
+    assert {f"policy_tp0_pp{p}.pt" for p in range(world)} <= names, names
+    tr2 = PPORLHFTrainer(rcfg, dev)
+    load_checkpoint(base, trainer=tr2)
+    torch.cuda.synchronize()
+    assert torch.equal(tr2.stage.model.flat, tr.stage.model.flat) and tr2.step_count == tr.step_count
+    for name in tr._stage_names(rank):
+        assert torch.equal(tr2.rollout.s[name], tr.stage.model.s[name]), ("rollout after load", name)
+    dist.barrier()
+    if rank == 0:
+        import shutil
+
+        shutil.rmtree(base, ignore_errors=True)
     if rank == 0:
         print("PP_WORKER_OK", worst, out)
     dist.barrier()

@@ -138,6 +138,31 @@ def main():
                 assert torch.equal(tr.sync.full.s[name], chk.s[name]), ("GRPO replica", name)
         moved = (tr.model.flat - before).abs().max().item()
         assert moved > 0, "weights did not move"
+        if mode == "replica":
+            # sharded checkpoint: every rank writes its own TP shard and marker, and a
+            # fresh trainer on each rank gets its own shard back bit for bit
+            import tempfile
+
+            from turbol_b200.utils.checkpoint import latest_step, load_checkpoint, save_checkpoint
+
+            base = os.path.join(tempfile.gettempdir(), f"tb_tp_ckpt_{os.environ.get('MASTER_PORT', '0')}")
+            save_checkpoint(base, 2, tr)
+            dist.barrier()
+            names = set(os.listdir(os.path.join(base, "step_2")))
+            want = {f"policy_tp{t}_pp0.pt" for t in range(world)} | {f"COMPLETE_dp0_tp{t}_pp0" for t in range(world)}
+            assert want <= names and latest_step(base) == 2, names
+            tr2 = GRPOTrainer(gcfg, str(dev), dp="fused", tp=2, tp_mode="train", rollout=mode)
+            load_checkpoint(base, trainer=tr2)
+            torch.cuda.synchronize()
+            assert torch.equal(tr2.model.flat, tr.model.flat) and tr2.step_count == tr.step_count
+            for name in chk.offsets:  # the replica follows the loaded shards
+                assert torch.equal(tr2.sync.full.s[name], chk.s[name]), ("replica after load", name)
+            dist.barrier()
+            if rank == 0:
+                import shutil
+
+                shutil.rmtree(base, ignore_errors=True)
+            del tr2
         rep_sum = tr.model.flat[: tr.model.rep_numel].double().sum().reshape(1)
         sums = [torch.zeros_like(rep_sum) for _ in range(world)]
         dist.all_gather(sums, rep_sum)

@@ -134,6 +134,41 @@ class PPORLHFTrainer:
         self.step_count = 0
         self.sync_weights()
 
+    # ------------------------------------------------------------ checkpoint
+    def checkpoint_ranks(self) -> dict:
+        """One shard per (tensor rank, pipeline stage): ``policy_tp<t>_pp<p>``."""
+        return {"tp_rank": self.tp_rank, "pp_rank": self.stage.stage,
+                "layout": {"tp": self.tp, "pp": self.n_stages, "dp": 0}}
+
+    def state_dict(self) -> dict:
+        """This rank's stage: fp32 master weights (+ value head), the frozen
+        reference shard, optimizer state and the step counter (which keys the
+        prompt and sampling streams)."""
+        st = self.stage
+        pol = {"flat": st.model.flat, "shadow": st.model.shadow}
+        opt = {"stage": st.opt.state_dict()}
+        if st.value_head:
+            pol["value_head"] = st.vh
+            opt["value_head"] = st.vh_opt.state_dict()
+        return {"policy": pol, "optim": opt, "ref_shadow": self.ref.model.shadow, "step_count": self.step_count,
+                "gen_calls": self.gen.calls}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict):
+        st = self.stage
+        st.model.flat.copy_(sd["policy"]["flat"])
+        st.model.shadow.copy_(sd["policy"]["shadow"])
+        st.opt.load_state_dict(sd["optim"]["stage"])
+        if st.value_head:
+            st.vh.copy_(sd["policy"]["value_head"])
+            st.vh_opt.load_state_dict(sd["optim"]["value_head"])
+            st.sync_value_head()
+        self.ref.model.shadow.copy_(sd["ref_shadow"])
+        self.ref.model._make_views()
+        self.step_count = int(sd["step_count"])
+        self.gen.calls = int(sd["gen_calls"])
+        self.sync_weights()  # the rollout copy follows the loaded weights
+
     # ------------------------------------------------------------ weight sync
     @torch.no_grad()
     def sync_weights(self):
