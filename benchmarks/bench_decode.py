@@ -108,18 +108,22 @@ def main():
             bias = torch.randn(N, device=dev)
             ws = torch.zeros(max(o.gemm_workspace_numel(M, N, K), 1), device=dev)
             row = {}
-            for label, kw in (("auto", {}), ("split-k", {"workspace": ws})):
-                if epi == o.EPI_SWIGLU and "workspace" in kw:
+            # auto / split-k: the general tcgen05 GEMM; decode: the weight-stationary
+            # decode GEMM (cluster split-K), not used for the LM head
+            variants = [("auto", {}), ("split-k", {"workspace": ws})]
+            if name != "lm_head":
+                variants.append(("decode", None))
+            for label, kw in variants:
+                if epi == o.EPI_SWIGLU and kw and "workspace" in kw:
                     continue
 
                 def run():
                     for W in Ws:
-                        if epi == o.EPI_BIAS:
-                            o.gemm(A, W, C, bias=bias, epi=epi, **kw)
-                        elif epi == o.EPI_RESIDUAL:
-                            o.gemm(A, W, C, aux=aux, epi=epi, **kw)
+                        ep = {"bias": bias} if epi == o.EPI_BIAS else ({"aux": aux} if epi == o.EPI_RESIDUAL else {})
+                        if kw is None:
+                            o.gemm_decode(A, W, C, epi=epi, **ep)
                         else:
-                            o.gemm(A, W, C, epi=epi, **kw)
+                            o.gemm(A, W, C, epi=epi, **ep, **kw)
                 us = graph_time(run) / nl
                 row[label] = us
                 print(f"gemm {name:8s} M={M:5d} N={N:6d} K={K:5d} {label:8s} {us:8.1f} us  "

@@ -104,13 +104,16 @@ def main():
     P = net.p
     res["out_fwd_us"] = {"gemm": t(lambda: o.gemm(h2, S["w3"], ws["out"], bias=P["b3"], epi=o.EPI_BIAS)),
                          "cuda_core": t(lambda: o.mlp_head_fwd(h2, S["w3"], P["b3"], H, ws["out"]))}
-    # tile widths of the two K = 512 GEMMs (whole K, and kgroup: each tile only
-    # its head's diagonal block) and of the hidden-layer weight gradient
+    # tile widths of the two K = 512 GEMMs (kg0: the whole K over a dense
+    # block-diagonal W2; kgroup: each tile only its head's K range, reading the
+    # packed diagonal blocks) and of the hidden-layer weight gradient
+    w2_dense = torch.block_diag(S["w2a"], S["w2c"]).contiguous()
     for kg in (0, H):
+        w2 = S["w2"] if kg else w2_dense
         for bn in (64, 128, 256):
-            res[f"h2_fwd_kg{kg}_bn{bn}_us"] = t(lambda: o.gemm(h1, S["w2"], h2, bias=P["b2"], epi=o.EPI_BIAS_TANH,
+            res[f"h2_fwd_kg{kg}_bn{bn}_us"] = t(lambda: o.gemm(h1, w2, h2, bias=P["b2"], epi=o.EPI_BIAS_TANH,
                                                                bn=bn, kgroup=kg))
-            res[f"dZ1_kg{kg}_bn{bn}_us"] = t(lambda: o.gemm(dz2, S["w2"], dz1, False, True, aux=h1,
+            res[f"dZ1_kg{kg}_bn{bn}_us"] = t(lambda: o.gemm(dz2, w2, dz1, False, True, aux=h1,
                                                             epi=o.EPI_TANH_BWD, colsum=G["b1"], bn=bn, kgroup=kg))
     for bn in (128, 256):
         for sk in (0, 8, 16, 32):

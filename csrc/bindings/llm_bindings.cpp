@@ -26,8 +26,11 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   chk(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: last dim must be contiguous");
   const int64_t M = a_mn ? A.size(1) : A.size(0);
   const int64_t K = a_mn ? A.size(0) : A.size(1);
-  const int64_t N = b_mn ? B.size(1) : B.size(0);
-  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  // kgroup with B's inner dimension one block wide: B holds only the diagonal
+  // blocks, packed side by side (then N == K, the outer dimension of B)
+  const bool packed = kgroup > 0 && B.size(1) == kgroup && B.size(0) == K && K > kgroup;
+  const int64_t N = packed ? K : (b_mn ? B.size(1) : B.size(0));
+  const int64_t Kb = packed ? K : (b_mn ? B.size(0) : B.size(1));
   chk(K == Kb, "gemm: K mismatch");
   const int64_t nc = epi == TB_EPI_SWIGLU ? N / 2 : (epi == TB_EPI_SWIGLU_BWD ? 2 * N : N);
   chk(C.size(0) == M && C.size(1) == nc, "gemm: C shape mismatch");
@@ -65,6 +68,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   a.split_k = split_k;
   a.bn_hint = bn;
   a.kgroup = kgroup;
+  a.kgroup_packed = packed ? 1 : 0;
   if (!err.is_none()) a.error = err.cast<at::Tensor>().data_ptr<int>();
   at::Tensor ws, cs;
   if (!workspace.is_none()) {
@@ -90,9 +94,55 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor C, bool a_mn, boo
   cuda_ok(tb_gemm_bf16(&a, turbol::StreamFor(C)), "gemm_bf16");
 }
 
+// Decode-shaped GEMM (few tokens, weight-stationary, cluster split-K).
+void gemm_decode(const at::Tensor& X, const at::Tensor& W, at::Tensor C, py::object bias, py::object aux, int epi,
+                 int splits, py::object err) {
+  chk(X.is_cuda() && W.is_cuda() && C.is_cuda(), "gemm_decode: CUDA tensors required");
+  chk(X.scalar_type() == at::kBFloat16 && W.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+      "gemm_decode: bf16 X, W and C");
+  chk(X.dim() == 2 && W.dim() == 2 && C.dim() == 2 && X.stride(1) == 1 && W.stride(1) == 1 && C.stride(1) == 1,
+      "gemm_decode: 2-D operands with a contiguous last dim");
+  chk(X.size(1) == W.size(1), "gemm_decode: K mismatch");
+  const int64_t T = X.size(0), N = W.size(0);
+  chk(C.size(0) == T && C.size(1) == (epi == TB_EPI_SWIGLU ? N / 2 : N), "gemm_decode: C shape mismatch");
+  TbDecodeGemmArgs a{};
+  a.X = X.data_ptr();
+  a.ldx = X.stride(0);
+  a.W = W.data_ptr();
+  a.ldw = W.stride(0);
+  a.C = C.data_ptr();
+  a.ldc = C.stride(0);
+  a.T = static_cast<int>(T);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(X.size(1));
+  a.epi = epi;
+  a.splits = splits;
+  at::Tensor b, x;
+  if (!bias.is_none()) {
+    b = bias.cast<at::Tensor>();
+    chk(b.is_cuda() && b.scalar_type() == at::kFloat && b.is_contiguous() && b.numel() == N,
+        "gemm_decode: bias must be fp32 [N]");
+    a.bias = b.data_ptr<float>();
+  }
+  if (!aux.is_none()) {
+    x = aux.cast<at::Tensor>();
+    chk(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(0) == T &&
+            x.size(1) == N,
+        "gemm_decode: aux must be bf16 [T, N]");
+    a.aux = x.data_ptr();
+    a.ld_aux = x.stride(0);
+  }
+  if (!err.is_none()) a.error = err.cast<at::Tensor>().data_ptr<int>();
+  cuda_ok(tb_gemm_decode(&a, turbol::StreamFor(C)), "gemm_decode");
+}
+
 }  // namespace
 
 void register_llm_ops(py::module_& m) {
+  m.def("gemm_decode", &gemm_decode, py::arg("X"), py::arg("W"), py::arg("C"), py::arg("bias") = py::none(),
+        py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("splits") = 0, py::arg("error") = py::none(),
+        "C = epi(X W^T) for few tokens: weight-stationary tcgen05 GEMM, K split over a cluster");
+  m.def("gemm_decode_splits", &tb_gemm_decode_splits, py::arg("N"), py::arg("K"));
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn") = false, py::arg("b_mn") = false,
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0f, py::arg("split_k") = 0, py::arg("bn") = 0, py::arg("error") = py::none(),

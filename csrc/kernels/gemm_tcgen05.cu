@@ -86,6 +86,7 @@ struct DevArgs {
   __nv_bfloat16* c2;  // EPI_SWIGLU, optional: the raw gate/up accumulator [M, N] (bf16), row stride ldc2
   long long ldc2;
   int kg_ntiles;      // block-diagonal B: n-tiles per diagonal block (0 = off); k_blocks is then per block
+  int kg_packed;      // block-diagonal B stored packed: only the diagonal blocks, side by side along its inner dim
   TpArgs tp;
 };
 
@@ -698,6 +699,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.tp.trace && p.tp.trace[blockIdx.x * 8 + 4] == 0) p.tp.trace[blockIdx.x * 8 + 4] = global_ns();
         }
       }
+      // packed block-diagonal B: its inner coordinate is local to the block
+      const int goff = p.kg_packed ? (nt / p.kg_ntiles) * p.k_blocks * BK : 0;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
         uint8_t* sa = smem + stage * S::kStageBytes;
@@ -715,9 +718,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (B_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 64 * BK * 2, &tmB, &full[stage], n0 + 64 * j, k0);
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(sb + j * 64 * BK * 2, &tmB, &full[stage], n0 - goff + 64 * j, k0);
         } else {
-          tma_load_2d(sb, &tmB, &full[stage], k0, n0);
+          tma_load_2d(sb, &tmB, &full[stage], k0 - goff, n0);
         }
         ++issued;
         if (++stage == S::kStages) {
@@ -1331,7 +1335,10 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   CUtensorMap ta, tbm;
   // A: K-major -> matrix [M, K]; MN-major -> matrix [K, M]
   const bool okA = a->a_mn ? make_map(&ta, a->A, a->K, a->M, a->lda, BK) : make_map(&ta, a->A, a->M, a->K, a->lda, BM);
-  const bool okB = a->b_mn ? make_map(&tbm, a->B, a->K, a->N, a->ldb, BK) : make_map(&tbm, a->B, a->N, a->K, a->ldb, BN);
+  // packed block-diagonal B: its inner dimension is one block (kg) wide
+  const int b_inner_n = kg && a->kgroup_packed ? kg : a->N, b_inner_k = kg && a->kgroup_packed ? kg : a->K;
+  const bool okB = a->b_mn ? make_map(&tbm, a->B, a->K, b_inner_n, a->ldb, BK)
+                           : make_map(&tbm, a->B, a->N, b_inner_k, a->ldb, BN);
   if (!okA || !okB) return static_cast<int>(cudaErrorInvalidValue);
 
   DevArgs p{};
@@ -1378,6 +1385,7 @@ int tb_gemm_bf16(const TbGemmArgs* a, cudaStream_t stream) {
   p.c2 = static_cast<__nv_bfloat16*>(a->C2);
   p.ldc2 = a->ldc2;
   p.kg_ntiles = kg ? kg / BN : 0;
+  p.kg_packed = kg && a->kgroup_packed ? 1 : 0;
   const int total = tiles * p.splits;
   const int grid = total < num_sms() ? total : num_sms();
   const int am = a->a_mn ? 1 : 0, bm = a->b_mn ? 1 : 0;

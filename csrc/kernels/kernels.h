@@ -191,9 +191,40 @@ typedef struct {
   // [g * kgroup, (g + 1) * kgroup) with g = n / kgroup; the kernel skips the rest.
   // Needs K == N and kgroup a multiple of 64 that divides N.
   int kgroup;
+  // With kgroup: B holds the diagonal blocks only, packed along its inner
+  // dimension (K-major: [N, kgroup], row n = block g's row; MN-major:
+  // [K, kgroup], row k = block g's row), ldb >= kgroup.
+  int kgroup_packed;
 } TbGemmArgs;
 
 int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
+
+// Small-M GEMM for decode (gemm_decode.cu): C[T, N] = epi(X[T, K] . W[N, K]^T)
+// with the weight as the tensor cores' M side and K split over a thread-block
+// cluster (reduced through distributed shared memory).  bf16 operands and
+// output; epi is TB_EPI_NONE, TB_EPI_BIAS (fp32 [N]), TB_EPI_RESIDUAL (aux bf16
+// [T, N]) or TB_EPI_SWIGLU (interleaved gate / up rows of W, C [T, N / 2]).
+// N, K and every leading dimension a multiple of 8, base pointers 16-byte
+// aligned; any T (256 tokens per launch).
+typedef struct {
+  const void* X;
+  long long ldx;
+  const void* W;
+  long long ldw;
+  void* C;
+  long long ldc;
+  int T, N, K;
+  int epi;
+  const float* bias;
+  const void* aux;
+  long long ld_aux;
+  int splits;  // 0: automatic (fill the SMs, at most 8 per cluster)
+  int* error;  // optional: set when a wait ran out
+} TbDecodeGemmArgs;
+
+int tb_gemm_decode(const TbDecodeGemmArgs* args, cudaStream_t s);
+// The automatic split count for an [N, K] weight.
+int tb_gemm_decode_splits(int N, int K);
 // PPO output layer + clipped loss + output-layer backward in one pass over the
 // hidden activations H2 = [H2a | H2c] (bf16 [M, 2H]); categorical actor with A
 // actions.  W3 bf16 [>= crow + 1, 2H] (actor rows 0..A-1 over columns [0, H),

@@ -206,12 +206,15 @@ def test_gemm_swiglu_save_and_backward_epilogues(M, N, K, b_mn, bn, dev):
     assert torch.allclose(d_gu.float(), exp, atol=tol, rtol=2e-2), (d_gu.float() - exp).abs().max()
 
 
+@pytest.mark.parametrize("packed", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
 @pytest.mark.parametrize("kg,bn", [(256, 128), (256, 0), (128, 64)])
-def test_gemm_block_diagonal_k_range(b_mn, kg, bn, dev):
+def test_gemm_block_diagonal_k_range(b_mn, kg, bn, packed, dev):
     """kgroup: output column n reads only the K range of its diagonal block of B.
     B's off-diagonal blocks hold garbage here, so a kernel that still read them
-    would not match the fp32 product with the masked (block-diagonal) B."""
+    would not match the fp32 product with the masked (block-diagonal) B.
+    packed: B holds only the diagonal blocks, [N, kg] (row r = its block's
+    row), inside a wider buffer so that ldb > kg."""
     M, N = 1000, 512
     A = _mk((M, N), dev, 3)
     B = _mk((N, N), dev, 4)
@@ -219,6 +222,11 @@ def test_gemm_block_diagonal_k_range(b_mn, kg, bn, dev):
     for g in range(N // kg):
         mask[g * kg:(g + 1) * kg, g * kg:(g + 1) * kg] = True
     Bm = torch.where(mask, B, torch.zeros_like(B))
+    if packed:
+        wide = _mk((N, kg + 64), dev, 6)
+        for g in range(N // kg):
+            wide[g * kg:(g + 1) * kg, :kg] = B[g * kg:(g + 1) * kg, g * kg:(g + 1) * kg]
+        B = wide[:, :kg]
     aux = _mk((M, N), dev, 5)
     bias = torch.randn(N, device=dev)
     for epi, kw in ((0, {}), (ops().EPI_BIAS_TANH, {"bias": bias}), (ops().EPI_TANH_BWD, {"aux": aux})):
@@ -231,3 +239,45 @@ def test_gemm_block_diagonal_k_range(b_mn, kg, bn, dev):
             acc = acc * (1 - aux.float() ** 2)
         torch.cuda.synchronize()
         assert torch.allclose(C.float(), acc, atol=3e-2 * (kg ** 0.5) / 8 + 2e-2, rtol=2e-2), (epi, (C.float() - acc).abs().max())
+
+
+@pytest.mark.parametrize("T,N,K,splits", [(1, 256, 64, 0), (37, 2048, 1536, 0), (256, 1536, 8960, 0),
+                                          (300, 384, 520, 3), (200, 1000, 1536, 1), (512, 1536, 1536, 8),
+                                          (16, 136, 72, 2)])
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "swiglu"])
+def test_gemm_decode_matches_fp32(T, N, K, splits, epi, dev):
+    """Weight-stationary decode GEMM (cluster split-K over DSMEM) against the
+    fp32 product; odd token counts, a ragged last K block, partial weight
+    tiles, several passes of 256 tokens and every epilogue."""
+    o = ops()
+    X = _mk((T, K), dev, 7)
+    W = _mk((N, K), dev, 8)
+    acc = X.float() @ W.float().t()
+    kw = {}
+    code = {"none": o.EPI_NONE, "bias": o.EPI_BIAS, "residual": o.EPI_RESIDUAL, "swiglu": o.EPI_SWIGLU}[epi]
+    if epi == "bias":
+        kw["bias"] = torch.randn(N, device=dev)
+        exp = acc + kw["bias"]
+    elif epi == "residual":
+        kw["aux"] = _mk((T, N), dev, 9)
+        exp = acc + kw["aux"].float()
+    elif epi == "swiglu":
+        exp = torch.nn.functional.silu(acc[:, 0::2]) * acc[:, 1::2]
+    else:
+        exp = acc
+    C = torch.full((T, N // 2 if epi == "swiglu" else N), float("nan"), device=dev, dtype=torch.bfloat16)
+    err = torch.zeros(1, device=dev, dtype=torch.int32)
+    o.gemm_decode(X, W, C, epi=code, splits=splits, error=err, **kw)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    tol = 2e-2 * max(1.0, float(exp.abs().max()))
+    assert torch.allclose(C.float(), exp, atol=tol, rtol=2e-2), (C.float() - exp).abs().max()
+
+
+def test_gemm_decode_rejects_misaligned(dev):
+    o = ops()
+    X = _mk((4, 64), dev, 1)
+    W = _mk((12, 64), dev, 2)  # N not a multiple of 8
+    C = torch.empty(4, 12, device=dev, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        o.gemm_decode(X, W, C)

@@ -2,9 +2,11 @@
 
 Two tanh MLPs (actor obs -> H -> H -> A logits, critic obs -> H -> H -> 1)
 run as one network with block-diagonal layers: the actor and the critic are
-the two diagonal blocks of W2 [2H, 2H] and W3 [16, 2H] (the off-diagonal
-blocks are zero and receive no gradient, so they stay zero), so every layer is
-a single launch for both heads.  The 8-feature first layer runs on CUDA cores
+the two diagonal blocks of W2 and W3 [16, 2H], so every layer is a single
+launch for both heads.  W2 stores only its two [H, H] diagonal blocks, packed
+as [2H, H] (the GEMM's packed `kgroup` operand), so neither the optimizer nor
+the data-parallel exchange touches the zero off-diagonal half; W3's
+off-diagonal blocks are zero and receive no gradient, so they stay zero.  The 8-feature first layer runs on CUDA cores
 (a tensor-core tile would be mostly K padding); the rest on the tcgen05 GEMM
 (:func:`turbol_b200.ops.gemm`) with the pointwise work fused into the GEMM
 epilogues:
@@ -12,7 +14,8 @@ epilogues:
   forward   H1 = tanh(X W1^T + b1)          [B, 2H], CUDA-core kernel
             H2 = tanh(H1 W2^T + b2)         [B, 2H], one GEMM over the diagonal
                                             blocks only (kgroup: each output tile
-                                            iterates over its head's K range)
+                                            iterates over its head's K range and
+                                            reads its head's packed block)
             out = H2 W3^T + b3              [B, 16] fp32 (logits | value), one GEMM
   training  with 2 actions and H in {128, 256}: output layer + clipped PPO loss +
             dZ2, dW3, db3, db2 in ONE CUDA-core pass over H2 (ppo_head.cu:
@@ -56,7 +59,9 @@ class FusedActorCritic:
         # the one-pass output layer + loss + output-layer backward (ppo_head.cu)
         self.fused_head = act_dim == 2 and H in (128, 256)
         # parameter layout in the flat buffer; every offset 64-element aligned
-        shapes = [("w1", (2 * H, PAD)), ("b1", (2 * H,)), ("w2", (2 * H, 2 * H)), ("b2", (2 * H,)),
+        # W2 holds only the two diagonal blocks, packed: rows [0, H) are the
+        # actor's [H, H] block, rows [H, 2H) the critic's
+        shapes = [("w1", (2 * H, PAD)), ("b1", (2 * H,)), ("w2", (2 * H, H)), ("b2", (2 * H,)),
                   ("w3", (2 * PAD, 2 * H)), ("b3", (2 * PAD,))]
         self.offsets, off = {}, 0
         for name, shp in shapes:
@@ -91,7 +96,7 @@ class FusedActorCritic:
 
         def views(buf):
             d = {n: self._view(buf, n) for n in self.offsets}
-            d["w2a"], d["w2c"] = d["w2"][:H, :H], d["w2"][H:, H:]
+            d["w2a"], d["w2c"] = d["w2"][:H], d["w2"][H:]
             d["b2a"], d["b2c"] = d["b2"][:H], d["b2"][H:]
             d["w3a"], d["w3c"] = d["w3"][:PAD, :H], d["w3"][PAD:, H:]
             d["b3a"], d["b3c"] = d["b3"][:PAD], d["b3"][PAD:]
@@ -215,7 +220,7 @@ class FusedActorCritic:
         for head, cols in (("a", slice(0, H)), ("c", slice(H, 2 * H))):
             o.gemm(dz2[:, cols], h1[:, cols], G["w2" + head], True, True, workspace=wsk, bn=128, split_k=32)
         o.gemm(dz2, S["w2"], dz1, False, True, aux=h1, epi=o.EPI_TANH_BWD, colsum=G["b1"],   # dZ1, db1
-               kgroup=self.H)                                                    # (diagonal blocks of W2 only)
+               kgroup=self.H)                                                    # (packed diagonal blocks of W2)
         o.gemm(dz1, x_bf16, G["w1"], True, True, workspace=wsk)                              # dW1 = dZ1^T X
 
     def backward(self, x_bf16: torch.Tensor, ws, out_bias_grads_done: bool = False):
@@ -225,7 +230,7 @@ class FusedActorCritic:
         The hidden-layer bias gradients come out of the tanh-backward GEMM
         epilogues (column sums); the output-layer bias gradients come from the
         loss kernel when ``out_bias_grads_done`` (else a column-sum kernel).
-        Weight gradients are computed for the diagonal blocks only, so the
+        W3's gradient is computed for its diagonal blocks only, so its
         off-diagonal gradient (and weights) stay zero."""
         o = _ops()
         S, G = self.s, self.g

@@ -37,13 +37,16 @@ from ..models.llm import DecoderLM, LMConfig
 
 class LLMGenerator:
     def __init__(self, model: DecoderLM, max_batch: int, max_len: int, block_size: int = 16, seed: int = 0,
-                 cuda_graph: bool = True):
+                 cuda_graph: bool = True, decode_gemm: bool = False):
         self.m = model
         self.cfg = model.cfg
         self.device = model.device
         self.max_batch, self.max_len, self.bs = max_batch, max_len, block_size
         self.seed = seed
         self.cuda_graph = cuda_graph
+        # the layer projections of a decode step on the weight-stationary decode
+        # GEMM (gemm_decode.cu); False: the general tcgen05 GEMM
+        self.decode_gemm = decode_gemm
         cfg = self.cfg
         self.blocks_per_seq = (max_len + block_size - 1) // block_size
         # worst case: every sequence private (no sharing) -> max_batch * blocks
@@ -106,10 +109,16 @@ class LLMGenerator:
         kw = {"workspace": ws} if ws is not None else {}
         kw_down = {"workspace": st["ws_down"]} if "ws_down" in st else kw
         scale = 1.0 / math.sqrt(D)
+        dg = self.decode_gemm
         for li, i in enumerate(m.layers):
             P = f"l{i}."
             o.rmsnorm_fwd(x, m.f32[P + "ln1"], h, None, cfg.rms_eps)
-            if cfg.qkv_bias:
+            if dg:
+                if cfg.qkv_bias:
+                    o.gemm_decode(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS)
+                else:
+                    o.gemm_decode(h, m.s[P + "wqkv"], qkv)
+            elif cfg.qkv_bias:
                 o.gemm(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS, **kw)
             else:
                 o.gemm(h, m.s[P + "wqkv"], qkv, **kw)
@@ -118,10 +127,16 @@ class LLMGenerator:
                        self.vc[li], cfg.n_kv_heads, D, self.bs)
             o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], attn, cfg.n_heads,
                                cfg.n_kv_heads, D, self.bs, scale)
-            o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL, **kw)
-            o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
-            o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
-            o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw_down)
+            if dg:
+                o.gemm_decode(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL)
+                o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
+                o.gemm_decode(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
+                o.gemm_decode(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
+            else:
+                o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL, **kw)
+                o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
+                o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
+                o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw_down)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
         self._sample(st)
@@ -177,7 +192,7 @@ class LLMGenerator:
             "done": torch.zeros(B, device=dev, dtype=torch.uint8),
             "lengths": torch.full((B,), steps, device=dev, dtype=torch.int32),
             "n_done": torch.zeros(1, device=dev, dtype=torch.int32),
-            **self._split_workspace(B),
+            **({} if self.decode_gemm else self._split_workspace(B)),
         }
 
     def _split_workspace(self, B: int) -> dict:
