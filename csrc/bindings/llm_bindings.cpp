@@ -142,7 +142,7 @@ void register_llm_ops(py::module_& m) {
   m.def("gemm_decode", &gemm_decode, py::arg("X"), py::arg("W"), py::arg("C"), py::arg("bias") = py::none(),
         py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("splits") = 0, py::arg("error") = py::none(),
         "C = epi(X W^T) for few tokens: weight-stationary tcgen05 GEMM, K split over a cluster");
-  m.def("gemm_decode_splits", &tb_gemm_decode_splits, py::arg("N"), py::arg("K"));
+  m.def("gemm_decode_splits", &tb_gemm_decode_splits, py::arg("T"), py::arg("N"), py::arg("K"));
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn") = false, py::arg("b_mn") = false,
         py::arg("bias") = py::none(), py::arg("aux") = py::none(), py::arg("epi") = 0, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0f, py::arg("split_k") = 0, py::arg("bn") = 0, py::arg("error") = py::none(),

@@ -2,26 +2,27 @@
 // split over a thread-block cluster and reduced through distributed shared
 // memory.
 //
-//   C[T, N] = epilogue( X[T, K] . W[N, K]^T ),   T tokens (any count; 256 per pass)
+//   C[T, N] = epilogue( X[T, K] . W[N, K]^T ),   T tokens (a few to a few hundred)
 //
-// At decode time T is the number of sequences in the batch (a few hundred)
-// and the projection weight is almost all of the traffic.  The general GEMM
-// (gemm_tcgen05.cu) tiles the output 128 tokens x BN columns, so every tile
-// re-reads its 128 token rows for only BN weight columns, and with few token
-// tiles most SMs idle or stream the same rows again.  Here the operands swap
-// roles:
-//   * the MMA's M side is a 128-row tile of W and its N side is all T tokens
-//     of the pass (N = T rounded up to 16, at most 256), so the weight crosses
-//     from DRAM exactly once and one MMA covers every token;
+// At decode time T is the number of sequences in the batch and the weight is
+// most of the traffic.  The general GEMM (gemm_tcgen05.cu) tiles the output as
+// 128 tokens x BN weight rows; with few token tiles each SM streams a long
+// K range of both operands, and per-SM load throughput (not DRAM) sets the
+// time.  Here the operands swap roles and the work is cut finer:
+//   * a CTA owns 256 weight rows (two M = 128 MMAs that share one token tile)
+//     and a group of TG <= 128 tokens (the MMAs' N side), so one token tile
+//     serves twice the weight rows and the weight crosses from DRAM once;
 //   * K is split over a cluster of S CTAs (grid.x = S; grid.y = weight tiles,
-//     one cluster each): each CTA accumulates its K range in TMEM, copies the
-//     [128 x T] fp32 partial into its own shared memory token-major, and after
-//     a cluster barrier CTA r sums tokens [r T / S, (r + 1) T / S) of all S
-//     partials with ld.shared::cluster and runs the epilogue.  A second cluster
-//     barrier keeps every CTA's shared memory alive until its peers have read
-//     it.  No global workspace, no atomics, one launch.
+//     grid.z = token groups): each CTA accumulates its K range in TMEM, copies
+//     its [256 x TG] fp32 partial into its own shared memory token-major, and
+//     after a cluster barrier CTA r sums tokens [r TG / S, (r + 1) TG / S) over
+//     the S partials with ld.shared::cluster (all S loads in flight) and runs
+//     the epilogue.  A second cluster barrier keeps each CTA's shared memory
+//     alive until its peers have read it.  No global workspace, no atomics.
 //   * epilogues: none, + bias[n], + residual aux[t, n], SwiGLU over
 //     interleaved (gate, up) weight rows; bf16 output, 16-byte stores.
+// The host picks (TG, S) from a per-SM traffic model under the number of
+// clusters that fit on the GPU at once (cudaOccupancyMaxActiveClusters).
 // Warp roles: warp 0 (one thread) issues TMA tile loads (plain loads into this
 // CTA's shared memory) into a 4-stage ring; warp 1 allocates TMEM and one of
 // its threads issues the MMAs; warps 2-5 read TMEM.  All six warps join the
@@ -43,21 +44,21 @@ namespace {
 
 using namespace tb::sm100;
 
-constexpr int kRows = 128;     // weight rows per tile (MMA M)
+constexpr int kRows = 256;     // weight rows per CTA (two MMAs of M = 128)
 constexpr int kBK = 64;        // K per stage (one 128-byte swizzle row of bf16)
-constexpr int kMaxT = 256;     // tokens per pass (MMA N at most 256)
+constexpr int kMaxTG = 128;    // tokens per CTA (the MMAs' N)
 constexpr int kStages = 4;
 constexpr int kThreads = 192;  // warps 0 TMA, 1 MMA + TMEM, 2-5 TMEM readers
 constexpr int kMaxSplits = 8;  // portable cluster size
-constexpr int kWBytes = kRows * kBK * 2;             // 16 KB
-constexpr int kXBytes = kMaxT * kBK * 2;             // 32 KB
+constexpr int kWBytes = kRows * kBK * 2;             // 32 KB
+constexpr int kXBytes = kMaxTG * kBK * 2;            // 16 KB
 constexpr int kStageBytes = kWBytes + kXBytes;       // 48 KB
-constexpr int kBarOffset = kStages * kStageBytes;    // 192 KB; the partial [T][128] fp32 (<= 128 KB) reuses the ring
+constexpr int kBarOffset = kStages * kStageBytes;    // 192 KB; the partial [TG][256] fp32 (<= 128 KB) reuses the ring
 constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers, + slack for 1024-byte alignment
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 256;                  // accumulator a at columns [128 a, 128 a + TG)
 
 struct DecArgs {
-  int T, N, K, t_pad, kb_total;
+  int T, N, K, tg, kb_total;
   int epi;
   const float* bias;
   const __nv_bfloat16* aux;
@@ -72,11 +73,6 @@ __device__ __forceinline__ uint32_t cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ uint32_t cluster_size() {
-  uint32_t n;
-  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
-  return n;
-}
 // Every thread of every CTA in the cluster; release / acquire order the
 // shared-memory writes before the barrier against the peers' reads after it.
 __device__ __forceinline__ void cluster_sync() {
@@ -85,19 +81,42 @@ __device__ __forceinline__ void cluster_sync() {
 // The address of the same shared-memory location in cluster CTA `rank`.
 __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
   uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
   return out;
 }
+// Not volatile: the loads sit between the two cluster barriers (whose asm
+// carries the memory clobber), and the compiler may issue them back to back.
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+// Sum over the S cluster partials of 8 consecutive fp32 at byte offset `off`:
+// every load is issued before the first add.
+template <int S>
+__device__ __forceinline__ void sum_partials(uint32_t base, uint32_t off, float* acc) {
+  float4 x[S], y[S];
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    const uint32_t a = map_to_rank(base + off, static_cast<uint32_t>(s));
+    x[s] = ld_cluster_f4(a);
+    y[s] = ld_cluster_f4(a + 16);
+  }
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    acc[0] += x[s].x;
+    acc[1] += x[s].y;
+    acc[2] += x[s].z;
+    acc[3] += x[s].w;
+    acc[4] += y[s].x;
+    acc[5] += y[s].y;
+    acc[6] += y[s].z;
+    acc[7] += y[s].w;
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, DecArgs p) {
@@ -112,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = static_cast<int>(gridDim.x), split = static_cast<int>(blockIdx.x);
   const int n0 = static_cast<int>(blockIdx.y) * kRows;
+  const int tg = p.tg, t0 = static_cast<int>(blockIdx.z) * tg;
   // balanced K ranges: every split gets at least one k-block (the host keeps S <= kb_total)
   const int kb0 = split * p.kb_total / S, kb1 = (split + 1) * p.kb_total / S;
 
@@ -131,19 +151,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t x_bytes = static_cast<uint32_t>(p.t_pad) * kBK * 2;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
+    const uint32_t bytes = kWBytes + static_cast<uint32_t>(tg) * kBK * 2;
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0, last_par = 0;  // per stage: issued at least once / parity of its last issue
     for (int kb = kb0; kb < kb1; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
       uint8_t* sw = smem + stage * kStageBytes;
-      mbar_arrive_expect_tx(&full[stage], kWBytes + x_bytes);
+      mbar_arrive_expect_tx(&full[stage], bytes);
       tma_load_2d(sw, &tmW, &full[stage], kb * kBK, n0);
-      tma_load_2d(sw + kWBytes, &tmX, &full[stage], kb * kBK, 0);
+      tma_load_2d(sw + kWBytes, &tmX, &full[stage], kb * kBK, t0);
       issued_mask |= 1u << stage;
       last_par = (last_par & ~(1u << stage)) | (phase << stage);
       if (++stage == kStages) {
@@ -155,14 +175,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       // copies still in flight land in this CTA's shared memory: let them finish
       for (int s = 0; s < kStages; ++s) {
         if (!(issued_mask >> s & 1u)) continue;
-        const unsigned long long t0 = global_ns();
-        while (!mbar_try_wait(&full[s], last_par >> s & 1u) && global_ns() - t0 < 100000000ull) {
+        const unsigned long long w0 = global_ns();
+        while (!mbar_try_wait(&full[s], last_par >> s & 1u) && global_ns() - w0 < 100000000ull) {
         }
       }
     }
   } else if (warp == 1 && lane == 0) {
-    // ------------------------------------------------ MMA issuer
-    const uint32_t idesc = idesc_bf16(kRows, p.t_pad, 0, 0);
+    // ------------------------------------------------ MMA issuer: two M = 128 MMAs per K step share the token tile
+    const uint32_t idesc = idesc_bf16(128, tg, 0, 0);
     int stage = 0;
     uint32_t phase = 0;
     bool any = false;
@@ -173,9 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sx = sw + kWBytes;
 #pragma unroll
       for (int kk = 0; kk < kBK / 16; ++kk) {
-        // both operands K-major: +32 bytes per K = 16 step inside the swizzle atom
-        mma_f16(tmem_base, smem_desc_sw128(sw + kk * 32, 16, 1024), smem_desc_sw128(sx + kk * 32, 16, 1024), idesc,
-                (kb > kb0 || kk > 0) ? 1u : 0u);
+        // K-major operands: +32 bytes per K = 16 step inside the swizzle atom;
+        // weight rows 128-255 start 128 rows x 128 bytes into the tile
+        const uint64_t bd = smem_desc_sw128(sx + kk * 32, 16, 1024);
+        const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
+        mma_f16(tmem_base, smem_desc_sw128(sw + kk * 32, 16, 1024), bd, idesc, acc);
+        mma_f16(tmem_base + 128, smem_desc_sw128(sw + 128 * 128 + kk * 32, 16, 1024), bd, idesc, acc);
       }
       mma_commit(&empty[stage]);
       any = true;
@@ -188,18 +211,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (any) mma_commit(done);
     else mbar_arrive(done);
   } else if (warp >= 2) {
-    // ------------------------------------------------ TMEM -> shared memory (token-major partial)
+    // ------------------------------------------------ TMEM -> shared memory (token-major partial [tg][256])
     const int q = warp & 3;  // this warp's TMEM lane quarter
-    const int row = q * 32 + lane;
     const bool ok = mbar_wait(done, 0, abort_flag);
     tc_fence_after();
     float* part = reinterpret_cast<float*>(smem);
-    for (int c = 0; c < p.t_pad; c += 32) {
-      float v[32];
-      tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c), v);
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c + j < p.T) part[(c + j) * kRows + row] = ok ? v[j] : 0.f;
+    for (int a = 0; a < 2; ++a) {
+      const int row = a * 128 + q * 32 + lane;
+      for (int c = 0; c < tg; c += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(a * 128 + c), v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c + j < tg) part[(c + j) * kRows + row] = ok ? v[j] : 0.f;
+      }
     }
   }
   tc_fence_before();
@@ -213,36 +239,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------------------------ cluster reduction + epilogue
   cluster_sync();
   {
-    const uint32_t r = cluster_rank(), ns = cluster_size();
-    const int tc = (p.T + static_cast<int>(ns) - 1) / static_cast<int>(ns);
-    const int t_lo = static_cast<int>(r) * tc, t_hi = min(p.T, t_lo + tc);
-    const int items = max(0, t_hi - t_lo) * (kRows / 8);
+    const int r = static_cast<int>(cluster_rank());
+    const int valid = min(tg, p.T - t0);  // real tokens of this group
+    const int tc = (valid + S - 1) / S;
+    const int t_lo = r * tc, t_hi = min(valid, t_lo + tc);
+    constexpr int kGroups = kRows / 8;
+    const int items = max(0, t_hi - t_lo) * kGroups;
     const uint32_t part_base = smem_u32(smem);
     for (int it = threadIdx.x; it < items; it += kThreads) {
-      const int t = t_lo + it / (kRows / 8), g = it % (kRows / 8);
+      const int tl = t_lo + it / kGroups, g = it % kGroups;
       const int n = n0 + g * 8;
-      const uint32_t off = static_cast<uint32_t>((t * kRows + g * 8) * 4);
+      const uint32_t off = static_cast<uint32_t>((tl * kRows + g * 8) * 4);
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (uint32_t s = 0; s < ns; ++s) {
-        const uint32_t a = map_to_rank(part_base + off, s);
-        const float4 x = ld_cluster_f4(a), y = ld_cluster_f4(a + 16);
-        acc[0] += x.x;
-        acc[1] += x.y;
-        acc[2] += x.z;
-        acc[3] += x.w;
-        acc[4] += y.x;
-        acc[5] += y.y;
-        acc[6] += y.z;
-        acc[7] += y.w;
+      switch (S) {
+        case 1: sum_partials<1>(part_base, off, acc); break;
+        case 2: sum_partials<2>(part_base, off, acc); break;
+        case 3: sum_partials<3>(part_base, off, acc); break;
+        case 4: sum_partials<4>(part_base, off, acc); break;
+        case 5: sum_partials<5>(part_base, off, acc); break;
+        case 6: sum_partials<6>(part_base, off, acc); break;
+        case 7: sum_partials<7>(part_base, off, acc); break;
+        default: sum_partials<8>(part_base, off, acc); break;
       }
       if (n >= p.N) continue;
+      const long long t = t0 + tl;
       if (p.epi == TB_EPI_SWIGLU) {
         // weight rows (2j, 2j + 1) are (gate, up) of output column j
         uint2 pk;
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
         h[0] = __floats2bfloat162_rn(silu(acc[0]) * acc[1], silu(acc[2]) * acc[3]);
         h[1] = __floats2bfloat162_rn(silu(acc[4]) * acc[5], silu(acc[6]) * acc[7]);
-        *reinterpret_cast<uint2*>(p.C + static_cast<long long>(t) * p.ldc + n / 2) = pk;
+        *reinterpret_cast<uint2*>(p.C + t * p.ldc + n / 2) = pk;
         continue;
       }
       if (p.epi == TB_EPI_BIAS) {
@@ -257,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc[6] += b1.z;
         acc[7] += b1.w;
       } else if (p.epi == TB_EPI_RESIDUAL) {
-        const uint4 a = *reinterpret_cast<const uint4*>(p.aux + static_cast<long long>(t) * p.ld_aux + n);
+        const uint4 a = *reinterpret_cast<const uint4*>(p.aux + t * p.ld_aux + n);
         const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&a);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -270,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
       for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
-      *reinterpret_cast<uint4*>(p.C + static_cast<long long>(t) * p.ldc + n) = pk;
+      *reinterpret_cast<uint4*>(p.C + t * p.ldc + n) = pk;
     }
   }
   // no CTA leaves (and frees its shared memory) while a peer may still read it
@@ -309,24 +336,81 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long cols, 
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-  int dev = 0, n = 0;
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Clusters of size s that can be resident at once (one CTA per SM at this
+// kernel's shared memory), per device.
+int cluster_capacity(int s) {
+  static std::mutex mu;
+  static int cache[64][kMaxSplits + 1] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  return n > 0 ? n : 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) dev = 0;
+  int& c = cache[dev][s];
+  if (c == 0) {
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    int n = 0;
+    if (tb::ensure_dyn_smem(reinterpret_cast<const void*>(gemm_decode_kernel), kSmemBytes) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(s, 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = s;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(gemm_decode_kernel), &cfg) != cudaSuccess)
+        n = 0;
+      cudaGetLastError();
+    }
+    c = n > 0 ? n : sms / s;
+  }
+  return c;
 }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+struct DecPlan {
+  int tg, splits;
+};
+
+// Per-SM load model: a CTA streams ceil(kb / S) k-blocks of (256 weight rows
+// + TG token rows) x 128 bytes, and with S > 1 reads its share of the S fp32
+// partials (256 x TG x 4 bytes, mostly remote); clusters beyond what fits at
+// once run in further waves.  The cheapest (TG, S) wins.
+DecPlan plan(int T, int N, int K, int splits) {
+  const int tiles = (N + kRows - 1) / kRows, kb = (K + kBK - 1) / kBK;
+  const int t16 = (T + 15) / 16 * 16;
+  DecPlan best{t16 < kMaxTG ? t16 : kMaxTG, 1};
+  double best_cost = 1e300;
+  for (int tg = 16; tg <= kMaxTG; tg *= 2) {
+    const int tgc = tg < t16 ? tg : t16;  // never wider than the (padded) token count
+    const int groups = (T + tgc - 1) / tgc;
+    const int s_lo = splits > 0 ? splits : 1, s_hi = splits > 0 ? splits : (kb < kMaxSplits ? kb : kMaxSplits);
+    for (int s = s_lo; s <= s_hi; ++s) {
+      const long long clusters = static_cast<long long>(tiles) * groups;
+      const long long cap = cluster_capacity(s);
+      const long long waves = (clusters + cap - 1) / cap;
+      const double per_cta = static_cast<double>((kb + s - 1) / s) * (kWBytes + tgc * kBK * 2) +
+                             (s > 1 ? 4.0 * kRows * tgc : 0.0) + 32768.0;  // + fixed setup, in bytes
+      const double cost = waves * per_cta;
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = DecPlan{tgc, s};
+      }
+    }
+    if (tgc == t16) break;
+  }
+  return best;
+}
 
 }  // namespace
 
-int tb_gemm_decode_splits(int N, int K) {
-  const int tiles = (N + kRows - 1) / kRows, kb = (K + kBK - 1) / kBK;
-  int s = sm_count() / (tiles > 0 ? tiles : 1);
-  if (s > kMaxSplits) s = kMaxSplits;
-  if (s > kb) s = kb;
-  return s < 1 ? 1 : s;
-}
+int tb_gemm_decode_splits(int T, int N, int K) { return plan(T, N, K, 0).splits; }
 
 int tb_gemm_decode(const TbDecodeGemmArgs* a, cudaStream_t stream) {
   if (a == nullptr || a->T < 0 || a->N <= 0 || a->K <= 0) return static_cast<int>(cudaErrorInvalidValue);
@@ -343,47 +427,38 @@ int tb_gemm_decode(const TbDecodeGemmArgs* a, cudaStream_t stream) {
   if (epi == TB_EPI_RESIDUAL && (a->aux == nullptr || a->ld_aux % 8 || !aligned16(a->aux)))
     return static_cast<int>(cudaErrorInvalidValue);
   const int kb_total = (a->K + kBK - 1) / kBK;
-  int S = a->splits > 0 ? a->splits : tb_gemm_decode_splits(a->N, a->K);
-  if (S > kMaxSplits || S > kb_total) return static_cast<int>(cudaErrorInvalidValue);
-  CUtensorMap tw;
-  if (!make_map(&tw, a->W, a->N, a->K, a->ldw, kRows)) return static_cast<int>(cudaErrorInvalidValue);
+  if (a->splits < 0 || a->splits > kMaxSplits || a->splits > kb_total) return static_cast<int>(cudaErrorInvalidValue);
   cudaError_t e = tb::ensure_dyn_smem(reinterpret_cast<const void*>(gemm_decode_kernel), kSmemBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  const int tiles = (a->N + kRows - 1) / kRows;
-  for (int t0 = 0; t0 < a->T; t0 += kMaxT) {
-    const int T = a->T - t0 < kMaxT ? a->T - t0 : kMaxT;
-    const int t_pad = (T + 15) / 16 * 16;
-    CUtensorMap tx;
-    const __nv_bfloat16* X = static_cast<const __nv_bfloat16*>(a->X) + static_cast<long long>(t0) * a->ldx;
-    if (!make_map(&tx, X, T, a->K, a->ldx, t_pad)) return static_cast<int>(cudaErrorInvalidValue);
-    DecArgs p{};
-    p.T = T;
-    p.N = a->N;
-    p.K = a->K;
-    p.t_pad = t_pad;
-    p.kb_total = kb_total;
-    p.epi = epi;
-    p.bias = a->bias;
-    p.aux = epi == TB_EPI_RESIDUAL ? static_cast<const __nv_bfloat16*>(a->aux) + static_cast<long long>(t0) * a->ld_aux
-                                   : nullptr;
-    p.ld_aux = a->ld_aux;
-    p.C = static_cast<__nv_bfloat16*>(a->C) + static_cast<long long>(t0) * a->ldc;
-    p.ldc = a->ldc;
-    p.err = a->error;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(S, tiles, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = S;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, tx, p);
-    if (e != cudaSuccess) return static_cast<int>(e);
-  }
-  return 0;
+  const DecPlan pl = plan(a->T, a->N, a->K, a->splits);
+  CUtensorMap tw, tx;
+  if (!make_map(&tw, a->W, a->N, a->K, a->ldw, kRows) || !make_map(&tx, a->X, a->T, a->K, a->ldx, pl.tg))
+    return static_cast<int>(cudaErrorInvalidValue);
+  DecArgs p{};
+  p.T = a->T;
+  p.N = a->N;
+  p.K = a->K;
+  p.tg = pl.tg;
+  p.kb_total = kb_total;
+  p.epi = epi;
+  p.bias = a->bias;
+  p.aux = static_cast<const __nv_bfloat16*>(a->aux);
+  p.ld_aux = a->ld_aux;
+  p.C = static_cast<__nv_bfloat16*>(a->C);
+  p.ldc = a->ldc;
+  p.err = a->error;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, (a->N + kRows - 1) / kRows, (a->T + pl.tg - 1) / pl.tg);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = pl.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, tx, p);
+  return static_cast<int>(e);
 }

@@ -205,7 +205,7 @@ int tb_gemm_bf16(const TbGemmArgs* args, cudaStream_t s);
 // output; epi is TB_EPI_NONE, TB_EPI_BIAS (fp32 [N]), TB_EPI_RESIDUAL (aux bf16
 // [T, N]) or TB_EPI_SWIGLU (interleaved gate / up rows of W, C [T, N / 2]).
 // N, K and every leading dimension a multiple of 8, base pointers 16-byte
-// aligned; any T (256 tokens per launch).
+// aligned; any T.
 typedef struct {
   const void* X;
   long long ldx;
@@ -223,8 +223,8 @@ typedef struct {
 } TbDecodeGemmArgs;
 
 int tb_gemm_decode(const TbDecodeGemmArgs* args, cudaStream_t s);
-// The automatic split count for an [N, K] weight.
-int tb_gemm_decode_splits(int N, int K);
+// The automatic split count (cluster size) for T tokens and an [N, K] weight.
+int tb_gemm_decode_splits(int T, int N, int K);
 // PPO output layer + clipped loss + output-layer backward in one pass over the
 // hidden activations H2 = [H2a | H2c] (bf16 [M, 2H]); categorical actor with A
 // actions.  W3 bf16 [>= crow + 1, 2H] (actor rows 0..A-1 over columns [0, H),

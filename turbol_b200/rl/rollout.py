@@ -37,15 +37,18 @@ from ..models.llm import DecoderLM, LMConfig
 
 class LLMGenerator:
     def __init__(self, model: DecoderLM, max_batch: int, max_len: int, block_size: int = 16, seed: int = 0,
-                 cuda_graph: bool = True, decode_gemm: bool = False):
+                 cuda_graph: bool = True, decode_gemm: Optional[bool] = None):
         self.m = model
         self.cfg = model.cfg
         self.device = model.device
         self.max_batch, self.max_len, self.bs = max_batch, max_len, block_size
         self.seed = seed
         self.cuda_graph = cuda_graph
-        # the layer projections of a decode step on the weight-stationary decode
-        # GEMM (gemm_decode.cu); False: the general tcgen05 GEMM
+        # which layer projections of a decode step run on the weight-stationary
+        # decode GEMM (gemm_decode.cu) instead of the general tcgen05 GEMM:
+        # None = by batch size as measured on B200 (all four up to 64
+        # sequences; beyond that the down projection only, the general GEMM
+        # being as fast or faster for QKV, O and gate/up); True / False = all / none
         self.decode_gemm = decode_gemm
         cfg = self.cfg
         self.blocks_per_seq = (max_len + block_size - 1) // block_size
@@ -109,7 +112,7 @@ class LLMGenerator:
         kw = {"workspace": ws} if ws is not None else {}
         kw_down = {"workspace": st["ws_down"]} if "ws_down" in st else kw
         scale = 1.0 / math.sqrt(D)
-        dg = self.decode_gemm
+        dg, dg_down = self._decode_gemm_use(B)
         for li, i in enumerate(m.layers):
             P = f"l{i}."
             o.rmsnorm_fwd(x, m.f32[P + "ln1"], h, None, cfg.rms_eps)
@@ -131,11 +134,13 @@ class LLMGenerator:
                 o.gemm_decode(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL)
                 o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
                 o.gemm_decode(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
-                o.gemm_decode(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
             else:
                 o.gemm(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL, **kw)
                 o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
                 o.gemm(h, m.s[P + "wgu"], act, epi=o.EPI_SWIGLU)
+            if dg_down:
+                o.gemm_decode(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL)
+            else:
                 o.gemm(act, m.s[P + "wdown"], x, aux=x2, epi=o.EPI_RESIDUAL, **kw_down)
         o.rmsnorm_fwd(x, m.f32["norm"], h, None, cfg.rms_eps)
         o.gemm(h, m.head_weight(), st["logits"])
@@ -192,11 +197,21 @@ class LLMGenerator:
             "done": torch.zeros(B, device=dev, dtype=torch.uint8),
             "lengths": torch.full((B,), steps, device=dev, dtype=torch.int32),
             "n_done": torch.zeros(1, device=dev, dtype=torch.int32),
-            **({} if self.decode_gemm else self._split_workspace(B)),
+            **self._split_workspace(B),
         }
 
+    def _decode_gemm_use(self, B: int):
+        """(QKV / O / gate-up on the decode GEMM, down projection on it)."""
+        if self.decode_gemm is not None:
+            return bool(self.decode_gemm), bool(self.decode_gemm)
+        return B <= 64, True
+
     def _split_workspace(self, B: int) -> dict:
+        """Split-K partials of the general GEMM, for the projections it runs."""
         o, cfg = _ops(), self.cfg
+        dg, dg_down = self._decode_gemm_use(B)
+        if (B > 64 and dg_down) or (B <= 64 and dg):
+            return {}
         if B > 64:
             # many sequences: only the down projection (long K = ffn, few output
             # tiles) gains from splitting K; the others keep the narrow-tile plan
@@ -434,6 +449,7 @@ class TPLLMGenerator(LLMGenerator):
         self.max_batch, self.max_len, self.bs = max_batch, max_len, block_size
         self.seed = seed
         self.cuda_graph = cuda_graph
+        self.decode_gemm = False  # the projections are the fused TP collectives
         self.blocks_per_seq = (max_len + block_size - 1) // block_size
         self.num_blocks = max_batch * self.blocks_per_seq + 1
         self.kv = _core().KVBlockManager(self.num_blocks, block_size)
