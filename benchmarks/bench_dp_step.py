@@ -12,6 +12,9 @@ slower of (the step's HBM bytes at the measured copy bandwidth) and (the
 bytes this rank sends over NVLink at 770 GB/s per direction):
 each rank sends, per element, (W-1)/W of its gradient (4 B) to the owners, and
 the owner sends its updated fp32 weight (4 B) and bf16 copy (2 B) to W-1 peers.
+For vectors up to REPLICATED_MAX_NUMEL the replicated one-handshake step is
+timed too (every rank reads the W-1 peers' whole gradients, 4 B each, and
+updates the whole vector locally).
 """
 import argparse
 import datetime
@@ -25,7 +28,7 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from turbol_b200.ops.rl import FusedAdam  # noqa: E402
-from turbol_b200.parallel.peer import FusedDataParallelAdam  # noqa: E402
+from turbol_b200.parallel.peer import REPLICATED_MAX_NUMEL, FusedDataParallelAdam  # noqa: E402
 
 
 def main():
@@ -55,12 +58,20 @@ def main():
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         return ms.item()
 
-    opt = FusedDataParallelAdam(n, None, lr=1e-6)
+    opt = FusedDataParallelAdam(n, None, lr=1e-6, replicated=False)
     opt.grad.normal_()
     fused_ms = timed(opt.step)
     opt.check()
     del opt
     torch.cuda.empty_cache()
+    rep_ms = None
+    if n <= REPLICATED_MAX_NUMEL:  # the one-handshake step (every rank pulls every gradient, full Adam)
+        opt = FusedDataParallelAdam(n, None, lr=1e-6, replicated=True)
+        opt.grad.normal_()
+        rep_ms = timed(opt.step)
+        opt.check()
+        del opt
+        torch.cuda.empty_cache()
     p = torch.zeros(n, device=dev)
     g = torch.randn(n, device=dev)
     sh = torch.zeros(n, device=dev, dtype=torch.bfloat16)
@@ -79,7 +90,9 @@ def main():
         hbm_bytes = n / world * (4 * world + 16 + 8 + 6 * world)
         roof_ms = max(nvlink_bytes / link, hbm_bytes / 6.56e12) * 1e3
         print(json.dumps({"benchmark": "dp_optimizer_step", "world": world, "numel": n,
-                          "fused_ms": fused_ms, "nccl_allreduce_plus_adam_ms": nccl_ms,
+                          "fused_ms": fused_ms, "fused_replicated_ms": rep_ms,
+                          "replicated_nvlink_bytes_per_rank": n * 4 * (world - 1),
+                          "nccl_allreduce_plus_adam_ms": nccl_ms,
                           "roofline_ms": roof_ms, "fused_frac_of_roofline": roof_ms / fused_ms,
                           "nvlink_bytes_per_rank": nvlink_bytes, "timing": "CUDA events, max over ranks"}))
     dist.barrier()

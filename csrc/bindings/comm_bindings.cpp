@@ -237,5 +237,19 @@ void register_comm_ops(py::module_& m) {
                                             reinterpret_cast<const long long*>(step.data_ptr<int64_t>()),
                                             p.DoneCounter(), p.ErrorWord(), cur_stream(p.device())),
                      "peer_allreduce_adam");
+           })
+      .def("allreduce_adam_rep",
+           [](PeerMemory& p, int64_t grad_off, int64_t send_off, int64_t param_off, int64_t shadow_off, int64_t n,
+              at::Tensor m1, at::Tensor m2, float lr, float b1, float b2, float eps, float wd, float grad_scale,
+              at::Tensor step) {
+             if (!m1.is_cuda() || m1.scalar_type() != at::kFloat || m1.numel() < n || !m2.is_cuda() ||
+                 m2.scalar_type() != at::kFloat || m2.numel() < n || step.scalar_type() != at::kLong)
+               throw std::invalid_argument("allreduce_adam_rep: m and v must be fp32 CUDA tensors of the whole vector");
+             TbAdamParams hp{lr, b1, b2, eps, wd, grad_scale, 0.f, 0};
+             cuda_ok(tb_peer_allreduce_adam_rep(p.Table(), grad_off, send_off, param_off, shadow_off, n,
+                                                m1.data_ptr<float>(), m2.data_ptr<float>(), hp,
+                                                reinterpret_cast<const long long*>(step.data_ptr<int64_t>()),
+                                                p.RepEpoch(), p.DoneCounter(), p.ErrorWord(), cur_stream(p.device())),
+                     "peer_allreduce_adam_rep");
            });
 }

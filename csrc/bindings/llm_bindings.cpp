@@ -253,6 +253,23 @@ void register_llm_ops(py::module_& m) {
                         vc.data_ptr(), static_cast<int>(qkv.size(0)), Hk, D, bs, turbol::StreamFor(qkv)),
             "kv_write");
   });
+  m.def("rope_kv_write", [=](at::Tensor qkv, at::Tensor pos, at::Tensor table, int Hq, int Hk, int D,
+                             at::Tensor seq_of_token, at::Tensor block_table, at::Tensor kc, at::Tensor vc, int bs) {
+    bf16_2d(qkv, "qkv");
+    i32c(pos, "pos");
+    f32c(table, "table");
+    i32c(seq_of_token, "seq_of_token");
+    i32c(block_table, "block_table");
+    chk(pos.numel() == qkv.size(0) && seq_of_token.numel() == qkv.size(0), "rope_kv_write: one position per row");
+    chk(qkv.size(1) >= static_cast<int64_t>(Hq + 2 * Hk) * D, "rope_kv_write: qkv narrower than (Hq + 2 Hk) D");
+    chk(kc.scalar_type() == at::kBFloat16 && vc.scalar_type() == at::kBFloat16 && kc.is_contiguous() &&
+            vc.is_contiguous(), "rope_kv_write: bf16 contiguous caches");
+    cuda_ok(tb_rope_kv_write(qkv.data_ptr(), qkv.stride(0), pos.data_ptr<int>(), table.data_ptr<float>(), Hq, Hk, D,
+                             seq_of_token.data_ptr<int>(), block_table.data_ptr<int>(),
+                             static_cast<int>(block_table.size(1)), kc.data_ptr(), vc.data_ptr(),
+                             static_cast<int>(qkv.size(0)), bs, turbol::StreamFor(qkv)),
+            "rope_kv_write");
+  });
   m.def("decode_attention", [=](at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table,
                                 at::Tensor ctx_len, at::Tensor out, int Hq, int Hk, int D, int bs, float scale) {
     bf16_2d(q, "q");

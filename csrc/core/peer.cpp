@@ -87,6 +87,7 @@ TbPeerTable PeerMemory::Table() const {
 
 unsigned* PeerMemory::DoneCounter() const { return reinterpret_cast<unsigned*>(static_cast<char*>(counters_) + 64); }
 int* PeerMemory::ErrorWord() const { return reinterpret_cast<int*>(static_cast<char*>(counters_) + 128); }
+unsigned* PeerMemory::RepEpoch() const { return reinterpret_cast<unsigned*>(static_cast<char*>(counters_) + 192); }
 void* PeerMemory::Payload() const { return static_cast<char*>(local_) + header_bytes_; }
 
 }  // namespace turbol

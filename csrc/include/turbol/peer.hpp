@@ -22,6 +22,9 @@ class PeerMemory {
   TbPeerTable Table() const;
   unsigned* DoneCounter() const;
   int* ErrorWord() const;
+  // Epoch of the replicated-Adam step (its own sequence, separate from the
+  // other collectives on this buffer).
+  unsigned* RepEpoch() const;
   void* Payload() const;  // local payload base (device pointer)
   size_t PayloadBytes() const { return total_bytes_ - header_bytes_; }
   int rank() const { return rank_; }

@@ -31,6 +31,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstddef>
+
 #include "device_common.cuh"
 #include "kernels.h"
 
@@ -50,8 +52,23 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Warp 0 (converged, all 32 lanes) stores `epoch` into every rank's flag at
+// byte offset `off` of its header: lane p stores rank p's flag after its own
+// system-scope fence (fence + relaxed store = a release).  One NVLink round
+// trip for all ranks, where a release store per rank from one thread waits
+// for each previous one to be performed.  The caller's __syncthreads orders
+// the block's writes before the fences.
+__device__ __forceinline__ void publish_all(const TbPeerTable& t, size_t off, unsigned epoch) {
+  const int lane = threadIdx.x & 31;
+  if (lane < t.world) {
+    __threadfence_system();
+    st_relaxed(reinterpret_cast<unsigned*>(static_cast<char*>(t.hdr[lane]) + off), epoch);
+  }
+  __syncwarp();
 }
 
 // Waits until flags[0..W) (local memory, written by peers) all reach `epoch`.
@@ -71,9 +88,16 @@ __device__ bool wait_all(const unsigned* flags, int W, unsigned epoch, int* err,
   return true;
 }
 
+// Blocks of the replicated-Adam step (one slice of the vector each; every
+// rank runs the same grid, so block b of every rank owns the same slice).
+constexpr int kRepBlocks = 148;
+
 struct Hdr {
   unsigned flags_in[TB_MAX_PEERS];   // "peer p's inputs are ready" (epoch)
   unsigned flags_out[TB_MAX_PEERS];  // "peer p finished writing its outputs into me" (epoch)
+  // replicated-Adam step, per block slice b (its own epoch sequence):
+  unsigned rep_ready[kRepBlocks][TB_MAX_PEERS];  // "peer p's send slice b is ready"
+  unsigned rep_read[kRepBlocks][TB_MAX_PEERS];   // "peer p has finished reading my send slice b"
 };
 
 // Slice [lo, hi) of n elements owned by `rank`, rounded to multiples of 4
@@ -89,16 +113,17 @@ __host__ __device__ __forceinline__ void owned_slice(long long n, int rank, int 
 
 __device__ void publish_and_finish(const TbPeerTable& t, unsigned epoch, unsigned* done_ctr, int* err) {
   // every block: make this block's peer stores visible, then count in
+  __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
-    const unsigned prev = atomicAdd(done_ctr, 1u);
-    if (prev == gridDim.x - 1) {  // last block of this rank
-      *done_ctr = 0;
-      for (int p = 0; p < t.world; ++p) {
-        Hdr* h = reinterpret_cast<Hdr*>(t.hdr[p]);
-        st_release(&h->flags_out[t.rank], epoch);
-      }
+    s_last = atomicAdd(done_ctr, 1u) == gridDim.x - 1 ? 1 : 0;  // the last block of this rank
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x < 32) {
+    if (threadIdx.x == 0) *done_ctr = 0;
+    publish_all(t, offsetof(Hdr, flags_out) + t.rank * sizeof(unsigned), epoch);
+    if (threadIdx.x == 0) {
       wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_out, t.world, epoch, err, 2);
       *t.epoch_ctr = epoch;  // next call uses epoch + 1
     }
@@ -108,13 +133,13 @@ __device__ void publish_and_finish(const TbPeerTable& t, unsigned epoch, unsigne
 __device__ unsigned begin_call(const TbPeerTable& t, int* err, bool* ok) {
   const unsigned epoch = *t.epoch_ctr + 1;
   __shared__ int s_ok;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
     // every block publishes "this rank's inputs are ready" (the same epoch,
     // idempotent), so no block waits on another block of its own grid being
     // scheduled: the only waits are on other ranks
-    __threadfence_system();
-    for (int p = 0; p < t.world; ++p) st_release(&reinterpret_cast<Hdr*>(t.hdr[p])->flags_in[t.rank], epoch);
-    s_ok = wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_in, t.world, epoch, err, 1) ? 1 : 0;
+    publish_all(t, offsetof(Hdr, flags_in) + t.rank * sizeof(unsigned), epoch);
+    if (threadIdx.x == 0)
+      s_ok = wait_all(reinterpret_cast<Hdr*>(t.hdr[t.rank])->flags_in, t.world, epoch, err, 1) ? 1 : 0;
   }
   __syncthreads();
   *ok = s_ok != 0;
@@ -260,6 +285,110 @@ __global__ void __launch_bounds__(kBlock) allreduce_adam_kernel(TbPeerTable t, l
   publish_and_finish(t, epoch, done_ctr, err);
 }
 
+// Data-parallel optimizer step with one handshake, for small vectors (the
+// PPO minibatch step, ~0.6 MB, is latency-bound).  Every rank pulls every
+// peer's whole gradient and runs Adam on the whole vector itself (full-size
+// moments on every rank; the sum runs in rank order on every rank, so the
+// ranks' weights stay bit-identical), so no updated weights cross NVLink and
+// nothing waits for the peers at the end of the call.  Block b of every rank
+// owns slice b:
+//   1. wait until every peer has finished reading my send slice b of the
+//      previous call (set long ago in practice: a local flag read);
+//   2. copy my gradient slice into my send buffer (a snapshot, so the next
+//      backward may overwrite the gradient while peers still read);
+//   3. publish "slice b ready" into every peer, wait for every peer's;
+//   4. sum the slice over the peers' send buffers, Adam, write the local fp32
+//      weights and bf16 copy;
+//   5. tell every peer "I have read your slice b".
+// The epoch advances once per call (the last block to finish, locally).
+__global__ void __launch_bounds__(kBlock) allreduce_adam_rep_kernel(TbPeerTable t, long long grad_off,
+                                                                    long long send_off, long long param_off,
+                                                                    long long shadow_off, long long n, float* m,
+                                                                    float* v, TbAdamParams hp,
+                                                                    const long long* step_ptr, unsigned* rep_epoch,
+                                                                    unsigned* done_ctr, int* err) {
+  const unsigned epoch = *rep_epoch + 1;
+  const int b = blockIdx.x;
+  Hdr* mine = reinterpret_cast<Hdr*>(t.hdr[t.rank]);
+  const long long n4 = (n + 3) / 4, per = (n4 + gridDim.x - 1) / gridDim.x;
+  const long long lo = min(n, b * per * 4), hi = min(n, (b + 1) * per * 4);
+  const float* grad = reinterpret_cast<const float*>(static_cast<const char*>(t.base[t.rank]) + grad_off);
+  float* send = reinterpret_cast<float*>(static_cast<char*>(t.base[t.rank]) + send_off);
+  float* param = reinterpret_cast<float*>(static_cast<char*>(t.base[t.rank]) + param_off);
+  __nv_bfloat16* shadow = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(t.base[t.rank]) + shadow_off);
+  __shared__ int s_ok;
+  // 1. my previous send slice has been read by everyone
+  if (threadIdx.x == 0) s_ok = wait_all(mine->rep_read[b], t.world, epoch - 1, err, 21) ? 1 : 0;
+  __syncthreads();
+  bool ok = s_ok != 0;
+  // 2. snapshot of my gradient slice
+  if (ok) {
+    for (long long i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+      if (i + 4 <= hi) {
+        *reinterpret_cast<float4*>(send + i) = *reinterpret_cast<const float4*>(grad + i);
+      } else {
+        for (long long j = i; j < hi; ++j) send[j] = grad[j];
+      }
+    }
+  }
+  // 3. publish it; wait for everyone's
+  __syncthreads();
+  if (ok && threadIdx.x < 32) {
+    publish_all(t, offsetof(Hdr, rep_ready) + (static_cast<size_t>(b) * TB_MAX_PEERS + t.rank) * sizeof(unsigned),
+                epoch);
+    if (threadIdx.x == 0) s_ok = wait_all(mine->rep_ready[b], t.world, epoch, err, 22) ? 1 : 0;
+  }
+  __syncthreads();
+  ok = ok && s_ok != 0;
+  // 4. reduce in rank order + Adam on the whole slice, local writes only
+  if (ok) {
+    const long long step = (step_ptr ? *step_ptr : hp.step) + 1;
+    const float bc1 = 1.f - powf(hp.beta1, static_cast<float>(step));
+    const float bc2 = 1.f - powf(hp.beta2, static_cast<float>(step));
+    const float gs = hp.grad_scale;
+    for (long long i = lo + threadIdx.x * 4; i < hi; i += blockDim.x * 4) {
+      const int cnt = static_cast<int>(min(4LL, hi - i));
+      float g[4] = {0.f, 0.f, 0.f, 0.f};
+      if (cnt == 4) {
+        const float4 x = sum_peers4(t, send_off, i);
+        g[0] = x.x;
+        g[1] = x.y;
+        g[2] = x.z;
+        g[3] = x.w;
+      } else {
+        for (int p = 0; p < t.world; ++p) {
+          const float* src = reinterpret_cast<const float*>(static_cast<const char*>(t.base[p]) + send_off) + i;
+          for (int j = 0; j < cnt; ++j) g[j] += src[j];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j < cnt) {
+          float pv = param[i + j], mm = m[i + j], vv = v[i + j];
+          adam1(pv, g[j] * gs, mm, vv, hp, bc1, bc2);
+          param[i + j] = pv;
+          m[i + j] = mm;
+          v[i + j] = vv;
+          shadow[i + j] = __float2bfloat16_rn(pv);
+        }
+      }
+    }
+  }
+  // 5. done reading every peer's slice b
+  __syncthreads();
+  if (ok && threadIdx.x < 32)
+    publish_all(t, offsetof(Hdr, rep_read) + (static_cast<size_t>(b) * TB_MAX_PEERS + t.rank) * sizeof(unsigned),
+                epoch);
+  if (threadIdx.x == 0) {
+    // the last block of this rank advances the epoch (a local counter)
+    __threadfence();
+    if (atomicAdd(done_ctr, 1u) == gridDim.x - 1) {
+      *done_ctr = 0;
+      *rep_epoch = epoch;
+    }
+  }
+}
+
 // Scatter all-gather with a layout change (the trainer -> rollout weight sync
 // of a tensor-parallel trainer with a full-model rollout copy on every rank).
 // Segment k copies `rows` rows of `row_bytes` from this rank's source buffer
@@ -364,6 +493,21 @@ int tb_peer_allreduce_adam(TbPeerTable t, long long grad_off, long long param_of
     return static_cast<int>(cudaErrorInvalidValue);
   allreduce_adam_kernel<<<grid_for(n, t.world), kBlock, 0, s>>>(t, grad_off, param_off, shadow_off, n, m, v, hp,
                                                                 step_ptr, done_ctr, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int tb_peer_allreduce_adam_rep(TbPeerTable t, long long grad_off, long long send_off, long long param_off,
+                               long long shadow_off, long long n, float* m, float* v, TbAdamParams hp,
+                               const long long* step_ptr, unsigned* rep_epoch, unsigned* done_ctr, int* err,
+                               cudaStream_t s) {
+  if (t.world < 1 || t.world > TB_MAX_PEERS || n <= 0 || (grad_off & 15) || (send_off & 15) || (param_off & 15) ||
+      (shadow_off & 7))
+    return static_cast<int>(cudaErrorInvalidValue);
+  // one float4 per thread where possible; the same grid on every rank (it depends on n only)
+  long long g = ((n + 3) / 4 + kBlock - 1) / kBlock;
+  if (g > kRepBlocks) g = kRepBlocks;
+  allreduce_adam_rep_kernel<<<static_cast<int>(g), kBlock, 0, s>>>(t, grad_off, send_off, param_off, shadow_off, n, m,
+                                                                   v, hp, step_ptr, rep_epoch, done_ctr, err);
   return static_cast<int>(cudaGetLastError());
 }
 

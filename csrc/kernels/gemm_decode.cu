@@ -38,6 +38,7 @@
 
 #include "device_common.cuh"
 #include "kernels.h"
+#include "pdl.cuh"
 #include "sm100_primitives.cuh"
 
 namespace {
@@ -155,10 +156,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
     const uint32_t bytes = kWBytes + static_cast<uint32_t>(tg) * kBK * 2;
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, last_par = 0;  // per stage: issued at least once / parity of its last issue
-    for (int kb = kb0; kb < kb1; ++kb) {
+    // The weight is constant: the first ring's weight tiles load before the
+    // wait for the preceding kernel (which may still be running under PDL);
+    // the token tiles (its output) only after it.
+    const int pre = min(kStages, kb1 - kb0);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], bytes);
+      tma_load_2d(smem + i * kStageBytes, &tmW, &full[i], (kb0 + i) * kBK, n0);
+    }
+    tb::pdl_wait();
+    tb::pdl_trigger();
+    for (int i = 0; i < pre; ++i) tma_load_2d(smem + i * kStageBytes + kWBytes, &tmX, &full[i], (kb0 + i) * kBK, t0);
+    uint32_t issued_mask = (1u << pre) - 1u, last_par = 0;  // per stage: issued at least once / parity of its last issue
+    int stage = pre % kStages;
+    uint32_t phase = pre == kStages ? 1u : 0u;
+    for (int kb = kb0 + pre; kb < kb1; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) break;
       uint8_t* sw = smem + stage * kStageBytes;
       mbar_arrive_expect_tx(&full[stage], bytes);
@@ -238,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------ cluster reduction + epilogue
   cluster_sync();
+  tb::pdl_wait();  // the epilogue reads aux / bias and writes C: after the preceding kernel
   {
     const int r = static_cast<int>(cluster_rank());
     const int valid = min(tg, p.T - t0);  // real tokens of this group
@@ -459,6 +472,13 @@ int tb_gemm_decode(const TbDecodeGemmArgs* a, cudaStream_t stream) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  cudaLaunchAttribute attrs[2] = {attr[0], {}};
+  if (tb::pdl_enabled()) {
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.numAttrs = 2;
+  }
+  cfg.attrs = attrs;
   e = cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tw, tx, p);
   return static_cast<int>(e);
 }

@@ -32,6 +32,7 @@
 
 #include "kernels.h"
 #include "device_common.cuh"
+#include "pdl.cuh"
 #include "sm100_primitives.cuh"
 
 namespace {
@@ -664,6 +665,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if constexpr (!kTp) {
+    // launched with programmatic dependent launch: global memory only after the preceding kernel
+    tb::pdl_wait();
+    tb::pdl_trigger();
+  }
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
@@ -1203,6 +1209,11 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tbm, const DevArgs& p, int 
   using S = Smem<BN>;
   auto k = gemm_tcgen05_kernel<BN, A_MN, B_MN, TP>;
   tb::ensure_dyn_smem(reinterpret_cast<const void*>(k), S::kTotal);
+  if constexpr (TP != 1 && TP != 2) {
+    // single-GPU variants: programmatic dependent launch (the prologue overlaps the previous kernel)
+    return static_cast<int>(tb::launch_pdl(k, dim3(grid), dim3(kThreads), S::kTotal, s, ta, tbm,
+                                           ta2 ? *ta2 : ta, ta3 ? *ta3 : ta, p));
+  }
   k<<<grid, kThreads, S::kTotal, s>>>(ta, tbm, ta2 ? *ta2 : ta, ta3 ? *ta3 : ta, p);
   return static_cast<int>(cudaGetLastError());
 }

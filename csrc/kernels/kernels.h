@@ -280,6 +280,12 @@ int tb_swiglu_fwd(const void* gu, void* act, long long T, int F, cudaStream_t s)
 int tb_kv_write(const void* qkv, long long ld, int k_off, int v_off, const int* seq_of_token, const int* pos,
                 const int* block_table, int max_blocks, void* kc, void* vc, int T, int Hk, int D, int bs,
                 cudaStream_t s);
+// RoPE (in place on the q and k heads of fused QKV rows, k / v at columns
+// Hq*D and (Hq+Hk)*D) and the paged-cache write of the rotated k and of v, in
+// one launch.
+int tb_rope_kv_write(void* qkv, long long ld, const int* pos, const void* table, int Hq, int Hk, int D,
+                     const int* seq_of_token, const int* block_table, int max_blocks, void* kc, void* vc, int T, int bs,
+                     cudaStream_t s);
 int tb_decode_attention(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
                         int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk, int D,
                         int bs, float scale, cudaStream_t s);
@@ -340,6 +346,14 @@ typedef struct {
 } TbPeerTable;
 
 size_t tb_peer_header_bytes(void);
+// Data-parallel Adam with one handshake for small vectors: every rank pulls
+// every peer's whole gradient (snapshotted into its send buffer at send_off)
+// and runs Adam on the whole vector (m, v full-size on every rank); only
+// local weights are written.  rep_epoch: the step's own epoch counter.
+int tb_peer_allreduce_adam_rep(TbPeerTable t, long long grad_off, long long send_off, long long param_off,
+                               long long shadow_off, long long n, float* m, float* v, TbAdamParams hp,
+                               const long long* step_ptr, unsigned* rep_epoch, unsigned* done_ctr, int* err,
+                               cudaStream_t s);
 // One row-segment copy of tb_peer_scatter_copy (all sizes and offsets in bytes,
 // multiples of 16).
 typedef struct {

@@ -16,6 +16,7 @@
 
 #include "device_common.cuh"
 #include "kernels.h"
+#include "pdl.cuh"
 
 namespace {
 
@@ -46,6 +47,8 @@ __device__ __forceinline__ void st8(bf16* p, const float* f) {
 // One warp per row; D % 256 == 0 (8 bf16 per lane per step).
 __global__ void rmsnorm_fwd_kernel(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ y,
                                    float* __restrict__ rstd_out, int T, int D, float eps) {
+  tb::pdl_wait();
+  tb::pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= T) return;
   const bf16* xr = x + static_cast<long long>(row) * D;
@@ -188,6 +191,8 @@ __global__ void rope_kernel(bf16* __restrict__ qkv, long long ld, const int* __r
 // ------------------------------------------------------------------ embedding
 __global__ void embed_fwd_kernel(const int* __restrict__ ids, const bf16* __restrict__ W, bf16* __restrict__ out,
                                  int T, int D, int V, int* __restrict__ err) {
+  tb::pdl_wait();
+  tb::pdl_trigger();
   const long long total = static_cast<long long>(T) * (D / 8);
   for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -286,6 +291,58 @@ __global__ void kv_write_kernel(const bf16* __restrict__ qkv, long long ld, int 
     const bf16* row = qkv + static_cast<long long>(t) * ld;
     *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(row + k_off + h * D + c);
     *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(row + v_off + h * D + c);
+  }
+}
+
+// RoPE on the q and k heads of fused QKV rows (in place) and the paged-cache
+// write of the rotated k and of v, in one pass (the decode step's pair of
+// rope_kernel + kv_write_kernel).  Per token: (Hq + Hk) x D/8 rotation items
+// (4 rotated pairs each; k items also store their 8 values into the cache)
+// and Hk x D/8 v-copy items.
+__global__ void rope_kv_write_kernel(bf16* __restrict__ qkv, long long ld, const int* __restrict__ pos,
+                                     const float2* __restrict__ table, int Hq, int Hk, int D,
+                                     const int* __restrict__ seq_of_token, const int* __restrict__ block_table,
+                                     int max_blocks, bf16* __restrict__ kc, bf16* __restrict__ vc, int T, int bs) {
+  tb::pdl_wait();
+  tb::pdl_trigger();
+  const int half = D / 2, q4 = half / 4;
+  const long long rot = static_cast<long long>(Hq + Hk) * q4, per_tok = rot + static_cast<long long>(Hk) * (D / 8);
+  const long long total = static_cast<long long>(T) * per_tok;
+  for (long long e = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(e / per_tok);
+    const long long r = e - static_cast<long long>(t) * per_tok;
+    const int p = pos[t];
+    bf16* row = qkv + static_cast<long long>(t) * ld;
+    auto slot = [&](int kh) {
+      const int blk = block_table[static_cast<long long>(seq_of_token[t]) * max_blocks + p / bs];
+      return ((static_cast<long long>(blk) * Hk + kh) * bs + (p % bs)) * D;
+    };
+    if (r < rot) {
+      const int h = static_cast<int>(r / q4), j = static_cast<int>(r % q4) * 4;
+      bf16* base = row + static_cast<long long>(h) * D;
+      const float2* tab = table + static_cast<long long>(p) * half;
+      __align__(8) bf16 lo[4], hi[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 cs = tab[j + k];
+        const float x1 = bf(base[j + k]), x2 = bf(base[j + k + half]);
+        lo[k] = __float2bfloat16_rn(x1 * cs.x - x2 * cs.y);
+        hi[k] = __float2bfloat16_rn(x2 * cs.x + x1 * cs.y);
+        base[j + k] = lo[k];
+        base[j + k + half] = hi[k];
+      }
+      if (h >= Hq) {
+        bf16* dst = kc + slot(h - Hq);
+        *reinterpret_cast<uint2*>(dst + j) = *reinterpret_cast<const uint2*>(lo);
+        *reinterpret_cast<uint2*>(dst + j + half) = *reinterpret_cast<const uint2*>(hi);
+      }
+    } else {
+      const long long v = r - rot;
+      const int kh = static_cast<int>(v / (D / 8)), c = static_cast<int>(v % (D / 8)) * 8;
+      *reinterpret_cast<uint4*>(vc + slot(kh) + c) =
+          *reinterpret_cast<const uint4*>(row + static_cast<long long>(Hq + Hk) * D + kh * D + c);
+    }
   }
 }
 
@@ -416,6 +473,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
                                                             const int* __restrict__ block_table, int max_blocks,
                                                             const int* __restrict__ ctx_len, bf16* __restrict__ out,
                                                             long long ldo, int Hk, int G, float scale) {
+  tb::pdl_wait();
+  tb::pdl_trigger();
   constexpr int D = 128, BS = 16, NW = 4;
   extern __shared__ __align__(128) uint8_t dyn_smem[];
   auto sKV = reinterpret_cast<uint8_t(*)[2][2][BS * 256]>(dyn_smem);  // [warp][stage][K/V]
@@ -923,9 +982,8 @@ extern "C" {
 int tb_rmsnorm_fwd(const void* x, const float* w, void* y, float* rstd, int T, int D, float eps, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 256) return static_cast<int>(cudaErrorInvalidValue);
-  rmsnorm_fwd_kernel<<<(T + 7) / 8, 256, 0, s>>>(static_cast<const bf16*>(x), w, static_cast<bf16*>(y), rstd, T, D,
-                                                  eps);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(tb::launch_pdl(rmsnorm_fwd_kernel, dim3((T + 7) / 8), dim3(256), 0, s,
+                                         static_cast<const bf16*>(x), w, static_cast<bf16*>(y), rstd, T, D, eps));
 }
 
 size_t tb_rmsnorm_bwd_ws_floats(int D) { return static_cast<size_t>(2 * 148) * (D > 0 ? D : 0); }
@@ -971,9 +1029,8 @@ int tb_rope(void* qkv, long long ld, const int* pos, const void* table, int T, i
 int tb_embed_fwd(const int* ids, const void* W, void* out, int T, int D, int V, int* err, cudaStream_t s) {
   if (T <= 0) return 0;
   if (D % 8) return static_cast<int>(cudaErrorInvalidValue);
-  embed_fwd_kernel<<<grid_for(static_cast<long long>(T) * D / 8), 256, 0, s>>>(
-      ids, static_cast<const bf16*>(W), static_cast<bf16*>(out), T, D, V, err);
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(tb::launch_pdl(embed_fwd_kernel, dim3(grid_for(static_cast<long long>(T) * D / 8)), dim3(256),
+                                         0, s, ids, static_cast<const bf16*>(W), static_cast<bf16*>(out), T, D, V, err));
 }
 
 int tb_embed_bwd(const int* ids, const void* dout, float* dW, int T, int D, int V, cudaStream_t s) {
@@ -1008,6 +1065,18 @@ int tb_kv_write(const void* qkv, long long ld, int k_off, int v_off, const int* 
   return static_cast<int>(cudaGetLastError());
 }
 
+int tb_rope_kv_write(void* qkv, long long ld, const int* pos, const void* table, int Hq, int Hk, int D,
+                     const int* seq_of_token, const int* block_table, int max_blocks, void* kc, void* vc, int T, int bs,
+                     cudaStream_t s) {
+  if (T <= 0) return 0;
+  if (D % 8 || ld % 8) return static_cast<int>(cudaErrorInvalidValue);
+  const long long work = static_cast<long long>(T) * ((Hq + Hk) * (D / 8) + Hk * (D / 8));
+  return static_cast<int>(tb::launch_pdl(rope_kv_write_kernel, dim3(grid_for(work)), dim3(256), 0, s,
+                                         static_cast<bf16*>(qkv), ld, pos, static_cast<const float2*>(table), Hq, Hk,
+                                         D, seq_of_token, block_table, max_blocks, static_cast<bf16*>(kc),
+                                         static_cast<bf16*>(vc), T, bs));
+}
+
 int tb_decode_attention(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
                         int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk, int D,
                         int bs, float scale, cudaStream_t s) {
@@ -1022,9 +1091,8 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
   if (bs == 16 && G <= 8) {
     const cudaError_t e = tb::ensure_dyn_smem(reinterpret_cast<const void*>(decode_attn_tc_kernel), kDecTcSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
-    decode_attn_tc_kernel<<<grid, 128, kDecTcSmem, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk,
-                                                        G, scale);
-    return static_cast<int>(cudaGetLastError());
+    return static_cast<int>(tb::launch_pdl(decode_attn_tc_kernel, grid, dim3(128), kDecTcSmem, s, qq, ldq, k, v,
+                                           block_table, max_blocks, ctx_len, o, ldo, Hk, G, scale));
   }
   switch (G) {
     case 1: decode_attn_kernel<1><<<grid, 128, 0, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk, bs, scale); break;

@@ -1,7 +1,8 @@
 """Worker for the multi-GPU data-parallel tests (launched by test_dp_multigpu.py
 under torch.distributed.run, one process per GPU).  Checks:
   1. the peer-memory all-reduce against the arithmetic result;
-  2. the fused all-reduce + Adam kernel against all-reduce + the fp32 Adam oracle;
+  2. the fused all-reduce + Adam kernels (ZeRO-1 and replicated one-handshake)
+     against all-reduce + the fp32 Adam oracle;
   3. PPO with the fused data-parallel step keeps identical weights on all ranks
      and matches the NCCL path after one iteration.
 Exits non-zero on any mismatch."""
@@ -37,25 +38,33 @@ def main():
         assert torch.allclose(buf, exp, rtol=1e-6), f"allreduce mismatch on rank {rank}"
     pb.check()
 
-    # 2. fused all-reduce + Adam vs all-reduce + oracle Adam
+    # 2. fused all-reduce + Adam vs all-reduce + oracle Adam, in both modes
+    #    (ZeRO-1 reduce-scatter / all-gather, and the replicated one-handshake step)
     m = 65541
-    opt = FusedDataParallelAdam(m, None, lr=1e-3)
-    g0 = torch.Generator().manual_seed(0)
-    init = torch.randn(m, generator=g0)
-    opt.param.copy_(init.to(dev))
-    opt.shadow.copy_(opt.param)
-    p_ref = init.clone().double()
-    m_ref, v_ref = torch.zeros(m, dtype=torch.float64), torch.zeros(m, dtype=torch.float64)
-    for step in range(1, 4):
-        grads = [torch.randn(m, generator=torch.Generator().manual_seed(100 * step + r)) for r in range(world)]
-        opt.grad.copy_(grads[rank].to(dev))
-        opt.step()
-        torch.cuda.synchronize()
-        gmean = sum(g.double() for g in grads) / world
-        ref.adam_step(p_ref, gmean, m_ref, v_ref, step, 1e-3)
-        assert torch.allclose(opt.param.cpu().double(), p_ref, atol=2e-6), f"fused adam mismatch rank {rank}"
-        assert torch.allclose(opt.shadow.float().cpu(), opt.param.cpu(), atol=1e-2, rtol=1e-2)
-    opt.check()
+    for replicated in (False, True):
+        opt = FusedDataParallelAdam(m, None, lr=1e-3, replicated=replicated)
+        g0 = torch.Generator().manual_seed(0)
+        init = torch.randn(m, generator=g0)
+        opt.param.copy_(init.to(dev))
+        opt.shadow.copy_(opt.param)
+        p_ref = init.clone().double()
+        m_ref, v_ref = torch.zeros(m, dtype=torch.float64), torch.zeros(m, dtype=torch.float64)
+        for step in range(1, 5):
+            grads = [torch.randn(m, generator=torch.Generator().manual_seed(100 * step + r)) for r in range(world)]
+            opt.grad.copy_(grads[rank].to(dev))
+            opt.step()
+            torch.cuda.synchronize()
+            gmean = sum(g.double() for g in grads) / world
+            ref.adam_step(p_ref, gmean, m_ref, v_ref, step, 1e-3)
+            assert torch.allclose(opt.param.cpu().double(), p_ref, atol=2e-6), \
+                f"fused adam mismatch rank {rank} (replicated={replicated}, step {step})"
+            assert torch.allclose(opt.shadow.float().cpu(), opt.param.cpu(), atol=1e-2, rtol=1e-2)
+        opt.check()
+        # replicated: every rank computed the same weights, bit for bit
+        ws = [torch.empty_like(opt.param) for _ in range(world)]
+        dist.all_gather(ws, opt.param)
+        for other in ws:
+            assert torch.equal(other, opt.param), f"rank {rank}: weights differ across ranks (replicated={replicated})"
 
     # 3. PPO: weights identical across ranks after fused-DP iterations
     from turbol_b200.rl.ppo import PPOConfig, PPOTrainer

@@ -61,6 +61,28 @@ def test_rope_roundtrip(dev):
     assert torch.allclose(qkv.float(), orig.float(), atol=5e-2)
 
 
+def test_rope_kv_write_matches_separate_kernels(dev):
+    """The fused RoPE + paged KV write equals rope followed by kv_write, bit for bit."""
+    cfg = LMConfig.tiny()
+    tab = rope_table(cfg, dev)
+    T, Hq, Hk, D, bs = 37, 6, 2, 128, 16
+    qkv = bf(torch.randn(T, (Hq + 2 * Hk) * D + 64, device=dev))[:, :(Hq + 2 * Hk) * D]  # strided rows
+    # distinct (sequence, position) per token: each cache slot is written once
+    seq = (torch.arange(T, device=dev) % 5).to(torch.int32)
+    pos = ((torch.arange(T, device=dev) // 5) * 37 + seq * 3).to(torch.int32)
+    nblk = 5 * 20 + 1
+    table = torch.randperm(nblk - 1, device=dev).to(torch.int32)[:5 * 20].view(5, 20)
+    kc1 = bf(torch.zeros(nblk, Hk, bs, D, device=dev))
+    vc1, kc2, vc2 = kc1.clone(), kc1.clone(), kc1.clone()
+    a, b = qkv.clone(), qkv.clone()
+    ops().rope(a, pos, tab, Hq + Hk, D)
+    ops().kv_write(a, Hq * D, (Hq + Hk) * D, seq, pos, table, kc1, vc1, Hk, D, bs)
+    ops().rope_kv_write(b, pos, tab, Hq, Hk, D, seq, table, kc2, vc2, bs)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+
+
 @pytest.mark.parametrize("impl,use_ws", [("tc", True), ("tc", False), ("mma", False)])
 @pytest.mark.parametrize("B,T,Hq,Hk", [(2, 128, 4, 2), (1, 200, 12, 2), (2, 64, 8, 8), (1, 777, 12, 2),
                                        (2, 320, 32, 8)])

@@ -125,9 +125,8 @@ class LLMGenerator:
                 o.gemm(h, m.s[P + "wqkv"], qkv, bias=m.f32[P + "bqkv"], epi=o.EPI_BIAS, **kw)
             else:
                 o.gemm(h, m.s[P + "wqkv"], qkv, **kw)
-            o.rope(qkv, st["pos"], m.table, cfg.n_heads + cfg.n_kv_heads, D)
-            o.kv_write(qkv, cfg.q_dim, cfg.q_dim + cfg.kv_dim, st["seq"], st["pos"], st["table"], self.kc[li],
-                       self.vc[li], cfg.n_kv_heads, D, self.bs)
+            o.rope_kv_write(qkv, st["pos"], m.table, cfg.n_heads, cfg.n_kv_heads, D, st["seq"], st["table"],
+                            self.kc[li], self.vc[li], self.bs)
             o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], attn, cfg.n_heads,
                                cfg.n_kv_heads, D, self.bs, scale)
             if dg:
