@@ -27,8 +27,14 @@ def test_ppo_example_cpu(tmp_path):
 def test_ppo_example_gpu(tmp_path, dev):
     import ppo_example
 
+    # the default fp32 compute (the 256-env workload's precision) ...
     tr = ppo_example.main(["--device", "cuda:0", "--num-updates", "3", "--num-envs", "1024", "--rollout-steps", "16",
-                           "--batch-size", "4096", "--print-every", "1", "--log-dir", str(tmp_path)])
+                           "--batch-size", "4096", "--print-every", "1", "--log-dir", str(tmp_path / "fp32")])
+    assert tr.iteration == 3 and not tr.fused
+    # ... and bf16, which runs the fused tensor-core MLP
+    tr = ppo_example.main(["--device", "cuda:0", "--num-updates", "3", "--num-envs", "1024", "--rollout-steps", "16",
+                           "--batch-size", "4096", "--print-every", "1", "--log-dir", str(tmp_path / "bf16"),
+                           "--dtype", "bf16"])
     assert tr.iteration == 3 and tr.fused
 
 
