@@ -271,16 +271,39 @@ void register_llm_ops(py::module_& m) {
             "rope_kv_write");
   });
   m.def("decode_attention", [=](at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor block_table,
-                                at::Tensor ctx_len, at::Tensor out, int Hq, int Hk, int D, int bs, float scale) {
+                                at::Tensor ctx_len, at::Tensor out, int Hq, int Hk, int D, int bs, float scale,
+                                int n_split, py::object part, py::object counters) {
     bf16_2d(q, "q");
     bf16_2d(out, "out");
     i32c(block_table, "block_table");
     i32c(ctx_len, "ctx_len");
-    cuda_ok(tb_decode_attention(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), block_table.data_ptr<int>(),
-                                static_cast<int>(block_table.size(1)), ctx_len.data_ptr<int>(), out.data_ptr(),
-                                out.stride(0), static_cast<int>(ctx_len.numel()), Hq, Hk, D, bs, scale,
-                                turbol::StreamFor(q)),
+    const int B = static_cast<int>(ctx_len.numel());
+    float* pp = nullptr;
+    int* cp = nullptr;
+    at::Tensor pt, ct;
+    if (n_split > 1) {
+      chk(!part.is_none() && !counters.is_none(), "decode_attention: n_split > 1 needs part and counters");
+      pt = part.cast<at::Tensor>();
+      ct = counters.cast<at::Tensor>();
+      f32c(pt, "part");
+      i32c(ct, "counters");
+      chk(static_cast<size_t>(pt.numel()) >= tb_decode_attention_part_floats(B, Hq, Hk, n_split) &&
+              ct.numel() >= static_cast<int64_t>(B) * Hk,
+          "decode_attention: part / counters too small");
+      pp = pt.data_ptr<float>();
+      cp = ct.data_ptr<int>();
+    }
+    cuda_ok(tb_decode_attention_split(q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(),
+                                      block_table.data_ptr<int>(), static_cast<int>(block_table.size(1)),
+                                      ctx_len.data_ptr<int>(), out.data_ptr(), out.stride(0), B, Hq, Hk, D, bs, scale,
+                                      n_split, pp, cp, turbol::StreamFor(q)),
             "decode_attention");
+  }, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("block_table"), py::arg("ctx_len"), py::arg("out"),
+     py::arg("Hq"), py::arg("Hk"), py::arg("D"), py::arg("bs"), py::arg("scale"), py::arg("n_split") = 1,
+     py::arg("part") = py::none(), py::arg("counters") = py::none());
+  m.def("decode_attention_splits", &tb_decode_attention_splits, py::arg("B"), py::arg("Hk"));
+  m.def("decode_attention_part_numel", [](int B, int Hq, int Hk, int n_split) {
+    return static_cast<int64_t>(tb_decode_attention_part_floats(B, Hq, Hk, n_split));
   });
   m.def("sample", [=](at::Tensor logits, float temperature, uint64_t seed, py::object step_ptr, int64_t step,
                       at::Tensor out_tok, py::object out_logp, py::object tok_mat, py::object lp_mat,

@@ -289,6 +289,18 @@ int tb_rope_kv_write(void* qkv, long long ld, const int* pos, const void* table,
 int tb_decode_attention(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
                         int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk, int D,
                         int bs, float scale, cudaStream_t s);
+// The same with each (sequence, KV head) context split into n_split chunks
+// run by separate CTAs (head dim 128, 16-token blocks, <= 8 query heads per
+// KV head); the last chunk to finish merges the partials.  part: fp32
+// scratch of tb_decode_attention_part_floats(); counters: B * Hk ints, zero
+// before the first call and left zero by every call.
+int tb_decode_attention_split(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
+                              int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk,
+                              int D, int bs, float scale, int n_split, float* part, int* counters, cudaStream_t s);
+// Chunks per context that fill the SMs' resident CTA slots in the fewest
+// waves (for long contexts), 1..8.
+int tb_decode_attention_splits(int B, int Hk);
+size_t tb_decode_attention_part_floats(int B, int Hq, int Hk, int n_split);
 // seed_ptr / temp_ptr (optional) override seed / temperature from device
 // memory, so a captured CUDA graph can be replayed with new values.
 int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,

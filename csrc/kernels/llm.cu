@@ -472,7 +472,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
                                                             const bf16* __restrict__ kc, const bf16* __restrict__ vc,
                                                             const int* __restrict__ block_table, int max_blocks,
                                                             const int* __restrict__ ctx_len, bf16* __restrict__ out,
-                                                            long long ldo, int Hk, int G, float scale) {
+                                                            long long ldo, int Hk, int G, float scale, int n_split,
+                                                            float* __restrict__ part, int* __restrict__ counters) {
   tb::pdl_wait();
   tb::pdl_trigger();
   constexpr int D = 128, BS = 16, NW = 4;
@@ -481,7 +482,9 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
   // after the main loop the staging area is reused for the partial outputs
   auto sm_o = reinterpret_cast<float(*)[16][D + 4]>(dyn_smem);
   __shared__ float sm_m[NW][16], sm_l[NW][16];
-  const int s = blockIdx.x / Hk, hk = blockIdx.x % Hk;
+  // context split: CTA (sequence, kv head, chunk c) takes blocks [c nblk / n_split, (c + 1) nblk / n_split)
+  const int c_split = blockIdx.x % n_split, sh = blockIdx.x / n_split;
+  const int s = sh / Hk, hk = sh % Hk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
   const int L = ctx_len[s];
   const int nblk = (L + BS - 1) / BS;
@@ -511,14 +514,16 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
   const int* bt = block_table + static_cast<long long>(s) * max_blocks;
   auto src_k = [&](int j) { return kc + (static_cast<long long>(bt[j]) * Hk + hk) * BS * D; };
   auto src_v = [&](int j) { return vc + (static_cast<long long>(bt[j]) * Hk + hk) * BS * D; };
+  const int jb0 = static_cast<int>(static_cast<long long>(c_split) * nblk / n_split);
+  const int jb1 = static_cast<int>(static_cast<long long>(c_split + 1) * nblk / n_split);
   int st = 0;
-  if (warp < nblk) {
-    dtc::stage(sKV[warp][0][0], src_k(warp), lane);
-    dtc::stage(sKV[warp][0][1], src_v(warp), lane);
+  if (jb0 + warp < jb1) {
+    dtc::stage(sKV[warp][0][0], src_k(jb0 + warp), lane);
+    dtc::stage(sKV[warp][0][1], src_v(jb0 + warp), lane);
   }
-  for (int j = warp; j < nblk; j += NW) {
+  for (int j = jb0 + warp; j < jb1; j += NW) {
     const int jn = j + NW;
-    if (jn < nblk) {
+    if (jn < jb1) {
       dtc::stage(sKV[warp][st ^ 1][0], src_k(jn), lane);
       dtc::stage(sKV[warp][st ^ 1][1], src_v(jn), lane);
       asm volatile("cp.async.wait_group 2;" ::: "memory");
@@ -607,6 +612,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
     sm_o[warp][g][d * 8 + 2 * t4 + 1] = o[d][1];
   }
   __syncthreads();
+  // this CTA's chunk: partial [G][D + 2] = (unnormalized o, m in log2 units, l)
+  float* mine = part ? part + (static_cast<long long>(sh) * n_split + c_split) * G * (D + 2) : nullptr;
   for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
     const int r = e / D, d = e % D;
     float M = -INFINITY;
@@ -620,9 +627,44 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const bf16* __restr
       Ls += sm_l[w][r] * c;
       acc += sm_o[w][r][d] * c;
     }
+    if (n_split == 1) {
+      out[static_cast<long long>(s) * ldo + static_cast<long long>(hk * G + r) * D + d] =
+          __float2bfloat16_rn(Ls > 0.f ? acc / Ls : 0.f);
+    } else {
+      mine[r * (D + 2) + d] = acc;
+      if (d == 0) {
+        mine[r * (D + 2) + D] = M;
+        mine[r * (D + 2) + D + 1] = Ls;
+      }
+    }
+  }
+  if (n_split == 1) return;
+  // the last chunk of (sequence, kv head) to finish merges the chunks (flash-decoding)
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counters + sh, 1) == n_split - 1 ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* all = part + static_cast<long long>(sh) * n_split * G * (D + 2);
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int r = e / D, d = e % D;
+    float M = -INFINITY;
+    for (int c = 0; c < n_split; ++c) M = fmaxf(M, __ldcg(all + (c * G + r) * (D + 2) + D));
+    float Ls = 0.f, acc = 0.f;
+    for (int c = 0; c < n_split; ++c) {
+      const float* pc = all + (c * G + r) * (D + 2);
+      const float mc = __ldcg(pc + D);
+      if (mc == -INFINITY) continue;
+      const float w = exp2f(mc - M);
+      Ls += __ldcg(pc + D + 1) * w;
+      acc += __ldcg(pc + d) * w;
+    }
     out[static_cast<long long>(s) * ldo + static_cast<long long>(hk * G + r) * D + d] =
         __float2bfloat16_rn(Ls > 0.f ? acc / Ls : 0.f);
   }
+  if (threadIdx.x == 0) counters[sh] = 0;  // ready for the next call (CUDA-graph replays)
 }
 
 // ------------------------------------------------------------------ sampling
@@ -1092,7 +1134,8 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
     const cudaError_t e = tb::ensure_dyn_smem(reinterpret_cast<const void*>(decode_attn_tc_kernel), kDecTcSmem);
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(tb::launch_pdl(decode_attn_tc_kernel, grid, dim3(128), kDecTcSmem, s, qq, ldq, k, v,
-                                           block_table, max_blocks, ctx_len, o, ldo, Hk, G, scale));
+                                           block_table, max_blocks, ctx_len, o, ldo, Hk, G, scale, 1,
+                                           static_cast<float*>(nullptr), static_cast<int*>(nullptr)));
   }
   switch (G) {
     case 1: decode_attn_kernel<1><<<grid, 128, 0, s>>>(qq, ldq, k, v, block_table, max_blocks, ctx_len, o, ldo, Hk, bs, scale); break;
@@ -1103,6 +1146,50 @@ int tb_decode_attention(const void* q, long long ldq, const void* kc, const void
     default: return static_cast<int>(cudaErrorInvalidValue);
   }
   return static_cast<int>(cudaGetLastError());
+}
+
+int tb_decode_attention_splits(int B, int Hk) {
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (tb::ensure_dyn_smem(reinterpret_cast<const void*>(decode_attn_tc_kernel), kDecTcSmem) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_attn_tc_kernel, 128, kDecTcSmem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 3;
+  if (sms <= 0) sms = 148;
+  const long long slots = static_cast<long long>(sms) * per_sm, units = static_cast<long long>(B) * Hk;
+  // waves x (1 / split) for a long context: the smallest wins, ties to fewer chunks
+  int best = 1;
+  double best_t = static_cast<double>((units + slots - 1) / slots);
+  for (int sp = 2; sp <= 8; ++sp) {
+    const double t = static_cast<double>((units * sp + slots - 1) / slots) / sp;
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = sp;
+    }
+  }
+  return best;
+}
+
+size_t tb_decode_attention_part_floats(int B, int Hq, int Hk, int n_split) {
+  return static_cast<size_t>(B) * Hk * n_split * (Hq / Hk) * (128 + 2);
+}
+
+int tb_decode_attention_split(const void* q, long long ldq, const void* kc, const void* vc, const int* block_table,
+                              int max_blocks, const int* ctx_len, void* out, long long ldo, int B, int Hq, int Hk,
+                              int D, int bs, float scale, int n_split, float* part, int* counters, cudaStream_t s) {
+  if (n_split <= 1)
+    return tb_decode_attention(q, ldq, kc, vc, block_table, max_blocks, ctx_len, out, ldo, B, Hq, Hk, D, bs, scale, s);
+  const int G = Hq / Hk;
+  if (B <= 0) return 0;
+  if (D != 128 || bs != 16 || G > 8 || Hq % Hk || part == nullptr || counters == nullptr)
+    return static_cast<int>(cudaErrorInvalidValue);
+  const cudaError_t e = tb::ensure_dyn_smem(reinterpret_cast<const void*>(decode_attn_tc_kernel), kDecTcSmem);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  return static_cast<int>(tb::launch_pdl(decode_attn_tc_kernel, dim3(B * Hk * n_split), dim3(128), kDecTcSmem, s,
+                                         static_cast<const bf16*>(q), ldq, static_cast<const bf16*>(kc),
+                                         static_cast<const bf16*>(vc), block_table, max_blocks, ctx_len,
+                                         static_cast<bf16*>(out), ldo, Hk, G, scale, n_split, part, counters));
 }
 
 int tb_sample(const void* logits, long long ld, int B, int V, float temperature, unsigned long long seed,

@@ -37,7 +37,7 @@ from ..models.llm import DecoderLM, LMConfig
 
 class LLMGenerator:
     def __init__(self, model: DecoderLM, max_batch: int, max_len: int, block_size: int = 16, seed: int = 0,
-                 cuda_graph: bool = True, decode_gemm: Optional[bool] = None):
+                 cuda_graph: bool = True, decode_gemm: Optional[bool] = None, attn_split: int = 1):
         self.m = model
         self.cfg = model.cfg
         self.device = model.device
@@ -50,6 +50,12 @@ class LLMGenerator:
         # sequences; beyond that the down projection only, the general GEMM
         # being as fast or faster for QKV, O and gate/up); True / False = all / none
         self.decode_gemm = decode_gemm
+        # context chunks per (sequence, KV head) in the decode attention: 1 =
+        # one CTA per context (measured fastest: splitting 512 sequences into 3
+        # chunks each took the GRPO rollout from 2.21 s to 2.94 s, the chunks'
+        # pipeline fill outweighing the fuller last wave); 0 = the wave model of
+        # decode_attention_splits; n > 1 = n chunks
+        self.attn_split = attn_split
         cfg = self.cfg
         self.blocks_per_seq = (max_len + block_size - 1) // block_size
         # worst case: every sequence private (no sharing) -> max_batch * blocks
@@ -128,7 +134,8 @@ class LLMGenerator:
             o.rope_kv_write(qkv, st["pos"], m.table, cfg.n_heads, cfg.n_kv_heads, D, st["seq"], st["table"],
                             self.kc[li], self.vc[li], self.bs)
             o.decode_attention(qkv, self.kc[li], self.vc[li], st["table"], st["ctx"], attn, cfg.n_heads,
-                               cfg.n_kv_heads, D, self.bs, scale)
+                               cfg.n_kv_heads, D, self.bs, scale, st["attn_split"], st.get("attn_part"),
+                               st.get("attn_cnt"))
             if dg:
                 o.gemm_decode(attn, m.s[P + "wo"], x2, aux=x, epi=o.EPI_RESIDUAL)
                 o.rmsnorm_fwd(x2, m.f32[P + "ln2"], h, None, cfg.rms_eps)
@@ -197,7 +204,24 @@ class LLMGenerator:
             "lengths": torch.full((B,), steps, device=dev, dtype=torch.int32),
             "n_done": torch.zeros(1, device=dev, dtype=torch.int32),
             **self._split_workspace(B),
+            **self._attn_split_state(B),
         }
+
+    def _attn_split_state(self, B: int) -> dict:
+        """Context split of the decode attention (``attn_split``), with the
+        merge scratch."""
+        cfg, o = self.cfg, _ops()
+        G = cfg.n_heads // cfg.n_kv_heads
+        want = getattr(self, "attn_split", 1)
+        if want == 1 or self.bs != 16 or cfg.head_dim != 128 or G > 8 or cfg.n_heads % cfg.n_kv_heads:
+            return {"attn_split": 1}
+        n = int(o.decode_attention_splits(B, cfg.n_kv_heads)) if want == 0 else int(want)
+        if n <= 1:
+            return {"attn_split": 1}
+        return {"attn_split": n,
+                "attn_part": torch.empty(o.decode_attention_part_numel(B, cfg.n_heads, cfg.n_kv_heads, n),
+                                         device=self.device),
+                "attn_cnt": torch.zeros(B * cfg.n_kv_heads, device=self.device, dtype=torch.int32)}
 
     def _decode_gemm_use(self, B: int):
         """(QKV / O / gate-up on the decode GEMM, down projection on it)."""
