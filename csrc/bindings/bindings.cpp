@@ -639,6 +639,81 @@ PYBIND11_MODULE(turbol_core, m) {
       .def("reset", &KVBlockManager::Reset);
 
   // ---------------- helpers ----------------
+  // host versions of the fused policy passes and of Adam (CPU tensors)
+  auto host_f32 = [](const at::Tensor& t, const char* what) {
+    if (t.is_cuda() || t.scalar_type() != at::kFloat || !t.is_contiguous())
+      throw std::invalid_argument(std::string(what) + ": a contiguous fp32 CPU tensor is required");
+  };
+  m.def("lin_gauss_act_host",
+        [host_f32](const at::Tensor& x, const at::Tensor& p, at::Tensor act, at::Tensor logp, int O, int A, float stdv,
+                   uint64_t seed, uint32_t counter) {
+          host_f32(x, "x");
+          host_f32(p, "params");
+          host_f32(act, "act");
+          host_f32(logp, "logp");
+          const int64_t N = x.numel() / O;
+          if (x.numel() != N * O || act.numel() < N * A || logp.numel() < N || p.numel() < A * O + A)
+            throw std::invalid_argument("lin_gauss_act_host: shapes");
+          throw_if(LinGaussActHost(x.data_ptr<float>(), p.data_ptr<float>(), act.data_ptr<float>(),
+                                   logp.data_ptr<float>(), static_cast<int>(N), O, A, stdv, seed, counter));
+        },
+        py::arg("x"), py::arg("params"), py::arg("act"), py::arg("logp"), py::arg("O"), py::arg("A"), py::arg("std"),
+        py::arg("seed"), py::arg("counter"));
+  m.def("lin_gauss_grad_host",
+        [host_f32](const at::Tensor& batch, const at::Tensor& p, at::Tensor g, int O, int A, float stdv, float clip,
+                   float vf_coef, bool has_old) {
+          host_f32(batch, "batch");
+          host_f32(p, "params");
+          host_f32(g, "grad");
+          if (batch.dim() != 2 || p.numel() < A * O + A + O + 1 || g.numel() < A * O + A + O + 1)
+            throw std::invalid_argument("lin_gauss_grad_host: shapes");
+          throw_if(LinGaussGradHost(batch.data_ptr<float>(), static_cast<int>(batch.size(1)), p.data_ptr<float>(),
+                                    g.data_ptr<float>(), static_cast<int>(batch.size(0)), O, A, stdv, clip, vf_coef,
+                                    has_old));
+        },
+        py::arg("batch"), py::arg("params"), py::arg("grad"), py::arg("O"), py::arg("A"), py::arg("std"),
+        py::arg("clip"), py::arg("vf_coef"), py::arg("has_old"));
+  m.def("adam_host",
+        [host_f32](at::Tensor p, const at::Tensor& g, at::Tensor m1, at::Tensor m2, int64_t step, float lr, float b1,
+                   float b2, float eps, float wd, float grad_scale) {
+          host_f32(p, "param");
+          host_f32(g, "grad");
+          host_f32(m1, "m");
+          host_f32(m2, "v");
+          const int64_t n = p.numel();
+          if (g.numel() != n || m1.numel() != n || m2.numel() != n) throw std::invalid_argument("adam_host: sizes");
+          AdamHost(p.data_ptr<float>(), g.data_ptr<float>(), m1.data_ptr<float>(), m2.data_ptr<float>(), n, step, lr,
+                   b1, b2, eps, wd, grad_scale);
+        },
+        py::arg("param"), py::arg("grad"), py::arg("m"), py::arg("v"), py::arg("step"), py::arg("lr"), py::arg("b1"),
+        py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("grad_scale"));
+
+  m.def("gae_host",
+        [host_f32](const at::Tensor& r, const at::Tensor& v, const at::Tensor& d, at::Tensor adv, at::Tensor ret,
+                   py::object stats, float gamma, float lam) {
+          host_f32(r, "rewards");
+          host_f32(v, "values");
+          host_f32(adv, "adv");
+          host_f32(ret, "ret");
+          if (r.dim() != 2 || v.dim() != 2 || v.size(0) != r.size(0) + 1 || v.size(1) != r.size(1) ||
+              d.numel() != r.numel() || d.element_size() != 1 || !d.is_contiguous() || d.is_cuda() ||
+              adv.numel() != r.numel() || ret.numel() != r.numel())
+            throw std::invalid_argument("gae_host: rewards / dones [T, N], values [T + 1, N], byte dones");
+          double* sp = nullptr;
+          at::Tensor st;
+          if (!stats.is_none()) {
+            st = stats.cast<at::Tensor>();
+            if (st.is_cuda() || st.scalar_type() != at::kDouble || st.numel() < 2 || !st.is_contiguous())
+              throw std::invalid_argument("gae_host: stats must be float64 [2] on the CPU");
+            sp = st.data_ptr<double>();
+          }
+          throw_if(GaeHost(r.data_ptr<float>(), v.data_ptr<float>(), static_cast<const uint8_t*>(d.data_ptr()),
+                           adv.data_ptr<float>(), ret.data_ptr<float>(), static_cast<int>(r.size(0)),
+                           static_cast<int>(r.size(1)), gamma, lam, sp));
+        },
+        py::arg("rewards"), py::arg("values"), py::arg("dones"), py::arg("adv"), py::arg("ret"),
+        py::arg("stats") = py::none(), py::arg("gamma") = 0.99f, py::arg("lam") = 0.95f);
+
   m.def("get_version", []() { return std::string("1.0.0"); });
   m.def("get_device_count", &GetCudaDeviceCount);
   m.def("get_memory_info",

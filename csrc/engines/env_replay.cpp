@@ -33,6 +33,36 @@ uint64_t HostPhiloxWord(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, ui
 
 namespace {
 
+// Word 0 of Philox4x32-10 for counters (c0 + j, c1, c2, c3), j < 8, written as
+// independent lanes so the compiler can vectorize the rounds (the same values
+// as HostPhiloxWord(seed, c0 + j, c1, c2, c3, 0)).
+void host_philox_word0_x8(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t* out) {
+  constexpr int L = 8;
+  uint32_t x0[L], x1[L], x2[L], x3[L];
+  for (int j = 0; j < L; ++j) {
+    x0[j] = c0 + static_cast<uint32_t>(j);
+    x1[j] = c1;
+    x2[j] = c2;
+    x3[j] = c3;
+  }
+  uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+  for (int r = 0; r < 10; ++r) {
+    for (int j = 0; j < L; ++j) {
+      const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * x0[j];
+      const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * x2[j];
+      const uint32_t n0 = static_cast<uint32_t>(p1 >> 32) ^ x1[j] ^ k0;
+      const uint32_t n2 = static_cast<uint32_t>(p0 >> 32) ^ x3[j] ^ k1;
+      x1[j] = static_cast<uint32_t>(p1);
+      x3[j] = static_cast<uint32_t>(p0);
+      x0[j] = n0;
+      x2[j] = n2;
+    }
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  for (int j = 0; j < L; ++j) out[j] = x0[j];
+}
+
 float host_u01(uint32_t x) { return static_cast<float>(x >> 8) * (1.0f / 16777216.0f); }
 
 float ref_reset_unit(unsigned i, unsigned d, unsigned seed) {
@@ -167,26 +197,35 @@ Status GPUEnvironment::StepInto(const at::Tensor& action, at::Tensor& obs, at::T
       obs.view({num_envs_, obs_dim_}).copy_(s, /*non_blocking=*/true);
       return Status::Ok();
     }
+    if (obs.scalar_type() != at::kFloat || reward.scalar_type() != at::kFloat)
+      return Status::InvalidArgument("StepInto: obs and reward must be Float32");
     float* st = s.data_ptr<float>();
     const float* ap = a.data_ptr<float>();
     float* rp = reward.data_ptr<float>();
     auto* dp = static_cast<uint8_t*>(done.data_ptr());
+    float* op = obs.data_ptr<float>();
+    const int O = obs_dim_, A = act_dim_;
+    const float decay = decay_, force = force_, thr = done_threshold_;
+    // Rounded like the device kernel (and the reference): each product and
+    // sum once, in this order, no fused multiply-add (the host core is built
+    // with -ffp-contract=off); the reward sums the squares in dimension order.
     for (int i = 0; i < num_envs_; ++i) {
-      float cost = 0.f, first = 0.f;
-      for (int k = 0; k < obs_dim_; ++k) {
-        const int ak = k < act_dim_ ? k : act_dim_ - 1;
-        volatile float t1 = decay_ * st[static_cast<size_t>(i) * obs_dim_ + k];  // no FMA contraction
-        volatile float t2 = force_ * ap[static_cast<size_t>(i) * act_dim_ + ak];
+      float* x = st + static_cast<size_t>(i) * O;
+      const float* ai = ap + static_cast<size_t>(i) * A;
+      float* oi = op + static_cast<size_t>(i) * O;
+      float cost = 0.f;
+      for (int k = 0; k < O; ++k) {
+        const float t1 = decay * x[k];
+        const float t2 = force * ai[k < A ? k : A - 1];
         const float v = t1 + t2;
-        st[static_cast<size_t>(i) * obs_dim_ + k] = v;
-        volatile float sq = v * v;
+        x[k] = v;
+        oi[k] = v;
+        const float sq = v * v;
         cost = cost + sq;
-        if (k == 0) first = v;
       }
       rp[i] = -cost;
-      dp[i] = std::fabs(first) > done_threshold_ ? 1 : 0;
+      dp[i] = std::fabs(x[0]) > thr ? 1 : 0;
     }
-    obs.view({num_envs_, obs_dim_}).copy_(s);
     return Status::Ok();
   }
   // CartPole
@@ -271,10 +310,17 @@ Status RingBuffer::PushBatch(const Tensor& obs, const Tensor& act, const Tensor&
   if (act.numel() < B * act_dim_) return Status::InvalidArgument("act batch dims mismatch");
   if (reward.numel() < B || done.numel() < B) return Status::InvalidArgument("reward/done batch mismatch");
   auto opts = at::TensorOptions().device(device_.torch());
-  at::Tensor o = obs.torch().reshape({-1}).narrow(0, 0, B * obs_dim_).to(opts.dtype(at::kFloat)).contiguous();
-  at::Tensor a = act.torch().reshape({-1}).narrow(0, 0, B * act_dim_).to(opts.dtype(at::kFloat)).contiguous();
-  at::Tensor r = reward.torch().reshape({-1}).narrow(0, 0, B).to(opts.dtype(at::kFloat)).contiguous();
-  at::Tensor d = done.torch().reshape({-1}).narrow(0, 0, B).to(opts.dtype(at::kBool)).contiguous();
+  // inputs already of the buffer's dtype, device and layout are used as they
+  // are (no conversion ops on the hot path)
+  auto as = [&](const Tensor& t, int64_t n, at::ScalarType dt) {
+    const at::Tensor& x = t.torch();
+    if (x.scalar_type() == dt && x.device() == device_.torch() && x.is_contiguous() && x.numel() >= n) return x;
+    return x.reshape({-1}).narrow(0, 0, n).to(opts.dtype(dt)).contiguous();
+  };
+  at::Tensor o = as(obs, B * obs_dim_, at::kFloat);
+  at::Tensor a = as(act, B * act_dim_, at::kFloat);
+  at::Tensor r = as(reward, B, at::kFloat);
+  at::Tensor d = as(done, B, at::kBool);
   // Only the last `capacity` rows survive a push larger than the ring.
   int64_t skip = 0;
   if (B > capacity_) {
@@ -292,12 +338,24 @@ Status RingBuffer::PushBatch(const Tensor& obs, const Tensor& act, const Tensor&
     TURBOL_RETURN_IF_ERROR(
         check_cuda(tb_ring_push(fs, 4, static_cast<int>(B), head_, capacity_, StreamFor(o)), "ring_push"));
   } else {
-    for (int64_t i = 0; i < B; ++i) {
-      const int64_t slot = (head_ + i) % capacity_;
-      std::memcpy(obs_.data<float>() + slot * obs_dim_, o.data_ptr<float>() + (skip + i) * obs_dim_, obs_dim_ * 4);
-      std::memcpy(act_.data<float>() + slot * act_dim_, a.data_ptr<float>() + (skip + i) * act_dim_, act_dim_ * 4);
-      rew_.data<float>()[slot] = r.data_ptr<float>()[skip + i];
-      done_.data<bool>()[slot] = d.data_ptr<bool>()[skip + i];
+    // at most two contiguous runs of slots (before and after the wrap)
+    float* bo = obs_.data<float>();
+    float* ba = act_.data<float>();
+    float* br = rew_.data<float>();
+    bool* bd = done_.data<bool>();
+    const float* so = o.data_ptr<float>() + skip * obs_dim_;
+    const float* sa = a.data_ptr<float>() + skip * act_dim_;
+    const float* sr = r.data_ptr<float>() + skip;
+    const bool* sd = d.data_ptr<bool>() + skip;
+    int64_t done_rows = 0;
+    while (done_rows < B) {
+      const int64_t slot = (head_ + done_rows) % capacity_;
+      const int64_t n = std::min(B - done_rows, capacity_ - slot);
+      std::memcpy(bo + slot * obs_dim_, so + done_rows * obs_dim_, static_cast<size_t>(n * obs_dim_) * 4);
+      std::memcpy(ba + slot * act_dim_, sa + done_rows * act_dim_, static_cast<size_t>(n * act_dim_) * 4);
+      std::memcpy(br + slot, sr + done_rows, static_cast<size_t>(n) * 4);
+      std::memcpy(bd + slot, sd + done_rows, static_cast<size_t>(n));
+      done_rows += n;
     }
   }
   head_ = (head_ + B) % capacity_;
@@ -314,10 +372,14 @@ at::Tensor RingBuffer::SampleIndices(int batch_size) {
     const int e = tb_sample_indices(idx.data_ptr<int>(), batch_size, size_, seed_, ctr, StreamFor(idx));
     if (e != 0) throw std::runtime_error("sample_indices failed");
   } else {
-    for (int i = 0; i < batch_size; ++i) {
-      const uint32_t w = static_cast<uint32_t>(HostPhiloxWord(seed_, i, static_cast<uint32_t>(ctr),
-                                                              static_cast<uint32_t>(ctr >> 32), 0x52504C59u, 0));
-      idx.data_ptr<int>()[i] = static_cast<int>((static_cast<uint64_t>(w) * static_cast<uint64_t>(size_)) >> 32);
+    int* ip = idx.data_ptr<int>();
+    const uint64_t n = static_cast<uint64_t>(size_);
+    uint32_t w[8];
+    for (int i0 = 0; i0 < batch_size; i0 += 8) {
+      host_philox_word0_x8(seed_, static_cast<uint32_t>(i0), static_cast<uint32_t>(ctr),
+                           static_cast<uint32_t>(ctr >> 32), 0x52504C59u, w);
+      for (int j = 0; j < 8 && i0 + j < batch_size; ++j)
+        ip[i0 + j] = static_cast<int>((static_cast<uint64_t>(w[j]) * n) >> 32);
     }
   }
   return idx;
@@ -325,7 +387,9 @@ at::Tensor RingBuffer::SampleIndices(int batch_size) {
 
 Status RingBuffer::Gather(const at::Tensor& idx_in, Tensor* obs, Tensor* act, Tensor* reward, Tensor* done) {
   if (!obs || !act || !reward || !done) return Status::InvalidArgument("null output pointer");
-  at::Tensor idx = idx_in.to(at::TensorOptions().dtype(at::kInt).device(device_.torch())).contiguous();
+  at::Tensor idx = idx_in.scalar_type() == at::kInt && idx_in.device() == device_.torch() && idx_in.is_contiguous()
+                      ? idx_in
+                      : idx_in.to(at::TensorOptions().dtype(at::kInt).device(device_.torch())).contiguous();
   const int64_t B = idx.numel();
   auto opts = at::TensorOptions().device(device_.torch());
   at::Tensor o = at::empty({B, obs_dim_}, opts.dtype(at::kFloat));
@@ -342,13 +406,22 @@ Status RingBuffer::Gather(const at::Tensor& idx_in, Tensor* obs, Tensor* act, Te
         check_cuda(tb_ring_gather(fs, 4, static_cast<int>(B), idx.data_ptr<int>(), StreamFor(o)), "ring_gather"));
   } else {
     const int* ip = idx.data_ptr<int>();
+    const float* bo = obs_.data<float>();
+    const float* ba = act_.data<float>();
+    const float* br = rew_.data<float>();
+    const bool* bd = done_.data<bool>();
+    float* po = o.data_ptr<float>();
+    float* pa = a.data_ptr<float>();
+    float* pr = r.data_ptr<float>();
+    bool* pd = d.data_ptr<bool>();
+    const size_t ob = static_cast<size_t>(obs_dim_) * 4, ab = static_cast<size_t>(act_dim_) * 4;
     for (int64_t i = 0; i < B; ++i) {
       const int64_t s = ip[i];
       if (s < 0 || s >= capacity_) return Status::InvalidArgument("gather index out of range");
-      std::memcpy(o.data_ptr<float>() + i * obs_dim_, obs_.data<float>() + s * obs_dim_, obs_dim_ * 4);
-      std::memcpy(a.data_ptr<float>() + i * act_dim_, act_.data<float>() + s * act_dim_, act_dim_ * 4);
-      r.data_ptr<float>()[i] = rew_.data<float>()[s];
-      d.data_ptr<bool>()[i] = done_.data<bool>()[s];
+      std::memcpy(po + i * obs_dim_, bo + s * obs_dim_, ob);
+      std::memcpy(pa + i * act_dim_, ba + s * act_dim_, ab);
+      pr[i] = br[s];
+      pd[i] = bd[s];
     }
   }
   *obs = Tensor(o);
@@ -362,8 +435,43 @@ Status RingBuffer::Sample(int batch_size, Tensor* obs, Tensor* act, Tensor* rewa
   if (!obs || !act || !reward || !done) return Status::InvalidArgument("null output pointer");
   if (size_ == 0) return Status::InvalidArgument("Buffer is empty");
   if (batch_size <= 0) return Status::InvalidArgument("batch_size must be > 0");
-  at::Tensor idx = SampleIndices(batch_size);
-  return Gather(idx, obs, act, reward, done);
+  if (device_.is_cuda()) return Gather(SampleIndices(batch_size), obs, act, reward, done);
+  // host: the indices of SampleIndices (same Philox stream and counter),
+  // drawn 8 at a time and copied straight into the outputs
+  const int64_t B = batch_size;
+  auto opts = at::TensorOptions().device(device_.torch());
+  at::Tensor o = at::empty({B, obs_dim_}, opts.dtype(at::kFloat));
+  at::Tensor a = at::empty({B, act_dim_}, opts.dtype(at::kFloat));
+  at::Tensor r = at::empty({B}, opts.dtype(at::kFloat));
+  at::Tensor d = at::empty({B}, opts.dtype(at::kBool));
+  const uint64_t ctr = sample_counter_++;
+  const uint64_t n = static_cast<uint64_t>(size_);
+  const float* bo = obs_.data<float>();
+  const float* ba = act_.data<float>();
+  const float* br = rew_.data<float>();
+  const bool* bd = done_.data<bool>();
+  float* po = o.data_ptr<float>();
+  float* pa = a.data_ptr<float>();
+  float* pr = r.data_ptr<float>();
+  bool* pd = d.data_ptr<bool>();
+  const size_t ob = static_cast<size_t>(obs_dim_) * 4, ab = static_cast<size_t>(act_dim_) * 4;
+  uint32_t w[8];
+  for (int64_t i0 = 0; i0 < B; i0 += 8) {
+    host_philox_word0_x8(seed_, static_cast<uint32_t>(i0), static_cast<uint32_t>(ctr), static_cast<uint32_t>(ctr >> 32),
+                         0x52504C59u, w);
+    for (int j = 0; j < 8 && i0 + j < B; ++j) {
+      const int64_t i = i0 + j, src = static_cast<int64_t>((static_cast<uint64_t>(w[j]) * n) >> 32);
+      std::memcpy(po + i * obs_dim_, bo + src * obs_dim_, ob);
+      std::memcpy(pa + i * act_dim_, ba + src * act_dim_, ab);
+      pr[i] = br[src];
+      pd[i] = bd[src];
+    }
+  }
+  *obs = Tensor(o);
+  *act = Tensor(a);
+  *reward = Tensor(r);
+  *done = Tensor(d);
+  return Status::Ok();
 }
 
 // ============================================================================

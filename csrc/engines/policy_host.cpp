@@ -1,0 +1,181 @@
+// Host (CPU) versions of the linear Gaussian policy's fused steps, of the
+// Adam update and of GAE: the same math as csrc/kernels/policy.cu, optim.cu
+// and advantage.cu, one pass in plain loops, so the CPU paths pay no
+// per-operator framework dispatch.
+//
+//   mean = tanh(W_a x + b_a) [A],   value = W_c x + b_c
+//   parameter layout (flat fp32): W_a [A, O], b_a [A], W_c [O], b_c
+#include <math.h>
+
+#include <algorithm>
+#include <cmath>
+#include <vector>
+
+#include "turbol/engines.hpp"
+
+namespace turbol {
+
+namespace {
+
+constexpr float kPi = 3.14159265358979323846f;
+
+void philox4(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t* out) {
+  uint32_t c[4] = {c0, c1, c2, c3};
+  uint32_t k0 = static_cast<uint32_t>(seed), k1 = static_cast<uint32_t>(seed >> 32);
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = static_cast<uint64_t>(0xD2511F53u) * c[0];
+    const uint64_t p1 = static_cast<uint64_t>(0xCD9E8D57u) * c[2];
+    const uint32_t n0 = static_cast<uint32_t>(p1 >> 32) ^ c[1] ^ k0;
+    const uint32_t n2 = static_cast<uint32_t>(p0 >> 32) ^ c[3] ^ k1;
+    c[1] = static_cast<uint32_t>(p1);
+    c[3] = static_cast<uint32_t>(p0);
+    c[0] = n0;
+    c[2] = n2;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  for (int i = 0; i < 4; ++i) out[i] = c[i];
+}
+
+float u01(uint32_t x) { return static_cast<float>(x >> 8) * (1.0f / 16777216.0f); }
+float u01_open(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+
+Status check_dims(int N, int O, int A) {
+  if (N < 0 || O <= 0 || A <= 0) return Status::InvalidArgument("linear Gaussian policy: bad dimensions");
+  return Status::Ok();
+}
+
+}  // namespace
+
+Status LinGaussActHost(const float* x, const float* p, float* act, float* logp, int N, int O, int A, float stdv,
+                       uint64_t seed, uint32_t counter) {
+  TURBOL_RETURN_IF_ERROR(check_dims(N, O, A));
+  const float var = stdv * stdv, c = -0.5f * std::log(2.f * kPi * var);
+  const float* W = p;
+  const float* b = p + static_cast<size_t>(A) * O;
+  for (int64_t row = 0; row < N; ++row) {
+    const float* xr = x + static_cast<size_t>(row) * O;
+    float* ar = act + static_cast<size_t>(row) * A;
+    float lp = 0.f;
+    for (int j0 = 0; j0 < A; j0 += 2) {
+      // two standard normals (Box-Muller) from the Philox block of (row, j0, call)
+      uint32_t r[4];
+      philox4(seed, static_cast<uint32_t>(row), static_cast<uint32_t>(j0), counter, 0u, r);
+      const float rad = std::sqrt(-2.f * std::log(u01_open(r[0])));
+      float sn, cs;
+      sincosf(2.f * kPi * u01(r[1]), &sn, &cs);
+      const float nz[2] = {rad * cs, rad * sn};
+      for (int t = 0; t < 2 && j0 + t < A; ++t) {
+        const int j = j0 + t;
+        float z = b[j];
+        const float* wj = W + static_cast<size_t>(j) * O;
+        for (int k = 0; k < O; ++k) z += wj[k] * xr[k];
+        const float m = std::tanh(z);
+        const float a = std::min(1.f, std::max(-1.f, m + stdv * nz[t]));
+        ar[j] = a;
+        lp += -0.5f * (a - m) * (a - m) / var + c;
+      }
+    }
+    logp[row] = lp;
+  }
+  return Status::Ok();
+}
+
+Status LinGaussGradHost(const float* batch, int row_w, const float* p, float* g, int N, int O, int A, float stdv,
+                        float clip, float vf_coef, bool has_old) {
+  TURBOL_RETURN_IF_ERROR(check_dims(N, O, A));
+  if (row_w < O + A + 2 + (has_old ? 1 : 0)) return Status::InvalidArgument("linear Gaussian policy: row too narrow");
+  if (N == 0) return Status::Ok();
+  const float var = stdv * stdv, c = -0.5f * std::log(2.f * kPi * var);
+  const float inv_n = 1.f / static_cast<float>(N);
+  const float* Wa = p;
+  const float* ba = Wa + static_cast<size_t>(A) * O;
+  const float* Wc = ba + A;
+  const float bc = Wc[O];
+  float* gWa = g;
+  float* gba = gWa + static_cast<size_t>(A) * O;
+  float* gWc = gba + A;
+  float* gbc = gWc + O;
+  std::vector<float> m(A);
+  for (int row = 0; row < N; ++row) {
+    const float* r = batch + static_cast<size_t>(row) * row_w;
+    const float* xr = r;
+    const float* a = r + O;
+    const float adv = r[O + A], ret = r[O + A + 1];
+    float lp = 0.f;
+    for (int j = 0; j < A; ++j) {
+      float z = ba[j];
+      const float* wj = Wa + static_cast<size_t>(j) * O;
+      for (int k = 0; k < O; ++k) z += wj[k] * xr[k];
+      m[j] = std::tanh(z);
+      lp += -0.5f * (a[j] - m[j]) * (a[j] - m[j]) / var + c;
+    }
+    const float old = has_old ? r[O + A + 2] : lp;
+    const float ratio = std::exp(lp - old);
+    const float unc = ratio * adv, clp = std::min(std::max(ratio, 1.f - clip), 1.f + clip) * adv;
+    // d(-min(unclipped, clipped)) / d logp: nonzero where the unclipped term is the minimum or the ratio is inside
+    const float g_lp = (unc <= clp || (ratio > 1.f - clip && ratio < 1.f + clip)) ? -unc * inv_n : 0.f;
+    for (int j = 0; j < A; ++j) {
+      const float gz = g_lp * (a[j] - m[j]) / var * (1.f - m[j] * m[j]);
+      float* gj = gWa + static_cast<size_t>(j) * O;
+      for (int k = 0; k < O; ++k) gj[k] += gz * xr[k];
+      gba[j] += gz;
+    }
+    // value head: vf * mean((v - ret)^2)
+    float v = bc;
+    for (int k = 0; k < O; ++k) v += Wc[k] * xr[k];
+    const float gv = vf_coef * 2.f * (v - ret) * inv_n;
+    for (int k = 0; k < O; ++k) gWc[k] += gv * xr[k];
+    *gbc += gv;
+  }
+  return Status::Ok();
+}
+
+void AdamHost(float* p, const float* g, float* m, float* v, int64_t n, int64_t step, float lr, float b1, float b2,
+              float eps, float wd, float grad_scale) {
+  const float bc1 = 1.f - std::pow(b1, static_cast<float>(step));
+  const float bc2 = 1.f - std::pow(b2, static_cast<float>(step));
+  for (int64_t i = 0; i < n; ++i) {
+    const float gi = g[i] * grad_scale;
+    m[i] = b1 * m[i] + (1.f - b1) * gi;
+    v[i] = b2 * v[i] + (1.f - b2) * gi * gi;
+    p[i] -= lr * ((m[i] / bc1) / (std::sqrt(v[i] / bc2) + eps) + wd * p[i]);
+  }
+}
+
+Status GaeHost(const float* rewards, const float* values, const uint8_t* dones, float* adv, float* ret, int T, int N,
+               float gamma, float lam, double* stats) {
+  if (T < 0 || N < 0) return Status::InvalidArgument("gae: bad dimensions");
+  const float gl = static_cast<float>(static_cast<double>(gamma) * lam);
+  std::vector<float> last(static_cast<size_t>(N), 0.f);
+  double s1 = 0.0, s2 = 0.0;
+  // backward over time, vectorizable over the environments
+  for (int t = T - 1; t >= 0; --t) {
+    const float* r = rewards + static_cast<size_t>(t) * N;
+    const float* v0 = values + static_cast<size_t>(t) * N;
+    const float* v1 = v0 + N;
+    const uint8_t* d = dones + static_cast<size_t>(t) * N;
+    float* a = adv + static_cast<size_t>(t) * N;
+    float* rt = ret + static_cast<size_t>(t) * N;
+    for (int n = 0; n < N; ++n) {
+      const float nd = d[n] ? 0.f : 1.f;
+      const float delta = r[n] + gamma * nd * v1[n] - v0[n];
+      const float l = delta + gl * nd * last[n];
+      last[n] = l;
+      a[n] = l;
+      rt[n] = l + v0[n];
+    }
+    if (stats)
+      for (int n = 0; n < N; ++n) {
+        s1 += a[n];
+        s2 += static_cast<double>(a[n]) * a[n];
+      }
+  }
+  if (stats) {
+    stats[0] += s1;
+    stats[1] += s2;
+  }
+  return Status::Ok();
+}
+
+}  // namespace turbol

@@ -24,6 +24,21 @@ namespace turbol {
 
 uint64_t HostPhiloxWord(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, int which);
 
+// Host versions of the linear Gaussian policy's fused act / gradient passes
+// and of the Adam step (csrc/engines/policy_host.cpp); flat fp32 parameters
+// W_a [A, O], b_a [A], W_c [O], b_c.  The gradient is added into `grad`.
+Status LinGaussActHost(const float* x, const float* params, float* act, float* logp, int N, int O, int A, float stdv,
+                       uint64_t seed, uint32_t counter);
+Status LinGaussGradHost(const float* batch, int row_w, const float* params, float* grad, int N, int O, int A,
+                        float stdv, float clip, float vf_coef, bool has_old);
+void AdamHost(float* p, const float* g, float* m, float* v, int64_t n, int64_t step, float lr, float b1, float b2,
+              float eps, float wd, float grad_scale);
+// GAE over [T, N] (values [T + 1, N], dones as bytes): advantages and returns
+// in one backward sweep; stats (optional, float64 [2]) += sum and sum of
+// squares of the advantages.
+Status GaeHost(const float* rewards, const float* values, const uint8_t* dones, float* adv, float* ret, int T, int N,
+               float gamma, float lam, double* stats);
+
 // ---------------------------------------------------------------------------
 enum class EnvType { kLinear, kCartPole };
 

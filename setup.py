@@ -61,7 +61,9 @@ nvcc_flags = ARCH + [
     "-Xptxas=-v" if os.environ.get("TURBOL_PTXAS_VERBOSE") else "-Xptxas=-O3",
     "-DTURBOL_CUDA=1",
 ]
-cxx_flags = ["-O3", "-std=c++17", "-DTURBOL_CUDA=1", "-Wno-unused-function"]
+# -ffp-contract=off: host arithmetic that restates a device kernel (the linear
+# environment, the Philox draws) rounds every product and sum like it
+cxx_flags = ["-O3", "-std=c++17", "-ffp-contract=off", "-DTURBOL_CUDA=1", "-Wno-unused-function"]
 
 CPU_ONLY = os.environ.get("TURBOL_CPU_ONLY", "") not in ("", "0")
 
@@ -80,7 +82,8 @@ cpu_ext = CppExtension(
     name="turbol_b200.turbol_core",
     sources=cpu_sources(),
     include_dirs=[os.path.join(ROOT, "csrc/include"), os.path.join(ROOT, "csrc/kernels")],
-    extra_compile_args=["-O3", "-std=c++17", "-DTURBOL_CUDA=0", "-Wno-unused-function", "-Wno-unused-parameter"],
+    extra_compile_args=["-O3", "-std=c++17", "-ffp-contract=off", "-DTURBOL_CUDA=0", "-Wno-unused-function",
+                        "-Wno-unused-parameter"],
     extra_link_args=["-l:libstdc++.so.6"],
 )
 

@@ -62,6 +62,23 @@ def test_grpo_kernel(G, dev):
     assert torch.allclose(got, exp, atol=1e-5)
 
 
+@pytest.mark.parametrize("T,N", [(1, 5), (37, 130), (256, 4096)])
+def test_gae_host_sweep_matches_oracle(T, N):
+    """CPU tensors take the core's one-sweep GAE; it equals the float64 oracle
+    and accumulates the advantage sum and sum of squares."""
+    g = torch.Generator().manual_seed(T)
+    r = torch.randn(T, N, generator=g)
+    v = torch.randn(T + 1, N, generator=g)
+    d = torch.rand(T, N, generator=g) < 0.05
+    stats = torch.zeros(2, dtype=torch.float64)
+    a, rt = gae(r, v, d, 0.99, 0.95, stats=stats)
+    ea, er = ref.gae(r.double(), v.double(), d, 0.99, 0.95)
+    assert torch.allclose(a.double(), ea, atol=1e-4, rtol=1e-4)
+    assert torch.allclose(rt.double(), er, atol=1e-4, rtol=1e-4)
+    assert abs(float(stats[0]) - float(ea.sum())) < 1e-3 * max(1.0, float(ea.abs().sum()))
+    assert abs(float(stats[1]) - float((ea * ea).sum())) < 1e-3 * max(1.0, float((ea * ea).sum()))
+
+
 def test_static_scratch_gae_bound_cpu():
     """The allocation-free GAE entry point's size check (host arithmetic, no
     GPU): fits() agrees with the 1 MiB array for every shape probed, and under

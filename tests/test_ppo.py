@@ -42,6 +42,60 @@ def test_policy_engine_reference_api():
     assert not torch.equal(before, pe.net.fp.flat)
 
 
+@pytest.mark.parametrize("has_old", [False, True])
+def test_policy_engine_host_linear_gaussian_matches_autograd(has_old):
+    """On the CPU the linear Gaussian model acts and computes its gradient in
+    the core's host loops; the update equals the autograd path's, the log-prob
+    is the Gaussian density of the sample, and the noise is standard normal."""
+    O, A, N = 16, 4, 300
+    host = turbol.PolicyEngine(obs_dim=O, act_dim=A, device="cpu", seed=3)
+    eager = turbol.PolicyEngine(obs_dim=O, act_dim=A, device="cpu", seed=3)
+    host.initialize()
+    eager.initialize()
+    eager._host_fused = lambda: False
+    assert host._host_fused()
+    g = torch.Generator().manual_seed(5)
+    obs = torch.randn(N, O, generator=g)
+    act = (torch.rand(N, A, generator=g) * 2 - 1) * 0.9
+    adv, ret = torch.randn(N, 1, generator=g), torch.randn(N, 1, generator=g)
+    cols = [obs, act, adv, ret]
+    if has_old:
+        cols.append(torch.randn(N, 1, generator=g) * 0.3 - 4.0)
+    batch = torch.cat(cols, 1)
+    for _ in range(3):
+        assert host.update(batch).ok() and eager.update(batch).ok()
+    assert torch.allclose(host.net.fp.flat, eager.net.fp.flat, atol=2e-5, rtol=1e-4), \
+        (host.net.fp.flat - eager.net.fp.flat).abs().max()
+    x = torch.randn(4096, O)
+    a, lp = host.act(x)
+    assert a.shape == (4096, A) and lp.shape == (4096,) and float(a.abs().max()) <= 1.0
+    with torch.no_grad():
+        mean = host.net.actor(x)
+        assert torch.allclose(lp, host.net.gaussian_logprob(mean, a), atol=1e-4, rtol=1e-4)
+    assert not torch.equal(a, host.act(x)[0])
+    narrow = turbol.PolicyEngine(obs_dim=O, act_dim=A, device="cpu", seed=4, std=0.05)
+    narrow.initialize()
+    z = narrow.act(torch.zeros(1 << 15, O))[0] / 0.05
+    assert abs(float(z.mean())) < 0.03 and abs(float(z.std()) - 1.0) < 0.03
+    assert abs(float((z.abs() < 1).float().mean()) - 0.6827) < 0.015
+
+
+def test_host_adam_matches_the_oracle():
+    from turbol_b200.ops import reference as ref
+
+    n = 1001
+    g0 = torch.Generator().manual_seed(1)
+    p = torch.randn(n, generator=g0)
+    opt = FusedAdam(p.clone(), torch.zeros(n), lr=1e-3, weight_decay=0.01)
+    pr, mr, vr = p.clone().double(), torch.zeros(n, dtype=torch.float64), torch.zeros(n, dtype=torch.float64)
+    for step in range(1, 5):
+        grad = torch.randn(n, generator=g0)
+        opt.g.copy_(grad)
+        opt.step(grad_scale=0.5)
+        ref.adam_step(pr, grad.double(), mr, vr, step, 1e-3, wd=0.01, grad_scale=0.5)
+        assert torch.allclose(opt.p.double(), pr, atol=1e-6), step
+
+
 def test_policy_engine_discrete_ppo_update():
     pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu", hidden=(32,), discrete=True)
     pe.initialize()

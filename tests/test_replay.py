@@ -53,6 +53,41 @@ def test_push_batch_larger_than_capacity():
     assert sorted(o[:, 0].tolist()) == list(range(12, 20))
 
 
+def test_host_sample_indices_follow_the_philox_stream():
+    """Index i of sample call k is Philox(seed; i, k, 0, 0x52504C59) word 0,
+    reduced to [0, size) by multiply-shift (the device kernel's definition);
+    batch sizes that are not multiples of the host's 8-lane batches."""
+    from turbol_b200.ops import reference as ref
+
+    cap = 1000
+    b = turbol.RingBuffer(cap, 3, 1, "cpu", seed=77)
+    b.push_batch(_t(torch.randn(cap, 3)), _t(torch.randn(cap, 1)), _t(torch.randn(cap)),
+                 _t(torch.zeros(cap, dtype=torch.bool)))
+    for k, n in enumerate((37, 8, 1, 100)):
+        got = b.sample_indices(n).tolist()
+        exp = [(ref.philox4x32_10(77, i, k, 0, 0x52504C59)[0] * cap) >> 32 for i in range(n)]
+        assert got == exp, k
+
+
+def test_host_sample_equals_indices_then_gather():
+    """On the CPU, sample() draws the same indices as sample_indices() (same
+    counter stream) and returns the rows gather() returns for them."""
+    cap = 500
+    b1 = turbol.RingBuffer(cap, 5, 2, "cpu", seed=9)
+    b2 = turbol.RingBuffer(cap, 5, 2, "cpu", seed=9)
+    g = torch.Generator().manual_seed(2)
+    o, a, r = torch.randn(cap, 5, generator=g), torch.randn(cap, 2, generator=g), torch.randn(cap, generator=g)
+    d = torch.rand(cap, generator=g) < 0.3
+    for b in (b1, b2):
+        b.push_batch(_t(o), _t(a), _t(r), _t(d))
+    for n in (13, 64):
+        so, sa, sr, sd = turbol.Tensor(), turbol.Tensor(), turbol.Tensor(), turbol.Tensor()
+        assert b1.sample(n, so, sa, sr, sd).ok()
+        exp = b2.gather(b2.sample_indices(n))
+        for x, y in zip((so, sa, sr, sd), exp):
+            assert torch.equal(x.torch(), y)
+
+
 def test_uniform_sampling_chi_square():
     cap = 64
     b = turbol.RingBuffer(capacity=cap, obs_dim=1, act_dim=1, device="cpu", seed=7)

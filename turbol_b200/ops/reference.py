@@ -11,6 +11,21 @@ import torch
 import torch.nn.functional as F
 
 
+def philox4x32_10(seed: int, c0: int, c1: int, c2: int, c3: int = 0):
+    """Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11): the four output words
+    for key ``seed`` (64-bit) and counter (c0, c1, c2, c3), as the device and
+    host generators compute them."""
+    m0, m1, w0, w1 = 0xD2511F53, 0xCD9E8D57, 0x9E3779B9, 0xBB67AE85
+    mask = 0xFFFFFFFF
+    c = [c0 & mask, c1 & mask, c2 & mask, c3 & mask]
+    k0, k1 = seed & mask, (seed >> 32) & mask
+    for _ in range(10):
+        p0, p1 = m0 * c[0], m1 * c[2]
+        c = [((p1 >> 32) ^ c[1] ^ k0) & mask, p1 & mask, ((p0 >> 32) ^ c[3] ^ k1) & mask, p0 & mask]
+        k0, k1 = (k0 + w0) & mask, (k1 + w1) & mask
+    return c
+
+
 def gae(rewards, values, dones, gamma: float = 0.99, lam: float = 0.95):
     """GAE over [T, N] (values [T+1, N]); recurrence of the reference's
     turbol_vllm/src/cuda/gae.cu:31-44."""

@@ -4,7 +4,7 @@ from __future__ import annotations
 
 import torch
 
-from .._native import ops as _ops
+from .._native import core as _core, ops as _ops
 from . import reference as ref
 
 
@@ -15,6 +15,12 @@ def gae(rewards, values, dones, gamma: float = 0.99, lam: float = 0.95, stats=No
     advantages; ``scratch`` is the chunk-map workspace (allocated here if
     needed and not given)."""
     if not rewards.is_cuda:
+        if rewards.dtype == torch.float32 and values.dtype == torch.float32 and rewards.dim() == 2:
+            # one backward sweep in the core (the recurrence of ref.gae)
+            adv, ret = out if out is not None else (torch.empty_like(rewards), torch.empty_like(rewards))
+            d = dones if dones.dtype in (torch.bool, torch.uint8) else dones.to(torch.uint8)
+            _core().gae_host(rewards.contiguous(), values.contiguous(), d.contiguous(), adv, ret, stats, gamma, lam)
+            return adv, ret
         return ref.gae(rewards, values, dones, gamma, lam)
     adv, ret = out if out is not None else (torch.empty_like(rewards), torch.empty_like(rewards))
     d = dones if dones.dtype in (torch.bool, torch.uint8) else dones.to(torch.uint8)
@@ -87,8 +93,14 @@ class FusedAdam:
     def step(self, grad_scale: float = 1.0):
         if not self.p.is_cuda:
             self._host_step += 1
-            ref.adam_step(self.p.data, self.g, self.m, self.v, self._host_step, self.lr, self.betas[0],
-                          self.betas[1], self.eps, self.wd, grad_scale)
+            p = self.p.data
+            if all(t.dtype == torch.float32 and t.is_contiguous() for t in (p, self.g, self.m, self.v)):
+                # one pass in the core (the same update as ref.adam_step)
+                _core().adam_host(p, self.g, self.m, self.v, self._host_step, self.lr, self.betas[0], self.betas[1],
+                                  self.eps, self.wd, grad_scale)
+            else:
+                ref.adam_step(p, self.g, self.m, self.v, self._host_step, self.lr, self.betas[0], self.betas[1],
+                              self.eps, self.wd, grad_scale)
             if self.shadow is not None:
                 self.shadow.copy_(self.p)
             return

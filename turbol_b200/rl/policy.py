@@ -19,7 +19,8 @@ Here:
     computes its gradient in one fused kernel each (``lin_gauss_act`` /
     ``lin_gauss_grad``: Philox noise, clipped-PPO + value loss, block-reduced
     parameter gradients), so a step is four launches instead of an autograd
-    graph;
+    graph; on the CPU the same passes and Adam run as host loops in the core
+    (``lin_gauss_act_host`` / ``lin_gauss_grad_host`` / ``adam_host``);
   * ``forward(obs)`` without out-parameters returns ``(action, logprob)``,
     the form the reference README documents (README.md:149).
 """
@@ -76,6 +77,12 @@ class PolicyEngine:
         return (self.device.type == "cuda" and not self.hidden and not self.discrete and self.obs_dim <= 64
                 and self.act_dim <= 16)
 
+    def _host_fused(self) -> bool:
+        """On the CPU the same model runs the host versions of those passes
+        (``lin_gauss_act_host`` / ``lin_gauss_grad_host``): plain loops, no
+        per-operator dispatch for the small tensors."""
+        return self.device.type == "cpu" and not self.hidden and not self.discrete
+
     # -------------------------------------------------------------- acting
     @torch.no_grad()
     def act(self, obs: torch.Tensor):
@@ -87,14 +94,18 @@ class PolicyEngine:
             logp_all = F.log_softmax(logits, -1)
             a = torch.multinomial(logp_all.exp(), 1, generator=self._gen).squeeze(1)
             return a.to(torch.int32), logp_all.gather(1, a[:, None]).squeeze(1)
-        if self._fused():
-            from .._native import ops as _ops
+        if self._fused() or self._host_fused():
             x = obs.reshape(-1, self.obs_dim).contiguous()
             a = torch.empty(x.shape[0], self.act_dim, device=self.device)
             lp = torch.empty(x.shape[0], device=self.device)
             self._calls += 1
-            _ops().lin_gauss_act(x, self.net.fp.flat, a, lp, self.obs_dim, self.act_dim, self.std,
-                                 self.seed + 12345, self._calls & 0xFFFFFFFF)
+            if self._fused():
+                from .._native import ops as _ops
+                _ops().lin_gauss_act(x, self.net.fp.flat, a, lp, self.obs_dim, self.act_dim, self.std,
+                                     self.seed + 12345, self._calls & 0xFFFFFFFF)
+            else:
+                _core().lin_gauss_act_host(x, self.net.fp.flat.detach(), a, lp, self.obs_dim, self.act_dim, self.std,
+                                           self.seed + 12345, self._calls & 0xFFFFFFFF)
             return a, lp
         mean = self.net.actor(obs)
         noise = torch.randn(mean.shape, device=self.device, generator=self._gen)
@@ -141,6 +152,13 @@ class PolicyEngine:
             self.net.fp.grad.zero_()
             _ops().lin_gauss_grad(b.contiguous(), self.net.fp.flat, self.net.fp.grad, self.obs_dim, self.act_dim,
                                   self.std, self.clip, self.vf_coef, has_old)
+            self.opt.step()
+            return _core().Status()
+        if self._host_fused():
+            g = self.net.fp.grad
+            g.zero_()
+            _core().lin_gauss_grad_host(b.contiguous(), self.net.fp.flat.detach(), g, self.obs_dim, self.act_dim,
+                                        self.std, self.clip, self.vf_coef, has_old)
             self.opt.step()
             return _core().Status()
         obs = b[:, : self.obs_dim]
