@@ -714,6 +714,19 @@ PYBIND11_MODULE(turbol_core, m) {
         py::arg("rewards"), py::arg("values"), py::arg("dones"), py::arg("adv"), py::arg("ret"),
         py::arg("stats") = py::none(), py::arg("gamma") = 0.99f, py::arg("lam") = 0.95f);
 
+  m.def("ppo_minibatch_host",
+        [](const at::Tensor& flat, const at::Tensor& grad, const std::vector<int64_t>& dims_a,
+           const std::vector<int64_t>& dims_c, const at::Tensor& obs, const at::Tensor& act,
+           const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret, const at::Tensor& idx, float clip,
+           float vf_coef, float ent_coef, const at::Tensor& stats) {
+          if (flat.is_cuda() || obs.is_cuda()) throw std::invalid_argument("ppo_minibatch_host: CPU tensors");
+          throw_if(PpoCategoricalMinibatchHost(flat, grad, dims_a, dims_c, obs, act, old_logp, adv, ret, idx, clip,
+                                               vf_coef, ent_coef, stats));
+        },
+        py::arg("flat"), py::arg("grad"), py::arg("dims_actor"), py::arg("dims_critic"), py::arg("obs"),
+        py::arg("act"), py::arg("old_logp"), py::arg("adv"), py::arg("ret"), py::arg("idx"), py::arg("clip"),
+        py::arg("vf_coef"), py::arg("ent_coef"), py::arg("stats"));
+
   m.def("get_version", []() { return std::string("1.0.0"); });
   m.def("get_device_count", &GetCudaDeviceCount);
   m.def("get_memory_info",

@@ -131,15 +131,19 @@ Status LinGaussGradHost(const float* batch, int row_w, const float* p, float* g,
   return Status::Ok();
 }
 
-void AdamHost(float* p, const float* g, float* m, float* v, int64_t n, int64_t step, float lr, float b1, float b2,
-              float eps, float wd, float grad_scale) {
-  const float bc1 = 1.f - std::pow(b1, static_cast<float>(step));
-  const float bc2 = 1.f - std::pow(b2, static_cast<float>(step));
+void AdamHost(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+              int64_t n, int64_t step, float lr, float b1, float b2, float eps, float wd, float grad_scale) {
+  const float ibc1 = 1.f / (1.f - std::pow(b1, static_cast<float>(step)));
+  const float ibc2 = 1.f / (1.f - std::pow(b2, static_cast<float>(step)));
+  // distinct arrays (restrict), the bias corrections as multiplications and
+  // IEEE sqrt / divide: the loop vectorizes
   for (int64_t i = 0; i < n; ++i) {
     const float gi = g[i] * grad_scale;
-    m[i] = b1 * m[i] + (1.f - b1) * gi;
-    v[i] = b2 * v[i] + (1.f - b2) * gi * gi;
-    p[i] -= lr * ((m[i] / bc1) / (std::sqrt(v[i] / bc2) + eps) + wd * p[i]);
+    const float mi = b1 * m[i] + (1.f - b1) * gi;
+    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    p[i] -= lr * ((mi * ibc1) / (std::sqrt(vi * ibc2) + eps) + wd * p[i]);
   }
 }
 

@@ -33,6 +33,18 @@ Status LinGaussGradHost(const float* batch, int row_w, const float* params, floa
                         float stdv, float clip, float vf_coef, bool has_old);
 void AdamHost(float* p, const float* g, float* m, float* v, int64_t n, int64_t step, float lr, float b1, float b2,
               float eps, float wd, float grad_scale);
+// One PPO minibatch step of an actor-critic MLP pair on the host
+// (csrc/engines/mlp_host.cpp): actor widths dims_a (obs -> ... -> actions,
+// categorical), critic widths dims_c (obs -> ... -> 1), tanh hidden layers,
+// parameters laid out layer by layer (W [out, in], b [out]), actor first.
+// Rows idx of the rollout tensors; gradients added into grad; stats (fp32
+// [6]) += policy-loss sum, value-loss sum, entropy sum, approximate-KL sum,
+// clipped count and row count.
+Status PpoCategoricalMinibatchHost(const at::Tensor& flat, const at::Tensor& grad, const std::vector<int64_t>& dims_a,
+                                   const std::vector<int64_t>& dims_c, const at::Tensor& obs, const at::Tensor& act,
+                                   const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret,
+                                   const at::Tensor& idx, float clip, float vf_coef, float ent_coef,
+                                   const at::Tensor& stats);
 // GAE over [T, N] (values [T + 1, N], dones as bytes): advantages and returns
 // in one backward sweep; stats (optional, float64 [2]) += sum and sum of
 // squares of the advantages.

@@ -25,6 +25,24 @@ def test_ppo_cpu_learns_cartpole():
     assert last > 2 * first and last > 60, (first, last)
 
 
+@pytest.mark.parametrize("hidden,ent", [((64, 64), 0.0), ((32,), 0.01)])
+def test_cpu_ppo_host_minibatch_matches_autograd(hidden, ent):
+    """The CPU trainer's minibatch step in the core (no autograd) gives the
+    same update and loss statistics as the autograd path."""
+    cfg = PPOConfig(num_envs=64, rollout_steps=8, hidden=hidden, epochs=2, minibatch_size=64, seed=2, ent_coef=ent)
+    a = PPOTrainer(cfg, device="cpu")
+    b = PPOTrainer(cfg, device="cpu")
+    b.host_update = False
+    for t in (a, b):
+        t._rollout_cpu()
+    assert torch.equal(a.obs_buf, b.obs_buf) and torch.equal(a.adv, b.adv)
+    for t in (a, b):
+        t._update_cpu()
+    assert torch.allclose(a.policy.fp.flat, b.policy.fp.flat, atol=2e-6, rtol=1e-5), \
+        (a.policy.fp.flat - b.policy.fp.flat).abs().max()
+    assert torch.allclose(a.loss_stats, b.loss_stats, atol=1e-3, rtol=1e-4), (a.loss_stats, b.loss_stats)
+
+
 def test_policy_engine_reference_api():
     pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu")
     assert pe.initialize().ok()

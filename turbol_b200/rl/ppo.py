@@ -319,15 +319,26 @@ class PPOTrainer:
         act, logp, adv, ret = (x.reshape(B) for x in (self.act_buf, self.logp_buf, self.adv, self.ret))
         if cfg.norm_adv:
             adv = (adv - adv.mean()) / (adv.std() + 1e-8)
+        # the minibatch step in the core (forward, loss and hand-written
+        # backward, no autograd graph), or through autograd when host_update
+        # is off; both compute the same gradient
+        host = getattr(self, "host_update", True)
+        dims_a, dims_c = [4, *cfg.hidden, 2], [4, *cfg.hidden, 1]
+        flat = self.policy.fp.flat.detach()
+        adv = adv.contiguous()
         for _ in range(cfg.epochs):
             perm = torch.randperm(B, generator=self._cpu_gen)
             for k in range(cfg.n_minibatches):
                 idx = perm[k * cfg.minibatch_size:(k + 1) * cfg.minibatch_size]
                 self.policy.fp.grad.zero_()
-                logits, v = self.policy(obs[idx])
-                loss = ppo_categorical_loss(logits, v, act[idx], logp[idx], adv[idx], ret[idx], cfg.clip,
-                                            cfg.vf_coef, cfg.ent_coef, stats=self.loss_stats)
-                loss.backward()
+                if host:
+                    _core().ppo_minibatch_host(flat, self.flat_grad, dims_a, dims_c, obs, act, logp, adv, ret, idx,
+                                               cfg.clip, cfg.vf_coef, cfg.ent_coef, self.loss_stats)
+                else:
+                    logits, v = self.policy(obs[idx])
+                    loss = ppo_categorical_loss(logits, v, act[idx], logp[idx], adv[idx], ret[idx], cfg.clip,
+                                                cfg.vf_coef, cfg.ent_coef, stats=self.loss_stats)
+                    loss.backward()
                 scale = self.grad_sync(self.flat_grad) if self.grad_sync is not None else 1.0
                 self.opt.step(grad_scale=scale)
 
