@@ -60,6 +60,12 @@ class PPOConfig:
     compute_dtype: str = "bf16"  # "bf16" (tensor cores, fp32 master weights) or "fp32"
     cuda_graphs: bool = True
     env: str = "cartpole"
+    # CPU device: intra-op threads during an iteration (0 = automatic: one
+    # thread when the minibatch's matrix products are small, where forking
+    # the thread pool per operator costs more than the arithmetic; measured
+    # 60.8 K vs 44.6 K env-steps/s on 8 cores for 256 envs, MLP 64-64,
+    # minibatch 64); the process's setting is restored after the iteration
+    cpu_threads: int = 0
 
     @property
     def batch(self) -> int:
@@ -348,8 +354,18 @@ class PPOTrainer:
         lazily by :meth:`metrics`, which synchronizes)."""
         cfg = self.cfg
         if not self.cuda:
-            self._rollout_cpu()
-            self._update_cpu()
+            prev = torch.get_num_threads()
+            want = cfg.cpu_threads
+            if want <= 0:
+                want = 1 if cfg.minibatch_size * max(cfg.hidden or (1,)) <= 65536 else prev
+            if want != prev:
+                torch.set_num_threads(want)
+            try:
+                self._rollout_cpu()
+                self._update_cpu()
+            finally:
+                if want != prev:
+                    torch.set_num_threads(prev)
             self.iteration += 1
             return
         if cfg.cuda_graphs and self._graphs is None:
