@@ -47,17 +47,8 @@ class TPReplicaSync:
             raise ValueError("TPReplicaSync needs the trainer's fp32 master weights")
         self.model = model
         cfg = model.cfg
-        self.tp, self.rank = model.tp, model.rank
         dev = model.device
-        # layout of the full replica (bf16) and of its fp32 tensors
-        self.full_offsets, self.full_numel = self._full_layout(cfg, model)
-        self.f32_offsets, off = {}, 0
-        for name, (_, shape) in self.full_offsets.items():
-            if name.endswith(_F32_NAMES):
-                self.f32_offsets[name] = (off, shape)
-                off += (math.prod(shape) + ALIGN - 1) // ALIGN * ALIGN
-        self.f32_numel = off
-        self.bf16_bytes = _align(self.full_numel * 2)
+        self._layout(model)
         self.pb = PeerBuffers(self.bf16_bytes + _align(self.f32_numel * 4), group, device=dev.index)
         shadow = self.pb.tensor(0, self.full_numel, torch.bfloat16)
         self.full = DecoderLM(cfg, dev, layers=model.layers, embed=model.has_embed, head=model.has_head,
@@ -73,6 +64,19 @@ class TPReplicaSync:
         self.segs = t.to(dev)
         self.n_seg = len(segs)
         self.bytes_sent = sum(s[5] * s[6] for s in segs if s[8]) * (self.tp - 1)
+
+    def _layout(self, model):
+        """Offsets of the full replica (bf16) and of its fp32 tensors in the
+        peer buffer: [bf16 replica | fp32 norms and QKV bias]."""
+        self.tp, self.rank = model.tp, model.rank
+        self.full_offsets, self.full_numel = self._full_layout(model.cfg, model)
+        self.f32_offsets, off = {}, 0
+        for name, (_, shape) in self.full_offsets.items():
+            if name.endswith(_F32_NAMES):
+                self.f32_offsets[name] = (off, shape)
+                off += (math.prod(shape) + ALIGN - 1) // ALIGN * ALIGN
+        self.f32_numel = off
+        self.bf16_bytes = _align(self.full_numel * 2)
 
     @staticmethod
     def _full_layout(cfg, model):
