@@ -37,6 +37,12 @@ void philox4(uint64_t seed, uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, 
   for (int i = 0; i < 4; ++i) out[i] = c[i];
 }
 
+// tanh through one exp: tanh(z) = sign(z) (1 - e^{-2|z|}) / (1 + e^{-2|z|}) (no overflow for large |z|)
+inline float tanh_exp(float z) {
+  const float e = std::exp(-2.f * std::fabs(z));
+  return std::copysign((1.f - e) / (1.f + e), z);
+}
+
 float u01(uint32_t x) { return static_cast<float>(x >> 8) * (1.0f / 16777216.0f); }
 float u01_open(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
 
@@ -70,7 +76,7 @@ Status LinGaussActHost(const float* x, const float* p, float* act, float* logp, 
         float z = b[j];
         const float* wj = W + static_cast<size_t>(j) * O;
         for (int k = 0; k < O; ++k) z += wj[k] * xr[k];
-        const float m = std::tanh(z);
+        const float m = tanh_exp(z);
         const float a = std::min(1.f, std::max(-1.f, m + stdv * nz[t]));
         ar[j] = a;
         lp += -0.5f * (a - m) * (a - m) / var + c;
