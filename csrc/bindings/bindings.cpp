@@ -727,6 +727,29 @@ PYBIND11_MODULE(turbol_core, m) {
         py::arg("act"), py::arg("old_logp"), py::arg("adv"), py::arg("ret"), py::arg("idx"), py::arg("clip"),
         py::arg("vf_coef"), py::arg("ent_coef"), py::arg("stats"));
 
+  m.def("ppo_update_host",
+        [](const at::Tensor& flat, const at::Tensor& grad, const at::Tensor& m1, const at::Tensor& m2, int64_t step,
+           const std::vector<int64_t>& dims_a, const std::vector<int64_t>& dims_c, const at::Tensor& obs,
+           const at::Tensor& act, const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret,
+           const at::Tensor& perms, int64_t minibatch, float clip, float vf_coef, float ent_coef, float lr, float b1,
+           float b2, float eps, float wd, const at::Tensor& stats) {
+          if (flat.is_cuda() || obs.is_cuda()) throw std::invalid_argument("ppo_update_host: CPU tensors");
+          Status st;
+          int64_t last;
+          {
+            py::gil_scoped_release release;
+            last = PpoCategoricalUpdateHost(flat, grad, m1, m2, step, dims_a, dims_c, obs, act, old_logp, adv, ret,
+                                            perms, minibatch, clip, vf_coef, ent_coef, lr, b1, b2, eps, wd, stats,
+                                            &st);
+          }
+          throw_if(st);
+          return last;
+        },
+        py::arg("flat"), py::arg("grad"), py::arg("m"), py::arg("v"), py::arg("step"), py::arg("dims_actor"),
+        py::arg("dims_critic"), py::arg("obs"), py::arg("act"), py::arg("old_logp"), py::arg("adv"), py::arg("ret"),
+        py::arg("perms"), py::arg("minibatch"), py::arg("clip"), py::arg("vf_coef"), py::arg("ent_coef"),
+        py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("stats"));
+
   m.def("get_version", []() { return std::string("1.0.0"); });
   m.def("get_device_count", &GetCudaDeviceCount);
   m.def("get_memory_info",

@@ -8,6 +8,7 @@
 #include <ATen/ATen.h>
 #include <c10/core/InferenceMode.h>
 
+#include <algorithm>
 #include <cmath>
 #include <vector>
 
@@ -157,6 +158,37 @@ Status PpoCategoricalMinibatchHost(const at::Tensor& flat, const at::Tensor& gra
   st[4] += static_cast<float>(s_clip);
   st[5] += static_cast<float>(B);
   return Status::Ok();
+}
+
+int64_t PpoCategoricalUpdateHost(const at::Tensor& flat, const at::Tensor& grad, const at::Tensor& m,
+                                  const at::Tensor& v, int64_t step, const std::vector<int64_t>& dims_a,
+                                  const std::vector<int64_t>& dims_c, const at::Tensor& obs, const at::Tensor& act,
+                                  const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret,
+                                  const at::Tensor& perms, int64_t minibatch, float clip, float vf_coef,
+                                  float ent_coef, float lr, float b1, float b2, float eps, float wd,
+                                  const at::Tensor& stats, Status* st) {
+  *st = Status::Ok();
+  if (perms.dim() != 2 || perms.scalar_type() != at::kLong || !perms.is_contiguous() || minibatch <= 0 ||
+      m.numel() != flat.numel() || v.numel() != flat.numel() || m.scalar_type() != at::kFloat ||
+      v.scalar_type() != at::kFloat || !m.is_contiguous() || !v.is_contiguous()) {
+    *st = Status::InvalidArgument("ppo update: perms [epochs, rows] int64, moments like the parameters");
+    return step;
+  }
+  const int64_t rows = perms.size(1), n_mb = rows / minibatch;
+  float* g = grad.data_ptr<float>();
+  const int64_t n = flat.numel();
+  for (int64_t e = 0; e < perms.size(0); ++e) {
+    const at::Tensor pe = perms[e];
+    for (int64_t k = 0; k < n_mb; ++k) {
+      std::fill(g, g + n, 0.f);
+      *st = PpoCategoricalMinibatchHost(flat, grad, dims_a, dims_c, obs, act, old_logp, adv, ret,
+                                        pe.narrow(0, k * minibatch, minibatch), clip, vf_coef, ent_coef, stats);
+      if (!st->ok()) return step;
+      AdamHost(flat.data_ptr<float>(), g, m.data_ptr<float>(), v.data_ptr<float>(), n, ++step, lr, b1, b2, eps, wd,
+               1.f);
+    }
+  }
+  return step;
 }
 
 }  // namespace turbol

@@ -45,6 +45,17 @@ Status PpoCategoricalMinibatchHost(const at::Tensor& flat, const at::Tensor& gra
                                    const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret,
                                    const at::Tensor& idx, float clip, float vf_coef, float ent_coef,
                                    const at::Tensor& stats);
+// A whole PPO update on the host: for every epoch e and minibatch k, the rows
+// perms[e, k*minibatch : (k+1)*minibatch] go through
+// PpoCategoricalMinibatchHost and one Adam step (moments m, v; the step
+// counter continues from `step`).  Returns the last step number.
+int64_t PpoCategoricalUpdateHost(const at::Tensor& flat, const at::Tensor& grad, const at::Tensor& m,
+                                  const at::Tensor& v, int64_t step, const std::vector<int64_t>& dims_a,
+                                  const std::vector<int64_t>& dims_c, const at::Tensor& obs, const at::Tensor& act,
+                                  const at::Tensor& old_logp, const at::Tensor& adv, const at::Tensor& ret,
+                                  const at::Tensor& perms, int64_t minibatch, float clip, float vf_coef,
+                                  float ent_coef, float lr, float b1, float b2, float eps, float wd,
+                                  const at::Tensor& stats, Status* st);
 // GAE over [T, N] (values [T + 1, N], dones as bytes): advantages and returns
 // in one backward sweep; stats (optional, float64 [2]) += sum and sum of
 // squares of the advantages.

@@ -36,11 +36,16 @@ def test_cpu_ppo_host_minibatch_matches_autograd(hidden, ent):
     for t in (a, b):
         t._rollout_cpu()
     assert torch.equal(a.obs_buf, b.obs_buf) and torch.equal(a.adv, b.adv)
-    for t in (a, b):
+    c = PPOTrainer(cfg, device="cpu")  # host minibatch steps, driven from Python one at a time
+    c.grad_sync = lambda g: 1.0
+    c._rollout_cpu()
+    for t in (a, b, c):
         t._update_cpu()
-    assert torch.allclose(a.policy.fp.flat, b.policy.fp.flat, atol=2e-6, rtol=1e-5), \
-        (a.policy.fp.flat - b.policy.fp.flat).abs().max()
-    assert torch.allclose(a.loss_stats, b.loss_stats, atol=1e-3, rtol=1e-4), (a.loss_stats, b.loss_stats)
+    for t in (b, c):
+        assert torch.allclose(a.policy.fp.flat, t.policy.fp.flat, atol=2e-6, rtol=1e-5), \
+            (a.policy.fp.flat - t.policy.fp.flat).abs().max()
+        assert torch.allclose(a.loss_stats, t.loss_stats, atol=1e-3, rtol=1e-4), (a.loss_stats, t.loss_stats)
+    assert a.opt._host_step == b.opt._host_step == c.opt._host_step == cfg.epochs * cfg.n_minibatches
 
 
 def test_policy_engine_reference_api():

@@ -332,6 +332,16 @@ class PPOTrainer:
         dims_a, dims_c = [4, *cfg.hidden, 2], [4, *cfg.hidden, 1]
         flat = self.policy.fp.flat.detach()
         adv = adv.contiguous()
+        if host and self.grad_sync is None:
+            # the whole update in one call: the same minibatch order (one
+            # permutation per epoch from the trainer's generator) and Adam steps
+            perms = torch.stack([torch.randperm(B, generator=self._cpu_gen) for _ in range(cfg.epochs)])
+            o = self.opt
+            o._host_step = int(_core().ppo_update_host(
+                flat, self.flat_grad, o.m, o.v, o._host_step, dims_a, dims_c, obs, act, logp, adv, ret, perms,
+                cfg.minibatch_size, cfg.clip, cfg.vf_coef, cfg.ent_coef, o.lr, o.betas[0], o.betas[1], o.eps, o.wd,
+                self.loss_stats))
+            return
         for _ in range(cfg.epochs):
             perm = torch.randperm(B, generator=self._cpu_gen)
             for k in range(cfg.n_minibatches):
