@@ -32,4 +32,11 @@ rm -rf "$HERE/_ref/turbol" "$HERE/_ref/examples"
 cp -r "$SRC/turbol_vllm/python/turbol" "$HERE/_ref/"
 cp -r "$SRC/turbol_vllm/examples" "$HERE/_ref/examples"
 cp "$BLD"/benchmark_components "$BLD"/benchmark_tensor "$BLD"/benchmark_attention "$BLD"/turbol_example "$HERE/_ref/bin/"
+# The reference's attention kernel is compiled into its library, but nothing it
+# builds calls it (its benchmark_attention only prints sizes).  Its extern "C"
+# launcher flash_attention_forward goes into a shared library of its own, from
+# the unmodified source, so benchmarks/benchmark_attention.py can time it.
+mkdir -p "$HERE/_ref/lib"
+nvcc -O3 -std=c++17 -gencode arch=compute_100,code=sm_100 -shared -Xcompiler -fPIC \
+  "$SRC/turbol_vllm/src/cuda/attention.cu" -o "$HERE/_ref/lib/libref_attention.so"
 echo "reference installed in $HERE/_ref"
