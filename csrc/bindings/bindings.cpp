@@ -750,6 +750,25 @@ PYBIND11_MODULE(turbol_core, m) {
         py::arg("perms"), py::arg("minibatch"), py::arg("clip"), py::arg("vf_coef"), py::arg("ent_coef"),
         py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("stats"));
 
+  m.def("ppo_cartpole_rollout_host",
+        [](GPUEnvironment& env, const at::Tensor& flat, const std::vector<int64_t>& dims_a,
+           const std::vector<int64_t>& dims_c, const at::Tensor& obs_buf, const at::Tensor& act_buf,
+           const at::Tensor& logp_buf, const at::Tensor& val_buf, const at::Tensor& rew_buf, const at::Tensor& done_buf,
+           uint64_t seed, uint64_t counter) {
+          Status st;
+          {
+            py::gil_scoped_release release;
+            st = PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, obs_buf, act_buf, logp_buf, val_buf, rew_buf,
+                                        done_buf, seed, counter);
+          }
+          throw_if(st);
+        },
+        "The CPU PPO rollout on CartPole (T = obs_buf.shape[0] steps) in one call: policy forward, sampling, "
+        "environment step, buffers.",
+        py::arg("env"), py::arg("flat"), py::arg("dims_actor"), py::arg("dims_critic"), py::arg("obs_buf"),
+        py::arg("act_buf"), py::arg("logp_buf"), py::arg("val_buf"), py::arg("rew_buf"), py::arg("done_buf"),
+        py::arg("seed"), py::arg("counter"));
+
   m.def("get_version", []() { return std::string("1.0.0"); });
   m.def("get_device_count", &GetCudaDeviceCount);
   m.def("get_memory_info",

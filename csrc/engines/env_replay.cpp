@@ -243,31 +243,42 @@ Status GPUEnvironment::StepInto(const at::Tensor& action, at::Tensor& obs, at::T
                                    seed_, cp_.params(), StreamFor(s));
     return check_cuda(e, "cartpole_step");
   }
-  float* st = s.data_ptr<float>();
+  TURBOL_RETURN_IF_ERROR(StepCartPoleHost(a.data_ptr<int>(), reward.data_ptr<float>(),
+                                          static_cast<uint8_t*>(done.data_ptr())));
+  obs.view({num_envs_, 4}).copy_(s);
+  return Status::Ok();
+}
+
+Status GPUEnvironment::StepCartPoleHost(const int* action, float* reward, uint8_t* done) {
+  if (type_ != EnvType::kCartPole || device_.is_cuda())
+    return Status::InvalidArgument("StepCartPoleHost: a CPU CartPole environment");
+  float* st = states_.torch().data_ptr<float>();
   float* stats = stats_.data<float>();
+  int* ep_len = ep_len_.data<int>();
+  float* ep_ret = ep_ret_.data<float>();
+  int* ep_count = ep_count_.data<int>();
   for (int i = 0; i < num_envs_; ++i) {
     float* x = st + 4 * static_cast<size_t>(i);
-    const bool term = cartpole_physics(x, a.data_ptr<int>()[i], cp_);
-    const int len = ep_len_.data<int>()[i] + 1;
-    const float ret = ep_ret_.data<float>()[i] + 1.f;
+    const bool term = cartpole_physics(x, action[i], cp_);
+    const int len = ep_len[i] + 1;
+    const float ret = ep_ret[i] + 1.f;
     const bool fin = term || len >= cp_.max_steps;
     if (fin) {
-      const unsigned e = static_cast<unsigned>(ep_count_.data<int>()[i]) + 1;
-      ep_count_.data<int>()[i] = static_cast<int>(e);
+      const unsigned e = static_cast<unsigned>(ep_count[i]) + 1;
+      ep_count[i] = static_cast<int>(e);
       cartpole_initial(seed_, i, e, cp_.init_range, x);
-      ep_len_.data<int>()[i] = 0;
-      ep_ret_.data<float>()[i] = 0.f;
+      ep_len[i] = 0;
+      ep_ret[i] = 0.f;
       stats[0] += ret;
       stats[1] += 1.f;
       stats[2] += static_cast<float>(len);
     } else {
-      ep_len_.data<int>()[i] = len;
-      ep_ret_.data<float>()[i] = ret;
+      ep_len[i] = len;
+      ep_ret[i] = ret;
     }
-    reward.data_ptr<float>()[i] = 1.f;
-    static_cast<uint8_t*>(done.data_ptr())[i] = fin ? 1 : 0;
+    reward[i] = 1.f;
+    done[i] = fin ? 1 : 0;
   }
-  obs.view({num_envs_, 4}).copy_(s);
   return Status::Ok();
 }
 

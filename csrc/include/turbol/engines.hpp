@@ -85,6 +85,10 @@ class GPUEnvironment {
   Status Step(const Tensor& action, Tensor* obs, Tensor* reward, Tensor* done);
   // Writes into caller-owned tensors of the right shape/dtype (no allocation).
   Status StepInto(const at::Tensor& action, at::Tensor& obs, at::Tensor& reward, at::Tensor& done);
+  // CPU CartPole only: one step from int32 actions [N] on raw pointers; the
+  // state advances in place (finished episodes reset), reward / done [N] are
+  // written, episode statistics accumulate.  No observation copy.
+  Status StepCartPoleHost(const int* action, float* reward, uint8_t* done);
   Tensor Observe() const { return states_.Clone(); }
   // The live state tensor (CartPole: [N, 4]); used by the fused PPO rollout.
   at::Tensor& StateTensor() { return states_.torch(); }
@@ -242,5 +246,17 @@ class RewardEngine {
   double mean_ = 0.0, m2_ = 0.0;
   int64_t count_ = 0;
 };
+
+// The CPU PPO rollout on CartPole in one call: T steps of (record the state in
+// obs_buf[t], actor / critic forward of the categorical MLP policy, an action
+// drawn from the softmax by inverse CDF with the Philox uniform of
+// (seed; env, t, counter), its log-probability and the value into act_buf[t],
+// logp_buf[t], val_buf[t], then one host CartPole step into rew_buf[t],
+// done_buf[t]), and the value of the final state into val_buf[T].  Layout of
+// flat and the widths as for PpoCategoricalMinibatchHost.
+Status PpoCartPoleRolloutHost(GPUEnvironment* env, const at::Tensor& flat, const std::vector<int64_t>& dims_a,
+                              const std::vector<int64_t>& dims_c, const at::Tensor& obs_buf, const at::Tensor& act_buf,
+                              const at::Tensor& logp_buf, const at::Tensor& val_buf, const at::Tensor& rew_buf,
+                              const at::Tensor& done_buf, uint64_t seed, uint64_t counter);
 
 }  // namespace turbol

@@ -48,6 +48,100 @@ def test_cpu_ppo_host_minibatch_matches_autograd(hidden, ent):
     assert a.opt._host_step == b.opt._host_step == c.opt._host_step == cfg.epochs * cfg.n_minibatches
 
 
+@pytest.mark.parametrize("hidden,B,scale", [((64, 64), 64, 1.0), ((20, 37), 13, 0.3), ((48,), 7, 4.0), ((), 5, 1.0)])
+def test_host_minibatch_gradient_matches_fp64_autograd(hidden, B, scale):
+    """The core's minibatch step (register-tiled products, vector tanh)
+    against float64 autograd of the same actor / critic MLPs and PPO loss:
+    widths that are not multiples of the vector width, row counts that are not
+    multiples of 4, saturated (scale 4) and near-linear (scale 0.3) hidden
+    layers."""
+    from turbol_b200._native import core
+    g = torch.Generator().manual_seed(3)
+    O, A, N = 4, 3, 97
+    clip, vf, ent = 0.2, 0.5, 0.01
+    dims_a, dims_c = [O, *hidden, A], [O, *hidden, 1]
+    parts = []
+    for dims in (dims_a, dims_c):
+        for i, o in zip(dims[:-1], dims[1:]):
+            parts += [torch.randn(o * i, generator=g) * scale / i ** 0.5, torch.randn(o, generator=g) * 0.1]
+    flat = torch.cat(parts)
+    obs = torch.randn(N, O, generator=g) * 2
+    act = torch.randint(0, A, (N,), generator=g, dtype=torch.int32)
+    old_logp = torch.randn(N, generator=g) * 0.3 - 1.1
+    adv, ret = torch.randn(N, generator=g), torch.randn(N, generator=g)
+    idx = torch.randperm(N, generator=g)[:B]
+    grad, stats = torch.zeros_like(flat), torch.zeros(6)
+    core().ppo_minibatch_host(flat, grad, dims_a, dims_c, obs, act, old_logp, adv, ret, idx, clip, vf, ent, stats)
+
+    p64 = flat.double().requires_grad_()
+    x = obs[idx].double()
+
+    def mlp(dims, off):
+        h = x
+        for li, (i, o) in enumerate(zip(dims[:-1], dims[1:])):
+            W = p64[off:off + o * i].view(o, i)
+            b = p64[off + o * i:off + o * i + o]
+            off += o * i + o
+            h = h @ W.t() + b
+            if li + 2 < len(dims):
+                h = torch.tanh(h)
+        return h, off
+
+    logits, off = mlp(dims_a, 0)
+    value = mlp(dims_c, off)[0].squeeze(1)
+    lp_all = torch.log_softmax(logits, -1)
+    lp = lp_all.gather(1, act[idx].long().view(-1, 1)).squeeze(1)
+    ratio = torch.exp(lp - old_logp[idx].double())
+    a_, r_ = adv[idx].double(), ret[idx].double()
+    pg = -torch.min(ratio * a_, ratio.clamp(1 - clip, 1 + clip) * a_)
+    entropy = -(lp_all.exp() * lp_all).sum(-1)
+    loss = pg.mean() + vf * (0.5 * (value - r_) ** 2).mean() - ent * entropy.mean()
+    loss.backward()
+    assert torch.allclose(grad.double(), p64.grad, rtol=1e-4, atol=1e-6), (grad.double() - p64.grad).abs().max()
+    assert abs(stats[0].item() - pg.sum().item()) < 1e-4 * max(1.0, abs(pg.sum().item()))
+    assert abs(stats[2].item() - entropy.sum().item()) < 1e-4 * entropy.sum().item() and stats[5].item() == B
+
+
+def test_cpu_host_rollout_matches_policy_and_environment():
+    """The one-call CPU rollout (ppo_cartpole_rollout_host): the recorded
+    observations replay bit-exactly through a second environment stepped with
+    the recorded actions; log-probabilities and values equal the torch
+    policy's; the actions follow the policy's probabilities; the same seed and
+    iteration give the same rollout."""
+    cfg = PPOConfig(num_envs=256, rollout_steps=16, hidden=(32, 24), seed=4)
+    tr = PPOTrainer(cfg, device="cpu")
+    with torch.no_grad():  # a policy that is not near-uniform, so the sampling test has power
+        tr.policy.actor_params[-2].mul_(60.0)
+    s0 = tr.state.clone()
+    tr._rollout_cpu()
+    T, N = cfg.rollout_steps, cfg.num_envs
+    assert torch.equal(tr.obs_buf[0], s0)
+    env = turbol.GPUEnvironment(N, 4, 2, "cpu", "cartpole", seed=tr.env.seed())
+    assert torch.equal(env.state(), s0)
+    obs, rew, done = torch.empty(N, 4), torch.empty(N), torch.empty(N, dtype=torch.uint8)
+    for t in range(T):
+        env.step_into(tr.act_buf[t], obs, rew, done)
+        assert torch.equal(obs, tr.obs_buf[t + 1] if t + 1 < T else tr.state), t
+        assert torch.equal(rew, tr.rew_buf[t]) and torch.equal(done, tr.done_buf[t]), t
+    with torch.no_grad():
+        logits, v = tr.policy(tr.obs_buf.view(T * N, 4))
+        lp_all = torch.log_softmax(logits, -1)
+        lp = lp_all.gather(1, tr.act_buf.view(-1, 1).long()).squeeze(1)
+        assert torch.allclose(lp, tr.logp_buf.view(-1), atol=2e-5, rtol=1e-5)
+        assert torch.allclose(v, tr.val_buf[:T].reshape(-1), atol=2e-5, rtol=1e-5)
+        assert torch.allclose(tr.policy.critic(tr.state), tr.val_buf[T], atol=2e-5, rtol=1e-5)
+    p1 = lp_all[:, 1].exp().double()
+    n1 = (tr.act_buf == 1).sum().item()
+    sd = (p1 * (1 - p1)).sum().sqrt().item()
+    assert 0.02 < p1.mean().item() < 0.98 and abs(n1 - p1.sum().item()) < 5 * sd, (n1, p1.sum().item(), sd)
+    again = PPOTrainer(cfg, device="cpu")
+    with torch.no_grad():
+        again.policy.actor_params[-2].mul_(60.0)
+    again._rollout_cpu()
+    for name in ("obs_buf", "act_buf", "logp_buf", "val_buf", "rew_buf", "done_buf"):
+        assert torch.equal(getattr(tr, name), getattr(again, name)), name
+
+
 def test_policy_engine_reference_api():
     pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu")
     assert pe.initialize().ok()

@@ -297,6 +297,18 @@ class PPOTrainer:
     # ------------------------------------------------------------------ CPU
     def _rollout_cpu(self):
         T = self.cfg.rollout_steps
+        if getattr(self, "host_rollout", True):
+            # the T steps in one call into the core: policy forward, sampling
+            # (Philox uniform of (policy seed; env, step, iteration), inverse
+            # CDF), environment step and buffers; the loop below is the
+            # torch-op path with the same buffer layout
+            cfg = self.cfg
+            _core().ppo_cartpole_rollout_host(self.env, self.policy.fp.flat.detach(), [4, *cfg.hidden, 2],
+                                              [4, *cfg.hidden, 1], self.obs_buf, self.act_buf, self.logp_buf,
+                                              self.val_buf, self.rew_buf, self.done_buf, self.policy_seed,
+                                              self.iteration)
+            gae(self.rew_buf, self.val_buf, self.done_buf, cfg.gamma, cfg.lam, out=(self.adv, self.ret))
+            return
         with torch.no_grad():
             for t in range(T):
                 logits, v = self.policy(self.state)
