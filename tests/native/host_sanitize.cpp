@@ -6,8 +6,11 @@
 // alongside (the reference's ExportJSON re-locked its own mutex,
 // turbol_vllm/src/profiler/profiler.cpp:192-200), the TCP rendezvous store
 // with a server thread per client, the KV block allocator through many
-// allocate/append/free cycles, and the file formats (Config, TFRecord event
-// files, Prometheus text, JSONL datasets) through write/read round trips.
+// allocate/append/free cycles, the file formats (Config, TFRecord event
+// files, Prometheus text, JSONL datasets) through write/read round trips, and
+// the CPU trainer's host engines (CartPole rollout, PPO minibatch step and
+// update with Adam, GAE) on sizes that are not multiples of the vector tiles,
+// from two threads at once.
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -16,16 +19,17 @@
 #include <thread>
 #include <vector>
 
+#include <ATen/ATen.h>
+#include <ATen/CPUGeneratorImpl.h>
+
 #include "kernels.h"
 #include "turbol/config.hpp"
+#include "turbol/engines.hpp"
 #include "turbol/observability.hpp"
 #include "turbol/runtime.hpp"
 
-// The host core's only kernel dependency (TensorUtils on CUDA tensors); the
-// sanitizer build links no kernels, and CPU tensors never reach it.
-extern "C" int tb_elementwise(float*, const float*, const float*, long long, float, int, cudaStream_t) {
-  return static_cast<int>(cudaErrorNotSupported);
-}
+// The sanitizer build links no kernels: the launchers come from the CPU-only
+// build's stubs (csrc/cpu_only/kernel_stubs.cpp), which CPU tensors never reach.
 
 using namespace turbol;
 
@@ -180,6 +184,53 @@ static void schedules_tokenizer_dataset(const std::string& dir) {
   EXPECT(batches == 8);
 }
 
+// One CPU PPO iteration through the host engines: rollout on CartPole, GAE,
+// the update (epochs x minibatches with Adam), one stand-alone minibatch step,
+// and a rejected call (a row index past the data) that must not read it.
+static void ppo_host_iteration(uint64_t seed) {
+  const int N = 37, T = 5, B = T * N, MB = 37;
+  const std::vector<int64_t> dims_a{4, 20, 37, 2}, dims_c{4, 20, 37, 1};
+  int64_t n = 0;
+  for (const auto* d : {&dims_a, &dims_c})
+    for (size_t l = 0; l + 1 < d->size(); ++l) n += (*d)[l + 1] * ((*d)[l] + 1);
+  // a generator of this thread's own: the global one is shared state
+  const at::Generator gen = at::detail::createCPUGenerator(seed);
+  const at::Tensor flat = at::randn({n}, gen) * 0.2, grad = at::zeros({n}), m = at::zeros({n}), v = at::zeros({n});
+  GPUEnvironment env(N, 4, 2, Device::CPU(), EnvType::kCartPole, seed);
+  const auto i32 = at::TensorOptions().dtype(at::kInt), u8 = at::TensorOptions().dtype(at::kByte);
+  const at::Tensor obs = at::zeros({T, N, 4}), act = at::zeros({T, N}, i32), logp = at::zeros({T, N}),
+                   val = at::zeros({T + 1, N}), rew = at::zeros({T, N}), done = at::zeros({T, N}, u8);
+  EXPECT(PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, obs, act, logp, val, rew, done, seed, 0).ok());
+  EXPECT(act.min().item<int>() >= 0 && act.max().item<int>() <= 1 && at::all(logp <= 0).item<bool>());
+  const at::Tensor adv = at::zeros({T, N}), ret = at::zeros({T, N});
+  double st2[2] = {0, 0};
+  EXPECT(GaeHost(rew.data_ptr<float>(), val.data_ptr<float>(), done.data_ptr<uint8_t>(), adv.data_ptr<float>(),
+                 ret.data_ptr<float>(), T, N, 0.99f, 0.95f, st2)
+             .ok());
+  const at::Tensor perms = at::stack({at::randperm(B, gen), at::randperm(B, gen)});
+  const at::Tensor stats = at::zeros({8});
+  Status st;
+  const int64_t last = PpoCategoricalUpdateHost(flat, grad, m, v, 0, dims_a, dims_c, obs.view({B, 4}),
+                                                act.view({B}), logp.view({B}), adv.view({B}), ret.view({B}), perms,
+                                                MB, 0.2f, 0.5f, 0.01f, 3e-4f, 0.9f, 0.999f, 1e-5f, 0.f, stats, &st);
+  EXPECT(st.ok() && last == 2 * (B / MB) && stats[5].item<float>() == 2.f * B);
+  const at::Tensor idx = at::randperm(B, gen).narrow(0, 0, 13);
+  EXPECT(PpoCategoricalMinibatchHost(flat, grad, dims_a, dims_c, obs.view({B, 4}), act.view({B}), logp.view({B}),
+                                     adv.view({B}), ret.view({B}), idx, 0.2f, 0.5f, 0.01f, stats)
+             .ok());
+  const at::Tensor bad = at::full({3}, static_cast<int64_t>(B));
+  EXPECT(!PpoCategoricalMinibatchHost(flat, grad, dims_a, dims_c, obs.view({B, 4}), act.view({B}), logp.view({B}),
+                                      adv.view({B}), ret.view({B}), bad, 0.2f, 0.5f, 0.01f, stats)
+              .ok());
+  EXPECT(at::all(at::isfinite(flat)).item<bool>());
+}
+
+static void ppo_host_threads() {
+  std::thread a(ppo_host_iteration, 11), b(ppo_host_iteration, 12);
+  a.join();
+  b.join();
+}
+
 int main(int argc, char** argv) {
   const std::string dir = argc > 1 ? argv[1] : "/tmp";
   config_roundtrip(dir);
@@ -188,6 +239,7 @@ int main(int argc, char** argv) {
   tcp_store();
   kv_blocks();
   schedules_tokenizer_dataset(dir);
+  ppo_host_threads();
   if (g_fail) {
     std::fprintf(stderr, "%d checks failed\n", g_fail);
     return 1;

@@ -1,9 +1,10 @@
 """Race and memory checks of the host core under the compiler's sanitizers
 (AddressSanitizer + UndefinedBehaviorSanitizer in one build, ThreadSanitizer in
 another; tests/native/host_sanitize.cpp drives the profiler from several
-threads, the TCP store with concurrent clients, the KV block allocator and
-the file formats).  Device-side checking is done by the kernels' own error
-words; this covers the host runtime around them."""
+threads, the TCP store with concurrent clients, the KV block allocator, the
+file formats, and the CPU trainer's host engines from two threads).
+Device-side checking is done by the kernels' own error words; this covers the
+host runtime around them."""
 import os
 import shutil
 import subprocess
