@@ -24,6 +24,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -155,10 +156,14 @@ TB_INLINE void gemm_tile(const float* A, int64_t sam, int64_t sak, const float* 
     for (int v = 0; v < V; ++v) vstore<W>(C + r * ldc + v * W, acc[r][v]);
 }
 
+// Row blocks of 8 with AVX-512 (16 accumulators + 2 operands of its 32
+// registers), else 4 (8 + 2 of 16), then single rows.
 template <int W, int V>
 TB_INLINE void gemm_rows(int64_t M, int64_t K, const float* A, int64_t sam, int64_t sak, const float* Bm, int64_t ldb,
                          float* C, int64_t ldc, const float* bias, Init init) {
   int64_t m = 0;
+  if constexpr (W == 16)
+    for (; m + 8 <= M; m += 8) gemm_tile<W, 8, V>(A + m * sam, sam, sak, Bm, ldb, K, C + m * ldc, ldc, bias, init);
   for (; m + 4 <= M; m += 4) gemm_tile<W, 4, V>(A + m * sam, sam, sak, Bm, ldb, K, C + m * ldc, ldc, bias, init);
   for (; m < M; ++m) gemm_tile<W, 1, V>(A + m * sam, sam, sak, Bm, ldb, K, C + m * ldc, ldc, bias, init);
 }
@@ -193,6 +198,23 @@ TB_INLINE void gemm(int64_t M, int64_t N, int64_t K, const float* A, int64_t sam
     for (int64_t j = 0; j < w; ++j) C[m * ldc + n + j] = pc[m * W + j];
 }
 
+// Allocator for the workspace vectors: 64-byte (cache-line) aligned, so that
+// a vector load of a row that starts at a multiple of 16 floats stays in one line.
+template <typename T>
+struct LineAllocator {
+  using value_type = T;
+  LineAllocator() = default;
+  template <typename U>
+  LineAllocator(const LineAllocator<U>&) {}
+  T* allocate(size_t n) { return static_cast<T*>(::operator new(n * sizeof(T), std::align_val_t(64))); }
+  void deallocate(T* p, size_t) { ::operator delete(p, std::align_val_t(64)); }
+  template <typename U>
+  bool operator==(const LineAllocator<U>&) const { return true; }
+  template <typename U>
+  bool operator!=(const LineAllocator<U>&) const { return false; }
+};
+using Buf = std::vector<float, LineAllocator<float>>;
+
 struct Mlp {
   std::vector<int64_t> dims;  // widths dims[0] -> ... -> dims[L]
   std::vector<int64_t> woff;  // per layer: offset of W [out, in] in the flat buffers (b follows W)
@@ -210,10 +232,10 @@ Mlp mlp_layout(const std::vector<int64_t>& dims, int64_t* off) {
 // Buffers of one minibatch step (or one rollout step), sized once for B rows and reused.
 struct Workspace {
   int64_t B = 0;
-  std::vector<float> x;                   // [B, dims[0]] gathered observations
-  std::vector<std::vector<float>> ha, hc;  // per layer: output [B, dims[l + 1]] (tanh applied on hidden layers)
-  std::vector<float> d0, d1, wt;          // gradient ping-pong [B, max width], W^T of one layer
-  std::vector<float> pb, pc;              // W-wide padded operand / output of a product's last columns
+  Buf x;                   // [B, dims[0]] gathered observations
+  std::vector<Buf> ha, hc;  // per layer: output [B, dims[l + 1]] (tanh applied on hidden layers)
+  Buf d0, d1, wt;          // gradient ping-pong [B, max width], W^T of one layer
+  Buf pb, pc;              // W-wide padded operand / output of a product's last columns
 
   void size_for(const Mlp& a, const Mlp& c, int64_t rows) {
     B = rows;
@@ -224,7 +246,7 @@ struct Workspace {
         if (l + 1 < m->dims.size()) wt_max = std::max(wt_max, m->dims[l] * m->dims[l + 1]);
       }
     x.assign(static_cast<size_t>(rows * a.dims[0]), 0.f);
-    auto make = [&](const Mlp& m, std::vector<std::vector<float>>* h) {
+    auto make = [&](const Mlp& m, std::vector<Buf>* h) {
       h->clear();
       for (size_t l = 0; l + 1 < m.dims.size(); ++l) h->emplace_back(static_cast<size_t>(rows * m.dims[l + 1]));
     };
@@ -242,16 +264,22 @@ struct Workspace {
 // h[l] = tanh(h[l - 1] W_l^T + b_l) (no tanh on the last layer), h[-1] = x
 template <int W>
 TB_INLINE void mlp_forward(const Mlp& m, const float* p, const float* x, Workspace* ws,
-                           std::vector<std::vector<float>>* h) {
+                           std::vector<Buf>* h) {
   const size_t L = m.dims.size() - 1;
   const int64_t B = ws->B;
   const float* in = x;
   for (size_t l = 0; l < L; ++l) {
     const int64_t ni = m.dims[l], no = m.dims[l + 1];
     const float* Wl = p + m.woff[l];
+    // W^T in 16 x 16 blocks: a plain column-order copy writes rows of wt
+    // no floats apart and evicts its own lines (6x slower at 256 x 256)
     float* wt = ws->wt.data();
-    for (int64_t o = 0; o < no; ++o)
-      for (int64_t k = 0; k < ni; ++k) wt[k * no + o] = Wl[o * ni + k];
+    for (int64_t o0 = 0; o0 < no; o0 += 16)
+      for (int64_t k0 = 0; k0 < ni; k0 += 16) {
+        const int64_t oe = std::min(o0 + 16, no), ke = std::min(k0 + 16, ni);
+        for (int64_t o = o0; o < oe; ++o)
+          for (int64_t k = k0; k < ke; ++k) wt[k * no + o] = Wl[o * ni + k];
+      }
     float* y = (*h)[l].data();
     gemm<W>(B, no, ni, in, ni, 1, wt, no, y, no, Wl + no * ni, Init::kBias, ws->pb.data(), ws->pc.data());
     if (l + 1 < L) tanh_inplace<W>(y, B * no);
@@ -263,7 +291,7 @@ TB_INLINE void mlp_forward(const Mlp& m, const float* p, const float* x, Workspa
 // Per layer: gb += column sums of dy, gW += dy^T input, dx = dy W, then dx *= 1 - h^2.
 template <int W>
 TB_INLINE void mlp_backward(const Mlp& m, const float* p, float* g, const float* x, Workspace* ws,
-                            const std::vector<std::vector<float>>& h) {
+                            const std::vector<Buf>& h) {
   const int64_t B = ws->B;
   float* d = ws->d0.data();
   float* dn = ws->d1.data();
