@@ -30,6 +30,7 @@ def _have_runtime(name: str) -> bool:
                       "UBSAN_OPTIONS": "print_stacktrace=1:halt_on_error=1"}),
     ("tsan", "tsan", {"TSAN_OPTIONS": "halt_on_error=1:second_deadlock_stack=1"}),
 ])
+@pytest.mark.timeout(2700)  # build (up to 900 s) + instrumented run (up to 1500 s) on a slow, shared machine
 def test_host_core_under_sanitizer(kind, runtime, env):
     if not _have_runtime(runtime):
         pytest.skip(f"no lib{runtime} for {SANCXX}")
@@ -38,7 +39,7 @@ def test_host_core_under_sanitizer(kind, runtime, env):
     assert b.returncode == 0, b.stdout[-3000:] + b.stderr[-3000:]
     with tempfile.TemporaryDirectory() as d:
         r = subprocess.run([os.path.join(OUT, f"host_sanitize_{kind}"), d], capture_output=True, text=True,
-                           timeout=600, env=dict(os.environ, **env))
+                           timeout=1500, env=dict(os.environ, **env))
     report = r.stdout[-4000:] + r.stderr[-4000:]
     assert r.returncode == 0 and "HOST_SANITIZE_OK" in r.stdout, report
     for marker in ("ERROR: AddressSanitizer", "runtime error:", "WARNING: ThreadSanitizer"):
