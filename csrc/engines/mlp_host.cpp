@@ -19,6 +19,7 @@
 // libtorch); this file is the categorical MLP actor-critic PPO step of the CPU
 // trainer.
 #include <ATen/ATen.h>
+#include <ATen/Parallel.h>
 
 #include <algorithm>
 #include <cmath>
@@ -26,6 +27,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "turbol/engines.hpp"
@@ -35,6 +37,12 @@ namespace turbol {
 namespace {
 
 #define TB_INLINE static inline __attribute__((always_inline))
+// Attributes of the AVX-512 and AVX2 entry points (see the end of this
+// namespace); fp-contract=fast lets the compiler fuse the products'
+// multiply-adds where the target has FMA (the rest of the host core is built
+// without contraction).
+#define TB_AVX512 __attribute__((target("avx512f,avx512vl,avx2,fma,prefer-vector-width=512"), optimize("fp-contract=fast")))
+#define TB_AVX2 __attribute__((target("avx2,fma"), optimize("fp-contract=fast")))
 
 // The vector values below never cross a call boundary (every helper is
 // inlined into the per-instruction-set entry points), so the note that their
@@ -319,12 +327,16 @@ struct LossArgs {
   float clip, vf_coef, ent_coef;
 };
 
-// Forward, loss and backward for the rows idx[0:B]; adds the loss statistics to st[0:6].
+// Forward, loss and backward for the rows idx[0:ws->B] of a minibatch whose
+// loss is averaged with inv_b (1 / its row count, which may be more rows than
+// this call's when threads share the minibatch); adds the gradient into g and
+// the loss statistics to st[0:6].
 // Inlined (like every helper above) into the per-instruction-set entry points
 // below, so that it is compiled for their targets.
 template <int W>
 TB_INLINE Status minibatch_step(const Mlp& a, const Mlp& c, const float* p, float* g, const float* obs,
-                                int64_t obs_rows, const int64_t* idx, const LossArgs& la, Workspace* ws, float* st) {
+                                int64_t obs_rows, const int64_t* idx, const LossArgs& la, Workspace* ws, float inv_b,
+                                float* st) {
   const int64_t B = ws->B, O = a.dims[0], A = a.dims.back();
   for (int64_t i = 0; i < B; ++i) {
     const int64_t row = idx[i];
@@ -337,7 +349,6 @@ TB_INLINE Status minibatch_step(const Mlp& a, const Mlp& c, const float* p, floa
   const float* L = ws->ha.back().data();
   const float* V = ws->hc.back().data();
   float* dL = ws->d0.data();
-  const float inv_b = 1.f / static_cast<float>(B);
   double s_pg = 0, s_v = 0, s_ent = 0, s_kl = 0, s_clip = 0;
   std::vector<float> lsm(A), pr(A);
   for (int64_t i = 0; i < B; ++i) {
@@ -385,20 +396,98 @@ TB_INLINE Status minibatch_step(const Mlp& a, const Mlp& c, const float* p, floa
   return Status::Ok();
 }
 
-// The update loop (epochs x minibatches of perms, Adam after each when adam) for one instruction set.
+// One thread's share of a minibatch: rows idx[0:ws->B], gradient added into
+// g, statistics into st.
+struct Chunk {
+  const Mlp* a;
+  const Mlp* c;
+  const float* p;
+  float* g;
+  const float* obs;
+  int64_t obs_rows;
+  const int64_t* idx;
+  const LossArgs* la;
+  Workspace* ws;
+  float inv_b;
+  float st[6];
+  Status status;
+};
+
+template <int W>
+TB_INLINE void run_chunk(Chunk* k) {
+  k->status = minibatch_step<W>(*k->a, *k->c, k->p, k->g, k->obs, k->obs_rows, k->idx, *k->la, k->ws, k->inv_b, k->st);
+}
+// thread entry points, compiled for their instruction set like the callers
+TB_AVX512 void chunk_avx512(Chunk* k) { run_chunk<16>(k); }
+TB_AVX2 void chunk_avx2(Chunk* k) { run_chunk<8>(k); }
+void chunk_base(Chunk* k) { run_chunk<4>(k); }
+
+// Multiply-adds per row of a minibatch step: the forward and the two backward
+// products of every layer of both networks.
+int64_t macs_per_row(const Mlp& a, const Mlp& c) {
+  int64_t s = 0;
+  for (const Mlp* m : {&a, &c})
+    for (size_t l = 0; l + 1 < m->dims.size(); ++l) s += 3 * m->dims[l] * m->dims[l + 1];
+  return s;
+}
+
+// Threads for a minibatch of `rows`: at most torch's intra-op thread count,
+// each with at least 4 M multiply-adds (~60 us, well above the cost of
+// starting a thread) and 8 rows; small minibatches (a CartPole MLP 64-64 at
+// 64 rows is 1.7 M) stay on the calling thread.
+int threads_for(int64_t rows, int64_t per_row) {
+  constexpr int64_t kMinThreadMacs = int64_t{4} << 20;
+  const int64_t p = std::min<int64_t>({static_cast<int64_t>(at::get_num_threads()), rows * per_row / kMinThreadMacs,
+                                       rows / 8});
+  return p < 1 ? 1 : static_cast<int>(p);
+}
+
+// The update loop (epochs x minibatches of perms, Adam after each when adam)
+// for one instruction set.  A large minibatch is split by rows over threads,
+// each with its own workspace and gradient buffer; the buffers are summed
+// into g (the sum's order depends on the thread count, not on timing).
 template <int W>
 TB_INLINE Status update_loop(const Mlp& a, const Mlp& c, float* p, float* g, float* m1, float* m2, int64_t n,
                              int64_t* step, const float* obs, int64_t obs_rows, const int64_t* perms, int64_t epochs,
                              int64_t rows, int64_t minibatch, bool adam, const LossArgs& la, float lr, float b1,
                              float b2, float eps, float wd, float* st) {
-  Workspace ws;
-  ws.size_for(a, c, minibatch);
+  const int P0 = threads_for(minibatch, macs_per_row(a, c));
+  const int64_t per = (minibatch + P0 - 1) / P0;
+  const int P = static_cast<int>((minibatch + per - 1) / per);  // chunks that hold rows
+  std::vector<Workspace> ws(P);
+  for (auto& w : ws) w.size_for(a, c, per);
+  std::vector<Buf> gbuf(P - 1, Buf(static_cast<size_t>(n)));
+  void (*const fn)(Chunk*) = W == 16 ? chunk_avx512 : (W == 8 ? chunk_avx2 : chunk_base);
+  const float inv_b = 1.f / static_cast<float>(minibatch);
   const int64_t n_mb = rows / minibatch;
   for (int64_t e = 0; e < epochs; ++e)
     for (int64_t k = 0; k < n_mb; ++k) {
       if (adam) std::fill(g, g + n, 0.f);
-      TURBOL_RETURN_IF_ERROR(
-          minibatch_step<W>(a, c, p, g, obs, obs_rows, perms + e * rows + k * minibatch, la, &ws, st));
+      const int64_t* idx = perms + e * rows + k * minibatch;
+      if (P == 1) {
+        ws[0].B = minibatch;
+        TURBOL_RETURN_IF_ERROR(minibatch_step<W>(a, c, p, g, obs, obs_rows, idx, la, &ws[0], inv_b, st));
+      } else {
+        std::vector<Chunk> ch(P);
+        for (int t = 0; t < P; ++t) {
+          const int64_t r0 = t * per, r1 = std::min(minibatch, r0 + per);
+          ws[t].B = r1 - r0;
+          float* gt = t == 0 ? g : gbuf[t - 1].data();
+          if (t > 0) std::fill(gt, gt + n, 0.f);
+          ch[t] = Chunk{&a, &c, p, gt, obs, obs_rows, idx + r0, &la, &ws[t], inv_b, {0, 0, 0, 0, 0, 0}, Status::Ok()};
+        }
+        std::vector<std::thread> th;
+        th.reserve(P - 1);
+        for (int t = 1; t < P; ++t) th.emplace_back(fn, &ch[t]);
+        fn(&ch[0]);
+        for (auto& x : th) x.join();
+        for (int t = 0; t < P; ++t) {
+          TURBOL_RETURN_IF_ERROR(ch[t].status);
+          for (int j = 0; j < 6; ++j) st[j] += ch[t].st[j];
+          if (t > 0)
+            for (int64_t i = 0; i < n; ++i) g[i] += gbuf[t - 1][i];
+        }
+      }
       if (adam) AdamHost(p, g, m1, m2, n, ++*step, lr, b1, b2, eps, wd, 1.f);
     }
   return Status::Ok();
@@ -469,13 +558,9 @@ TB_INLINE Status rollout_loop(const Mlp& a, const Mlp& c, const float* p, const 
 #define TB_UPDATE_PASS a, c, p, g, m1, m2, n, step, obs, obs_rows, perms, epochs, rows, minibatch, adam, la, lr, b1, b2, eps, wd, st
 #define TB_ROLLOUT_ARGS const Mlp &a, const Mlp &c, const float *p, const RolloutArgs &r
 
-// One entry point per instruction set; fp-contract=fast lets the compiler
-// fuse the products' multiply-adds where the target has FMA (the rest of the
-// host core is built without contraction).  Chosen at run time, not through
-// an ifunc, which would run while the loader relocates the library (before a
+// One entry point per instruction set, chosen at run time, not through an
+// ifunc, which would run while the loader relocates the library (before a
 // sanitizer runtime has started).
-#define TB_AVX512 __attribute__((target("avx512f,avx512vl,avx2,fma,prefer-vector-width=512"), optimize("fp-contract=fast")))
-#define TB_AVX2 __attribute__((target("avx2,fma"), optimize("fp-contract=fast")))
 
 TB_AVX512 Status update_avx512(TB_UPDATE_ARGS) { return update_loop<16>(TB_UPDATE_PASS); }
 TB_AVX2 Status update_avx2(TB_UPDATE_ARGS) { return update_loop<8>(TB_UPDATE_PASS); }

@@ -21,6 +21,7 @@
 
 #include <ATen/ATen.h>
 #include <ATen/CPUGeneratorImpl.h>
+#include <ATen/Parallel.h>
 
 #include "kernels.h"
 #include "turbol/config.hpp"
@@ -231,6 +232,30 @@ static void ppo_host_threads() {
   b.join();
 }
 
+// One minibatch large enough that the update splits its rows over 4 threads
+// (per-thread workspaces and gradient buffers, summed after the join).
+static void ppo_host_split() {
+  const int B = 601;
+  const std::vector<int64_t> dims_a{4, 96, 80, 2}, dims_c{4, 96, 80, 1};
+  int64_t n = 0;
+  for (const auto* d : {&dims_a, &dims_c})
+    for (size_t l = 0; l + 1 < d->size(); ++l) n += (*d)[l + 1] * ((*d)[l] + 1);
+  const at::Generator gen = at::detail::createCPUGenerator(21);
+  const at::Tensor flat = at::randn({n}, gen) * 0.1, grad = at::zeros({n}), m = at::zeros({n}), v = at::zeros({n});
+  const at::Tensor obs = at::randn({B, 4}, gen), logp = at::randn({B}, gen) * 0.1 - 0.7, adv = at::randn({B}, gen),
+                   ret = at::randn({B}, gen), stats = at::zeros({8});
+  const at::Tensor act = at::randint(0, 2, {B}, gen, at::TensorOptions().dtype(at::kInt));
+  const at::Tensor perms = at::randperm(B, gen).view({1, B});
+  const int prev = at::get_num_threads();
+  at::set_num_threads(4);
+  Status st;
+  const int64_t last = PpoCategoricalUpdateHost(flat, grad, m, v, 0, dims_a, dims_c, obs, act, logp, adv, ret, perms,
+                                                B, 0.2f, 0.5f, 0.01f, 3e-4f, 0.9f, 0.999f, 1e-5f, 0.f, stats, &st);
+  at::set_num_threads(prev);
+  EXPECT(st.ok() && last == 1 && stats[5].item<float>() == static_cast<float>(B));
+  EXPECT(at::all(at::isfinite(flat)).item<bool>());
+}
+
 int main(int argc, char** argv) {
   const std::string dir = argc > 1 ? argv[1] : "/tmp";
   config_roundtrip(dir);
@@ -240,6 +265,7 @@ int main(int argc, char** argv) {
   kv_blocks();
   schedules_tokenizer_dataset(dir);
   ppo_host_threads();
+  ppo_host_split();
   if (g_fail) {
     std::fprintf(stderr, "%d checks failed\n", g_fail);
     return 1;

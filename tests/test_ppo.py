@@ -48,16 +48,17 @@ def test_cpu_ppo_host_minibatch_matches_autograd(hidden, ent):
     assert a.opt._host_step == b.opt._host_step == c.opt._host_step == cfg.epochs * cfg.n_minibatches
 
 
-@pytest.mark.parametrize("hidden,B,scale", [((64, 64), 64, 1.0), ((20, 37), 13, 0.3), ((48,), 7, 4.0), ((), 5, 1.0)])
-def test_host_minibatch_gradient_matches_fp64_autograd(hidden, B, scale):
+@pytest.mark.parametrize("hidden,B,scale,threads", [((64, 64), 64, 1.0, 1), ((20, 37), 13, 0.3, 1),
+                                                    ((48,), 7, 4.0, 1), ((), 5, 1.0, 1), ((96, 80), 601, 1.0, 4)])
+def test_host_minibatch_gradient_matches_fp64_autograd(hidden, B, scale, threads):
     """The core's minibatch step (register-tiled products, vector tanh)
     against float64 autograd of the same actor / critic MLPs and PPO loss:
     widths that are not multiples of the vector width, row counts that are not
     multiples of 4, saturated (scale 4) and near-linear (scale 0.3) hidden
-    layers."""
+    layers, and a minibatch large enough to be split over 4 threads."""
     from turbol_b200._native import core
     g = torch.Generator().manual_seed(3)
-    O, A, N = 4, 3, 97
+    O, A, N = 4, 3, max(97, B + 11)
     clip, vf, ent = 0.2, 0.5, 0.01
     dims_a, dims_c = [O, *hidden, A], [O, *hidden, 1]
     parts = []
@@ -71,7 +72,12 @@ def test_host_minibatch_gradient_matches_fp64_autograd(hidden, B, scale):
     adv, ret = torch.randn(N, generator=g), torch.randn(N, generator=g)
     idx = torch.randperm(N, generator=g)[:B]
     grad, stats = torch.zeros_like(flat), torch.zeros(6)
-    core().ppo_minibatch_host(flat, grad, dims_a, dims_c, obs, act, old_logp, adv, ret, idx, clip, vf, ent, stats)
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        core().ppo_minibatch_host(flat, grad, dims_a, dims_c, obs, act, old_logp, adv, ret, idx, clip, vf, ent, stats)
+    finally:
+        torch.set_num_threads(prev)
 
     p64 = flat.double().requires_grad_()
     x = obs[idx].double()

@@ -60,11 +60,13 @@ class PPOConfig:
     compute_dtype: str = "bf16"  # "bf16" (tensor cores, fp32 master weights) or "fp32"
     cuda_graphs: bool = True
     env: str = "cartpole"
-    # CPU device: intra-op threads during an iteration (0 = automatic: one
-    # thread when the minibatch's matrix products are small, where forking
-    # the thread pool per operator costs more than the arithmetic; measured
-    # 60.8 K vs 44.6 K env-steps/s on 8 cores for 256 envs, MLP 64-64,
-    # minibatch 64); the process's setting is restored after the iteration
+    # CPU device: intra-op threads during an iteration (0 = automatic: the
+    # process's setting for the core's host rollout / update, which split a
+    # large minibatch over at most that many threads and keep a small one on
+    # the calling thread; for the torch-op path, one thread when the
+    # minibatch's matrix products are small, where forking the thread pool
+    # per operator costs more than the arithmetic); the process's setting is
+    # restored after the iteration
     cpu_threads: int = 0
 
     @property
@@ -379,7 +381,9 @@ class PPOTrainer:
             prev = torch.get_num_threads()
             want = cfg.cpu_threads
             if want <= 0:
-                want = 1 if cfg.minibatch_size * max(cfg.hidden or (1,)) <= 65536 else prev
+                host = getattr(self, "host_update", True) and getattr(self, "host_rollout", True)
+                small = cfg.minibatch_size * max(cfg.hidden or (1,)) <= 65536
+                want = prev if host or not small else 1
             if want != prev:
                 torch.set_num_threads(want)
             try:
