@@ -502,50 +502,101 @@ struct RolloutArgs {
   uint64_t seed, counter;
 };
 
+// One thread's rows [row0, row0 + ws->B) of a rollout step: the critic's
+// values of the observations ob (rows of the whole batch) and, unless
+// values_only, the actor's action and its log-probability.  A row's result
+// depends on its own data only (the Philox key is the global env index), so
+// any split over threads gives the same rollout.
+struct RolloutChunk {
+  const Mlp* a;
+  const Mlp* c;
+  const float* p;
+  const float* ob;
+  int64_t row0;
+  Workspace* ws;
+  int* act;
+  float* logp;
+  float* val;
+  bool values_only;
+  uint64_t seed;
+  uint32_t t, ctr_lo, ctr_hi;
+};
+
+template <int W>
+TB_INLINE void rollout_rows(RolloutChunk* k) {
+  const Mlp& a = *k->a;
+  Workspace* ws = k->ws;
+  const int64_t O = a.dims[0], A = a.dims.back(), n = ws->B, r0 = k->row0;
+  const float* ob = k->ob + r0 * O;
+  mlp_forward<W>(*k->c, k->p, ob, ws, &ws->hc);
+  const float* V = ws->hc.back().data();
+  for (int64_t i = 0; i < n; ++i) k->val[r0 + i] = V[i];
+  if (k->values_only) return;
+  mlp_forward<W>(a, k->p, ob, ws, &ws->ha);
+  const float* L = ws->ha.back().data();
+  for (int64_t i = 0; i < n; ++i) {
+    const float* li = L + i * A;
+    float mx = li[0];
+    for (int64_t j = 1; j < A; ++j) mx = std::max(mx, li[j]);
+    float se = 0.f;
+    for (int64_t j = 0; j < A; ++j) se += std::exp(li[j] - mx);
+    const float lse = mx + std::log(se);
+    // inverse CDF of the softmax at u in [0, 1): the first action whose
+    // cumulative probability passes u (the last one if rounding leaves the sum below u)
+    const uint32_t w =
+        static_cast<uint32_t>(HostPhiloxWord(k->seed, static_cast<uint32_t>(r0 + i), k->t, k->ctr_lo, k->ctr_hi, 0));
+    const float u = static_cast<float>(w >> 8) * (1.0f / 16777216.0f);
+    int64_t pick = A - 1;
+    float cum = 0.f;
+    for (int64_t j = 0; j < A; ++j) {
+      cum += std::exp(li[j] - lse);
+      if (u < cum) {
+        pick = j;
+        break;
+      }
+    }
+    k->act[r0 + i] = static_cast<int>(pick);
+    k->logp[r0 + i] = li[pick] - lse;
+  }
+}
+// thread entry points, compiled for their instruction set like the callers
+TB_AVX512 void rchunk_avx512(RolloutChunk* k) { rollout_rows<16>(k); }
+TB_AVX2 void rchunk_avx2(RolloutChunk* k) { rollout_rows<8>(k); }
+void rchunk_base(RolloutChunk* k) { rollout_rows<4>(k); }
+
 // The CPU CartPole rollout for one instruction set (see PpoCartPoleRolloutHost).
+// Each step's forward and sampling are split by rows over threads when the
+// batch is large (threads_for on the forward's multiply-adds); the
+// environment step stays on the calling thread.
 template <int W>
 TB_INLINE Status rollout_loop(const Mlp& a, const Mlp& c, const float* p, const RolloutArgs& r) {
-  Workspace ws;
-  ws.size_for(a, c, r.N);
+  const int64_t O = a.dims[0], N = r.N;
+  const int P0 = threads_for(N, macs_per_row(a, c) / 3);
+  const int64_t per = (N + P0 - 1) / P0;
+  const int P = static_cast<int>((N + per - 1) / per);
+  std::vector<Workspace> ws(P);
+  for (auto& w : ws) w.size_for(a, c, per);
+  Buf last(static_cast<size_t>(N * O));  // the observations after the last step (values only)
+  void (*const fn)(RolloutChunk*) = W == 16 ? rchunk_avx512 : (W == 8 ? rchunk_avx2 : rchunk_base);
   const float* state = r.env->StateTensor().data_ptr<float>();
-  const int64_t O = a.dims[0], A = a.dims.back(), N = r.N;
   const uint32_t ctr_lo = static_cast<uint32_t>(r.counter), ctr_hi = static_cast<uint32_t>(r.counter >> 32);
+  std::vector<RolloutChunk> ch(P);
+  std::vector<std::thread> th;
   for (int64_t t = 0; t <= r.T; ++t) {
-    float* ob = t < r.T ? r.obs + t * N * O : ws.x.data();
+    float* ob = t < r.T ? r.obs + t * N * O : last.data();
     std::memcpy(ob, state, sizeof(float) * N * O);
-    mlp_forward<W>(c, p, ob, &ws, &ws.hc);
-    const float* V = ws.hc.back().data();
-    float* val = r.val + t * N;
-    for (int64_t i = 0; i < N; ++i) val[i] = V[i];
-    if (t == r.T) break;
-    mlp_forward<W>(a, p, ob, &ws, &ws.ha);
-    const float* L = ws.ha.back().data();
     int* act = r.act + t * N;
-    float* logp = r.logp + t * N;
-    for (int64_t i = 0; i < N; ++i) {
-      const float* li = L + i * A;
-      float mx = li[0];
-      for (int64_t j = 1; j < A; ++j) mx = std::max(mx, li[j]);
-      float se = 0.f;
-      for (int64_t j = 0; j < A; ++j) se += std::exp(li[j] - mx);
-      const float lse = mx + std::log(se);
-      // inverse CDF of the softmax at u in [0, 1): the first action whose
-      // cumulative probability passes u (the last one if rounding leaves the sum below u)
-      const uint32_t w = static_cast<uint32_t>(
-          HostPhiloxWord(r.seed, static_cast<uint32_t>(i), static_cast<uint32_t>(t), ctr_lo, ctr_hi, 0));
-      const float u = static_cast<float>(w >> 8) * (1.0f / 16777216.0f);
-      int64_t pick = A - 1;
-      float cum = 0.f;
-      for (int64_t j = 0; j < A; ++j) {
-        cum += std::exp(li[j] - lse);
-        if (u < cum) {
-          pick = j;
-          break;
-        }
-      }
-      act[i] = static_cast<int>(pick);
-      logp[i] = li[pick] - lse;
+    for (int k = 0; k < P; ++k) {
+      const int64_t r0 = k * per;
+      ws[k].B = std::min(N, r0 + per) - r0;
+      ch[k] = RolloutChunk{&a, &c, p, ob, r0, &ws[k], act, r.logp + t * N, r.val + t * N, t == r.T, r.seed,
+                           static_cast<uint32_t>(t), ctr_lo, ctr_hi};
     }
+    th.clear();
+    for (int k = 1; k < P; ++k) th.emplace_back(fn, &ch[k]);
+    fn(&ch[0]);
+    for (auto& x : th) x.join();
+    if (t == r.T) break;
     TURBOL_RETURN_IF_ERROR(r.env->StepCartPoleHost(act, r.rew + t * N, r.done + t * N));
   }
   return Status::Ok();

@@ -232,8 +232,9 @@ static void ppo_host_threads() {
   b.join();
 }
 
-// One minibatch large enough that the update splits its rows over 4 threads
-// (per-thread workspaces and gradient buffers, summed after the join).
+// One minibatch large enough that the update splits its rows over threads
+// (per-thread workspaces and gradient buffers, summed after the join), and a
+// rollout whose steps split their rows the same way.
 static void ppo_host_split() {
   const int B = 601;
   const std::vector<int64_t> dims_a{4, 96, 80, 2}, dims_c{4, 96, 80, 1};
@@ -251,9 +252,15 @@ static void ppo_host_split() {
   Status st;
   const int64_t last = PpoCategoricalUpdateHost(flat, grad, m, v, 0, dims_a, dims_c, obs, act, logp, adv, ret, perms,
                                                 B, 0.2f, 0.5f, 0.01f, 3e-4f, 0.9f, 0.999f, 1e-5f, 0.f, stats, &st);
+  const int T = 2;
+  GPUEnvironment env(B, 4, 2, Device::CPU(), EnvType::kCartPole, 21);
+  const at::Tensor ro = at::zeros({T, B, 4}), ra = at::zeros({T, B}, at::TensorOptions().dtype(at::kInt)),
+                   rl = at::zeros({T, B}), rv = at::zeros({T + 1, B}), rr = at::zeros({T, B}),
+                   rd = at::zeros({T, B}, at::TensorOptions().dtype(at::kByte));
+  EXPECT(PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, ro, ra, rl, rv, rr, rd, 21, 0).ok());
   at::set_num_threads(prev);
   EXPECT(st.ok() && last == 1 && stats[5].item<float>() == static_cast<float>(B));
-  EXPECT(at::all(at::isfinite(flat)).item<bool>());
+  EXPECT(at::all(at::isfinite(flat)).item<bool>() && at::all(at::isfinite(rv)).item<bool>());
 }
 
 int main(int argc, char** argv) {

@@ -148,6 +148,26 @@ def test_cpu_host_rollout_matches_policy_and_environment():
         assert torch.equal(getattr(tr, name), getattr(again, name)), name
 
 
+def test_cpu_host_rollout_is_the_same_on_any_thread_count():
+    """A rollout large enough to be split by rows over threads (1,024 envs,
+    MLP 128-128) gives bit-identical buffers with 1 and with 4 intra-op
+    threads: each row's forward and draw depend on that row only.  (Both
+    trainers are built under the same thread count: the orthogonal
+    initialization itself rounds differently on different counts.)"""
+    cfg = PPOConfig(num_envs=1024, rollout_steps=4, hidden=(128, 128), seed=6)
+    out = [PPOTrainer(cfg, device="cpu") for _ in range(2)]
+    assert torch.equal(out[0].policy.fp.flat, out[1].policy.fp.flat)
+    prev = torch.get_num_threads()
+    try:
+        for tr, threads in zip(out, (1, 4)):
+            torch.set_num_threads(threads)
+            tr._rollout_cpu()
+    finally:
+        torch.set_num_threads(prev)
+    for name in ("obs_buf", "act_buf", "logp_buf", "val_buf", "rew_buf", "done_buf"):
+        assert torch.equal(getattr(out[0], name), getattr(out[1], name)), name
+
+
 def test_policy_engine_reference_api():
     pe = turbol.PolicyEngine(obs_dim=4, act_dim=2, device="cpu")
     assert pe.initialize().ok()
