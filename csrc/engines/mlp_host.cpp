@@ -11,8 +11,9 @@
 // plus the tanh passes.  Here every product is a register-tiled loop over
 // native-width float vectors (GCC vector types), compiled three times
 // (AVX-512, AVX2 + FMA, baseline x86-64 with SSE) and chosen once at run time
-// from the CPU's features.  tanh is a vectorized restatement through expm1
-// (below).
+// from the CPU's features (TURBOL_HOST_ISA can name a narrower one).  tanh is
+// a vectorized restatement through expm1 (below).  A large minibatch or
+// rollout batch is split by rows over torch's intra-op thread count.
 //
 // Reference: turbol_vllm/src/policy/policy_engine.cpp:103-138 (the reference's
 // PolicyEngine::Update: one autograd step of a linear Gaussian policy through
@@ -434,11 +435,17 @@ int64_t macs_per_row(const Mlp& a, const Mlp& c) {
 // Threads for a minibatch of `rows`: at most torch's intra-op thread count,
 // each with at least 4 M multiply-adds (~60 us, well above the cost of
 // starting a thread) and 8 rows; small minibatches (a CartPole MLP 64-64 at
-// 64 rows is 1.7 M) stay on the calling thread.
+// 64 rows is 1.7 M) stay on the calling thread.  TURBOL_HOST_THREAD_MACS,
+// read once per process, replaces the 4 M (the sanitizer tests lower it to
+// split small batches).
 int threads_for(int64_t rows, int64_t per_row) {
-  constexpr int64_t kMinThreadMacs = int64_t{4} << 20;
-  const int64_t p = std::min<int64_t>({static_cast<int64_t>(at::get_num_threads()), rows * per_row / kMinThreadMacs,
-                                       rows / 8});
+  static const int64_t min_macs = [] {
+    const char* e = std::getenv("TURBOL_HOST_THREAD_MACS");
+    const long long v = e ? std::atoll(e) : 0;
+    return v > 0 ? static_cast<int64_t>(v) : int64_t{4} << 20;
+  }();
+  const int64_t p =
+      std::min<int64_t>({static_cast<int64_t>(at::get_num_threads()), rows * per_row / min_macs, rows / 8});
   return p < 1 ? 1 : static_cast<int>(p);
 }
 

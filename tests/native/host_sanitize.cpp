@@ -12,6 +12,7 @@
 // update with Adam, GAE) on sizes that are not multiples of the vector tiles,
 // from two threads at once.
 #include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -80,6 +81,9 @@ static void profiler_threads(const std::string& dir) {
       (void)prof.GetStats();
       (void)prof.Summary();
       ++n;
+      // exports walk every span under the profiler's lock; back to back they
+      // can starve the recording threads (minutes under a sanitizer)
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
     }
     EXPECT(n > 0);
   });
@@ -232,12 +236,14 @@ static void ppo_host_threads() {
   b.join();
 }
 
-// One minibatch large enough that the update splits its rows over threads
-// (per-thread workspaces and gradient buffers, summed after the join), and a
-// rollout whose steps split their rows the same way.
+// A minibatch and a rollout batch split by rows over threads (per-thread
+// workspaces and gradient buffers, summed after the join): main lowers the
+// work per thread (TURBOL_HOST_THREAD_MACS) so that these small batches
+// split; every tensor is made before the thread count is raised, so only the
+// core's own threads run while it is 4.
 static void ppo_host_split() {
-  const int B = 601;
-  const std::vector<int64_t> dims_a{4, 96, 80, 2}, dims_c{4, 96, 80, 1};
+  const int B = 67, N = 70, T = 2;
+  const std::vector<int64_t> dims_a{4, 16, 24, 2}, dims_c{4, 16, 24, 1};
   int64_t n = 0;
   for (const auto* d : {&dims_a, &dims_c})
     for (size_t l = 0; l + 1 < d->size(); ++l) n += (*d)[l + 1] * ((*d)[l] + 1);
@@ -247,32 +253,41 @@ static void ppo_host_split() {
                    ret = at::randn({B}, gen), stats = at::zeros({8});
   const at::Tensor act = at::randint(0, 2, {B}, gen, at::TensorOptions().dtype(at::kInt));
   const at::Tensor perms = at::randperm(B, gen).view({1, B});
+  GPUEnvironment env(N, 4, 2, Device::CPU(), EnvType::kCartPole, 21);
+  const at::Tensor ro = at::zeros({T, N, 4}), ra = at::zeros({T, N}, at::TensorOptions().dtype(at::kInt)),
+                   rl = at::zeros({T, N}), rv = at::zeros({T + 1, N}), rr = at::zeros({T, N}),
+                   rd = at::zeros({T, N}, at::TensorOptions().dtype(at::kByte));
   const int prev = at::get_num_threads();
   at::set_num_threads(4);
   Status st;
   const int64_t last = PpoCategoricalUpdateHost(flat, grad, m, v, 0, dims_a, dims_c, obs, act, logp, adv, ret, perms,
                                                 B, 0.2f, 0.5f, 0.01f, 3e-4f, 0.9f, 0.999f, 1e-5f, 0.f, stats, &st);
-  const int T = 2;
-  GPUEnvironment env(B, 4, 2, Device::CPU(), EnvType::kCartPole, 21);
-  const at::Tensor ro = at::zeros({T, B, 4}), ra = at::zeros({T, B}, at::TensorOptions().dtype(at::kInt)),
-                   rl = at::zeros({T, B}), rv = at::zeros({T + 1, B}), rr = at::zeros({T, B}),
-                   rd = at::zeros({T, B}, at::TensorOptions().dtype(at::kByte));
-  EXPECT(PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, ro, ra, rl, rv, rr, rd, 21, 0).ok());
+  const Status rs = PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, ro, ra, rl, rv, rr, rd, 21, 0);
   at::set_num_threads(prev);
   EXPECT(st.ok() && last == 1 && stats[5].item<float>() == static_cast<float>(B));
-  EXPECT(at::all(at::isfinite(flat)).item<bool>() && at::all(at::isfinite(rv)).item<bool>());
+  EXPECT(rs.ok() && at::all(at::isfinite(flat)).item<bool>() && at::all(at::isfinite(rv)).item<bool>());
 }
 
 int main(int argc, char** argv) {
+  // small batches split over threads in ppo_host_split (read once, before any host-engine call)
+  setenv("TURBOL_HOST_THREAD_MACS", "16384", 1);
   const std::string dir = argc > 1 ? argv[1] : "/tmp";
-  config_roundtrip(dir);
-  profiler_threads(dir);
-  writers(dir);
-  tcp_store();
-  kv_blocks();
-  schedules_tokenizer_dataset(dir);
-  ppo_host_threads();
-  ppo_host_split();
+  // each section's wall time goes to stdout (instrumented code is slow; this shows where)
+  auto section = [](const char* name, auto&& fn) {
+    const auto t0 = std::chrono::steady_clock::now();
+    fn();
+    std::printf("%-28s %8.2f s\n", name,
+                std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+    std::fflush(stdout);
+  };
+  section("config", [&] { config_roundtrip(dir); });
+  section("profiler threads", [&] { profiler_threads(dir); });
+  section("writers", [&] { writers(dir); });
+  section("tcp store", [] { tcp_store(); });
+  section("kv blocks", [] { kv_blocks(); });
+  section("schedules/tokenizer/dataset", [&] { schedules_tokenizer_dataset(dir); });
+  section("ppo host (two threads)", [] { ppo_host_threads(); });
+  section("ppo host (split batches)", [] { ppo_host_split(); });
   if (g_fail) {
     std::fprintf(stderr, "%d checks failed\n", g_fail);
     return 1;
