@@ -3,6 +3,7 @@ gloo ranks: a rank that exits non-zero, and a rank that goes silent (no
 heartbeat), both end the attempt; the relaunch resumes from the per-rank
 checkpoint and finishes with the same result as an uninterrupted run."""
 import os
+import random
 import socket
 import sys
 
@@ -14,10 +15,36 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 WORKER = os.path.join(HERE, "launch_worker.py")
 
 
-def _port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+_RNG = random.Random()
+
+
+def _port(span: int = 2):
+    """A port p with p .. p + span - 1 all free (the launcher relaunches on
+    port + attempt), taken below the kernel's ephemeral range: a port the
+    kernel handed out (bind to 0) can be followed by one that the first
+    attempt's own gloo connections are using."""
+    rng = _RNG
+    lo = 20000
+    try:
+        with open("/proc/sys/net/ipv4/ip_local_port_range") as f:
+            lo = min(lo, int(f.read().split()[0]) - 2000)
+    except (OSError, ValueError, IndexError):
+        pass
+    for _ in range(200):
+        p = rng.randrange(max(1024, lo - 8000), lo)
+        socks = []
+        try:
+            for q in range(p, p + span):
+                s = socket.socket()
+                socks.append(s)
+                s.bind(("127.0.0.1", q))
+            return p
+        except OSError:
+            continue
+        finally:
+            for s in socks:
+                s.close()
+    raise RuntimeError("no free port pair")
 
 
 def _results(d, world):
