@@ -28,6 +28,7 @@
 #include <cstring>
 #include <new>
 #include <string>
+#include <system_error>
 #include <thread>
 #include <vector>
 
@@ -423,6 +424,25 @@ TB_AVX512 void chunk_avx512(Chunk* k) { run_chunk<16>(k); }
 TB_AVX2 void chunk_avx2(Chunk* k) { run_chunk<8>(k); }
 void chunk_base(Chunk* k) { run_chunk<4>(k); }
 
+// Runs fn on every chunk: chunks 1.. on threads of their own, chunk 0 on the
+// calling thread, then joins.  A chunk whose thread cannot be started (the
+// process is out of threads) runs on the calling thread instead, so no
+// started thread is ever left unjoined.
+template <typename C>
+void run_chunks(void (*fn)(C*), std::vector<C>& ch) {
+  std::vector<std::thread> th;
+  th.reserve(ch.size());
+  size_t started = 1;
+  try {
+    for (; started < ch.size(); ++started) th.emplace_back(fn, &ch[started]);
+  } catch (const std::system_error&) {
+    // the rest run below
+  }
+  fn(&ch[0]);
+  for (size_t k = started; k < ch.size(); ++k) fn(&ch[k]);
+  for (auto& x : th) x.join();
+}
+
 // Multiply-adds per row of a minibatch step: the forward and the two backward
 // products of every layer of both networks.
 int64_t macs_per_row(const Mlp& a, const Mlp& c) {
@@ -483,11 +503,7 @@ TB_INLINE Status update_loop(const Mlp& a, const Mlp& c, float* p, float* g, flo
           if (t > 0) std::fill(gt, gt + n, 0.f);
           ch[t] = Chunk{&a, &c, p, gt, obs, obs_rows, idx + r0, &la, &ws[t], inv_b, {0, 0, 0, 0, 0, 0}, Status::Ok()};
         }
-        std::vector<std::thread> th;
-        th.reserve(P - 1);
-        for (int t = 1; t < P; ++t) th.emplace_back(fn, &ch[t]);
-        fn(&ch[0]);
-        for (auto& x : th) x.join();
+        run_chunks(fn, ch);
         for (int t = 0; t < P; ++t) {
           TURBOL_RETURN_IF_ERROR(ch[t].status);
           for (int j = 0; j < 6; ++j) st[j] += ch[t].st[j];
@@ -588,7 +604,6 @@ TB_INLINE Status rollout_loop(const Mlp& a, const Mlp& c, const float* p, const 
   const float* state = r.env->StateTensor().data_ptr<float>();
   const uint32_t ctr_lo = static_cast<uint32_t>(r.counter), ctr_hi = static_cast<uint32_t>(r.counter >> 32);
   std::vector<RolloutChunk> ch(P);
-  std::vector<std::thread> th;
   for (int64_t t = 0; t <= r.T; ++t) {
     float* ob = t < r.T ? r.obs + t * N * O : last.data();
     std::memcpy(ob, state, sizeof(float) * N * O);
@@ -599,10 +614,7 @@ TB_INLINE Status rollout_loop(const Mlp& a, const Mlp& c, const float* p, const 
       ch[k] = RolloutChunk{&a, &c, p, ob, r0, &ws[k], act, r.logp + t * N, r.val + t * N, t == r.T, r.seed,
                            static_cast<uint32_t>(t), ctr_lo, ctr_hi};
     }
-    th.clear();
-    for (int k = 1; k < P; ++k) th.emplace_back(fn, &ch[k]);
-    fn(&ch[0]);
-    for (auto& x : th) x.join();
+    run_chunks(fn, ch);
     if (t == r.T) break;
     TURBOL_RETURN_IF_ERROR(r.env->StepCartPoleHost(act, r.rew + t * N, r.done + t * N));
   }
