@@ -7,8 +7,12 @@
 //   parameter layout (flat fp32): W_a [A, O], b_a [A], W_c [O], b_c
 #include <math.h>
 
+#include <ATen/Parallel.h>
+
 #include <algorithm>
 #include <cmath>
+#include <system_error>
+#include <thread>
 #include <vector>
 
 #include "turbol/engines.hpp"
@@ -190,21 +194,23 @@ void AdamHost(float* p, const float* g, float* m, float* v, int64_t n, int64_t s
   adam_fn()(p, g, m, v, n, lr, b1, b2, eps, wd, grad_scale, ibc1, ibc2);
 }
 
-Status GaeHost(const float* rewards, const float* values, const uint8_t* dones, float* adv, float* ret, int T, int N,
-               float gamma, float lam, double* stats) {
-  if (T < 0 || N < 0) return Status::InvalidArgument("gae: bad dimensions");
-  const float gl = static_cast<float>(static_cast<double>(gamma) * lam);
-  std::vector<float> last(static_cast<size_t>(N), 0.f);
+namespace {
+
+// The backward sweep over environments [n0, n1) (vectorizable over them);
+// adds the sum and sum of squares of their advantages into s[0], s[1].
+void gae_columns(const float* rewards, const float* values, const uint8_t* dones, float* adv, float* ret, int T,
+                 int N, int n0, int n1, float gamma, float gl, bool want_stats, double* s) {
+  std::vector<float> last(static_cast<size_t>(n1 - n0), 0.f);
   double s1 = 0.0, s2 = 0.0;
-  // backward over time, vectorizable over the environments
   for (int t = T - 1; t >= 0; --t) {
-    const float* r = rewards + static_cast<size_t>(t) * N;
-    const float* v0 = values + static_cast<size_t>(t) * N;
+    const size_t o = static_cast<size_t>(t) * N + n0;
+    const float* r = rewards + o;
+    const float* v0 = values + o;
     const float* v1 = v0 + N;
-    const uint8_t* d = dones + static_cast<size_t>(t) * N;
-    float* a = adv + static_cast<size_t>(t) * N;
-    float* rt = ret + static_cast<size_t>(t) * N;
-    for (int n = 0; n < N; ++n) {
+    const uint8_t* d = dones + o;
+    float* a = adv + o;
+    float* rt = ret + o;
+    for (int n = 0; n < n1 - n0; ++n) {
       const float nd = d[n] ? 0.f : 1.f;
       const float delta = r[n] + gamma * nd * v1[n] - v0[n];
       const float l = delta + gl * nd * last[n];
@@ -212,16 +218,52 @@ Status GaeHost(const float* rewards, const float* values, const uint8_t* dones, 
       a[n] = l;
       rt[n] = l + v0[n];
     }
-    if (stats)
-      for (int n = 0; n < N; ++n) {
+    if (want_stats)
+      for (int n = 0; n < n1 - n0; ++n) {
         s1 += a[n];
         s2 += static_cast<double>(a[n]) * a[n];
       }
   }
-  if (stats) {
-    stats[0] += s1;
-    stats[1] += s2;
+  s[0] += s1;
+  s[1] += s2;
+}
+
+}  // namespace
+
+// Environments are independent columns of the sweep: a large [T, N] is split
+// by column blocks (multiples of 64) over torch's intra-op threads, at least
+// 1 M elements each; a block whose thread cannot be started runs on the
+// calling thread.  The statistics add up block by block in block order.
+Status GaeHost(const float* rewards, const float* values, const uint8_t* dones, float* adv, float* ret, int T, int N,
+               float gamma, float lam, double* stats) {
+  if (T < 0 || N < 0) return Status::InvalidArgument("gae: bad dimensions");
+  const float gl = static_cast<float>(static_cast<double>(gamma) * lam);
+  const int64_t work = static_cast<int64_t>(T) * N;
+  const int P = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>({static_cast<int64_t>(at::get_num_threads()), work >> 20, N / 64})));
+  const int per = P == 1 ? N : (N / P + 63) / 64 * 64;
+  const int blocks = P == 1 ? 1 : (N + per - 1) / per;
+  std::vector<double> s(2 * static_cast<size_t>(blocks), 0.0);
+  auto run = [&](int k) {
+    const int n0 = k * per, n1 = std::min(N, n0 + per);
+    gae_columns(rewards, values, dones, adv, ret, T, N, n0, n1, gamma, gl, stats != nullptr, &s[2 * k]);
+  };
+  std::vector<std::thread> th;
+  th.reserve(blocks);
+  int started = 1;
+  try {
+    for (; started < blocks; ++started) th.emplace_back(run, started);
+  } catch (const std::system_error&) {
+    // the rest run below
   }
+  run(0);
+  for (int k = started; k < blocks; ++k) run(k);
+  for (auto& x : th) x.join();
+  if (stats)
+    for (int k = 0; k < blocks; ++k) {
+      stats[0] += s[2 * k];
+      stats[1] += s[2 * k + 1];
+    }
   return Status::Ok();
 }
 

@@ -13,6 +13,7 @@
 // from two threads at once.
 #include <atomic>
 #include <chrono>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -257,13 +258,21 @@ static void ppo_host_split() {
   const at::Tensor ro = at::zeros({T, N, 4}), ra = at::zeros({T, N}, at::TensorOptions().dtype(at::kInt)),
                    rl = at::zeros({T, N}), rv = at::zeros({T + 1, N}), rr = at::zeros({T, N}),
                    rd = at::zeros({T, N}, at::TensorOptions().dtype(at::kByte));
+  const int GT = 40, GN = 64 * 1024;  // GAE over 2.6 M elements: split into column blocks
+  const at::Tensor gr = at::randn({GT, GN}, gen), gv = at::randn({GT + 1, GN}, gen),
+                   gd = at::zeros({GT, GN}, at::TensorOptions().dtype(at::kByte)), ga = at::empty({GT, GN}),
+                   gret = at::empty({GT, GN});
+  double gs[2] = {0, 0};
   const int prev = at::get_num_threads();
   at::set_num_threads(4);
   Status st;
   const int64_t last = PpoCategoricalUpdateHost(flat, grad, m, v, 0, dims_a, dims_c, obs, act, logp, adv, ret, perms,
                                                 B, 0.2f, 0.5f, 0.01f, 3e-4f, 0.9f, 0.999f, 1e-5f, 0.f, stats, &st);
   const Status rs = PpoCartPoleRolloutHost(&env, flat, dims_a, dims_c, ro, ra, rl, rv, rr, rd, 21, 0);
+  const Status gst = GaeHost(gr.data_ptr<float>(), gv.data_ptr<float>(), gd.data_ptr<uint8_t>(), ga.data_ptr<float>(),
+                             gret.data_ptr<float>(), GT, GN, 0.99f, 0.95f, gs);
   at::set_num_threads(prev);
+  EXPECT(gst.ok() && std::isfinite(gs[0]) && gs[1] > 0 && at::all(at::isfinite(gret)).item<bool>());
   EXPECT(st.ok() && last == 1 && stats[5].item<float>() == static_cast<float>(B));
   EXPECT(rs.ok() && at::all(at::isfinite(flat)).item<bool>() && at::all(at::isfinite(rv)).item<bool>());
 }

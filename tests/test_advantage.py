@@ -79,6 +79,32 @@ def test_gae_host_sweep_matches_oracle(T, N):
     assert abs(float(stats[1]) - float((ea * ea).sum())) < 1e-3 * max(1.0, float((ea * ea).sum()))
 
 
+def test_gae_host_split_over_threads_matches_one_thread():
+    """A [128, 40000] sweep is split by environment blocks over 4 threads:
+    advantages and returns are bit-identical to one thread's (each
+    environment's recurrence is the same), the statistics agree to rounding,
+    and both equal the float64 oracle."""
+    g = torch.Generator().manual_seed(9)
+    T, N = 128, 40000
+    r = torch.randn(T, N, generator=g)
+    v = torch.randn(T + 1, N, generator=g)
+    d = torch.rand(T, N, generator=g) < 0.05
+    out = []
+    prev = torch.get_num_threads()
+    try:
+        for threads in (1, 4):
+            torch.set_num_threads(threads)
+            stats = torch.zeros(2, dtype=torch.float64)
+            a, rt = gae(r, v, d, 0.99, 0.95, stats=stats)
+            out.append((a, rt, stats))
+    finally:
+        torch.set_num_threads(prev)
+    assert torch.equal(out[0][0], out[1][0]) and torch.equal(out[0][1], out[1][1])
+    assert torch.allclose(out[0][2], out[1][2], rtol=1e-9, atol=1e-6)
+    ea, _ = ref.gae(r.double(), v.double(), d, 0.99, 0.95)
+    assert torch.allclose(out[1][0].double(), ea, atol=1e-4, rtol=1e-4)
+
+
 def test_static_scratch_gae_bound_cpu():
     """The allocation-free GAE entry point's size check (host arithmetic, no
     GPU): fits() agrees with the 1 MiB array for every shape probed, and under
